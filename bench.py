@@ -1,0 +1,475 @@
+#!/usr/bin/env python
+"""Benchmark of the attention-share audit path on B200: audited KV tokens/s and % of HBM roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config llama8b|llama70b|long]
+                    [--mode reference|all-heads] [--impl ours|reference]
+
+One step is one audit step of the configured model over synthetic seeded inputs: the audit kernel
+for every layer (captured in one CUDA graph, as the engine captures its decode step), which also
+leaves the exact per-block shares on the device; with N > 1 ranks (one per GPU, KV heads split over
+the ranks) one NCCL all-reduce combines the ranks' shares. ``value`` is whole-job audited KV tokens/s
+(one token = one (row, position, layer, audited KV head) key vector) with inputs resident in HBM;
+``e2e`` is the same through the public API with the step's host inputs copied in from pinned memory
+and its shares copied out every step. ``view`` times the block-view build of the view stress shape
+(1024 rows x 8192 blocks, per-row `sum` budgets), row-sharded over the ranks.
+
+``--impl reference`` times the reference algorithm on the host cores instead (the C restatement of
+the reference kernel in oracle/, all threads), on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "sigmod-kvscope_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HEAD_DIM = 128
+BLOCK = 16
+TILE_BLOCKS = 2
+
+CONFIGS = {
+    # Llama-3.1-8B decode audit on one B200 (the metric's headline configuration)
+    "llama8b": dict(rows=64, q_heads=32, kv_heads=8, layers=32, pool=40_000, lens=("uniform", 1024, 8192), pools=8),
+    # Llama-3-70B head-sharded audit (the scaling configuration)
+    "llama70b": dict(rows=256, q_heads=64, kv_heads=8, layers=80, pool=60_000, lens=("lognormal", 2048, 1.0, 64, 32768),
+                     pools=4),
+    # long context: 8 rows of 32k-128k tokens
+    "long": dict(rows=8, q_heads=32, kv_heads=8, layers=32, pool=66_000, lens=("uniform", 32768, 131072), pools=4),
+}
+
+# dram__bytes_read.sum + dram__bytes_write.sum per audit launch from the committed ncu capture
+# (profiles/audit_kernel_llama8b.md), scaled to one full-size launch; None until captured.
+NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"llama8b": None}
+
+
+def lengths(spec, rows: int, rng: np.random.Generator) -> np.ndarray:
+    if spec[0] == "uniform":
+        return rng.integers(spec[1], spec[2] + 1, rows)
+    _, median, sigma, lo, hi = spec
+    return np.clip(np.round(rng.lognormal(math.log(median), sigma, rows)), lo, hi).astype(np.int64)
+
+
+def bytes_per_unit(group_rows: int) -> float:
+    """Algorithmic DRAM bytes per audited key vector: its K row, its table entry (per block), the
+    m and l cells (per block, G values each), and the share accumulator write (per block)."""
+    return 2 * HEAD_DIM + 4 / BLOCK + 8 * group_rows / BLOCK + 4 / BLOCK
+
+
+def measured_peak() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock and throttle samples every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) == 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---- the workload -------------------------------------------------------------------------------------
+
+
+class Workload:
+    """Seeded synthetic inputs of one rank: KV pools, block tables, lengths and queries on the device."""
+
+    def __init__(self, cfg: dict, rank: int, world: int, mode: str, seed: int = 0) -> None:
+        self.cfg = cfg
+        self.rows, self.layers = cfg["rows"], cfg["layers"]
+        self.group_rows = cfg["q_heads"] // cfg["kv_heads"]
+        if cfg["kv_heads"] % world:
+            raise SystemExit(f"{cfg['kv_heads']} KV heads do not split over {world} GPUs")
+        self.kv_local = cfg["kv_heads"] // world
+        self.heads = self.kv_local if mode == "all-heads" else 1
+        rng = np.random.default_rng(seed)  # identical on every rank: one batch, heads split
+        self.lens = lengths(cfg["lens"], self.rows, rng).astype(np.int32)
+        self.width = int(math.ceil(self.lens.max() / BLOCK))
+        blocks = -(-self.lens // BLOCK)
+        pool = max(cfg["pool"], int(blocks.sum()) + 1)
+        self.pool = pool
+        # distinct random blocks for the positions each row holds; the rest of a row is never read
+        ids = rng.permutation(pool)[: int(blocks.sum())].astype(np.int32)
+        table = np.zeros((self.rows, self.width), dtype=np.int32)
+        start = 0
+        for r, n in enumerate(blocks):
+            table[r, :n] = ids[start : start + n]
+            start += n
+        self.table_host = table
+        dev = torch.device("cuda", torch.cuda.current_device())
+        gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+        self.caches = [
+            torch.randn(pool, 2, BLOCK, self.kv_local, HEAD_DIM, device=dev, generator=gen, dtype=torch.bfloat16)
+            for _ in range(cfg["pools"])
+        ]
+        tokens = self.rows
+        self.queries = [
+            torch.randn(tokens, self.kv_local * self.group_rows, HEAD_DIM, device=dev, generator=gen,
+                        dtype=torch.bfloat16) for _ in range(cfg["pools"])
+        ]
+        self.table = torch.from_numpy(table).to(dev)
+        self.lens_t = torch.from_numpy(self.lens).to(dev)
+        self.qrow = np.arange(self.rows, dtype=np.int32)
+        self.select = np.ones(self.rows, dtype=bool)
+        self.scale = 1.0 / math.sqrt(HEAD_DIM)
+
+    def units_per_step(self) -> int:
+        return int(self.lens.astype(np.int64).sum()) * self.layers * self.heads
+
+    def keys(self, layer: int) -> torch.Tensor:
+        return self.caches[layer % len(self.caches)][:, 0]
+
+    def query(self, layer: int) -> torch.Tensor:
+        return self.queries[layer % len(self.queries)]
+
+
+def make_plane(w: Workload):
+    from ekv.runtime.audit_kernel import RecordingPlane
+
+    os.environ.setdefault("EKV_RUNTIME_DIR", tempfile.mkdtemp(prefix="ekv_bench_"))
+    plane = RecordingPlane(w.layers, w.rows, w.width, w.group_rows, BLOCK, heads=w.heads)
+    plane.attach([0x1000 + i for i in range(w.layers)])
+    plane.select(w.select, w.qrow)
+    plane.set(True)
+    return plane
+
+
+def audit_step(plane, w: Workload) -> None:
+    for layer in range(w.layers):
+        plane.launch(layer, w.table, w.lens_t, w.query(layer), w.keys(layer), w.scale)
+
+
+def capture(fn) -> torch.cuda.CUDAGraph:
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        fn()  # warm: one-time kernel attributes are set outside the capture
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    torch.cuda.synchronize()
+    return graph
+
+
+def timed(fn, steps: int, warmup: int, dist_on: bool) -> float:
+    """Seconds for `steps` calls of fn, max over ranks; CUDA events on the current stream."""
+    import torch.distributed as dist
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if dist_on:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    seconds = start.elapsed_time(end) / 1e3
+    if dist_on:
+        t = torch.tensor([seconds], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        seconds = float(t.item())
+    return seconds
+
+
+def view_bench(rank: int, world: int, steps: int, warmup: int, dist_on: bool) -> dict:
+    """The view stress shape: 1024 rows x 8192, per-row `sum` budgets, rows split over the ranks."""
+    from ekv.runtime.block_view import plan_view
+
+    rows_total, width = 1024, 8192
+    gen = torch.Generator().manual_seed(0)
+    n = torch.randint(1, width + 1, (rows_total,), generator=gen).to(torch.int32)
+    table = torch.randint(0, 2**20, (rows_total, width), generator=gen, dtype=torch.int32)
+    scores = torch.distributions.Dirichlet(torch.full((width,), 0.3, dtype=torch.float64)).sample((rows_total,))
+    scores = torch.where(torch.arange(width)[None, :] < n[:, None].long(), scores, torch.zeros_like(scores)).float()
+    fraction = 0.2 + 0.8 * torch.rand(rows_total, generator=gen, dtype=torch.float64)
+    lens = n * BLOCK
+    mine = slice(rank * rows_total // world, (rank + 1) * rows_total // world)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    t, nn, ln, sc, fr = (x[mine].contiguous().to(dev) for x in (table, n, lens, scores, fraction))
+    out = (torch.empty_like(t), torch.empty(len(nn), dtype=torch.int32, device=dev))
+
+    def build():
+        plan_view(t, ln, BLOCK, nn, scores=sc, policy="sum", row_fraction=fr, recent_blocks=0, out=out)
+
+    graph = capture(build)
+    seconds = timed(graph.replay, steps, warmup, dist_on)
+    ids = int(n.long().sum())
+    return {"us": round(seconds / steps * 1e6, 2), "rows": rows_total, "width": width, "ids": ids,
+            "policy": "sum per row", "rows_per_gpu": len(nn), "launches_per_build": 2}
+
+
+# ---- the CPU arms ----------------------------------------------------------------------------------------
+
+
+class CpuSample:
+    """The C restatement of the reference kernel (oracle/audit_cpu.c) on every host thread, over a
+    sample of the workload: all its rows and lengths, one KV head's keys (the audited head of a
+    layer), repeated for as many layers as the time target allows."""
+
+    def __init__(self, cfg: dict) -> None:
+        from oracle import audit as oaud
+        from oracle import cpu as ocpu
+
+        ocpu.build()
+        self.ocpu, self.oaud = ocpu, oaud
+        rng = np.random.default_rng(0)
+        self.lens = lengths(cfg["lens"], cfg["rows"], rng).astype(np.int32)
+        self.g_rows = cfg["q_heads"] // cfg["kv_heads"]
+        self.rows = cfg["rows"]
+        self.width = int(math.ceil(self.lens.max() / BLOCK))
+        blocks = -(-self.lens // BLOCK)
+        pool = int(blocks.sum()) + 1
+        gen = np.random.default_rng(1)
+        k = gen.standard_normal((pool, BLOCK, 1, HEAD_DIM), dtype=np.float32)
+        self.k16 = (k.view(np.uint32) >> 16).astype(np.uint16)  # bf16 bit patterns
+        q = gen.standard_normal((self.rows, self.g_rows, HEAD_DIM), dtype=np.float32)
+        self.q16 = (q.view(np.uint32) >> 16).astype(np.uint16)
+        ids = gen.permutation(pool)[: int(blocks.sum())].astype(np.int32)
+        self.table = np.zeros((self.rows, self.width), dtype=np.int32)
+        start = 0
+        for r, n in enumerate(blocks):
+            self.table[r, :n] = ids[start : start + n]
+            start += n
+        self.threads = ocpu.threads()
+        self.layers = 1
+
+    def run(self, layers: int) -> tuple[float, int]:
+        lse = self.oaud.new_table(layers, self.rows, self.width, self.g_rows)
+        qrow = np.arange(self.rows, dtype=np.int32)
+        select = np.ones(self.rows, dtype=np.uint8)
+        t0 = time.perf_counter()
+        for layer in range(layers):
+            self.ocpu.tile_lse(self.q16, self.k16, "bf16", self.table, self.lens, qrow, select, 1, lse,
+                               1 / math.sqrt(HEAD_DIM), layer, 0, BLOCK, TILE_BLOCKS, self.threads)
+        return time.perf_counter() - t0, int(self.lens.astype(np.int64).sum()) * layers
+
+    def calibrate(self, seconds_target: float) -> None:
+        sec, units = self.run(1)
+        self.layers = max(1, int(seconds_target / max(sec, 1e-6)))
+
+    def describe(self, units: int) -> str:
+        return (f"{self.rows} rows x {self.layers} layers of the workload ({units} key vectors, one KV head's keys "
+                f"per layer), C restatement of tile_lse_kernel on {self.threads} OpenMP threads")
+
+
+def cpu_sample(cfg: dict, seconds_target: float) -> dict:
+    """Audited tokens/s of the reference algorithm on the host cores, over a bounded sample."""
+    sample = CpuSample(cfg)
+    sample.calibrate(seconds_target)
+    sec, units = sample.run(sample.layers)
+    return {"value": units / sec, "unit": "audited KV tokens/s", "cores": sample.threads, "kind": "port",
+            "sample": sample.describe(units), "seconds": round(sec, 2)}
+
+
+def reference_arm(args, cfg: dict) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sample = CpuSample(cfg)
+    sample.calibrate(seconds_target=2.0)
+    rates, units = [], 0
+    for step in range(args.warmup + args.steps):
+        sec, units = sample.run(sample.layers)
+        if step >= args.warmup:
+            rates.append(units / sec)
+    value = statistics.median(rates)
+    per_step = [{"kind": "port", "cores": sample.threads, "sample": sample.describe(units)}]
+    line = {
+        "impl": "reference", "metric": "audited KV tokens/s", "value": value, "unit": "audited KV tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "weak", "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": args.config, "mode": args.mode, "rows": cfg["rows"], "layers": cfg["layers"]},
+        "cpu_baseline": {k: per_step[-1][k] for k in ("kind", "cores", "sample")} | {"value": value,
+                                                                                     "unit": "audited KV tokens/s"},
+        "e2e": {"value": value, "unit": "audited KV tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "vs_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---- our arm ---------------------------------------------------------------------------------------------
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="llama8b")
+    ap.add_argument("--mode", choices=["reference", "all-heads"], default="reference")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the timed CPU sample")
+    ap.add_argument("--no-view", action="store_true", help="skip the block-view build timing")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        reference_arm(args, cfg)
+        return
+
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist_on = world > 1
+    if dist_on:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    import ekv.build
+
+    ekv.build.build()
+    from ekv.observe.ranks import allreduce_shares
+
+    w = Workload(cfg, rank, world, args.mode)
+    plane = make_plane(w)
+    graph = capture(lambda: audit_step(plane, w))
+    share = plane.shares()
+
+    def step():
+        graph.replay()
+        if dist_on:
+            allreduce_shares(share)
+
+    with ClockSampler(local) as clocks:
+        seconds = timed(step, args.steps, args.warmup, dist_on)
+    status = plane.status()
+    if status:
+        raise SystemExit(f"the audit kernel reported status {status}")
+    units_rank = w.units_per_step()
+    units_all = units_rank * world
+    value = units_all * args.steps / seconds
+    launch_seconds = seconds / args.steps / w.layers
+    per_launch_bytes = units_rank / w.layers * bytes_per_unit(w.heads * w.group_rows)
+    achieved = per_launch_bytes / launch_seconds / 1e9
+    peak, peak_kind = measured_peak()
+
+    # e2e: the step's host inputs in from pinned memory, the shares out, every step
+    pinned_table = torch.from_numpy(w.table_host).pin_memory()
+    pinned_lens = torch.from_numpy(w.lens).pin_memory()
+    pinned_sel = torch.from_numpy(w.select.astype(np.uint8)).pin_memory()
+    pinned_tok = torch.from_numpy(w.qrow).pin_memory()
+    out_host = torch.empty(share.shape, dtype=share.dtype).pin_memory()
+
+    def e2e_step():
+        w.table.copy_(pinned_table, non_blocking=True)
+        w.lens_t.copy_(pinned_lens, non_blocking=True)
+        plane._select.copy_(pinned_sel, non_blocking=True)
+        plane._token.copy_(pinned_tok, non_blocking=True)
+        graph.replay()
+        if dist_on:
+            allreduce_shares(share)
+        out_host.copy_(share, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    e2e_seconds = timed(e2e_step, args.steps, args.warmup, dist_on)
+    h2d = pinned_table.nbytes + pinned_lens.nbytes + pinned_sel.nbytes + pinned_tok.nbytes
+    d2h = out_host.nbytes
+    view = None if args.no_view else view_bench(rank, world, args.steps, args.warmup, dist_on)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_sample(cfg, seconds_target=10.0)
+    if dist_on:
+        dist.barrier()
+        del graph
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    traffic = NCU_TRAFFIC_PER_LAUNCH.get(args.config) if args.mode == "reference" else None
+    line = {
+        "metric": "audited KV tokens/s", "value": value, "unit": "audited KV tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": seconds / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak" if args.mode == "reference" else "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": args.config, "mode": args.mode, "rows": w.rows, "layers": w.layers,
+                   "q_heads": cfg["q_heads"], "kv_heads": cfg["kv_heads"], "kv_heads_per_gpu": w.kv_local,
+                   "audited_heads_per_layer_per_gpu": w.heads, "block_size": BLOCK, "tile_blocks": TILE_BLOCKS,
+                   "mean_len": float(w.lens.mean()), "width": w.width, "pools": cfg["pools"],
+                   "l2": f"inputs larger than L2: {units_rank / w.layers * 256 / 1e6:.0f} MB of keys per launch",
+                   "parallelism": f"tp{world} (KV heads)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "peak_kind": peak_kind,
+                     "bytes_per_unit": bytes_per_unit(w.heads * w.group_rows),
+                     "note": "per audit launch; duration = step time / layers, launch gaps included"},
+        "e2e": {"value": units_all * args.steps / e2e_seconds, "unit": "audited KV tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "note": "block table, lengths, selection, query rows in; shares out; KV cache resident"},
+        "gpu_launches": args.steps * w.layers,
+        "clocks": clocks.summary(),
+        "view": view,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,198 @@
+/*
+ * ekv_b200.h -- C ABI of libekv_b200.so, the sm_100a implementation of KVScope's attention-share
+ * audit and block-table view path.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes, and a CUDA stream given
+ * as `void*` (a cudaStream_t; NULL is the legacy default stream). None allocates device memory, none
+ * synchronises the host, and each launches a grid whose shape depends on its size arguments only, so
+ * a sequence of calls can be captured in a CUDA graph. Every function returns EKV_OK (0) or a
+ * negative EKV_E* code; ekv_last_error_string() then describes the failure (thread-local).
+ *
+ * Citations point into the reference project (jc-su/SIGMOD-KVSCOPE) by path:line.
+ */
+#ifndef EKV_B200_H
+#define EKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes ---------------------------------------------------------------------------- */
+#define EKV_OK 0
+#define EKV_EINVAL (-1)  /* a shape, stride or argument error: the Python layer raises ValueError   */
+#define EKV_ERANGE (-2)  /* a count beyond what a buffer was sized for: RuntimeError                 */
+#define EKV_ENOTSUP (-3) /* a configuration this build has no kernel for: RuntimeError               */
+#define EKV_ECUDA (-4)   /* the CUDA runtime reported an error at launch: RuntimeError               */
+
+/* ---- element types of the query and the key cache --------------------------------------------- */
+#define EKV_DTYPE_F16 0
+#define EKV_DTYPE_BF16 1
+
+/* ---- how the shares of layers and query rows combine (observe/tile_shares.py:58-103) ------------- */
+#define EKV_AGG_MEAN 0
+#define EKV_AGG_MAX 1
+
+/* ---- share_flags of ekv_audit_launch --------------------------------------------------------- */
+#define EKV_SHARE_RESET 1    /* this launch starts an audit step: overwrite the share accumulators */
+#define EKV_SHARE_FINALIZE 2 /* this launch ends it: write the normalised shares to share_out       */
+
+/* ---- bits a kernel ORs into the optional device status word ---------------------------------- */
+#define EKV_STATUS_BAD_BLOCK_ID 1u  /* a table entry outside [0, pool_blocks): its keys were skipped */
+#define EKV_STATUS_LEN_OVER_WIDTH 2u /* a length beyond width*block_size: clamped to the table width */
+#define EKV_STATUS_BAD_QROW 4u      /* a query token index outside [0, q_tokens): the row was skipped */
+#define EKV_STATUS_WAIT_TIMEOUT 8u  /* a bounded wait on a bulk copy gave up: the output is invalid  */
+
+/* ---- ranking policies of the view builder (observe/allocation.py:79-118, daemon.py:49) --------- */
+#define EKV_POLICY_SUM 0     /* highest share first; equal shares: the newer block first           */
+#define EKV_POLICY_UNIFORM 1 /* highest share first; equal shares: the older block first           */
+#define EKV_POLICY_NEWEST 2  /* the fixed rule scores = arange(n): the newest open blocks           */
+
+/* Tiles of one audit CTA; the audit workspace holds one partial per (row, chunk of this many tiles). */
+#define EKV_AUDIT_CHUNK_TILES 8
+
+/* Human-readable description of the last error on this thread ("" if none). */
+const char* ekv_last_error_string(void);
+
+/* ABI version of this library: bumped on any signature change. */
+int ekv_abi_version(void);
+
+/* Bytes of workspace ekv_audit_launch needs for its fused share epilogue: a ticket per row and one
+ * (max, sum) partial per (row, chunk, query row). The first rows*4 bytes, rounded up to 256, are the
+ * tickets: they must be zero before the first launch, and every launch leaves them zero again. */
+size_t ekv_audit_workspace_bytes(int rows, int width, int group_rows, int heads, int block_size,
+                                 int tile_blocks);
+
+/*
+ * ekv_audit_launch -- record the attention-share statistic of one layer.
+ *
+ * Replaces the Triton launch of tile_lse_kernel at runtime/audit_kernel.py:239-265 (kernel body
+ * :34-109); the first 22 arguments keep that kernel's names and meaning:
+ *   q        [tokens, q_heads, head_dim] query of the step, element strides q_stride_token/head;
+ *   k        [pool_blocks, block_size, kv_heads, head_dim] key cache of the layer (kv_cache[:, 0]);
+ *   table    int32 [rows, width] block table (row stride table_stride), lens int32 [rows] tokens;
+ *   qrow     int32 [rows] token index of each row's query; select uint8 [rows]; flag uint32 [1];
+ *   lse      float32 [2][layers][rows][width][heads*group_rows]: plane 0 the tile max m, plane 1 the
+ *            tile sum l, written into every block cell of a tile whose first token is < lens[row].
+ * For each row with select != 0 (and only when *flag != 0), KV head `group + h` for h < heads, and
+ * each tile of tile_blocks*block_size tokens, it computes m = max_j q.k_j*scale and
+ * l = sum_j exp(q.k_j*scale - m) over the tile's tokens below lens[row]. heads = 1 is the
+ * reference's sampling (one KV group per layer, group = layer % kv_heads, :250).
+ *
+ * With share_acc != NULL it also folds the layer into the exact per-block attention share, in the
+ * same launch: the last CTA of each row normalises that row's tile values into block shares
+ * (observe/tile_shares.py:58-103 with row_blocks = ceil(lens/block_size)) and adds them (mean) or
+ * takes their maximum (max) into share_acc [rows][width]; contributors [rows] counts the query rows
+ * with data. EKV_SHARE_RESET overwrites instead of accumulating; EKV_SHARE_FINALIZE writes the final
+ * share of every row to share_out [rows][width]: NaN for a row that is not selected or has no data.
+ * workspace must hold ekv_audit_workspace_bytes(...) bytes (256-byte aligned). status (optional)
+ * receives EKV_STATUS_* bits. q_tokens bounds qrow. Supported: head_dim 128, block_size*tile_blocks
+ * in {16, 32, 64}, heads*group_rows <= 128, group_rows <= 16.
+ */
+int ekv_audit_launch(const void* q, const void* k, const int32_t* table, const int32_t* lens,
+                     const int32_t* qrow, const uint8_t* select, const uint32_t* flag, float* lse,
+                     float scale, int layer, int group, int64_t q_stride_token,
+                     int64_t q_stride_head, int64_t k_stride_block, int64_t k_stride_pos,
+                     int64_t k_stride_head, int64_t table_stride, int layers, int rows, int width,
+                     int group_rows, int block_size, int tile_blocks, int head_dim, int dtype,
+                     int heads, int kv_heads, int64_t pool_blocks, int64_t q_tokens,
+                     float* share_acc, int32_t* contributors, float* share_out, int aggregate,
+                     int share_flags, void* workspace, size_t workspace_bytes, uint32_t* status,
+                     void* stream);
+
+/*
+ * ekv_normalize_tile_lse -- the controller's read of the statistic, on the device.
+ *
+ * Replaces read_tile_rows (observe/tile_shares.py:129-173) followed by normalize_tile_lse
+ * (:58-103), as TileShareSource.read calls them (observe/controller.py:111-136). For the count rows
+ * row_ids[i] (int32, any order) of the table lse (layout as above, `table_layers` layers of which the
+ * first `layers` are read, group_rows values per cell), it forms u = m + log(l) - log(tile_blocks),
+ * gives a partial last tile's weight back to its blocks, drops cells at or beyond row_blocks[i],
+ * softmax-normalises each (layer, row, query row) and takes the mean or max over layers and query
+ * rows. share [count][width] float32; NaN rows where no (layer, query row) has a finite value.
+ * contributors (optional) [count] receives the number of (layer, query row) pairs with data.
+ */
+int ekv_normalize_tile_lse(const float* lse, int table_layers, int layers, int rows, int width,
+                           int group_rows, const int32_t* row_ids, const int32_t* row_blocks,
+                           int count, int tile_blocks, int aggregate, float* share,
+                           int32_t* contributors, void* stream);
+
+/*
+ * ekv_normalize_log_weights -- normalize_tile_lse (observe/tile_shares.py:58-103) on the device for
+ * u values already read: u float32 [layers][rows][width][group_rows], row_blocks int32 [rows].
+ * share [rows][width] float32 and contributors (optional) [rows] as in ekv_normalize_tile_lse.
+ */
+int ekv_normalize_log_weights(const float* u, int layers, int rows, int width, int group_rows,
+                              const int32_t* row_blocks, int tile_blocks, int aggregate,
+                              float* share, int32_t* contributors, void* stream);
+
+/*
+ * ekv_share_finalize -- normalise accumulated shares when no launch carried EKV_SHARE_FINALIZE.
+ * share_out[r] = share_acc[r] / contributors[r] (mean) or share_acc[r] / sum(share_acc[r]) (max);
+ * NaN rows where contributors is 0 or select[r] is 0 (select may be NULL).
+ */
+int ekv_share_finalize(const float* share_acc, const int32_t* contributors, const uint8_t* select,
+                       int rows, int width, int aggregate, float* share_out, void* stream);
+
+/*
+ * ekv_allocate_quotas -- how many unpinned blocks each row keeps.
+ *
+ * The budget arithmetic of Controller._allocate (observe/controller.py:398-451) and the quotas of
+ * allocate/_uniform (observe/allocation.py:55-91). Row r holds row_blocks[r] blocks; it is measured
+ * when row_blocks[r] > cap_above_blocks (and > 0). Its pins are block 0, the newest
+ * recent_blocks + 1 blocks (none for recent_blocks = -1), and the blocks from measured_blocks[r] on
+ * (measured_blocks may be NULL). With row_fraction == NULL the measured rows share one budget --
+ * `budget` when it is >= 0 (allocate()'s argument), else max(pins, ceil(budget_fraction * blocks))
+ * as the controller computes it -- split by `uniform` quotas with largest remainders (objective
+ * EKV_POLICY_UNIFORM or EKV_POLICY_NEWEST). With row_fraction != NULL (float64 [rows]) every row is
+ * its own allocate() call with budget max(pins, ceil(row_fraction[r] * row_blocks[r])) (any
+ * objective). quota [rows] int32: the unpinned blocks to keep, or -1 for a row that is not measured
+ * (it reads in full). One CTA; rows <= 8192 for a shared budget, <= 65536 otherwise.
+ */
+int ekv_allocate_quotas(const int32_t* row_blocks, const int32_t* measured_blocks,
+                        int recent_blocks, int cap_above_blocks, double budget_fraction,
+                        int64_t budget, const double* row_fraction, int objective, int rows,
+                        int32_t* quota, void* stream);
+
+/*
+ * ekv_view_build -- the per-row keep decision and the compacted block-table view, in one kernel.
+ *
+ * Ranking mode (keep == NULL): row r keeps its pins (as in ekv_allocate_quotas, recent_blocks >= -1)
+ * and the quota[r]
+ * best unpinned blocks among its first row_blocks[r], ranked by max(scores, 0) (float32, NaN as 0)
+ * under `policy` -- the per-request ranking of allocation.py:89 (uniform) and :107-113 (sum, one
+ * request) -- or the newest ones (EKV_POLICY_NEWEST); blocks at or beyond row_blocks[r] are kept,
+ * and quota[r] < 0 keeps every block. mask_out (optional, uint8 [rows][width]) receives this mask,
+ * the row the controller commits (controller.py:401, :445).
+ * Mask mode (keep != NULL, uint8): the committed mask is `keep`.
+ * Then, as DecodeView.build (runtime/block_view.py:272-292): rows with full_rows[r] != 0 keep every
+ * block, released blocks (optional uint8 mask) are dropped, and compact_block_table
+ * (runtime/block_view.py:36-56) keeps block 0 and the last block of ceil(seq_lens/block_size),
+ * writes the kept blocks in order followed by the others in order into view, and
+ * view_lens = (kept - 1) * block_size + tokens of the last block (0 for an empty row).
+ * width <= 32768.
+ */
+int ekv_view_build(const int32_t* table, int64_t table_stride, const int32_t* seq_lens,
+                   const int32_t* row_blocks, const int32_t* quota, const int32_t* measured_blocks,
+                   int recent_blocks, const float* scores, int64_t score_stride, int policy,
+                   const uint8_t* keep, int64_t keep_stride, const uint8_t* full_rows,
+                   const uint8_t* released, int64_t released_stride, int rows, int width,
+                   int block_size, int32_t* view, int64_t view_stride, int32_t* view_lens,
+                   uint8_t* mask_out, int64_t mask_stride, void* stream);
+
+/*
+ * ekv_compact_block_table -- compact_block_table (runtime/block_view.py:36-56) on the device:
+ * ekv_view_build in mask mode with no full rows and no released blocks.
+ */
+int ekv_compact_block_table(const int32_t* table, int64_t table_stride, const int32_t* seq_lens,
+                            const uint8_t* keep, int64_t keep_stride, int rows, int width,
+                            int block_size, int32_t* view, int64_t view_stride,
+                            int32_t* view_lens, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* EKV_B200_H */

@@ -1,0 +1,138 @@
+"""Allocate a read budget across requests by the attention each block carries, on the device.
+
+Drop-in for observe/allocation.py of the reference: ``Objective``, ``Request`` and ``allocate``
+keep their names, signature, pins, validation and tie rules. ``uniform`` gives every request the
+same fraction of its unpinned blocks by largest remainder (equal remainders to the earlier request)
+and keeps each request's best blocks by its own shares, equal shares to the older block
+(allocation.py:79-91). ``sum`` keeps the unpinned blocks with the largest weighted share, equal
+shares to the newer block (:94-118). The quotas and the per-request top-k selection run in the
+sm_100a kernels ``ekv_allocate_quotas`` and ``ekv_view_build``.
+
+Device ranking compares max(score, 0) as float32. For float32-exact scores that is the reference's
+ranking by float64 shares exactly: dividing distinct float32 values by the same total keeps them
+distinct and ordered, and equal values stay equal. Scores that float32 cannot hold exactly,
+``sum`` over several requests (a global top-k), and ``maxmin`` are not implemented on the device
+and raise ``RuntimeError``; NaN scores count as 0, as the controller passes them (controller.py:337).
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+from dataclasses import dataclass
+from typing import Literal
+
+import numpy as np
+import torch
+
+from .. import _lib
+
+Objective = Literal["sum", "maxmin", "uniform"]
+_POLICIES = {"sum": _lib.POLICY_SUM, "uniform": _lib.POLICY_UNIFORM, "newest": _lib.POLICY_NEWEST}
+
+
+@dataclass(frozen=True)
+class Request:
+    """One request: the score of each of its blocks, and how much its retained share counts."""
+
+    scores: np.ndarray
+    weight: float = 1.0
+    pinned: np.ndarray | None = None
+
+    def pinned_mask(self) -> np.ndarray:
+        if self.pinned is not None:
+            return np.asarray(self.pinned, dtype=bool)
+        mask = np.zeros(len(self.scores), dtype=bool)
+        mask[[0, -1]] = len(self.scores) > 0
+        return mask
+
+    def shares(self) -> np.ndarray:
+        """Scores normalised to sum to 1 (float64). A request with no evidence gets equal shares."""
+        scores = np.maximum(np.asarray(self.scores, dtype=np.float64), 0.0)
+        total = scores.sum()
+        if total <= 0.0:
+            return np.full(len(scores), 1.0 / max(len(scores), 1))
+        return scores / total
+
+
+def _pin_start(pinned: np.ndarray) -> int:
+    """``ps`` with pinned == {0} | [ps, n) (the controller's pins); RuntimeError for other pin sets."""
+    n = len(pinned)
+    if n == 0:
+        return 0
+    tail = n
+    while tail > 0 and pinned[tail - 1]:
+        tail -= 1
+    expected = np.zeros(n, dtype=bool)
+    expected[0] = True
+    expected[tail:] = True
+    if not np.array_equal(pinned, expected):
+        raise RuntimeError("the device allocation supports pins of block 0 and a newest suffix only")
+    return tail
+
+
+def allocate(requests: Sequence[Request], budget: int, objective: Objective = "sum") -> list[np.ndarray]:
+    """Return, for each request, a bool mask of the blocks to keep. At most ``budget`` blocks are kept."""
+    sizes = [len(r.scores) for r in requests]
+    pinned = [r.pinned_mask() for r in requests]
+    if any(len(p) != n for p, n in zip(pinned, sizes, strict=True)):
+        raise ValueError("a pinned mask must have one entry per block")
+    if budget < 0:
+        raise ValueError("the budget cannot be negative")
+    must = sum(int(p.sum()) for p in pinned)
+    if must > budget and budget < sum(sizes):
+        raise ValueError(f"the budget {budget} cannot hold the {must} pinned blocks")
+    if budget >= sum(sizes):
+        return [np.ones(n, dtype=bool) for n in sizes]
+    if objective not in ("sum", "maxmin", "uniform"):
+        raise ValueError(f"unknown objective {objective!r}")
+    if objective in ("maxmin", "uniform") and any(r.weight != 1.0 for r in requests):
+        raise ValueError(f"the {objective} objective does not use request weights")
+    if objective == "maxmin":
+        raise RuntimeError("the maxmin objective is not implemented on the device")
+    if objective == "sum" and len(requests) > 1:
+        raise RuntimeError("`sum` over several requests needs a global top-k, not implemented on the device")
+    free = budget - must
+    width = max(sizes) if sizes else 0
+    rows = len(requests)
+    if rows == 0 or width == 0:
+        return [p.copy() for p in pinned]
+    scores = np.zeros((rows, width), dtype=np.float32)
+    for r, req in enumerate(requests):
+        s = np.asarray(req.scores, dtype=np.float64)
+        finite = ~np.isnan(s)
+        s32 = np.where(finite, s, 0.0).astype(np.float32)
+        if not np.array_equal(s32.astype(np.float64)[finite], s[finite]):
+            raise RuntimeError("the device ranking needs scores that float32 holds exactly")
+        if objective == "sum" and req.weight < 0.0:
+            raise RuntimeError("negative request weights are not supported on the device")
+        if objective == "sum" and req.weight == 0.0:
+            s32[:] = 0.0  # every gain is 0: all tie
+        scores[r, : sizes[r]] = s32
+    # pins {0} | [pin_start, n): passed as the "measured" start, with no recent pins of their own
+    pin_starts = torch.tensor([_pin_start(p) for p in pinned], dtype=torch.int32)
+    device = torch.device("cuda", torch.cuda.current_device())
+    lib = _lib.load()
+    stream = _lib.current_stream()
+    row_blocks = torch.tensor(sizes, dtype=torch.int32).to(device)
+    measured = pin_starts.to(device)
+    quota = torch.empty(rows, dtype=torch.int32, device=device)
+    if objective == "uniform":
+        rc = lib.ekv_allocate_quotas(row_blocks.data_ptr(), measured.data_ptr(), -1, -1, 0.0, int(budget), None,
+                                     _lib.POLICY_UNIFORM, rows, quota.data_ptr(), stream)
+        _lib.check(rc, "ekv_allocate_quotas")
+    else:
+        quota.fill_(int(free))
+    scores_t = torch.from_numpy(scores).to(device)
+    table = torch.zeros(rows, width, dtype=torch.int32, device=device)
+    lens = torch.zeros(rows, dtype=torch.int32, device=device)
+    view = torch.empty(rows, width, dtype=torch.int32, device=device)
+    view_lens = torch.empty(rows, dtype=torch.int32, device=device)
+    mask = torch.empty(rows, width, dtype=torch.uint8, device=device)
+    rc = lib.ekv_view_build(
+        table.data_ptr(), width, lens.data_ptr(), row_blocks.data_ptr(), quota.data_ptr(), measured.data_ptr(),
+        -1, scores_t.data_ptr(), width, _POLICIES[objective], None, 0, None, None, 0, rows, width, 16,
+        view.data_ptr(), width, view_lens.data_ptr(), mask.data_ptr(), width, stream,
+    )
+    _lib.check(rc, "ekv_view_build")
+    out = mask.cpu().numpy().astype(bool)
+    return [out[r, : sizes[r]].copy() for r in range(rows)]

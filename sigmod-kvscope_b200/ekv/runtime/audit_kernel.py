@@ -1,0 +1,258 @@
+"""The attention-share statistic recorded by the sm_100a audit kernel, for any attention backend.
+
+Drop-in for runtime/audit_kernel.py of the reference: ``TILE_BLOCKS`` and ``RecordingPlane`` keep
+their names, constructor, methods, table layout, NaN initialisation, descriptor files and
+exceptions. For one KV group per layer (group ``layer % kv_heads``, as the reference samples) and
+only for the rows of an audit step, the kernel records
+
+  m[layer][row][block][query row] = the largest score over the keys of the block's tile
+  l[layer][row][block][query row] = the sum of exp(score - m) over those keys
+
+and, in the same launch, folds the layer into the exact per-block attention share of each row
+(``shares()``), which the reference computed later on the host (observe/tile_shares.py). The launch
+is the same on every step (the flag is read on the device), so a CUDA graph can capture it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+
+import numpy as np
+import torch
+
+from .. import _lib
+from .audit import AuditPlane, runtime_dir
+
+TILE_BLOCKS = 2  # blocks per tile: one value per tile, as the reference kernel records
+
+_DTYPES = {torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16}
+_AGGREGATES = {"mean": _lib.AGG_MEAN, "max": _lib.AGG_MAX}
+
+
+def pub_path(pid: int) -> str:
+    return f"{runtime_dir()}/ekv_pass_{pid}.json"
+
+
+class RecordingPlane(AuditPlane):
+    """An audit plane whose statistic block is allocated here and recorded by the audit kernel.
+
+    ``heads`` > 1 records that many KV heads per layer side by side in a cell (all-heads mode,
+    ``group_rows`` then counts the query rows of one KV head); 1 is the reference's sampling.
+    ``aggregate`` chooses how the fused shares combine layers and query rows ("mean" or "max").
+    """
+
+    def __init__(
+        self,
+        layers: int,
+        rows: int,
+        width: int,
+        group_rows: int,
+        block_size: int,
+        *,
+        heads: int = 1,
+        aggregate: str = "mean",
+    ) -> None:
+        super().__init__()
+        if group_rows > 16:
+            raise ValueError(f"{group_rows} query heads per KV head: the kernel handles at most 16")
+        if (block_size * TILE_BLOCKS) & (block_size * TILE_BLOCKS - 1):
+            raise ValueError("a tile of the audit kernel must hold a power of two of tokens")
+        if aggregate not in _AGGREGATES:
+            raise ValueError(f"unknown aggregate {aggregate!r}")
+        if heads < 1:
+            raise ValueError("heads must be positive")
+        self._layers = layers
+        self.rows, self.width, self.group_rows, self.block_size = rows, width, group_rows, block_size
+        self.heads = heads
+        self.cell = heads * group_rows  # values per (layer, row, block)
+        self.aggregate = aggregate
+        self._layer_of: dict[str, int] = {}  # layer name -> number, in the order the layers first run
+        self._lib = _lib.load()
+        lse_bytes = 2 * layers * rows * width * self.cell * 4
+        self._lse = self._allocate(lse_bytes)
+        self._cuda.cudaMemset(ctypes.c_void_p(self._lse), 0xFF, ctypes.c_size_t(lse_bytes))  # NaN: unwritten
+        self._flag_dev = self._allocate(4)
+        self._table_dev = self._allocate(layers * 8)
+        self._cuda.cudaMemset(ctypes.c_void_p(self._flag_dev), 0, ctypes.c_size_t(4))
+        self._cuda.cudaMemset(ctypes.c_void_p(self._table_dev), 0, ctypes.c_size_t(layers * 8))
+        device = torch.device("cuda", torch.cuda.current_device())
+        self._select = torch.zeros(rows, dtype=torch.uint8, device=device)
+        self._token = torch.zeros(rows, dtype=torch.int32, device=device)
+        # the fused share: accumulator, contributors, final shares, and the kernel's workspace
+        self._share_acc = torch.zeros(rows, width, dtype=torch.float32, device=device)
+        self._contributors = torch.zeros(rows, dtype=torch.int32, device=device)
+        self._share = torch.full((rows, width), float("nan"), dtype=torch.float32, device=device)
+        self._workspace_bytes = int(
+            self._lib.ekv_audit_workspace_bytes(rows, width, group_rows, heads, block_size, TILE_BLOCKS)
+        )
+        self._workspace = torch.zeros(self._workspace_bytes + 256, dtype=torch.uint8, device=device)
+        self._status = torch.zeros(1, dtype=torch.int32, device=device)
+        torch.cuda.synchronize()
+        self._publish()
+
+    # -- device memory of the statistic block (cudaMalloc, so that it can be exported by IPC) -------
+
+    def _allocate(self, size: int) -> int:
+        pointer = ctypes.c_void_p()
+        rc = self._cuda.cudaMalloc(ctypes.byref(pointer), ctypes.c_size_t(size))
+        if rc != 0 or pointer.value is None:
+            raise RuntimeError(f"cudaMalloc of {size} bytes failed with code {rc}")
+        return pointer.value
+
+    def _ipc(self, address: int) -> str:
+        handle = (ctypes.c_ubyte * 64)()
+        rc = self._cuda.cudaIpcGetMemHandle(ctypes.byref(handle), ctypes.c_void_p(address))
+        if rc != 0:
+            raise RuntimeError(f"cudaIpcGetMemHandle failed with code {rc}")
+        return bytes(handle).hex()
+
+    def _publish(self) -> None:
+        """Descriptor lines in the reference's format, so a controller reads this block unchanged."""
+        entry = {
+            "host_va": self._lse,
+            "ncap": self.width,
+            "max_rows": self.rows,
+            "tile_lse_dev": self._lse,
+            "tile_lse_ipc": self._ipc(self._lse),
+            "tile_lse_layers": self._layers,
+            "tile_lse_group_rows": self.cell,
+            "stat_flag_dev": self._flag_dev,
+            "layer_table_dev": self._table_dev,
+            "layer_table_ipc": self._ipc(self._table_dev),
+        }
+        path = pub_path(self.pid)
+        with open(path, "a") as f:
+            f.write(json.dumps(entry) + "\n")
+        os.chmod(path, 0o600)
+        coverage = {"host_va": self._lse, "attn_share_tile_blocks": TILE_BLOCKS}
+        with open(path.replace("ekv_pass_", "ekv_coverage_"), "a") as f:
+            f.write(json.dumps(coverage) + "\n")
+
+    def _discover(self) -> bool:
+        return True  # the block exists from construction
+
+    def close(self) -> None:
+        """Free the cudaMalloc blocks (the tensors go with the object)."""
+        for address in (self._lse, self._flag_dev, self._table_dev):
+            if address:
+                self._cuda.cudaFree(ctypes.c_void_p(address))
+        self._lse = self._flag_dev = self._table_dev = 0
+
+    # -- the engine-facing calls -------------------------------------------------------------------
+
+    @property
+    def layer_names(self) -> list[str]:
+        """The attention layers in the order they first ran, which is their layer number."""
+        return sorted(self._layer_of, key=lambda name: self._layer_of[name])
+
+    def select(self, audited: np.ndarray, token_start: np.ndarray) -> None:
+        """Choose the rows to record in the next step, and the token index of each row's query."""
+        rows = len(audited)
+        self._select[:rows].copy_(torch.from_numpy(np.asarray(audited).astype(np.uint8)))
+        self._token[:rows].copy_(torch.from_numpy(np.asarray(token_start).astype(np.int32)))
+
+    def record(
+        self,
+        layer_name: str,
+        table: torch.Tensor,
+        lens: torch.Tensor,
+        query: torch.Tensor,
+        kv_cache: torch.Tensor,
+        scale: float,
+    ) -> None:
+        """Launch the kernel for one attention layer, after the layer has attended.
+
+        A layer is numbered by its name in the order the layers first run (cache addresses are not
+        stable while the engine profiles memory; names are). ``kv_cache`` is [blocks, 2, block, heads, dim].
+        """
+        if kv_cache.ndim != 5 or kv_cache.shape[1] != 2:
+            raise ValueError(f"expected a KV cache [blocks, 2, block, heads, dim], got {tuple(kv_cache.shape)}")
+        if kv_cache.shape[2] != self.block_size:
+            raise ValueError("the KV cache's block size differs from the view's")
+        layer = self._layer_of.setdefault(layer_name, len(self._layer_of))
+        self.launch(layer, table, lens, query, kv_cache[:, 0], scale)
+
+    def launch(
+        self,
+        layer: int,
+        table: torch.Tensor,
+        lens: torch.Tensor,
+        query: torch.Tensor,
+        keys: torch.Tensor,
+        scale: float,
+        stream: int | None = None,
+    ) -> None:
+        """Launch the kernel for ``layer``; ``keys`` is the layer's key cache [blocks, block, heads, dim].
+
+        Layer 0 starts the audit step's share accumulation and the plane's last layer finalises it.
+        """
+        if layer >= self._layers:
+            raise RuntimeError(f"more attention layers ran than the {self._layers} the plane was sized for")
+        kv_heads, dim = keys.shape[2], keys.shape[3]
+        if kv_heads * self.group_rows != query.shape[1] or dim != query.shape[2]:
+            raise ValueError("the query and KV cache shapes do not match the plane's group size")
+        if query.dtype not in _DTYPES or keys.dtype != query.dtype:
+            raise ValueError(f"query and keys must both be float16 or bfloat16, got {query.dtype}, {keys.dtype}")
+        if query.stride(2) != 1 or keys.stride(3) != 1:
+            raise ValueError("the head dimension of the query and the keys must be contiguous")
+        if table.dtype != torch.int32 or lens.dtype != torch.int32:
+            raise ValueError("the block table and the lengths must be int32")
+        if table.shape[1] != self.width or table.shape[0] < self.rows or lens.shape[0] < self.rows:
+            raise ValueError("the block table does not match the plane's rows and width")
+        if self.heads == 1:
+            group = layer % kv_heads
+        else:
+            if self.heads != kv_heads:
+                raise ValueError(f"an all-heads plane of {self.heads} heads got a cache of {kv_heads}")
+            group = 0
+        flags = (_lib.SHARE_RESET if layer == 0 else 0) | (_lib.SHARE_FINALIZE if layer == self._layers - 1 else 0)
+        workspace = (self._workspace.data_ptr() + 255) // 256 * 256
+        rc = self._lib.ekv_audit_launch(
+            query.data_ptr(), keys.data_ptr(), table.data_ptr(), lens.data_ptr(), self._token.data_ptr(),
+            self._select.data_ptr(), self._flag_dev, self._lse, float(scale), layer, group,
+            query.stride(0), query.stride(1), keys.stride(0), keys.stride(1), keys.stride(2), table.stride(0),
+            self._layers, self.rows, self.width, self.group_rows, self.block_size, TILE_BLOCKS, dim,
+            _DTYPES[query.dtype], self.heads, kv_heads, keys.shape[0], query.shape[0],
+            self._share_acc.data_ptr(), self._contributors.data_ptr(), self._share.data_ptr(),
+            _AGGREGATES[self.aggregate], flags, workspace, self._workspace_bytes, self._status.data_ptr(),
+            _lib.current_stream() if stream is None else stream,
+        )
+        _lib.check(rc, "ekv_audit_launch")
+
+    # -- what the fused launch leaves behind --------------------------------------------------------
+
+    def shares(self) -> torch.Tensor:
+        """The attention share per (row, block) of the last completed audit step, float32 on the device.
+
+        A row not audited in that step, or with no data, is NaN; every other row sums to 1. It equals
+        normalize_tile_lse over the step's cells with row_blocks = ceil(lens / block_size).
+        """
+        return self._share
+
+    def status(self) -> int:
+        """The EKV_STATUS_* bits the kernel raised since the last ``clear_status`` (synchronises)."""
+        return int(self._status.item())
+
+    def clear_status(self) -> None:
+        self._status.zero_()
+
+    def table(self) -> torch.Tensor:
+        """A view of the statistic table [2, layers, rows, width, cell] as a float32 tensor (no copy)."""
+        return _wrap(self._lse, (2, self._layers, self.rows, self.width, self.cell))
+
+
+def _wrap(address: int, shape: tuple[int, ...]) -> torch.Tensor:
+    """A float32 tensor over device memory this process allocated with cudaMalloc (no ownership)."""
+
+    class _Array:
+        __cuda_array_interface__ = {
+            "shape": shape,
+            "typestr": "<f4",
+            "data": (address, False),
+            "version": 3,
+            "strides": None,
+        }
+
+    return torch.as_tensor(_Array(), device=torch.device("cuda", torch.cuda.current_device()))

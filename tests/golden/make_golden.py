@@ -1,0 +1,238 @@
+"""Generate the golden fixtures of tests/golden/ by running the reference's own code.
+
+Run in a container that has the reference checkout (default /root/reference, or $EKV_REFERENCE):
+
+    python tests/golden/make_golden.py
+
+It imports the reference read-only and runs, on CPU:
+  * its Triton audit kernel ``tile_lse_kernel`` (runtime/audit_kernel.py:34-109) under
+    ``TRITON_INTERPRET=1``, launched as RecordingPlane.launch does (:239-265). bf16 cases are run on
+    the exact float32 upcast, because the interpreter's ``tl.dot`` on bf16 is wrong;
+  * ``read_tile_rows`` and ``normalize_tile_lse`` (observe/tile_shares.py) through a fake D2H reader;
+  * ``allocate`` (observe/allocation.py) with the pins and budget of Controller._allocate;
+  * ``compact_block_table`` (runtime/block_view.py:36-56).
+Inputs are seeded; the fixtures hold inputs and outputs, so the tests never need the reference.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import sys
+
+os.environ["TRITON_INTERPRET"] = "1"
+REFERENCE = os.environ.get("EKV_REFERENCE", "/root/reference")
+sys.path.insert(0, REFERENCE)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import triton  # noqa: E402
+from observe.allocation import Request, allocate  # noqa: E402
+from observe.tile_shares import normalize_tile_lse, read_tile_rows  # noqa: E402
+from runtime.audit_kernel import TILE_BLOCKS, tile_lse_kernel  # noqa: E402
+from runtime.block_view import compact_block_table  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def reference_launch(lse, layers, rows, width, group_rows, block_size, layer, table, lens, query, keys,
+                     scale, token, select, flag):
+    """tile_lse_kernel launched with the arguments RecordingPlane.launch gives it, on CPU tensors."""
+    kv_heads = keys.shape[2]
+    tile_lse_kernel[(rows, triton.cdiv(width, TILE_BLOCKS))](
+        query, keys, table, lens, token, select, flag, lse, scale, layer, layer % kv_heads,
+        query.stride(0), query.stride(1), keys.stride(0), keys.stride(1), keys.stride(2), table.stride(0),
+        rows * width * group_rows, width * group_rows, layers * rows * width * group_rows,
+        BLOCK_SIZE=block_size, TILE_BLOCKS=TILE_BLOCKS, GROUP_ROWS=group_rows, ROWS_PAD=16,
+        HEAD_DIM=keys.shape[3],
+    )
+
+
+class FakeCuda:
+    """Serves the D2H reads of read_tile_rows from a host copy of the table."""
+
+    def __init__(self, blob: bytes) -> None:
+        self.blob = blob
+
+    def d2h_many(self, requests):
+        return [self.blob[a : a + n] for a, n in requests]
+
+
+def audit_case(name, seed, rows, q_heads, kv_heads, layers, len_lo, len_hi, pool, dtype, select=None,
+               flags=None, width=None, block_size=16):
+    rng = np.random.default_rng(seed)
+    head_dim = 128
+    group_rows = q_heads // kv_heads
+    lens = rng.integers(len_lo, len_hi + 1, rows).astype(np.int32)
+    width = width or int(math.ceil(lens.max() / block_size)) + 2
+    perm = rng.permutation(pool).astype(np.int32)
+    table = perm[(np.arange(rows)[:, None] * width + np.arange(width)[None, :]) % pool].astype(np.int32)
+    tokens = rows + 3
+    qrow = rng.permutation(tokens)[:rows].astype(np.int32)
+    select = np.ones(rows, dtype=np.uint8) if select is None else np.asarray(select, dtype=np.uint8)
+    flags = [1] * layers if flags is None else flags
+    scale = 1.0 / math.sqrt(head_dim)
+    np_dtype = np.float16 if dtype == "fp16" else np.float32
+    queries, pools = [], []
+    for _layer in range(layers):
+        q = rng.standard_normal((tokens, q_heads, head_dim)).astype(np.float32)
+        k = np.zeros((pool, block_size, kv_heads, head_dim), dtype=np.float32)  # unused blocks stay 0
+        used = np.unique(np.concatenate([table[r, : -(-int(lens[r]) // block_size)] for r in range(rows)]))
+        k[used] = rng.standard_normal((len(used), block_size, kv_heads, head_dim)).astype(np.float32)
+        if dtype == "bf16":  # values exactly representable in bf16
+            q = torch.from_numpy(q).to(torch.bfloat16).float().numpy()
+            k = torch.from_numpy(k).to(torch.bfloat16).float().numpy()
+        queries.append(q.astype(np_dtype))
+        pools.append(k.astype(np_dtype))
+    lse = torch.full((2 * layers * rows * width * group_rows,), float("nan"), dtype=torch.float32)
+    t_table, t_lens = torch.from_numpy(table), torch.from_numpy(lens)
+    t_token, t_select = torch.from_numpy(qrow), torch.from_numpy(select)
+    for layer in range(layers):
+        flag = torch.tensor([flags[layer]], dtype=torch.int32)
+        q = torch.from_numpy(queries[layer].astype(np.float16 if dtype == "fp16" else np.float32))
+        k = torch.from_numpy(pools[layer].astype(np.float16 if dtype == "fp16" else np.float32))
+        kv = torch.stack([k, torch.zeros_like(k)], dim=1)  # [blocks, 2, block, heads, dim], as vLLM's cache
+        reference_launch(lse, layers, rows, width, group_rows, block_size, layer, t_table, t_lens, q,
+                         kv[:, 0], scale, t_token, t_select, flag)
+    lse_np = lse.numpy().reshape(2, layers, rows, width, group_rows)
+    row_blocks = np.where(select != 0, -(-lens // block_size), 0).astype(np.int64)
+    live = np.flatnonzero(row_blocks > 0)
+    u = read_tile_rows(FakeCuda(lse.numpy().tobytes()), 0, layers, layers, rows, width, group_rows, live, TILE_BLOCKS)
+    out = {}
+    for aggregate in ("mean", "max"):
+        share = np.full((rows, width), np.nan)
+        if live.size:
+            share[live] = normalize_tile_lse(u, row_blocks[live], TILE_BLOCKS, aggregate)
+        out[f"share_{aggregate}"] = share
+    # the controller's uniform keep mask at budget 0.5 with its default pins, and the view
+    recent = 4
+    requests, chosen = [], []
+    for r in range(rows):
+        n = int(row_blocks[r])
+        if n <= 0:
+            continue
+        pinned = np.zeros(n, dtype=bool)
+        pinned[0] = True
+        pinned[max(0, n - 1 - recent):] = True
+        requests.append(Request(scores=np.nan_to_num(out["share_mean"][r, :n], nan=0.0), pinned=pinned))
+        chosen.append(r)
+    keep = np.ones((rows, width), dtype=np.uint8)
+    if requests:
+        total = sum(len(q.scores) for q in requests)
+        floor = sum(int(q.pinned_mask().sum()) for q in requests)
+        budget = max(floor, int(np.ceil(0.5 * total)))
+        for r, mask in zip(chosen, allocate(requests, budget, "uniform"), strict=True):
+            keep[r, : len(mask)] = mask
+    view, view_lens = compact_block_table(t_table, t_lens, torch.from_numpy(keep.astype(bool)), block_size)
+    def packed(x):  # fp16 as is; bf16-exact float32 as its upper 16 bits
+        x = np.stack(x)
+        return x if dtype == "fp16" else (x.astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+
+    np.savez_compressed(
+        os.path.join(HERE, f"{name}.npz"),
+        query=packed(queries), keys=packed(pools), table=table, lens=lens,
+        qrow=qrow, select=select, flags=np.asarray(flags, dtype=np.int32), scale=np.float32(scale),
+        block_size=block_size, tile_blocks=TILE_BLOCKS, kv_heads=kv_heads, group_rows=group_rows,
+        dtype=dtype, lse=lse_np, u=u, live=live, row_blocks=row_blocks, keep=keep,
+        view=view.numpy(), view_lens=view_lens.numpy(), **out,
+    )
+    print(name, "rows", rows, "width", width, "layers", layers, "written")
+
+
+def shares_cases():
+    """normalize_tile_lse on random u tables with NaN, -inf, partial tails and empty rows."""
+    rng = np.random.default_rng(11)
+    cases = {}
+    for i in range(12):
+        layers, rows, width, q = int(rng.integers(1, 5)), int(rng.integers(1, 7)), int(rng.integers(1, 30)), int(rng.integers(1, 9))
+        tile_blocks = int(rng.choice([1, 2, 4]))
+        u = rng.normal(0, 4, (layers, rows, width, q)).astype(np.float32)
+        u[rng.random(u.shape) < 0.1] = np.nan
+        u[rng.random(u.shape) < 0.05] = -np.inf
+        row_blocks = rng.integers(0, width + 3, rows)
+        if i % 4 == 0:
+            u[:, 0] = np.nan  # a row with no evidence
+        cases[f"u{i}"] = u
+        cases[f"rb{i}"] = row_blocks
+        cases[f"tb{i}"] = np.int64(tile_blocks)
+        for aggregate in ("mean", "max"):
+            cases[f"{aggregate}{i}"] = normalize_tile_lse(u, row_blocks, tile_blocks, aggregate)
+    # read_tile_rows over a table with a tile of no keys (l = 0)
+    table_layers, layers, rows, width, group, tile_blocks = 4, 3, 5, 6, 2, 2
+    cells = table_layers * rows * width * group
+    m = rng.normal(0, 3, cells).astype(np.float32)
+    total = rng.uniform(0.5, 9, cells).astype(np.float32)
+    total[7] = 0.0
+    blob = np.concatenate([m, total])
+    cases["read_table"] = blob
+    cases["read_rows"] = np.array([0, 2, 3])
+    cases["read_u"] = read_tile_rows(FakeCuda(blob.tobytes()), 0, table_layers, layers, rows, width, group,
+                                     cases["read_rows"], tile_blocks)
+    np.savez_compressed(os.path.join(HERE, "shares_cases.npz"), **cases)
+    print("shares_cases written")
+
+
+def allocation_cases():
+    """allocate() with many ties: uniform over several requests, sum over one and over several."""
+    rng = np.random.default_rng(21)
+    cases = {}
+    for i in range(60):
+        n_req = int(rng.integers(1, 6))
+        sizes = rng.integers(1, 40, n_req)
+        ties = i % 2 == 0
+        scores = [
+            (rng.integers(0, 4, n).astype(np.float32) if ties else rng.random(n).astype(np.float32)).astype(np.float64)
+            for n in sizes
+        ]
+        if i % 7 == 3:
+            scores[0][:] = 0.0  # no evidence: equal shares
+        recent = int(rng.integers(0, 5))
+        pinned = []
+        for n in sizes:
+            p = np.zeros(n, dtype=bool)
+            p[0] = True
+            p[max(0, n - 1 - recent):] = True
+            pinned.append(p)
+        must = sum(int(p.sum()) for p in pinned)
+        total = int(sizes.sum())
+        budget = int(rng.integers(must, total + 2))
+        objective = "uniform" if i % 3 else "sum"
+        requests = [Request(scores=s, pinned=p) for s, p in zip(scores, pinned, strict=True)]
+        masks = allocate(requests, budget, objective)
+        cases[f"sizes{i}"] = sizes
+        cases[f"scores{i}"] = np.concatenate(scores)
+        cases[f"recent{i}"] = np.int64(recent)
+        cases[f"budget{i}"] = np.int64(budget)
+        cases[f"objective{i}"] = objective
+        cases[f"mask{i}"] = np.concatenate(masks)
+    # keep-newest: the fixed rule scores = arange(n), budget 0.5, no recent pins, 10 blocks
+    req = Request(scores=np.arange(10, dtype=float), pinned=np.eye(1, 10, 0, dtype=bool)[0] | np.eye(1, 10, 9, dtype=bool)[0])
+    cases["newest_mask"] = allocate([req], max(2, int(np.ceil(0.5 * 10))), "uniform")[0]
+    np.savez_compressed(os.path.join(HERE, "allocation_cases.npz"), **cases)
+    print("allocation_cases written")
+
+
+def view_cases():
+    """compact_block_table on 300 random batches, as the reference's own randomized check draws them."""
+    rng = np.random.default_rng(31)
+    cases = {}
+    for i in range(300):
+        rows, width = int(rng.integers(1, 7)), int(rng.integers(1, 41))
+        table = rng.integers(1, 10_000, (rows, width)).astype(np.int32)
+        lens = rng.integers(0, width * 16 + 1, rows).astype(np.int32)
+        keep = rng.random((rows, width)) < 0.5
+        view, view_lens = compact_block_table(torch.from_numpy(table), torch.from_numpy(lens), torch.from_numpy(keep), 16)
+        cases[f"table{i}"], cases[f"lens{i}"], cases[f"keep{i}"] = table, lens, keep
+        cases[f"view{i}"], cases[f"view_lens{i}"] = view.numpy(), view_lens.numpy()
+    np.savez_compressed(os.path.join(HERE, "view_cases.npz"), **cases)
+    print("view_cases written")
+
+
+if __name__ == "__main__":
+    audit_case("audit_cfg1_fp16", 0, rows=4, q_heads=8, kv_heads=2, layers=1, len_lo=100, len_hi=600, pool=256, dtype="fp16")
+    audit_case("audit_layers_fp16", 1, rows=6, q_heads=8, kv_heads=2, layers=3, len_lo=1, len_hi=300, pool=256,
+               dtype="fp16", select=[1, 1, 0, 1, 1, 1], flags=[1, 0, 1])
+    audit_case("audit_g8_bf16", 2, rows=5, q_heads=16, kv_heads=2, layers=2, len_lo=5, len_hi=200, pool=128, dtype="bf16")
+    shares_cases()
+    allocation_cases()
+    view_cases()

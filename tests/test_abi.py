@@ -1,0 +1,122 @@
+"""The C ABI: the library loads, exports every function include/ekv_b200.h declares, and rejects
+bad arguments with the documented codes before it touches a device. CPU only."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+from conftest import ROOT
+
+import ekv._lib as L
+
+HEADER = os.path.join(ROOT, "include", "ekv_b200.h")
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(ekv_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import ekv.build
+
+    ekv.build.build()
+    return L.load()
+
+
+def test_every_declared_function_is_exported_and_bound(lib):
+    names = declared_functions()
+    assert "ekv_audit_launch" in names and "ekv_view_build" in names
+    for name in names:
+        assert hasattr(lib, name), f"{name} is declared but not exported"
+        assert name in L.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_constants_agree_with_the_header():
+    text = open(HEADER).read()
+    defines = dict(re.findall(r"#define\s+(EKV_[A-Z0-9_]+)\s+\(?(-?\d+)u?\)?", text))
+    assert int(defines["EKV_EINVAL"]) == L.EINVAL and int(defines["EKV_ENOTSUP"]) == L.ENOTSUP
+    assert int(defines["EKV_SHARE_RESET"]) == L.SHARE_RESET and int(defines["EKV_SHARE_FINALIZE"]) == L.SHARE_FINALIZE
+    assert int(defines["EKV_POLICY_SUM"]) == L.POLICY_SUM and int(defines["EKV_POLICY_NEWEST"]) == L.POLICY_NEWEST
+    assert int(defines["EKV_AUDIT_CHUNK_TILES"]) == L.AUDIT_CHUNK_TILES
+    assert int(defines["EKV_DTYPE_BF16"]) == L.DTYPE_BF16
+
+
+def test_workspace_size(lib):
+    # tickets (rows * 4 rounded to 256) + rows * chunks * heads * G * 8 bytes
+    rows, width, g, heads = 64, 512, 4, 1
+    chunks = -(-(-(-width // 2)) // L.AUDIT_CHUNK_TILES)
+    assert lib.ekv_audit_workspace_bytes(rows, width, g, heads, 16, 2) == 256 + rows * chunks * heads * g * 8
+    assert lib.ekv_audit_workspace_bytes(0, width, g, heads, 16, 2) == 0
+
+
+def audit_args(**over):
+    fake = ctypes.c_void_p(0x1000)  # never dereferenced: validation fails first
+    args = dict(
+        q=fake, k=ctypes.c_void_p(0x2000), table=fake, lens=fake, qrow=fake, select=fake, flag=fake, lse=fake,
+        scale=0.1, layer=0, group=0, qs0=1024, qs1=128, ks0=4096, ks1=256, ks2=128, ts=8,
+        layers=1, rows=4, width=8, G=4, bs=16, tb=2, D=128, dtype=L.DTYPE_BF16, heads=1, kv_heads=2,
+        pool=256, q_tokens=8, acc=None, contrib=None, out=None, agg=L.AGG_MEAN, flags=0, ws=None, ws_bytes=0,
+        status=None, stream=None,
+    )
+    args.update(over)
+    return list(args.values())
+
+
+@pytest.mark.parametrize(
+    "over, code",
+    [
+        (dict(q=None), L.EINVAL),
+        (dict(layer=1), L.ERANGE),
+        (dict(G=17), L.EINVAL),
+        (dict(group=2), L.EINVAL),
+        (dict(bs=12), L.EINVAL),  # a tile of 24 tokens is not a power of two
+        (dict(D=64), L.ENOTSUP),
+        (dict(dtype=7), L.EINVAL),
+        (dict(ks1=100), L.EINVAL),  # key rows not in whole 16-byte units
+        (dict(ts=4), L.EINVAL),
+        (dict(agg=5), L.EINVAL),
+        (dict(acc=ctypes.c_void_p(0x3000)), L.EINVAL),  # no contributors
+        (dict(acc=ctypes.c_void_p(0x3000), contrib=ctypes.c_void_p(0x4000), ws=None), L.ERANGE),
+    ],
+)
+def test_audit_launch_rejects_bad_arguments(lib, over, code):
+    rc = lib.ekv_audit_launch(*audit_args(**over))
+    assert rc == code
+    assert lib.ekv_last_error_string()
+
+
+def test_error_codes_map_to_the_reference_exceptions(lib):
+    rc = lib.ekv_audit_launch(*audit_args(G=17))
+    with pytest.raises(ValueError, match="16"):
+        L.check(rc, "ekv_audit_launch")
+    rc = lib.ekv_audit_launch(*audit_args(layer=3))
+    with pytest.raises(RuntimeError, match="layer"):
+        L.check(rc, "ekv_audit_launch")
+
+
+def test_other_entry_points_validate_before_launching(lib):
+    fake = ctypes.c_void_p(0x1000)
+    assert lib.ekv_normalize_tile_lse(fake, 1, 1, 1, 1, 1, fake, fake, 1, 2, 9, fake, None, None) == L.EINVAL
+    assert lib.ekv_normalize_tile_lse(fake, 1, 2, 1, 1, 1, fake, fake, 1, 2, 0, fake, None, None) == L.ERANGE
+    assert lib.ekv_normalize_tile_lse(fake, 1, 1, 1, 1, 1, fake, fake, 0, 2, 0, fake, None, None) == L.OK  # no rows
+    assert lib.ekv_normalize_log_weights(fake, 1, 1, 1, 1, fake, 0, 0, fake, None, None) == L.EINVAL
+    assert lib.ekv_share_finalize(None, fake, None, 1, 1, 0, fake, None) == L.EINVAL
+    assert lib.ekv_allocate_quotas(fake, None, 4, 0, 0.5, -1, None, L.POLICY_SUM, 4, fake, None) == L.ENOTSUP
+    assert lib.ekv_allocate_quotas(fake, None, 4, 0, 1.5, -1, None, L.POLICY_UNIFORM, 4, fake, None) == L.EINVAL
+    assert lib.ekv_allocate_quotas(fake, None, 4, 0, 0.5, -1, None, L.POLICY_UNIFORM, 9000, fake, None) == L.ENOTSUP
+    view_args = [fake, 8, fake, fake, fake, None, 0, None, 8, L.POLICY_SUM, None, 0, None, None, 0, 2, 8, 16,
+                 fake, 8, fake, None, 0, None]
+    assert lib.ekv_view_build(*view_args) == L.EINVAL  # ranking by shares without scores
+    view_args[16] = 40000
+    assert lib.ekv_view_build(*view_args) == L.ENOTSUP  # wider than 32768
+    assert lib.ekv_compact_block_table(fake, 8, fake, None, 8, 2, 8, 16, fake, 8, fake, None) == L.EINVAL
+
+
+def test_abi_version(lib):
+    assert lib.ekv_abi_version() == 1

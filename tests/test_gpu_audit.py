@@ -1,0 +1,329 @@
+"""Parity of the sm_100a audit kernel (tile LSE + fused shares) with the reference and the oracle.
+
+Tolerances: the tile values m and l are float32 reductions of float32 dot products whose summation
+order differs from the reference kernel's, so they agree to rtol 1e-4 / atol 1e-4; shares agree with
+the reference normalisation to 1e-3 relative, with atol 1e-9 for shares that
+underflow differently. Cells the reference leaves unwritten must be NaN here too (bit-exact pattern).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+from conftest import load_golden
+
+from oracle import audit as oaud
+from oracle import shares as osh
+
+pytestmark = pytest.mark.gpu
+
+LSE_TOL = dict(rtol=1e-4, atol=1e-4)
+SHARE_TOL = dict(rtol=1e-3, atol=1e-9)
+
+
+def unpack(x: np.ndarray, dtype: str) -> torch.Tensor:
+    if dtype == "fp16":
+        return torch.from_numpy(x.astype(np.float16))
+    return torch.from_numpy((x.astype(np.uint32) << 16).view(np.float32)).to(torch.bfloat16)
+
+
+@pytest.fixture
+def runtime_dir(tmp_path, monkeypatch):
+    monkeypatch.setenv("EKV_RUNTIME_DIR", str(tmp_path))
+    return tmp_path
+
+
+def run_plane_on_golden(g: dict, aggregate: str = "mean"):
+    from ekv.runtime.audit_kernel import RecordingPlane
+
+    dtype = str(g["dtype"])
+    q_all, k_all = unpack(g["query"], dtype), unpack(g["keys"], dtype)
+    layers = q_all.shape[0]
+    rows, width = g["table"].shape
+    plane = RecordingPlane(layers, rows, width, int(g["group_rows"]), int(g["block_size"]), aggregate=aggregate)
+    plane.attach([0x1000 + i for i in range(layers)])
+    plane.select(g["select"].astype(bool), g["qrow"])
+    table = torch.from_numpy(g["table"]).cuda()
+    lens = torch.from_numpy(g["lens"]).cuda()
+    for layer in range(layers):
+        plane.set(bool(g["flags"][layer]))
+        k = k_all[layer].cuda()
+        kv_cache = torch.stack([k, torch.zeros_like(k)], dim=1)
+        plane.record(f"layer.{layer}", table, lens, q_all[layer].cuda(), kv_cache, float(g["scale"]))
+    torch.cuda.synchronize()
+    return plane
+
+
+@pytest.mark.parametrize("name", ["audit_cfg1_fp16", "audit_layers_fp16", "audit_g8_bf16"])
+def test_recording_plane_matches_the_reference_kernel(name, runtime_dir):
+    g = load_golden(name)
+    plane = run_plane_on_golden(g)
+    lse = plane.table().cpu().numpy()
+    ref = g["lse"]
+    assert np.array_equal(np.isnan(lse), np.isnan(ref)), "the written cells differ from the reference's"
+    written = ~np.isnan(ref)
+    np.testing.assert_allclose(lse[written], ref[written], **LSE_TOL)
+    assert plane.status() == 0
+    assert plane.layer_names == [f"layer.{i}" for i in range(ref.shape[1])]
+
+
+@pytest.mark.parametrize("name", ["audit_cfg1_fp16", "audit_layers_fp16", "audit_g8_bf16"])
+@pytest.mark.parametrize("aggregate", ["mean", "max"])
+def test_fused_shares_match_the_reference_normalisation(name, aggregate, runtime_dir):
+    g = load_golden(name)
+    plane = run_plane_on_golden(g, aggregate)
+    share = plane.shares().cpu().numpy().astype(np.float64)
+    ref = g[f"share_{aggregate}"]
+    assert np.array_equal(np.isnan(share), np.isnan(ref))
+    np.testing.assert_allclose(share, ref, equal_nan=True, **SHARE_TOL)
+    live = ~np.isnan(ref).all(axis=1)
+    np.testing.assert_allclose(share[live].sum(axis=1), 1.0, rtol=1e-5)
+
+
+def test_the_descriptor_is_published_in_the_reference_format(runtime_dir):
+    from ekv.observe.tile_shares import share_descriptor
+    from ekv.runtime.audit_kernel import RecordingPlane
+
+    plane = RecordingPlane(2, 4, 8, 4, 16)
+    d = share_descriptor(plane.pid)
+    assert d["tile_lse_dev"] == plane._lse and d["ncap"] == 8 and d["max_rows"] == 4
+    assert d["tile_lse_layers"] == 2 and d["tile_lse_group_rows"] == 4 and d["attn_share_tile_blocks"] == 2
+    assert len(d["tile_lse_ipc"]) == 128 and len(d["layer_table_ipc"]) == 128
+    assert np.isnan(plane.table().cpu().numpy()).all(), "a new table is all NaN"
+
+
+def test_plane_validation_raises_the_reference_exceptions(runtime_dir):
+    from ekv.runtime.audit_kernel import RecordingPlane
+
+    with pytest.raises(ValueError):
+        RecordingPlane(1, 2, 4, 17, 16)
+    with pytest.raises(ValueError):
+        RecordingPlane(1, 2, 4, 4, 12)
+    plane = RecordingPlane(1, 2, 4, 4, 16)
+    with pytest.raises(RuntimeError):
+        plane.set(True)  # before the layer table is filled
+    plane.attach([0x1000])
+    q = torch.zeros(2, 8, 128, dtype=torch.bfloat16, device="cuda")
+    kv = torch.zeros(16, 2, 16, 2, 128, dtype=torch.bfloat16, device="cuda")
+    table = torch.zeros(2, 4, dtype=torch.int32, device="cuda")
+    lens = torch.zeros(2, dtype=torch.int32, device="cuda")
+    with pytest.raises(ValueError):
+        plane.record("a", table, lens, q, kv[:, :, :8], 0.1)  # block size differs
+    with pytest.raises(ValueError):
+        plane.record("a", table, lens, q[:, :6], kv, 0.1)  # group size differs
+    plane.record("a", table, lens, q, kv, 0.1)
+    with pytest.raises(RuntimeError):
+        plane.record("b", table, lens, q, kv, 0.1)  # more layers than the plane holds
+
+
+# ---- random cases through the C ABI against the oracle ------------------------------------------------
+
+
+def random_case(seed, rows, width, q_heads, kv_heads, lens, dtype=torch.bfloat16, block_size=16, pool=None):
+    gen = torch.Generator().manual_seed(seed)
+    pool = pool or rows * width + 7
+    tokens = rows + 5
+    q = torch.randn(tokens, q_heads, 128, generator=gen).to(dtype)
+    k = torch.randn(pool, block_size, kv_heads, 128, generator=gen).to(dtype)
+    table = torch.randperm(pool, generator=gen)[: rows * width].reshape(rows, width).to(torch.int32)
+    qrow = torch.randperm(tokens, generator=gen)[:rows].to(torch.int32)
+    return q, k, table, torch.tensor(lens, dtype=torch.int32), qrow
+
+
+def launch(q, k, table, lens, qrow, select, flag_on, layers, layer, group_rows, heads=1, group=None,
+           tile_blocks=2, aggregate="mean", flags=None, lse=None, acc=None, status=None):
+    import ekv._lib as L
+
+    lib = L.load()
+    rows, width = table.shape
+    block_size, kv_heads = k.shape[1], k.shape[2]
+    cell = heads * group_rows
+    dev = torch.device("cuda")
+    if lse is None:
+        lse = torch.full((2, layers, rows, width, cell), float("nan"), device=dev)
+    if acc is None:
+        acc = (torch.zeros(rows, width, device=dev), torch.zeros(rows, dtype=torch.int32, device=dev),
+               torch.full((rows, width), float("nan"), device=dev))
+    ws_bytes = lib.ekv_audit_workspace_bytes(rows, width, group_rows, heads, block_size, tile_blocks)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev) if status is None else status
+    flag = torch.tensor([1 if flag_on else 0], dtype=torch.int32, device=dev)
+    sel = torch.as_tensor(np.asarray(select, dtype=np.uint8)).to(dev)
+    qd, kd, td, ld, rd = (x.to(dev) for x in (q, k, table, lens, qrow))
+    if flags is None:
+        flags = (L.SHARE_RESET if layer == 0 else 0) | (L.SHARE_FINALIZE if layer == layers - 1 else 0)
+    rc = lib.ekv_audit_launch(
+        qd.data_ptr(), kd.data_ptr(), td.data_ptr(), ld.data_ptr(), rd.data_ptr(), sel.data_ptr(), flag.data_ptr(),
+        lse.data_ptr(), 1 / math.sqrt(128), layer, layer % kv_heads if group is None else group,
+        qd.stride(0), qd.stride(1), kd.stride(0), kd.stride(1), kd.stride(2), td.stride(0),
+        layers, rows, width, group_rows, block_size, tile_blocks, 128,
+        L.DTYPE_BF16 if q.dtype == torch.bfloat16 else L.DTYPE_F16, heads, kv_heads, kd.shape[0], qd.shape[0],
+        acc[0].data_ptr(), acc[1].data_ptr(), acc[2].data_ptr(), L.AGG_MEAN if aggregate == "mean" else L.AGG_MAX,
+        flags, ws.data_ptr(), ws_bytes, status.data_ptr(), L.current_stream(),
+    )
+    L.check(rc, "ekv_audit_launch")
+    torch.cuda.synchronize()
+    return lse, acc, status
+
+
+def oracle_case(table, lens, qrow, select, layers_q, layers_k, group_rows, block_size, tile_blocks, heads=1,
+                groups=None):
+    rows, width = table.shape
+    layers = len(layers_q)
+    lse = oaud.new_table(layers, rows, width, heads * group_rows)
+    for layer in range(layers):
+        group = (layer % k.shape[2]) if groups is None else groups[layer]
+        oaud.tile_lse(layers_q[layer].float().numpy(), layers_k[layer].float().numpy(), table.numpy(), lens.numpy(),
+                      qrow.numpy(), np.asarray(select), 1, lse, 1 / math.sqrt(128), layer, group, block_size,
+                      tile_blocks, heads)
+    return lse
+
+
+def compare_shares(lse_ref, lens, select, block_size, tile_blocks, got_share, aggregate="mean"):
+    rows = len(lens)
+    row_blocks = np.where(np.asarray(select) != 0, -(-np.asarray(lens) // block_size), 0)
+    live = np.flatnonzero(row_blocks > 0)
+    ref = np.full(got_share.shape, np.nan)
+    if live.size:
+        u = osh.log_weights(lse_ref, lse_ref.shape[1], live, tile_blocks)
+        ref[live] = osh.normalize(u, row_blocks[live], tile_blocks, aggregate)
+    got = got_share.astype(np.float64)
+    assert np.array_equal(np.isnan(got), np.isnan(ref)), (np.isnan(got).sum(), np.isnan(ref).sum(), rows)
+    np.testing.assert_allclose(got, ref, equal_nan=True, **SHARE_TOL)
+
+
+@pytest.mark.parametrize(
+    "q_heads, kv_heads, tile_blocks, dtype",
+    [(32, 8, 2, torch.bfloat16), (64, 8, 2, torch.bfloat16), (8, 8, 2, torch.float16), (48, 4, 2, torch.bfloat16),
+     (24, 8, 2, torch.float16), (32, 8, 1, torch.bfloat16), (32, 8, 4, torch.bfloat16)],
+)
+def test_random_rows_match_the_oracle(q_heads, kv_heads, tile_blocks, dtype):
+    """G = 4, 8, 1, 12 (two n-tiles), 3 (odd); tiles of 32, 16 and 64 tokens; edge lengths."""
+    rows, width, block_size, layers = 9, 40, 16, 3
+    lens = [640, 1, 0, 31, 32, 33, 100, 17, 639]
+    select = [1, 1, 1, 1, 0, 1, 1, 1, 1]
+    group_rows = q_heads // kv_heads
+    gen_layers = [random_case(11 + layer, rows, width, q_heads, kv_heads, lens, dtype) for layer in range(layers)]
+    _, _, table, lens_t, qrow = gen_layers[0]
+    lse = acc = None
+    for layer in range(layers):
+        q, k = gen_layers[layer][0], gen_layers[layer][1]
+        lse, acc, status = launch(q, k, table, lens_t, qrow, select, True, layers, layer, group_rows,
+                                  tile_blocks=tile_blocks, lse=lse, acc=acc)
+        assert int(status.item()) == 0
+    ref = oracle_case(table, lens_t, qrow, select, [g[0] for g in gen_layers], [g[1] for g in gen_layers],
+                      group_rows, block_size, tile_blocks)
+    got = lse.cpu().numpy()
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    w = ~np.isnan(ref)
+    np.testing.assert_allclose(got[w], ref[w], **LSE_TOL)
+    compare_shares(ref, lens, select, block_size, tile_blocks, acc[2].cpu().numpy())
+
+
+def test_all_heads_mode_matches_the_oracle():
+    rows, width, layers, q_heads, kv_heads = 4, 24, 2, 32, 8
+    lens = [377, 16, 200, 384]
+    select = [1, 1, 1, 1]
+    gen_layers = [random_case(40 + layer, rows, width, q_heads, kv_heads, lens) for layer in range(layers)]
+    _, _, table, lens_t, qrow = gen_layers[0]
+    lse = acc = None
+    for layer in range(layers):
+        lse, acc, _ = launch(gen_layers[layer][0], gen_layers[layer][1], table, lens_t, qrow, select, True, layers,
+                             layer, q_heads // kv_heads, heads=kv_heads, group=0, lse=lse, acc=acc)
+    ref = oracle_case(table, lens_t, qrow, select, [g[0] for g in gen_layers], [g[1] for g in gen_layers],
+                      q_heads // kv_heads, 16, 2, heads=kv_heads, groups=[0] * layers)
+    got = lse.cpu().numpy()
+    w = ~np.isnan(ref)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    np.testing.assert_allclose(got[w], ref[w], **LSE_TOL)
+    compare_shares(ref, lens, select, 16, 2, acc[2].cpu().numpy())
+
+
+def test_the_flag_off_writes_nothing():
+    q, k, table, lens, qrow = random_case(3, 4, 16, 32, 8, [100, 200, 50, 256])
+    lse, acc, _ = launch(q, k, table, lens, qrow, [1, 1, 1, 1], False, 1, 0, 4)
+    assert torch.isnan(lse).all()
+    assert torch.isnan(acc[2]).all()  # the share output is untouched too
+    assert (acc[0] == 0).all()
+
+
+def test_out_of_range_block_ids_are_skipped_and_reported():
+    import ekv._lib as L
+
+    q, k, table, lens, qrow = random_case(5, 3, 16, 32, 8, [100, 200, 250], pool=64)
+    table = table % 64
+    table[1, 2] = 64  # one past the pool
+    table[2, 0] = -5
+    _, _, status = launch(q, k, table, lens, qrow, [1, 1, 1], True, 1, 0, 4)
+    assert int(status.item()) & L.STATUS_BAD_BLOCK_ID
+
+
+def test_a_length_past_the_table_is_clamped_and_reported():
+    import ekv._lib as L
+
+    q, k, table, lens, qrow = random_case(6, 2, 8, 32, 8, [128, 129])
+    lse, _, status = launch(q, k, table, lens, qrow, [1, 1], True, 1, 0, 4)
+    assert int(status.item()) & L.STATUS_LEN_OVER_WIDTH
+    assert not torch.isnan(lse[0, 0, 1]).any()
+
+
+def test_a_bad_query_row_is_skipped_and_reported():
+    import ekv._lib as L
+
+    q, k, table, lens, qrow = random_case(7, 2, 8, 32, 8, [100, 100])
+    qrow[1] = q.shape[0] + 3
+    lse, acc, status = launch(q, k, table, lens, qrow, [1, 1], True, 1, 0, 4)
+    assert int(status.item()) & L.STATUS_BAD_QROW
+    assert torch.isnan(lse[:, :, 1]).all() and torch.isnan(acc[2][1]).all()
+    assert not torch.isnan(lse[0, 0, 0, :7]).any()
+
+
+def test_repeated_launches_are_deterministic():
+    q, k, table, lens, qrow = random_case(8, 16, 64, 32, 8, list(np.random.default_rng(0).integers(1, 1024, 16)))
+    a = launch(q, k, table, lens, qrow, [1] * 16, True, 1, 0, 4)
+    b = launch(q, k, table, lens, qrow, [1] * 16, True, 1, 0, 4)
+    assert torch.equal(torch.nan_to_num(a[0], 7.0), torch.nan_to_num(b[0], 7.0))
+    assert torch.equal(torch.nan_to_num(a[1][2], 7.0), torch.nan_to_num(b[1][2], 7.0))
+
+
+def test_full_size_llama8b_rows_sum_to_one():
+    """Size-independent properties at the Llama-3.1-8B shape (64 rows, lengths up to 8192, a pool of
+    32868 blocks): every audited row's shares are finite, non-negative and sum to 1, the unaudited row
+    is NaN, and four rows match the oracle cell for cell and share for share."""
+    rows, width, q_heads, kv_heads, pool = 64, 512, 32, 8, 64 * 512 + 100
+    rng = np.random.default_rng(1)
+    lens = rng.integers(1024, 8193, rows)
+    select = np.ones(rows, dtype=np.uint8)
+    select[5] = 0
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    q = torch.randn(rows + 5, q_heads, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    k = torch.randn(pool, 16, kv_heads, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    table = torch.from_numpy(rng.permutation(pool)[: rows * width].reshape(rows, width).astype(np.int32))
+    qrow = torch.from_numpy(rng.permutation(rows + 5)[:rows].astype(np.int32))
+    lens_t = torch.from_numpy(lens.astype(np.int32))
+    lse, acc, status = launch(q, k, table, lens_t, qrow, select, True, 1, 0, 4)
+    assert int(status.item()) == 0
+    share = acc[2].cpu().numpy().astype(np.float64)
+    assert np.isnan(share[5]).all()
+    live = np.flatnonzero(select)
+    assert np.isfinite(share[live]).all() and (share[live] >= 0).all()
+    np.testing.assert_allclose(share[live].sum(axis=1), 1.0, rtol=1e-4)
+    # the oracle on four rows, over a compacted copy of just their blocks
+    pick = np.array([0, 17, 40, 63])
+    ids = np.unique(np.concatenate([table[r, : -(-int(lens[r]) // 16)].numpy() for r in pick]))
+    remap = np.full(pool, 0, dtype=np.int32)
+    remap[ids] = np.arange(len(ids), dtype=np.int32)
+    small_table = remap[table.numpy()[pick]]
+    k_small = k[torch.from_numpy(ids).cuda()].float().cpu().numpy()
+    ref = oaud.new_table(1, len(pick), width, 4)
+    oaud.tile_lse(q.float().cpu().numpy(), k_small, small_table, lens[pick], qrow.numpy()[pick],
+                  np.ones(len(pick), dtype=np.uint8), 1, ref, 1 / math.sqrt(128), 0, 0, 16, 2)
+    got = lse.cpu().numpy()[:, :, pick]
+    w = ~np.isnan(ref)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    np.testing.assert_allclose(got[w], ref[w], **LSE_TOL)
+    u = osh.log_weights(ref, 1, np.arange(len(pick)), 2)
+    np.testing.assert_allclose(share[pick], osh.normalize(u, -(-lens[pick] // 16), 2), **SHARE_TOL)

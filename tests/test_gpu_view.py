@@ -1,0 +1,247 @@
+"""Parity of the device view builder with the reference: compaction, allocation and the controller's
+keep mask, bit-exact (ids, order and lengths), on the golden vectors, the oracle, and the full-size
+view stress shape through size-independent properties."""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+from conftest import load_golden
+
+from oracle import allocation as oa
+from oracle import view as ov
+
+pytestmark = pytest.mark.gpu
+
+
+def test_compact_block_table_matches_300_reference_batches():
+    from ekv.runtime.block_view import compact_block_table
+
+    g = load_golden("view_cases")
+    for i in range(300):
+        table = torch.from_numpy(g[f"table{i}"]).cuda()
+        lens = torch.from_numpy(g[f"lens{i}"]).cuda()
+        keep = torch.from_numpy(g[f"keep{i}"]).cuda()
+        view, view_lens = compact_block_table(table, lens, keep, 16)
+        np.testing.assert_array_equal(view.cpu().numpy(), g[f"view{i}"], err_msg=f"batch {i}")
+        np.testing.assert_array_equal(view_lens.cpu().numpy(), g[f"view_lens{i}"], err_msg=f"batch {i}")
+
+
+def test_known_answer_views_on_the_device():
+    from ekv.runtime.block_view import compact_block_table
+
+    def view_of(table, lens, keep):
+        t = torch.tensor(table, dtype=torch.int32).cuda()
+        return compact_block_table(t, torch.tensor(lens, dtype=torch.int32).cuda(), torch.tensor(keep).cuda(), 16)
+
+    v, n = view_of([[7, 8, 9, 10]], [40], [[False] * 4])
+    assert v[0, :2].tolist() == [7, 9] and n.tolist() == [24]
+    v, n = view_of([[1, 2, 3, 4, 5, 6]], [96], [[True, False, True, False, True, False]])
+    assert v[0, :4].tolist() == [1, 3, 5, 6] and n.tolist() == [64]
+    _, n = view_of([[1, 2], [3, 4]], [0, 20], [[True, True], [False, False]])
+    assert n.tolist() == [0, 20]
+    v, n = view_of([[5]], [3], [[False]])
+    assert v[0, 0].item() == 5 and n.tolist() == [3]
+
+
+def golden_requests(g, i):
+    sizes = g[f"sizes{i}"]
+    flat = g[f"scores{i}"]
+    bounds = np.concatenate([[0], np.cumsum(sizes)])
+    scores = [flat[bounds[j] : bounds[j + 1]] for j in range(len(sizes))]
+    recent = int(g[f"recent{i}"])
+    pinned = [oa.controller_pins(int(n), recent) for n in sizes]
+    return scores, pinned
+
+
+def test_allocate_matches_the_reference_bit_exactly_including_ties():
+    from ekv.observe.allocation import Request, allocate
+
+    g = load_golden("allocation_cases")
+    checked = 0
+    for i in range(60):
+        scores, pinned = golden_requests(g, i)
+        objective = str(g[f"objective{i}"])
+        requests = [Request(scores=s, pinned=p) for s, p in zip(scores, pinned, strict=True)]
+        if objective == "sum" and len(requests) > 1:
+            with pytest.raises(RuntimeError):
+                allocate(requests, int(g[f"budget{i}"]), objective)
+            continue
+        masks = allocate(requests, int(g[f"budget{i}"]), objective)
+        np.testing.assert_array_equal(np.concatenate(masks), g[f"mask{i}"], err_msg=f"case {i}")
+        checked += 1
+    assert checked >= 40
+
+
+def test_allocate_against_the_oracle_with_many_ties():
+    from ekv.observe.allocation import Request, allocate
+
+    rng = np.random.default_rng(5)
+    for trial in range(80):
+        n_req = 1 if trial % 2 else int(rng.integers(1, 9))
+        objective = "sum" if (trial % 2 and trial % 4 == 1) else "uniform"
+        scores = [rng.integers(0, 3, int(rng.integers(1, 300))).astype(np.float64) for _ in range(n_req)]
+        if trial % 5 == 0:
+            scores = [rng.random(len(s)).astype(np.float32).astype(np.float64) for s in scores]
+        recent = int(rng.integers(0, 6))
+        pinned = [oa.controller_pins(len(s), recent) for s in scores]
+        must = sum(int(p.sum()) for p in pinned)
+        total = sum(len(s) for s in scores)
+        budget = int(rng.integers(must, total + 1))
+        got = allocate([Request(scores=s, pinned=p) for s, p in zip(scores, pinned, strict=True)], budget, objective)
+        want = oa.allocate(scores, budget, objective, pinned)
+        for a, b in zip(got, want, strict=True):
+            np.testing.assert_array_equal(a, b, err_msg=f"trial {trial}")
+
+
+@pytest.mark.parametrize("name", ["audit_cfg1_fp16", "audit_layers_fp16", "audit_g8_bf16"])
+def test_plan_view_matches_the_reference_controller_and_view(name):
+    """The controller's uniform keep mask at budget 0.5 (recent_blocks 4) and the view, as the golden
+    fixture's reference pipeline computed them from the reference shares."""
+    from ekv.runtime.block_view import plan_view
+
+    g = load_golden(name)
+    rows, width = g["table"].shape
+    table = torch.from_numpy(g["table"]).cuda()
+    lens = torch.from_numpy(g["lens"]).cuda()
+    scores = torch.from_numpy(np.nan_to_num(g["share_mean"], nan=0.0).astype(np.float32)).cuda()
+    # the reference ranked the float64 shares; the float32 copies rank identically unless two shares
+    # collapse to one float32 value, which the fixture does not contain
+    f32 = np.nan_to_num(g["share_mean"], nan=0.0).astype(np.float32)
+    keep_f32 = oa.controller_keep(g["row_blocks"], width, lambda r, n: f32[r, :n].astype(np.float64), 0.5, "uniform",
+                                  recent_blocks=4)
+    np.testing.assert_array_equal(keep_f32, g["keep"])
+    mask = torch.empty(rows, width, dtype=torch.uint8).cuda()
+    view, view_lens = plan_view(table, lens, 16, torch.from_numpy(g["row_blocks"].astype(np.int32)).cuda(),
+                                scores=scores, policy="uniform", budget_fraction=0.5, recent_blocks=4, mask_out=mask)
+    np.testing.assert_array_equal(mask.cpu().numpy(), g["keep"])
+    np.testing.assert_array_equal(view.cpu().numpy(), g["view"])
+    np.testing.assert_array_equal(view_lens.cpu().numpy(), g["view_lens"])
+
+
+def test_keep_newest_gives_the_reference_answer():
+    from ekv.runtime.block_view import plan_view
+
+    table = torch.arange(12, dtype=torch.int32).reshape(1, 12).cuda() + 100
+    lens = torch.tensor([160], dtype=torch.int32).cuda()
+    mask = torch.empty(1, 12, dtype=torch.uint8).cuda()
+    view, view_lens = plan_view(table, lens, 16, torch.tensor([10], dtype=torch.int32).cuda(), scores=None,
+                                policy="newest", budget_fraction=0.5, recent_blocks=0, mask_out=mask)
+    assert np.flatnonzero(mask.cpu().numpy()[0, :10]).tolist() == [0, 6, 7, 8, 9]
+    assert view[0, :5].tolist() == [100, 106, 107, 108, 109] and view_lens.tolist() == [80]
+
+
+def view_stress_inputs(rows, width, seed=0):
+    """The view stress shape: 1..width blocks per row, ids from a 2^20 pool, Dirichlet(0.3) shares,
+    per-row budget fractions in [0.2, 1.0]."""
+    gen = torch.Generator().manual_seed(seed)
+    n = torch.randint(1, width + 1, (rows,), generator=gen).to(torch.int32)
+    table = torch.randint(0, 2**20, (rows, width), generator=gen, dtype=torch.int32)
+    conc = torch.full((width,), 0.3, dtype=torch.float64)
+    scores = torch.distributions.Dirichlet(conc).sample((rows,)).to(torch.float32)
+    scores = torch.where(torch.arange(width)[None, :] < n[:, None].long(), scores, torch.zeros_like(scores))
+    fraction = 0.2 + 0.8 * torch.rand(rows, generator=gen, dtype=torch.float64)
+    lens = n * 16 - torch.randint(0, 16, (rows,), generator=gen, dtype=torch.int32)
+    return table, n, lens, scores, fraction
+
+
+@pytest.mark.parametrize("policy", ["sum", "uniform"])
+def test_view_stress_rows_match_the_oracle(policy):
+    """Per-row budgets (each row its own allocate call): 256 rows of width 8192 against the oracle."""
+    from ekv.runtime.block_view import plan_view
+
+    rows, width = 256, 8192
+    table, n, lens, scores, fraction = view_stress_inputs(rows, width, seed=1 if policy == "sum" else 2)
+    mask = torch.empty(rows, width, dtype=torch.uint8).cuda()
+    view, view_lens = plan_view(table.cuda(), lens.cuda(), 16, n.cuda(), scores=scores.cuda(), policy=policy,
+                                row_fraction=fraction.cuda(), recent_blocks=0, mask_out=mask)
+    keep = oa.per_row_keep(n.numpy(), width, scores.numpy().astype(np.float64), fraction.numpy(), policy)
+    np.testing.assert_array_equal(mask.cpu().numpy(), keep)
+    ref_view, ref_lens = ov.compact_block_table(table.numpy(), lens.numpy(), keep, 16)
+    np.testing.assert_array_equal(view.cpu().numpy(), ref_view)
+    np.testing.assert_array_equal(view_lens.cpu().numpy(), ref_lens)
+
+
+def test_full_size_view_stress_properties():
+    """1024 rows x 8192: the view is a permutation of the row, kept ids come first in their original
+    order, the kept count is pins + quota, and the length formula holds."""
+    from ekv.runtime.block_view import plan_view
+
+    rows, width = 1024, 8192
+    table, n, lens, scores, fraction = view_stress_inputs(rows, width)
+    mask = torch.empty(rows, width, dtype=torch.uint8).cuda()
+    view, view_lens = plan_view(table.cuda(), lens.cuda(), 16, n.cuda(), scores=scores.cuda(), policy="sum",
+                                row_fraction=fraction.cuda(), recent_blocks=0, mask_out=mask)
+    v, m, t = view.cpu().numpy(), mask.cpu().numpy().astype(bool), table.numpy()
+    nn, fr = n.numpy(), fraction.numpy()
+    for r in range(0, rows, 7):
+        k = m[r] & (np.arange(width) < nn[r])
+        k[0] = True
+        k[nn[r] - 1] = True
+        kept = int(k.sum())
+        pins = 1 if nn[r] == 1 else 2
+        budget = max(pins, math.ceil(fr[r] * nn[r]))
+        assert kept == min(budget, nn[r]), r
+        np.testing.assert_array_equal(v[r, :kept], t[r, k])
+        np.testing.assert_array_equal(np.sort(v[r]), np.sort(t[r]))
+        assert view_lens[r].item() == (kept - 1) * 16 + int(lens[r]) - (nn[r] - 1) * 16
+
+
+def test_decode_view_policy_lease_audit_and_release():
+    """The DecodeView contract: identity before a commit, the committed view while the lease lives,
+    identity after expiry, a full read for an audited row, never a released block."""
+    import time
+
+    from ekv.runtime.block_view import DecodeView
+
+    class Plane:
+        def __init__(self):
+            self.flags, self.selected = [], []
+
+        def set(self, on):
+            self.flags.append(on)
+
+        def select(self, audited, token_start):
+            self.selected.append(audited.copy())
+
+    table = torch.tensor([[1, 2, 3, 4], [5, 6, 7, 8]], dtype=torch.int32).cuda()
+    lens = torch.tensor([64, 48], dtype=torch.int32).cuda()
+    decode = torch.ones(2, dtype=torch.int32)
+    mask = np.array([[1, 0, 0, 1], [1, 1, 0, 0]], dtype=np.uint32)
+    hour = 3600 * 10**9
+
+    view = DecodeView(rows=2, width=4, block_size=16)
+    t, n = view.build(table, lens, decode)
+    assert t.tolist() == table.tolist() and n.tolist() == [64, 48]
+    view.write_row_controls(mask)
+    view.write_lease_deadline(time.monotonic_ns() + hour)
+    t, n = view.build(table, lens, decode)
+    assert t[0, :2].tolist() == [1, 4] and n.tolist() == [32, 48]
+    assert t[1, :3].tolist() == [5, 6, 7]
+    view.write_lease_deadline(time.monotonic_ns() - 1)
+    t, n = view.build(table, lens, decode)
+    assert n.tolist() == [64, 48]
+    assert view.read_breakdown()["expired"] == 7
+
+    plane = Plane()
+    view = DecodeView(rows=2, width=4, block_size=16, audit=plane)
+    view.write_row_controls(mask)
+    view.write_lease_deadline(time.monotonic_ns() + hour)
+    view.write_audit_rows(np.array([True, False]))
+    t, n = view.build(table, lens, decode)
+    assert n.tolist() == [64, 48] and plane.flags[-1] is True and plane.selected[-1].tolist() == [True, False]
+    t, n = view.build(table, lens, decode)  # the audit request was consumed
+    assert n.tolist() == [32, 48] and plane.flags[-1] is False
+    assert view.audits_completed == 1 and view.audited_blocks[0] == 4
+    new = view.write_release(np.array([[0, 1, 1, 1], [0, 1, 0, 0]]))
+    assert new == [(0, 1), (0, 2)]  # block 0 and the last block at the audit are never released
+    view.write_lease_deadline(time.monotonic_ns() - 1)
+    t, n = view.build(table, lens, decode)
+    assert t[0, :2].tolist() == [1, 4] and n.tolist() == [32, 48]  # expired, yet released blocks stay out
+    prefill = torch.tensor([1, 5], dtype=torch.int32)
+    view.write_lease_deadline(time.monotonic_ns() + hour)
+    t, n = view.build(table, lens, prefill)
+    assert n.tolist() == [32, 48]  # row 1 prefills: it reads in full

@@ -1,0 +1,183 @@
+"""The oracle pinned against the reference: golden vectors made by running the reference's own code
+(tests/golden/make_golden.py), and the known answers of the reference's own unit tests. CPU only."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+from conftest import load_golden
+
+from oracle import allocation as oa
+from oracle import audit as oaud
+from oracle import shares as osh
+from oracle import view as ov
+
+
+def unpack(x: np.ndarray, dtype: str) -> np.ndarray:
+    """fp16 arrays as stored; bf16 stored as the upper 16 bits of float32."""
+    if dtype == "fp16":
+        return x.astype(np.float32)
+    return (x.astype(np.uint32) << 16).view(np.float32)
+
+
+def run_oracle_audit(g: dict) -> np.ndarray:
+    dtype = str(g["dtype"])
+    q, k = unpack(g["query"], dtype), unpack(g["keys"], dtype)
+    layers = q.shape[0]
+    rows, width = g["table"].shape
+    lse = oaud.new_table(layers, rows, width, int(g["group_rows"]))
+    for layer in range(layers):
+        oaud.tile_lse(q[layer], k[layer], g["table"], g["lens"], g["qrow"], g["select"], int(g["flags"][layer]),
+                      lse, float(g["scale"]), layer, layer % int(g["kv_heads"]), int(g["block_size"]),
+                      int(g["tile_blocks"]))
+    return lse
+
+
+AUDIT_CASES = ["audit_cfg1_fp16", "audit_layers_fp16", "audit_g8_bf16"]
+
+
+@pytest.mark.parametrize("name", AUDIT_CASES)
+def test_oracle_tile_lse_matches_the_reference_kernel(name):
+    g = load_golden(name)
+    lse = run_oracle_audit(g)
+    ref = g["lse"]
+    assert np.array_equal(np.isnan(lse), np.isnan(ref)), "the same cells are written"
+    written = ~np.isnan(ref)
+    assert written.any()
+    np.testing.assert_allclose(lse[written], ref[written], rtol=2e-5, atol=2e-5)
+
+
+def test_unselected_rows_and_layers_with_the_flag_off_stay_nan():
+    g = load_golden("audit_layers_fp16")
+    ref = g["lse"]
+    assert np.isnan(ref[:, 1]).all(), "layer 1 ran with the flag off"
+    assert np.isnan(ref[:, :, 2]).all(), "row 2 was not selected"
+
+
+@pytest.mark.parametrize("name", AUDIT_CASES)
+@pytest.mark.parametrize("aggregate", ["mean", "max"])
+def test_oracle_shares_match_the_reference_normalisation(name, aggregate):
+    g = load_golden(name)
+    live = g["live"]
+    u = osh.log_weights(g["lse"], g["lse"].shape[1], live, int(g["tile_blocks"]))
+    np.testing.assert_array_equal(u, g["u"])  # the same float32 arithmetic as read_tile_rows
+    share = np.full_like(g[f"share_{aggregate}"], np.nan)
+    share[live] = osh.normalize(u, g["row_blocks"][live], int(g["tile_blocks"]), aggregate)
+    np.testing.assert_allclose(share, g[f"share_{aggregate}"], rtol=1e-12, atol=1e-15, equal_nan=True)
+
+
+@pytest.mark.parametrize("name", AUDIT_CASES)
+def test_oracle_controller_view_matches_the_reference(name):
+    g = load_golden(name)
+    rows, width = g["table"].shape
+    share = g["share_mean"]
+    keep = oa.controller_keep(g["row_blocks"], width, lambda r, n: np.nan_to_num(share[r, :n], nan=0.0), 0.5, "uniform",
+                              recent_blocks=4)
+    np.testing.assert_array_equal(keep, g["keep"])
+    view, view_lens = ov.compact_block_table(g["table"], g["lens"], keep, int(g["block_size"]))
+    np.testing.assert_array_equal(view, g["view"])
+    np.testing.assert_array_equal(view_lens, g["view_lens"])
+
+
+def test_oracle_normalize_matches_reference_cases():
+    g = load_golden("shares_cases")
+    for i in range(12):
+        for aggregate in ("mean", "max"):
+            got = osh.normalize(g[f"u{i}"], g[f"rb{i}"], int(g[f"tb{i}"]), aggregate)
+            np.testing.assert_allclose(got, g[f"{aggregate}{i}"], rtol=1e-12, atol=1e-15, equal_nan=True)
+
+
+def test_oracle_log_weights_match_read_tile_rows():
+    g = load_golden("shares_cases")
+    table_layers, layers, rows, width, group, tile_blocks = 4, 3, 5, 6, 2, 2
+    lse = g["read_table"].reshape(2, table_layers, rows, width, group)
+    u = osh.log_weights(lse, layers, g["read_rows"], tile_blocks)
+    np.testing.assert_array_equal(u, g["read_u"])
+    assert u[0, 0, 3, 1] == -np.inf  # cell 7 holds l = 0: no weight
+
+
+def test_oracle_allocation_matches_the_reference_bit_exactly():
+    g = load_golden("allocation_cases")
+    for i in range(60):
+        sizes = g[f"sizes{i}"]
+        flat = g[f"scores{i}"]
+        bounds = np.concatenate([[0], np.cumsum(sizes)])
+        scores = [flat[bounds[j] : bounds[j + 1]] for j in range(len(sizes))]
+        recent = int(g[f"recent{i}"])
+        pinned = [oa.controller_pins(int(n), recent) for n in sizes]
+        masks = oa.allocate(scores, int(g[f"budget{i}"]), str(g[f"objective{i}"]), pinned)
+        np.testing.assert_array_equal(np.concatenate(masks), g[f"mask{i}"], err_msg=f"case {i}")
+
+
+def test_oracle_view_matches_300_reference_batches():
+    g = load_golden("view_cases")
+    for i in range(300):
+        view, lens = ov.compact_block_table(g[f"table{i}"], g[f"lens{i}"], g[f"keep{i}"], 16)
+        np.testing.assert_array_equal(view, g[f"view{i}"], err_msg=f"batch {i}")
+        np.testing.assert_array_equal(lens, g[f"view_lens{i}"], err_msg=f"batch {i}")
+
+
+# ---- known answers of the reference's own unit tests ---------------------------------------------
+
+
+def test_known_answer_unwritten_cells_and_empty_blocks_carry_no_mass():
+    u = np.full((1, 2, 4, 2), np.nan, dtype=np.float32)
+    u[0, 0, :, 0] = [0.0, np.log(3.0), -np.inf, np.nan]
+    got = osh.normalize(u, np.array([4, 4]), 1)
+    np.testing.assert_allclose(got[0], [0.25, 0.75, 0.0, 0.0])
+    assert np.isnan(got[1]).all()
+
+
+def test_known_answer_a_query_row_without_data_does_not_dilute_the_mean():
+    u = np.full((1, 1, 3, 2), np.nan, dtype=np.float32)
+    u[0, 0, :, 0] = np.log([1.0, 1.0, 2.0])
+    np.testing.assert_allclose(osh.normalize(u, np.array([3]), 1)[0], [0.25, 0.25, 0.5])
+
+
+def test_known_answer_a_partial_last_tile_gets_its_whole_mass():
+    cells = np.repeat(np.log(np.array([1.0, 2.0, 5.0]) / 2), 2).astype(np.float32).reshape(1, 1, 6, 1)
+    got = osh.normalize(cells, np.array([5]), 2)
+    np.testing.assert_allclose(got[0], np.array([0.5, 0.5, 1.0, 1.0, 5.0, 0.0]) / 8.0, rtol=1e-6)
+
+
+def test_known_answer_a_complete_last_tile_is_left_alone():
+    cells = np.repeat(np.log(np.array([3.0, 1.0]) / 2), 2).astype(np.float32).reshape(1, 1, 4, 1)
+    np.testing.assert_allclose(osh.normalize(cells, np.array([4]), 2)[0], [0.375, 0.375, 0.125, 0.125], rtol=1e-6)
+
+
+def test_known_answer_max_keeps_a_block_that_one_head_needs():
+    u = np.log(np.array([[9.0, 1.0, 1.0], [1.0, 9.0, 1.0]])).T.astype(np.float32).reshape(1, 1, 3, 2)
+    np.testing.assert_allclose(osh.normalize(u, np.array([3]), 1)[0], np.array([10.0, 10.0, 2.0]) / 22.0, atol=1e-6)
+    np.testing.assert_allclose(osh.normalize(u, np.array([3]), 1, "max")[0], np.array([9.0, 9.0, 1.0]) / 19.0, atol=1e-6)
+
+
+def test_known_answer_views():
+    def view_of(table, lens, keep):
+        v, n = ov.compact_block_table(np.array(table), np.array(lens), np.array(keep), 16)
+        return v, n
+
+    v, n = view_of([[7, 8, 9, 10]], [64], [[True] * 4])
+    assert v.tolist() == [[7, 8, 9, 10]] and n.tolist() == [64]
+    v, n = view_of([[7, 8, 9, 10]], [40], [[False] * 4])
+    assert v[0, :2].tolist() == [7, 9] and n.tolist() == [24]
+    v, n = view_of([[7, 8, 9, 10]], [64], [[False, True, False, False]])
+    assert v[0, :3].tolist() == [7, 8, 10] and n.tolist() == [48]
+    v, n = view_of([[1, 2, 3, 4, 5, 6]], [96], [[True, False, True, False, True, False]])
+    assert v[0, :4].tolist() == [1, 3, 5, 6] and n.tolist() == [64]
+    _, n = view_of([[1, 2], [3, 4]], [0, 20], [[True, True], [False, False]])
+    assert n.tolist() == [0, 20]
+    v, n = view_of([[5]], [3], [[False]])
+    assert v[0, 0] == 5 and n.tolist() == [3]
+
+
+def test_known_answer_keep_newest():
+    """The fixed rule scores = arange(n) at budget 0.5 with no recent pins keeps [0, 6, 7, 8, 9]."""
+    keep = oa.controller_keep(np.array([10]), 12, lambda r, n: np.arange(n, dtype=float), 0.5, "uniform", recent_blocks=0)
+    assert np.flatnonzero(keep[0, :10]).tolist() == [0, 6, 7, 8, 9]
+    g = load_golden("allocation_cases")
+    assert np.flatnonzero(g["newest_mask"]).tolist() == [0, 6, 7, 8, 9]
+
+
+def test_oracle_rejects_a_budget_below_the_pins():
+    with pytest.raises(ValueError):
+        oa.allocate([np.ones(5)], 1, "sum")

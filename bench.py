@@ -79,7 +79,7 @@ def measured_peak() -> tuple[float, str]:
 
 
 class ClockSampler:
-    """nvidia-smi clock and throttle samples every 200 ms during the timed region."""
+    """nvidia-smi clock and throttle samples every 100 ms during the timed region."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -96,9 +96,13 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        deadline = time.time() + 5.0  # let the sampler print its first line before timing starts
+        while time.time() < deadline and os.path.getsize(self.path) == 0:
+            time.sleep(0.05)
         return self
 
     def __exit__(self, *exc):
@@ -359,17 +363,21 @@ def reference_arm(args, cfg: dict) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", choices=sorted(CONFIGS), default="llama8b")
     ap.add_argument("--mode", choices=["reference", "all-heads"], default="reference")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the timed CPU sample")
     ap.add_argument("--no-view", action="store_true", help="skip the block-view build timing")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end timing")
+    ap.add_argument("--pools", type=int, default=None, help="distinct KV pools cycled over the layers")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.pools:
+        cfg["pools"] = args.pools
     if args.impl == "reference":
         reference_arm(args, cfg)
         return
@@ -431,7 +439,7 @@ def main() -> None:
         out_host.copy_(share, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
-    e2e_seconds = timed(e2e_step, args.steps, args.warmup, dist_on)
+    e2e_seconds = timed(e2e_step, args.steps, args.warmup, dist_on) if not args.no_e2e else float("nan")
     h2d = pinned_table.nbytes + pinned_lens.nbytes + pinned_sel.nbytes + pinned_tok.nbytes
     d2h = out_host.nbytes
     view = None if args.no_view else view_bench(rank, world, args.steps, args.warmup, dist_on)

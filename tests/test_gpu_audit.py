@@ -175,7 +175,7 @@ def oracle_case(table, lens, qrow, select, layers_q, layers_k, group_rows, block
     layers = len(layers_q)
     lse = oaud.new_table(layers, rows, width, heads * group_rows)
     for layer in range(layers):
-        group = (layer % k.shape[2]) if groups is None else groups[layer]
+        group = (layer % layers_k[layer].shape[2]) if groups is None else groups[layer]
         oaud.tile_lse(layers_q[layer].float().numpy(), layers_k[layer].float().numpy(), table.numpy(), lens.numpy(),
                       qrow.numpy(), np.asarray(select), 1, lse, 1 / math.sqrt(128), layer, group, block_size,
                       tile_blocks, heads)

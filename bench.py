@@ -186,12 +186,12 @@ class Workload:
         return self.queries[layer % len(self.queries)]
 
 
-def make_plane(w: Workload):
+def make_plane(w: Workload, deferred: bool):
     from ekv.runtime.audit_kernel import RecordingPlane
 
     os.environ.setdefault("EKV_RUNTIME_DIR", tempfile.mkdtemp(prefix="ekv_bench_"))
-    plane = RecordingPlane(w.layers, w.rows, w.width, w.group_rows, BLOCK, heads=w.heads)
-    plane.attach([0x1000 + i for i in range(w.layers)])
+    plane = RecordingPlane(w.layers, w.rows, w.width, w.group_rows, BLOCK, heads=w.heads, deferred=deferred)
+    plane.attach([w.caches[layer % len(w.caches)].data_ptr() for layer in range(w.layers)])
     plane.select(w.select, w.qrow)
     plane.set(True)
     return plane
@@ -372,6 +372,8 @@ def main() -> None:
     ap.add_argument("--no-view", action="store_true", help="skip the block-view build timing")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end timing")
     ap.add_argument("--pools", type=int, default=None, help="distinct KV pools cycled over the layers")
+    ap.add_argument("--record", choices=["deferred", "per-layer"], default="deferred",
+                    help="RecordingPlane mode: every layer in one launch after the last, or a launch per layer")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -399,7 +401,7 @@ def main() -> None:
     from ekv.observe.ranks import allreduce_shares
 
     w = Workload(cfg, rank, world, args.mode)
-    plane = make_plane(w)
+    plane = make_plane(w, deferred=args.record == "deferred")
     graph = capture(lambda: audit_step(plane, w))
     share = plane.shares()
 
@@ -413,6 +415,15 @@ def main() -> None:
     status = plane.status()
     if status:
         raise SystemExit(f"the audit kernel reported status {status}")
+    per_layer = None
+    if args.record == "deferred" and not args.no_e2e:
+        # the same step recorded layer by layer (a launch per layer), for comparison
+        plane_pl = make_plane(w, deferred=False)
+        graph_pl = capture(lambda: audit_step(plane_pl, w))
+        pl_seconds = timed(graph_pl.replay, args.steps, args.warmup, dist_on)
+        per_layer = {"value": w.units_per_step() * world * args.steps / pl_seconds, "unit": "audited KV tokens/s",
+                     "ms_per_step": pl_seconds / args.steps * 1e3}
+        del graph_pl
     units_rank = w.units_per_step()
     units_all = units_rank * world
     value = units_all * args.steps / seconds
@@ -458,7 +469,8 @@ def main() -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": seconds / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak" if args.mode == "reference" else "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": args.config, "mode": args.mode, "rows": w.rows, "layers": w.layers,
+        "config": {"workload": args.config, "mode": args.mode, "record": args.record, "rows": w.rows,
+                   "layers": w.layers,
                    "q_heads": cfg["q_heads"], "kv_heads": cfg["kv_heads"], "kv_heads_per_gpu": w.kv_local,
                    "audited_heads_per_layer_per_gpu": w.heads, "block_size": BLOCK, "tile_blocks": TILE_BLOCKS,
                    "mean_len": float(w.lens.mean()), "width": w.width, "pools": cfg["pools"],
@@ -467,12 +479,13 @@ def main() -> None:
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_kind": peak_kind,
                      "bytes_per_unit": bytes_per_unit(w.heads * w.group_rows),
-                     "note": "per audit launch; duration = step time / layers, launch gaps included"},
+                     "note": "per layer; duration = step time / layers, every launch of the step included"},
         "e2e": {"value": units_all * args.steps / e2e_seconds, "unit": "audited KV tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "note": "block table, lengths, selection, query rows in; shares out; KV cache resident"},
-        "gpu_launches": args.steps * w.layers,
+        "gpu_launches": args.steps * (w.layers + 1 if args.record == "deferred" else w.layers),
         "clocks": clocks.summary(),
+        "per_layer_launches": per_layer,
         "view": view,
         "cpu_baseline": cpu,
     }

@@ -36,8 +36,7 @@ extern "C" {
 #define EKV_AGG_MAX 1
 
 /* ---- share_flags of ekv_audit_launch --------------------------------------------------------- */
-#define EKV_SHARE_RESET 1    /* this launch starts an audit step: overwrite the share accumulators */
-#define EKV_SHARE_FINALIZE 2 /* this launch ends it: write the normalised shares to share_out       */
+#define EKV_SHARE_FINALIZE 2 /* this launch ends the audit step: combine its layers into share_out   */
 
 /* ---- bits a kernel ORs into the optional device status word ---------------------------------- */
 #define EKV_STATUS_BAD_BLOCK_ID 1u  /* a table entry outside [0, pool_blocks): its keys were skipped */
@@ -50,7 +49,7 @@ extern "C" {
 #define EKV_POLICY_UNIFORM 1 /* highest share first; equal shares: the older block first           */
 #define EKV_POLICY_NEWEST 2  /* the fixed rule scores = arange(n): the newest open blocks           */
 
-/* Tiles of one audit CTA; the audit workspace holds one partial per (row, chunk of this many tiles). */
+/* Tiles of one audit work item (a chunk of a row): the unit a warp of the audit kernel takes. */
 #define EKV_AUDIT_CHUNK_TILES 8
 
 /* Human-readable description of the last error on this thread ("" if none). */
@@ -59,11 +58,11 @@ const char* ekv_last_error_string(void);
 /* ABI version of this library: bumped on any signature change. */
 int ekv_abi_version(void);
 
-/* Bytes of workspace ekv_audit_launch needs for its fused share epilogue: a ticket per row and one
- * (max, sum) partial per (row, chunk, query row). The first rows*4 bytes, rounded up to 256, are the
- * tickets: they must be zero before the first launch, and every launch leaves them zero again. */
-size_t ekv_audit_workspace_bytes(int rows, int width, int group_rows, int heads, int block_size,
-                                 int tile_blocks);
+/* Bytes of workspace the fused share of ekv_audit_launch / ekv_audit_step needs for a table of
+ * `layers` layers: tickets per (layer, row) and per row, contributors per (layer, row), and a share
+ * vector per (layer, row). It must be zero before the first launch (every launch leaves the
+ * tickets zero again) and 256-byte aligned. */
+size_t ekv_audit_workspace_bytes(int layers, int rows, int width);
 
 /*
  * ekv_audit_launch -- record the attention-share statistic of one layer.
@@ -81,15 +80,15 @@ size_t ekv_audit_workspace_bytes(int rows, int width, int group_rows, int heads,
  * l = sum_j exp(q.k_j*scale - m) over the tile's tokens below lens[row]. heads = 1 is the
  * reference's sampling (one KV group per layer, group = layer % kv_heads, :250).
  *
- * With share_acc != NULL it also folds the layer into the exact per-block attention share, in the
- * same launch: the last CTA of each row normalises that row's tile values into block shares
- * (observe/tile_shares.py:58-103 with row_blocks = ceil(lens/block_size)) and adds them (mean) or
- * takes their maximum (max) into share_acc [rows][width]; contributors [rows] counts the query rows
- * with data. EKV_SHARE_RESET overwrites instead of accumulating; EKV_SHARE_FINALIZE writes the final
- * share of every row to share_out [rows][width]: NaN for a row that is not selected or has no data.
- * workspace must hold ekv_audit_workspace_bytes(...) bytes (256-byte aligned). status (optional)
- * receives EKV_STATUS_* bits. q_tokens bounds qrow. Supported: head_dim 128, block_size*tile_blocks
- * in {16, 32, 64}, heads*group_rows <= 128, group_rows <= 16.
+ * With share_out != NULL it also folds the layer into the exact per-block attention share in the
+ * same launch: the (layer, row)'s tile values become block shares as normalize_tile_lse computes
+ * them (observe/tile_shares.py:58-103 with row_blocks = ceil(lens/block_size)), kept per layer in
+ * the workspace. With EKV_SHARE_FINALIZE (the step's last layer) the layers [0, layers) are
+ * combined -- mean or max over layers and query rows -- into share_out [rows][width] and
+ * contributors [rows] (query rows with data); a row that is not selected or has no data is NaN.
+ * status (optional) receives EKV_STATUS_* bits. q_tokens bounds qrow. Supported: head_dim 128,
+ * block_size*tile_blocks in {16, 32, 64}, tile_blocks <= 8, heads*group_rows <= 128,
+ * group_rows <= 16, rows <= 2048.
  */
 int ekv_audit_launch(const void* q, const void* k, const int32_t* table, const int32_t* lens,
                      const int32_t* qrow, const uint8_t* select, const uint32_t* flag, float* lse,
@@ -98,9 +97,41 @@ int ekv_audit_launch(const void* q, const void* k, const int32_t* table, const i
                      int64_t k_stride_head, int64_t table_stride, int layers, int rows, int width,
                      int group_rows, int block_size, int tile_blocks, int head_dim, int dtype,
                      int heads, int kv_heads, int64_t pool_blocks, int64_t q_tokens,
-                     float* share_acc, int32_t* contributors, float* share_out, int aggregate,
-                     int share_flags, void* workspace, size_t workspace_bytes, uint32_t* status,
-                     void* stream);
+                     float* share_out, int32_t* contributors, int aggregate, int share_flags,
+                     void* workspace, size_t workspace_bytes, uint32_t* status, void* stream);
+
+/*
+ * ekv_audit_stash -- keep one layer's queries for a later ekv_audit_step.
+ *
+ * Copies q[qrow[r], (group + h) * group_rows + g, :] to stash[r][h * group_rows + g][:] for every row
+ * r < rows, h < heads, g < group_rows (16-byte aligned buffers). The deferred form of
+ * RecordingPlane.record: the engine reuses its query buffer across layers, the stash does not.
+ */
+int ekv_audit_stash(const void* q, int64_t q_stride_token, int64_t q_stride_head, const int32_t* qrow,
+                    int rows, int64_t q_tokens, int group, int heads, int group_rows, int head_dim,
+                    void* stash, uint32_t* status, void* stream);
+
+/*
+ * ekv_audit_step -- every layer of an audit step in one launch.
+ *
+ * The work of n_layers ekv_audit_launch calls for layers [layer0, layer0 + n_layers), the last one
+ * finalising, in one persistent launch. k_layers and q_layers are device arrays of uint64 addresses
+ * per table layer: the key cache of layer L (as the plane's layer table holds them,
+ * runtime/audit.py:86-100) and its queries, laid out as the engine's query (q_layout 0: query head
+ * (KV head) * group_rows + g) or as a stash (q_layout 1: query head h * group_rows + g). The KV head
+ * of layer L is (group + L) % kv_heads with rotate != 0 (the reference's sampling), else
+ * group + h for h < heads. share_out, contributors and workspace are required.
+ */
+int ekv_audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table,
+                   const int32_t* lens, const int32_t* qrow, const uint8_t* select,
+                   const uint32_t* flag, float* lse, float scale, int layer0, int n_layers,
+                   int group, int rotate, int q_layout, int64_t q_stride_token,
+                   int64_t q_stride_head, int64_t k_stride_block, int64_t k_stride_pos,
+                   int64_t k_stride_head, int64_t table_stride, int layers, int rows, int width,
+                   int group_rows, int block_size, int tile_blocks, int head_dim, int dtype,
+                   int heads, int kv_heads, int64_t pool_blocks, int64_t q_tokens,
+                   float* share_out, int32_t* contributors, int aggregate, void* workspace,
+                   size_t workspace_bytes, uint32_t* status, void* stream);
 
 /*
  * ekv_normalize_tile_lse -- the controller's read of the statistic, on the device.

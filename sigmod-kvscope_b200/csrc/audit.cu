@@ -1,34 +1,44 @@
 // The audit kernel: per-tile log-sum-exp of q.K over a paged key cache, with the exact per-block
-// attention share folded in by the last CTA of each row.
+// attention share folded in, for one layer or for every layer of an audit step in one launch.
 //
-// Work unit. A CTA owns one (row, chunk of EKV_AUDIT_CHUNK_TILES tiles, KV head). Each of its WARPS
-// warps owns TPW tiles of TT tokens. At CTA start every warp asks the TMA engine for all its tiles
-// at once: one 2*D-byte bulk copy per token row (lane i copies token i), landing in a shared-memory
-// stage whose rows are padded to 2*D+16 bytes so that ldmatrix reads them without bank conflicts.
-// The copies carry an L2 evict-first hint: the keys are read once, the statistic table is not.
+// Work. An item is one (layer, KV head, row, chunk of EKV_AUDIT_CHUNK_TILES tiles); the items of a
+// launch are numbered layer-major and every warp of a persistent grid (SMs x resident CTAs) works
+// through items worker, worker + workers, ... on its own. A warp owns a ring of STAGES shared-memory
+// stages, one tile of TT tokens each, and keeps STAGES tiles in flight across item boundaries: for
+// the next tile each lane asks the TMA engine for one 2*D-byte key row (cp.async.bulk, L2
+// evict-first) and lane 0 arms the stage's mbarrier with the byte count. Rows land 2*D+16 bytes
+// apart, so ldmatrix reads them without bank conflicts.
 //
-// Scores. One m16n8k16 mma per (16 tokens, 16 dims): A = 16 key rows from shared memory through
-// ldmatrix, B = the G query rows of the KV group (held in registers for the whole CTA, padded to 8
-// or 16 columns), accumulating in fp32. The C fragment puts tokens on rows and query rows on
-// columns, so the tile max and sum are three xor-shuffles per column. This is the computation of
-// tile_lse_kernel (runtime/audit_kernel.py:70-96); the cells are stored as at :97-109.
+// Scores. One m16n8k16 mma per (16 tokens, 16 dims): A = 16 key rows by ldmatrix, B = the G query
+// rows of the KV head (registers, padded to 8 or 16 columns), fp32 accumulation. Tokens sit on the
+// C fragment's rows and query rows on its columns, so the tile max and sum are three xor-shuffles
+// per column: tile_lse_kernel's computation (runtime/audit_kernel.py:70-96), stored as at :97-109.
 //
-// Shares. Each CTA also reduces its tiles into a (max, sum) partial per query row of
-// u = m + log(l) - log(tile_blocks) (observe/tile_shares.py:172-173), writes it to the workspace and
-// takes a ticket on its row. The CTA that takes the last ticket merges the partials into the row's
-// log total per query row, reads the row's cells back (they are in L2), forms the share of every
-// block exactly as normalize_tile_lse does (:82-103, with the partial tail tile's weight given back
-// to its blocks) and adds it into the row's accumulator. No CTA waits on another.
-#include <cstdarg>
-#include <cstdio>
-
+// Shares. When a warp finishes an item it takes a ticket on the (layer, row); the warp that takes
+// the last ticket reads the row's cells back from L2, forms u = m + log(l) - log(tile_blocks)
+// (observe/tile_shares.py:172-173), the row's log total per query row, and every block's share with
+// the partial tail tile's weight given back to its blocks (:82-103), and writes the (layer, row)
+// share vector. The warp that completes a row's last layer (a second ticket, or the FINALIZE flag of
+// a single-layer launch) sums or maxes the layers in layer order and writes the row's final share.
+// No warp waits on another; every sum has a fixed order, so the output is deterministic.
 #include "ekv_common.cuh"
 
 namespace ekv {
 
+constexpr int kWarps = 4;
+constexpr int kMaxQ = 128;
+constexpr int kMaxRows = 2048;
+constexpr int kChunkTiles = EKV_AUDIT_CHUNK_TILES;
+
 struct AuditParams {
+  // per-layer sources: device arrays of addresses, or one address for a single layer
+  const uint64_t* q_layers;
+  const uint64_t* k_layers;
   const void* q;
   const void* k;
+  int layer0, n_layers;
+  int group, rotate;  // KV head of layer L: rotate ? (group + L) % kv_heads : group
+  int q_stash;        // queries hold only the audited heads: query head = head * G + g
   const int32_t* table;
   const int32_t* lens;
   const int32_t* qrow;
@@ -36,459 +46,646 @@ struct AuditParams {
   const uint32_t* flag;
   float* lse;
   float scale;
-  int layer;
-  int group;
-  int64_t q_s0, q_s1;
-  int64_t k_s0, k_s1, k_s2;
-  int64_t table_s0;
+  int64_t q_s0, q_s1, k_s0, k_s1, k_s2, table_s0;
   int layers, rows, width;
-  int G;      // query rows per KV head
-  int heads;  // KV heads recorded by this launch
-  int Q;      // values per cell: heads * G
+  int G, heads, Q;
   int block_size, tile_blocks;
-  int64_t pool_blocks;
-  int64_t q_tokens;
-  float* share_acc;
-  int32_t* contrib;
+  int kv_heads;
+  int64_t pool_blocks, q_tokens;
+  // the fused share
   float* share_out;
+  int32_t* contrib_out;
   int aggregate;
-  int share_flags;
-  uint32_t* tickets;
-  float2* partials;
-  int max_chunks;
+  int finalize;             // the launch ends the step: combine layers [0, layers) (single layer)
+  uint32_t* tickets;        // [layers][rows]
+  uint32_t* row_tickets;    // [rows]
+  int32_t* contrib_layer;   // [layers][rows]
+  float* share_layer;       // [layers][rows][width]
   uint32_t* status;
 };
 
-constexpr int kAuditWarps = 4;
-constexpr int kAuditTilesPerWarp = EKV_AUDIT_CHUNK_TILES / kAuditWarps;
-constexpr int kMaxQ = 128;
-
 template <int D>
-struct AuditLayout {
+struct Layout {
   static constexpr int kRowBytes = 2 * D;
-  static constexpr int kRowStride = 2 * D + 16;  // 16-byte pad: conflict-free ldmatrix
+  static constexpr int kRowStride = 2 * D + 16;
 };
 
-// Writes the NaN row (FINALIZE) and clears the accumulators (RESET) of a row that no CTA records.
-__device__ void audit_row_without_tiles(const AuditParams& p, int row, bool selected) {
-  const size_t base = (size_t)row * p.width;
-  if ((p.share_flags & EKV_SHARE_RESET) && selected) {
-    for (int b = threadIdx.x; b < p.width; b += blockDim.x) p.share_acc[base + b] = 0.f;
-    if (threadIdx.x == 0) p.contrib[row] = 0;
+template <int TT>
+struct Ring {
+  static constexpr int kStages = TT <= 16 ? 6 : (TT <= 32 ? 3 : 2);
+};
+
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Row r of the launch: its length, blocks, tiles and chunks; no chunks when it records nothing.
+struct RowInfo {
+  int n_blocks, n_tiles, n_chunks, len;
+};
+
+__device__ __forceinline__ RowInfo row_info(const AuditParams& p, int r, bool report) {
+  RowInfo ri{0, 0, 0, 0};
+  if (!p.select[r]) return ri;
+  int len = p.lens[r];
+  if (len <= 0) return ri;
+  int n = (len + p.block_size - 1) / p.block_size;
+  if (n > p.width) {
+    if (report) set_status(p.status, EKV_STATUS_LEN_OVER_WIDTH);
+    n = p.width;
+    len = p.width * p.block_size;
   }
-  if (p.share_flags & EKV_SHARE_FINALIZE) {
-    for (int b = threadIdx.x; b < p.width; b += blockDim.x) p.share_out[base + b] = NAN;
+  const int token = p.qrow[r];
+  if (token < 0 || (int64_t)token >= p.q_tokens) {
+    if (report) set_status(p.status, EKV_STATUS_BAD_QROW);
+    return ri;
+  }
+  ri.len = len;
+  ri.n_blocks = n;
+  ri.n_tiles = (n + p.tile_blocks - 1) / p.tile_blocks;
+  ri.n_chunks = (ri.n_tiles + kChunkTiles - 1) / kChunkTiles;
+  return ri;
+}
+
+__device__ __forceinline__ int kv_head_of(const AuditParams& p, int layer, int h) {
+  return (p.rotate ? (p.group + layer) % p.kv_heads : p.group) + h;
+}
+
+// The combine over layers [la, lb) of row r, by one warp: sum (mean) or max (max) of the layers'
+// share vectors in layer order, skipping layers without data; the row's final share and count.
+__device__ void combine_layers(const AuditParams& p, int r, int la, int lb, int n_blocks) {
+  const int lane = threadIdx.x & 31;
+  int c = 0;
+  for (int L = la + lane; L < lb; L += 32) c += __ldcg(p.contrib_layer + (size_t)L * p.rows + r);
+  for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(kFullMask, c, off);
+  float* out = p.share_out + (size_t)r * p.width;
+  if (lane == 0) p.contrib_out[r] = c;
+  if (c == 0) {
+    for (int b = lane; b < p.width; b += 32) out[b] = NAN;
+    return;
+  }
+  const bool agg_max = p.aggregate == EKV_AGG_MAX;
+  float part = 0.f;
+  for (int b = lane; b < n_blocks; b += 32) {
+    float v = 0.f;
+    for (int L = la; L < lb; ++L) {
+      if (__ldcg(p.contrib_layer + (size_t)L * p.rows + r) == 0) continue;
+      const float s = __ldcg(p.share_layer + ((size_t)L * p.rows + r) * p.width + b);
+      v = agg_max ? fmaxf(v, s) : v + s;
+    }
+    out[b] = v;
+    part += v;
+  }
+  float total = part;
+  for (int off = 16; off > 0; off >>= 1) total += __shfl_xor_sync(kFullMask, total, off);
+  for (int b = lane; b < p.width; b += 32) {
+    float v = 0.f;
+    if (b < n_blocks) v = agg_max ? (total > 0.f ? out[b] / total : 0.f) : out[b] / (float)c;
+    out[b] = v;
   }
 }
 
-// The last CTA of a row: partials -> log totals -> per-block shares -> accumulator (-> final).
-template <int THREADS>
-__device__ void audit_share_epilogue(const AuditParams& p, int row, int n_blocks, int n_chunks) {
-  __shared__ float s_lse[kMaxQ];
-  __shared__ int s_has[kMaxQ];
-  __shared__ float s_red[THREADS / 32];
-  __shared__ int s_contrib;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int Q = p.Q;
-  const int TB = p.tile_blocks;
+// The (layer, row) epilogue, run by one warp: log totals, then the share of every block.
+__device__ void layer_row_epilogue(const AuditParams& p, int L, int r, int n_blocks, float* s_lse,
+                                   uint8_t* s_has) {
+  const int lane = threadIdx.x & 31;
+  const int Q = p.Q, TB = p.tile_blocks;
+  const int n_tiles = (n_blocks + TB - 1) / TB;
   const float log_tb = logf((float)TB);
-
-  // 1. The log total of each query row: merge the chunk partials, a fixed tree per query row.
-  for (int j = warp; j < Q; j += THREADS / 32) {
-    float m = -INFINITY, s = 0.f;
-    for (int c = lane; c < n_chunks; c += 32) {
-      const float2 part = __ldcg(&p.partials[((size_t)row * p.max_chunks + c) * Q + j]);
-      lse_merge(m, s, part.x, part.y);
-    }
-    for (int off = 16; off > 0; off >>= 1) {
-      const float m2 = __shfl_xor_sync(kFullMask, m, off);
-      const float s2 = __shfl_xor_sync(kFullMask, s, off);
-      lse_merge(m, s, m2, s2);
-    }
-    if (lane == 0) {
-      s_has[j] = m != -INFINITY;
-      s_lse[j] = m != -INFINITY ? log_tb + m + logf(s) : 0.f;
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int c = 0;
-    for (int j = 0; j < Q; ++j) c += s_has[j];
-    const int prev = (p.share_flags & EKV_SHARE_RESET) ? 0 : p.contrib[row];
-    s_contrib = prev + c;
-    p.contrib[row] = prev + c;
-  }
-
-  // 2. The share of each block: exp(u + regain - log total), summed (mean) or maxed over query rows.
   const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
-  const float* cell_m = p.lse + ((size_t)p.layer * p.rows + row) * p.width * Q;
-  const float* cell_l = cell_m + plane;
-  const int tail = n_blocks % TB;
-  const int tail_start = n_blocks - tail;
-  const float regain = tail ? logf((float)TB / (float)tail) : 0.f;
-  const bool reset = (p.share_flags & EKV_SHARE_RESET) != 0;
-  const bool agg_max = p.aggregate == EKV_AGG_MAX;
-  float* acc = p.share_acc + (size_t)row * p.width;
-  const int limit = reset ? p.width : n_blocks;
-  for (int b = threadIdx.x; b < limit; b += THREADS) {
-    float a = 0.f;
-    if (b < n_blocks) {
-      const float rg = b >= tail_start ? regain : 0.f;
-      for (int j = 0; j < Q; ++j) {
-        const float m = __ldcg(cell_m + (size_t)b * Q + j);
-        const float l = __ldcg(cell_l + (size_t)b * Q + j);
-        const float u = m + logf(l) - log_tb;
-        if (s_has[j] && isfinite(u)) {
-          const float sh = __expf(u + rg - s_lse[j]);
-          a = agg_max ? fmaxf(a, sh) : a + sh;
+  const float* cm = p.lse + ((size_t)L * p.rows + r) * p.width * Q;
+  const float* cl = cm + plane;
+  // 1. the log total of each query row over the row's tiles (one cell per tile: its first block)
+  for (int j0 = 0; j0 < Q; j0 += 16) {
+    float m[16], s[16];
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) m[jj] = -INFINITY, s[jj] = 0.f;
+    for (int t = lane; t < n_tiles; t += 32) {
+      const size_t cell = (size_t)t * TB * Q + j0;
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        if (j0 + jj < Q) {
+          const float u = __ldcg(cm + cell + jj) + logf(__ldcg(cl + cell + jj)) - log_tb;
+          if (isfinite(u)) lse_merge(m[jj], s[jj], u, 1.f);
         }
       }
     }
-    const float prev = reset ? 0.f : acc[b];
-    acc[b] = agg_max ? fmaxf(prev, a) : prev + a;
-  }
-
-  // 3. On the last layer: the normalised share of the row.
-  if (p.share_flags & EKV_SHARE_FINALIZE) {
-    __syncthreads();
-    const int contributors = s_contrib;
-    float total = 1.f;
-    if (agg_max) {
-      float part = 0.f;
-      for (int b = threadIdx.x; b < n_blocks; b += THREADS) part += acc[b];
-      total = block_sum_fixed_order<THREADS>(part, s_red);
-    }
-    float* out = p.share_out + (size_t)row * p.width;
-    for (int b = threadIdx.x; b < p.width; b += THREADS) {
-      float v;
-      if (contributors == 0) {
-        v = NAN;
-      } else if (b >= n_blocks) {
-        v = 0.f;
-      } else if (agg_max) {
-        v = total > 0.f ? acc[b] / total : 0.f;
-      } else {
-        v = acc[b] / (float)contributors;
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) {
+      for (int off = 16; off > 0; off >>= 1) {
+        const float m2 = __shfl_xor_sync(kFullMask, m[jj], off);
+        const float s2 = __shfl_xor_sync(kFullMask, s[jj], off);
+        lse_merge(m[jj], s[jj], m2, s2);
       }
-      out[b] = v;
+      if (lane == 0 && j0 + jj < Q) {
+        s_has[j0 + jj] = m[jj] != -INFINITY;
+        s_lse[j0 + jj] = m[jj] != -INFINITY ? log_tb + m[jj] + logf(s[jj]) : 0.f;
+      }
     }
   }
+  __syncwarp();
+  int c = 0;
+  for (int j = lane; j < Q; j += 32) c += s_has[j];
+  for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(kFullMask, c, off);
+  // 2. every block's share, summed (mean) or maxed (max) over the query rows
+  const int tail = n_blocks % TB;
+  const int tail_start = n_blocks - tail;
+  const float regain = tail ? logf((float)TB / (float)tail) : 0.f;
+  const bool agg_max = p.aggregate == EKV_AGG_MAX;
+  float* sl = p.share_layer + ((size_t)L * p.rows + r) * p.width;
+  for (int b = lane; b < n_blocks; b += 32) {
+    const float rg = b >= tail_start ? regain : 0.f;
+    float a = 0.f;
+    for (int j = 0; j < Q; ++j) {
+      if (!s_has[j]) continue;
+      const float u = __ldcg(cm + (size_t)b * Q + j) + logf(__ldcg(cl + (size_t)b * Q + j)) - log_tb;
+      if (isfinite(u)) {
+        const float sh = __expf(u + rg - s_lse[j]);
+        a = agg_max ? fmaxf(a, sh) : a + sh;
+      }
+    }
+    sl[b] = a;
+  }
+  if (lane == 0) p.contrib_layer[(size_t)L * p.rows + r] = c;
+  __syncwarp();
 }
 
-template <typename T, int D, int TT, int NT>
-__global__ void __launch_bounds__(kAuditWarps * 32)
-    audit_kernel(const AuditParams p) {
-  using L = AuditLayout<D>;
-  constexpr int THREADS = kAuditWarps * 32;
-  constexpr int TPW = kAuditTilesPerWarp;
-  constexpr int CT = EKV_AUDIT_CHUNK_TILES;
-  constexpr int STAGE = TT * L::kRowStride;
-  constexpr int MT = TT / 16;     // m16 tiles per token tile
-  constexpr int KS = D / 16;      // k16 steps over the head dimension
-  constexpr int TOK_PER_LANE = (TT + 31) / 32;
+// A warp's position in its sequence of tiles: the item and the tile inside it.
+struct Cursor {
+  long long item;  // index into the launch's items; >= the total when done
+  int layer, head, row, t, t_end;
+};
+
+template <int TT, int NT, int D, typename T>
+__global__ void __launch_bounds__(kWarps * 32) audit_kernel(const AuditParams p) {
+  using Lay = Layout<D>;
+  constexpr int STAGES = Ring<TT>::kStages;
+  constexpr int STAGE = TT * Lay::kRowStride;
+  constexpr int MT = TT / 16;
+  constexpr int KS = D / 16;
+  constexpr int WORDS = (TT + 31) / 32;
 
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + CT * STAGE);
-  __shared__ float2 s_merge[kAuditWarps][16];
-  __shared__ int s_last;
+  uint8_t* rings = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * STAGES * STAGE);
+  uint32_t* vmasks = reinterpret_cast<uint32_t*>(bars + kWarps * STAGES);  // [warp][stage][WORDS]
+  int* prefix = reinterpret_cast<int*>(vmasks + kWarps * STAGES * WORDS);  // [rows + 1]
+  __shared__ float s_lse[kWarps][kMaxQ];
+  __shared__ uint8_t s_has[kWarps][kMaxQ];
+  __shared__ int s_scan[kWarps + 1];
 
-  const int chunk = blockIdx.x, row = blockIdx.y, head = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  if (*p.flag == 0) return;  // the statistic is off: this launch records nothing (:64)
-  const bool selected = p.select[row] != 0;
-  const bool with_share = p.share_acc != nullptr;
-  const int BS = p.block_size, TB = p.tile_blocks;
-
-  int len = p.lens[row];
-  if (len < 0) len = 0;
-  int n_blocks = (len + BS - 1) / BS;
-  if (n_blocks > p.width) {
-    if (chunk == 0 && head == 0 && threadIdx.x == 0) set_status(p.status, EKV_STATUS_LEN_OVER_WIDTH);
-    n_blocks = p.width;
-    len = p.width * BS;
-  }
-  const int token = p.qrow[row];
-  const bool bad_qrow = token < 0 || (int64_t)token >= p.q_tokens;
-  if (selected && n_blocks > 0 && bad_qrow) {
-    if (chunk == 0 && head == 0 && threadIdx.x == 0) set_status(p.status, EKV_STATUS_BAD_QROW);
-  }
-  const int n_tiles = (n_blocks + TB - 1) / TB;
-  const int n_chunks = (n_tiles + CT - 1) / CT;
-  if (!selected || n_tiles == 0 || bad_qrow) {
-    if (with_share && chunk == 0 && head == 0) audit_row_without_tiles(p, row, selected);
+  const bool with_share = p.share_layer != nullptr;
+  if (*p.flag == 0) {  // the statistic is off: nothing is recorded (:64)
+    if (with_share && blockIdx.x == 0)
+      for (int i = threadIdx.x; i < p.n_layers * p.rows; i += blockDim.x)
+        p.contrib_layer[(size_t)(p.layer0 + i / p.rows) * p.rows + i % p.rows] = 0;
     return;
   }
-  if (chunk >= n_chunks) return;
 
-  const int kv_head = p.group + head;
-  const T* kbase = static_cast<const T*>(p.k) + (int64_t)kv_head * p.k_s2;
-  const int32_t* trow = p.table + (int64_t)row * p.table_s0;
+  // ---- the launch's items: chunks per row, prefix-summed in shared memory ------------------------
+  {
+    int carry = 0;
+    for (int base = 0; base < p.rows; base += kWarps * 32) {
+      const int r = base + threadIdx.x;
+      const int chunks = r < p.rows ? row_info(p, r, blockIdx.x == 0).n_chunks : 0;
+      int total = 0;
+      const int before = block_exclusive_scan<kWarps * 32>(chunks, s_scan, &total);
+      if (r < p.rows) prefix[r] = carry + before;
+      carry += total;
+    }
+    if (threadIdx.x == 0) prefix[p.rows] = carry;
+    __syncthreads();
+  }
+  const int chunks_per_lh = prefix[p.rows];
+  const long long total_items = (long long)chunks_per_lh * p.heads * p.n_layers;
 
-  // ---- issue every bulk copy of this warp's tiles --------------------------------------------
+  // ---- rows that record nothing: no contributors; NaN share rows in a finalising launch ----------
+  if (with_share) {
+    for (int r = blockIdx.x; r < p.rows; r += gridDim.x) {
+      if (prefix[r + 1] != prefix[r]) continue;
+      for (int i = threadIdx.x; i < p.n_layers; i += blockDim.x)
+        p.contrib_layer[(size_t)(p.layer0 + i) * p.rows + r] = 0;
+      if (p.finalize) {
+        for (int b = threadIdx.x; b < p.width; b += blockDim.x) p.share_out[(size_t)r * p.width + b] = NAN;
+        if (threadIdx.x == 0) p.contrib_out[r] = 0;
+      }
+    }
+  }
+
+  const long long workers = (long long)gridDim.x * kWarps;
+  const long long worker = (long long)blockIdx.x * kWarps + warp;
+  if (worker >= total_items) return;
+
+  auto decode = [&](long long item, Cursor& c) {
+    c.item = item;
+    if (item >= total_items) return;
+    const long long lh = item / chunks_per_lh;
+    const int idx = (int)(item - lh * chunks_per_lh);
+    int lo = 0, hi = p.rows;  // the last row with prefix[row] <= idx
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (prefix[mid] <= idx) lo = mid; else hi = mid;
+    }
+    c.row = lo;
+    c.layer = p.layer0 + (int)(lh / p.heads);
+    c.head = (int)(lh % p.heads);
+    const int chunk = idx - prefix[lo];
+    const RowInfo ri = row_info(p, lo, false);
+    c.t = chunk * kChunkTiles;
+    c.t_end = min(c.t + kChunkTiles, ri.n_tiles);
+  };
+  auto advance = [&](Cursor& c) {
+    if (++c.t >= c.t_end) decode(c.item + workers, c);
+  };
+
+  uint8_t* my_ring = rings + warp * STAGES * STAGE;
+  uint64_t* my_bars = bars + warp * STAGES;
+  uint32_t* my_masks = vmasks + warp * STAGES * WORDS;
   if (lane == 0) {
-    for (int i = 0; i < TPW; ++i) mbar_init(&bars[warp * TPW + i], 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(&my_bars[s], 1);
     fence_mbar_init();
   }
   __syncwarp();
   const uint64_t policy = l2_evict_first_policy();
-  uint32_t vmask[TPW][TOK_PER_LANE];  // ballot of tokens whose block was copied, per tile
-#pragma unroll
-  for (int i = 0; i < TPW; ++i) {
-    const int t = chunk * CT + i * kAuditWarps + warp;
-    uint8_t* stage = smem + (warp * TPW + i) * STAGE;
-    uint64_t* bar = &bars[warp * TPW + i];
-#pragma unroll
-    for (int r = 0; r < TOK_PER_LANE; ++r) vmask[i][r] = 0;
-    if (t >= n_tiles) continue;
-    int64_t src_off[TOK_PER_LANE];
+
+  // Issue the bulk copies of the tile at cursor c into stage s.
+  auto issue = [&](const Cursor& c, int s) {
+    const RowInfo ri = row_info(p, c.row, false);
+    const T* kbase = static_cast<const T*>(p.k_layers ? reinterpret_cast<const void*>(p.k_layers[c.layer]) : p.k);
+    const bool aligned = (reinterpret_cast<uintptr_t>(kbase) & 15) == 0;
+    kbase += (int64_t)kv_head_of(p, c.layer, c.head) * p.k_s2;
+    const int32_t* trow = p.table + (int64_t)c.row * p.table_s0;
     uint32_t total = 0;
+    int64_t off[WORDS];
+    uint32_t mask[WORDS];
 #pragma unroll
-    for (int r = 0; r < TOK_PER_LANE; ++r) {
-      const int tok = lane + 32 * r;
+    for (int w = 0; w < WORDS; ++w) {
+      const int tok = lane + 32 * w;
       bool ok = false;
-      src_off[r] = 0;
+      off[w] = 0;
       if (tok < TT) {
-        const int b = t * TB + tok / BS;
-        if (b < n_blocks) {
+        const int b = c.t * p.tile_blocks + tok / p.block_size;
+        if (b < ri.n_blocks) {
           const int32_t id = __ldg(trow + b);
-          ok = id >= 0 && (int64_t)id < p.pool_blocks;
-          if (!ok && tok % BS == 0) set_status(p.status, EKV_STATUS_BAD_BLOCK_ID);
-          src_off[r] = (int64_t)id * p.k_s0 + (int64_t)(tok % BS) * p.k_s1;
+          ok = aligned && id >= 0 && (int64_t)id < p.pool_blocks;
+          if (!ok && tok % p.block_size == 0) set_status(p.status, EKV_STATUS_BAD_BLOCK_ID);
+          off[w] = (int64_t)id * p.k_s0 + (int64_t)(tok % p.block_size) * p.k_s1;
         }
       }
-      vmask[i][r] = __ballot_sync(kFullMask, ok);
-      total += __popc(vmask[i][r]);
+      mask[w] = __ballot_sync(kFullMask, ok);
+      total += __popc(mask[w]);
     }
     if (lane == 0) {
+#pragma unroll
+      for (int w = 0; w < WORDS; ++w) my_masks[s * WORDS + w] = mask[w];
       if (total) {
-        mbar_arrive_expect_tx(bar, total * L::kRowBytes);
+        mbar_arrive_expect_tx(&my_bars[s], total * Lay::kRowBytes);
       } else {
-        mbar_arrive(bar);
+        mbar_arrive(&my_bars[s]);
       }
     }
     __syncwarp();
+    uint8_t* stage = my_ring + s * STAGE;
 #pragma unroll
-    for (int r = 0; r < TOK_PER_LANE; ++r) {
-      if ((vmask[i][r] >> lane) & 1u) {
-        const int tok = lane + 32 * r;
-        bulk_copy_g2s(stage + tok * L::kRowStride, kbase + src_off[r], L::kRowBytes, bar, policy);
-      }
-    }
+    for (int w = 0; w < WORDS; ++w)
+      if ((mask[w] >> lane) & 1u)
+        bulk_copy_g2s(stage + (lane + 32 * w) * Lay::kRowStride, kbase + off[w], Lay::kRowBytes, &my_bars[s], policy);
+  };
+
+  // ---- prologue: fill the ring ---------------------------------------------------------------------
+  Cursor in{}, out{};
+  decode(worker, in);
+  out = in;
+  long long issued = 0;
+  for (int s = 0; s < STAGES && in.item < total_items; ++s) {
+    issue(in, s);
+    ++issued;
+    advance(in);
   }
 
-  // ---- the query rows of this KV head, as mma B fragments (k16 x n8, column = query row) ------
-  uint32_t bq[NT][KS][2];
-  {
-    const T* qtok = static_cast<const T*>(p.q) + (int64_t)token * p.q_s0;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int g = nt * 8 + (lane >> 2);
-      const bool ok = g < p.G;
-      const T* qh = qtok + (int64_t)(kv_head * p.G + (ok ? g : 0)) * p.q_s1;
-#pragma unroll
-      for (int s = 0; s < KS; ++s) {
-        const int d = s * 16 + 2 * (lane & 3);
-        bq[nt][s][0] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qh + d)) : 0u;
-        bq[nt][s][1] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qh + d + 8)) : 0u;
-      }
-    }
-  }
-
-  // ---- consume the tiles in order --------------------------------------------------------------
-  const float log_tb = logf((float)TB);
   const size_t plane = (size_t)p.layers * p.rows * p.width * p.Q;
-  float* cell_row = p.lse + ((size_t)p.layer * p.rows + row) * p.width * p.Q + head * p.G;
-  float run_m[NT][2], run_s[NT][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) run_m[nt][e] = -INFINITY, run_s[nt][e] = 0.f;
+  uint32_t bq[NT][KS][2];
+  int q_layer = -1, q_row = -1, q_head = -1;
   bool timed_out = false;
+  long long consumed = 0, unwaited = 0;  // copies from tile `unwaited` on were never waited for
 
+  while (out.item < total_items) {
+    const int s = (int)(consumed % STAGES);
+    const uint32_t parity = (uint32_t)((consumed / STAGES) & 1);
+    // the query rows of this (layer, row, head), as mma B fragments
+    if (out.layer != q_layer || out.row != q_row || out.head != q_head) {
+      q_layer = out.layer, q_row = out.row, q_head = out.head;
+      const void* qsrc = p.q_layers ? reinterpret_cast<const void*>(p.q_layers[out.layer]) : p.q;
+      const bool q_ok = (reinterpret_cast<uintptr_t>(qsrc) & 3) == 0;
+      const T* qtok = static_cast<const T*>(qsrc) + (int64_t)p.qrow[out.row] * p.q_s0;
+      const int qhead = p.q_stash ? out.head : kv_head_of(p, out.layer, out.head);
 #pragma unroll
-  for (int i = 0; i < TPW; ++i) {
-    const int t = chunk * CT + i * kAuditWarps + warp;
-    if (t >= n_tiles || timed_out) continue;
-    uint8_t* stage = smem + (warp * TPW + i) * STAGE;
-    if (!mbar_wait_bounded(&bars[warp * TPW + i], 0, p.status)) {
-      timed_out = true;
-      continue;
+      for (int nt = 0; nt < NT; ++nt) {
+        const int g = nt * 8 + (lane >> 2);
+        const bool ok = q_ok && g < p.G;
+        const T* qh = qtok + (int64_t)(qhead * p.G + (ok ? g : 0)) * p.q_s1;
+#pragma unroll
+        for (int k = 0; k < KS; ++k) {
+          const int d = k * 16 + 2 * (lane & 3);
+          bq[nt][k][0] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qh + d)) : 0u;
+          bq[nt][k][1] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qh + d + 8)) : 0u;
+        }
+      }
     }
-    float c[MT][NT][4];
+    if (!timed_out && !mbar_wait_bounded(&my_bars[s], parity, p.status)) {
+      timed_out = true;
+      unwaited = consumed;
+    }
+    const RowInfo ri = row_info(p, out.row, false);
+    if (!timed_out) {
+      const uint8_t* stage = my_ring + s * STAGE;
+      float c[MT][NT][4];
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) c[mt][nt][e] = 0.f;
+      const uint32_t a_base =
+          smem_u32(stage) + ((lane & 7) + ((lane >> 3) & 1) * 8) * Lay::kRowStride + (lane >> 4) * 16;
+#pragma unroll
+      for (int k = 0; k < KS; ++k) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          uint32_t a[4];
+          ldmatrix_x4(a, a_base + mt * 16 * Lay::kRowStride + k * 32);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) Mma<T>::run(c[mt][nt], a, bq[nt][k]);
+        }
+      }
+      uint32_t vm[WORDS];
+#pragma unroll
+      for (int w = 0; w < WORDS; ++w) vm[w] = my_masks[s * WORDS + w];
+      const int first = out.t * TT;
+      float mx[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mx[nt][0] = mx[nt][1] = -INFINITY;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int tok = mt * 16 + (lane >> 2) + 8 * h;  // bit tok % 32 of word tok / 32 = mt / 2
+          const bool ok = first + tok < ri.len && ((vm[mt >> 1] >> (tok & 31)) & 1u);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float sc = ok ? c[mt][nt][2 * h + e] * p.scale : -INFINITY;
+              c[mt][nt][2 * h + e] = sc;
+              mx[nt][e] = fmaxf(mx[nt][e], sc);
+            }
+        }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) c[mt][nt][e] = 0.f;
-    const uint32_t a_base =
-        smem_u32(stage) + ((lane & 7) + ((lane >> 3) & 1) * 8) * L::kRowStride + (lane >> 4) * 16;
+        for (int e = 0; e < 2; ++e)
 #pragma unroll
-    for (int s = 0; s < KS; ++s) {
+          for (int off = 4; off < 32; off <<= 1)
+            mx[nt][e] = fmaxf(mx[nt][e], __shfl_xor_sync(kFullMask, mx[nt][e], off));
+      float sm[NT][2];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        uint32_t a[4];
-        ldmatrix_x4(a, a_base + mt * 16 * L::kRowStride + s * 32);
+      for (int nt = 0; nt < NT; ++nt) sm[nt][0] = sm[nt][1] = 0.f;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) Mma<T>::run(c[mt][nt], a, bq[nt][s]);
-      }
-    }
-    // scale, mask tokens at or past the length (or of a skipped block), column max and sum
-    const int first = t * TT;
-    float mx[NT][2];
+      for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) mx[nt][0] = mx[nt][1] = -INFINITY;
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+          for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int tok = mt * 16 + (lane >> 2) + 8 * h;  // vmask word mt / 2, bit tok % 32
-        const bool ok = first + tok < len && ((vmask[i][mt >> 1] >> ((mt & 1) * 16 + (lane >> 2) + 8 * h)) & 1u);
+            for (int e = 0; e < 2; ++e) sm[nt][e] += __expf(c[mt][nt][2 * h + e] - mx[nt][e]);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+#pragma unroll
+          for (int off = 4; off < 32; off <<= 1) sm[nt][e] += __shfl_xor_sync(kFullMask, sm[nt][e], off);
+      // every block cell of the tile inside the row gets the tile's (m, l); lane / 4 picks the block
+      const int bi = lane >> 2;
+      const int b = out.t * p.tile_blocks + bi;
+      if (bi < p.tile_blocks && b < ri.n_blocks) {
+        float* cm = p.lse + (((size_t)out.layer * p.rows + out.row) * p.width + b) * p.Q + out.head * p.G;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const float sc = ok ? c[mt][nt][2 * h + e] * p.scale : -INFINITY;
-            c[mt][nt][2 * h + e] = sc;
-            mx[nt][e] = fmaxf(mx[nt][e], sc);
+            const int g = nt * 8 + 2 * (lane & 3) + e;
+            if (g < p.G) {
+              cm[g] = mx[nt][e];
+              cm[g + plane] = sm[nt][e];
+            }
           }
       }
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e)
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1)
-          mx[nt][e] = fmaxf(mx[nt][e], __shfl_xor_sync(kFullMask, mx[nt][e], off));
-    float sm[NT][2];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) sm[nt][0] = sm[nt][1] = 0.f;
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) sm[nt][e] += __expf(c[mt][nt][2 * h + e] - mx[nt][e]);
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e)
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1)
-          sm[nt][e] += __shfl_xor_sync(kFullMask, sm[nt][e], off);
-
-    // every block cell of the tile inside the row gets the tile's (m, l); lane/4 picks the block
-    const int bi = lane >> 2;
-    const int b = t * TB + bi;
-    if (bi < TB && b < n_blocks) {
-      float* cm = cell_row + (size_t)b * p.Q;
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int g = nt * 8 + 2 * (lane & 3) + e;
-          if (g < p.G) {
-            cm[g] = mx[nt][e];
-            cm[g + plane] = sm[nt][e];
+    }
+    // the stage is consumed: refill it with the tile STAGES ahead
+    __syncwarp();
+    fence_proxy_async();
+    ++consumed;
+    if (in.item < total_items && !timed_out) {
+      issue(in, (int)(issued % STAGES));
+      ++issued;
+      advance(in);
+    }
+    // an item ends: take its ticket; the last one of the (layer, row) runs the epilogue
+    const Cursor done = out;
+    advance(out);
+    if (with_share && done.t + 1 >= done.t_end) {
+      __threadfence();
+      uint32_t last = 0;
+      if (lane == 0) {
+        const uint32_t target = (uint32_t)(ri.n_chunks * p.heads);
+        last = atomicAdd(&p.tickets[(size_t)done.layer * p.rows + done.row], 1u) == target - 1;
+      }
+      last = __shfl_sync(kFullMask, last, 0);
+      if (last) {
+        __threadfence();
+        if (lane == 0) p.tickets[(size_t)done.layer * p.rows + done.row] = 0;
+        layer_row_epilogue(p, done.layer, done.row, ri.n_blocks, s_lse[warp], s_has[warp]);
+        __threadfence();
+        if (p.n_layers == 1) {
+          if (p.finalize) combine_layers(p, done.row, 0, p.layers, ri.n_blocks);
+        } else {
+          uint32_t row_last = 0;
+          if (lane == 0) row_last = atomicAdd(&p.row_tickets[done.row], 1u) == (uint32_t)(p.n_layers - 1);
+          row_last = __shfl_sync(kFullMask, row_last, 0);
+          if (row_last) {
+            __threadfence();
+            if (lane == 0) p.row_tickets[done.row] = 0;
+            combine_layers(p, done.row, p.layer0, p.layer0 + p.n_layers, ri.n_blocks);
           }
         }
-    }
-    if (with_share) {
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float u = mx[nt][e] + logf(sm[nt][e]) - log_tb;
-          if (isfinite(u)) lse_merge(run_m[nt][e], run_s[nt][e], u, 1.f);
-        }
+      }
     }
   }
   if (timed_out) {
-    // Let every copy still in flight land before the CTA's shared memory is released.
-#pragma unroll
-    for (int i = 0; i < TPW; ++i) {
-      const int t = chunk * CT + i * kAuditWarps + warp;
-      if (t < n_tiles) mbar_wait_bounded(&bars[warp * TPW + i], 0, p.status);
-    }
+    // let copies still in flight land before the shared memory is released
+    for (long long i = unwaited; i < issued; ++i)
+      mbar_wait_bounded(&my_bars[i % STAGES], (uint32_t)((i / STAGES) & 1), p.status);
   }
-  if (!with_share) return;
-
-  // ---- this CTA's (max, sum) partial per query row, then the row ticket ------------------------
-  if (lane < 4) {
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) s_merge[warp][nt * 8 + 2 * lane + e] = make_float2(run_m[nt][e], run_s[nt][e]);
-  }
-  __syncthreads();
-  if (threadIdx.x < p.G) {
-    float m = -INFINITY, s = 0.f;
-    for (int w = 0; w < kAuditWarps; ++w) lse_merge(m, s, s_merge[w][threadIdx.x].x, s_merge[w][threadIdx.x].y);
-    p.partials[((size_t)row * p.max_chunks + chunk) * p.Q + head * p.G + threadIdx.x] = make_float2(m, s);
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const uint32_t ticket = atomicAdd(&p.tickets[row], 1u);
-    s_last = ticket == (uint32_t)(n_chunks * p.heads - 1);
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  if (threadIdx.x == 0) p.tickets[row] = 0;  // ready for the next launch
-  audit_share_epilogue<THREADS>(p, row, n_blocks, n_chunks);
 }
 
-template <typename T, int D, int TT, int NT>
+template <int TT, int NT, int D, typename T>
 int launch_audit(const AuditParams& p, cudaStream_t stream) {
-  using L = AuditLayout<D>;
-  constexpr int smem = EKV_AUDIT_CHUNK_TILES * TT * L::kRowStride + EKV_AUDIT_CHUNK_TILES * 8;
-  static bool configured[kMaxDevices] = {};
+  using Lay = Layout<D>;
+  constexpr int STAGES = Ring<TT>::kStages;
+  constexpr int WORDS = (TT + 31) / 32;
+  constexpr size_t fixed = (size_t)kWarps * STAGES * TT * Lay::kRowStride + kWarps * STAGES * (8 + WORDS * 4);
+  const size_t smem = fixed + (size_t)(p.rows + 1) * 4;
+  static int grid_of[kMaxDevices] = {};
+  static size_t smem_of[kMaxDevices] = {};
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
     return check_launch("cudaGetDevice");
-  if (!configured[device]) {
-    if (cudaFuncSetAttribute(audit_kernel<T, D, TT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             smem) != cudaSuccess)
+  auto kernel = audit_kernel<TT, NT, D, T>;
+  if (grid_of[device] == 0 || smem_of[device] != smem) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(fixed + (size_t)(kMaxRows + 1) * 4)) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(audit_kernel)");
-    configured[device] = true;
+    int sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+      return check_launch("cudaDeviceGetAttribute");
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kWarps * 32, smem) != cudaSuccess)
+      return check_launch("cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    grid_of[device] = sms * (per_sm > 0 ? per_sm : 1);
+    smem_of[device] = smem;
   }
-  const int tiles = cdiv(p.width, p.tile_blocks);
-  dim3 grid(cdiv(tiles, EKV_AUDIT_CHUNK_TILES), p.rows, p.heads);
-  audit_kernel<T, D, TT, NT><<<grid, kAuditWarps * 32, smem, stream>>>(p);
+  kernel<<<grid_of[device], kWarps * 32, smem, stream>>>(p);
   return check_launch("audit_kernel");
 }
 
 template <typename T>
-int dispatch_audit(const AuditParams& p, int tt, cudaStream_t stream) {
+int dispatch(const AuditParams& p, int tt, cudaStream_t stream) {
   const int nt = p.G <= 8 ? 1 : 2;
   switch (tt * 4 + nt) {
-    case 16 * 4 + 1: return launch_audit<T, 128, 16, 1>(p, stream);
-    case 16 * 4 + 2: return launch_audit<T, 128, 16, 2>(p, stream);
-    case 32 * 4 + 1: return launch_audit<T, 128, 32, 1>(p, stream);
-    case 32 * 4 + 2: return launch_audit<T, 128, 32, 2>(p, stream);
-    case 64 * 4 + 1: return launch_audit<T, 128, 64, 1>(p, stream);
-    case 64 * 4 + 2: return launch_audit<T, 128, 64, 2>(p, stream);
+    case 16 * 4 + 1: return launch_audit<16, 1, 128, T>(p, stream);
+    case 16 * 4 + 2: return launch_audit<16, 2, 128, T>(p, stream);
+    case 32 * 4 + 1: return launch_audit<32, 1, 128, T>(p, stream);
+    case 32 * 4 + 2: return launch_audit<32, 2, 128, T>(p, stream);
+    case 64 * 4 + 1: return launch_audit<64, 1, 128, T>(p, stream);
+    case 64 * 4 + 2: return launch_audit<64, 2, 128, T>(p, stream);
     default: break;
   }
   return fail(EKV_ENOTSUP, "no audit kernel for a tile of %d tokens", tt);
 }
 
-size_t audit_ticket_bytes(int rows) { return round_up((size_t)rows * 4, 256); }
+struct WorkspaceLayout {
+  size_t tickets, row_tickets, contrib, share, total;
+};
+
+WorkspaceLayout workspace_layout(int layers, int rows, int width) {
+  WorkspaceLayout w{};
+  w.tickets = 0;
+  w.row_tickets = round_up((size_t)layers * rows * 4, 256);
+  w.contrib = w.row_tickets + round_up((size_t)rows * 4, 256);
+  w.share = w.contrib + round_up((size_t)layers * rows * 4, 256);
+  w.total = w.share + round_up((size_t)layers * rows * width * 4, 256);
+  return w;
+}
+
+// Checks shared by both entry points; fills the common fields of p.
+int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int32_t* qrow,
+            const uint8_t* select, const uint32_t* flag, float* lse, float scale, int64_t q_s0,
+            int64_t q_s1, int64_t k_s0, int64_t k_s1, int64_t k_s2, int64_t table_s0, int layers,
+            int rows, int width, int group_rows, int block_size, int tile_blocks, int head_dim,
+            int dtype, int heads, int kv_heads, int64_t pool_blocks, int64_t q_tokens,
+            float* share_out, int32_t* contributors, int aggregate, void* workspace,
+            size_t workspace_bytes, uint32_t* status) {
+  if (!table || !lens || !qrow || !select || !flag || !lse)
+    return fail(EKV_EINVAL, "a required device pointer is NULL");
+  if (rows <= 0 || width <= 0 || layers <= 0) return fail(EKV_EINVAL, "rows, width and layers must be positive");
+  if (rows > kMaxRows) return fail(EKV_ENOTSUP, "%d rows: this build handles up to %d", rows, kMaxRows);
+  if (group_rows < 1 || group_rows > 16)
+    return fail(EKV_EINVAL, "%d query heads per KV head: the kernel handles 1 to 16", group_rows);
+  if (heads < 1 || heads > kv_heads) return fail(EKV_EINVAL, "%d heads per layer of a cache with %d", heads, kv_heads);
+  if (heads * group_rows > kMaxQ) return fail(EKV_ENOTSUP, "%d values per cell exceed %d", heads * group_rows, kMaxQ);
+  if (block_size <= 0 || tile_blocks <= 0) return fail(EKV_EINVAL, "block_size and tile_blocks must be positive");
+  const int tt = block_size * tile_blocks;
+  if (tt & (tt - 1)) return fail(EKV_EINVAL, "a tile of the audit kernel must hold a power of two of tokens");
+  if (tile_blocks > 8) return fail(EKV_ENOTSUP, "tile_blocks %d: this build handles up to 8", tile_blocks);
+  if (head_dim != 128) return fail(EKV_ENOTSUP, "head_dim %d: this build has kernels for 128", head_dim);
+  if (dtype != EKV_DTYPE_F16 && dtype != EKV_DTYPE_BF16) return fail(EKV_EINVAL, "unknown dtype %d", dtype);
+  if (pool_blocks <= 0 || q_tokens <= 0) return fail(EKV_EINVAL, "pool_blocks and q_tokens must be positive");
+  if ((k_s0 & 7) || (k_s1 & 7) || (k_s2 & 7))
+    return fail(EKV_EINVAL, "the key cache's strides must be whole 16-byte units");
+  if ((q_s0 & 1) || (q_s1 & 1)) return fail(EKV_EINVAL, "the query's strides must be even");
+  if (table_s0 < width) return fail(EKV_EINVAL, "table_stride %lld < width %d", (long long)table_s0, width);
+  if (aggregate != EKV_AGG_MEAN && aggregate != EKV_AGG_MAX) return fail(EKV_EINVAL, "unknown aggregate %d", aggregate);
+  p.table = table; p.lens = lens; p.qrow = qrow; p.select = select; p.flag = flag; p.lse = lse;
+  p.scale = scale; p.q_s0 = q_s0; p.q_s1 = q_s1; p.k_s0 = k_s0; p.k_s1 = k_s1; p.k_s2 = k_s2;
+  p.table_s0 = table_s0; p.layers = layers; p.rows = rows; p.width = width; p.G = group_rows;
+  p.heads = heads; p.Q = heads * group_rows; p.block_size = block_size; p.tile_blocks = tile_blocks;
+  p.kv_heads = kv_heads; p.pool_blocks = pool_blocks; p.q_tokens = q_tokens; p.status = status;
+  p.share_out = share_out; p.contrib_out = contributors; p.aggregate = aggregate;
+  if (share_out) {
+    if (!contributors) return fail(EKV_EINVAL, "share_out needs contributors");
+    const WorkspaceLayout w = workspace_layout(layers, rows, width);
+    if (!workspace || workspace_bytes < w.total)
+      return fail(EKV_ERANGE, "the audit workspace holds %zu bytes, the launch needs %zu", workspace_bytes, w.total);
+    if ((uintptr_t)workspace & 255) return fail(EKV_EINVAL, "the audit workspace must be 256-byte aligned");
+    uint8_t* base = static_cast<uint8_t*>(workspace);
+    p.tickets = reinterpret_cast<uint32_t*>(base + w.tickets);
+    p.row_tickets = reinterpret_cast<uint32_t*>(base + w.row_tickets);
+    p.contrib_layer = reinterpret_cast<int32_t*>(base + w.contrib);
+    p.share_layer = reinterpret_cast<float*>(base + w.share);
+  }
+  return EKV_OK;
+}
+
+// Copies the query rows of the audited heads of every row, q[qrow[r], (group + h) * G + g, :], into
+// stash[r][h * G + g][:] (16 bytes per thread), so a later multi-layer launch can read them.
+template <int D>
+__global__ void __launch_bounds__(256) stash_kernel(const uint8_t* q, int64_t q_s0, int64_t q_s1,
+                                                    const int32_t* qrow, int rows, int64_t q_tokens,
+                                                    int first_head, int heads_x_g, uint8_t* stash,
+                                                    uint32_t* status) {
+  constexpr int kChunks = 2 * D / 16;  // 16-byte pieces of one query row
+  const long long total = (long long)rows * heads_x_g * kChunks;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int piece = (int)(i % kChunks);
+    const long long rj = i / kChunks;
+    const int j = (int)(rj % heads_x_g);
+    const int r = (int)(rj / heads_x_g);
+    const int token = qrow[r];
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (token >= 0 && (int64_t)token < q_tokens) {
+      v = *reinterpret_cast<const uint4*>(q + 2 * ((int64_t)token * q_s0 + (int64_t)(first_head + j) * q_s1) + 16 * piece);
+    } else if (piece == 0 && j == 0) {
+      set_status(status, EKV_STATUS_BAD_QROW);
+    }
+    *reinterpret_cast<uint4*>(stash + ((long long)r * heads_x_g + j) * 2 * D + 16 * piece) = v;
+  }
+}
 
 }  // namespace ekv
 
 using namespace ekv;
 
-extern "C" size_t ekv_audit_workspace_bytes(int rows, int width, int group_rows, int heads,
-                                            int block_size, int tile_blocks) {
-  (void)block_size;
-  if (rows <= 0 || width <= 0 || group_rows <= 0 || heads <= 0 || tile_blocks <= 0) return 0;
-  const int chunks = cdiv(cdiv(width, tile_blocks), EKV_AUDIT_CHUNK_TILES);
-  return audit_ticket_bytes(rows) + (size_t)rows * chunks * heads * group_rows * sizeof(float2);
+extern "C" int ekv_audit_stash(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                               const int32_t* qrow, int rows, int64_t q_tokens, int group, int heads,
+                               int group_rows, int head_dim, void* stash, uint32_t* status, void* stream) {
+  clear_error();
+  if (!q || !qrow || !stash) return fail(EKV_EINVAL, "a required device pointer is NULL");
+  if (rows <= 0 || heads <= 0 || group_rows <= 0 || group < 0 || q_tokens <= 0)
+    return fail(EKV_EINVAL, "rows, heads, group_rows and q_tokens must be positive");
+  if (head_dim != 128) return fail(EKV_ENOTSUP, "head_dim %d: this build has kernels for 128", head_dim);
+  if (((uintptr_t)q & 15) || (q_stride_token & 7) || (q_stride_head & 7) || ((uintptr_t)stash & 15))
+    return fail(EKV_EINVAL, "the query and the stash must be 16-byte aligned with strides of whole 16-byte units");
+  const long long pieces = (long long)rows * heads * group_rows * (2 * 128 / 16);
+  const int blocks = (int)((pieces + 255) / 256 < 1024 ? (pieces + 255) / 256 : 1024);
+  stash_kernel<128><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(q), q_stride_token, q_stride_head, qrow, rows, q_tokens, group * group_rows,
+      heads * group_rows, static_cast<uint8_t*>(stash), status);
+  return check_launch("stash_kernel");
+}
+
+extern "C" size_t ekv_audit_workspace_bytes(int layers, int rows, int width) {
+  if (layers <= 0 || rows <= 0 || width <= 0) return 0;
+  return workspace_layout(layers, rows, width).total;
 }
 
 extern "C" int ekv_audit_launch(
@@ -497,60 +694,57 @@ extern "C" int ekv_audit_launch(
     int64_t q_stride_token, int64_t q_stride_head, int64_t k_stride_block, int64_t k_stride_pos,
     int64_t k_stride_head, int64_t table_stride, int layers, int rows, int width, int group_rows,
     int block_size, int tile_blocks, int head_dim, int dtype, int heads, int kv_heads,
-    int64_t pool_blocks, int64_t q_tokens, float* share_acc, int32_t* contributors,
-    float* share_out, int aggregate, int share_flags, void* workspace, size_t workspace_bytes,
-    uint32_t* status, void* stream) {
+    int64_t pool_blocks, int64_t q_tokens, float* share_out, int32_t* contributors, int aggregate,
+    int share_flags, void* workspace, size_t workspace_bytes, uint32_t* status, void* stream) {
   clear_error();
-  if (!q || !k || !table || !lens || !qrow || !select || !flag || !lse)
-    return fail(EKV_EINVAL, "a required device pointer is NULL");
-  if (rows <= 0 || width <= 0 || layers <= 0)
-    return fail(EKV_EINVAL, "rows, width and layers must be positive");
+  if (!q || !k) return fail(EKV_EINVAL, "a required device pointer is NULL");
+  AuditParams p{};
+  const int rc = prepare(p, table, lens, qrow, select, flag, lse, scale, q_stride_token, q_stride_head,
+                         k_stride_block, k_stride_pos, k_stride_head, table_stride, layers, rows, width,
+                         group_rows, block_size, tile_blocks, head_dim, dtype, heads, kv_heads,
+                         pool_blocks, q_tokens, share_out, contributors, aggregate, workspace,
+                         workspace_bytes, status);
+  if (rc != EKV_OK) return rc;
   if (layer < 0 || layer >= layers)
     return fail(EKV_ERANGE, "layer %d is outside the %d layers the table was sized for", layer, layers);
-  if (group_rows < 1 || group_rows > 16)
-    return fail(EKV_EINVAL, "%d query heads per KV head: the kernel handles 1 to 16", group_rows);
-  if (heads < 1 || group < 0 || group + heads > kv_heads)
+  if (group < 0 || group + heads > kv_heads)
     return fail(EKV_EINVAL, "KV heads [%d, %d) are outside the cache's %d heads", group, group + heads, kv_heads);
-  if (heads * group_rows > kMaxQ)
-    return fail(EKV_ENOTSUP, "%d values per cell exceed %d", heads * group_rows, kMaxQ);
-  if (block_size <= 0 || tile_blocks <= 0)
-    return fail(EKV_EINVAL, "block_size and tile_blocks must be positive");
-  if (tile_blocks > 8) return fail(EKV_ENOTSUP, "tile_blocks %d: this build handles up to 8", tile_blocks);
-  if (rows > 65535 || heads > 64) return fail(EKV_ENOTSUP, "rows <= 65535 and heads <= 64");
-  const int tt = block_size * tile_blocks;
-  if (tt & (tt - 1)) return fail(EKV_EINVAL, "a tile of the audit kernel must hold a power of two of tokens");
-  if (head_dim != 128) return fail(EKV_ENOTSUP, "head_dim %d: this build has kernels for 128", head_dim);
-  if (dtype != EKV_DTYPE_F16 && dtype != EKV_DTYPE_BF16) return fail(EKV_EINVAL, "unknown dtype %d", dtype);
-  if (pool_blocks <= 0 || q_tokens <= 0) return fail(EKV_EINVAL, "pool_blocks and q_tokens must be positive");
-  // Bulk copies move whole 256-byte key rows; the query is read as pairs of elements.
-  if (((uintptr_t)k & 15) || (k_stride_block & 7) || (k_stride_pos & 7) || (k_stride_head & 7))
-    return fail(EKV_EINVAL, "the key cache must be 16-byte aligned with strides of whole 16-byte units");
-  if (((uintptr_t)q & 3) || (q_stride_token & 1) || (q_stride_head & 1))
-    return fail(EKV_EINVAL, "the query must be 4-byte aligned with even strides");
-  if (table_stride < width) return fail(EKV_EINVAL, "table_stride %lld < width %d", (long long)table_stride, width);
-  if (aggregate != EKV_AGG_MEAN && aggregate != EKV_AGG_MAX) return fail(EKV_EINVAL, "unknown aggregate %d", aggregate);
-
-  AuditParams p{};
-  p.q = q; p.k = k; p.table = table; p.lens = lens; p.qrow = qrow; p.select = select; p.flag = flag;
-  p.lse = lse; p.scale = scale; p.layer = layer; p.group = group;
-  p.q_s0 = q_stride_token; p.q_s1 = q_stride_head;
-  p.k_s0 = k_stride_block; p.k_s1 = k_stride_pos; p.k_s2 = k_stride_head; p.table_s0 = table_stride;
-  p.layers = layers; p.rows = rows; p.width = width; p.G = group_rows; p.heads = heads;
-  p.Q = heads * group_rows; p.block_size = block_size; p.tile_blocks = tile_blocks;
-  p.pool_blocks = pool_blocks; p.q_tokens = q_tokens;
-  p.share_acc = share_acc; p.contrib = contributors; p.share_out = share_out;
-  p.aggregate = aggregate; p.share_flags = share_flags; p.status = status;
-  p.max_chunks = cdiv(cdiv(width, tile_blocks), EKV_AUDIT_CHUNK_TILES);
-  if (share_acc) {
-    if (!contributors) return fail(EKV_EINVAL, "share_acc needs contributors");
-    if ((share_flags & EKV_SHARE_FINALIZE) && !share_out) return fail(EKV_EINVAL, "EKV_SHARE_FINALIZE needs share_out");
-    const size_t need = ekv_audit_workspace_bytes(rows, width, group_rows, heads, block_size, tile_blocks);
-    if (!workspace || workspace_bytes < need)
-      return fail(EKV_ERANGE, "the audit workspace holds %zu bytes, the launch needs %zu", workspace_bytes, need);
-    if ((uintptr_t)workspace & 255) return fail(EKV_EINVAL, "the audit workspace must be 256-byte aligned");
-    p.tickets = static_cast<uint32_t*>(workspace);
-    p.partials = reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) + audit_ticket_bytes(rows));
-  }
+  if (((uintptr_t)k & 15) || ((uintptr_t)q & 3))
+    return fail(EKV_EINVAL, "the key cache must be 16-byte aligned and the query 4-byte aligned");
+  p.q = q; p.k = k; p.layer0 = layer; p.n_layers = 1; p.group = group; p.rotate = 0;
+  p.finalize = (share_flags & EKV_SHARE_FINALIZE) != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return dtype == EKV_DTYPE_BF16 ? dispatch_audit<__nv_bfloat16>(p, tt, s) : dispatch_audit<__half>(p, tt, s);
+  const int tt = block_size * tile_blocks;
+  return dtype == EKV_DTYPE_BF16 ? dispatch<__nv_bfloat16>(p, tt, s) : dispatch<__half>(p, tt, s);
+}
+
+extern "C" int ekv_audit_step(
+    const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table, const int32_t* lens,
+    const int32_t* qrow, const uint8_t* select, const uint32_t* flag, float* lse, float scale,
+    int layer0, int n_layers, int group, int rotate, int q_layout, int64_t q_stride_token, int64_t q_stride_head,
+    int64_t k_stride_block, int64_t k_stride_pos, int64_t k_stride_head, int64_t table_stride,
+    int layers, int rows, int width, int group_rows, int block_size, int tile_blocks, int head_dim,
+    int dtype, int heads, int kv_heads, int64_t pool_blocks, int64_t q_tokens, float* share_out,
+    int32_t* contributors, int aggregate, void* workspace, size_t workspace_bytes,
+    uint32_t* status, void* stream) {
+  clear_error();
+  if (!q_layers || !k_layers) return fail(EKV_EINVAL, "the per-layer address arrays must not be NULL");
+  AuditParams p{};
+  const int rc = prepare(p, table, lens, qrow, select, flag, lse, scale, q_stride_token, q_stride_head,
+                         k_stride_block, k_stride_pos, k_stride_head, table_stride, layers, rows, width,
+                         group_rows, block_size, tile_blocks, head_dim, dtype, heads, kv_heads,
+                         pool_blocks, q_tokens, share_out, contributors, aggregate, workspace,
+                         workspace_bytes, status);
+  if (rc != EKV_OK) return rc;
+  if (n_layers <= 0 || layer0 < 0 || layer0 + n_layers > layers)
+    return fail(EKV_ERANGE, "layers [%d, %d) are outside the %d the table was sized for", layer0,
+                layer0 + n_layers, layers);
+  if (group < 0 || (rotate ? (heads != 1 || group >= kv_heads) : group + heads > kv_heads))
+    return fail(EKV_EINVAL, "KV head %d (rotate %d, %d heads) does not fit a cache of %d heads", group,
+                rotate, heads, kv_heads);
+  p.q_layers = q_layers; p.k_layers = k_layers; p.layer0 = layer0; p.n_layers = n_layers;
+  p.group = group; p.rotate = rotate != 0; p.finalize = 1; p.q_stash = q_layout != 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int tt = block_size * tile_blocks;
+  return dtype == EKV_DTYPE_BF16 ? dispatch<__nv_bfloat16>(p, tt, s) : dispatch<__half>(p, tt, s);
 }

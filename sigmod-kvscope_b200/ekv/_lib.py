@@ -17,7 +17,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 OK, EINVAL, ERANGE, ENOTSUP, ECUDA = 0, -1, -2, -3, -4
 DTYPE_F16, DTYPE_BF16 = 0, 1
 AGG_MEAN, AGG_MAX = 0, 1
-SHARE_RESET, SHARE_FINALIZE = 1, 2
+SHARE_FINALIZE = 2
 STATUS_BAD_BLOCK_ID, STATUS_LEN_OVER_WIDTH, STATUS_BAD_QROW, STATUS_WAIT_TIMEOUT = 1, 2, 4, 8
 POLICY_SUM, POLICY_UNIFORM, POLICY_NEWEST = 0, 1, 2
 AUDIT_CHUNK_TILES = 8
@@ -34,7 +34,7 @@ _sz = _c.c_size_t
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ekv_last_error_string": (_c.c_char_p, []),
     "ekv_abi_version": (_i32, []),
-    "ekv_audit_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32]),
+    "ekv_audit_workspace_bytes": (_sz, [_i32, _i32, _i32]),
     "ekv_audit_launch": (
         _i32,
         [_p, _p, _p, _p, _p, _p, _p, _p,  # q k table lens qrow select flag lse
@@ -42,7 +42,18 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _i64, _i64, _i64, _i64, _i64, _i64,  # q strides, k strides, table stride
          _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,  # layers rows width G bs tb D dtype
          _i32, _i32, _i64, _i64,  # heads kv_heads pool_blocks q_tokens
-         _p, _p, _p, _i32, _i32,  # share_acc contributors share_out aggregate flags
+         _p, _p, _i32, _i32,  # share_out contributors aggregate flags
+         _p, _sz, _p, _p],  # workspace bytes status stream
+    ),
+    "ekv_audit_stash": (_i32, [_p, _i64, _i64, _p, _i32, _i64, _i32, _i32, _i32, _i32, _p, _p, _p]),
+    "ekv_audit_step": (
+        _i32,
+        [_p, _p, _p, _p, _p, _p, _p, _p,  # q_layers k_layers table lens qrow select flag lse
+         _f32, _i32, _i32, _i32, _i32, _i32,  # scale layer0 n_layers group rotate q_layout
+         _i64, _i64, _i64, _i64, _i64, _i64,  # q strides, k strides, table stride
+         _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,  # layers rows width G bs tb D dtype
+         _i32, _i32, _i64, _i64,  # heads kv_heads pool_blocks q_tokens
+         _p, _p, _i32,  # share_out contributors aggregate
          _p, _sz, _p, _p],  # workspace bytes status stream
     ),
     "ekv_normalize_tile_lse": (

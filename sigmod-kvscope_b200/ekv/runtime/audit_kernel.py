@@ -41,6 +41,11 @@ class RecordingPlane(AuditPlane):
     ``heads`` > 1 records that many KV heads per layer side by side in a cell (all-heads mode,
     ``group_rows`` then counts the query rows of one KV head); 1 is the reference's sampling.
     ``aggregate`` chooses how the fused shares combine layers and query rows ("mean" or "max").
+    ``deferred`` keeps each layer's audited queries (a small copy per layer) and records every layer
+    in one launch after the last layer: the cells and shares are the same, written at the end of the
+    step instead of after each layer. It needs the layer table (``attach``) to hold the caches the
+    layers are recorded from. ``None`` (the default) defers every step that starts with the layer
+    table filled and records the others layer by layer.
     """
 
     def __init__(
@@ -53,6 +58,7 @@ class RecordingPlane(AuditPlane):
         *,
         heads: int = 1,
         aggregate: str = "mean",
+        deferred: bool | None = None,
     ) -> None:
         super().__init__()
         if group_rows > 16:
@@ -68,7 +74,10 @@ class RecordingPlane(AuditPlane):
         self.heads = heads
         self.cell = heads * group_rows  # values per (layer, row, block)
         self.aggregate = aggregate
+        self.deferred = deferred
+        self._step_deferred = False  # the mode of the step in progress, chosen at its layer 0
         self._layer_of: dict[str, int] = {}  # layer name -> number, in the order the layers first run
+        self._addresses: list[int] = []
         self._lib = _lib.load()
         lse_bytes = 2 * layers * rows * width * self.cell * 4
         self._lse = self._allocate(lse_bytes)
@@ -78,19 +87,29 @@ class RecordingPlane(AuditPlane):
         self._cuda.cudaMemset(ctypes.c_void_p(self._flag_dev), 0, ctypes.c_size_t(4))
         self._cuda.cudaMemset(ctypes.c_void_p(self._table_dev), 0, ctypes.c_size_t(layers * 8))
         device = torch.device("cuda", torch.cuda.current_device())
+        self._device = device
         self._select = torch.zeros(rows, dtype=torch.uint8, device=device)
         self._token = torch.zeros(rows, dtype=torch.int32, device=device)
-        # the fused share: accumulator, contributors, final shares, and the kernel's workspace
-        self._share_acc = torch.zeros(rows, width, dtype=torch.float32, device=device)
+        # the fused share: final shares and contributors, and the kernel's workspace
         self._contributors = torch.zeros(rows, dtype=torch.int32, device=device)
         self._share = torch.full((rows, width), float("nan"), dtype=torch.float32, device=device)
-        self._workspace_bytes = int(
-            self._lib.ekv_audit_workspace_bytes(rows, width, group_rows, heads, block_size, TILE_BLOCKS)
-        )
+        self._workspace_bytes = int(self._lib.ekv_audit_workspace_bytes(layers, rows, width))
         self._workspace = torch.zeros(self._workspace_bytes + 256, dtype=torch.uint8, device=device)
         self._status = torch.zeros(1, dtype=torch.int32, device=device)
+        # deferred recording: per-layer query stash, its addresses, and stash row indices
+        self._stash: torch.Tensor | None = None
+        self._stash_addresses: torch.Tensor | None = None
+        self._rows_index = torch.arange(rows, dtype=torch.int32, device=device)
+        self._key_shape: tuple | None = None
         torch.cuda.synchronize()
         self._publish()
+
+    def attach(self, cache_addresses: list[int]) -> bool:
+        """Fill the layer table with each layer's KV-cache base address (also kept on the host)."""
+        filled = super().attach(cache_addresses)
+        if filled and not self._addresses:
+            self._addresses = [int(a) for a in cache_addresses]
+        return filled
 
     # -- device memory of the statistic block (cudaMalloc, so that it can be exported by IPC) -------
 
@@ -186,7 +205,7 @@ class RecordingPlane(AuditPlane):
     ) -> None:
         """Launch the kernel for ``layer``; ``keys`` is the layer's key cache [blocks, block, heads, dim].
 
-        Layer 0 starts the audit step's share accumulation and the plane's last layer finalises it.
+        The plane's last layer finalises the step's shares (and, deferred, records every layer).
         """
         if layer >= self._layers:
             raise RuntimeError(f"more attention layers ran than the {self._layers} the plane was sized for")
@@ -207,19 +226,65 @@ class RecordingPlane(AuditPlane):
             if self.heads != kv_heads:
                 raise ValueError(f"an all-heads plane of {self.heads} heads got a cache of {kv_heads}")
             group = 0
-        flags = (_lib.SHARE_RESET if layer == 0 else 0) | (_lib.SHARE_FINALIZE if layer == self._layers - 1 else 0)
+        stream = _lib.current_stream() if stream is None else stream
+        dtype = _DTYPES[query.dtype]
         workspace = (self._workspace.data_ptr() + 255) // 256 * 256
+        if layer == 0:
+            self._step_deferred = bool(self._addresses) if self.deferred is None else self.deferred
+        if self._step_deferred:
+            self._record_deferred(layer, group, table, lens, query, keys, scale, dtype, workspace, stream)
+            return
+        flags = _lib.SHARE_FINALIZE if layer == self._layers - 1 else 0
         rc = self._lib.ekv_audit_launch(
             query.data_ptr(), keys.data_ptr(), table.data_ptr(), lens.data_ptr(), self._token.data_ptr(),
             self._select.data_ptr(), self._flag_dev, self._lse, float(scale), layer, group,
             query.stride(0), query.stride(1), keys.stride(0), keys.stride(1), keys.stride(2), table.stride(0),
             self._layers, self.rows, self.width, self.group_rows, self.block_size, TILE_BLOCKS, dim,
-            _DTYPES[query.dtype], self.heads, kv_heads, keys.shape[0], query.shape[0],
-            self._share_acc.data_ptr(), self._contributors.data_ptr(), self._share.data_ptr(),
-            _AGGREGATES[self.aggregate], flags, workspace, self._workspace_bytes, self._status.data_ptr(),
-            _lib.current_stream() if stream is None else stream,
+            dtype, self.heads, kv_heads, keys.shape[0], query.shape[0],
+            self._share.data_ptr(), self._contributors.data_ptr(), _AGGREGATES[self.aggregate], flags,
+            workspace, self._workspace_bytes, self._status.data_ptr(), stream,
         )
         _lib.check(rc, "ekv_audit_launch")
+
+    def _record_deferred(self, layer, group, table, lens, query, keys, scale, dtype, workspace, stream) -> None:
+        """Keep the layer's audited queries; after the last layer record every layer in one launch."""
+        if len(self._addresses) <= layer:
+            raise RuntimeError("deferred recording needs the layer table filled with every layer's cache")
+        if keys.data_ptr() != self._addresses[layer]:
+            raise ValueError(f"layer {layer}'s key cache is not the one in the layer table")
+        shape = (tuple(keys.shape), tuple(keys.stride()), query.dtype)
+        if self._key_shape is None:
+            self._key_shape = shape
+        elif shape != self._key_shape:
+            raise ValueError("every layer's key cache must have the same shape and strides")
+        if self._stash is None:
+            self._stash = torch.empty(self._layers, self.rows, self.cell, query.shape[2], dtype=query.dtype,
+                                      device=self._device)
+            step = self._stash[0].numel() * self._stash.element_size()
+            addresses = [self._stash.data_ptr() + i * step for i in range(self._layers)]
+            self._stash_addresses = torch.tensor(addresses, dtype=torch.uint64, device=self._device)
+        if self._stash.dtype != query.dtype:
+            raise ValueError("every layer's query must have the same dtype")
+        rc = self._lib.ekv_audit_stash(
+            query.data_ptr(), query.stride(0), query.stride(1), self._token.data_ptr(), self.rows, query.shape[0],
+            group, self.heads, self.group_rows, query.shape[2], self._stash[layer].data_ptr(), self._status.data_ptr(),
+            stream,
+        )
+        _lib.check(rc, "ekv_audit_stash")
+        if layer != self._layers - 1:
+            return
+        stash = self._stash[0]
+        rc = self._lib.ekv_audit_step(
+            self._stash_addresses.data_ptr(), self._table_dev, table.data_ptr(), lens.data_ptr(),
+            self._rows_index.data_ptr(), self._select.data_ptr(), self._flag_dev, self._lse, float(scale),
+            0, self._layers, 0 if self.heads > 1 else 0, 1 if self.heads == 1 else 0, 1,
+            stash.stride(0), stash.stride(1), keys.stride(0), keys.stride(1), keys.stride(2), table.stride(0),
+            self._layers, self.rows, self.width, self.group_rows, self.block_size, TILE_BLOCKS, keys.shape[3],
+            dtype, self.heads, keys.shape[2], keys.shape[0], self.rows,
+            self._share.data_ptr(), self._contributors.data_ptr(), _AGGREGATES[self.aggregate],
+            workspace, self._workspace_bytes, self._status.data_ptr(), stream,
+        )
+        _lib.check(rc, "ekv_audit_step")
 
     # -- what the fused launch leaves behind --------------------------------------------------------
 

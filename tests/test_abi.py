@@ -41,18 +41,22 @@ def test_constants_agree_with_the_header():
     text = open(HEADER).read()
     defines = dict(re.findall(r"#define\s+(EKV_[A-Z0-9_]+)\s+\(?(-?\d+)u?\)?", text))
     assert int(defines["EKV_EINVAL"]) == L.EINVAL and int(defines["EKV_ENOTSUP"]) == L.ENOTSUP
-    assert int(defines["EKV_SHARE_RESET"]) == L.SHARE_RESET and int(defines["EKV_SHARE_FINALIZE"]) == L.SHARE_FINALIZE
+    assert int(defines["EKV_SHARE_FINALIZE"]) == L.SHARE_FINALIZE
     assert int(defines["EKV_POLICY_SUM"]) == L.POLICY_SUM and int(defines["EKV_POLICY_NEWEST"]) == L.POLICY_NEWEST
     assert int(defines["EKV_AUDIT_CHUNK_TILES"]) == L.AUDIT_CHUNK_TILES
     assert int(defines["EKV_DTYPE_BF16"]) == L.DTYPE_BF16
 
 
 def test_workspace_size(lib):
-    # tickets (rows * 4 rounded to 256) + rows * chunks * heads * G * 8 bytes
-    rows, width, g, heads = 64, 512, 4, 1
-    chunks = -(-(-(-width // 2)) // L.AUDIT_CHUNK_TILES)
-    assert lib.ekv_audit_workspace_bytes(rows, width, g, heads, 16, 2) == 256 + rows * chunks * heads * g * 8
-    assert lib.ekv_audit_workspace_bytes(0, width, g, heads, 16, 2) == 0
+    # tickets [layers][rows] + row tickets [rows] + contributors [layers][rows] + shares [layers][rows][width]
+    layers, rows, width = 32, 64, 512
+
+    def up(x):
+        return -(-x // 256) * 256
+
+    want = up(layers * rows * 4) + up(rows * 4) + up(layers * rows * 4) + up(layers * rows * width * 4)
+    assert lib.ekv_audit_workspace_bytes(layers, rows, width) == want
+    assert lib.ekv_audit_workspace_bytes(0, rows, width) == 0
 
 
 def audit_args(**over):
@@ -61,7 +65,7 @@ def audit_args(**over):
         q=fake, k=ctypes.c_void_p(0x2000), table=fake, lens=fake, qrow=fake, select=fake, flag=fake, lse=fake,
         scale=0.1, layer=0, group=0, qs0=1024, qs1=128, ks0=4096, ks1=256, ks2=128, ts=8,
         layers=1, rows=4, width=8, G=4, bs=16, tb=2, D=128, dtype=L.DTYPE_BF16, heads=1, kv_heads=2,
-        pool=256, q_tokens=8, acc=None, contrib=None, out=None, agg=L.AGG_MEAN, flags=0, ws=None, ws_bytes=0,
+        pool=256, q_tokens=8, out=None, contrib=None, agg=L.AGG_MEAN, flags=0, ws=None, ws_bytes=0,
         status=None, stream=None,
     )
     args.update(over)
@@ -81,8 +85,9 @@ def audit_args(**over):
         (dict(ks1=100), L.EINVAL),  # key rows not in whole 16-byte units
         (dict(ts=4), L.EINVAL),
         (dict(agg=5), L.EINVAL),
-        (dict(acc=ctypes.c_void_p(0x3000)), L.EINVAL),  # no contributors
-        (dict(acc=ctypes.c_void_p(0x3000), contrib=ctypes.c_void_p(0x4000), ws=None), L.ERANGE),
+        (dict(out=ctypes.c_void_p(0x3000)), L.EINVAL),  # no contributors
+        (dict(out=ctypes.c_void_p(0x3000), contrib=ctypes.c_void_p(0x4000), ws=None), L.ERANGE),
+        (dict(rows=4096), L.ENOTSUP),
     ],
 )
 def test_audit_launch_rejects_bad_arguments(lib, over, code):
@@ -118,5 +123,20 @@ def test_other_entry_points_validate_before_launching(lib):
     assert lib.ekv_compact_block_table(fake, 8, fake, None, 8, 2, 8, 16, fake, 8, fake, None) == L.EINVAL
 
 
+def test_step_and_stash_validate_before_launching(lib):
+    fake = ctypes.c_void_p(0x1000)
+    step = [fake, fake, fake, fake, fake, fake, fake, fake, 0.1, 0, 4, 0, 1, 0, 1024, 128, 4096, 256, 128, 8,
+            4, 4, 8, 4, 16, 2, 128, L.DTYPE_BF16, 1, 2, 256, 8, fake, fake, L.AGG_MEAN, None, 0, None, None]
+    assert lib.ekv_audit_step(*step) == L.ERANGE  # share_out without a workspace
+    step[35], step[36] = fake, 1 << 30
+    step[10] = 5
+    assert lib.ekv_audit_step(*step) == L.ERANGE  # layers [0, 5) of a table of 4
+    step[0] = None
+    assert lib.ekv_audit_step(*step) == L.EINVAL
+    assert lib.ekv_audit_stash(None, 8, 128, fake, 4, 8, 0, 1, 4, 128, fake, None, None) == L.EINVAL
+    assert lib.ekv_audit_stash(fake, 8, 128, fake, 4, 8, 0, 1, 4, 64, fake, None, None) == L.ENOTSUP
+    assert lib.ekv_audit_stash(ctypes.c_void_p(0x1008), 8, 128, fake, 4, 8, 0, 1, 4, 128, fake, None, None) == L.EINVAL
+
+
 def test_abi_version(lib):
-    assert lib.ekv_abi_version() == 1
+    assert lib.ekv_abi_version() == 2

@@ -36,23 +36,30 @@ def runtime_dir(tmp_path, monkeypatch):
     return tmp_path
 
 
-def run_plane_on_golden(g: dict, aggregate: str = "mean"):
+def run_plane_on_golden(g: dict, aggregate: str = "mean", deferred: bool = False):
+    """The golden case through RecordingPlane: per layer (eager) or all layers after the last (deferred)."""
     from ekv.runtime.audit_kernel import RecordingPlane
 
     dtype = str(g["dtype"])
     q_all, k_all = unpack(g["query"], dtype), unpack(g["keys"], dtype)
     layers = q_all.shape[0]
     rows, width = g["table"].shape
-    plane = RecordingPlane(layers, rows, width, int(g["group_rows"]), int(g["block_size"]), aggregate=aggregate)
-    plane.attach([0x1000 + i for i in range(layers)])
+    caches = []
+    for layer in range(layers):
+        k = k_all[layer].cuda()
+        caches.append(torch.stack([k, torch.zeros_like(k)], dim=1))
+    plane = RecordingPlane(layers, rows, width, int(g["group_rows"]), int(g["block_size"]), aggregate=aggregate,
+                           deferred=deferred)
+    plane.attach([c.data_ptr() for c in caches])
     plane.select(g["select"].astype(bool), g["qrow"])
     table = torch.from_numpy(g["table"]).cuda()
     lens = torch.from_numpy(g["lens"]).cuda()
     for layer in range(layers):
-        plane.set(bool(g["flags"][layer]))
-        k = k_all[layer].cuda()
-        kv_cache = torch.stack([k, torch.zeros_like(k)], dim=1)
-        plane.record(f"layer.{layer}", table, lens, q_all[layer].cuda(), kv_cache, float(g["scale"]))
+        if not deferred:
+            plane.set(bool(g["flags"][layer]))
+        elif layer == 0:
+            plane.set(True)
+        plane.record(f"layer.{layer}", table, lens, q_all[layer].cuda(), caches[layer], float(g["scale"]))
     torch.cuda.synchronize()
     return plane
 
@@ -83,6 +90,30 @@ def test_fused_shares_match_the_reference_normalisation(name, aggregate, runtime
     np.testing.assert_allclose(share[live].sum(axis=1), 1.0, rtol=1e-5)
 
 
+@pytest.mark.parametrize("name", ["audit_cfg1_fp16", "audit_g8_bf16"])
+@pytest.mark.parametrize("aggregate", ["mean", "max"])
+def test_deferred_recording_matches_the_reference(name, aggregate, runtime_dir):
+    """All layers in one launch after the last layer: the same cells and shares as the reference."""
+    g = load_golden(name)
+    plane = run_plane_on_golden(g, aggregate, deferred=True)
+    lse = plane.table().cpu().numpy()
+    ref = g["lse"]
+    assert np.array_equal(np.isnan(lse), np.isnan(ref))
+    w = ~np.isnan(ref)
+    np.testing.assert_allclose(lse[w], ref[w], **LSE_TOL)
+    share = plane.shares().cpu().numpy().astype(np.float64)
+    np.testing.assert_allclose(share, g[f"share_{aggregate}"], equal_nan=True, **SHARE_TOL)
+    assert plane.status() == 0
+
+
+def test_deferred_and_per_layer_recording_agree_bit_for_bit(runtime_dir):
+    g = load_golden("audit_g8_bf16")
+    eager = run_plane_on_golden(g, deferred=False)
+    deferred = run_plane_on_golden(g, deferred=True)
+    assert torch.equal(torch.nan_to_num(eager.table(), 3.0), torch.nan_to_num(deferred.table(), 3.0))
+    assert torch.equal(torch.nan_to_num(eager.shares(), 3.0), torch.nan_to_num(deferred.shares(), 3.0))
+
+
 def test_the_descriptor_is_published_in_the_reference_format(runtime_dir):
     from ekv.observe.tile_shares import share_descriptor
     from ekv.runtime.audit_kernel import RecordingPlane
@@ -102,7 +133,7 @@ def test_plane_validation_raises_the_reference_exceptions(runtime_dir):
         RecordingPlane(1, 2, 4, 17, 16)
     with pytest.raises(ValueError):
         RecordingPlane(1, 2, 4, 4, 12)
-    plane = RecordingPlane(1, 2, 4, 4, 16)
+    plane = RecordingPlane(1, 2, 4, 4, 16, deferred=False)
     with pytest.raises(RuntimeError):
         plane.set(True)  # before the layer table is filled
     plane.attach([0x1000])
@@ -133,40 +164,49 @@ def random_case(seed, rows, width, q_heads, kv_heads, lens, dtype=torch.bfloat16
     return q, k, table, torch.tensor(lens, dtype=torch.int32), qrow
 
 
+class Run:
+    """The device buffers of one audit step through the C ABI: table, workspace, shares, status."""
+
+    def __init__(self, layers, rows, width, cell):
+        import ekv._lib as L
+
+        dev = torch.device("cuda")
+        self.lse = torch.full((2, layers, rows, width, cell), float("nan"), device=dev)
+        self.ws_bytes = L.load().ekv_audit_workspace_bytes(layers, rows, width)
+        self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=dev)
+        self.share = torch.full((rows, width), float("nan"), device=dev)
+        self.contrib = torch.zeros(rows, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+
 def launch(q, k, table, lens, qrow, select, flag_on, layers, layer, group_rows, heads=1, group=None,
-           tile_blocks=2, aggregate="mean", flags=None, lse=None, acc=None, status=None):
+           tile_blocks=2, aggregate="mean", finalize=None, run=None):
+    """One ekv_audit_launch; returns (lse, (share, contributors), status) and keeps `run` for the step."""
     import ekv._lib as L
 
     lib = L.load()
     rows, width = table.shape
     block_size, kv_heads = k.shape[1], k.shape[2]
-    cell = heads * group_rows
     dev = torch.device("cuda")
-    if lse is None:
-        lse = torch.full((2, layers, rows, width, cell), float("nan"), device=dev)
-    if acc is None:
-        acc = (torch.zeros(rows, width, device=dev), torch.zeros(rows, dtype=torch.int32, device=dev),
-               torch.full((rows, width), float("nan"), device=dev))
-    ws_bytes = lib.ekv_audit_workspace_bytes(rows, width, group_rows, heads, block_size, tile_blocks)
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
-    status = torch.zeros(1, dtype=torch.int32, device=dev) if status is None else status
+    run = run or Run(layers, rows, width, heads * group_rows)
     flag = torch.tensor([1 if flag_on else 0], dtype=torch.int32, device=dev)
     sel = torch.as_tensor(np.asarray(select, dtype=np.uint8)).to(dev)
     qd, kd, td, ld, rd = (x.to(dev) for x in (q, k, table, lens, qrow))
-    if flags is None:
-        flags = (L.SHARE_RESET if layer == 0 else 0) | (L.SHARE_FINALIZE if layer == layers - 1 else 0)
+    if finalize is None:
+        finalize = layer == layers - 1
     rc = lib.ekv_audit_launch(
         qd.data_ptr(), kd.data_ptr(), td.data_ptr(), ld.data_ptr(), rd.data_ptr(), sel.data_ptr(), flag.data_ptr(),
-        lse.data_ptr(), 1 / math.sqrt(128), layer, layer % kv_heads if group is None else group,
+        run.lse.data_ptr(), 1 / math.sqrt(128), layer, layer % kv_heads if group is None else group,
         qd.stride(0), qd.stride(1), kd.stride(0), kd.stride(1), kd.stride(2), td.stride(0),
         layers, rows, width, group_rows, block_size, tile_blocks, 128,
         L.DTYPE_BF16 if q.dtype == torch.bfloat16 else L.DTYPE_F16, heads, kv_heads, kd.shape[0], qd.shape[0],
-        acc[0].data_ptr(), acc[1].data_ptr(), acc[2].data_ptr(), L.AGG_MEAN if aggregate == "mean" else L.AGG_MAX,
-        flags, ws.data_ptr(), ws_bytes, status.data_ptr(), L.current_stream(),
+        run.share.data_ptr(), run.contrib.data_ptr(), L.AGG_MEAN if aggregate == "mean" else L.AGG_MAX,
+        L.SHARE_FINALIZE if finalize else 0, run.ws.data_ptr(), run.ws_bytes, run.status.data_ptr(),
+        L.current_stream(),
     )
     L.check(rc, "ekv_audit_launch")
     torch.cuda.synchronize()
-    return lse, acc, status
+    return run
 
 
 def oracle_case(table, lens, qrow, select, layers_q, layers_k, group_rows, block_size, tile_blocks, heads=1,
@@ -208,19 +248,19 @@ def test_random_rows_match_the_oracle(q_heads, kv_heads, tile_blocks, dtype):
     group_rows = q_heads // kv_heads
     gen_layers = [random_case(11 + layer, rows, width, q_heads, kv_heads, lens, dtype) for layer in range(layers)]
     _, _, table, lens_t, qrow = gen_layers[0]
-    lse = acc = None
+    run = None
     for layer in range(layers):
         q, k = gen_layers[layer][0], gen_layers[layer][1]
-        lse, acc, status = launch(q, k, table, lens_t, qrow, select, True, layers, layer, group_rows,
-                                  tile_blocks=tile_blocks, lse=lse, acc=acc)
-        assert int(status.item()) == 0
+        run = launch(q, k, table, lens_t, qrow, select, True, layers, layer, group_rows, tile_blocks=tile_blocks,
+                     run=run)
+        assert int(run.status.item()) == 0
     ref = oracle_case(table, lens_t, qrow, select, [g[0] for g in gen_layers], [g[1] for g in gen_layers],
                       group_rows, block_size, tile_blocks)
-    got = lse.cpu().numpy()
+    got = run.lse.cpu().numpy()
     assert np.array_equal(np.isnan(got), np.isnan(ref))
     w = ~np.isnan(ref)
     np.testing.assert_allclose(got[w], ref[w], **LSE_TOL)
-    compare_shares(ref, lens, select, block_size, tile_blocks, acc[2].cpu().numpy())
+    compare_shares(ref, lens, select, block_size, tile_blocks, run.share.cpu().numpy())
 
 
 def test_all_heads_mode_matches_the_oracle():
@@ -229,25 +269,24 @@ def test_all_heads_mode_matches_the_oracle():
     select = [1, 1, 1, 1]
     gen_layers = [random_case(40 + layer, rows, width, q_heads, kv_heads, lens) for layer in range(layers)]
     _, _, table, lens_t, qrow = gen_layers[0]
-    lse = acc = None
+    run = None
     for layer in range(layers):
-        lse, acc, _ = launch(gen_layers[layer][0], gen_layers[layer][1], table, lens_t, qrow, select, True, layers,
-                             layer, q_heads // kv_heads, heads=kv_heads, group=0, lse=lse, acc=acc)
+        run = launch(gen_layers[layer][0], gen_layers[layer][1], table, lens_t, qrow, select, True, layers, layer,
+                     q_heads // kv_heads, heads=kv_heads, group=0, run=run)
     ref = oracle_case(table, lens_t, qrow, select, [g[0] for g in gen_layers], [g[1] for g in gen_layers],
                       q_heads // kv_heads, 16, 2, heads=kv_heads, groups=[0] * layers)
-    got = lse.cpu().numpy()
+    got = run.lse.cpu().numpy()
     w = ~np.isnan(ref)
     assert np.array_equal(np.isnan(got), np.isnan(ref))
     np.testing.assert_allclose(got[w], ref[w], **LSE_TOL)
-    compare_shares(ref, lens, select, 16, 2, acc[2].cpu().numpy())
+    compare_shares(ref, lens, select, 16, 2, run.share.cpu().numpy())
 
 
 def test_the_flag_off_writes_nothing():
     q, k, table, lens, qrow = random_case(3, 4, 16, 32, 8, [100, 200, 50, 256])
-    lse, acc, _ = launch(q, k, table, lens, qrow, [1, 1, 1, 1], False, 1, 0, 4)
-    assert torch.isnan(lse).all()
-    assert torch.isnan(acc[2]).all()  # the share output is untouched too
-    assert (acc[0] == 0).all()
+    run = launch(q, k, table, lens, qrow, [1, 1, 1, 1], False, 1, 0, 4)
+    assert torch.isnan(run.lse).all()
+    assert torch.isnan(run.share).all()  # the share output is untouched too
 
 
 def test_out_of_range_block_ids_are_skipped_and_reported():
@@ -257,17 +296,17 @@ def test_out_of_range_block_ids_are_skipped_and_reported():
     table = table % 64
     table[1, 2] = 64  # one past the pool
     table[2, 0] = -5
-    _, _, status = launch(q, k, table, lens, qrow, [1, 1, 1], True, 1, 0, 4)
-    assert int(status.item()) & L.STATUS_BAD_BLOCK_ID
+    run = launch(q, k, table, lens, qrow, [1, 1, 1], True, 1, 0, 4)
+    assert int(run.status.item()) & L.STATUS_BAD_BLOCK_ID
 
 
 def test_a_length_past_the_table_is_clamped_and_reported():
     import ekv._lib as L
 
     q, k, table, lens, qrow = random_case(6, 2, 8, 32, 8, [128, 129])
-    lse, _, status = launch(q, k, table, lens, qrow, [1, 1], True, 1, 0, 4)
-    assert int(status.item()) & L.STATUS_LEN_OVER_WIDTH
-    assert not torch.isnan(lse[0, 0, 1]).any()
+    run = launch(q, k, table, lens, qrow, [1, 1], True, 1, 0, 4)
+    assert int(run.status.item()) & L.STATUS_LEN_OVER_WIDTH
+    assert not torch.isnan(run.lse[0, 0, 1]).any()
 
 
 def test_a_bad_query_row_is_skipped_and_reported():
@@ -275,18 +314,18 @@ def test_a_bad_query_row_is_skipped_and_reported():
 
     q, k, table, lens, qrow = random_case(7, 2, 8, 32, 8, [100, 100])
     qrow[1] = q.shape[0] + 3
-    lse, acc, status = launch(q, k, table, lens, qrow, [1, 1], True, 1, 0, 4)
-    assert int(status.item()) & L.STATUS_BAD_QROW
-    assert torch.isnan(lse[:, :, 1]).all() and torch.isnan(acc[2][1]).all()
-    assert not torch.isnan(lse[0, 0, 0, :7]).any()
+    run = launch(q, k, table, lens, qrow, [1, 1], True, 1, 0, 4)
+    assert int(run.status.item()) & L.STATUS_BAD_QROW
+    assert torch.isnan(run.lse[:, :, 1]).all() and torch.isnan(run.share[1]).all()
+    assert not torch.isnan(run.lse[0, 0, 0, :7]).any()
 
 
 def test_repeated_launches_are_deterministic():
     q, k, table, lens, qrow = random_case(8, 16, 64, 32, 8, list(np.random.default_rng(0).integers(1, 1024, 16)))
     a = launch(q, k, table, lens, qrow, [1] * 16, True, 1, 0, 4)
     b = launch(q, k, table, lens, qrow, [1] * 16, True, 1, 0, 4)
-    assert torch.equal(torch.nan_to_num(a[0], 7.0), torch.nan_to_num(b[0], 7.0))
-    assert torch.equal(torch.nan_to_num(a[1][2], 7.0), torch.nan_to_num(b[1][2], 7.0))
+    assert torch.equal(torch.nan_to_num(a.lse, 7.0), torch.nan_to_num(b.lse, 7.0))
+    assert torch.equal(torch.nan_to_num(a.share, 7.0), torch.nan_to_num(b.share, 7.0))
 
 
 def test_full_size_llama8b_rows_sum_to_one():
@@ -304,9 +343,9 @@ def test_full_size_llama8b_rows_sum_to_one():
     table = torch.from_numpy(rng.permutation(pool)[: rows * width].reshape(rows, width).astype(np.int32))
     qrow = torch.from_numpy(rng.permutation(rows + 5)[:rows].astype(np.int32))
     lens_t = torch.from_numpy(lens.astype(np.int32))
-    lse, acc, status = launch(q, k, table, lens_t, qrow, select, True, 1, 0, 4)
-    assert int(status.item()) == 0
-    share = acc[2].cpu().numpy().astype(np.float64)
+    run = launch(q, k, table, lens_t, qrow, select, True, 1, 0, 4)
+    assert int(run.status.item()) == 0
+    share = run.share.cpu().numpy().astype(np.float64)
     assert np.isnan(share[5]).all()
     live = np.flatnonzero(select)
     assert np.isfinite(share[live]).all() and (share[live] >= 0).all()
@@ -321,9 +360,59 @@ def test_full_size_llama8b_rows_sum_to_one():
     ref = oaud.new_table(1, len(pick), width, 4)
     oaud.tile_lse(q.float().cpu().numpy(), k_small, small_table, lens[pick], qrow.numpy()[pick],
                   np.ones(len(pick), dtype=np.uint8), 1, ref, 1 / math.sqrt(128), 0, 0, 16, 2)
-    got = lse.cpu().numpy()[:, :, pick]
+    got = run.lse.cpu().numpy()[:, :, pick]
     w = ~np.isnan(ref)
     assert np.array_equal(np.isnan(got), np.isnan(ref))
     np.testing.assert_allclose(got[w], ref[w], **LSE_TOL)
     u = osh.log_weights(ref, 1, np.arange(len(pick)), 2)
     np.testing.assert_allclose(share[pick], osh.normalize(u, -(-lens[pick] // 16), 2), **SHARE_TOL)
+
+
+def test_one_step_launch_equals_per_layer_launches():
+    """ekv_audit_step over every layer gives bit-identical cells and shares to per-layer launches."""
+    import ekv._lib as L
+
+    rows, width, q_heads, kv_heads, layers = 7, 48, 32, 8, 5
+    lens = [700, 16, 0, 500, 768, 33, 1]
+    select = [1, 1, 1, 0, 1, 1, 1]
+    gen_layers = [random_case(60 + layer, rows, width, q_heads, kv_heads, lens) for layer in range(layers)]
+    _, _, table, lens_t, qrow = gen_layers[0]
+    run = None
+    for layer in range(layers):
+        run = launch(gen_layers[layer][0], gen_layers[layer][1], table, lens_t, qrow, select, True, layers, layer, 4,
+                     run=run)
+    dev = torch.device("cuda")
+    qs = [g[0].to(dev) for g in gen_layers]
+    ks = [g[1].to(dev) for g in gen_layers]
+    q_addr = torch.tensor([q.data_ptr() for q in qs], dtype=torch.uint64, device=dev)
+    k_addr = torch.tensor([k.data_ptr() for k in ks], dtype=torch.uint64, device=dev)
+    step = Run(layers, rows, width, 4)
+    flag = torch.ones(1, dtype=torch.int32, device=dev)
+    sel = torch.tensor(select, dtype=torch.uint8, device=dev)
+    td, ld, rd = table.to(dev), lens_t.to(dev), qrow.to(dev)
+    rc = L.load().ekv_audit_step(
+        q_addr.data_ptr(), k_addr.data_ptr(), td.data_ptr(), ld.data_ptr(), rd.data_ptr(), sel.data_ptr(),
+        flag.data_ptr(), step.lse.data_ptr(), 1 / math.sqrt(128), 0, layers, 0, 1, 0, qs[0].stride(0), qs[0].stride(1),
+        ks[0].stride(0), ks[0].stride(1), ks[0].stride(2), td.stride(0), layers, rows, width, 4, 16, 2, 128,
+        L.DTYPE_BF16, 1, kv_heads, ks[0].shape[0], qs[0].shape[0], step.share.data_ptr(), step.contrib.data_ptr(),
+        L.AGG_MEAN, step.ws.data_ptr(), step.ws_bytes, step.status.data_ptr(), L.current_stream(),
+    )
+    L.check(rc, "ekv_audit_step")
+    torch.cuda.synchronize()
+    assert int(step.status.item()) == 0
+    assert torch.equal(torch.nan_to_num(run.lse, 3.0), torch.nan_to_num(step.lse, 3.0))
+    assert torch.equal(torch.nan_to_num(run.share, 3.0), torch.nan_to_num(step.share, 3.0))
+    assert torch.equal(run.contrib, step.contrib)
+    assert torch.isnan(step.share[2]).all() and torch.isnan(step.share[3]).all()
+    assert step.contrib.tolist() == [20, 20, 0, 0, 20, 20, 20]
+    # the tickets are left zero for the next step: a second step gives the same result
+    rc = L.load().ekv_audit_step(
+        q_addr.data_ptr(), k_addr.data_ptr(), td.data_ptr(), ld.data_ptr(), rd.data_ptr(), sel.data_ptr(),
+        flag.data_ptr(), step.lse.data_ptr(), 1 / math.sqrt(128), 0, layers, 0, 1, 0, qs[0].stride(0), qs[0].stride(1),
+        ks[0].stride(0), ks[0].stride(1), ks[0].stride(2), td.stride(0), layers, rows, width, 4, 16, 2, 128,
+        L.DTYPE_BF16, 1, kv_heads, ks[0].shape[0], qs[0].shape[0], step.share.data_ptr(), step.contrib.data_ptr(),
+        L.AGG_MEAN, step.ws.data_ptr(), step.ws_bytes, step.status.data_ptr(), L.current_stream(),
+    )
+    L.check(rc, "ekv_audit_step")
+    torch.cuda.synchronize()
+    assert torch.equal(torch.nan_to_num(run.share, 3.0), torch.nan_to_num(step.share, 3.0))

@@ -58,10 +58,10 @@ const char* ekv_last_error_string(void);
 /* ABI version of this library: bumped on any signature change. */
 int ekv_abi_version(void);
 
-/* Bytes of workspace the fused share of ekv_audit_launch / ekv_audit_step needs for a table of
- * `layers` layers: tickets per (layer, row) and per row, contributors per (layer, row), and a share
- * vector per (layer, row). It must be zero before the first launch (every launch leaves the
- * tickets zero again) and 256-byte aligned. */
+/* Bytes of workspace the share pass of ekv_audit_launch / ekv_audit_step needs for a table of
+ * `layers` layers: a ticket per row, contributors per (layer, row) and a share vector per
+ * (layer, row). It must be zero before the first launch (every launch leaves the tickets zero
+ * again) and 256-byte aligned. */
 size_t ekv_audit_workspace_bytes(int layers, int rows, int width);
 
 /*
@@ -80,12 +80,12 @@ size_t ekv_audit_workspace_bytes(int layers, int rows, int width);
  * l = sum_j exp(q.k_j*scale - m) over the tile's tokens below lens[row]. heads = 1 is the
  * reference's sampling (one KV group per layer, group = layer % kv_heads, :250).
  *
- * With share_out != NULL it also folds the layer into the exact per-block attention share in the
- * same launch: the (layer, row)'s tile values become block shares as normalize_tile_lse computes
- * them (observe/tile_shares.py:58-103 with row_blocks = ceil(lens/block_size)), kept per layer in
- * the workspace. With EKV_SHARE_FINALIZE (the step's last layer) the layers [0, layers) are
- * combined -- mean or max over layers and query rows -- into share_out [rows][width] and
- * contributors [rows] (query rows with data); a row that is not selected or has no data is NaN.
+ * With share_out != NULL and EKV_SHARE_FINALIZE (the step's last layer) the same call then turns
+ * the cells of every layer [0, layers) into the exact per-block attention share, in a second kernel
+ * over (layer, row) pairs that reads the cells back from L2: block shares as normalize_tile_lse
+ * computes them (observe/tile_shares.py:58-103 with row_blocks = ceil(lens/block_size)), then the
+ * mean or max over layers and query rows into share_out [rows][width] and contributors [rows]
+ * (query rows with data); a row that is not selected or has no data is NaN.
  * status (optional) receives EKV_STATUS_* bits. q_tokens bounds qrow. Supported: head_dim 128,
  * block_size*tile_blocks in {16, 32, 64}, tile_blocks <= 8, heads*group_rows <= 128,
  * group_rows <= 16, rows <= 2048.

@@ -1,26 +1,26 @@
-// The audit kernel: per-tile log-sum-exp of q.K over a paged key cache, with the exact per-block
-// attention share folded in, for one layer or for every layer of an audit step in one launch.
+// The audit step on the device: a streaming kernel that records every (layer, row, tile) cell, and a
+// share kernel that turns the cells into the exact per-block attention share.
 //
-// Work. An item is one (layer, KV head, row, chunk of EKV_AUDIT_CHUNK_TILES tiles); the items of a
-// launch are numbered layer-major and every warp of a persistent grid (SMs x resident CTAs) works
-// through items worker, worker + workers, ... on its own. A warp owns a ring of STAGES shared-memory
-// stages, one tile of TT tokens each, and keeps STAGES tiles in flight across item boundaries: for
-// the next tile each lane asks the TMA engine for one 2*D-byte key row (cp.async.bulk, L2
-// evict-first) and lane 0 arms the stage's mbarrier with the byte count. Rows land 2*D+16 bytes
-// apart, so ldmatrix reads them without bank conflicts.
+// Streaming. An item is one (layer, KV head, row, chunk of EKV_AUDIT_CHUNK_TILES tiles); the items of
+// a launch are numbered layer-major and every warp of a persistent grid (SMs x resident CTAs) works
+// through items worker, worker + workers, ... on its own, with a ring of STAGES shared-memory stages
+// of one tile each kept in flight across item boundaries. For each tile every lane asks the TMA
+// engine for one 2*D-byte key row (cp.async.bulk, L2 evict-first) and lane 0 arms the stage's
+// mbarrier with the byte count; rows land 2*D+16 bytes apart, so ldmatrix reads them without bank
+// conflicts. Nothing on a tile's critical path reads global memory: the rows' lengths and query
+// tokens sit in shared memory, the block ids of the next item and the query fragments of the next
+// item are prefetched into registers one item ahead.
 //
 // Scores. One m16n8k16 mma per (16 tokens, 16 dims): A = 16 key rows by ldmatrix, B = the G query
 // rows of the KV head (registers, padded to 8 or 16 columns), fp32 accumulation. Tokens sit on the
 // C fragment's rows and query rows on its columns, so the tile max and sum are three xor-shuffles
 // per column: tile_lse_kernel's computation (runtime/audit_kernel.py:70-96), stored as at :97-109.
 //
-// Shares. When a warp finishes an item it takes a ticket on the (layer, row); the warp that takes
-// the last ticket reads the row's cells back from L2, forms u = m + log(l) - log(tile_blocks)
-// (observe/tile_shares.py:172-173), the row's log total per query row, and every block's share with
-// the partial tail tile's weight given back to its blocks (:82-103), and writes the (layer, row)
-// share vector. The warp that completes a row's last layer (a second ticket, or the FINALIZE flag of
-// a single-layer launch) sums or maxes the layers in layer order and writes the row's final share.
-// No warp waits on another; every sum has a fixed order, so the output is deterministic.
+// Shares. The share kernel runs one CTA per (layer, row): it reads the row's cells back (from L2),
+// forms u = m + log(l) - log(tile_blocks) (observe/tile_shares.py:172-173), the row's log total per
+// query row, and every block's share with the partial tail tile's weight given back to its blocks
+// (:82-103); the CTA that completes a row's last layer (a ticket) sums or maxes the layers in layer
+// order into the row's final share. Every sum has a fixed order, so the output is deterministic.
 #include "ekv_common.cuh"
 
 namespace ekv {
@@ -28,7 +28,9 @@ namespace ekv {
 constexpr int kWarps = 4;
 constexpr int kMaxQ = 128;
 constexpr int kMaxRows = 2048;
+constexpr int kMaxLayers = 1024;
 constexpr int kChunkTiles = EKV_AUDIT_CHUNK_TILES;
+constexpr int kShareThreads = 128;
 
 struct AuditParams {
   // per-layer sources: device arrays of addresses, or one address for a single layer
@@ -52,12 +54,10 @@ struct AuditParams {
   int block_size, tile_blocks;
   int kv_heads;
   int64_t pool_blocks, q_tokens;
-  // the fused share
+  // the share
   float* share_out;
   int32_t* contrib_out;
   int aggregate;
-  int finalize;             // the launch ends the step: combine layers [0, layers) (single layer)
-  uint32_t* tickets;        // [layers][rows]
   uint32_t* row_tickets;    // [rows]
   int32_t* contrib_layer;   // [layers][rows]
   float* share_layer;       // [layers][rows][width]
@@ -79,7 +79,8 @@ __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Row r of the launch: its length, blocks, tiles and chunks; no chunks when it records nothing.
+// Row r of the step: its length (tokens, clamped to the table), blocks, tiles and chunks; no chunks
+// when it records nothing (not selected, empty, or a query token outside the batch).
 struct RowInfo {
   int n_blocks, n_tiles, n_chunks, len;
 };
@@ -111,113 +112,14 @@ __device__ __forceinline__ int kv_head_of(const AuditParams& p, int layer, int h
   return (p.rotate ? (p.group + layer) % p.kv_heads : p.group) + h;
 }
 
-// The combine over layers [la, lb) of row r, by one warp: sum (mean) or max (max) of the layers'
-// share vectors in layer order, skipping layers without data; the row's final share and count.
-__device__ void combine_layers(const AuditParams& p, int r, int la, int lb, int n_blocks) {
-  const int lane = threadIdx.x & 31;
-  int c = 0;
-  for (int L = la + lane; L < lb; L += 32) c += __ldcg(p.contrib_layer + (size_t)L * p.rows + r);
-  for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(kFullMask, c, off);
-  float* out = p.share_out + (size_t)r * p.width;
-  if (lane == 0) p.contrib_out[r] = c;
-  if (c == 0) {
-    for (int b = lane; b < p.width; b += 32) out[b] = NAN;
-    return;
-  }
-  const bool agg_max = p.aggregate == EKV_AGG_MAX;
-  float part = 0.f;
-  for (int b = lane; b < n_blocks; b += 32) {
-    float v = 0.f;
-    for (int L = la; L < lb; ++L) {
-      if (__ldcg(p.contrib_layer + (size_t)L * p.rows + r) == 0) continue;
-      const float s = __ldcg(p.share_layer + ((size_t)L * p.rows + r) * p.width + b);
-      v = agg_max ? fmaxf(v, s) : v + s;
-    }
-    out[b] = v;
-    part += v;
-  }
-  float total = part;
-  for (int off = 16; off > 0; off >>= 1) total += __shfl_xor_sync(kFullMask, total, off);
-  for (int b = lane; b < p.width; b += 32) {
-    float v = 0.f;
-    if (b < n_blocks) v = agg_max ? (total > 0.f ? out[b] / total : 0.f) : out[b] / (float)c;
-    out[b] = v;
-  }
-}
-
-// The (layer, row) epilogue, run by one warp: log totals, then the share of every block.
-__device__ void layer_row_epilogue(const AuditParams& p, int L, int r, int n_blocks, float* s_lse,
-                                   uint8_t* s_has) {
-  const int lane = threadIdx.x & 31;
-  const int Q = p.Q, TB = p.tile_blocks;
-  const int n_tiles = (n_blocks + TB - 1) / TB;
-  const float log_tb = logf((float)TB);
-  const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
-  const float* cm = p.lse + ((size_t)L * p.rows + r) * p.width * Q;
-  const float* cl = cm + plane;
-  // 1. the log total of each query row over the row's tiles (one cell per tile: its first block)
-  for (int j0 = 0; j0 < Q; j0 += 16) {
-    float m[16], s[16];
-#pragma unroll
-    for (int jj = 0; jj < 16; ++jj) m[jj] = -INFINITY, s[jj] = 0.f;
-    for (int t = lane; t < n_tiles; t += 32) {
-      const size_t cell = (size_t)t * TB * Q + j0;
-#pragma unroll
-      for (int jj = 0; jj < 16; ++jj) {
-        if (j0 + jj < Q) {
-          const float u = __ldcg(cm + cell + jj) + logf(__ldcg(cl + cell + jj)) - log_tb;
-          if (isfinite(u)) lse_merge(m[jj], s[jj], u, 1.f);
-        }
-      }
-    }
-#pragma unroll
-    for (int jj = 0; jj < 16; ++jj) {
-      for (int off = 16; off > 0; off >>= 1) {
-        const float m2 = __shfl_xor_sync(kFullMask, m[jj], off);
-        const float s2 = __shfl_xor_sync(kFullMask, s[jj], off);
-        lse_merge(m[jj], s[jj], m2, s2);
-      }
-      if (lane == 0 && j0 + jj < Q) {
-        s_has[j0 + jj] = m[jj] != -INFINITY;
-        s_lse[j0 + jj] = m[jj] != -INFINITY ? log_tb + m[jj] + logf(s[jj]) : 0.f;
-      }
-    }
-  }
-  __syncwarp();
-  int c = 0;
-  for (int j = lane; j < Q; j += 32) c += s_has[j];
-  for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(kFullMask, c, off);
-  // 2. every block's share, summed (mean) or maxed (max) over the query rows
-  const int tail = n_blocks % TB;
-  const int tail_start = n_blocks - tail;
-  const float regain = tail ? logf((float)TB / (float)tail) : 0.f;
-  const bool agg_max = p.aggregate == EKV_AGG_MAX;
-  float* sl = p.share_layer + ((size_t)L * p.rows + r) * p.width;
-  for (int b = lane; b < n_blocks; b += 32) {
-    const float rg = b >= tail_start ? regain : 0.f;
-    float a = 0.f;
-    for (int j = 0; j < Q; ++j) {
-      if (!s_has[j]) continue;
-      const float u = __ldcg(cm + (size_t)b * Q + j) + logf(__ldcg(cl + (size_t)b * Q + j)) - log_tb;
-      if (isfinite(u)) {
-        const float sh = __expf(u + rg - s_lse[j]);
-        a = agg_max ? fmaxf(a, sh) : a + sh;
-      }
-    }
-    sl[b] = a;
-  }
-  if (lane == 0) p.contrib_layer[(size_t)L * p.rows + r] = c;
-  __syncwarp();
-}
-
 // A warp's position in its sequence of tiles: the item and the tile inside it.
 struct Cursor {
   long long item;  // index into the launch's items; >= the total when done
-  int layer, head, row, t, t_end;
+  int layer, head, row, t0, t, t_end;
 };
 
 template <int TT, int NT, int D, typename T>
-__global__ void __launch_bounds__(kWarps * 32) audit_kernel(const AuditParams p) {
+__global__ void __launch_bounds__(kWarps * 32) record_kernel(const AuditParams p) {
   using Lay = Layout<D>;
   constexpr int STAGES = Ring<TT>::kStages;
   constexpr int STAGE = TT * Lay::kRowStride;
@@ -230,27 +132,28 @@ __global__ void __launch_bounds__(kWarps * 32) audit_kernel(const AuditParams p)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * STAGES * STAGE);
   uint32_t* vmasks = reinterpret_cast<uint32_t*>(bars + kWarps * STAGES);  // [warp][stage][WORDS]
   int* prefix = reinterpret_cast<int*>(vmasks + kWarps * STAGES * WORDS);  // [rows + 1]
-  __shared__ float s_lse[kWarps][kMaxQ];
-  __shared__ uint8_t s_has[kWarps][kMaxQ];
+  int* s_blocks = prefix + p.rows + 1;                                     // [rows]
+  int* s_len = s_blocks + p.rows;                                          // [rows]
+  int* s_tok = s_len + p.rows;                                             // [rows]
   __shared__ int s_scan[kWarps + 1];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool with_share = p.share_layer != nullptr;
-  if (*p.flag == 0) {  // the statistic is off: nothing is recorded (:64)
-    if (with_share && blockIdx.x == 0)
-      for (int i = threadIdx.x; i < p.n_layers * p.rows; i += blockDim.x)
-        p.contrib_layer[(size_t)(p.layer0 + i / p.rows) * p.rows + i % p.rows] = 0;
-    return;
-  }
+  if (*p.flag == 0) return;  // the statistic is off: nothing is recorded (:64)
 
-  // ---- the launch's items: chunks per row, prefix-summed in shared memory ------------------------
+  // ---- the rows of the step and the items: chunks per row, prefix-summed in shared memory --------
   {
     int carry = 0;
     for (int base = 0; base < p.rows; base += kWarps * 32) {
       const int r = base + threadIdx.x;
-      const int chunks = r < p.rows ? row_info(p, r, blockIdx.x == 0).n_chunks : 0;
+      RowInfo ri{0, 0, 0, 0};
+      if (r < p.rows) {
+        ri = row_info(p, r, blockIdx.x == 0);
+        s_blocks[r] = ri.n_blocks;
+        s_len[r] = ri.len;
+        s_tok[r] = ri.n_chunks ? p.qrow[r] : 0;
+      }
       int total = 0;
-      const int before = block_exclusive_scan<kWarps * 32>(chunks, s_scan, &total);
+      const int before = block_exclusive_scan<kWarps * 32>(ri.n_chunks, s_scan, &total);
       if (r < p.rows) prefix[r] = carry + before;
       carry += total;
     }
@@ -259,20 +162,6 @@ __global__ void __launch_bounds__(kWarps * 32) audit_kernel(const AuditParams p)
   }
   const int chunks_per_lh = prefix[p.rows];
   const long long total_items = (long long)chunks_per_lh * p.heads * p.n_layers;
-
-  // ---- rows that record nothing: no contributors; NaN share rows in a finalising launch ----------
-  if (with_share) {
-    for (int r = blockIdx.x; r < p.rows; r += gridDim.x) {
-      if (prefix[r + 1] != prefix[r]) continue;
-      for (int i = threadIdx.x; i < p.n_layers; i += blockDim.x)
-        p.contrib_layer[(size_t)(p.layer0 + i) * p.rows + r] = 0;
-      if (p.finalize) {
-        for (int b = threadIdx.x; b < p.width; b += blockDim.x) p.share_out[(size_t)r * p.width + b] = NAN;
-        if (threadIdx.x == 0) p.contrib_out[r] = 0;
-      }
-    }
-  }
-
   const long long workers = (long long)gridDim.x * kWarps;
   const long long worker = (long long)blockIdx.x * kWarps + warp;
   if (worker >= total_items) return;
@@ -290,13 +179,41 @@ __global__ void __launch_bounds__(kWarps * 32) audit_kernel(const AuditParams p)
     c.row = lo;
     c.layer = p.layer0 + (int)(lh / p.heads);
     c.head = (int)(lh % p.heads);
-    const int chunk = idx - prefix[lo];
-    const RowInfo ri = row_info(p, lo, false);
-    c.t = chunk * kChunkTiles;
-    c.t_end = min(c.t + kChunkTiles, ri.n_tiles);
+    const int n_tiles = (s_blocks[lo] + p.tile_blocks - 1) / p.tile_blocks;
+    c.t0 = c.t = (idx - prefix[lo]) * kChunkTiles;
+    c.t_end = min(c.t + kChunkTiles, n_tiles);
   };
-  auto advance = [&](Cursor& c) {
-    if (++c.t >= c.t_end) decode(c.item + workers, c);
+
+  // the block ids of an item: lane i holds blocks t0 * tile_blocks + i and + 32 + i
+  auto load_ids = [&](const Cursor& c, int32_t& lo_id, int32_t& hi_id) {
+    lo_id = hi_id = -1;
+    if (c.item >= total_items) return;
+    const int32_t* trow = p.table + (int64_t)c.row * p.table_s0;
+    const int b0 = c.t0 * p.tile_blocks;
+    const int nb = min(s_blocks[c.row], c.t_end * p.tile_blocks) - b0;
+    if (lane < nb) lo_id = __ldg(trow + b0 + lane);
+    if (lane + 32 < nb) hi_id = __ldg(trow + b0 + lane + 32);
+  };
+
+  // the query rows of an item's (layer, row, head), as mma B fragments (k16 x n8, column = query row)
+  auto load_q = [&](const Cursor& c, uint32_t (&bq)[NT][KS][2]) {
+    if (c.item >= total_items) return;
+    const void* qsrc = p.q_layers ? reinterpret_cast<const void*>(p.q_layers[c.layer]) : p.q;
+    const bool q_ok = (reinterpret_cast<uintptr_t>(qsrc) & 3) == 0;
+    const T* qtok = static_cast<const T*>(qsrc) + (int64_t)s_tok[c.row] * p.q_s0;
+    const int qhead = p.q_stash ? c.head : kv_head_of(p, c.layer, c.head);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int g = nt * 8 + (lane >> 2);
+      const bool ok = q_ok && g < p.G;
+      const T* qh = qtok + (int64_t)(qhead * p.G + (ok ? g : 0)) * p.q_s1;
+#pragma unroll
+      for (int k = 0; k < KS; ++k) {
+        const int d = k * 16 + 2 * (lane & 3);
+        bq[nt][k][0] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qh + d)) : 0u;
+        bq[nt][k][1] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qh + d + 8)) : 0u;
+      }
+    }
   };
 
   uint8_t* my_ring = rings + warp * STAGES * STAGE;
@@ -309,29 +226,37 @@ __global__ void __launch_bounds__(kWarps * 32) audit_kernel(const AuditParams p)
   __syncwarp();
   const uint64_t policy = l2_evict_first_policy();
 
-  // Issue the bulk copies of the tile at cursor c into stage s.
-  auto issue = [&](const Cursor& c, int s) {
-    const RowInfo ri = row_info(p, c.row, false);
-    const T* kbase = static_cast<const T*>(p.k_layers ? reinterpret_cast<const void*>(p.k_layers[c.layer]) : p.k);
+  // the issue side: cursor `in`, the ids of its item and of the item after it
+  Cursor in{}, in_next{};
+  int32_t ids_lo, ids_hi, nids_lo, nids_hi;
+  decode(worker, in);
+  load_ids(in, ids_lo, ids_hi);
+  decode(worker + workers, in_next);
+  load_ids(in_next, nids_lo, nids_hi);
+
+  // Issue the bulk copies of the tile at `in` into stage s, then step `in` forward.
+  auto issue_and_advance = [&](int s) {
+    const T* kbase = static_cast<const T*>(p.k_layers ? reinterpret_cast<const void*>(p.k_layers[in.layer]) : p.k);
     const bool aligned = (reinterpret_cast<uintptr_t>(kbase) & 15) == 0;
-    kbase += (int64_t)kv_head_of(p, c.layer, c.head) * p.k_s2;
-    const int32_t* trow = p.table + (int64_t)c.row * p.table_s0;
+    kbase += (int64_t)kv_head_of(p, in.layer, in.head) * p.k_s2;
+    const int n_blocks = s_blocks[in.row];
+    const int tl = in.t - in.t0;
     uint32_t total = 0;
     int64_t off[WORDS];
     uint32_t mask[WORDS];
 #pragma unroll
     for (int w = 0; w < WORDS; ++w) {
       const int tok = lane + 32 * w;
+      const int bi = tl * p.tile_blocks + (tok < TT ? tok : 0) / p.block_size;  // block of the item
+      const int32_t lo_id = __shfl_sync(kFullMask, ids_lo, bi & 31);
+      const int32_t hi_id = __shfl_sync(kFullMask, ids_hi, bi & 31);
+      const int32_t id = bi < 32 ? lo_id : hi_id;
       bool ok = false;
       off[w] = 0;
-      if (tok < TT) {
-        const int b = c.t * p.tile_blocks + tok / p.block_size;
-        if (b < ri.n_blocks) {
-          const int32_t id = __ldg(trow + b);
-          ok = aligned && id >= 0 && (int64_t)id < p.pool_blocks;
-          if (!ok && tok % p.block_size == 0) set_status(p.status, EKV_STATUS_BAD_BLOCK_ID);
-          off[w] = (int64_t)id * p.k_s0 + (int64_t)(tok % p.block_size) * p.k_s1;
-        }
+      if (tok < TT && in.t * p.tile_blocks + tok / p.block_size < n_blocks) {
+        ok = aligned && id >= 0 && (int64_t)id < p.pool_blocks;
+        if (!ok && tok % p.block_size == 0) set_status(p.status, EKV_STATUS_BAD_BLOCK_ID);
+        off[w] = (int64_t)id * p.k_s0 + (int64_t)(tok % p.block_size) * p.k_s1;
       }
       mask[w] = __ballot_sync(kFullMask, ok);
       total += __popc(mask[w]);
@@ -351,53 +276,46 @@ __global__ void __launch_bounds__(kWarps * 32) audit_kernel(const AuditParams p)
     for (int w = 0; w < WORDS; ++w)
       if ((mask[w] >> lane) & 1u)
         bulk_copy_g2s(stage + (lane + 32 * w) * Lay::kRowStride, kbase + off[w], Lay::kRowBytes, &my_bars[s], policy);
+    if (++in.t >= in.t_end) {  // the next item: its ids were prefetched; prefetch the one after
+      in = in_next;
+      ids_lo = nids_lo;
+      ids_hi = nids_hi;
+      decode(in.item + workers, in_next);
+      load_ids(in_next, nids_lo, nids_hi);
+    }
   };
 
-  // ---- prologue: fill the ring ---------------------------------------------------------------------
-  Cursor in{}, out{};
-  decode(worker, in);
-  out = in;
   long long issued = 0;
   for (int s = 0; s < STAGES && in.item < total_items; ++s) {
-    issue(in, s);
+    issue_and_advance(s);
     ++issued;
-    advance(in);
   }
 
+  // the consume side: cursor `out`, the query fragments of its item and of the next one
+  Cursor out{};
+  decode(worker, out);
+  uint32_t bq[NT][KS][2], bqn[NT][KS][2];
+  load_q(out, bqn);
   const size_t plane = (size_t)p.layers * p.rows * p.width * p.Q;
-  uint32_t bq[NT][KS][2];
-  int q_layer = -1, q_row = -1, q_head = -1;
   bool timed_out = false;
   long long consumed = 0, unwaited = 0;  // copies from tile `unwaited` on were never waited for
 
   while (out.item < total_items) {
     const int s = (int)(consumed % STAGES);
     const uint32_t parity = (uint32_t)((consumed / STAGES) & 1);
-    // the query rows of this (layer, row, head), as mma B fragments
-    if (out.layer != q_layer || out.row != q_row || out.head != q_head) {
-      q_layer = out.layer, q_row = out.row, q_head = out.head;
-      const void* qsrc = p.q_layers ? reinterpret_cast<const void*>(p.q_layers[out.layer]) : p.q;
-      const bool q_ok = (reinterpret_cast<uintptr_t>(qsrc) & 3) == 0;
-      const T* qtok = static_cast<const T*>(qsrc) + (int64_t)p.qrow[out.row] * p.q_s0;
-      const int qhead = p.q_stash ? out.head : kv_head_of(p, out.layer, out.head);
+    if (out.t == out.t0) {  // an item starts: its fragments were prefetched; prefetch the next item's
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int g = nt * 8 + (lane >> 2);
-        const bool ok = q_ok && g < p.G;
-        const T* qh = qtok + (int64_t)(qhead * p.G + (ok ? g : 0)) * p.q_s1;
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int k = 0; k < KS; ++k) {
-          const int d = k * 16 + 2 * (lane & 3);
-          bq[nt][k][0] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qh + d)) : 0u;
-          bq[nt][k][1] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qh + d + 8)) : 0u;
-        }
-      }
+        for (int k = 0; k < KS; ++k) bq[nt][k][0] = bqn[nt][k][0], bq[nt][k][1] = bqn[nt][k][1];
+      Cursor nxt{};
+      decode(out.item + workers, nxt);
+      load_q(nxt, bqn);
     }
     if (!timed_out && !mbar_wait_bounded(&my_bars[s], parity, p.status)) {
       timed_out = true;
       unwaited = consumed;
     }
-    const RowInfo ri = row_info(p, out.row, false);
     if (!timed_out) {
       const uint8_t* stage = my_ring + s * STAGE;
       float c[MT][NT][4];
@@ -423,6 +341,7 @@ __global__ void __launch_bounds__(kWarps * 32) audit_kernel(const AuditParams p)
 #pragma unroll
       for (int w = 0; w < WORDS; ++w) vm[w] = my_masks[s * WORDS + w];
       const int first = out.t * TT;
+      const int len = s_len[out.row];
       float mx[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) mx[nt][0] = mx[nt][1] = -INFINITY;
@@ -431,7 +350,7 @@ __global__ void __launch_bounds__(kWarps * 32) audit_kernel(const AuditParams p)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int tok = mt * 16 + (lane >> 2) + 8 * h;  // bit tok % 32 of word tok / 32 = mt / 2
-          const bool ok = first + tok < ri.len && ((vm[mt >> 1] >> (tok & 31)) & 1u);
+          const bool ok = first + tok < len && ((vm[mt >> 1] >> (tok & 31)) & 1u);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -468,7 +387,7 @@ __global__ void __launch_bounds__(kWarps * 32) audit_kernel(const AuditParams p)
       // every block cell of the tile inside the row gets the tile's (m, l); lane / 4 picks the block
       const int bi = lane >> 2;
       const int b = out.t * p.tile_blocks + bi;
-      if (bi < p.tile_blocks && b < ri.n_blocks) {
+      if (bi < p.tile_blocks && b < s_blocks[out.row]) {
         float* cm = p.lse + (((size_t)out.layer * p.rows + out.row) * p.width + b) * p.Q + out.head * p.G;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
@@ -487,40 +406,10 @@ __global__ void __launch_bounds__(kWarps * 32) audit_kernel(const AuditParams p)
     fence_proxy_async();
     ++consumed;
     if (in.item < total_items && !timed_out) {
-      issue(in, (int)(issued % STAGES));
+      issue_and_advance((int)(issued % STAGES));
       ++issued;
-      advance(in);
     }
-    // an item ends: take its ticket; the last one of the (layer, row) runs the epilogue
-    const Cursor done = out;
-    advance(out);
-    if (with_share && done.t + 1 >= done.t_end) {
-      __threadfence();
-      uint32_t last = 0;
-      if (lane == 0) {
-        const uint32_t target = (uint32_t)(ri.n_chunks * p.heads);
-        last = atomicAdd(&p.tickets[(size_t)done.layer * p.rows + done.row], 1u) == target - 1;
-      }
-      last = __shfl_sync(kFullMask, last, 0);
-      if (last) {
-        __threadfence();
-        if (lane == 0) p.tickets[(size_t)done.layer * p.rows + done.row] = 0;
-        layer_row_epilogue(p, done.layer, done.row, ri.n_blocks, s_lse[warp], s_has[warp]);
-        __threadfence();
-        if (p.n_layers == 1) {
-          if (p.finalize) combine_layers(p, done.row, 0, p.layers, ri.n_blocks);
-        } else {
-          uint32_t row_last = 0;
-          if (lane == 0) row_last = atomicAdd(&p.row_tickets[done.row], 1u) == (uint32_t)(p.n_layers - 1);
-          row_last = __shfl_sync(kFullMask, row_last, 0);
-          if (row_last) {
-            __threadfence();
-            if (lane == 0) p.row_tickets[done.row] = 0;
-            combine_layers(p, done.row, p.layer0, p.layer0 + p.n_layers, ri.n_blocks);
-          }
-        }
-      }
-    }
+    if (++out.t >= out.t_end) decode(out.item + workers, out);
   }
   if (timed_out) {
     // let copies still in flight land before the shared memory is released
@@ -529,23 +418,148 @@ __global__ void __launch_bounds__(kWarps * 32) audit_kernel(const AuditParams p)
   }
 }
 
+// ---- the share kernel: one CTA per (layer, row) ------------------------------------------------------
+
+__global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams p) {
+  __shared__ float s_m[kShareThreads], s_s[kShareThreads];
+  __shared__ float s_lse[kMaxQ];
+  __shared__ uint8_t s_has[kMaxQ];
+  __shared__ int s_count;
+  __shared__ int s_last;
+  __shared__ float s_red[kShareThreads / 32];
+  __shared__ uint8_t s_layer_on[kMaxLayers];
+  const int L = p.layer0 + blockIdx.x, r = blockIdx.y;
+  const int tid = threadIdx.x;
+  if (*p.flag == 0) return;  // nothing was recorded this step
+  const RowInfo ri = row_info(p, r, false);
+  const size_t lr = (size_t)L * p.rows + r;
+  if (ri.n_chunks == 0) {  // the row records nothing: no contributors, a NaN share row
+    if (tid == 0) p.contrib_layer[lr] = 0;
+    if (blockIdx.x == 0) {
+      for (int b = tid; b < p.width; b += kShareThreads) p.share_out[(size_t)r * p.width + b] = NAN;
+      if (tid == 0) p.contrib_out[r] = 0;
+    }
+    return;
+  }
+  const int Q = p.Q, TB = p.tile_blocks, n = ri.n_blocks;
+  const float log_tb = logf((float)TB);
+  const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
+  const float* cm = p.lse + lr * p.width * Q;
+  const float* cl = cm + plane;
+  // 1. the log total of each query row over the row's tiles (one cell per tile: its first block)
+  const int per_j = kShareThreads / Q;
+  const int j = tid % Q;
+  float m = -INFINITY, s = 0.f;
+  if (tid < per_j * Q) {
+    for (int t = tid / Q; t < ri.n_tiles; t += per_j) {
+      const size_t cell = (size_t)t * TB * Q + j;
+      const float u = __ldcg(cm + cell) + logf(__ldcg(cl + cell)) - log_tb;
+      if (isfinite(u)) lse_merge(m, s, u, 1.f);
+    }
+  }
+  s_m[tid] = m;
+  s_s[tid] = s;
+  __syncthreads();
+  if (tid < Q) {
+    float mj = -INFINITY, sj = 0.f;
+    for (int k = 0; k < per_j; ++k) lse_merge(mj, sj, s_m[k * Q + tid], s_s[k * Q + tid]);
+    s_has[tid] = mj != -INFINITY;
+    s_lse[tid] = mj != -INFINITY ? log_tb + mj + logf(sj) : 0.f;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int c = 0;
+    for (int k = 0; k < Q; ++k) c += s_has[k];
+    s_count = c;
+    p.contrib_layer[lr] = c;
+  }
+  // 2. every block's share, summed (mean) or maxed (max) over the query rows
+  const int tail = n % TB;
+  const int tail_start = n - tail;
+  const float regain = tail ? logf((float)TB / (float)tail) : 0.f;
+  const bool agg_max = p.aggregate == EKV_AGG_MAX;
+  float* sl = p.share_layer + lr * p.width;
+  for (int b = tid; b < n; b += kShareThreads) {
+    const float rg = b >= tail_start ? regain : 0.f;
+    float a = 0.f;
+    for (int k = 0; k < Q; ++k) {
+      const float u = __ldcg(cm + (size_t)b * Q + k) + logf(__ldcg(cl + (size_t)b * Q + k)) - log_tb;
+      const float sh = (s_has[k] && isfinite(u)) ? __expf(u + rg - s_lse[k]) : 0.f;
+      a = agg_max ? fmaxf(a, sh) : a + sh;
+    }
+    sl[b] = a;
+  }
+  // 3. the CTA that completes the row's last layer combines the layers in layer order
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&p.row_tickets[r], 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int la = p.layer0, lb = p.layer0 + gridDim.x;
+  int c = 0;
+  for (int k = la + tid; k < lb; k += kShareThreads) {
+    const int ck = __ldcg(p.contrib_layer + (size_t)k * p.rows + r);
+    s_layer_on[k - la] = ck != 0;
+    c += ck;
+  }
+  for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(kFullMask, c, off);
+  __shared__ int s_c[kShareThreads / 32];
+  if ((tid & 31) == 0) s_c[tid >> 5] = c;
+  __syncthreads();
+  if (tid == 0) {
+    p.row_tickets[r] = 0;  // ready for the next step
+    int total = 0;
+    for (int w = 0; w < kShareThreads / 32; ++w) total += s_c[w];
+    s_count = total;
+    p.contrib_out[r] = total;
+  }
+  __syncthreads();
+  const int contributors = s_count;
+  float* out = p.share_out + (size_t)r * p.width;
+  float part = 0.f;
+  for (int b = tid; b < n; b += kShareThreads) {
+    float v = 0.f;
+    for (int k = la; k < lb; ++k) {
+      const float x = __ldcg(p.share_layer + ((size_t)k * p.rows + r) * p.width + b);
+      v = s_layer_on[k - la] ? (agg_max ? fmaxf(v, x) : v + x) : v;
+    }
+    out[b] = v;
+    part += v;
+  }
+  const float total = agg_max ? block_sum_fixed_order<kShareThreads>(part, s_red) : 1.f;
+  for (int b = tid; b < p.width; b += kShareThreads) {
+    float v;
+    if (contributors == 0) {
+      v = NAN;
+    } else if (b >= n) {
+      v = 0.f;
+    } else {
+      v = agg_max ? (total > 0.f ? out[b] / total : 0.f) : out[b] / (float)contributors;
+    }
+    out[b] = v;
+  }
+}
+
+// The record kernel over p.layer0 .. p.layer0 + p.n_layers, then (finalize) the share kernel over the
+// layers [share0, share0 + share_layers): every layer of the step, so the table's current cells decide.
 template <int TT, int NT, int D, typename T>
-int launch_audit(const AuditParams& p, cudaStream_t stream) {
+int launch_audit(const AuditParams& p, bool finalize, int share0, int share_layers, cudaStream_t stream) {
   using Lay = Layout<D>;
   constexpr int STAGES = Ring<TT>::kStages;
   constexpr int WORDS = (TT + 31) / 32;
   constexpr size_t fixed = (size_t)kWarps * STAGES * TT * Lay::kRowStride + kWarps * STAGES * (8 + WORDS * 4);
-  const size_t smem = fixed + (size_t)(p.rows + 1) * 4;
+  const size_t smem = fixed + (size_t)(4 * p.rows + 1) * 4;
   static int grid_of[kMaxDevices] = {};
   static size_t smem_of[kMaxDevices] = {};
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
     return check_launch("cudaGetDevice");
-  auto kernel = audit_kernel<TT, NT, D, T>;
+  auto kernel = record_kernel<TT, NT, D, T>;
   if (grid_of[device] == 0 || smem_of[device] != smem) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(fixed + (size_t)(kMaxRows + 1) * 4)) != cudaSuccess)
-      return check_launch("cudaFuncSetAttribute(audit_kernel)");
+                             (int)(fixed + (size_t)(4 * kMaxRows + 1) * 4)) != cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(record_kernel)");
     int sms = 0, per_sm = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
       return check_launch("cudaDeviceGetAttribute");
@@ -555,33 +569,38 @@ int launch_audit(const AuditParams& p, cudaStream_t stream) {
     smem_of[device] = smem;
   }
   kernel<<<grid_of[device], kWarps * 32, smem, stream>>>(p);
-  return check_launch("audit_kernel");
+  int rc = check_launch("record_kernel");
+  if (rc != EKV_OK || !finalize || p.share_out == nullptr) return rc;
+  AuditParams ps = p;
+  ps.layer0 = share0;
+  ps.n_layers = share_layers;
+  share_kernel<<<dim3(share_layers, p.rows), kShareThreads, 0, stream>>>(ps);
+  return check_launch("share_kernel");
 }
 
 template <typename T>
-int dispatch(const AuditParams& p, int tt, cudaStream_t stream) {
+int dispatch(const AuditParams& p, int tt, bool finalize, int share0, int share_layers, cudaStream_t stream) {
   const int nt = p.G <= 8 ? 1 : 2;
   switch (tt * 4 + nt) {
-    case 16 * 4 + 1: return launch_audit<16, 1, 128, T>(p, stream);
-    case 16 * 4 + 2: return launch_audit<16, 2, 128, T>(p, stream);
-    case 32 * 4 + 1: return launch_audit<32, 1, 128, T>(p, stream);
-    case 32 * 4 + 2: return launch_audit<32, 2, 128, T>(p, stream);
-    case 64 * 4 + 1: return launch_audit<64, 1, 128, T>(p, stream);
-    case 64 * 4 + 2: return launch_audit<64, 2, 128, T>(p, stream);
+    case 16 * 4 + 1: return launch_audit<16, 1, 128, T>(p, finalize, share0, share_layers, stream);
+    case 16 * 4 + 2: return launch_audit<16, 2, 128, T>(p, finalize, share0, share_layers, stream);
+    case 32 * 4 + 1: return launch_audit<32, 1, 128, T>(p, finalize, share0, share_layers, stream);
+    case 32 * 4 + 2: return launch_audit<32, 2, 128, T>(p, finalize, share0, share_layers, stream);
+    case 64 * 4 + 1: return launch_audit<64, 1, 128, T>(p, finalize, share0, share_layers, stream);
+    case 64 * 4 + 2: return launch_audit<64, 2, 128, T>(p, finalize, share0, share_layers, stream);
     default: break;
   }
   return fail(EKV_ENOTSUP, "no audit kernel for a tile of %d tokens", tt);
 }
 
 struct WorkspaceLayout {
-  size_t tickets, row_tickets, contrib, share, total;
+  size_t row_tickets, contrib, share, total;
 };
 
 WorkspaceLayout workspace_layout(int layers, int rows, int width) {
   WorkspaceLayout w{};
-  w.tickets = 0;
-  w.row_tickets = round_up((size_t)layers * rows * 4, 256);
-  w.contrib = w.row_tickets + round_up((size_t)rows * 4, 256);
+  w.row_tickets = 0;
+  w.contrib = round_up((size_t)rows * 4, 256);
   w.share = w.contrib + round_up((size_t)layers * rows * 4, 256);
   w.total = w.share + round_up((size_t)layers * rows * width * 4, 256);
   return w;
@@ -599,6 +618,7 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
     return fail(EKV_EINVAL, "a required device pointer is NULL");
   if (rows <= 0 || width <= 0 || layers <= 0) return fail(EKV_EINVAL, "rows, width and layers must be positive");
   if (rows > kMaxRows) return fail(EKV_ENOTSUP, "%d rows: this build handles up to %d", rows, kMaxRows);
+  if (layers > kMaxLayers) return fail(EKV_ENOTSUP, "%d layers: this build handles up to %d", layers, kMaxLayers);
   if (group_rows < 1 || group_rows > 16)
     return fail(EKV_EINVAL, "%d query heads per KV head: the kernel handles 1 to 16", group_rows);
   if (heads < 1 || heads > kv_heads) return fail(EKV_EINVAL, "%d heads per layer of a cache with %d", heads, kv_heads);
@@ -628,7 +648,6 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
       return fail(EKV_ERANGE, "the audit workspace holds %zu bytes, the launch needs %zu", workspace_bytes, w.total);
     if ((uintptr_t)workspace & 255) return fail(EKV_EINVAL, "the audit workspace must be 256-byte aligned");
     uint8_t* base = static_cast<uint8_t*>(workspace);
-    p.tickets = reinterpret_cast<uint32_t*>(base + w.tickets);
     p.row_tickets = reinterpret_cast<uint32_t*>(base + w.row_tickets);
     p.contrib_layer = reinterpret_cast<int32_t*>(base + w.contrib);
     p.share_layer = reinterpret_cast<float*>(base + w.share);
@@ -712,10 +731,11 @@ extern "C" int ekv_audit_launch(
   if (((uintptr_t)k & 15) || ((uintptr_t)q & 3))
     return fail(EKV_EINVAL, "the key cache must be 16-byte aligned and the query 4-byte aligned");
   p.q = q; p.k = k; p.layer0 = layer; p.n_layers = 1; p.group = group; p.rotate = 0;
-  p.finalize = (share_flags & EKV_SHARE_FINALIZE) != 0;
+  const bool finalize = (share_flags & EKV_SHARE_FINALIZE) != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int tt = block_size * tile_blocks;
-  return dtype == EKV_DTYPE_BF16 ? dispatch<__nv_bfloat16>(p, tt, s) : dispatch<__half>(p, tt, s);
+  return dtype == EKV_DTYPE_BF16 ? dispatch<__nv_bfloat16>(p, tt, finalize, 0, layers, s)
+                                 : dispatch<__half>(p, tt, finalize, 0, layers, s);
 }
 
 extern "C" int ekv_audit_step(
@@ -743,8 +763,9 @@ extern "C" int ekv_audit_step(
     return fail(EKV_EINVAL, "KV head %d (rotate %d, %d heads) does not fit a cache of %d heads", group,
                 rotate, heads, kv_heads);
   p.q_layers = q_layers; p.k_layers = k_layers; p.layer0 = layer0; p.n_layers = n_layers;
-  p.group = group; p.rotate = rotate != 0; p.finalize = 1; p.q_stash = q_layout != 0;
+  p.group = group; p.rotate = rotate != 0; p.q_stash = q_layout != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int tt = block_size * tile_blocks;
-  return dtype == EKV_DTYPE_BF16 ? dispatch<__nv_bfloat16>(p, tt, s) : dispatch<__half>(p, tt, s);
+  return dtype == EKV_DTYPE_BF16 ? dispatch<__nv_bfloat16>(p, tt, true, layer0, n_layers, s)
+                                 : dispatch<__half>(p, tt, true, layer0, n_layers, s);
 }

@@ -48,13 +48,13 @@ def test_constants_agree_with_the_header():
 
 
 def test_workspace_size(lib):
-    # tickets [layers][rows] + row tickets [rows] + contributors [layers][rows] + shares [layers][rows][width]
+    # row tickets [rows] + contributors [layers][rows] + shares [layers][rows][width]
     layers, rows, width = 32, 64, 512
 
     def up(x):
         return -(-x // 256) * 256
 
-    want = up(layers * rows * 4) + up(rows * 4) + up(layers * rows * 4) + up(layers * rows * width * 4)
+    want = up(rows * 4) + up(layers * rows * 4) + up(layers * rows * width * 4)
     assert lib.ekv_audit_workspace_bytes(layers, rows, width) == want
     assert lib.ekv_audit_workspace_bytes(0, rows, width) == 0
 

@@ -166,9 +166,9 @@ class Workload:
             for _ in range(cfg["pools"])
         ]
         tokens = self.rows
-        self.queries = [
+        self.queries = [  # every layer's query of the step, resident in HBM
             torch.randn(tokens, self.kv_local * self.group_rows, HEAD_DIM, device=dev, generator=gen,
-                        dtype=torch.bfloat16) for _ in range(cfg["pools"])
+                        dtype=torch.bfloat16) for _ in range(self.layers)
         ]
         self.table = torch.from_numpy(table).to(dev)
         self.lens_t = torch.from_numpy(self.lens).to(dev)
@@ -183,7 +183,7 @@ class Workload:
         return self.caches[layer % len(self.caches)][:, 0]
 
     def query(self, layer: int) -> torch.Tensor:
-        return self.queries[layer % len(self.queries)]
+        return self.queries[layer]
 
 
 def make_plane(w: Workload, deferred: bool):
@@ -198,8 +198,16 @@ def make_plane(w: Workload, deferred: bool):
 
 
 def audit_step(plane, w: Workload) -> None:
+    """One audit step through RecordingPlane.record's path: a call per layer (deferred: a query stash
+    per layer and one launch of every layer after the last; per-layer: a launch per layer)."""
     for layer in range(w.layers):
         plane.launch(layer, w.table, w.lens_t, w.query(layer), w.keys(layer), w.scale)
+
+
+def audit_step_resident(plane, w: Workload) -> None:
+    """One audit step from queries resident per layer: one launch of every layer (record_step)."""
+    plane.record_step(w.table, w.lens_t, [w.query(layer) for layer in range(w.layers)],
+                      [w.caches[layer % len(w.caches)] for layer in range(w.layers)], w.scale)
 
 
 def capture(fn) -> torch.cuda.CUDAGraph:
@@ -402,7 +410,10 @@ def main() -> None:
 
     w = Workload(cfg, rank, world, args.mode)
     plane = make_plane(w, deferred=args.record == "deferred")
-    graph = capture(lambda: audit_step(plane, w))
+    if args.record == "deferred":
+        graph = capture(lambda: audit_step_resident(plane, w))
+    else:
+        graph = capture(lambda: audit_step(plane, w))
     share = plane.shares()
 
     def step():
@@ -439,12 +450,14 @@ def main() -> None:
     pinned_tok = torch.from_numpy(w.qrow).pin_memory()
     out_host = torch.empty(share.shape, dtype=share.dtype).pin_memory()
 
+    api_graph = capture(lambda: audit_step(plane, w)) if args.record == "deferred" else graph
+
     def e2e_step():
         w.table.copy_(pinned_table, non_blocking=True)
         w.lens_t.copy_(pinned_lens, non_blocking=True)
         plane._select.copy_(pinned_sel, non_blocking=True)
         plane._token.copy_(pinned_tok, non_blocking=True)
-        graph.replay()
+        api_graph.replay()
         if dist_on:
             allreduce_shares(share)
         out_host.copy_(share, non_blocking=True)
@@ -482,8 +495,10 @@ def main() -> None:
                      "note": "per layer; duration = step time / layers, every launch of the step included"},
         "e2e": {"value": units_all * args.steps / e2e_seconds, "unit": "audited KV tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "note": "block table, lengths, selection, query rows in; shares out; KV cache resident"},
-        "gpu_launches": args.steps * (w.layers + 1 if args.record == "deferred" else w.layers),
+                "note": "RecordingPlane.record per layer (a query stash per layer, one launch of every layer "
+                        "after the last) in a CUDA graph; block table, lengths, selection, query rows in from "
+                        "pinned host memory, shares out; KV cache resident"},
+        "gpu_launches": args.steps * (2 if args.record == "deferred" else w.layers + 1),
         "clocks": clocks.summary(),
         "per_layer_launches": per_layer,
         "view": view,

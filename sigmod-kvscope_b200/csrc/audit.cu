@@ -25,7 +25,15 @@
 
 namespace ekv {
 
-constexpr int kWarps = 4;
+// Warps per CTA of the record kernel and ring stages per warp (tiles of 32 tokens; tiles of 16 hold
+// twice as many, tiles of 64 half as many). Overridable at build time for tuning sweeps.
+#ifndef EKV_AUDIT_WARPS
+#define EKV_AUDIT_WARPS 4
+#endif
+#ifndef EKV_AUDIT_STAGES32
+#define EKV_AUDIT_STAGES32 3
+#endif
+constexpr int kWarps = EKV_AUDIT_WARPS;
 constexpr int kMaxQ = 128;
 constexpr int kMaxRows = 2048;
 constexpr int kMaxLayers = 1024;
@@ -72,7 +80,7 @@ struct Layout {
 
 template <int TT>
 struct Ring {
-  static constexpr int kStages = TT <= 16 ? 6 : (TT <= 32 ? 3 : 2);
+  static constexpr int kStages = TT <= 16 ? 2 * EKV_AUDIT_STAGES32 : (TT <= 32 ? EKV_AUDIT_STAGES32 : (EKV_AUDIT_STAGES32 + 1) / 2);
 };
 
 __device__ __forceinline__ void fence_proxy_async() {
@@ -451,10 +459,21 @@ __global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams 
   const int j = tid % Q;
   float m = -INFINITY, s = 0.f;
   if (tid < per_j * Q) {
-    for (int t = tid / Q; t < ri.n_tiles; t += per_j) {
-      const size_t cell = (size_t)t * TB * Q + j;
-      const float u = __ldcg(cm + cell) + logf(__ldcg(cl + cell)) - log_tb;
-      if (isfinite(u)) lse_merge(m, s, u, 1.f);
+    constexpr int U = 4;  // cells loaded before any is used
+    for (int t0 = tid / Q; t0 < ri.n_tiles; t0 += U * per_j) {
+      float mv[U], lv[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int t = t0 + u * per_j;
+        const size_t cell = (size_t)(t < ri.n_tiles ? t : 0) * TB * Q + j;
+        mv[u] = __ldcg(cm + cell);
+        lv[u] = __ldcg(cl + cell);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float x = mv[u] + logf(lv[u]) - log_tb;
+        if (t0 + u * per_j < ri.n_tiles && isfinite(x)) lse_merge(m, s, x, 1.f);
+      }
     }
   }
   s_m[tid] = m;
@@ -482,10 +501,22 @@ __global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams 
   for (int b = tid; b < n; b += kShareThreads) {
     const float rg = b >= tail_start ? regain : 0.f;
     float a = 0.f;
-    for (int k = 0; k < Q; ++k) {
-      const float u = __ldcg(cm + (size_t)b * Q + k) + logf(__ldcg(cl + (size_t)b * Q + k)) - log_tb;
-      const float sh = (s_has[k] && isfinite(u)) ? __expf(u + rg - s_lse[k]) : 0.f;
-      a = agg_max ? fmaxf(a, sh) : a + sh;
+    constexpr int U = 4;
+    for (int k0 = 0; k0 < Q; k0 += U) {
+      float mv[U], lv[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int k = k0 + u < Q ? k0 + u : 0;
+        mv[u] = __ldcg(cm + (size_t)b * Q + k);
+        lv[u] = __ldcg(cl + (size_t)b * Q + k);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int k = k0 + u;
+        const float x = mv[u] + logf(lv[u]) - log_tb;
+        const float sh = (k < Q && s_has[k < Q ? k : 0] && isfinite(x)) ? __expf(x + rg - s_lse[k < Q ? k : 0]) : 0.f;
+        a = agg_max ? fmaxf(a, sh) : a + sh;
+      }
     }
     sl[b] = a;
   }
@@ -520,9 +551,19 @@ __global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams 
   float part = 0.f;
   for (int b = tid; b < n; b += kShareThreads) {
     float v = 0.f;
-    for (int k = la; k < lb; ++k) {
-      const float x = __ldcg(p.share_layer + ((size_t)k * p.rows + r) * p.width + b);
-      v = s_layer_on[k - la] ? (agg_max ? fmaxf(v, x) : v + x) : v;
+    constexpr int U = 8;  // layers loaded before any is added, then added in layer order
+    for (int k0 = la; k0 < lb; k0 += U) {
+      float x[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int k = k0 + u < lb ? k0 + u : la;
+        x[u] = __ldcg(p.share_layer + ((size_t)k * p.rows + r) * p.width + b);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int k = k0 + u;
+        if (k < lb && s_layer_on[k - la]) v = agg_max ? fmaxf(v, x[u]) : v + x[u];
+      }
     }
     out[b] = v;
     part += v;
@@ -557,12 +598,15 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
     return check_launch("cudaGetDevice");
   auto kernel = record_kernel<TT, NT, D, T>;
   if (grid_of[device] == 0 || smem_of[device] != smem) {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(fixed + (size_t)(4 * kMaxRows + 1) * 4)) != cudaSuccess)
-      return check_launch("cudaFuncSetAttribute(record_kernel)");
-    int sms = 0, per_sm = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+    int sms = 0, per_sm = 0, optin = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device) != cudaSuccess)
       return check_launch("cudaDeviceGetAttribute");
+    if (smem > (size_t)optin)
+      return fail(EKV_ENOTSUP, "the record kernel needs %zu bytes of shared memory for %d rows; the device has %d",
+                  smem, p.rows, optin);
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(record_kernel)");
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kWarps * 32, smem) != cudaSuccess)
       return check_launch("cudaOccupancyMaxActiveBlocksPerMultiprocessor");
     grid_of[device] = sms * (per_sm > 0 ? per_sm : 1);

@@ -101,6 +101,7 @@ class RecordingPlane(AuditPlane):
         self._stash_addresses: torch.Tensor | None = None
         self._rows_index = torch.arange(rows, dtype=torch.int32, device=device)
         self._key_shape: tuple | None = None
+        self._step_addresses: dict[tuple, tuple[torch.Tensor, torch.Tensor]] = {}
         torch.cuda.synchronize()
         self._publish()
 
@@ -283,6 +284,57 @@ class RecordingPlane(AuditPlane):
             dtype, self.heads, keys.shape[2], keys.shape[0], self.rows,
             self._share.data_ptr(), self._contributors.data_ptr(), _AGGREGATES[self.aggregate],
             workspace, self._workspace_bytes, self._status.data_ptr(), stream,
+        )
+        _lib.check(rc, "ekv_audit_step")
+
+    def record_step(
+        self,
+        table: torch.Tensor,
+        lens: torch.Tensor,
+        queries: list[torch.Tensor],
+        kv_caches: list[torch.Tensor],
+        scale: float,
+        stream: int | None = None,
+    ) -> None:
+        """Record every layer of a step in one launch, from each layer's query and KV cache.
+
+        For a caller that holds every layer's query [tokens, q_heads, dim] (an offline audit, or an
+        engine that keeps them): the cells and shares equal those of ``record`` called layer by layer.
+        The layers are numbered 0 .. len(queries) - 1; the address arrays are cached per set of
+        tensors, so a CUDA graph can capture the call.
+        """
+        if len(queries) != self._layers or len(kv_caches) != self._layers:
+            raise ValueError(f"a step records all {self._layers} layers")
+        keys = [kv[:, 0] for kv in kv_caches]
+        q0, k0 = queries[0], keys[0]
+        for q, k in zip(queries, keys, strict=True):
+            if q.shape != q0.shape or q.stride() != q0.stride() or q.dtype != q0.dtype:
+                raise ValueError("every layer's query must have the same shape, strides and dtype")
+            if k.shape != k0.shape or k.stride() != k0.stride() or k.dtype != q0.dtype:
+                raise ValueError("every layer's key cache must have the same shape, strides and dtype as the query")
+        kv_heads, dim = k0.shape[2], k0.shape[3]
+        if kv_heads * self.group_rows != q0.shape[1] or dim != q0.shape[2] or q0.dtype not in _DTYPES:
+            raise ValueError("the query and KV cache shapes do not match the plane's group size")
+        if self.heads != 1 and self.heads != kv_heads:
+            raise ValueError(f"an all-heads plane of {self.heads} heads got a cache of {kv_heads}")
+        if table.dtype != torch.int32 or lens.dtype != torch.int32 or table.shape[1] != self.width:
+            raise ValueError("the block table and the lengths must be int32 and match the plane's width")
+        key = tuple(q.data_ptr() for q in queries) + tuple(k.data_ptr() for k in keys)
+        addresses = self._step_addresses.get(key)
+        if addresses is None:
+            q_addr = torch.tensor([q.data_ptr() for q in queries], dtype=torch.uint64, device=self._device)
+            k_addr = torch.tensor([k.data_ptr() for k in keys], dtype=torch.uint64, device=self._device)
+            addresses = self._step_addresses[key] = (q_addr, k_addr)
+        q_addr, k_addr = addresses
+        workspace = (self._workspace.data_ptr() + 255) // 256 * 256
+        rc = self._lib.ekv_audit_step(
+            q_addr.data_ptr(), k_addr.data_ptr(), table.data_ptr(), lens.data_ptr(), self._token.data_ptr(),
+            self._select.data_ptr(), self._flag_dev, self._lse, float(scale), 0, self._layers, 0,
+            1 if self.heads == 1 else 0, 0, q0.stride(0), q0.stride(1), k0.stride(0), k0.stride(1), k0.stride(2),
+            table.stride(0), self._layers, self.rows, self.width, self.group_rows, self.block_size, TILE_BLOCKS, dim,
+            _DTYPES[q0.dtype], self.heads, kv_heads, k0.shape[0], q0.shape[0], self._share.data_ptr(),
+            self._contributors.data_ptr(), _AGGREGATES[self.aggregate], workspace, self._workspace_bytes,
+            self._status.data_ptr(), _lib.current_stream() if stream is None else stream,
         )
         _lib.check(rc, "ekv_audit_step")
 

@@ -605,7 +605,7 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
     if (smem > (size_t)optin)
       return fail(EKV_ENOTSUP, "the record kernel needs %zu bytes of shared memory for %d rows; the device has %d",
                   smem, p.rows, optin);
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess)
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(record_kernel)");
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kWarps * 32, smem) != cudaSuccess)
       return check_launch("cudaOccupancyMaxActiveBlocksPerMultiprocessor");

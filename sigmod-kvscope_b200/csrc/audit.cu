@@ -31,7 +31,7 @@ namespace ekv {
 #define EKV_AUDIT_WARPS 4
 #endif
 #ifndef EKV_AUDIT_STAGES32
-#define EKV_AUDIT_STAGES32 3
+#define EKV_AUDIT_STAGES32 2
 #endif
 constexpr int kWarps = EKV_AUDIT_WARPS;
 constexpr int kMaxQ = 128;

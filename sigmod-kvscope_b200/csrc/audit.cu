@@ -80,7 +80,7 @@ struct Layout {
 
 template <int TT>
 struct Ring {
-  static constexpr int kStages = TT <= 16 ? 2 * EKV_AUDIT_STAGES32 : (TT <= 32 ? EKV_AUDIT_STAGES32 : (EKV_AUDIT_STAGES32 + 1) / 2);
+  static constexpr int kStages = TT <= 16 ? 2 * EKV_AUDIT_STAGES32 : (TT <= 32 ? EKV_AUDIT_STAGES32 : (EKV_AUDIT_STAGES32 + 1) / 2 > 2 ? (EKV_AUDIT_STAGES32 + 1) / 2 : 2);
 };
 
 __device__ __forceinline__ void fence_proxy_async() {

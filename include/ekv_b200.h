@@ -134,6 +134,32 @@ int ekv_audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int
                    size_t workspace_bytes, uint32_t* status, void* stream);
 
 /*
+ * ekv_audit_step_static -- ekv_audit_step for callers that cannot allocate device memory.
+ *
+ * No counterpart in the reference: an addition of this library. Some callers cannot call cudaMalloc
+ * when they record -- a binding with no CUDA allocator of its own (a cgo or ctypes caller that only
+ * holds the engine's tensors), or engine code after memory profiling has sized the KV-cache pool,
+ * where one more allocation can fail or fragment it. This entry point takes no workspace: it uses a
+ * static device array of ekv_audit_static_scratch_bytes() bytes (16 MiB) that every GPU loading the
+ * library holds until exit, and rejects with EKV_ERANGE a step whose ekv_audit_workspace_bytes()
+ * exceeds it. The caller still passes every input and output. It allocates nothing: the first call on
+ * a device looks the array's device address up (cudaGetSymbolAddress), so make that first call before
+ * any stream capture. Every call shares the array and clears its tickets first; calls whose launches
+ * overlap on the GPU race.
+ */
+size_t ekv_audit_static_scratch_bytes(void);
+int ekv_audit_step_static(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table,
+                          const int32_t* lens, const int32_t* qrow, const uint8_t* select,
+                          const uint32_t* flag, float* lse, float scale, int layer0, int n_layers,
+                          int group, int rotate, int q_layout, int64_t q_stride_token,
+                          int64_t q_stride_head, int64_t k_stride_block, int64_t k_stride_pos,
+                          int64_t k_stride_head, int64_t table_stride, int layers, int rows,
+                          int width, int group_rows, int block_size, int tile_blocks, int head_dim,
+                          int dtype, int heads, int kv_heads, int64_t pool_blocks, int64_t q_tokens,
+                          float* share_out, int32_t* contributors, int aggregate, uint32_t* status,
+                          void* stream);
+
+/*
  * ekv_normalize_tile_lse -- the controller's read of the statistic, on the device.
  *
  * Replaces read_tile_rows (observe/tile_shares.py:129-173) followed by normalize_tile_lse

@@ -813,3 +813,68 @@ extern "C" int ekv_audit_step(
   return dtype == EKV_DTYPE_BF16 ? dispatch<__nv_bfloat16>(p, tt, true, layer0, n_layers, s)
                                  : dispatch<__half>(p, tt, true, layer0, n_layers, s);
 }
+
+// ---- the audit step without a caller-provided workspace ---------------------------------------------
+//
+// Some callers cannot allocate device memory when they record: a binding that has no CUDA allocator of
+// its own (a cgo or ctypes caller that only holds the engine's tensors), or engine code after memory
+// profiling has sized the KV-cache pool, where one more cudaMalloc can fail or fragment the pool. For
+// them the step's workspace lives in this file-scope array, which every GPU that loads the library
+// holds until the process exits. Every call shares it: calls whose launches overlap on the GPU race.
+
+#define EKV_AUDIT_STATIC_SCRATCH_BYTES (16u << 20)
+
+static __device__ __align__(256) uint8_t g_audit_scratch[EKV_AUDIT_STATIC_SCRATCH_BYTES];
+
+#include <mutex>
+
+extern "C" size_t ekv_audit_static_scratch_bytes(void) { return EKV_AUDIT_STATIC_SCRATCH_BYTES; }
+
+extern "C" int ekv_audit_step_static(
+    const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table, const int32_t* lens,
+    const int32_t* qrow, const uint8_t* select, const uint32_t* flag, float* lse, float scale,
+    int layer0, int n_layers, int group, int rotate, int q_layout, int64_t q_stride_token,
+    int64_t q_stride_head, int64_t k_stride_block, int64_t k_stride_pos, int64_t k_stride_head,
+    int64_t table_stride, int layers, int rows, int width, int group_rows, int block_size,
+    int tile_blocks, int head_dim, int dtype, int heads, int kv_heads, int64_t pool_blocks,
+    int64_t q_tokens, float* share_out, int32_t* contributors, int aggregate, uint32_t* status,
+    void* stream) {
+  clear_error();
+  if (!share_out || !contributors) return fail(EKV_EINVAL, "share_out and contributors are required");
+  if (layers <= 0 || rows <= 0 || width <= 0) return fail(EKV_EINVAL, "rows, width and layers must be positive");
+  const size_t need = ekv_audit_workspace_bytes(layers, rows, width);
+  if (need > EKV_AUDIT_STATIC_SCRATCH_BYTES)
+    return fail(EKV_ERANGE,
+                "a step of %d layers x %d rows x %d blocks needs %zu bytes of workspace; the static one holds %u: "
+                "pass a workspace to ekv_audit_step instead",
+                layers, rows, width, need, (unsigned)EKV_AUDIT_STATIC_SCRATCH_BYTES);
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
+    return check_launch("cudaGetDevice");
+  // The array's name is a host-side stand-in; the device address is looked up once per device, with
+  // that device current.
+  static void* scratch_of[kMaxDevices] = {};
+  static std::mutex setup;
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(setup);
+    if (scratch_of[device] == nullptr) {
+      void* ptr = nullptr;
+      const cudaError_t err = cudaGetSymbolAddress(&ptr, g_audit_scratch);
+      if (err != cudaSuccess || ptr == nullptr)
+        return fail(EKV_ECUDA, "cudaGetSymbolAddress(static audit workspace): %s", cudaGetErrorString(err));
+      scratch_of[device] = ptr;
+    }
+    scratch = scratch_of[device];
+  }
+  // The array keeps the last call's contents: the row tickets must start at zero.
+  const WorkspaceLayout w = workspace_layout(layers, rows, width);
+  if (cudaMemsetAsync(static_cast<uint8_t*>(scratch) + w.row_tickets, 0, w.contrib - w.row_tickets,
+                      static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return check_launch("cudaMemsetAsync(static audit workspace)");
+  return ekv_audit_step(q_layers, k_layers, table, lens, qrow, select, flag, lse, scale, layer0, n_layers,
+                        group, rotate, q_layout, q_stride_token, q_stride_head, k_stride_block, k_stride_pos,
+                        k_stride_head, table_stride, layers, rows, width, group_rows, block_size, tile_blocks,
+                        head_dim, dtype, heads, kv_heads, pool_blocks, q_tokens, share_out, contributors,
+                        aggregate, scratch, EKV_AUDIT_STATIC_SCRATCH_BYTES, status, stream);
+}

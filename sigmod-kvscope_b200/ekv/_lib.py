@@ -56,6 +56,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _p, _p, _i32,  # share_out contributors aggregate
          _p, _sz, _p, _p],  # workspace bytes status stream
     ),
+    "ekv_audit_static_scratch_bytes": (_sz, []),
+    "ekv_audit_step_static": (
+        _i32,
+        [_p, _p, _p, _p, _p, _p, _p, _p,  # q_layers k_layers table lens qrow select flag lse
+         _f32, _i32, _i32, _i32, _i32, _i32,  # scale layer0 n_layers group rotate q_layout
+         _i64, _i64, _i64, _i64, _i64, _i64,  # q strides, k strides, table stride
+         _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,  # layers rows width G bs tb D dtype
+         _i32, _i32, _i64, _i64,  # heads kv_heads pool_blocks q_tokens
+         _p, _p, _i32,  # share_out contributors aggregate
+         _p, _p],  # status stream
+    ),
     "ekv_normalize_tile_lse": (
         _i32, [_p, _i32, _i32, _i32, _i32, _i32, _p, _p, _i32, _i32, _i32, _p, _p, _p]
     ),

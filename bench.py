@@ -51,9 +51,9 @@ CONFIGS = {
     "long": dict(rows=8, q_heads=32, kv_heads=8, layers=32, pool=66_000, lens=("uniform", 32768, 131072), pools=4),
 }
 
-# dram__bytes_read.sum + dram__bytes_write.sum per audit launch from the committed ncu capture
-# (profiles/audit_kernel_llama8b.md), scaled to one full-size launch; None until captured.
-NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"llama8b": None}
+# dram__bytes_read.sum + dram__bytes_write.sum of one record-kernel launch (an audit step of all 32
+# layers) of the llama8b workload, from an ncu capture of that launch.
+NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"llama8b": 2458.652e6 + 8.532e6}
 
 
 def lengths(spec, rows: int, rng: np.random.Generator) -> np.ndarray:
@@ -204,10 +204,10 @@ def audit_step(plane, w: Workload) -> None:
         plane.launch(layer, w.table, w.lens_t, w.query(layer), w.keys(layer), w.scale)
 
 
-def audit_step_resident(plane, w: Workload) -> None:
+def audit_step_resident(plane, w: Workload, shares: bool = True) -> None:
     """One audit step from queries resident per layer: one launch of every layer (record_step)."""
     plane.record_step(w.table, w.lens_t, [w.query(layer) for layer in range(w.layers)],
-                      [w.caches[layer % len(w.caches)] for layer in range(w.layers)], w.scale)
+                      [w.caches[layer % len(w.caches)] for layer in range(w.layers)], w.scale, shares=shares)
 
 
 def capture(fn) -> torch.cuda.CUDAGraph:
@@ -438,8 +438,17 @@ def main() -> None:
     units_rank = w.units_per_step()
     units_all = units_rank * world
     value = units_all * args.steps / seconds
-    launch_seconds = seconds / args.steps / w.layers
-    per_launch_bytes = units_rank / w.layers * bytes_per_unit(w.heads * w.group_rows)
+    # the roofline of the dominant kernel: the record kernel alone, one launch per audit step
+    # (deferred) or per layer (per-layer), timed over its own launches
+    if args.record == "deferred":
+        record_graph = capture(lambda: audit_step_resident(plane, w, shares=False))
+        launch_seconds = timed(record_graph.replay, args.steps, args.warmup, dist_on) / args.steps
+        per_launch_units = units_rank
+        del record_graph
+    else:
+        launch_seconds = seconds / args.steps / w.layers
+        per_launch_units = units_rank / w.layers
+    per_launch_bytes = per_launch_units * bytes_per_unit(w.heads * w.group_rows)
     achieved = per_launch_bytes / launch_seconds / 1e9
     peak, peak_kind = measured_peak()
 
@@ -476,7 +485,8 @@ def main() -> None:
         dist.destroy_process_group()
     if rank != 0:
         return
-    traffic = NCU_TRAFFIC_PER_LAUNCH.get(args.config) if args.mode == "reference" else None
+    traffic = NCU_TRAFFIC_PER_LAUNCH.get(args.config) if (args.mode == "reference" and args.record == "deferred"
+                                                          and world == 1) else None
     line = {
         "metric": "audited KV tokens/s", "value": value, "unit": "audited KV tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": seconds / args.steps * 1e3,
@@ -490,9 +500,11 @@ def main() -> None:
                    "l2": f"inputs larger than L2: {units_rank / w.layers * 256 / 1e6:.0f} MB of keys per launch",
                    "parallelism": f"tp{world} (KV heads)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "peak_kind": peak_kind,
-                     "bytes_per_unit": bytes_per_unit(w.heads * w.group_rows),
-                     "note": "per layer; duration = step time / layers, every launch of the step included"},
+                     "traffic": traffic, "peak_kind": peak_kind, "kernel": "record_kernel",
+                     "bytes_per_unit": bytes_per_unit(w.heads * w.group_rows), "units_per_launch": per_launch_units,
+                     "launch_us": launch_seconds * 1e6,
+                     "note": "record kernel alone, one launch per audit step of every layer (per-layer: one per "
+                             "layer); CUDA events over its own timed launches"},
         "e2e": {"value": units_all * args.steps / e2e_seconds, "unit": "audited KV tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "note": "RecordingPlane.record per layer (a query stash per layer, one launch of every layer "

@@ -295,13 +295,14 @@ class RecordingPlane(AuditPlane):
         kv_caches: list[torch.Tensor],
         scale: float,
         stream: int | None = None,
+        shares: bool = True,
     ) -> None:
         """Record every layer of a step in one launch, from each layer's query and KV cache.
 
         For a caller that holds every layer's query [tokens, q_heads, dim] (an offline audit, or an
         engine that keeps them): the cells and shares equal those of ``record`` called layer by layer.
         The layers are numbered 0 .. len(queries) - 1; the address arrays are cached per set of
-        tensors, so a CUDA graph can capture the call.
+        tensors, so a CUDA graph can capture the call. ``shares=False`` records the cells only.
         """
         if len(queries) != self._layers or len(kv_caches) != self._layers:
             raise ValueError(f"a step records all {self._layers} layers")
@@ -332,8 +333,9 @@ class RecordingPlane(AuditPlane):
             self._select.data_ptr(), self._flag_dev, self._lse, float(scale), 0, self._layers, 0,
             1 if self.heads == 1 else 0, 0, q0.stride(0), q0.stride(1), k0.stride(0), k0.stride(1), k0.stride(2),
             table.stride(0), self._layers, self.rows, self.width, self.group_rows, self.block_size, TILE_BLOCKS, dim,
-            _DTYPES[q0.dtype], self.heads, kv_heads, k0.shape[0], q0.shape[0], self._share.data_ptr(),
-            self._contributors.data_ptr(), _AGGREGATES[self.aggregate], workspace, self._workspace_bytes,
+            _DTYPES[q0.dtype], self.heads, kv_heads, k0.shape[0], q0.shape[0],
+            self._share.data_ptr() if shares else None, self._contributors.data_ptr() if shares else None,
+            _AGGREGATES[self.aggregate], workspace if shares else None, self._workspace_bytes if shares else 0,
             self._status.data_ptr(), _lib.current_stream() if stream is None else stream,
         )
         _lib.check(rc, "ekv_audit_step")

@@ -229,7 +229,7 @@ int ekv_allocate_quotas(const int32_t* row_blocks, const int32_t* measured_block
  * (runtime/block_view.py:36-56) keeps block 0 and the last block of ceil(seq_lens/block_size),
  * writes the kept blocks in order followed by the others in order into view, and
  * view_lens = (kept - 1) * block_size + tokens of the last block (0 for an empty row).
- * width <= 32768.
+ * width <= 16384 (a row is staged in shared memory).
  */
 int ekv_view_build(const int32_t* table, int64_t table_stride, const int32_t* seq_lens,
                    const int32_t* row_blocks, const int32_t* quota, const int32_t* measured_blocks,

@@ -162,166 +162,264 @@ struct ViewParams {
 };
 
 constexpr int kViewThreads = 512;
-constexpr int kViewMaxWidth = 32768;
+constexpr int kViewWarps = kViewThreads / 32;
+constexpr int kViewMaxWidth = 16384;               // rows staged in shared memory: 8 bytes per position
+constexpr int kViewMaxIters = kViewMaxWidth / kViewThreads;
+constexpr int kViewBins = 2048;                    // radix-select digits of 11, 11 and 9 bits
+static_assert(kViewBins == 4 * kViewThreads, "each thread owns four histogram bins");
 
 __device__ __forceinline__ uint32_t share_key(float x) {
-  // max(x, 0) with NaN as 0; for x >= 0 the IEEE bit pattern is monotone in x
+  // max(x, 0) with NaN as 0; for x >= 0 the IEEE bit pattern is monotone in x and bit 31 is clear
   return x > 0.f ? __float_as_uint(x) : 0u;
 }
 
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// n 32-bit words from global to shared memory (16-byte aligned) without blocking the thread.
+__device__ __forceinline__ void stage_words(uint32_t* dst, const uint32_t* src, int n) {
+  int done = 0;
+  if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    done = n & ~3;
+    for (int i = 4 * threadIdx.x; i < done; i += 4 * kViewThreads) cp_async16(dst + i, src + i);
+  }
+  for (int i = done + threadIdx.x; i < n; i += kViewThreads) cp_async4(dst + i, src + i);
+}
+
+// dst[i] = src[i] for i in [lo, hi), 16 bytes at a time where both rows allow it.
+__device__ __forceinline__ void copy_words(int32_t* dst, const int32_t* src, int lo, int hi) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0 && (lo & 3) == 0;
+  int i = lo;
+  if (vec) {
+    const int stop = lo + ((hi - lo) & ~3);
+    for (int j = lo + 4 * threadIdx.x; j < stop; j += 4 * kViewThreads)
+      *reinterpret_cast<int4*>(dst + j) = *reinterpret_cast<const int4*>(src + j);
+    i = stop;
+  }
+  for (int j = i + threadIdx.x; j < hi; j += kViewThreads) dst[j] = src[j];
+}
+
+__device__ __forceinline__ uint32_t lanes_below() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// Exclusive scan of one count per warp (warp 0 scans); returns this warp's base and sets *total.
+__device__ __forceinline__ int warp_bases(int count, int* s_w, int* total) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) s_w[warp] = count;
+  __syncthreads();
+  if (warp == 0) {
+    int v = lane < kViewWarps ? s_w[lane] : 0;
+    int inc = v;
+    for (int off = 1; off < 32; off <<= 1) {
+      const int n = __shfl_up_sync(kFullMask, inc, off);
+      if (lane >= off) inc += n;
+    }
+    if (lane < kViewWarps) s_w[lane] = inc - v;
+    if (lane == kViewWarps - 1) s_w[kViewWarps] = inc;
+  }
+  __syncthreads();
+  *total = s_w[kViewWarps];
+  return s_w[warp];
+}
+
+// One CTA per row.
+//
+// The ranking: the q-th largest key among positions [1, ps) by a three-pass MSB radix select (digits
+// of bits 30-20, 19-9 and 8-0; bit 31 of a key is always clear). Thread t owns histogram bins
+// [4t, 4t + 4): it reads them for the scan and clears them for the next pass in the same step. If
+// the chosen bin holds exactly the keys still wanted, every key with that prefix is kept and the
+// select stops early. The equal-key count comes from the last histogram, so the scan that ranks
+// equal keys by position runs only when some of them must be dropped.
+//
+// The layout: only positions [0, min(blocks, width)) can be kept, so those are laid out warp-striped
+// (warp w owns [w * 32 * iters, (w + 1) * 32 * iters), lane l of iteration i holds base + 32 * i + l,
+// so a ballot per iteration orders a warp's positions), and the rest of the row, never kept, keeps its
+// place: the view there is the table. With mask_out the layout covers the whole width, as every
+// position's committed flag is written.
 __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) {
-  extern __shared__ uint32_t s_keys[];  // [width] keys of the unpinned blocks (ranking mode)
-  __shared__ int s_hist[256];
-  __shared__ int s_scan[kViewThreads / 32 + 1];
-  __shared__ int s_pick[2];
+  extern __shared__ __align__(16) uint32_t smem_view[];
+  __shared__ __align__(16) int s_hist[kViewBins];
+  __shared__ int s_w[kViewWarps + 1];
+  __shared__ int s_pick[3];
+  __shared__ uint32_t s_bits[kViewWarps][kViewMaxIters];  // each warp's keep ballots, per iteration
   const int r = blockIdx.x;
   const int W = p.width, BS = p.block_size;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int w_pad = (W + kViewThreads - 1) / kViewThreads * kViewThreads;
+  uint32_t* keys = smem_view;                                      // [w_pad]: shares -> keys -> view row
+  int32_t* trow_s = reinterpret_cast<int32_t*>(smem_view + w_pad);  // [w_pad]: the table row
 
-  // ---- the committed mask: pins + selection (ranking mode) or the given mask ---------------------
+  const int seq = p.seq_lens[r];
+  const int blocks = seq > 0 ? (seq + BS - 1) / BS : 0;
+  uint8_t* mrow = p.mask_out ? p.mask_out + (int64_t)r * p.mask_s0 : nullptr;
+  const int live = mrow != nullptr ? W : (blocks < W ? blocks : W);
+  const int iters = (live + kViewThreads - 1) / kViewThreads;
+  const int wbase = warp * 32 * iters;
+  const int laid = iters * kViewThreads < W ? iters * kViewThreads : W;  // positions [0, laid) laid out
+
+  // ---- the row's committed mask: pins + selection (ranking mode) or the given mask ---------------
   const bool rank_mode = p.keep == nullptr;
-  int n_a = 0, ps = 0, q = -1;
-  bool select_all = false, select_none = true, by_threshold = false, newest = false;
-  uint32_t threshold = 0;
-  int k_eq = 0;  // keys equal to the threshold that are kept
-  bool ties_need_rank = false;
+  int ps = 0, q = 0, open_hi = 1;  // the selection applies to positions [1, open_hi)
+  bool by_threshold = false, newest = false;
   if (rank_mode) {
-    n_a = p.row_blocks[r];
+    int n_a = p.row_blocks[r];
     n_a = n_a < 0 ? 0 : (n_a > W ? W : n_a);
     q = p.quota[r];
     if (q >= 0 && n_a > 0) {
       ps = pin_start(n_a, p.recent, p.measured, r);
       const int n_open = ps > 1 ? ps - 1 : 0;
       if (q > n_open) q = n_open;
-      select_none = q == 0;
-      select_all = q == n_open && q > 0;
-      if (!select_none && !select_all) {
-        if (p.policy == EKV_POLICY_NEWEST) {
-          newest = true;
-        } else {
-          by_threshold = true;
+      if (q < n_open) {  // not every open position is selected
+        open_hi = ps;
+        if (q > 0) {
+          if (p.policy == EKV_POLICY_NEWEST) newest = true; else by_threshold = true;
         }
       }
     }
   }
   if (by_threshold) {
-    const float* srow = p.scores + (int64_t)r * p.score_s0;
-    for (int b = 1 + threadIdx.x; b < ps; b += kViewThreads) s_keys[b] = share_key(srow[b]);
-    uint32_t prefix = 0, pmask = 0;
+    stage_words(keys, reinterpret_cast<const uint32_t*>(p.scores + (int64_t)r * p.score_s0), ps);
+    cp_async_commit();
+  }
+  const int32_t* trow = p.table + (int64_t)r * p.table_s0;
+  stage_words(reinterpret_cast<uint32_t*>(trow_s), reinterpret_cast<const uint32_t*>(trow), laid);
+  cp_async_commit();
+
+  uint32_t prefix = 0, pmask = 0;
+  int k_eq = 0, eq_total = 0;
+  if (by_threshold) {
+    cp_async_wait<1>();  // the shares have landed (the table may still be in flight)
+    __syncthreads();
+    for (int b = 1 + threadIdx.x; b < ps; b += kViewThreads) keys[b] = share_key(__uint_as_float(keys[b]));
+    reinterpret_cast<int4*>(s_hist)[threadIdx.x] = make_int4(0, 0, 0, 0);
+    __syncthreads();
     int k = q;
 #pragma unroll 1
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      for (int i = threadIdx.x; i < 256; i += kViewThreads) s_hist[i] = 0;
-      __syncthreads();
+    for (int pass = 0; pass < 3; ++pass) {
+      const int shift = pass == 0 ? 20 : (pass == 1 ? 9 : 0);
+      const uint32_t dmask = pass == 2 ? 511u : 2047u;
       for (int b = 1 + threadIdx.x; b < ps; b += kViewThreads) {
-        const uint32_t key = s_keys[b];
-        if ((key & pmask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1);
+        const uint32_t key = keys[b];
+        if ((key & pmask) == prefix) atomicAdd(&s_hist[(key >> shift) & dmask], 1);
       }
       __syncthreads();
-      if (warp == 0) {
-        // lane owns digits [8*lane, 8*lane+8); count the keys above each digit from the top down
-        int local[8], sum = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) local[i] = s_hist[8 * lane + i], sum += local[i];
-        int above = sum;  // inclusive suffix sum over lanes >= lane
-        for (int off = 1; off < 32; off <<= 1) {
-          const int v = __shfl_down_sync(kFullMask, above, off);
-          if (lane + off < 32) above += v;
-        }
-        int gt = above - sum;  // keys in digits owned by higher lanes
-#pragma unroll
-        for (int i = 7; i >= 0; --i) {
-          if (gt < k && gt + local[i] >= k) {
-            s_pick[0] = 8 * lane + i;
-            s_pick[1] = gt;
-          }
-          gt += local[i];
-        }
+      const int4 h = reinterpret_cast<const int4*>(s_hist)[threadIdx.x];
+      reinterpret_cast<int4*>(s_hist)[threadIdx.x] = make_int4(0, 0, 0, 0);
+      const int sum = h.x + h.y + h.z + h.w;
+      int above = sum;  // keys in bins owned by this lane and the lanes above it in the warp
+      for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_down_sync(kFullMask, above, off);
+        if (lane + off < 32) above += v;
       }
+      if (lane == 0) s_w[warp] = above;
       __syncthreads();
-      const int d = s_pick[0];
+      int gt = above - sum;  // keys in higher bins
+      for (int w2 = warp + 1; w2 < kViewWarps; ++w2) gt += s_w[w2];
+      const int bin = 4 * threadIdx.x;
+      if (gt < k && gt + h.w >= k) s_pick[0] = bin + 3, s_pick[1] = gt, s_pick[2] = h.w;
+      gt += h.w;
+      if (gt < k && gt + h.z >= k) s_pick[0] = bin + 2, s_pick[1] = gt, s_pick[2] = h.z;
+      gt += h.z;
+      if (gt < k && gt + h.y >= k) s_pick[0] = bin + 1, s_pick[1] = gt, s_pick[2] = h.y;
+      gt += h.y;
+      if (gt < k && gt + h.x >= k) s_pick[0] = bin, s_pick[1] = gt, s_pick[2] = h.x;
+      __syncthreads();
       k -= s_pick[1];
-      prefix |= (uint32_t)d << shift;
-      pmask |= 255u << shift;
-      __syncthreads();  // s_pick is rewritten by the next pass
+      prefix |= (uint32_t)s_pick[0] << shift;
+      pmask |= dmask << shift;
+      eq_total = s_pick[2];  // the keys with the chosen prefix
+      if (eq_total == k) break;  // all of them are kept: the prefix is the threshold
     }
-    threshold = prefix;
     k_eq = k;
-    ties_need_rank = true;  // resolved below once the number of equal keys is known
   }
-
-  // ---- per-thread blocked ranges: thread t owns [t*ipt, (t+1)*ipt) ----------------------------------
-  const int ipt = (W + kViewThreads - 1) / kViewThreads;
-  const int b0 = threadIdx.x * ipt;
-  const int b1 = min(b0 + ipt, W);
-
-  // rank of equal keys: how many equal keys precede this thread's range
-  int eq_before = 0, eq_total = 0;
-  if (by_threshold) {
-    int cnt = 0;
-    for (int b = max(b0, 1); b < min(b1, ps); ++b) cnt += s_keys[b] == threshold;
-    eq_before = block_exclusive_scan<kViewThreads>(cnt, s_scan, &eq_total);
-    ties_need_rank = eq_total != k_eq;
-  }
+  const bool ties = eq_total != k_eq;  // only then do keys equal to the threshold need their rank
   const bool older_first = p.policy == EKV_POLICY_UNIFORM;
 
-  const int seq = p.seq_lens[r];
-  const int blocks = seq > 0 ? (seq + BS - 1) / BS : 0;
+  // ---- ties: each equal key's rank among the equal keys, in position order --------------------
+  int eq_base = 0;
+  if (ties) {
+    int cnt = 0;
+    for (int i = 0; i < iters; ++i) {
+      const int b = wbase + 32 * i + lane;
+      const bool eq = b >= 1 && b < ps && (keys[b] & pmask) == prefix;
+      cnt += __popc(__ballot_sync(kFullMask, eq));
+    }
+    int unused = 0;
+    eq_base = warp_bases(cnt, s_w, &unused);
+  }
+
   const bool full = p.full_rows != nullptr && p.full_rows[r] != 0;
-  const int32_t* trow = p.table + (int64_t)r * p.table_s0;
   const uint8_t* krow = rank_mode ? nullptr : p.keep + (int64_t)r * p.keep_s0;
   const uint8_t* rrow = p.released ? p.released + (int64_t)r * p.released_s0 : nullptr;
-  uint8_t* mrow = p.mask_out ? p.mask_out + (int64_t)r * p.mask_s0 : nullptr;
 
-  // The committed mask at b (ranking mode: the controller's row).
-  auto committed = [&](int b, int& eq_seen) -> bool {
-    if (!rank_mode) return krow[b] != 0;
-    if (q < 0 || n_a == 0 || b >= n_a || b == 0 || b >= ps) return true;
-    if (select_all) return true;
-    if (select_none) return false;
-    if (newest) return b >= ps - q;
-    const uint32_t key = s_keys[b];
-    if (key > threshold) return true;
-    if (key != threshold) return false;
-    const int before = eq_seen++;
-    if (!ties_need_rank) return true;
-    return older_first ? before < k_eq : (eq_total - before - 1) < k_eq;
-  };
-
-  // pass 1: the final keep flags of this thread's range, counted
-  int kept_local = 0;
-  {
-    int eq_seen = eq_before;
-    for (int b = b0; b < b1; ++b) {
-      bool k = committed(b, eq_seen) || full;
-      if (rrow != nullptr && rrow[b]) k = false;  // a released block is never read (block_view.py:280-281)
-      k = (k || b == 0 || b == blocks - 1) && b < blocks;
-      kept_local += k;
-    }
-  }
-  int kept_total = 0;
-  const int kept_before = block_exclusive_scan<kViewThreads>(kept_local, s_scan, &kept_total);
-
-  // pass 2: scatter kept blocks to the front and the rest after them, both in order
-  {
-    int eq_seen = eq_before;
-    int kept = kept_before;
-    int32_t* vrow = p.view + (int64_t)r * p.view_s0;
-    for (int b = b0; b < b1; ++b) {
-      const bool c = committed(b, eq_seen);
-      if (mrow != nullptr) mrow[b] = c;
-      bool k = c || full;
-      if (rrow != nullptr && rrow[b]) k = false;
-      k = (k || b == 0 || b == blocks - 1) && b < blocks;
-      const int32_t id = trow[b];
-      if (k) {
-        vrow[kept++] = id;
+  // ---- pass 1: the final keep flag of every laid-out position, as one ballot per iteration ---------
+  int kept_count = 0, eq_seen = eq_base;
+  for (int i = 0; i < iters; ++i) {
+    const int b = wbase + 32 * i + lane;
+    const bool in_row = b < W;
+    bool c = in_row;  // the committed mask at b
+    if (!rank_mode) {
+      c = in_row && krow[b] != 0;
+    } else if (b >= 1 && b < open_hi) {
+      if (newest) {
+        c = b >= ps - q;
+      } else if (by_threshold) {
+        const uint32_t key = keys[b] & pmask;
+        c = key > prefix || (key == prefix && !ties);  // every equal key is kept unless too many
       } else {
-        vrow[kept_total + (b - kept)] = id;
+        c = false;  // nothing selected
       }
     }
+    if (ties) {
+      const bool eq = b >= 1 && b < ps && (keys[b] & pmask) == prefix;
+      const uint32_t eqb = __ballot_sync(kFullMask, eq);
+      if (eq) {
+        const int before = eq_seen + __popc(eqb & lanes_below());
+        c = older_first ? before < k_eq : (eq_total - before - 1) < k_eq;
+      }
+      eq_seen += __popc(eqb);
+    }
+    if (mrow != nullptr && in_row) mrow[b] = c;
+    bool keep = c || full;
+    if (rrow != nullptr && in_row && rrow[b]) keep = false;  // a released block is never read (block_view.py:280-281)
+    keep = (keep || b == 0 || b == blocks - 1) && b < blocks && in_row;
+    const uint32_t bits = __ballot_sync(kFullMask, keep);
+    if (lane == 0) s_bits[warp][i] = bits;
+    kept_count += __popc(bits);
   }
+  int kept_total = 0;
+  const int kept_base = warp_bases(kept_count, s_w, &kept_total);  // (its barrier also ends every key read)
+
+  // ---- pass 2: kept ids first, then the others, both in position order, into shared memory -------
+  cp_async_wait<0>();
+  __syncthreads();  // the table row has landed
+  uint32_t* out = keys;
+  int kept = kept_base;
+  for (int i = 0; i < iters; ++i) {
+    const int b = wbase + 32 * i + lane;
+    const uint32_t bits = s_bits[warp][i];
+    const int before = kept + __popc(bits & lanes_below());
+    if (b < laid) {
+      const uint32_t id = static_cast<uint32_t>(trow_s[b]);
+      if ((bits >> lane) & 1u) out[before] = id; else out[kept_total + (b - before)] = id;
+    }
+    kept += __popc(bits);
+  }
+  __syncthreads();
+  int32_t* vrow = p.view + (int64_t)r * p.view_s0;
+  copy_words(vrow, reinterpret_cast<const int32_t*>(out), 0, laid);
+  copy_words(vrow, trow, laid, W);  // past the laid-out positions nothing is kept: the view is the table
   if (threadIdx.x == 0) {
     const int last = seq - (blocks - 1) * BS;
     p.view_lens[r] = blocks > 0 ? (kept_total - 1) * BS + last : 0;
@@ -329,16 +427,16 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
 }
 
 int launch_view(const ViewParams& p, cudaStream_t stream) {
-  const size_t smem = p.keep == nullptr ? (size_t)p.width * sizeof(uint32_t) : 0;
-  static bool configured[kMaxDevices] = {};
+  const size_t w_pad = (size_t)(p.width + kViewThreads - 1) / kViewThreads * kViewThreads;
+  const size_t smem = 2 * w_pad * sizeof(uint32_t);
+  static size_t configured[kMaxDevices] = {};
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
     return check_launch("cudaGetDevice");
-  if (!configured[device]) {
-    if (cudaFuncSetAttribute(view_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kViewMaxWidth * (int)sizeof(uint32_t)) != cudaSuccess)
+  if (configured[device] < smem) {
+    if (cudaFuncSetAttribute(view_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(view_kernel)");
-    configured[device] = true;
+    configured[device] = smem;
   }
   view_kernel<<<p.rows, kViewThreads, smem, stream>>>(p);
   return check_launch("view_kernel");
@@ -397,7 +495,7 @@ extern "C" int ekv_view_build(const int32_t* table, int64_t table_stride, const 
   if (!table || !seq_lens || !view || !view_lens) return fail(EKV_EINVAL, "a required pointer is NULL");
   if (rows <= 0 || width <= 0 || block_size <= 0)
     return fail(EKV_EINVAL, "rows, width and block_size must be positive");
-  if (width > kViewMaxWidth) return fail(EKV_ENOTSUP, "width %d > %d", width, kViewMaxWidth);
+  if (width > kViewMaxWidth) return fail(EKV_ENOTSUP, "width %d > %d (a view row is staged in shared memory)", width, kViewMaxWidth);
   if (rows > 2147483647) return fail(EKV_ENOTSUP, "too many rows");
   if (table_stride < width || view_stride < width) return fail(EKV_EINVAL, "a row stride is below the width");
   if (keep == nullptr) {

@@ -118,8 +118,8 @@ def test_other_entry_points_validate_before_launching(lib):
     view_args = [fake, 8, fake, fake, fake, None, 0, None, 8, L.POLICY_SUM, None, 0, None, None, 0, 2, 8, 16,
                  fake, 8, fake, None, 0, None]
     assert lib.ekv_view_build(*view_args) == L.EINVAL  # ranking by shares without scores
-    view_args[16] = 40000
-    assert lib.ekv_view_build(*view_args) == L.ENOTSUP  # wider than 32768
+    view_args[16] = 20000
+    assert lib.ekv_view_build(*view_args) == L.ENOTSUP  # wider than 16384
     assert lib.ekv_compact_block_table(fake, 8, fake, None, 8, 2, 8, 16, fake, 8, fake, None) == L.EINVAL
 
 

@@ -55,13 +55,14 @@ extern "C" {
 /* Human-readable description of the last error on this thread ("" if none). */
 const char* ekv_last_error_string(void);
 
-/* ABI version of this library: bumped on any signature change. */
+/* ABI version of this library: bumped on any change of a signature or of a documented contract. */
 int ekv_abi_version(void);
 
 /* Bytes of workspace the share pass of ekv_audit_launch / ekv_audit_step needs for a table of
- * `layers` layers: a ticket per row, contributors per (layer, row) and a share vector per
- * (layer, row). It must be zero before the first launch (every launch leaves the tickets zero
- * again) and 256-byte aligned. */
+ * `layers` layers: a ticket per row, contributors per (layer, row), a share vector per (layer, row)
+ * and, for ekv_audit_step, the key cache's TMA descriptor per layer (128 bytes each, rewritten by
+ * every step). It must be zero before the first launch (every launch leaves the tickets zero again)
+ * and 256-byte aligned. */
 size_t ekv_audit_workspace_bytes(int layers, int rows, int width);
 
 /*
@@ -87,8 +88,9 @@ size_t ekv_audit_workspace_bytes(int layers, int rows, int width);
  * mean or max over layers and query rows into share_out [rows][width] and contributors [rows]
  * (query rows with data); a row that is not selected or has no data is NaN.
  * status (optional) receives EKV_STATUS_* bits. q_tokens bounds qrow. Supported: head_dim 128,
+ * block_size a multiple of 8 (the key cache is read a block at a time through a TMA tensor map),
  * block_size*tile_blocks in {16, 32, 64}, tile_blocks <= 8, heads*group_rows <= 128,
- * group_rows <= 16, rows <= 2048.
+ * group_rows <= 16, rows <= 2048, pool_blocks < 2^31, key-cache strides in whole 16-byte units.
  */
 int ekv_audit_launch(const void* q, const void* k, const int32_t* table, const int32_t* lens,
                      const int32_t* qrow, const uint8_t* select, const uint32_t* flag, float* lse,
@@ -120,7 +122,9 @@ int ekv_audit_stash(const void* q, int64_t q_stride_token, int64_t q_stride_head
  * runtime/audit.py:86-100) and its queries, laid out as the engine's query (q_layout 0: query head
  * (KV head) * group_rows + g) or as a stash (q_layout 1: query head h * group_rows + g). The KV head
  * of layer L is (group + L) % kv_heads with rotate != 0 (the reference's sampling), else
- * group + h for h < heads. share_out, contributors and workspace are required.
+ * group + h for h < heads. The workspace is required: it holds each layer's key-cache descriptor
+ * (built on the device from k_layers by a small kernel ahead of the record kernel). share_out and
+ * contributors are optional: without them only the cells are recorded.
  */
 int ekv_audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table,
                    const int32_t* lens, const int32_t* qrow, const uint8_t* select,

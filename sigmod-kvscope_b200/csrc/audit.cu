@@ -4,12 +4,14 @@
 // Streaming. An item is one (layer, KV head, row, chunk of EKV_AUDIT_CHUNK_TILES tiles); the items of
 // a launch are numbered layer-major and every warp of a persistent grid (SMs x resident CTAs) works
 // through items worker, worker + workers, ... on its own, with a ring of STAGES shared-memory stages
-// of one tile each kept in flight across item boundaries. For each tile every lane asks the TMA
-// engine for one 2*D-byte key row (cp.async.bulk, L2 evict-first) and lane 0 arms the stage's
-// mbarrier with the byte count; rows land 2*D+16 bytes apart, so ldmatrix reads them without bank
-// conflicts. Nothing on a tile's critical path reads global memory: the rows' lengths and query
-// tokens sit in shared memory, the block ids of the next item and the query fragments of the next
-// item are prefetched into registers one item ahead.
+// of one tile each kept in flight across item boundaries. The key cache of a layer is a 4-D tensor
+// map (head dim, KV head, token of the block, block); for each block of a tile two lanes ask the TMA
+// engine for the block's 16 key rows of the audited head, one 64-dim half each (a 128-byte-swizzled
+// box, L2 evict-first), and lane 0 arms the stage's mbarrier with the byte count. Two copies per
+// block instead of one per key row keep the TMA issue cost off each warp's critical path; the swizzle
+// lets ldmatrix read the rows without bank conflicts. Nothing on a tile's critical path reads global
+// memory: the rows' lengths and query tokens sit in shared memory, the block ids of the next item and
+// the query fragments of the next item are prefetched into registers one item ahead.
 //
 // Scores. One m16n8k16 mma per (16 tokens, 16 dims): A = 16 key rows by ldmatrix, B = the G query
 // rows of the KV head (registers, padded to 8 or 16 columns), fp32 accumulation. Tokens sit on the
@@ -21,6 +23,9 @@
 // query row, and every block's share with the partial tail tile's weight given back to its blocks
 // (:82-103); the CTA that completes a row's last layer (a ticket) sums or maxes the layers in layer
 // order into the row's final share. Every sum has a fixed order, so the output is deterministic.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "ekv_common.cuh"
 
 namespace ekv {
@@ -41,6 +46,10 @@ constexpr int kChunkTiles = EKV_AUDIT_CHUNK_TILES;
 constexpr int kShareThreads = 128;
 
 struct AuditParams {
+  // the key cache of a single-layer launch as a tensor map (encoded on the host), or one map per
+  // layer in the workspace (written by kmap_kernel from k_layers)
+  CUtensorMap kmap0;
+  const CUtensorMap* kmaps;
   // per-layer sources: device arrays of addresses, or one address for a single layer
   const uint64_t* q_layers;
   const uint64_t* k_layers;
@@ -72,10 +81,13 @@ struct AuditParams {
   uint32_t* status;
 };
 
+// A stage holds a tile of TT key rows as two [TT][128 B] halves (dims 0-63, 64-127) in the TMA
+// engine's 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r % 8). Every box (one
+// block's rows of one half) starts on a 1024-byte boundary, so block_size must be a multiple of 8.
 template <int D>
 struct Layout {
-  static constexpr int kRowBytes = 2 * D;
-  static constexpr int kRowStride = 2 * D + 16;
+  static_assert(D == 128, "two 128-byte halves per key row");
+  static constexpr int kHalfRow = 128;
 };
 
 template <int TT>
@@ -85,6 +97,22 @@ struct Ring {
 
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Makes a tensor map written in global memory by an earlier kernel visible to this thread's copies.
+__device__ __forceinline__ void tensormap_acquire(const CUtensorMap* map) {
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(__cvta_generic_to_global(map))
+               : "memory");
+}
+
+// One tiled tensor copy global -> shared (4-D coordinates, innermost first), completing on `bar`.
+__device__ __forceinline__ void tensor_copy_g2s(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                                int c3, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
 }
 
 // Row r of the step: its length (tokens, clamped to the table), blocks, tiles and chunks; no chunks
@@ -127,19 +155,20 @@ struct Cursor {
 };
 
 template <int TT, int NT, int D, typename T>
-__global__ void __launch_bounds__(kWarps * 32) record_kernel(const AuditParams p) {
+__global__ void __launch_bounds__(kWarps * 32) record_kernel(const __grid_constant__ AuditParams p) {
   using Lay = Layout<D>;
   constexpr int STAGES = Ring<TT>::kStages;
-  constexpr int STAGE = TT * Lay::kRowStride;
+  constexpr int HALF = TT * Lay::kHalfRow;  // one half of a stage
+  constexpr int STAGE = 2 * HALF;
   constexpr int MT = TT / 16;
   constexpr int KS = D / 16;
-  constexpr int WORDS = (TT + 31) / 32;
 
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // swizzled boxes: 1024-aligned
   uint8_t* rings = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * STAGES * STAGE);
-  uint32_t* vmasks = reinterpret_cast<uint32_t*>(bars + kWarps * STAGES);  // [warp][stage][WORDS]
-  int* prefix = reinterpret_cast<int*>(vmasks + kWarps * STAGES * WORDS);  // [rows + 1]
+  uint32_t* vmasks = reinterpret_cast<uint32_t*>(bars + kWarps * STAGES);  // [warp][stage]: copied blocks
+  int* prefix = reinterpret_cast<int*>(vmasks + kWarps * STAGES);          // [rows + 1]
   int* s_blocks = prefix + p.rows + 1;                                     // [rows]
   int* s_len = s_blocks + p.rows;                                          // [rows]
   int* s_tok = s_len + p.rows;                                             // [rows]
@@ -226,7 +255,9 @@ __global__ void __launch_bounds__(kWarps * 32) record_kernel(const AuditParams p
 
   uint8_t* my_ring = rings + warp * STAGES * STAGE;
   uint64_t* my_bars = bars + warp * STAGES;
-  uint32_t* my_masks = vmasks + warp * STAGES * WORDS;
+  uint32_t* my_masks = vmasks + warp * STAGES;
+  const int bs_shift = __ffs(p.block_size) - 1;  // block_size is a power of two
+  int fenced_layer = -1;                         // the layer whose tensor map this warp has acquired
   if (lane == 0) {
     for (int s = 0; s < STAGES; ++s) mbar_init(&my_bars[s], 1);
     fence_mbar_init();
@@ -242,48 +273,50 @@ __global__ void __launch_bounds__(kWarps * 32) record_kernel(const AuditParams p
   decode(worker + workers, in_next);
   load_ids(in_next, nids_lo, nids_hi);
 
-  // Issue the bulk copies of the tile at `in` into stage s, then step `in` forward.
+  // Issue the tensor copies of the tile at `in` into stage s, then step `in` forward: lanes 2j and
+  // 2j + 1 copy the two halves of block j of the tile.
   auto issue_and_advance = [&](int s) {
-    const T* kbase = static_cast<const T*>(p.k_layers ? reinterpret_cast<const void*>(p.k_layers[in.layer]) : p.k);
-    const bool aligned = (reinterpret_cast<uintptr_t>(kbase) & 15) == 0;
-    kbase += (int64_t)kv_head_of(p, in.layer, in.head) * p.k_s2;
+    const CUtensorMap* map = &p.kmap0;
+    bool aligned = true;
+    if (p.kmaps != nullptr) {
+      map = p.kmaps + in.layer;
+      aligned = (p.k_layers[in.layer] & 15) == 0;
+      if (in.layer != fenced_layer) {
+        tensormap_acquire(map);
+        fenced_layer = in.layer;
+      }
+    }
+    const int TB = p.tile_blocks;
     const int n_blocks = s_blocks[in.row];
     const int tl = in.t - in.t0;
-    uint32_t total = 0;
-    int64_t off[WORDS];
-    uint32_t mask[WORDS];
-#pragma unroll
-    for (int w = 0; w < WORDS; ++w) {
-      const int tok = lane + 32 * w;
-      const int bi = tl * p.tile_blocks + (tok < TT ? tok : 0) / p.block_size;  // block of the item
-      const int32_t lo_id = __shfl_sync(kFullMask, ids_lo, bi & 31);
-      const int32_t hi_id = __shfl_sync(kFullMask, ids_hi, bi & 31);
-      const int32_t id = bi < 32 ? lo_id : hi_id;
-      bool ok = false;
-      off[w] = 0;
-      if (tok < TT && in.t * p.tile_blocks + tok / p.block_size < n_blocks) {
-        ok = aligned && id >= 0 && (int64_t)id < p.pool_blocks;
-        if (!ok && tok % p.block_size == 0) set_status(p.status, EKV_STATUS_BAD_BLOCK_ID);
-        off[w] = (int64_t)id * p.k_s0 + (int64_t)(tok % p.block_size) * p.k_s1;
-      }
-      mask[w] = __ballot_sync(kFullMask, ok);
-      total += __popc(mask[w]);
+    const int jb = (lane >> 1) < TB ? (lane >> 1) : 0;  // this lane's block of the tile
+    const int bi = tl * TB + jb;                        // ... of the item
+    const int32_t lo_id = __shfl_sync(kFullMask, ids_lo, bi & 31);
+    const int32_t hi_id = __shfl_sync(kFullMask, ids_hi, bi & 31);
+    const int32_t id = bi < 32 ? lo_id : hi_id;
+    bool ok = false;
+    if (lane < 2 * TB && in.t * TB + jb < n_blocks) {
+      ok = aligned && id >= 0 && (int64_t)id < p.pool_blocks;
+      if (!ok && (lane & 1) == 0) set_status(p.status, EKV_STATUS_BAD_BLOCK_ID);
     }
-    if (lane == 0) {
+    const uint32_t pairs = __ballot_sync(kFullMask, ok);
+    uint32_t bmask = 0;  // bit j: block j of the tile is copied
 #pragma unroll
-      for (int w = 0; w < WORDS; ++w) my_masks[s * WORDS + w] = mask[w];
-      if (total) {
-        mbar_arrive_expect_tx(&my_bars[s], total * Lay::kRowBytes);
+    for (int j = 0; j < TT / 8; ++j) bmask |= ((pairs >> (2 * j)) & 1u) << j;
+    if (lane == 0) {
+      my_masks[s] = bmask;
+      if (bmask) {
+        mbar_arrive_expect_tx(&my_bars[s], (uint32_t)__popc(bmask) * (uint32_t)p.block_size * 2u * Lay::kHalfRow);
       } else {
         mbar_arrive(&my_bars[s]);
       }
     }
     __syncwarp();
-    uint8_t* stage = my_ring + s * STAGE;
-#pragma unroll
-    for (int w = 0; w < WORDS; ++w)
-      if ((mask[w] >> lane) & 1u)
-        bulk_copy_g2s(stage + (lane + 32 * w) * Lay::kRowStride, kbase + off[w], Lay::kRowBytes, &my_bars[s], policy);
+    if (ok) {
+      const int half = lane & 1;
+      uint8_t* dst = my_ring + s * STAGE + half * HALF + (jb << bs_shift) * Lay::kHalfRow;
+      tensor_copy_g2s(dst, map, 64 * half, kv_head_of(p, in.layer, in.head), 0, id, &my_bars[s], policy);
+    }
     if (++in.t >= in.t_end) {  // the next item: its ids were prefetched; prefetch the one after
       in = in_next;
       ids_lo = nids_lo;
@@ -333,21 +366,21 @@ __global__ void __launch_bounds__(kWarps * 32) record_kernel(const AuditParams p
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
           for (int e = 0; e < 4; ++e) c[mt][nt][e] = 0.f;
-      const uint32_t a_base =
-          smem_u32(stage) + ((lane & 7) + ((lane >> 3) & 1) * 8) * Lay::kRowStride + (lane >> 4) * 16;
+      // lane l reads row (l % 8) + 8 * ((l / 8) % 2) of the m-tile, 16-byte chunk 2k + l / 16 of the
+      // row: in the swizzled half k / 4 that chunk sits at ((2k) % 8) ^ (l / 16) ^ (l % 8)
+      const uint32_t a_base = smem_u32(stage) + ((lane & 7) + ((lane >> 3) & 1) * 8) * Lay::kHalfRow;
+      const uint32_t swz = (uint32_t)((lane >> 4) ^ (lane & 7));
 #pragma unroll
       for (int k = 0; k < KS; ++k) {
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           uint32_t a[4];
-          ldmatrix_x4(a, a_base + mt * 16 * Lay::kRowStride + k * 32);
+          ldmatrix_x4(a, a_base + (k >> 2) * HALF + mt * 16 * Lay::kHalfRow + ((((2 * k) & 7) ^ swz) << 4));
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) Mma<T>::run(c[mt][nt], a, bq[nt][k]);
         }
       }
-      uint32_t vm[WORDS];
-#pragma unroll
-      for (int w = 0; w < WORDS; ++w) vm[w] = my_masks[s * WORDS + w];
+      const uint32_t vm = my_masks[s];
       const int first = out.t * TT;
       const int len = s_len[out.row];
       float mx[NT][2];
@@ -357,8 +390,8 @@ __global__ void __launch_bounds__(kWarps * 32) record_kernel(const AuditParams p
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int tok = mt * 16 + (lane >> 2) + 8 * h;  // bit tok % 32 of word tok / 32 = mt / 2
-          const bool ok = first + tok < len && ((vm[mt >> 1] >> (tok & 31)) & 1u);
+          const int tok = mt * 16 + (lane >> 2) + 8 * h;
+          const bool ok = first + tok < len && ((vm >> (tok >> bs_shift)) & 1u);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -582,14 +615,32 @@ __global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams 
   }
 }
 
+// One tensor map per layer of a step: the host-encoded template with the layer's key-cache address
+// (a misaligned address is left out; the record kernel skips that layer's copies and reports them).
+__global__ void __launch_bounds__(128) kmap_kernel(const __grid_constant__ CUtensorMap tmpl, const uint64_t* k_layers,
+                                                   int layer0, int n_layers, CUtensorMap* maps) {
+  for (int i = threadIdx.x; i < n_layers; i += blockDim.x) {
+    CUtensorMap* map = maps + layer0 + i;
+    const uint64_t* src = reinterpret_cast<const uint64_t*>(&tmpl);
+    uint64_t* dst = reinterpret_cast<uint64_t*>(map);
+#pragma unroll
+    for (int w = 0; w < 16; ++w) dst[w] = src[w];
+    const uint64_t k = k_layers[layer0 + i];
+    if ((k & 15) == 0)
+      asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;" ::"l"(
+                       __cvta_generic_to_global(map)), "l"(k)
+                   : "memory");
+  }
+  asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
+}
+
 // The record kernel over p.layer0 .. p.layer0 + p.n_layers, then (finalize) the share kernel over the
 // layers [share0, share0 + share_layers): every layer of the step, so the table's current cells decide.
 template <int TT, int NT, int D, typename T>
 int launch_audit(const AuditParams& p, bool finalize, int share0, int share_layers, cudaStream_t stream) {
   using Lay = Layout<D>;
   constexpr int STAGES = Ring<TT>::kStages;
-  constexpr int WORDS = (TT + 31) / 32;
-  constexpr size_t fixed = (size_t)kWarps * STAGES * TT * Lay::kRowStride + kWarps * STAGES * (8 + WORDS * 4);
+  constexpr size_t fixed = 1024 + (size_t)kWarps * STAGES * TT * 2 * Lay::kHalfRow + kWarps * STAGES * (8 + 4);
   const size_t smem = fixed + (size_t)(4 * p.rows + 1) * 4;
   static int grid_of[kMaxDevices] = {};
   static size_t smem_of[kMaxDevices] = {};
@@ -611,6 +662,11 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
       return check_launch("cudaOccupancyMaxActiveBlocksPerMultiprocessor");
     grid_of[device] = sms * (per_sm > 0 ? per_sm : 1);
     smem_of[device] = smem;
+  }
+  if (p.kmaps != nullptr) {
+    kmap_kernel<<<1, 128, 0, stream>>>(p.kmap0, p.k_layers, p.layer0, p.n_layers, const_cast<CUtensorMap*>(p.kmaps));
+    const int rc = check_launch("kmap_kernel");
+    if (rc != EKV_OK) return rc;
   }
   kernel<<<grid_of[device], kWarps * 32, smem, stream>>>(p);
   int rc = check_launch("record_kernel");
@@ -638,7 +694,7 @@ int dispatch(const AuditParams& p, int tt, bool finalize, int share0, int share_
 }
 
 struct WorkspaceLayout {
-  size_t row_tickets, contrib, share, total;
+  size_t row_tickets, contrib, share, kmaps, total;
 };
 
 WorkspaceLayout workspace_layout(int layers, int rows, int width) {
@@ -646,8 +702,40 @@ WorkspaceLayout workspace_layout(int layers, int rows, int width) {
   w.row_tickets = 0;
   w.contrib = round_up((size_t)rows * 4, 256);
   w.share = w.contrib + round_up((size_t)layers * rows * 4, 256);
-  w.total = w.share + round_up((size_t)layers * rows * width * 4, 256);
+  w.kmaps = w.share + round_up((size_t)layers * rows * width * 4, 256);
+  w.total = w.kmaps + round_up((size_t)layers * sizeof(CUtensorMap), 256);
   return w;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+// The key cache at `k` as a 4-D tensor (head dim, KV head, token of the block, block) with boxes of
+// 64 dims x 1 head x one block's tokens in the 128-byte swizzle.
+int encode_key_map(CUtensorMap* map, const void* k, const AuditParams& p, int dtype) {
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (encode == nullptr) return fail(EKV_ECUDA, "the driver does not provide cuTensorMapEncodeTiled");
+  const cuuint64_t dims[4] = {128, (cuuint64_t)p.kv_heads, (cuuint64_t)p.block_size, (cuuint64_t)p.pool_blocks};
+  const cuuint64_t strides[3] = {(cuuint64_t)p.k_s2 * 2, (cuuint64_t)p.k_s1 * 2, (cuuint64_t)p.k_s0 * 2};
+  const cuuint32_t box[4] = {64, 1, (cuuint32_t)p.block_size, 1};
+  const cuuint32_t unit[4] = {1, 1, 1, 1};
+  const CUresult r = encode(map, dtype == EKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                            4, const_cast<void*>(k), dims, strides, box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(EKV_ENOTSUP, "the key cache (strides %lld, %lld, %lld elements) has no tensor map (CUresult %d)",
+                (long long)p.k_s0, (long long)p.k_s1, (long long)p.k_s2, (int)r);
+  return EKV_OK;
 }
 
 // Checks shared by both entry points; fills the common fields of p.
@@ -657,7 +745,7 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
             int rows, int width, int group_rows, int block_size, int tile_blocks, int head_dim,
             int dtype, int heads, int kv_heads, int64_t pool_blocks, int64_t q_tokens,
             float* share_out, int32_t* contributors, int aggregate, void* workspace,
-            size_t workspace_bytes, uint32_t* status) {
+            size_t workspace_bytes, uint32_t* status, bool need_workspace) {
   if (!table || !lens || !qrow || !select || !flag || !lse)
     return fail(EKV_EINVAL, "a required device pointer is NULL");
   if (rows <= 0 || width <= 0 || layers <= 0) return fail(EKV_EINVAL, "rows, width and layers must be positive");
@@ -671,6 +759,9 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
   const int tt = block_size * tile_blocks;
   if (tt & (tt - 1)) return fail(EKV_EINVAL, "a tile of the audit kernel must hold a power of two of tokens");
   if (tile_blocks > 8) return fail(EKV_ENOTSUP, "tile_blocks %d: this build handles up to 8", tile_blocks);
+  if (block_size & 7)
+    return fail(EKV_ENOTSUP, "block_size %d: the kernel copies whole blocks of a multiple of 8 tokens", block_size);
+  if (pool_blocks > 0x7fffffffll) return fail(EKV_ENOTSUP, "%lld blocks in the pool exceed 2^31 - 1", (long long)pool_blocks);
   if (head_dim != 128) return fail(EKV_ENOTSUP, "head_dim %d: this build has kernels for 128", head_dim);
   if (dtype != EKV_DTYPE_F16 && dtype != EKV_DTYPE_BF16) return fail(EKV_EINVAL, "unknown dtype %d", dtype);
   if (pool_blocks <= 0 || q_tokens <= 0) return fail(EKV_EINVAL, "pool_blocks and q_tokens must be positive");
@@ -685,8 +776,8 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
   p.heads = heads; p.Q = heads * group_rows; p.block_size = block_size; p.tile_blocks = tile_blocks;
   p.kv_heads = kv_heads; p.pool_blocks = pool_blocks; p.q_tokens = q_tokens; p.status = status;
   p.share_out = share_out; p.contrib_out = contributors; p.aggregate = aggregate;
-  if (share_out) {
-    if (!contributors) return fail(EKV_EINVAL, "share_out needs contributors");
+  if (share_out && !contributors) return fail(EKV_EINVAL, "share_out needs contributors");
+  if (share_out || need_workspace) {
     const WorkspaceLayout w = workspace_layout(layers, rows, width);
     if (!workspace || workspace_bytes < w.total)
       return fail(EKV_ERANGE, "the audit workspace holds %zu bytes, the launch needs %zu", workspace_bytes, w.total);
@@ -695,6 +786,7 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
     p.row_tickets = reinterpret_cast<uint32_t*>(base + w.row_tickets);
     p.contrib_layer = reinterpret_cast<int32_t*>(base + w.contrib);
     p.share_layer = reinterpret_cast<float*>(base + w.share);
+    p.kmaps = need_workspace ? reinterpret_cast<const CUtensorMap*>(base + w.kmaps) : nullptr;
   }
   return EKV_OK;
 }
@@ -766,7 +858,7 @@ extern "C" int ekv_audit_launch(
                          k_stride_block, k_stride_pos, k_stride_head, table_stride, layers, rows, width,
                          group_rows, block_size, tile_blocks, head_dim, dtype, heads, kv_heads,
                          pool_blocks, q_tokens, share_out, contributors, aggregate, workspace,
-                         workspace_bytes, status);
+                         workspace_bytes, status, false);
   if (rc != EKV_OK) return rc;
   if (layer < 0 || layer >= layers)
     return fail(EKV_ERANGE, "layer %d is outside the %d layers the table was sized for", layer, layers);
@@ -775,6 +867,8 @@ extern "C" int ekv_audit_launch(
   if (((uintptr_t)k & 15) || ((uintptr_t)q & 3))
     return fail(EKV_EINVAL, "the key cache must be 16-byte aligned and the query 4-byte aligned");
   p.q = q; p.k = k; p.layer0 = layer; p.n_layers = 1; p.group = group; p.rotate = 0;
+  const int enc = encode_key_map(&p.kmap0, k, p, dtype);
+  if (enc != EKV_OK) return enc;
   const bool finalize = (share_flags & EKV_SHARE_FINALIZE) != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int tt = block_size * tile_blocks;
@@ -798,7 +892,7 @@ extern "C" int ekv_audit_step(
                          k_stride_block, k_stride_pos, k_stride_head, table_stride, layers, rows, width,
                          group_rows, block_size, tile_blocks, head_dim, dtype, heads, kv_heads,
                          pool_blocks, q_tokens, share_out, contributors, aggregate, workspace,
-                         workspace_bytes, status);
+                         workspace_bytes, status, true);
   if (rc != EKV_OK) return rc;
   if (n_layers <= 0 || layer0 < 0 || layer0 + n_layers > layers)
     return fail(EKV_ERANGE, "layers [%d, %d) are outside the %d the table was sized for", layer0,
@@ -808,6 +902,9 @@ extern "C" int ekv_audit_step(
                 rotate, heads, kv_heads);
   p.q_layers = q_layers; p.k_layers = k_layers; p.layer0 = layer0; p.n_layers = n_layers;
   p.group = group; p.rotate = rotate != 0; p.q_stash = q_layout != 0;
+  // the template of the per-layer maps: any aligned device address stands in for the layers' caches
+  const int enc = encode_key_map(&p.kmap0, workspace, p, dtype);
+  if (enc != EKV_OK) return enc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int tt = block_size * tile_blocks;
   return dtype == EKV_DTYPE_BF16 ? dispatch<__nv_bfloat16>(p, tt, true, layer0, n_layers, s)

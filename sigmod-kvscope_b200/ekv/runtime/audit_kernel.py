@@ -335,7 +335,7 @@ class RecordingPlane(AuditPlane):
             table.stride(0), self._layers, self.rows, self.width, self.group_rows, self.block_size, TILE_BLOCKS, dim,
             _DTYPES[q0.dtype], self.heads, kv_heads, k0.shape[0], q0.shape[0],
             self._share.data_ptr() if shares else None, self._contributors.data_ptr() if shares else None,
-            _AGGREGATES[self.aggregate], workspace if shares else None, self._workspace_bytes if shares else 0,
+            _AGGREGATES[self.aggregate], workspace, self._workspace_bytes,
             self._status.data_ptr(), _lib.current_stream() if stream is None else stream,
         )
         _lib.check(rc, "ekv_audit_step")

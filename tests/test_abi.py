@@ -48,13 +48,14 @@ def test_constants_agree_with_the_header():
 
 
 def test_workspace_size(lib):
-    # row tickets [rows] + contributors [layers][rows] + shares [layers][rows][width]
+    # row tickets [rows] + contributors [layers][rows] + shares [layers][rows][width] + a 128-byte
+    # key-cache descriptor per layer
     layers, rows, width = 32, 64, 512
 
     def up(x):
         return -(-x // 256) * 256
 
-    want = up(rows * 4) + up(layers * rows * 4) + up(layers * rows * width * 4)
+    want = up(rows * 4) + up(layers * rows * 4) + up(layers * rows * width * 4) + up(layers * 128)
     assert lib.ekv_audit_workspace_bytes(layers, rows, width) == want
     assert lib.ekv_audit_workspace_bytes(0, rows, width) == 0
 
@@ -139,4 +140,4 @@ def test_step_and_stash_validate_before_launching(lib):
 
 
 def test_abi_version(lib):
-    assert lib.ekv_abi_version() == 2
+    assert lib.ekv_abi_version() == 3

@@ -60,9 +60,9 @@ int ekv_abi_version(void);
 
 /* Bytes of workspace the share pass of ekv_audit_launch / ekv_audit_step needs for a table of
  * `layers` layers: a ticket per row, contributors per (layer, row), a share vector per (layer, row)
- * and, for ekv_audit_step, the key cache's TMA descriptor per layer (128 bytes each, rewritten by
- * every step). It must be zero before the first launch (every launch leaves the tickets zero again)
- * and 256-byte aligned. */
+ * and, for ekv_audit_step, a work counter and the key cache's TMA descriptor per layer (128 bytes
+ * each), both rewritten by every step. It must be zero before the first launch (every launch leaves
+ * the tickets zero again) and 256-byte aligned. */
 size_t ekv_audit_workspace_bytes(int layers, int rows, int width);
 
 /*

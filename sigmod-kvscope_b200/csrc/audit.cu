@@ -44,6 +44,8 @@ constexpr int kMaxRows = 2048;
 constexpr int kMaxLayers = 1024;
 constexpr int kChunkTiles = EKV_AUDIT_CHUNK_TILES;
 constexpr int kShareThreads = 128;
+constexpr int kMinCtas = 12 / kWarps > 0 ? 12 / kWarps : 1;  // registers for 12 warps per SM
+constexpr int kItemQueue = 16;  // items a warp has taken but not yet consumed (at most STAGES + 2)
 
 struct AuditParams {
   // the key cache of a single-layer launch as a tensor map (encoded on the host), or one map per
@@ -76,6 +78,7 @@ struct AuditParams {
   int32_t* contrib_out;
   int aggregate;
   uint32_t* row_tickets;    // [rows]
+  uint32_t* item_counter;   // items handed out beyond each warp's first (zeroed by kmap_kernel); NULL: static order
   int32_t* contrib_layer;   // [layers][rows]
   float* share_layer;       // [layers][rows][width]
   uint32_t* status;
@@ -155,13 +158,15 @@ struct Cursor {
 };
 
 template <int TT, int NT, int D, typename T>
-__global__ void __launch_bounds__(kWarps * 32) record_kernel(const __grid_constant__ AuditParams p) {
+__global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __grid_constant__ AuditParams p) {
   using Lay = Layout<D>;
   constexpr int STAGES = Ring<TT>::kStages;
   constexpr int HALF = TT * Lay::kHalfRow;  // one half of a stage
   constexpr int STAGE = 2 * HALF;
   constexpr int MT = TT / 16;
   constexpr int KS = D / 16;
+  // hold a whole tile's A fragments in registers (MT * KS * 4 of them) when that keeps 3 CTAs per SM
+  constexpr bool kEarlyRelease = MT * NT <= 2;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // swizzled boxes: 1024-aligned
@@ -173,6 +178,7 @@ __global__ void __launch_bounds__(kWarps * 32) record_kernel(const __grid_consta
   int* s_len = s_blocks + p.rows;                                          // [rows]
   int* s_tok = s_len + p.rows;                                             // [rows]
   __shared__ int s_scan[kWarps + 1];
+  __shared__ long long s_queue[kWarps][kItemQueue];  // each warp's items in the order it took them
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (*p.flag == 0) return;  // the statistic is off: nothing is recorded (:64)
@@ -201,7 +207,36 @@ __global__ void __launch_bounds__(kWarps * 32) record_kernel(const __grid_consta
   const long long total_items = (long long)chunks_per_lh * p.heads * p.n_layers;
   const long long workers = (long long)gridDim.x * kWarps;
   const long long worker = (long long)blockIdx.x * kWarps + warp;
+  uint32_t* const ctr = p.item_counter;
   if (worker >= total_items) return;
+
+  // Items: a warp's first is its own index; after that it takes the next free one from the counter
+  // (SMs do not stream at the same rate: with a static share the fast ones sit idle for the last
+  // third of a step), or with no counter every workers-th. The issue side takes them; the consume
+  // side follows the same sequence through s_queue.
+  long long n_taken = 0;
+  bool drained = false;
+  auto take = [&]() -> long long {
+    long long item = total_items;
+    if (!drained) {
+      if (n_taken == 0) {
+        item = worker;
+      } else if (ctr != nullptr) {
+        uint32_t v = 0;
+        if (lane == 0) v = atomicAdd(ctr, 1u);
+        item = workers + (long long)__shfl_sync(kFullMask, v, 0);
+      } else {
+        item = worker + n_taken * workers;
+      }
+      if (item >= total_items) {
+        item = total_items;
+        drained = true;
+      }
+    }
+    if (lane == 0) s_queue[warp][n_taken % kItemQueue] = item;
+    ++n_taken;
+    return item;
+  };
 
   auto decode = [&](long long item, Cursor& c) {
     c.item = item;
@@ -268,9 +303,9 @@ __global__ void __launch_bounds__(kWarps * 32) record_kernel(const __grid_consta
   // the issue side: cursor `in`, the ids of its item and of the item after it
   Cursor in{}, in_next{};
   int32_t ids_lo, ids_hi, nids_lo, nids_hi;
-  decode(worker, in);
+  decode(take(), in);
   load_ids(in, ids_lo, ids_hi);
-  decode(worker + workers, in_next);
+  decode(take(), in_next);
   load_ids(in_next, nids_lo, nids_hi);
 
   // Issue the tensor copies of the tile at `in` into stage s, then step `in` forward: lanes 2j and
@@ -321,7 +356,7 @@ __global__ void __launch_bounds__(kWarps * 32) record_kernel(const __grid_consta
       in = in_next;
       ids_lo = nids_lo;
       ids_hi = nids_hi;
-      decode(in.item + workers, in_next);
+      decode(take(), in_next);
       load_ids(in_next, nids_lo, nids_hi);
     }
   };
@@ -334,7 +369,9 @@ __global__ void __launch_bounds__(kWarps * 32) record_kernel(const __grid_consta
 
   // the consume side: cursor `out`, the query fragments of its item and of the next one
   Cursor out{};
-  decode(worker, out);
+  long long n_used = 0;  // the consume side's position in s_queue
+  __syncwarp();
+  decode(s_queue[warp][0], out);
   uint32_t bq[NT][KS][2], bqn[NT][KS][2];
   load_q(out, bqn);
   const size_t plane = (size_t)p.layers * p.rows * p.width * p.Q;
@@ -350,13 +387,15 @@ __global__ void __launch_bounds__(kWarps * 32) record_kernel(const __grid_consta
 #pragma unroll
         for (int k = 0; k < KS; ++k) bq[nt][k][0] = bqn[nt][k][0], bq[nt][k][1] = bqn[nt][k][1];
       Cursor nxt{};
-      decode(out.item + workers, nxt);
+      __syncwarp();
+      decode(s_queue[warp][(n_used + 1) % kItemQueue], nxt);
       load_q(nxt, bqn);
     }
     if (!timed_out && !mbar_wait_bounded(&my_bars[s], parity, p.status)) {
       timed_out = true;
       unwaited = consumed;
     }
+    bool released = false;
     if (!timed_out) {
       const uint8_t* stage = my_ring + s * STAGE;
       float c[MT][NT][4];
@@ -370,17 +409,42 @@ __global__ void __launch_bounds__(kWarps * 32) record_kernel(const __grid_consta
       // row: in the swizzled half k / 4 that chunk sits at ((2k) % 8) ^ (l / 16) ^ (l % 8)
       const uint32_t a_base = smem_u32(stage) + ((lane & 7) + ((lane >> 3) & 1) * 8) * Lay::kHalfRow;
       const uint32_t swz = (uint32_t)((lane >> 4) ^ (lane & 7));
+      const uint32_t vm = my_masks[s];
+      if constexpr (kEarlyRelease) {
+        // the whole tile into registers, the stage back to the TMA engine, then the math: both of the
+        // warp's stages stay in flight while it computes
+        uint32_t a[MT][KS][4];
 #pragma unroll
-      for (int k = 0; k < KS; ++k) {
+        for (int k = 0; k < KS; ++k)
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          uint32_t a[4];
-          ldmatrix_x4(a, a_base + (k >> 2) * HALF + mt * 16 * Lay::kHalfRow + ((((2 * k) & 7) ^ swz) << 4));
+          for (int mt = 0; mt < MT; ++mt)
+            ldmatrix_x4(a[mt][k], a_base + (k >> 2) * HALF + mt * 16 * Lay::kHalfRow + ((((2 * k) & 7) ^ swz) << 4));
+        __syncwarp();
+        fence_proxy_async();
+        ++consumed;
+        if (in.item < total_items) {
+          issue_and_advance((int)(issued % STAGES));
+          ++issued;
+        }
+        released = true;
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) Mma<T>::run(c[mt][nt], a, bq[nt][k]);
+        for (int k = 0; k < KS; ++k)
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) Mma<T>::run(c[mt][nt], a[mt][k], bq[nt][k]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < KS; ++k) {
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            uint32_t a[4];
+            ldmatrix_x4(a, a_base + (k >> 2) * HALF + mt * 16 * Lay::kHalfRow + ((((2 * k) & 7) ^ swz) << 4));
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) Mma<T>::run(c[mt][nt], a, bq[nt][k]);
+          }
         }
       }
-      const uint32_t vm = my_masks[s];
       const int first = out.t * TT;
       const int len = s_len[out.row];
       float mx[NT][2];
@@ -442,15 +506,20 @@ __global__ void __launch_bounds__(kWarps * 32) record_kernel(const __grid_consta
           }
       }
     }
-    // the stage is consumed: refill it with the tile STAGES ahead
-    __syncwarp();
-    fence_proxy_async();
-    ++consumed;
-    if (in.item < total_items && !timed_out) {
-      issue_and_advance((int)(issued % STAGES));
-      ++issued;
+    if (!released) {  // the stage is consumed: refill it with the tile STAGES ahead
+      __syncwarp();
+      fence_proxy_async();
+      ++consumed;
+      if (in.item < total_items && !timed_out) {
+        issue_and_advance((int)(issued % STAGES));
+        ++issued;
+      }
     }
-    if (++out.t >= out.t_end) decode(out.item + workers, out);
+    if (++out.t >= out.t_end) {
+      ++n_used;
+      __syncwarp();
+      decode(s_queue[warp][n_used % kItemQueue], out);
+    }
   }
   if (timed_out) {
     // let copies still in flight land before the shared memory is released
@@ -618,7 +687,8 @@ __global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams 
 // One tensor map per layer of a step: the host-encoded template with the layer's key-cache address
 // (a misaligned address is left out; the record kernel skips that layer's copies and reports them).
 __global__ void __launch_bounds__(128) kmap_kernel(const __grid_constant__ CUtensorMap tmpl, const uint64_t* k_layers,
-                                                   int layer0, int n_layers, CUtensorMap* maps) {
+                                                   int layer0, int n_layers, CUtensorMap* maps, uint32_t* item_counter) {
+  if (threadIdx.x == 0) *item_counter = 0u;  // the record kernel's dynamic items start again
   for (int i = threadIdx.x; i < n_layers; i += blockDim.x) {
     CUtensorMap* map = maps + layer0 + i;
     const uint64_t* src = reinterpret_cast<const uint64_t*>(&tmpl);
@@ -664,7 +734,8 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
     smem_of[device] = smem;
   }
   if (p.kmaps != nullptr) {
-    kmap_kernel<<<1, 128, 0, stream>>>(p.kmap0, p.k_layers, p.layer0, p.n_layers, const_cast<CUtensorMap*>(p.kmaps));
+    kmap_kernel<<<1, 128, 0, stream>>>(p.kmap0, p.k_layers, p.layer0, p.n_layers, const_cast<CUtensorMap*>(p.kmaps),
+                                       p.item_counter);
     const int rc = check_launch("kmap_kernel");
     if (rc != EKV_OK) return rc;
   }
@@ -694,13 +765,14 @@ int dispatch(const AuditParams& p, int tt, bool finalize, int share0, int share_
 }
 
 struct WorkspaceLayout {
-  size_t row_tickets, contrib, share, kmaps, total;
+  size_t row_tickets, counters, contrib, share, kmaps, total;
 };
 
 WorkspaceLayout workspace_layout(int layers, int rows, int width) {
   WorkspaceLayout w{};
   w.row_tickets = 0;
-  w.contrib = round_up((size_t)rows * 4, 256);
+  w.counters = round_up((size_t)rows * 4, 256);
+  w.contrib = w.counters + 256;
   w.share = w.contrib + round_up((size_t)layers * rows * 4, 256);
   w.kmaps = w.share + round_up((size_t)layers * rows * width * 4, 256);
   w.total = w.kmaps + round_up((size_t)layers * sizeof(CUtensorMap), 256);
@@ -762,6 +834,8 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
   if (block_size & 7)
     return fail(EKV_ENOTSUP, "block_size %d: the kernel copies whole blocks of a multiple of 8 tokens", block_size);
   if (pool_blocks > 0x7fffffffll) return fail(EKV_ENOTSUP, "%lld blocks in the pool exceed 2^31 - 1", (long long)pool_blocks);
+  if ((long long)rows * cdiv(width, tile_blocks * EKV_AUDIT_CHUNK_TILES) * heads * layers > 0x7fffffffll)
+    return fail(EKV_ENOTSUP, "a launch of more than 2^31 - 1 work items (rows x chunks x heads x layers)");
   if (head_dim != 128) return fail(EKV_ENOTSUP, "head_dim %d: this build has kernels for 128", head_dim);
   if (dtype != EKV_DTYPE_F16 && dtype != EKV_DTYPE_BF16) return fail(EKV_EINVAL, "unknown dtype %d", dtype);
   if (pool_blocks <= 0 || q_tokens <= 0) return fail(EKV_EINVAL, "pool_blocks and q_tokens must be positive");
@@ -784,6 +858,7 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
     if ((uintptr_t)workspace & 255) return fail(EKV_EINVAL, "the audit workspace must be 256-byte aligned");
     uint8_t* base = static_cast<uint8_t*>(workspace);
     p.row_tickets = reinterpret_cast<uint32_t*>(base + w.row_tickets);
+    p.item_counter = need_workspace ? reinterpret_cast<uint32_t*>(base + w.counters) : nullptr;
     p.contrib_layer = reinterpret_cast<int32_t*>(base + w.contrib);
     p.share_layer = reinterpret_cast<float*>(base + w.share);
     p.kmaps = need_workspace ? reinterpret_cast<const CUtensorMap*>(base + w.kmaps) : nullptr;

@@ -48,14 +48,14 @@ def test_constants_agree_with_the_header():
 
 
 def test_workspace_size(lib):
-    # row tickets [rows] + contributors [layers][rows] + shares [layers][rows][width] + a 128-byte
-    # key-cache descriptor per layer
+    # row tickets [rows] + the step's item counter + contributors [layers][rows] + shares
+    # [layers][rows][width] + a 128-byte key-cache descriptor per layer
     layers, rows, width = 32, 64, 512
 
     def up(x):
         return -(-x // 256) * 256
 
-    want = up(rows * 4) + up(layers * rows * 4) + up(layers * rows * width * 4) + up(layers * 128)
+    want = up(rows * 4) + 256 + up(layers * rows * 4) + up(layers * rows * width * 4) + up(layers * 128)
     assert lib.ekv_audit_workspace_bytes(layers, rows, width) == want
     assert lib.ekv_audit_workspace_bytes(0, rows, width) == 0
 

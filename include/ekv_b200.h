@@ -82,11 +82,12 @@ size_t ekv_audit_workspace_bytes(int layers, int rows, int width);
  * reference's sampling (one KV group per layer, group = layer % kv_heads, :250).
  *
  * With share_out != NULL and EKV_SHARE_FINALIZE (the step's last layer) the same call then turns
- * the cells of every layer [0, layers) into the exact per-block attention share, in a second kernel
- * over (layer, row) pairs that reads the cells back from L2: block shares as normalize_tile_lse
- * computes them (observe/tile_shares.py:58-103 with row_blocks = ceil(lens/block_size)), then the
- * mean or max over layers and query rows into share_out [rows][width] and contributors [rows]
- * (query rows with data); a row that is not selected or has no data is NaN.
+ * the cells of every layer [0, layers) into the exact per-block attention share: a kernel with one
+ * warp per (layer, row) reads the cells back from L2 and forms the block shares as
+ * normalize_tile_lse computes them (observe/tile_shares.py:58-103 with row_blocks =
+ * ceil(lens/block_size)), then a combine kernel takes the mean or max over layers and query rows
+ * into share_out [rows][width] and contributors [rows] (query rows with data); a row that is not
+ * selected or has no data is NaN.
  * status (optional) receives EKV_STATUS_* bits. q_tokens bounds qrow. Supported: head_dim 128,
  * block_size a multiple of 8 (the key cache is read a block at a time through a TMA tensor map),
  * block_size*tile_blocks in {16, 32, 64}, tile_blocks <= 8, heads*group_rows <= 128,

@@ -18,11 +18,12 @@
 // C fragment's rows and query rows on its columns, so the tile max and sum are three xor-shuffles
 // per column: tile_lse_kernel's computation (runtime/audit_kernel.py:70-96), stored as at :97-109.
 //
-// Shares. The share kernel runs one CTA per (layer, row): it reads the row's cells back (from L2),
-// forms u = m + log(l) - log(tile_blocks) (observe/tile_shares.py:172-173), the row's log total per
-// query row, and every block's share with the partial tail tile's weight given back to its blocks
-// (:82-103); the CTA that completes a row's last layer (a ticket) sums or maxes the layers in layer
-// order into the row's final share. Every sum has a fixed order, so the output is deterministic.
+// Shares. After the record kernel, the share kernel gives each (layer, row) one warp, which reads the
+// row's cells back from L2 (eight tiles' loads in flight per lane): u = m + log(l) - log(tile_blocks)
+// per tile (observe/tile_shares.py:172-173), the row's log total per query row, and every block's
+// share with the partial tail tile's weight given back to its blocks (:82-103). The combine kernel
+// then sums or maxes the layers in layer order into the row's final share, a thread per block. Every
+// sum has a fixed order, so the output is deterministic.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -43,7 +44,7 @@ constexpr int kMaxQ = 128;
 constexpr int kMaxRows = 2048;
 constexpr int kMaxLayers = 1024;
 constexpr int kChunkTiles = EKV_AUDIT_CHUNK_TILES;
-constexpr int kShareThreads = 128;
+constexpr int kCombineThreads = 128;
 constexpr int kMinCtas = 12 / kWarps > 0 ? 12 / kWarps : 1;  // registers for 12 warps per SM
 constexpr int kItemQueue = 16;  // items a warp has taken but not yet consumed (at most STAGES + 2)
 
@@ -528,160 +529,206 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
   }
 }
 
-// ---- the share kernel: one CTA per (layer, row) ------------------------------------------------------
+// ---- the share kernel: one warp per (layer, row) ---------------------------------------------------------
 
-__global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams p) {
-  __shared__ float s_m[kShareThreads], s_s[kShareThreads];
-  __shared__ float s_lse[kMaxQ];
-  __shared__ uint8_t s_has[kMaxQ];
-  __shared__ int s_count;
-  __shared__ int s_last;
-  __shared__ float s_red[kShareThreads / 32];
-  __shared__ uint8_t s_layer_on[kMaxLayers];
-  const int L = p.layer0 + blockIdx.x, r = blockIdx.y;
-  const int tid = threadIdx.x;
-  if (*p.flag == 0) return;  // nothing was recorded this step
-  const RowInfo ri = row_info(p, r, false);
+constexpr int kShareWarps = 4;
+constexpr int kShareBatch = 8;  // tiles whose cells a lane loads before it uses any
+
+// The block shares of layer L of row r (n blocks) from the cells of the row's tiles, into
+// share_layer[L][r][:n], and the number of query rows with data into contrib_layer[L][r]. Lane l
+// takes query row kl + 32 a (kl = l % lanes_q) of tiles rep, rep + reps, ... (rep = l / lanes_q),
+// lanes_q being the query rows rounded up to a power of two (at most 32).
+__device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, int n, float* w_lse, int* w_has) {
+  const int lane = threadIdx.x & 31;
+  const int Q = p.Q, TB = p.tile_blocks;
+  const int n_tiles = (n + TB - 1) / TB;
   const size_t lr = (size_t)L * p.rows + r;
-  if (ri.n_chunks == 0) {  // the row records nothing: no contributors, a NaN share row
-    if (tid == 0) p.contrib_layer[lr] = 0;
-    if (blockIdx.x == 0) {
-      for (int b = tid; b < p.width; b += kShareThreads) p.share_out[(size_t)r * p.width + b] = NAN;
-      if (tid == 0) p.contrib_out[r] = 0;
+  const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
+  const float* cm = p.lse + lr * p.width * Q;  // tile t's cell: its first block, t * TB
+  const float* cl = cm + plane;
+  int qp = 1;
+  while (qp < Q) qp <<= 1;
+  const int lanes_q = qp < 32 ? qp : 32;
+  const int reps = 32 / lanes_q;
+  const int kpl = qp > 32 ? qp / 32 : 1;  // query rows per lane (kMaxQ = 128: at most 4)
+  const int kl = lane % lanes_q, rep = lane / lanes_q;
+  const int steps = (n_tiles + reps - 1) / reps;
+
+  // 1. the log total of each query row: (max, sum) merged over the tiles in order, then over the
+  // replicas (lse_merge is commutative: both partners of a shuffle hold the same result)
+  const float log_tb = logf((float)TB);
+  int has = 0;
+  for (int a = 0; a < kpl; ++a) {
+    const int k = kl + 32 * a;
+    const bool active = k < Q;
+    float M = -INFINITY, S = 0.f;
+    for (int j0 = 0; j0 < steps; j0 += kShareBatch) {
+      float mv[kShareBatch], lv[kShareBatch];
+#pragma unroll
+      for (int u = 0; u < kShareBatch; ++u) {
+        const int t = rep + reps * (j0 + u);
+        const bool ok = active && t < n_tiles;
+        const size_t cell = (size_t)(ok ? t : 0) * TB * Q + (active ? k : 0);
+        mv[u] = ok ? __ldcg(cm + cell) : -INFINITY;
+        lv[u] = ok ? __ldcg(cl + cell) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kShareBatch; ++u)
+        if (mv[u] > -INFINITY && lv[u] > 0.f) lse_merge(M, S, mv[u], lv[u]);  // a tile with no data is skipped
     }
+    for (int off = lanes_q; off < 32; off <<= 1) {
+      const float m2 = __shfl_xor_sync(kFullMask, M, off), s2 = __shfl_xor_sync(kFullMask, S, off);
+      lse_merge(M, S, m2, s2);
+    }
+    if (rep == 0 && active) {
+      const bool h = M > -INFINITY;
+      w_has[k] = h;
+      w_lse[k] = h ? M + logf(S) + log_tb : 0.f;  // log of the sum over blocks of exp(u), plus log(TB)
+      has += h;
+    }
+  }
+  for (int off = 16; off > 0; off >>= 1) has += __shfl_xor_sync(kFullMask, has, off);
+  if (lane == 0) p.contrib_layer[lr] = has;
+  __syncwarp();
+
+  // 2. every tile's share, summed (mean) or maxed (max) over the query rows: exp(u - lse) =
+  // exp(m + log(l) - (M + log S)); the blocks of a partial last tile get its weight back,
+  // exp(u + log(TB / tail) - lse) = exp(u - lse) * TB / tail
+  const bool agg_max = p.aggregate == EKV_AGG_MAX;
+  const int tail = n % TB;
+  float* sl = p.share_layer + lr * p.width;
+  for (int j0 = 0; j0 < steps; j0 += kShareBatch) {
+    float e[kShareBatch];
+#pragma unroll
+    for (int u = 0; u < kShareBatch; ++u) e[u] = 0.f;
+    for (int a = 0; a < kpl; ++a) {
+      const int k = kl + 32 * a;
+      const bool active = k < Q && w_has[k < Q ? k : 0];
+      const float lse = active ? w_lse[k] : 0.f;
+      float mv[kShareBatch], lv[kShareBatch];
+#pragma unroll
+      for (int u = 0; u < kShareBatch; ++u) {
+        const int t = rep + reps * (j0 + u);
+        const bool ok = active && t < n_tiles;
+        const size_t cell = (size_t)(ok ? t : 0) * TB * Q + (ok ? k : 0);
+        mv[u] = ok ? __ldcg(cm + cell) : -INFINITY;
+        lv[u] = ok ? __ldcg(cl + cell) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kShareBatch; ++u) {
+        const float x = mv[u] + logf(lv[u]);
+        const float sh = x > -INFINITY ? __expf(x - lse) : 0.f;  // NaN cells fail the test: no share
+        e[u] = agg_max ? fmaxf(e[u], sh) : e[u] + sh;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kShareBatch; ++u) {
+      for (int off = 1; off < lanes_q; off <<= 1) {
+        const float o = __shfl_xor_sync(kFullMask, e[u], off);
+        e[u] = agg_max ? fmaxf(e[u], o) : e[u] + o;
+      }
+      const int t = rep + reps * (j0 + u);
+      if (t < n_tiles && kl == 0) {
+        const int b0 = t * TB, b1 = min(b0 + TB, n);
+        const float v = (tail && b1 == n) ? e[u] * ((float)TB / (float)tail) : e[u];
+        for (int b = b0; b < b1; ++b) sl[b] = v;
+      }
+    }
+  }
+}
+
+// Grid: (layers [layer0, layer0 + n_layers)) x rows pairs, kShareWarps per CTA.
+__global__ void __launch_bounds__(kShareWarps * 32) share_kernel(const AuditParams p) {
+  __shared__ float s_lse[kShareWarps][kMaxQ];
+  __shared__ int s_has[kShareWarps][kMaxQ];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (*p.flag == 0) return;  // nothing was recorded this step
+  const long long pair = (long long)blockIdx.x * kShareWarps + warp;
+  if (pair >= (long long)p.n_layers * p.rows) return;
+  const int L = p.layer0 + (int)(pair / p.rows), r = (int)(pair % p.rows);
+  const RowInfo ri = row_info(p, r, false);
+  if (ri.n_chunks == 0) {  // the row records nothing: no contributors
+    if (lane == 0) p.contrib_layer[(size_t)L * p.rows + r] = 0;
     return;
   }
-  const int Q = p.Q, TB = p.tile_blocks, n = ri.n_blocks;
-  const float log_tb = logf((float)TB);
-  const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
-  const float* cm = p.lse + lr * p.width * Q;
-  const float* cl = cm + plane;
-  // 1. the log total of each query row over the row's tiles (one cell per tile: its first block)
-  const int per_j = kShareThreads / Q;
-  const int j = tid % Q;
-  float m = -INFINITY, s = 0.f;
-  if (tid < per_j * Q) {
-    constexpr int U = 4;  // cells loaded before any is used
-    for (int t0 = tid / Q; t0 < ri.n_tiles; t0 += U * per_j) {
-      float mv[U], lv[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int t = t0 + u * per_j;
-        const size_t cell = (size_t)(t < ri.n_tiles ? t : 0) * TB * Q + j;
-        mv[u] = __ldcg(cm + cell);
-        lv[u] = __ldcg(cl + cell);
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const float x = mv[u] + logf(lv[u]) - log_tb;
-        if (t0 + u * per_j < ri.n_tiles && isfinite(x)) lse_merge(m, s, x, 1.f);
-      }
-    }
+  share_task(p, L, r, ri.n_blocks, s_lse[warp], s_has[warp]);
+}
+
+// ---- the combine kernel: a row's layers into its final share --------------------------------------------
+//
+// Grid (width / kCombineThreads, rows), one block per thread: the sum (mean) or max over the layers
+// [layer0, layer0 + n_layers) with data, in layer order, divided by the contributors (mean) or, by
+// the CTA that finishes the row last (a ticket), by the row's total (max). A row that records nothing
+// is NaN with no contributors.
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditParams p) {
+  __shared__ uint8_t s_on[kMaxLayers];
+  __shared__ int s_c[kCombineThreads / 32];
+  __shared__ float s_red[kCombineThreads / 32];
+  __shared__ int s_last;
+  const int r = blockIdx.y, tid = threadIdx.x;
+  if (*p.flag == 0) return;  // nothing was recorded this step
+  const RowInfo ri = row_info(p, r, false);
+  float* out = p.share_out + (size_t)r * p.width;
+  const int b = blockIdx.x * kCombineThreads + tid;
+  if (ri.n_chunks == 0) {
+    if (b < p.width) out[b] = NAN;
+    if (blockIdx.x == 0 && tid == 0) p.contrib_out[r] = 0;
+    return;
   }
-  s_m[tid] = m;
-  s_s[tid] = s;
+  const int la = p.layer0, lb = p.layer0 + p.n_layers;
+  int c = 0;
+  for (int k = la + tid; k < lb; k += kCombineThreads) {
+    const int ck = __ldcg(p.contrib_layer + (size_t)k * p.rows + r);
+    s_on[k - la] = ck != 0;
+    c += ck;
+  }
+  for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(kFullMask, c, off);
+  if ((tid & 31) == 0) s_c[tid >> 5] = c;
   __syncthreads();
-  if (tid < Q) {
-    float mj = -INFINITY, sj = 0.f;
-    for (int k = 0; k < per_j; ++k) lse_merge(mj, sj, s_m[k * Q + tid], s_s[k * Q + tid]);
-    s_has[tid] = mj != -INFINITY;
-    s_lse[tid] = mj != -INFINITY ? log_tb + mj + logf(sj) : 0.f;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    int c = 0;
-    for (int k = 0; k < Q; ++k) c += s_has[k];
-    s_count = c;
-    p.contrib_layer[lr] = c;
-  }
-  // 2. every block's share, summed (mean) or maxed (max) over the query rows
-  const int tail = n % TB;
-  const int tail_start = n - tail;
-  const float regain = tail ? logf((float)TB / (float)tail) : 0.f;
+  int contributors = 0;
+  for (int w = 0; w < kCombineThreads / 32; ++w) contributors += s_c[w];
+  if (blockIdx.x == 0 && tid == 0) p.contrib_out[r] = contributors;
   const bool agg_max = p.aggregate == EKV_AGG_MAX;
-  float* sl = p.share_layer + lr * p.width;
-  for (int b = tid; b < n; b += kShareThreads) {
-    const float rg = b >= tail_start ? regain : 0.f;
-    float a = 0.f;
-    constexpr int U = 4;
-    for (int k0 = 0; k0 < Q; k0 += U) {
-      float mv[U], lv[U];
+  const int n = ri.n_blocks;
+  if (b < p.width) {
+    float v = 0.f;
+    if (contributors == 0) {
+      v = NAN;
+    } else if (b < n) {
+      constexpr int U = 8;  // layers loaded before any is added, then added in layer order
+      for (int k0 = la; k0 < lb; k0 += U) {
+        float x[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int k = k0 + u < Q ? k0 + u : 0;
-        mv[u] = __ldcg(cm + (size_t)b * Q + k);
-        lv[u] = __ldcg(cl + (size_t)b * Q + k);
-      }
+        for (int u = 0; u < U; ++u) {
+          const int k = k0 + u < lb ? k0 + u : la;
+          x[u] = __ldcg(p.share_layer + ((size_t)k * p.rows + r) * p.width + b);
+        }
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int k = k0 + u;
-        const float x = mv[u] + logf(lv[u]) - log_tb;
-        const float sh = (k < Q && s_has[k < Q ? k : 0] && isfinite(x)) ? __expf(x + rg - s_lse[k < Q ? k : 0]) : 0.f;
-        a = agg_max ? fmaxf(a, sh) : a + sh;
+        for (int u = 0; u < U; ++u) {
+          const int k = k0 + u;
+          if (k < lb && s_on[k - la]) v = agg_max ? fmaxf(v, x[u]) : v + x[u];
+        }
       }
+      if (!agg_max) v /= (float)contributors;
     }
-    sl[b] = a;
+    out[b] = v;
   }
-  // 3. the CTA that completes the row's last layer combines the layers in layer order
+  if (!agg_max || contributors == 0) return;
+  // max: the last CTA of the row divides the row by its total
   __threadfence();
   __syncthreads();
   if (tid == 0) s_last = atomicAdd(&p.row_tickets[r], 1u) == gridDim.x - 1;
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  const int la = p.layer0, lb = p.layer0 + gridDim.x;
-  int c = 0;
-  for (int k = la + tid; k < lb; k += kShareThreads) {
-    const int ck = __ldcg(p.contrib_layer + (size_t)k * p.rows + r);
-    s_layer_on[k - la] = ck != 0;
-    c += ck;
-  }
-  for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(kFullMask, c, off);
-  __shared__ int s_c[kShareThreads / 32];
-  if ((tid & 31) == 0) s_c[tid >> 5] = c;
-  __syncthreads();
-  if (tid == 0) {
-    p.row_tickets[r] = 0;  // ready for the next step
-    int total = 0;
-    for (int w = 0; w < kShareThreads / 32; ++w) total += s_c[w];
-    s_count = total;
-    p.contrib_out[r] = total;
-  }
-  __syncthreads();
-  const int contributors = s_count;
-  float* out = p.share_out + (size_t)r * p.width;
   float part = 0.f;
-  for (int b = tid; b < n; b += kShareThreads) {
-    float v = 0.f;
-    constexpr int U = 8;  // layers loaded before any is added, then added in layer order
-    for (int k0 = la; k0 < lb; k0 += U) {
-      float x[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int k = k0 + u < lb ? k0 + u : la;
-        x[u] = __ldcg(p.share_layer + ((size_t)k * p.rows + r) * p.width + b);
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int k = k0 + u;
-        if (k < lb && s_layer_on[k - la]) v = agg_max ? fmaxf(v, x[u]) : v + x[u];
-      }
-    }
-    out[b] = v;
-    part += v;
+  for (int k = tid; k < n; k += kCombineThreads) part += __ldcg(out + k);
+  const float total = block_sum_fixed_order<kCombineThreads>(part, s_red);
+  for (int k = tid; k < n; k += kCombineThreads) {
+    const float v = __ldcg(out + k);
+    out[k] = total > 0.f ? v / total : 0.f;
   }
-  const float total = agg_max ? block_sum_fixed_order<kShareThreads>(part, s_red) : 1.f;
-  for (int b = tid; b < p.width; b += kShareThreads) {
-    float v;
-    if (contributors == 0) {
-      v = NAN;
-    } else if (b >= n) {
-      v = 0.f;
-    } else {
-      v = agg_max ? (total > 0.f ? out[b] / total : 0.f) : out[b] / (float)contributors;
-    }
-    out[b] = v;
-  }
+  if (tid == 0) p.row_tickets[r] = 0;  // ready for the next step
 }
 
 // One tensor map per layer of a step: the host-encoded template with the layer's key-cache address
@@ -745,8 +792,12 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
   AuditParams ps = p;
   ps.layer0 = share0;
   ps.n_layers = share_layers;
-  share_kernel<<<dim3(share_layers, p.rows), kShareThreads, 0, stream>>>(ps);
-  return check_launch("share_kernel");
+  const long long pairs = (long long)share_layers * p.rows;
+  share_kernel<<<(unsigned)((pairs + kShareWarps - 1) / kShareWarps), kShareWarps * 32, 0, stream>>>(ps);
+  rc = check_launch("share_kernel");
+  if (rc != EKV_OK) return rc;
+  combine_kernel<<<dim3(cdiv(p.width, kCombineThreads), p.rows), kCombineThreads, 0, stream>>>(ps);
+  return check_launch("combine_kernel");
 }
 
 template <typename T>

@@ -301,13 +301,22 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
   __syncwarp();
   const uint64_t policy = l2_evict_first_policy();
 
-  // the issue side: cursor `in`, the ids of its item and of the item after it
+  // the issue side: cursor `in`, the ids of its item and of the item after it. The next item is
+  // taken when `in` reaches its last tile: late enough that no warp holds an item it will not start
+  // soon (the end of a launch stays even), early enough for its block ids to land.
   Cursor in{}, in_next{};
-  int32_t ids_lo, ids_hi, nids_lo, nids_hi;
+  int32_t ids_lo, ids_hi, nids_lo = -1, nids_hi = -1;
+  bool next_taken = false;
+  auto take_next_if_due = [&]() {
+    if (!next_taken && in.item < total_items && in.t >= in.t_end - 1) {
+      decode(take(), in_next);
+      load_ids(in_next, nids_lo, nids_hi);
+      next_taken = true;
+    }
+  };
   decode(take(), in);
   load_ids(in, ids_lo, ids_hi);
-  decode(take(), in_next);
-  load_ids(in_next, nids_lo, nids_hi);
+  take_next_if_due();
 
   // Issue the tensor copies of the tile at `in` into stage s, then step `in` forward: lanes 2j and
   // 2j + 1 copy the two halves of block j of the tile.
@@ -353,12 +362,14 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
       uint8_t* dst = my_ring + s * STAGE + half * HALF + (jb << bs_shift) * Lay::kHalfRow;
       tensor_copy_g2s(dst, map, 64 * half, kv_head_of(p, in.layer, in.head), 0, id, &my_bars[s], policy);
     }
-    if (++in.t >= in.t_end) {  // the next item: its ids were prefetched; prefetch the one after
+    ++in.t;
+    take_next_if_due();
+    if (in.t >= in.t_end) {  // the next item: its ids were prefetched
       in = in_next;
       ids_lo = nids_lo;
       ids_hi = nids_hi;
-      decode(take(), in_next);
-      load_ids(in_next, nids_lo, nids_hi);
+      next_taken = false;
+      take_next_if_due();
     }
   };
 
@@ -382,11 +393,13 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
   while (out.item < total_items) {
     const int s = (int)(consumed % STAGES);
     const uint32_t parity = (uint32_t)((consumed / STAGES) & 1);
-    if (out.t == out.t0) {  // an item starts: its fragments were prefetched; prefetch the next item's
+    if (out.t == out.t0) {  // an item starts: its fragments were prefetched
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int k = 0; k < KS; ++k) bq[nt][k][0] = bqn[nt][k][0], bq[nt][k][1] = bqn[nt][k][1];
+    }
+    if (out.t == out.t_end - 1) {  // its last tile: the issue side has taken the next item; prefetch
       Cursor nxt{};
       __syncwarp();
       decode(s_queue[warp][(n_used + 1) % kItemQueue], nxt);

@@ -53,7 +53,7 @@ CONFIGS = {
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one record-kernel launch (an audit step of all 32
 # layers) of the llama8b workload, from an ncu capture of that launch.
-NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"llama8b": 2458.652e6 + 8.532e6}
+NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"llama8b": 2458.654e6 + 8.595e6}
 
 
 def lengths(spec, rows: int, rng: np.random.Generator) -> np.ndarray:
@@ -510,7 +510,9 @@ def main() -> None:
                 "note": "RecordingPlane.record per layer (a query stash per layer, one launch of every layer "
                         "after the last) in a CUDA graph; block table, lengths, selection, query rows in from "
                         "pinned host memory, shares out; KV cache resident"},
-        "gpu_launches": args.steps * (2 if args.record == "deferred" else w.layers + 1),
+        # per step: the descriptor, record, share and combine kernels (deferred), or a record kernel
+        # per layer plus the share and combine kernels (per-layer)
+        "gpu_launches": args.steps * (4 if args.record == "deferred" else w.layers + 2),
         "clocks": clocks.summary(),
         "per_layer_launches": per_layer,
         "view": view,

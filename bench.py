@@ -269,11 +269,22 @@ def view_bench(rank: int, world: int, steps: int, warmup: int, dist_on: bool) ->
     def build():
         plan_view(t, ln, BLOCK, nn, scores=sc, policy="sum", row_fraction=fr, recent_blocks=0, out=out)
 
-    graph = capture(build)
-    seconds = timed(graph.replay, steps, warmup, dist_on)
+    def build_shared():  # the controller's default: `sum` with one budget over every row
+        plan_view(t, ln, BLOCK, nn, scores=sc, policy="sum", budget_fraction=0.5, recent_blocks=4, out=out)
+
+    newest = torch.arange(width, dtype=torch.float32, device=dev).expand(len(nn), width).contiguous()
+
+    def build_newest():  # keep-newest: scores = arange(n) under `uniform`, budget 0.5
+        plan_view(t, ln, BLOCK, nn, scores=newest, policy="uniform", budget_fraction=0.5, recent_blocks=0, out=out)
+
     ids = int(n.long().sum())
-    return {"us": round(seconds / steps * 1e6, 2), "rows": rows_total, "width": width, "ids": ids,
-            "policy": "sum per row", "rows_per_gpu": len(nn), "launches_per_build": 2}
+    result = {"rows": rows_total, "width": width, "ids": ids, "policy": "sum per row", "rows_per_gpu": len(nn)}
+    for key, fn, launches in (("us", build, 2), ("sum_shared_us", build_shared, 10), ("newest_us", build_newest, 2)):
+        graph = capture(fn)
+        result[key] = round(timed(graph.replay, steps, warmup, dist_on) / steps * 1e6, 2)
+        result[key.replace("us", "launches")] = launches
+        del graph
+    return result
 
 
 # ---- the CPU arms ----------------------------------------------------------------------------------------

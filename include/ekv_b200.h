@@ -218,6 +218,29 @@ int ekv_allocate_quotas(const int32_t* row_blocks, const int32_t* measured_block
                         int64_t budget, const double* row_fraction, int objective, int rows,
                         int32_t* quota, void* stream);
 
+/* Bytes of workspace ekv_allocate_sum needs for `rows` rows of `width` blocks (256-byte aligned). */
+size_t ekv_allocate_sum_workspace_bytes(int rows, int width);
+
+/*
+ * ekv_allocate_sum -- the quotas of the `sum` objective with one budget shared by every measured row.
+ *
+ * Replaces allocate(requests, budget, "sum") over several requests (observe/allocation.py:55-76 and
+ * _greedy :94-118), the controller's default objective (observe/controller.py:30, :398-451). Row r
+ * is a request when row_blocks[r] > cap_above_blocks (and > 0); its n = min(row_blocks[r], width)
+ * scores are scores[r][0..n) (float32, row stride score_stride; NaN counts as 0), its weight
+ * weights[r] (float64; NULL: 1.0), its pins those of ekv_allocate_quotas. The budget is `budget` when
+ * it is >= 0, else max(pins, ceil(budget_fraction * blocks)). The reference keeps the `free`
+ * unpinned blocks of largest weight * max(score, 0) / total (float64, total = NumPy's pairwise sum
+ * of the request's clamped scores), equal gains to the newer block, then to the earlier request;
+ * this call computes, bit-exactly, how many of them fall in each row: quota [rows] int32 for
+ * ekv_view_build with EKV_POLICY_SUM and the same pins, or -1 for a row that is not a request.
+ * width <= 32768. Nine kernels and one memset on `stream`, no host synchronisation.
+ */
+int ekv_allocate_sum(const float* scores, int64_t score_stride, const double* weights,
+                     const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,
+                     int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
+                     int32_t* quota, void* workspace, size_t workspace_bytes, void* stream);
+
 /*
  * ekv_view_build -- the per-row keep decision and the compacted block-table view, in one kernel.
  *

@@ -4,14 +4,16 @@ Drop-in for observe/allocation.py of the reference: ``Objective``, ``Request`` a
 keep their names, signature, pins, validation and tie rules. ``uniform`` gives every request the
 same fraction of its unpinned blocks by largest remainder (equal remainders to the earlier request)
 and keeps each request's best blocks by its own shares, equal shares to the older block
-(allocation.py:79-91). ``sum`` keeps the unpinned blocks with the largest weighted share, equal
-shares to the newer block (:94-118). The quotas and the per-request top-k selection run in the
-sm_100a kernels ``ekv_allocate_quotas`` and ``ekv_view_build``.
+(allocation.py:79-91). ``sum`` keeps the unpinned blocks with the largest weighted share over all
+requests, equal gains to the newer block, then to the earlier request (:94-118). The quotas run in
+the sm_100a kernels ``ekv_allocate_quotas`` (uniform) and ``ekv_allocate_sum`` (sum: a global
+radix select over the float64 gains, with each request's total summed as NumPy sums it), the
+per-request top-k selection in ``ekv_view_build``.
 
-Device ranking compares max(score, 0) as float32. For float32-exact scores that is the reference's
-ranking by float64 shares exactly: dividing distinct float32 values by the same total keeps them
-distinct and ordered, and equal values stay equal. Scores that float32 cannot hold exactly,
-``sum`` over several requests (a global top-k), and ``maxmin`` are not implemented on the device
+Device ranking compares max(score, 0) as float32 within a request. For float32-exact scores that is
+the reference's ranking by float64 shares exactly: dividing distinct float32 values by the same total
+(and multiplying by one weight) keeps them distinct and ordered, and equal values stay equal. Scores
+that float32 cannot hold exactly, negative weights and ``maxmin`` are not implemented on the device
 and raise ``RuntimeError``; NaN scores count as 0, as the controller passes them (controller.py:337).
 """
 
@@ -70,6 +72,38 @@ def _pin_start(pinned: np.ndarray) -> int:
     return tail
 
 
+def sum_quotas(
+    scores: torch.Tensor,
+    row_blocks: torch.Tensor,
+    quota: torch.Tensor,
+    *,
+    measured: torch.Tensor | None,
+    recent_blocks: int,
+    cap_above_blocks: int,
+    budget: int = -1,
+    budget_fraction: float = 0.0,
+    weights: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """The per-row quotas of the ``sum`` objective with one shared budget (``ekv_allocate_sum``).
+
+    ``scores`` float32 [rows, width] on the device, ``row_blocks`` int32 [rows], ``quota`` int32 [rows]
+    (out), ``weights`` float64 [rows] or None; ``budget`` >= 0 as given, else from
+    ``budget_fraction`` as the controller computes it. No host synchronisation.
+    """
+    rows, width = int(scores.shape[0]), int(scores.shape[1])
+    lib = _lib.load()
+    size = int(lib.ekv_allocate_sum_workspace_bytes(rows, width))
+    workspace = torch.empty(size + 256, dtype=torch.uint8, device=scores.device)
+    base = (workspace.data_ptr() + 255) // 256 * 256
+    rc = lib.ekv_allocate_sum(
+        scores.data_ptr(), scores.stride(0), None if weights is None else weights.data_ptr(), row_blocks.data_ptr(),
+        None if measured is None else measured.data_ptr(), int(recent_blocks), int(cap_above_blocks),
+        float(budget_fraction), int(budget), rows, width, quota.data_ptr(), base, size, _lib.current_stream(),
+    )
+    _lib.check(rc, "ekv_allocate_sum")
+    return quota
+
+
 def allocate(requests: Sequence[Request], budget: int, objective: Objective = "sum") -> list[np.ndarray]:
     """Return, for each request, a bool mask of the blocks to keep. At most ``budget`` blocks are kept."""
     sizes = [len(r.scores) for r in requests]
@@ -89,9 +123,6 @@ def allocate(requests: Sequence[Request], budget: int, objective: Objective = "s
         raise ValueError(f"the {objective} objective does not use request weights")
     if objective == "maxmin":
         raise RuntimeError("the maxmin objective is not implemented on the device")
-    if objective == "sum" and len(requests) > 1:
-        raise RuntimeError("`sum` over several requests needs a global top-k, not implemented on the device")
-    free = budget - must
     width = max(sizes) if sizes else 0
     rows = len(requests)
     if rows == 0 or width == 0:
@@ -116,13 +147,15 @@ def allocate(requests: Sequence[Request], budget: int, objective: Objective = "s
     row_blocks = torch.tensor(sizes, dtype=torch.int32).to(device)
     measured = pin_starts.to(device)
     quota = torch.empty(rows, dtype=torch.int32, device=device)
+    scores_t = torch.from_numpy(scores).to(device)
     if objective == "uniform":
         rc = lib.ekv_allocate_quotas(row_blocks.data_ptr(), measured.data_ptr(), -1, -1, 0.0, int(budget), None,
                                      _lib.POLICY_UNIFORM, rows, quota.data_ptr(), stream)
         _lib.check(rc, "ekv_allocate_quotas")
     else:
-        quota.fill_(int(free))
-    scores_t = torch.from_numpy(scores).to(device)
+        weights = torch.tensor([float(r.weight) for r in requests], dtype=torch.float64).to(device)
+        sum_quotas(scores_t, row_blocks, quota, measured=measured, recent_blocks=-1, cap_above_blocks=-1,
+                   budget=int(budget), weights=weights)
     table = torch.zeros(rows, width, dtype=torch.int32, device=device)
     lens = torch.zeros(rows, dtype=torch.int32, device=device)
     view = torch.empty(rows, width, dtype=torch.int32, device=device)

@@ -117,14 +117,16 @@ def plan_view(
     full_rows: torch.Tensor | None = None,
     mask_out: torch.Tensor | None = None,
     out: tuple[torch.Tensor, torch.Tensor] | None = None,
+    weights: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
-    """Decide and compact in two kernels: the controller's quotas, then pins + top-k + compaction.
+    """Decide and compact: the controller's quotas, then pins + top-k + compaction.
 
     ``row_blocks`` int32 [rows]: each request's length in blocks at the decision (0 = no request).
     Rows at or below ``cap_above_blocks`` read in full. With ``budget_fraction`` the measured rows
-    share the budget max(pins, ceil(fraction * blocks)) split by uniform quotas
-    (controller.py:398-451); with ``row_fraction`` (float64 [rows]) each row is its own allocate()
-    call. ``policy`` "uniform"/"sum" ranks by ``scores`` (float32 [rows, width], the device shares),
+    share the budget max(pins, ceil(fraction * blocks)) (controller.py:398-451), split by uniform
+    quotas, or under ``sum`` by the global greedy over the weighted shares (``weights`` float64
+    [rows], None for 1.0; a row of weight 0 must pass zero scores); with ``row_fraction`` (float64
+    [rows]) each row is its own allocate() call. ``policy`` "uniform"/"sum" ranks by ``scores`` (float32 [rows, width], the device shares),
     "newest" keeps the newest blocks (the daemon's recency rule). ``mask_out`` receives the mask the
     controller commits.
     """
@@ -133,12 +135,21 @@ def plan_view(
     rows = int(table.shape[0])
     quota = torch.empty(rows, dtype=torch.int32, device=table.device)
     objective = _POLICIES[policy]
-    rc = _lib.load().ekv_allocate_quotas(
-        row_blocks.data_ptr(), _ptr(measured), int(recent_blocks), int(cap_above_blocks),
-        float(budget_fraction or 0.0), -1, _ptr(row_fraction), objective, rows, quota.data_ptr(),
-        _lib.current_stream(),
-    )
-    _lib.check(rc, "ekv_allocate_quotas")
+    if policy == "sum" and budget_fraction is not None:
+        # one budget over every measured row: the global greedy of the controller's default objective
+        if scores is None:
+            raise ValueError("the sum objective ranks by scores")
+        from ..observe.allocation import sum_quotas
+
+        sum_quotas(scores, row_blocks, quota, measured=measured, recent_blocks=recent_blocks,
+                   cap_above_blocks=cap_above_blocks, budget_fraction=float(budget_fraction), weights=weights)
+    else:
+        rc = _lib.load().ekv_allocate_quotas(
+            row_blocks.data_ptr(), _ptr(measured), int(recent_blocks), int(cap_above_blocks),
+            float(budget_fraction or 0.0), -1, _ptr(row_fraction), objective, rows, quota.data_ptr(),
+            _lib.current_stream(),
+        )
+        _lib.check(rc, "ekv_allocate_quotas")
     return _view_build(
         table, seq_lens, block_size, row_blocks=row_blocks, quota=quota, measured=measured,
         recent_blocks=recent_blocks, scores=scores, policy=policy, released=released, full_rows=full_rows,

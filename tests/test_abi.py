@@ -122,6 +122,19 @@ def test_other_entry_points_validate_before_launching(lib):
     view_args[16] = 20000
     assert lib.ekv_view_build(*view_args) == L.ENOTSUP  # wider than 16384
     assert lib.ekv_compact_block_table(fake, 8, fake, None, 8, 2, 8, 16, fake, 8, fake, None) == L.EINVAL
+    # the sum quotas: workspace, width, stride and budget are checked before anything is launched
+    assert lib.ekv_allocate_sum_workspace_bytes(0, 8) == 0
+    ws = lib.ekv_allocate_sum_workspace_bytes(2, 8)
+    assert ws >= 256 + 2048 * 4 + 2 * 8 * 2
+    sum_args = [fake, 8, None, fake, None, 4, 0, 0.5, -1, 2, 8, fake, None, 0, None]
+    assert lib.ekv_allocate_sum(*sum_args) == L.ERANGE  # no workspace
+    sum_args[12], sum_args[13] = ctypes.c_void_p(0x1000), ws
+    sum_args[1] = 4
+    assert lib.ekv_allocate_sum(*sum_args) == L.EINVAL  # score stride below the width
+    sum_args[1], sum_args[7] = 8, 1.5
+    assert lib.ekv_allocate_sum(*sum_args) == L.EINVAL  # a fraction above 1 with no explicit budget
+    sum_args[7], sum_args[10] = 0.5, 40000
+    assert lib.ekv_allocate_sum(*sum_args) == L.ENOTSUP  # wider than 32768
 
 
 def test_step_and_stash_validate_before_launching(lib):

@@ -61,19 +61,15 @@ def test_allocate_matches_the_reference_bit_exactly_including_ties():
     from ekv.observe.allocation import Request, allocate
 
     g = load_golden("allocation_cases")
-    checked = 0
+    several_sum = 0
     for i in range(60):
         scores, pinned = golden_requests(g, i)
         objective = str(g[f"objective{i}"])
         requests = [Request(scores=s, pinned=p) for s, p in zip(scores, pinned, strict=True)]
-        if objective == "sum" and len(requests) > 1:
-            with pytest.raises(RuntimeError):
-                allocate(requests, int(g[f"budget{i}"]), objective)
-            continue
         masks = allocate(requests, int(g[f"budget{i}"]), objective)
         np.testing.assert_array_equal(np.concatenate(masks), g[f"mask{i}"], err_msg=f"case {i}")
-        checked += 1
-    assert checked >= 40
+        several_sum += objective == "sum" and len(requests) > 1
+    assert several_sum >= 10  # the global greedy over several requests is among the pinned cases
 
 
 def test_allocate_against_the_oracle_with_many_ties():
@@ -95,6 +91,144 @@ def test_allocate_against_the_oracle_with_many_ties():
         want = oa.allocate(scores, budget, objective, pinned)
         for a, b in zip(got, want, strict=True):
             np.testing.assert_array_equal(a, b, err_msg=f"trial {trial}")
+
+
+def test_sum_over_many_requests_against_the_oracle():
+    """The global greedy: ties across requests (newer block, then earlier request), weights, requests
+    without evidence, and budgets from just above the pins to just below every block."""
+    from ekv.observe.allocation import Request, allocate
+
+    rng = np.random.default_rng(17)
+    for trial in range(60):
+        n_req = int(rng.integers(2, 40))
+        sizes = rng.integers(1, 400, n_req)
+        kind = trial % 3
+        scores = []
+        for n in sizes:
+            if kind == 0:
+                scores.append(rng.integers(0, 3, n).astype(np.float64))  # many ties
+            else:
+                scores.append((rng.random(n) ** 3).astype(np.float32).astype(np.float64))
+        if trial % 4 == 0:
+            scores[int(rng.integers(0, n_req))][:] = 0.0  # no evidence: equal shares 1/n
+        weights = [1.0] * n_req if trial % 2 else [float(rng.choice([0.0, 0.5, 1.0, 2.0, 3.0])) for _ in range(n_req)]
+        recent = int(rng.integers(0, 6))
+        pinned = [oa.controller_pins(len(x), recent) for x in scores]
+        must = sum(int(p.sum()) for p in pinned)
+        total = int(sizes.sum())
+        budget = int(rng.choice([must, must + 1, (must + total) // 2, total - 1, int(rng.integers(must, total + 1))]))
+        budget = max(budget, must)
+        requests = [Request(scores=x, weight=w, pinned=p) for x, w, p in zip(scores, weights, pinned, strict=True)]
+        got = allocate(requests, budget, "sum")
+        want = oa.allocate(scores, budget, "sum", pinned, weights)
+        for r, (a, b) in enumerate(zip(got, want, strict=True)):
+            np.testing.assert_array_equal(a, b, err_msg=f"trial {trial}, request {r}")
+        assert sum(int(m.sum()) for m in got) == min(budget, total)
+
+
+def test_sum_totals_follow_numpys_pairwise_summation():
+    """A request and a permutation of it hold the same scores but their float64 totals differ in the
+    last bits with the summation order, which then decides the ranking of equal scores across the two;
+    long rows exercise the pairwise tree above 128 values."""
+    from ekv.observe.allocation import Request, allocate
+
+    rng = np.random.default_rng(23)
+    order_sensitive = 0
+    for trial in range(20):
+        n = int(rng.integers(129, 6000))
+        base = np.exp(rng.normal(0.0, 4.0, n)).astype(np.float32).astype(np.float64)  # a wide range of magnitudes
+        scores = [base, rng.permutation(base), rng.permutation(base)]
+        order_sensitive += len({float(np.sum(x)) for x in scores}) > 1
+        pinned = [oa.controller_pins(n, 4) for _ in scores]
+        must = sum(int(p.sum()) for p in pinned)
+        budget = int(rng.integers(must + 1, 3 * n - 1))
+        got = allocate([Request(scores=x, pinned=p) for x, p in zip(scores, pinned, strict=True)], budget, "sum")
+        want = oa.allocate(scores, budget, "sum", pinned)
+        for a, b in zip(got, want, strict=True):
+            np.testing.assert_array_equal(a, b, err_msg=f"trial {trial}")
+    assert order_sensitive >= 10  # the totals of permuted copies differ: the summation order matters
+
+
+def test_plan_view_sum_with_a_shared_budget_matches_the_controller():
+    """The controller's default objective: one budget over every measured row (cap, recent pins and
+    unmeasured suffixes), then the view, against the oracle's controller and compaction."""
+    from ekv.runtime.block_view import plan_view
+
+    rng = np.random.default_rng(31)
+    for trial in range(12):
+        rows, width = int(rng.integers(1, 96)), int(rng.integers(8, 700))
+        row_blocks = rng.integers(0, width + 1, rows).astype(np.int32)
+        lens = (row_blocks * 16 - rng.integers(0, 16, rows)).clip(0).astype(np.int32)
+        table = rng.integers(0, 1 << 20, (rows, width)).astype(np.int32)
+        if trial % 2:
+            scores = rng.integers(0, 4, (rows, width)).astype(np.float32)
+        else:
+            scores = rng.dirichlet(np.full(width, 0.3), rows).astype(np.float32)
+        measured = rng.integers(0, width + 1, rows).astype(np.int32) if trial % 3 == 0 else None
+        cap = int(rng.choice([0, 0, 5]))
+        fraction = float(rng.choice([0.1, 0.25, 0.5, 0.9]))
+        keep = oa.controller_keep(row_blocks, width, lambda r, n: scores[r, :n].astype(np.float64), fraction, "sum",
+                                  recent_blocks=4, cap_above_blocks=cap, measured=measured)
+        mask = torch.empty(rows, width, dtype=torch.uint8).cuda()
+        view, view_lens = plan_view(
+            torch.from_numpy(table).cuda(), torch.from_numpy(lens).cuda(), 16, torch.from_numpy(row_blocks).cuda(),
+            scores=torch.from_numpy(scores).cuda(), policy="sum", budget_fraction=fraction, recent_blocks=4,
+            cap_above_blocks=cap, measured=None if measured is None else torch.from_numpy(measured).cuda(),
+            mask_out=mask)
+        got_mask = mask.cpu().numpy()
+        for r in range(rows):
+            n = min(int(row_blocks[r]), width)
+            np.testing.assert_array_equal(got_mask[r, :n], keep[r, :n], err_msg=f"trial {trial} row {r}")
+        ref_view, ref_lens = ov.compact_block_table(table, lens, keep.astype(bool), 16)
+        np.testing.assert_array_equal(view.cpu().numpy(), ref_view, err_msg=f"trial {trial}")
+        np.testing.assert_array_equal(view_lens.cpu().numpy(), ref_lens, err_msg=f"trial {trial}")
+
+
+def _greedy_masks(scores, pinned, free):
+    """allocation.py:_greedy restated with NumPy for a large case (the oracle's per-cell sort is slow)."""
+    open_blocks = [np.flatnonzero(~p) for p in pinned]
+    index = np.concatenate(open_blocks)
+    gain = np.concatenate([oa.shares(s)[b] for s, b in zip(scores, open_blocks, strict=True)])
+    worst = -gain
+    threshold = np.partition(worst, free - 1)[free - 1]
+    selected = worst < threshold
+    ties = np.flatnonzero(worst == threshold)
+    selected[ties[np.argsort(-index[ties], kind="stable")][: free - int(selected.sum())]] = True
+    kept, start = [p.copy() for p in pinned], 0
+    for r, b in enumerate(open_blocks):
+        kept[r][b[selected[start : start + len(b)]]] = True
+        start += len(b)
+    return kept
+
+
+def test_sum_at_the_view_stress_size():
+    """1024 requests of up to 8192 blocks under one budget (4.2 M gains), against NumPy."""
+    from ekv.observe.allocation import sum_quotas
+    from ekv.runtime.block_view import _view_build
+
+    rng = np.random.default_rng(41)
+    rows, width = 1024, 8192
+    n = rng.integers(1, width + 1, rows)
+    scores = np.zeros((rows, width), dtype=np.float32)
+    for r in range(rows):
+        scores[r, : n[r]] = rng.dirichlet(np.full(n[r], 0.3)).astype(np.float32)
+    pinned = [oa.controller_pins(int(k), 4) for k in n]
+    must = sum(int(p.sum()) for p in pinned)
+    budget = max(must, int(math.ceil(0.3 * int(n.sum()))))
+    want = _greedy_masks([scores[r, : n[r]].astype(np.float64) for r in range(rows)], pinned, budget - must)
+    dev = torch.device("cuda")
+    s_t = torch.from_numpy(scores).to(dev)
+    nb = torch.from_numpy(n.astype(np.int32)).to(dev)
+    quota = torch.empty(rows, dtype=torch.int32, device=dev)
+    sum_quotas(s_t, nb, quota, measured=None, recent_blocks=4, cap_above_blocks=0, budget=budget)
+    table = torch.zeros(rows, width, dtype=torch.int32, device=dev)
+    mask = torch.empty(rows, width, dtype=torch.uint8, device=dev)
+    _view_build(table, (nb * 16).contiguous(), 16, row_blocks=nb, quota=quota, measured=None, recent_blocks=4,
+                scores=s_t, policy="sum", mask_out=mask)
+    got = mask.cpu().numpy()
+    for r in range(rows):
+        np.testing.assert_array_equal(got[r, : n[r]].astype(bool), want[r], err_msg=f"row {r}")
+    assert int(sum(int(got[r, : n[r]].sum()) for r in range(rows))) == budget
 
 
 @pytest.mark.parametrize("name", ["audit_cfg1_fp16", "audit_layers_fp16", "audit_g8_bf16"])

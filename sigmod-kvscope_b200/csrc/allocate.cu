@@ -10,17 +10,21 @@
 // choice is, per row, "the q_r best blocks by score, newer first on ties" with
 //   q_r = (its gains above the threshold) + (its share of the ties at the threshold),
 // which ekv_view_build then carries out. This file computes q_r:
-//   1. sum_prep_kernel, one CTA per row: total_r exactly as numpy.add.reduce computes it (pairwise
-//      over leaves of at most 128 values, eight accumulators per leaf), the pins, and, in the CTA
-//      that finishes last, the budget.
-//   2. sum_select_kernel, six launches: an MSB radix select of the `free`-th largest gain over the
-//      63-bit keys of the non-negative float64 gains (digits of 11 bits, the last of 8). Each CTA
-//      histograms its share of the blocks in shared memory and merges it; the CTA that finishes
-//      last picks the digit. No CTA waits for another.
-//   3. sum_ties_kernel, one CTA per row: gains above the threshold, and a count of the ties at each
-//      block index; the CTA that finishes last finds the index i* at which the ties needed run out
-//      (ties are taken from the highest index down).
-//   4. sum_quota_kernel, one CTA per row: q_r, with the ties at i* going to the earliest rows.
+//   1. sum_prep_kernel, one CTA per row (its scores staged in shared memory): total_r exactly as
+//      numpy.add.reduce computes it (pairwise over leaves of at most 128 values, eight accumulators
+//      per leaf), then the 63-bit key of every unpinned block's gain (the bits of the non-negative
+//      float64 gain) and the histogram of their first digits; the CTA that finishes last sets the
+//      budget and picks that digit.
+//   2. The rest of an MSB radix select of the `free`-th largest key (digits of 11 bits, the last of
+//      8): sum_keys_pass_kernel reads every key again, counts per row the keys above the first
+//      digit and moves the keys of that digit to a candidate list; passes 2-5 read the candidates
+//      only. Each CTA histograms in shared memory and merges; the CTA that finishes last picks the
+//      digit. No CTA waits for another.
+//   3. sum_ties_kernel over the candidates: keys above the threshold per row and ties per block
+//      index; the CTA that finishes last finds the index i* at which the ties needed run out (ties
+//      are taken from the highest index down) and how many of the ties at i* are taken.
+//   4. sum_kept_kernel over the candidates (ties above i*, rows tied at i*) and sum_quota_kernel, one
+//      CTA, which hands the ties at i* to the earliest rows and writes q_r.
 #include "ekv_common.cuh"
 #include "pins.cuh"
 
@@ -29,18 +33,22 @@ namespace ekv {
 constexpr int kSumThreads = 256;
 constexpr int kSumBins = 2048;
 constexpr int kSumPasses = 6;
-constexpr int kMaxLeaves = 512;  // leaves of a pairwise sum over up to 32768 values (each > 64 values)
+constexpr int kSumChunk = 2048;   // blocks of one row per CTA in the passes over every key
+constexpr int kMaxNodes = 1024;   // pairwise tree of up to 32768 values: at most 512 leaves (each > 64 values)
+constexpr int kMaxLevels = 16;
 constexpr int kSumMaxWidth = 32768;
+constexpr int kSumMaxRows = 1 << 17;  // a candidate's place is (row << 15) | block
 
 enum SumMode : int { kSumSelect = 0, kSumNone = 1, kSumAll = 2 };
 
 struct SumState {
   unsigned long long prefix, mask;  // the threshold's known bits
-  long long k;                      // gains still to choose at the threshold's prefix
+  long long k;                      // keys still to choose at the threshold's prefix
   long long total_open, must, blocks;
   int mode, found;
   int istar;       // the lowest block index whose ties are (partly) taken
   long long m;     // ties taken at istar, from the earliest rows
+  unsigned int n_cand;
   unsigned int ticket;
 };
 
@@ -57,17 +65,23 @@ struct SumParams {
   int32_t* quota;
   // workspace
   SumState* state;
-  double* total;       // [rows]
-  double* weight;      // [rows]
-  int* row_n;          // [rows] blocks of a request, 0 for a row that is not one
-  int* row_ps;         // [rows] pin start
-  int* row_gt;         // [rows] gains above the threshold
-  unsigned int* hist;  // [kSumBins]
-  unsigned int* ties;  // [width] ties at each block index
+  unsigned int* hist;        // [kSumBins]
+  unsigned int* ties;        // [width] ties at each block index
+  int* row_above;            // [rows] keys above the threshold
+  int* row_kept;             // [rows] ties above i*
+  int* row_at;               // [rows] 1: a tie at i*
+  double* total;             // [rows]
+  double* weight;            // [rows]
+  int* row_n;                // [rows] blocks of a request, 0 for a row that is not one
+  int* row_ps;               // [rows] pin start
+  unsigned long long* keys;  // [rows][width] keys of the unpinned blocks [1, ps)
+  unsigned long long* cand_key;  // [rows * width]
+  unsigned int* cand_at;         // [rows * width] (row << 15) | block
 };
 
 struct SumLayout {
-  size_t state, total, weight, row_n, row_ps, row_gt, hist, ties, bytes;
+  size_t state, hist, ties, row_above, row_kept, row_at, zeroed, total, weight, row_n, row_ps, keys, cand_key,
+      cand_at, bytes;
 };
 
 SumLayout sum_layout(int rows, int width) {
@@ -81,11 +95,17 @@ SumLayout sum_layout(int rows, int width) {
   l.state = take(sizeof(SumState));
   l.hist = take(kSumBins * 4);
   l.ties = take((size_t)width * 4);
+  l.row_above = take((size_t)rows * 4);
+  l.row_kept = take((size_t)rows * 4);
+  l.row_at = take((size_t)rows * 4);
+  l.zeroed = o;  // everything before this starts at zero
   l.total = take((size_t)rows * 8);
   l.weight = take((size_t)rows * 8);
   l.row_n = take((size_t)rows * 4);
   l.row_ps = take((size_t)rows * 4);
-  l.row_gt = take((size_t)rows * 4);
+  l.keys = take((size_t)rows * width * 8);
+  l.cand_key = take((size_t)rows * width * 8);
+  l.cand_at = take((size_t)rows * width * 4);
   l.bytes = o;
   return l;
 }
@@ -109,7 +129,7 @@ __device__ __forceinline__ void digit_of(int pass, int& shift, unsigned long lon
 // numpy's pairwise_sum of one leaf (at most 128 values): eight accumulators, combined as
 // ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)), then the rest one by one; below 8 values a plain
 // loop from 0.
-__device__ double leaf_sum(const float* x, int len) {
+__device__ double leaf_sum(const float* x, int len) {  // x: the row's scores in shared memory
   if (len < 8) {
     double res = 0.0;
     for (int i = 0; i < len; ++i) res += clamped(x[i]);
@@ -127,142 +147,32 @@ __device__ double leaf_sum(const float* x, int len) {
   return res;
 }
 
-// The pairwise tree above the leaves: a segment of more than 128 values splits at n2 = n / 2 rounded
-// down to a multiple of 8. Leaves are consumed left to right.
-__device__ double tree_sum(int len, const double* leaf, int& next) {
-  if (len <= 128) return leaf[next++];
-  int n2 = len / 2;
-  n2 -= n2 % 8;
-  const double a = tree_sum(n2, leaf, next);
-  const double b = tree_sum(len - n2, leaf, next);
-  return a + b;
-}
-
-// One CTA per row.
-__global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p) {
-  __shared__ int s_lo[kMaxLeaves], s_len[kMaxLeaves];
-  __shared__ double s_leaf[kMaxLeaves];
-  __shared__ int s_leaves;
-  __shared__ bool s_last;
-  const int r = blockIdx.x, tid = threadIdx.x;
-  int n = p.row_blocks[r];
-  const bool request = n > p.cap && n > 0;
-  if (n > p.width) n = p.width;
-  const float* x = p.scores + (int64_t)r * p.score_s0;
-  double total = 0.0;
-  if (request) {
-    if (tid == 0) {  // the leaves, left to right
-      int stack_lo[32], stack_len[32], top = 0, count = 0;
-      stack_lo[0] = 0;
-      stack_len[0] = n;
-      top = 1;
-      while (top > 0) {
-        --top;
-        const int lo = stack_lo[top], len = stack_len[top];
-        if (len <= 128) {
-          s_lo[count] = lo;
-          s_len[count] = len;
-          ++count;
-        } else {
-          int n2 = len / 2;
-          n2 -= n2 % 8;
-          stack_lo[top] = lo + n2, stack_len[top] = len - n2, ++top;  // right half, popped second
-          stack_lo[top] = lo, stack_len[top] = n2, ++top;             // left half, popped first
-        }
-      }
-      s_leaves = count;
-    }
-    __syncthreads();
-    for (int i = tid; i < s_leaves; i += kSumThreads) s_leaf[i] = leaf_sum(x + s_lo[i], s_len[i]);
-    __syncthreads();
-    if (tid == 0) {
-      int next = 0;
-      total = tree_sum(n, s_leaf, next);
-    }
-  }
-  if (tid == 0) {
-    int ps = 0;
-    if (request) {
-      ps = pin_start(n, p.recent, p.measured, r);
-      atomicAdd((unsigned long long*)&p.state->total_open, (unsigned long long)(ps > 1 ? ps - 1 : 0));
-      atomicAdd((unsigned long long*)&p.state->must, (unsigned long long)pin_count(n, ps));
-      atomicAdd((unsigned long long*)&p.state->blocks, (unsigned long long)n);
-    }
-    p.total[r] = total;
-    p.weight[r] = p.weights ? p.weights[r] : 1.0;
-    p.row_n[r] = request ? n : 0;
-    p.row_ps[r] = ps;
-    __threadfence();
-    s_last = atomicAdd(&p.state->ticket, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!s_last || tid != 0) return;
-  // the budget (controller.py:435-437) and what to do with it (allocation.py:64-67, :98-104)
+// Whether this CTA is the last of the grid to get here (after its writes are fenced).
+__device__ __forceinline__ bool last_cta(unsigned int* ticket, bool* s_last) {
   __threadfence();
-  SumState* st = p.state;
-  const long long must = *(volatile long long*)&st->must, blocks = *(volatile long long*)&st->blocks;
-  const long long total_open = *(volatile long long*)&st->total_open;
-  long long budget = p.budget;
-  if (budget < 0) {
-    budget = (long long)ceil(p.fraction * (double)blocks);
-    if (budget < must) budget = must;
-  }
-  const long long free_ = budget - must;
-  if (budget >= blocks || free_ >= total_open) {
-    st->mode = kSumAll;
-  } else if (free_ <= 0) {
-    st->mode = kSumNone;
-  } else {
-    st->mode = kSumSelect;
-    st->k = free_;
-  }
-  st->prefix = 0;
-  st->mask = 0;
-  st->found = 0;
-  st->ticket = 0;
+  __syncthreads();
+  if (threadIdx.x == 0) *s_last = atomicAdd(ticket, 1u) == gridDim.x * gridDim.y - 1;
+  __syncthreads();
+  if (*s_last) __threadfence();
+  return *s_last;
 }
 
-// One pass of the radix select; the grid strides over every (row, block).
-__global__ void __launch_bounds__(kSumThreads) sum_select_kernel(const SumParams p, int pass) {
-  __shared__ unsigned int s_hist[kSumBins];
-  __shared__ bool s_last;
+// In the last CTA: the digit holding the k-th largest of the keys counted in `hist` (thread t owns
+// bins [8t, 8t + 8)); clears `hist` and updates the threshold. kSumThreads * 8 == kSumBins.
+__device__ void pick_digit(SumState* st, unsigned int* hist, int pass) {
+  __shared__ long long s_w[kSumThreads / 32];
   __shared__ int s_pick;
   __shared__ long long s_above;
   __shared__ unsigned int s_count;
-  __shared__ long long s_w[kSumThreads / 32];
-  const int tid = threadIdx.x;
-  SumState* st = p.state;
-  if (st->mode != kSumSelect || st->found) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int shift;
   unsigned long long dmask;
   digit_of(pass, shift, dmask);
-  const unsigned long long prefix = st->prefix, mask = st->mask;
-  for (int i = tid; i < kSumBins; i += kSumThreads) s_hist[i] = 0;
-  __syncthreads();
-  const long long cells = (long long)p.rows * p.width;
-  for (long long e = (long long)blockIdx.x * kSumThreads + tid; e < cells; e += (long long)gridDim.x * kSumThreads) {
-    const int r = (int)(e / p.width), b = (int)(e - (long long)r * p.width);
-    const int n = p.row_n[r];
-    if (n == 0 || b < 1 || b >= p.row_ps[r]) continue;
-    const unsigned long long key = gain_key(p.scores[(int64_t)r * p.score_s0 + b], p.total[r], p.weight[r], n);
-    if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & dmask], 1u);
-  }
-  __syncthreads();
-  for (int i = tid; i < kSumBins; i += kSumThreads)
-    if (s_hist[i]) atomicAdd(&p.hist[i], s_hist[i]);
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&st->ticket, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  // the CTA that finished last: the digit of the k-th largest key; thread t owns bins [8t, 8t + 8)
   unsigned int h[8];
   long long sum = 0;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) h[j] = __ldcg(p.hist + 8 * tid + j), sum += h[j];
-  const int warp = tid >> 5, lane = tid & 31;
-  long long above = sum;  // this thread's bins and the bins of the lanes above it
+  for (int j = 0; j < 8; ++j) h[j] = __ldcg(hist + 8 * tid + j), sum += h[j];
+  long long above = sum;  // this thread's bins and those of the lanes above it
   for (int off = 1; off < 32; off <<= 1) {
     const long long v = __shfl_down_sync(kFullMask, above, off);
     if (lane + off < 32) above += v;
@@ -283,50 +193,252 @@ __global__ void __launch_bounds__(kSumThreads) sum_select_kernel(const SumParams
   }
   __syncthreads();
 #pragma unroll
-  for (int j = 0; j < 8; ++j) p.hist[8 * tid + j] = 0;  // ready for the next pass
+  for (int j = 0; j < 8; ++j) hist[8 * tid + j] = 0;  // ready for the next pass
   if (tid == 0) {
     const long long k2 = k - s_above;
-    st->prefix = prefix | ((unsigned long long)s_pick << shift);
-    st->mask = mask | (dmask << shift);
+    st->prefix |= (unsigned long long)s_pick << shift;
+    st->mask |= dmask << shift;
     st->k = k2;
     st->found = (long long)s_count == k2 || pass == kSumPasses - 1;  // every key with the prefix is taken
-    st->ticket = 0;
   }
 }
 
-// One CTA per row: gains above the threshold, ties per block index; the CTA that finishes last finds
-// i*, the lowest block index of the ties taken, and m, the ties taken there.
+// One CTA per row: the total, the keys, the pins; the CTA that finishes last sets the budget.
+//
+// The total follows numpy's pairwise_sum tree: a segment of more than 128 values splits at
+// n2 = n / 2 rounded down to a multiple of 8, and its sum is sum(left) + sum(right). The tree is
+// built one level at a time (every node of a level splits in parallel and records its children),
+// the leaves are summed in parallel, and the levels are combined from the bottom up: the same
+// additions in the same order as numpy's recursion.
+__global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p) {
+  extern __shared__ float s_x[];  // [width]: the row's scores
+  __shared__ unsigned int s_hist[kSumBins];
+  __shared__ int s_lo[kMaxNodes], s_len[kMaxNodes], s_left[kMaxNodes];
+  __shared__ double s_val[kMaxNodes];
+  __shared__ int s_level[kMaxLevels + 2];
+  __shared__ int s_nodes, s_depth;
+  __shared__ double s_total;
+  __shared__ bool s_last;
+  const int r = blockIdx.x, tid = threadIdx.x;
+  int n = p.row_blocks[r];
+  const bool request = n > p.cap && n > 0;
+  if (n > p.width) n = p.width;
+  const float* xg = p.scores + (int64_t)r * p.score_s0;
+  const int ps = request ? pin_start(n, p.recent, p.measured, r) : 0;
+  const double w = p.weights ? p.weights[r] : 1.0;
+  for (int i = tid; i < kSumBins; i += kSumThreads) s_hist[i] = 0;
+  if (request) {
+    for (int i = tid; i < n; i += kSumThreads) s_x[i] = xg[i];
+    if (tid == 0) {
+      s_lo[0] = 0, s_len[0] = n, s_nodes = 1, s_level[0] = 0, s_level[1] = 1, s_depth = 1;
+    }
+    __syncthreads();
+    for (int d = 0; d < kMaxLevels; ++d) {  // split the level's nodes; children go after the level
+      const int a = s_level[d], b = s_level[d + 1];
+      if (a == b) break;
+      for (int i = a + tid; i < b; i += kSumThreads) {
+        const int lo = s_lo[i], len = s_len[i];
+        if (len <= 128) {
+          s_left[i] = -1;
+        } else {
+          int n2 = len / 2;
+          n2 -= n2 % 8;
+          const int c = atomicAdd(&s_nodes, 2);
+          s_lo[c] = lo, s_len[c] = n2, s_lo[c + 1] = lo + n2, s_len[c + 1] = len - n2;
+          s_left[i] = c;
+        }
+      }
+      __syncthreads();
+      if (tid == 0) s_level[d + 2] = s_nodes, s_depth = d + 1;
+      __syncthreads();
+    }
+    for (int i = tid; i < s_nodes; i += kSumThreads)
+      if (s_left[i] < 0) s_val[i] = leaf_sum(s_x + s_lo[i], s_len[i]);
+    __syncthreads();
+    for (int d = s_depth - 1; d >= 0; --d) {  // each inner node: left + right, deepest level first
+      for (int i = s_level[d] + tid; i < s_level[d + 1]; i += kSumThreads)
+        if (s_left[i] >= 0) s_val[i] = s_val[s_left[i]] + s_val[s_left[i] + 1];
+      __syncthreads();
+    }
+    if (tid == 0) s_total = s_val[0];
+    __syncthreads();
+    const double total = s_total;
+    unsigned long long* kr = p.keys + (int64_t)r * p.width;
+    int shift0;
+    unsigned long long dmask0;
+    digit_of(0, shift0, dmask0);
+    for (int base = 1; base < ps; base += kSumThreads) {  // the keys and pass 0 of the select
+      const int b = base + tid;  // (warp-uniform trip count)
+      unsigned int digit = kSumBins;
+      if (b < ps) {
+        const unsigned long long key = gain_key(s_x[b], total, w, n);
+        kr[b] = key;
+        digit = (unsigned int)((key >> shift0) & dmask0);
+      }
+      // the keys of a row share a few exponents: one shared-memory atomic per digit and warp
+      const unsigned int same = __match_any_sync(kFullMask, digit);
+      if (digit < kSumBins && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&s_hist[digit], __popc(same));
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < kSumBins; i += kSumThreads)
+    if (s_hist[i]) atomicAdd(&p.hist[i], s_hist[i]);
+  if (tid == 0) {
+    if (request) {
+      atomicAdd((unsigned long long*)&p.state->total_open, (unsigned long long)(ps > 1 ? ps - 1 : 0));
+      atomicAdd((unsigned long long*)&p.state->must, (unsigned long long)pin_count(n, ps));
+      atomicAdd((unsigned long long*)&p.state->blocks, (unsigned long long)n);
+    }
+    p.total[r] = request ? s_total : 0.0;
+    p.weight[r] = w;
+    p.row_n[r] = request ? n : 0;
+    p.row_ps[r] = ps;
+  }
+  if (!last_cta(&p.state->ticket, &s_last)) return;
+  // the budget (controller.py:435-437) and what to do with it (allocation.py:64-67, :98-104)
+  SumState* st = p.state;
+  if (tid == 0) {
+    const long long must = *(volatile long long*)&st->must, blocks = *(volatile long long*)&st->blocks;
+    const long long total_open = *(volatile long long*)&st->total_open;
+    long long budget = p.budget;
+    if (budget < 0) {
+      budget = (long long)ceil(p.fraction * (double)blocks);
+      if (budget < must) budget = must;
+    }
+    const long long free_ = budget - must;
+    if (budget >= blocks || free_ >= total_open) {
+      st->mode = kSumAll;
+    } else if (free_ <= 0) {
+      st->mode = kSumNone;
+    } else {
+      st->mode = kSumSelect;
+      st->k = free_;
+    }
+    st->ticket = 0;
+  }
+  __syncthreads();
+  if (st->mode == kSumSelect) pick_digit(st, p.hist, 0);  // pass 0 of the select
+}
+
+// Pass 1 over every key: grid (width / kSumChunk, rows). It counts each row's keys above the digit of
+// pass 0 and moves the keys of that digit to the candidates (each CTA's in one piece).
+__global__ void __launch_bounds__(kSumThreads) sum_keys_pass_kernel(const SumParams p) {
+  constexpr int pass = 1;
+  __shared__ unsigned int s_hist[kSumBins];
+  __shared__ unsigned long long s_ckey[kSumChunk];  // this CTA's candidates, moved out in one piece
+  __shared__ unsigned int s_cat[kSumChunk];
+  __shared__ unsigned int s_ncand, s_base;
+  __shared__ int s_above;
+  __shared__ bool s_last;
+  const int tid = threadIdx.x, lane = tid & 31, r = blockIdx.y;
+  SumState* st = p.state;
+  if (st->mode != kSumSelect) return;  // (uniform over the grid)
+  const bool histogram = !st->found;
+  int shift;
+  unsigned long long dmask;
+  digit_of(pass, shift, dmask);
+  const unsigned long long prefix = st->prefix;
+  int shift0;
+  unsigned long long dmask0;
+  digit_of(0, shift0, dmask0);
+  for (int i = tid; i < kSumBins; i += kSumThreads) s_hist[i] = 0;
+  if (tid == 0) s_above = 0, s_ncand = 0;
+  __syncthreads();
+  const int n = p.row_n[r], ps = p.row_ps[r];
+  const unsigned long long* kr = p.keys + (int64_t)r * p.width;
+  const int lo = 1 + blockIdx.x * kSumChunk, hi = min(lo + kSumChunk, ps);
+  int above = 0;
+  if (n > 0) {
+    for (int base = lo; base < hi; base += kSumThreads) {  // warp-uniform trip count
+      const int b = base + tid;
+      const bool in = b < hi;
+      const unsigned long long key = in ? kr[b] : 0ull;
+      // the prefix is pass 0's digit
+      const unsigned long long top = key & (dmask0 << shift0);
+      const bool cand = in && top == (prefix & (dmask0 << shift0));
+      above += in && top > (prefix & (dmask0 << shift0));
+      if (cand && histogram) atomicAdd(&s_hist[(key >> shift) & dmask], 1u);
+      const unsigned int ballot = __ballot_sync(kFullMask, cand);
+      if (ballot) {
+        unsigned int at = 0;
+        if (lane == 0) at = atomicAdd(&s_ncand, (unsigned int)__popc(ballot));
+        at = __shfl_sync(kFullMask, at, 0) + __popc(ballot & ((1u << lane) - 1u));
+        if (cand) {
+          s_ckey[at] = key;
+          s_cat[at] = ((unsigned int)r << 15) | (unsigned int)b;
+        }
+      }
+    }
+  }
+  for (int off = 16; off > 0; off >>= 1) above += __shfl_xor_sync(kFullMask, above, off);
+  if (lane == 0 && above) atomicAdd(&s_above, above);
+  __syncthreads();
+  if (tid == 0) {
+    if (s_above) atomicAdd(&p.row_above[r], s_above);
+    s_base = s_ncand ? atomicAdd(&st->n_cand, s_ncand) : 0u;
+  }
+  __syncthreads();
+  for (unsigned int i = tid; i < s_ncand; i += kSumThreads) {
+    p.cand_key[s_base + i] = s_ckey[i];
+    p.cand_at[s_base + i] = s_cat[i];
+  }
+  if (histogram)
+    for (int i = tid; i < kSumBins; i += kSumThreads)
+      if (s_hist[i]) atomicAdd(&p.hist[i], s_hist[i]);
+  if (!last_cta(&st->ticket, &s_last)) return;
+  if (histogram) pick_digit(st, p.hist, pass);
+  if (tid == 0) st->ticket = 0;
+}
+
+// Passes 2-5 over the candidates (the keys with pass 0's digit).
+__global__ void __launch_bounds__(kSumThreads) sum_cand_pass_kernel(const SumParams p, int pass) {
+  __shared__ unsigned int s_hist[kSumBins];
+  __shared__ bool s_last;
+  const int tid = threadIdx.x;
+  SumState* st = p.state;
+  if (st->mode != kSumSelect || st->found) return;
+  int shift;
+  unsigned long long dmask;
+  digit_of(pass, shift, dmask);
+  const unsigned long long prefix = st->prefix, mask = st->mask;
+  for (int i = tid; i < kSumBins; i += kSumThreads) s_hist[i] = 0;
+  __syncthreads();
+  const unsigned int count = st->n_cand;
+  for (unsigned int i = blockIdx.x * kSumThreads + tid; i < count; i += gridDim.x * kSumThreads) {
+    const unsigned long long key = p.cand_key[i];
+    if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & dmask], 1u);
+  }
+  __syncthreads();
+  for (int i = tid; i < kSumBins; i += kSumThreads)
+    if (s_hist[i]) atomicAdd(&p.hist[i], s_hist[i]);
+  if (!last_cta(&st->ticket, &s_last)) return;
+  pick_digit(st, p.hist, pass);
+  if (tid == 0) st->ticket = 0;
+}
+
+// Over the candidates: keys above the threshold per row, ties per block index; the CTA that
+// finishes last finds i*, the lowest block index of the ties taken, and m, the ties taken there.
 __global__ void __launch_bounds__(kSumThreads) sum_ties_kernel(const SumParams p) {
   __shared__ long long s_w[kSumThreads / 32];
   __shared__ bool s_last;
-  const int r = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   SumState* st = p.state;
   if (st->mode != kSumSelect) return;
   const unsigned long long prefix = st->prefix, mask = st->mask;
-  const int n = p.row_n[r], ps = p.row_ps[r];
-  long long gt = 0;
-  if (n > 0) {
-    const float* x = p.scores + (int64_t)r * p.score_s0;
-    const double total = p.total[r], w = p.weight[r];
-    for (int b = 1 + tid; b < ps; b += kSumThreads) {
-      const unsigned long long key = gain_key(x[b], total, w, n) & mask;
-      if (key > prefix) ++gt;
-      else if (key == prefix) atomicAdd(&p.ties[b], 1u);
-    }
+  const unsigned int count = st->n_cand;
+  for (unsigned int base = blockIdx.x * kSumThreads; base < count; base += gridDim.x * kSumThreads) {
+    const unsigned int i = base + tid;  // (warp-uniform trip count)
+    const bool in = i < count;
+    const unsigned long long key = in ? p.cand_key[i] & mask : 0ull;
+    const unsigned int at = in ? p.cand_at[i] : 0u;
+    const bool up = in && key > prefix;
+    // a CTA of the keys pass moved one row's candidates together: count a row once per warp
+    const unsigned int row = up ? at >> 15 : 0xffffffffu;
+    const unsigned int same = __match_any_sync(kFullMask, row);
+    if (up && lane == __ffs(same) - 1) atomicAdd(&p.row_above[row], __popc(same));
+    if (in && key == prefix) atomicAdd(&p.ties[at & 32767u], 1u);
   }
-  for (int off = 16; off > 0; off >>= 1) gt += __shfl_xor_sync(kFullMask, gt, off);
-  if (lane == 0) s_w[warp] = gt;
-  __syncthreads();
-  if (tid == 0) {
-    long long t = 0;
-    for (int w2 = 0; w2 < kSumThreads / 32; ++w2) t += s_w[w2];
-    p.row_gt[r] = (int)t;
-    __threadfence();
-    s_last = atomicAdd(&st->ticket, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
+  if (!last_cta(&st->ticket, &s_last)) return;
   // ties are taken from the highest block index down; thread t owns indices [t * per, t * per + per)
   const int per = (p.width + kSumThreads - 1) / kSumThreads;
   const int lo = tid * per, hi = min(lo + per, p.width);
@@ -337,7 +449,6 @@ __global__ void __launch_bounds__(kSumThreads) sum_ties_kernel(const SumParams p
     const long long v = __shfl_down_sync(kFullMask, above, off);
     if (lane + off < 32) above += v;
   }
-  __syncthreads();
   if (lane == 0) s_w[warp] = above;
   __syncthreads();
   long long taken = above - cnt;  // ties at indices >= hi
@@ -357,47 +468,50 @@ __global__ void __launch_bounds__(kSumThreads) sum_ties_kernel(const SumParams p
   if (tid == 0) st->ticket = 0;
 }
 
-// One CTA per row: its quota of unpinned blocks for ekv_view_build (-1: not a request, read in full).
-__global__ void __launch_bounds__(kSumThreads) sum_quota_kernel(const SumParams p) {
-  __shared__ long long s_w[kSumThreads / 32];
-  const int r = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+// Over the candidates: each row's ties above i* and whether it ties at i*.
+__global__ void __launch_bounds__(kSumThreads) sum_kept_kernel(const SumParams p) {
+  const int tid = threadIdx.x;
   const SumState* st = p.state;
-  const int n = p.row_n[r], ps = p.row_ps[r];
-  const int open = ps > 1 ? ps - 1 : 0;
-  if (n == 0 || st->mode != kSumSelect) {
-    if (tid == 0) p.quota[r] = n == 0 ? -1 : (st->mode == kSumAll ? open : 0);
-    return;
-  }
+  if (st->mode != kSumSelect) return;
   const unsigned long long prefix = st->prefix, mask = st->mask;
-  const int istar = st->istar;
+  const unsigned int istar = (unsigned int)st->istar, count = st->n_cand;
+  const int lane = tid & 31;
+  for (unsigned int base = blockIdx.x * kSumThreads; base < count; base += gridDim.x * kSumThreads) {
+    const unsigned int i = base + tid;  // (warp-uniform trip count)
+    const bool tie = i < count && (p.cand_key[i] & mask) == prefix;
+    const unsigned int at = tie ? p.cand_at[i] : 0u, b = at & 32767u, r = at >> 15;
+    const bool above = tie && b > istar;
+    const unsigned int same = __match_any_sync(kFullMask, above ? r : 0xffffffffu);
+    if (above && lane == __ffs(same) - 1) atomicAdd(&p.row_kept[r], __popc(same));
+    if (tie && b == istar) p.row_at[r] = 1;
+  }
+}
+
+// One CTA: the quotas; the m ties at i* go to the earliest rows that tie there.
+__global__ void __launch_bounds__(1024) sum_quota_kernel(const SumParams p) {
+  __shared__ int s_scan[1024 / 32 + 1];
+  const int tid = threadIdx.x;
+  const SumState* st = p.state;
+  const int mode = st->mode;
   const long long m = st->m;
-  // this row's ties above i*, and the rows before it that tie at i*
-  long long mine = 0, before = 0;
-  const float* x = p.scores + (int64_t)r * p.score_s0;
-  for (int b = istar + 1 + tid; b < ps; b += kSumThreads)
-    mine += (gain_key(x[b], p.total[r], p.weight[r], n) & mask) == prefix;
-  for (int q = tid; q < r; q += kSumThreads) {
-    const int nq = p.row_n[q];
-    if (nq > 0 && istar >= 1 && istar < p.row_ps[q])
-      before += (gain_key(p.scores[(int64_t)q * p.score_s0 + istar], p.total[q], p.weight[q], nq) & mask) == prefix;
-  }
-  for (int off = 16; off > 0; off >>= 1) {
-    mine += __shfl_xor_sync(kFullMask, mine, off);
-    before += __shfl_xor_sync(kFullMask, before, off);
-  }
-  if (lane == 0) s_w[warp] = mine;
-  __syncthreads();
-  long long t_mine = 0;
-  for (int w2 = 0; w2 < kSumThreads / 32; ++w2) t_mine += s_w[w2];
-  __syncthreads();
-  if (lane == 0) s_w[warp] = before;
-  __syncthreads();
-  if (tid == 0) {
-    long long t_before = 0;
-    for (int w2 = 0; w2 < kSumThreads / 32; ++w2) t_before += s_w[w2];
-    const bool tie_here =
-        istar >= 1 && istar < ps && (gain_key(x[istar], p.total[r], p.weight[r], n) & mask) == prefix;
-    p.quota[r] = (int)(p.row_gt[r] + t_mine + (tie_here && t_before < m ? 1 : 0));
+  int carry = 0;
+  for (int base = 0; base < p.rows; base += 1024) {
+    const int r = base + tid;
+    const bool in = r < p.rows;
+    const int n = in ? p.row_n[r] : 0;
+    const int at = in && n > 0 && mode == kSumSelect ? p.row_at[r] : 0;
+    int total = 0;
+    const int before = carry + block_exclusive_scan<1024>(at, s_scan, &total);
+    carry += total;
+    if (!in) continue;
+    if (n == 0) {
+      p.quota[r] = -1;  // not a request: it reads in full
+    } else if (mode != kSumSelect) {
+      const int ps = p.row_ps[r];
+      p.quota[r] = mode == kSumAll ? (ps > 1 ? ps - 1 : 0) : 0;
+    } else {
+      p.quota[r] = p.row_above[r] + p.row_kept[r] + (at && before < m ? 1 : 0);
+    }
   }
 }
 
@@ -418,6 +532,7 @@ extern "C" int ekv_allocate_sum(const float* scores, int64_t score_stride, const
   if (!scores || !row_blocks || !quota) return fail(EKV_EINVAL, "a required pointer is NULL");
   if (rows <= 0 || width <= 0) return fail(EKV_EINVAL, "rows and width must be positive");
   if (width > kSumMaxWidth) return fail(EKV_ENOTSUP, "width %d > %d", width, kSumMaxWidth);
+  if (rows > kSumMaxRows) return fail(EKV_ENOTSUP, "rows %d > %d", rows, kSumMaxRows);
   if (score_stride < width) return fail(EKV_EINVAL, "score_stride %lld < width %d", (long long)score_stride, width);
   if (recent_blocks < -1 || cap_above_blocks < -1) return fail(EKV_EINVAL, "invalid controller settings");
   if (budget < 0 && !(budget_fraction > 0.0 && budget_fraction <= 1.0))
@@ -434,32 +549,46 @@ extern "C" int ekv_allocate_sum(const float* scores, int64_t score_stride, const
   p.state = reinterpret_cast<SumState*>(base + l.state);
   p.hist = reinterpret_cast<unsigned int*>(base + l.hist);
   p.ties = reinterpret_cast<unsigned int*>(base + l.ties);
+  p.row_above = reinterpret_cast<int*>(base + l.row_above);
+  p.row_kept = reinterpret_cast<int*>(base + l.row_kept);
+  p.row_at = reinterpret_cast<int*>(base + l.row_at);
   p.total = reinterpret_cast<double*>(base + l.total);
   p.weight = reinterpret_cast<double*>(base + l.weight);
   p.row_n = reinterpret_cast<int*>(base + l.row_n);
   p.row_ps = reinterpret_cast<int*>(base + l.row_ps);
-  p.row_gt = reinterpret_cast<int*>(base + l.row_gt);
+  p.keys = reinterpret_cast<unsigned long long*>(base + l.keys);
+  p.cand_key = reinterpret_cast<unsigned long long*>(base + l.cand_key);
+  p.cand_at = reinterpret_cast<unsigned int*>(base + l.cand_at);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // the state, the histogram and the tie counts start at zero (they precede the per-row arrays)
-  if (cudaMemsetAsync(base, 0, l.total, s) != cudaSuccess) return check_launch("cudaMemsetAsync(sum workspace)");
+  if (cudaMemsetAsync(base, 0, l.zeroed, s) != cudaSuccess) return check_launch("cudaMemsetAsync(sum workspace)");
   int device = 0, sms = 0;
-  if (cudaGetDevice(&device) != cudaSuccess ||
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
     return check_launch("cudaDeviceGetAttribute");
-  sum_prep_kernel<<<rows, kSumThreads, 0, s>>>(p);
-  int rc = check_launch("sum_prep_kernel");
-  if (rc != EKV_OK) return rc;
-  const long long cells = (long long)rows * width;
-  const long long want = (cells + kSumThreads * 8 - 1) / (kSumThreads * 8);
-  const int grid = (int)(want < 8LL * sms ? (want > 0 ? want : 1) : 8LL * sms);
-  for (int pass = 0; pass < kSumPasses; ++pass) {
-    sum_select_kernel<<<grid, kSumThreads, 0, s>>>(p, pass);
-    rc = check_launch("sum_select_kernel");
-    if (rc != EKV_OK) return rc;
+  const size_t prep_smem = (size_t)width * sizeof(float);
+  static size_t configured[kMaxDevices] = {};
+  if (configured[device] < prep_smem) {
+    if (cudaFuncSetAttribute(sum_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem) !=
+        cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(sum_prep_kernel)");
+    configured[device] = prep_smem;
   }
-  sum_ties_kernel<<<rows, kSumThreads, 0, s>>>(p);
-  rc = check_launch("sum_ties_kernel");
+  sum_prep_kernel<<<rows, kSumThreads, prep_smem, s>>>(p);
+  int rc = check_launch("sum_prep_kernel");
+  if (rc == EKV_OK) {
+    sum_keys_pass_kernel<<<dim3(cdiv(width, kSumChunk), rows), kSumThreads, 0, s>>>(p);
+    rc = check_launch("sum_keys_pass_kernel");
+  }
+  const int cand_grid = 2 * sms;
+  for (int pass = 2; pass < kSumPasses && rc == EKV_OK; ++pass) {
+    sum_cand_pass_kernel<<<cand_grid, kSumThreads, 0, s>>>(p, pass);
+    rc = check_launch("sum_cand_pass_kernel");
+  }
   if (rc != EKV_OK) return rc;
-  sum_quota_kernel<<<rows, kSumThreads, 0, s>>>(p);
+  sum_ties_kernel<<<cand_grid, kSumThreads, 0, s>>>(p);
+  if ((rc = check_launch("sum_ties_kernel")) != EKV_OK) return rc;
+  sum_kept_kernel<<<cand_grid, kSumThreads, 0, s>>>(p);
+  if ((rc = check_launch("sum_kept_kernel")) != EKV_OK) return rc;
+  sum_quota_kernel<<<1, 1024, 0, s>>>(p);
   return check_launch("sum_quota_kernel");
 }

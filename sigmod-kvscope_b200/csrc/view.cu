@@ -107,16 +107,67 @@ __global__ void __launch_bounds__(kQuotaThreads) quota_kernel(const QuotaParams 
   if (keep_all) return;
   assigned = block_sum_ll(assigned, s_red);  // (its __syncthreads also publishes s_rem)
   const long long extra = free_ - assigned;
-  // The `extra` largest remainders get one more block; equal remainders go to the earlier row.
-  for (int r = threadIdx.x; r < R; r += kQuotaThreads) {
-    const double mine = s_rem[r];
-    if (mine < 0.0) continue;
-    long long rank = 0;
-    for (int i = 0; i < R; ++i) {
-      const double other = s_rem[i];
-      rank += other > mine || (other == mine && other >= 0.0 && i < r);
+  if (extra <= 0) return;
+  // The `extra` largest remainders get one more block; equal remainders go to the earlier row
+  // (allocation.py:85). The remainders are non-negative doubles, so their bits order them: a radix
+  // select over 63-bit keys (digits of 11 bits, the last of 8) finds the extra-th largest.
+  __shared__ int s_hist[2048];
+  __shared__ int s_pick[3];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned long long prefix = 0, mask = 0;
+  long long k = extra;
+  for (int pass = 0; pass < 6; ++pass) {
+    const int shift = pass < 5 ? 52 - 11 * pass : 0;
+    const unsigned long long dmask = pass < 5 ? 2047ull : 255ull;
+    for (int i = threadIdx.x; i < 2048; i += kQuotaThreads) s_hist[i] = 0;
+    __syncthreads();
+    for (int r = threadIdx.x; r < R; r += kQuotaThreads) {
+      if (s_rem[r] < 0.0) continue;  // not a request
+      const unsigned long long key = (unsigned long long)__double_as_longlong(s_rem[r]);
+      if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & dmask], 1);
     }
-    if (rank < extra) p.quota[r] += 1;
+    __syncthreads();
+    // thread t owns bins 2t and 2t + 1; the count of keys in the bins above it, from the top
+    const int h0 = s_hist[2 * threadIdx.x], h1 = s_hist[2 * threadIdx.x + 1];
+    const long long sum = (long long)h0 + h1;
+    long long above = sum;
+    for (int off = 1; off < 32; off <<= 1) {
+      const long long v = __shfl_down_sync(kFullMask, above, off);
+      if (lane + off < 32) above += v;
+    }
+    __syncthreads();
+    if (lane == 0) s_red[warp] = above;
+    __syncthreads();
+    long long gt = above - sum;
+    for (int w2 = warp + 1; w2 < kQuotaThreads / 32; ++w2) gt += s_red[w2];
+    if (gt < k && gt + h1 >= k) s_pick[0] = 2 * threadIdx.x + 1, s_pick[1] = (int)gt, s_pick[2] = h1;
+    gt += h1;
+    if (gt < k && gt + h0 >= k) s_pick[0] = 2 * threadIdx.x, s_pick[1] = (int)gt, s_pick[2] = h0;
+    __syncthreads();
+    k -= s_pick[1];
+    prefix |= (unsigned long long)s_pick[0] << shift;
+    mask |= dmask << shift;
+    const bool done = s_pick[2] == k;  // every key with the prefix is taken
+    __syncthreads();
+    if (done) break;
+  }
+  // keys above the threshold get one more; of the keys equal to it, the first k in row order
+  int carry = 0;
+  for (int base = 0; base < R; base += kQuotaThreads) {
+    const int r = base + threadIdx.x;
+    bool tie = false, up = false;
+    if (r < R && s_rem[r] >= 0.0) {
+      const unsigned long long key = (unsigned long long)__double_as_longlong(s_rem[r]) & mask;
+      up = key > prefix;
+      tie = key == prefix;
+    }
+    long long tie_rank = 0;
+    {
+      int total = 0;
+      tie_rank = carry + block_exclusive_scan<kQuotaThreads>(tie ? 1 : 0, reinterpret_cast<int*>(s_red), &total);
+      carry += total;
+    }
+    if (up || (tie && tie_rank < k)) p.quota[r] += 1;
   }
 }
 

@@ -93,6 +93,25 @@ def test_allocate_against_the_oracle_with_many_ties():
             np.testing.assert_array_equal(a, b, err_msg=f"trial {trial}")
 
 
+def test_uniform_quotas_over_thousands_of_requests():
+    """Largest remainders over ~2000 requests of a few sizes: many equal remainders, which go to the
+    earlier request (allocation.py:85)."""
+    from ekv.observe.allocation import Request, allocate
+
+    rng = np.random.default_rng(29)
+    for trial in range(4):
+        n_req = int(rng.integers(1500, 2500))
+        sizes = rng.choice([3, 7, 12, 40], n_req)
+        scores = [rng.integers(0, 3, n).astype(np.float64) for n in sizes]
+        pinned = [oa.controller_pins(int(n), 1) for n in sizes]
+        must = sum(int(p.sum()) for p in pinned)
+        budget = int(rng.integers(must + 1, int(sizes.sum())))
+        got = allocate([Request(scores=x, pinned=p) for x, p in zip(scores, pinned, strict=True)], budget, "uniform")
+        want = oa.allocate(scores, budget, "uniform", pinned)
+        for r, (a, b) in enumerate(zip(got, want, strict=True)):
+            np.testing.assert_array_equal(a, b, err_msg=f"trial {trial}, request {r}")
+
+
 def test_sum_over_many_requests_against_the_oracle():
     """The global greedy: ties across requests (newer block, then earlier request), weights, requests
     without evidence, and budgets from just above the pins to just below every block."""

@@ -277,8 +277,35 @@ def view_bench(rank: int, world: int, steps: int, warmup: int, dist_on: bool) ->
     def build_newest():  # keep-newest: scores = arange(n) under `uniform`, budget 0.5
         plan_view(t, ln, BLOCK, nn, scores=newest, policy="uniform", budget_fraction=0.5, recent_blocks=0, out=out)
 
+    # SGLang's CSR list: 256 decode rows of U[1, 8192] tokens (int64 slots), half the blocks kept
+    from ekv.runtime.sglang_compact import SlotCompactor
+
+    slot_rows, slot_width = 256, 512
+    sl_lens = torch.randint(1, slot_width * BLOCK + 1, (slot_rows,), generator=gen)
+    sl_indptr = torch.cat([torch.zeros(1, dtype=torch.int64), sl_lens.cumsum(0)]).to(torch.int32).to(dev)
+    entries = int(sl_lens.sum())
+    sl_slots = torch.randint(0, 1 << 30, (entries,), generator=gen, dtype=torch.int64).to(dev)
+    sl_keep = (torch.rand(slot_rows, slot_width, generator=gen) < 0.5).to(dev)
+    work_indptr, work_slots = sl_indptr.clone(), sl_slots.clone()
+    compactor = SlotCompactor(slot_width, BLOCK, dev)
+
+    def restore():  # the compaction rewrites its input in place
+        work_indptr.copy_(sl_indptr)
+        work_slots.copy_(sl_slots)
+
+    def slot_step():
+        restore()
+        compactor.compact(work_indptr, work_slots, sl_keep, None, True, slot_rows, slot_rows, entries)
+
     ids = int(n.long().sum())
     result = {"rows": rows_total, "width": width, "ids": ids, "policy": "sum per row", "rows_per_gpu": len(nn)}
+    for key, fn in (("sglang_restore_us", restore), ("sglang_us", slot_step)):
+        graph = capture(fn)
+        result[key] = round(timed(graph.replay, steps, warmup, dist_on) / steps * 1e6, 2)
+        del graph
+    result["sglang_us"] = round(result["sglang_us"] - result.pop("sglang_restore_us"), 2)
+    result["sglang_entries"] = entries
+    result["sglang_launches"] = 3
     for key, fn, launches in (("us", build, 2), ("sum_shared_us", build_shared, 9), ("newest_us", build_newest, 2)):
         graph = capture(fn)
         result[key] = round(timed(graph.replay, steps, warmup, dist_on) / steps * 1e6, 2)

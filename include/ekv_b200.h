@@ -218,6 +218,26 @@ int ekv_allocate_quotas(const int32_t* row_blocks, const int32_t* measured_block
                         int64_t budget, const double* row_fraction, int objective, int rows,
                         int32_t* quota, void* stream);
 
+/*
+ * ekv_slot_compact -- the view of SGLang's CSR key-value list, in place (runtime/sglang_compact.py:22-167,
+ * SlotCompactor.compact :131-167).
+ *
+ * Row r of the batch reads slots[indptr[r] : indptr[r + 1]] (int32 indptr [n_rows + 1]; slot entries of
+ * slot_bytes = 4 or 8 bytes; entries = indptr[n_rows], the list's length as the host knows it). Blocks
+ * are block_tokens consecutive entries. A row keeps its first and last block always, and a block b < width
+ * when keep[r][b] != 0 (uint8 or bool, row stride keep_stride), or every block when active == 0, when
+ * audit (uint8 [n_rows], may be NULL) marks it, or when r >= n_real (rows a CUDA graph adds). Writes the
+ * new lengths lens [n_rows], the kept blocks of each row in order to table [n_rows][table_stride], the new
+ * indptr to new_indptr [n_rows + 1] and then to indptr, and the new list to out [entries] and then to
+ * slots; adds to counts (int64 [5]: blocks read, blocks a full read reads, read in audits, read untrimmed,
+ * read with no live policy) over the rows before n_real. Rows must hold at most width blocks. Three
+ * kernels, no host synchronisation.
+ */
+int ekv_slot_compact(int32_t* indptr, void* slots, int slot_bytes, const uint8_t* keep, int64_t keep_stride,
+                     const uint8_t* audit, int active, int n_real, int n_rows, int64_t entries,
+                     int block_tokens, int width, int32_t* new_indptr, int32_t* lens, int32_t* table,
+                     int64_t table_stride, int64_t* counts, void* out, void* stream);
+
 /* Bytes of workspace ekv_allocate_sum needs for `rows` rows of `width` blocks (256-byte aligned). */
 size_t ekv_allocate_sum_workspace_bytes(int rows, int width);
 

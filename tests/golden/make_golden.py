@@ -10,7 +10,9 @@ It imports the reference read-only and runs, on CPU:
     the exact float32 upcast, because the interpreter's ``tl.dot`` on bf16 is wrong;
   * ``read_tile_rows`` and ``normalize_tile_lse`` (observe/tile_shares.py) through a fake D2H reader;
   * ``allocate`` (observe/allocation.py) with the pins and budget of Controller._allocate;
-  * ``compact_block_table`` (runtime/block_view.py:36-56).
+  * ``compact_block_table`` (runtime/block_view.py:36-56);
+  * ``SlotCompactor.compact`` (runtime/sglang_compact.py), the SGLang CSR compaction, both Triton
+    kernels under the interpreter.
 Inputs are seeded; the fixtures hold inputs and outputs, so the tests never need the reference.
 """
 
@@ -228,7 +230,55 @@ def view_cases():
     print("view_cases written")
 
 
-if __name__ == "__main__":
+def slot_cases():
+    """SlotCompactor.compact (runtime/sglang_compact.py:111-167) on SGLang-style CSR batches: the hand
+    cases of the reference's own test (tests/test_sglang_view.py:80-104) and seeded random batches with
+    audits, padding rows of a CUDA graph and a policy that is not live. Each case starts from fresh read
+    counters."""
+    from runtime.sglang_compact import SlotCompactor
+
+    block, width = 16, 20
+    rng = np.random.default_rng(43)
+    hand = [
+        ([5, 16, 17, 100, 33], np.ones((5, width), dtype=bool), 0, None, True),
+        ([200, 64, 150, 17, 1], (np.arange(width)[None, :] % 2 == 0).repeat(5, axis=0), 0, None, True),
+        ([200, 150, 90], np.zeros((3, width), dtype=bool), 0, np.array([False, True, False]), True),
+        ([200, 150, 90], np.zeros((3, width), dtype=bool), 0, None, False),
+        ([35], np.zeros((1, width), dtype=bool), 0, None, True),
+    ]
+    cases = {}
+    for i in range(60):
+        if i < len(hand):
+            lens, keep, padding, audited, active = hand[i]
+        else:
+            rows = int(rng.integers(1, 12))
+            keep = rng.random((rows, width)) < rng.random()
+            audited = rng.random(rows) < 0.3 if i % 2 else None
+            lens = rng.integers(1, block * width, rows).tolist()
+            padding = int(rng.integers(0, 4))
+            active = bool(i % 7)
+        full = list(lens) + [1] * padding
+        indptr = np.array([0, *np.cumsum(full).tolist()], dtype=np.int32)
+        slots = rng.permutation(100_000)[: indptr[-1]].astype(np.int64)
+        d_indptr = torch.from_numpy(indptr.copy())
+        d_slots = torch.from_numpy(np.concatenate([slots, np.full(7, -1, dtype=np.int64)]))
+        compactor = SlotCompactor(width, block, torch.device("cpu"))
+        audit = None if audited is None else torch.from_numpy(np.asarray(audited).astype(np.uint8))
+        new_lens = compactor.compact(d_indptr, d_slots, torch.from_numpy(keep), audit, active, len(lens), len(full),
+                                     int(indptr[-1]))
+        cases[f"indptr{i}"], cases[f"slots{i}"], cases[f"keep{i}"] = indptr, slots, keep
+        cases[f"audit{i}"] = np.zeros(0, dtype=np.uint8) if audited is None else np.asarray(audited).astype(np.uint8)
+        cases[f"active{i}"], cases[f"n_real{i}"] = np.int64(active), np.int64(len(lens))
+        cases[f"new_indptr{i}"] = d_indptr.numpy().copy()
+        total = int(d_indptr[len(full)])
+        cases[f"new_slots{i}"] = d_slots.numpy()[:total].copy()
+        cases[f"lens{i}"] = new_lens.numpy().copy()
+        cases[f"counts{i}"] = compactor.counts.numpy().copy()
+    np.savez_compressed(os.path.join(HERE, "slot_cases.npz"), **cases)
+    print("slot_cases written")
+
+
+def all_cases():
     audit_case("audit_cfg1_fp16", 0, rows=4, q_heads=8, kv_heads=2, layers=1, len_lo=100, len_hi=600, pool=256, dtype="fp16")
     audit_case("audit_layers_fp16", 1, rows=6, q_heads=8, kv_heads=2, layers=3, len_lo=1, len_hi=300, pool=256,
                dtype="fp16", select=[1, 1, 0, 1, 1, 1], flags=[1, 0, 1])
@@ -236,3 +286,13 @@ if __name__ == "__main__":
     shares_cases()
     allocation_cases()
     view_cases()
+    slot_cases()
+
+
+if __name__ == "__main__":
+    # `python make_golden.py` writes every fixture; `python make_golden.py slot_cases ...` only those named
+    chosen = sys.argv[1:]
+    if not chosen:
+        all_cases()
+    for name in chosen:
+        globals()[name]()

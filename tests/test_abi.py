@@ -135,6 +135,14 @@ def test_other_entry_points_validate_before_launching(lib):
     assert lib.ekv_allocate_sum(*sum_args) == L.EINVAL  # a fraction above 1 with no explicit budget
     sum_args[7], sum_args[10] = 0.5, 40000
     assert lib.ekv_allocate_sum(*sum_args) == L.ENOTSUP  # wider than 32768
+    # the SGLang compaction: entry size, pointers and strides
+    slot_args = [fake, fake, 8, fake, 20, None, 1, 2, 2, 40, 16, 20, fake, fake, fake, 20, fake, fake, None]
+    slot_args[2] = 3
+    assert lib.ekv_slot_compact(*slot_args) == L.EINVAL  # 3-byte entries
+    slot_args[2], slot_args[4] = 8, 10
+    assert lib.ekv_slot_compact(*slot_args) == L.EINVAL  # keep stride below the width
+    slot_args[4], slot_args[16] = 20, None
+    assert lib.ekv_slot_compact(*slot_args) == L.EINVAL  # no counters
 
 
 def test_step_and_stash_validate_before_launching(lib):

@@ -181,3 +181,20 @@ def test_known_answer_keep_newest():
 def test_oracle_rejects_a_budget_below_the_pins():
     with pytest.raises(ValueError):
         oa.allocate([np.ones(5)], 1, "sum")
+
+
+def test_oracle_slot_compaction_matches_the_reference_kernels():
+    """oracle.view.slot_compact against SlotCompactor.compact run by make_golden.py in the interpreter."""
+    from oracle import view as ov
+
+    g = load_golden("slot_cases")
+    for i in range(60):
+        indptr, slots, keep = g[f"indptr{i}"], g[f"slots{i}"], g[f"keep{i}"]
+        audit = g[f"audit{i}"] if len(g[f"audit{i}"]) else None
+        n_rows = len(indptr) - 1
+        new_indptr, new_slots, lens, counts = ov.slot_compact(indptr, slots, keep, audit, bool(g[f"active{i}"]),
+                                                              int(g[f"n_real{i}"]), n_rows, 16)
+        np.testing.assert_array_equal(new_indptr, g[f"new_indptr{i}"], err_msg=f"case {i}")
+        np.testing.assert_array_equal(new_slots, g[f"new_slots{i}"], err_msg=f"case {i}")
+        np.testing.assert_array_equal(lens, g[f"lens{i}"], err_msg=f"case {i}")
+        np.testing.assert_array_equal(counts, g[f"counts{i}"], err_msg=f"case {i}")

@@ -219,6 +219,23 @@ int ekv_allocate_quotas(const int32_t* row_blocks, const int32_t* measured_block
                         int32_t* quota, void* stream);
 
 /*
+ * ekv_decode_view -- DecodeView.build on the device: keep algebra, compaction and read counters in one
+ * kernel (runtime/block_view.py:272-329).
+ *
+ * row_flags uint8 [rows]: bit 0 the row reads every block (an expired lease, an audited row, a prefill
+ * row), bit 1 it decodes, bit 2 it is audited. keep uint8 [rows][keep_stride] is the committed mask;
+ * released (may be NULL) removes blocks last, so nothing brings a released block back. The view and its
+ * lengths are those of compact_block_table (:36-56). counts (int64 [5], may be NULL) receives, over the
+ * decoding rows, the blocks read, the blocks a full read would read, the blocks read by audited rows, by
+ * rows read whole under a live policy without an audit, and (expired != 0) all blocks read while no
+ * policy is live. width <= 16384.
+ */
+int ekv_decode_view(const int32_t* table, int64_t table_stride, const int32_t* seq_lens, const uint8_t* keep,
+                    int64_t keep_stride, const uint8_t* row_flags, const uint8_t* released,
+                    int64_t released_stride, int expired, int rows, int width, int block_size, int32_t* view,
+                    int64_t view_stride, int32_t* view_lens, int64_t* counts, void* stream);
+
+/*
  * ekv_slot_compact -- the view of SGLang's CSR key-value list, in place (runtime/sglang_compact.py:22-167,
  * SlotCompactor.compact :131-167).
  *

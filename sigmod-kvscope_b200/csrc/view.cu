@@ -195,7 +195,13 @@ struct ViewParams {
   int32_t* view_lens;
   uint8_t* mask_out;
   int64_t mask_s0;
+  // the read counters of a decode view (ekv_decode_view): full_rows then carries packed row flags
+  long long* counts;
+  int expired;
 };
+
+// Row flags of ekv_decode_view (full_rows): the row reads every block / decodes / is audited.
+constexpr uint8_t kRowFull = 1, kRowDecoding = 2, kRowAudited = 4;
 
 constexpr int kViewThreads = 512;
 constexpr int kViewWarps = kViewThreads / 32;
@@ -395,7 +401,8 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
     eq_base = warp_bases(cnt, s_w, &unused);
   }
 
-  const bool full = p.full_rows != nullptr && p.full_rows[r] != 0;
+  const uint8_t flags = p.full_rows != nullptr ? p.full_rows[r] : 0;
+  const bool full = (flags & kRowFull) != 0;
   const uint8_t* krow = rank_mode ? nullptr : p.keep + (int64_t)r * p.keep_s0;
   const uint8_t* rrow = p.released ? p.released + (int64_t)r * p.released_s0 : nullptr;
 
@@ -458,7 +465,20 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
   copy_words(vrow, trow, laid, W);  // past the laid-out positions nothing is kept: the view is the table
   if (threadIdx.x == 0) {
     const int last = seq - (blocks - 1) * BS;
-    p.view_lens[r] = blocks > 0 ? (kept_total - 1) * BS + last : 0;
+    const int view_len = blocks > 0 ? (kept_total - 1) * BS + last : 0;
+    p.view_lens[r] = view_len;
+    // DecodeView._count (runtime/block_view.py:297-329) for a decoding row: blocks read and blocks a full
+    // read would read; the reads of an audited row, of a row read whole under a live policy without an
+    // audit, and of any row while no policy is live
+    if (p.counts != nullptr && (flags & kRowDecoding)) {
+      const long long read = blocks > 0 ? kept_total : 0;
+      const bool audited = (flags & kRowAudited) != 0;
+      atomicAdd((unsigned long long*)&p.counts[0], (unsigned long long)read);
+      atomicAdd((unsigned long long*)&p.counts[1], (unsigned long long)blocks);
+      if (audited) atomicAdd((unsigned long long*)&p.counts[2], (unsigned long long)read);
+      if (view_len == seq && !audited && !p.expired) atomicAdd((unsigned long long*)&p.counts[3], (unsigned long long)read);
+      if (p.expired) atomicAdd((unsigned long long*)&p.counts[4], (unsigned long long)read);
+    }
   }
 }
 
@@ -549,7 +569,7 @@ extern "C" int ekv_view_build(const int32_t* table, int64_t table_stride, const 
   ViewParams p{table,   table_stride, seq_lens, row_blocks, quota,      measured_blocks,
                recent_blocks, scores, score_stride, policy, keep,      keep_stride,
                full_rows, released, released_stride, rows, width,     block_size,
-               view,    view_stride,  view_lens, mask_out,  mask_stride};
+               view,    view_stride,  view_lens, mask_out,  mask_stride, nullptr, 0};
   return launch_view(p, static_cast<cudaStream_t>(stream));
 }
 
@@ -565,4 +585,24 @@ extern "C" int ekv_compact_block_table(const int32_t* table, int64_t table_strid
   return ekv_view_build(table, table_stride, seq_lens, nullptr, nullptr, nullptr, 0, nullptr, 0,
                         EKV_POLICY_UNIFORM, keep, keep_stride, nullptr, nullptr, 0, rows, width,
                         block_size, view, view_stride, view_lens, nullptr, 0, stream);
+}
+
+extern "C" int ekv_decode_view(const int32_t* table, int64_t table_stride, const int32_t* seq_lens,
+                               const uint8_t* keep, int64_t keep_stride, const uint8_t* row_flags,
+                               const uint8_t* released, int64_t released_stride, int expired, int rows, int width,
+                               int block_size, int32_t* view, int64_t view_stride, int32_t* view_lens,
+                               int64_t* counts, void* stream) {
+  clear_error();
+  if (!table || !seq_lens || !keep || !row_flags || !view || !view_lens)
+    return fail(EKV_EINVAL, "a required pointer is NULL");
+  if (rows <= 0 || width <= 0 || block_size <= 0)
+    return fail(EKV_EINVAL, "rows, width and block_size must be positive");
+  if (width > kViewMaxWidth) return fail(EKV_ENOTSUP, "width %d > %d (a view row is staged in shared memory)", width, kViewMaxWidth);
+  if (table_stride < width || view_stride < width || keep_stride < width)
+    return fail(EKV_EINVAL, "a row stride is below the width");
+  if (released && released_stride < width) return fail(EKV_EINVAL, "released_stride < width");
+  ViewParams p{table, table_stride, seq_lens, nullptr, nullptr, nullptr, 0, nullptr, 0, EKV_POLICY_UNIFORM,
+               keep,  keep_stride,  row_flags, released, released_stride, rows, width, block_size,
+               view,  view_stride,  view_lens, nullptr, 0, reinterpret_cast<long long*>(counts), expired != 0};
+  return launch_view(p, static_cast<cudaStream_t>(stream));
 }

@@ -203,6 +203,8 @@ class DecodeView:
         self._audit_pending = False
         self._pending_rows = np.zeros(rows, dtype=bool)
         self._counts: torch.Tensor | None = None
+        self._flag_ring: list[torch.Tensor] | None = None
+        self._flag_slot = 0
         self._device: torch.device | None = None
         self._device_keep: torch.Tensor | None = None
         self._device_version = -1
@@ -210,7 +212,6 @@ class DecodeView:
         self._released_device_version = -1
         self._table: torch.Tensor | None = None
         self._lens: torch.Tensor | None = None
-        self._full: torch.Tensor | None = None
 
     # -- the controller-facing writes ------------------------------------------------------------
 
@@ -303,8 +304,7 @@ class DecodeView:
         if self._table is None:
             self._table = torch.zeros(self.rows, width, dtype=torch.int32, device=table.device)
             self._lens = torch.zeros(self.rows, dtype=torch.int32, device=table.device)
-            self._full = torch.zeros(self.rows, dtype=torch.uint8, device=table.device)
-        assert self._lens is not None and self._full is not None
+        assert self._lens is not None
         decode = query_lens.numpy() == 1
         servable = decode | (self.final_prefill[:num_reqs] & self.prefill_audit)
         self.final_prefill[:] = False
@@ -322,23 +322,46 @@ class DecodeView:
             self.start_audit()
             size = self.block_size
             self._pending_blocks[:num_reqs] = ((seq_lens[:num_reqs] + size - 1) // size).cpu().numpy()
-        # rows that read every block: all rows when the lease has expired, audited rows, prefill rows
-        full = np.ones(num_reqs, dtype=np.uint8) if not live else (audited[:num_reqs] | ~decode).astype(np.uint8)
-        self._full[:num_reqs].copy_(torch.from_numpy(full), non_blocking=False)
+        # one flag byte per row: it reads every block (an expired lease, an audited row, a prefill row),
+        # it decodes, it is audited; the view kernel applies them and counts the reads (:272-329)
+        full = np.ones(num_reqs, dtype=bool) if not live else (audited[:num_reqs] | ~decode)
+        flags = full.astype(np.uint8) | (decode.astype(np.uint8) << 1) | (audited[:num_reqs].astype(np.uint8) << 2)
+        row_flags = self._flags_on(flags, table.device)
         keep = self._keep_on(table.device)[:num_reqs]
         released = self._released_on(table.device)[:num_reqs] if self.released.any() else None
         if self.audit is not None:
             starts = np.concatenate(([0], np.cumsum(query_lens.numpy())[:-1]))
             self.audit.select(audited[:num_reqs], starts)
             self.audit.set(self.audit_step)
-        _view_build(
-            table[:num_reqs], seq_lens[:num_reqs], self.block_size, keep=keep, full_rows=self._full[:num_reqs],
-            released=released, out=(self._table[:num_reqs], self._lens[:num_reqs]),
+        if self._counts is None:
+            self._counts = torch.zeros(5, dtype=torch.int64, device=table.device)
+        t = table[:num_reqs]
+        if t.dtype != torch.int32 or seq_lens.dtype != torch.int32 or t.stride(1) != 1:
+            raise ValueError("the block table (rows contiguous) and the lengths must be int32")
+        rc = _lib.load().ekv_decode_view(
+            t.data_ptr(), t.stride(0), seq_lens.data_ptr(), keep.data_ptr(), keep.stride(0), row_flags.data_ptr(),
+            _ptr(released), 0 if released is None else released.stride(0), int(not live), num_reqs, width,
+            self.block_size, self._table.data_ptr(), self._table.stride(0), self._lens.data_ptr(),
+            self._counts.data_ptr(), _lib.current_stream(),
         )
-        decoding = None if bool(decode.all()) else torch.from_numpy(decode).to(table.device)
-        audited_rows = torch.from_numpy(audited[:num_reqs]).to(table.device)
-        self._count(self._lens[:num_reqs], seq_lens[:num_reqs], decoding, audited_rows, expired=not live)
+        _lib.check(rc, "ekv_decode_view")
         return self._table[:num_reqs], self._lens[:num_reqs]
+
+    def _flags_on(self, flags: np.ndarray, device: torch.device) -> torch.Tensor:
+        """The row flags on the device, through a ring of pinned buffers: no copy waits for the device."""
+        if self._flag_ring is None:
+            self._flag_ring = [torch.empty(self.rows, dtype=torch.uint8).pin_memory() for _ in range(4)]
+            self._flag_done: list[torch.cuda.Event | None] = [None] * 4
+            self._flags_dev = torch.zeros(self.rows, dtype=torch.uint8, device=device)
+        slot = self._flag_slot = (self._flag_slot + 1) % len(self._flag_ring)
+        if self._flag_done[slot] is not None:
+            self._flag_done[slot].synchronize()  # its copy four steps ago has long finished
+        self._flag_ring[slot].numpy()[: len(flags)] = flags
+        self._flags_dev[: len(flags)].copy_(self._flag_ring[slot][: len(flags)], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record()
+        self._flag_done[slot] = done
+        return self._flags_dev
 
     def _count(self, read_lens, full_lens, decoding, audited=None, expired: bool = False) -> None:
         """Read counters of decode rows: read, full, audited, untrimmed-live, expired (reference :297-329)."""

@@ -399,3 +399,55 @@ def test_decode_view_policy_lease_audit_and_release():
     view.write_lease_deadline(time.monotonic_ns() + hour)
     t, n = view.build(table, lens, prefill)
     assert n.tolist() == [32, 48]  # row 1 prefills: it reads in full
+
+
+def test_decode_view_counters_follow_the_reference_count():
+    """Thirty builds with new masks, live and expired leases, audits, prefill rows and released blocks: the
+    view against the oracle's keep algebra and compaction, and the five read counters against
+    DecodeView._count's formulas (runtime/block_view.py:297-329)."""
+    import time
+
+    from ekv.runtime.block_view import DecodeView
+
+    class Plane:
+        def set(self, on):
+            pass
+
+        def select(self, audited, token_start):
+            pass
+
+    rng = np.random.default_rng(71)
+    rows, width, bs = 48, 64, 16
+    view = DecodeView(rows=rows, width=width, block_size=bs, audit=Plane())
+    expected = np.zeros(5, dtype=np.int64)
+    hour = 3600 * 10**9
+    for step in range(30):
+        n = int(rng.integers(1, rows + 1))
+        lens = rng.integers(0, width * bs + 1, n).astype(np.int32)
+        table = rng.integers(0, 1 << 20, (n, width)).astype(np.int32)
+        query = np.where(rng.random(n) < 0.2, rng.integers(2, 9, n), 1).astype(np.int32)
+        if step % 4 == 0:
+            view.write_row_controls((rng.random((rows, width)) < 0.5).astype(np.uint8))
+        live = step % 5 != 3
+        view.write_lease_deadline(time.monotonic_ns() + (hour if live else -hour))
+        if step % 3 == 0:
+            view.write_audit_rows(rng.random(rows) < 0.2)
+        if step == 10:
+            view.released[:] = rng.random((rows, width)) < 0.1
+            view.released[:, 0] = False
+            view.released_version += 1
+        t, vl = view.build(torch.from_numpy(table).cuda(), torch.from_numpy(lens).cuda(), torch.from_numpy(query))
+        audited = view._pending_rows[:n]
+        decoding = query == 1
+        full = np.ones(n, dtype=bool) if not live else (audited | ~decoding)
+        keep = ov.decode_keep(view.keep[:n], full, view.released[:n] if view.released.any() else None)
+        ref_view, ref_lens = ov.compact_block_table(table, lens, keep, bs)
+        np.testing.assert_array_equal(t.cpu().numpy(), ref_view, err_msg=f"step {step}")
+        np.testing.assert_array_equal(vl.cpu().numpy(), ref_lens, err_msg=f"step {step}")
+        read = -(-ref_lens.astype(np.int64) // bs) * decoding
+        blocks = -(-lens.astype(np.int64) // bs) * decoding
+        whole = ref_lens == lens
+        expected += [read.sum(), blocks.sum(), (read * audited).sum(), (read * (whole & ~audited & live)).sum(),
+                     0 if live else read.sum()]
+        got = np.array(list(view.read_breakdown().values()), dtype=np.int64)
+        np.testing.assert_array_equal(got, expected, err_msg=f"step {step}")

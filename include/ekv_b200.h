@@ -235,6 +235,25 @@ int ekv_decode_view(const int32_t* table, int64_t table_stride, const int32_t* s
                     int64_t released_stride, int expired, int rows, int width, int block_size, int32_t* view,
                     int64_t view_stride, int32_t* view_lens, int64_t* counts, void* stream);
 
+/* Bytes of workspace ekv_allocate_maxmin needs for `rows` rows of `width` blocks (256-byte aligned). */
+size_t ekv_allocate_maxmin_workspace_bytes(int rows, int width);
+
+/*
+ * ekv_allocate_maxmin -- the quotas of the `maxmin` objective with one budget shared by every measured row.
+ *
+ * Replaces allocate(requests, budget, "maxmin") (observe/allocation.py:55-76 and _water_level :121-166):
+ * the highest retained-share level the budget affords (60 bisection steps over each request's running
+ * sums of its unpinned shares in decreasing order, float64 as NumPy computes them), then the blocks left
+ * over one at a time to the request with the lowest retained share (ties: the earlier request). Rows,
+ * pins, budget and quota as in ekv_allocate_sum (no weights: maxmin does not use them); the quotas are
+ * for ekv_view_build with EKV_POLICY_UNIFORM (equal shares to the older block). width <= 8192,
+ * rows <= 8192. Three kernels and one memset on `stream`, no host synchronisation.
+ */
+int ekv_allocate_maxmin(const float* scores, int64_t score_stride, const int32_t* row_blocks,
+                        const int32_t* measured_blocks, int recent_blocks, int cap_above_blocks,
+                        double budget_fraction, int64_t budget, int rows, int width, int32_t* quota,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
 /*
  * ekv_slot_compact -- the view of SGLang's CSR key-value list, in place (runtime/sglang_compact.py:22-167,
  * SlotCompactor.compact :131-167).

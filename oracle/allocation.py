@@ -69,6 +69,54 @@ def greedy(score_list, pinned_list, weights, free: int) -> list[np.ndarray]:
     return kept
 
 
+def water_level(score_list, pinned_list, free: int) -> list[np.ndarray]:
+    """maxmin (allocation.py:121-166): the highest level of retained share every request can reach within
+    ``free`` blocks (60 bisection steps over searchsorted running sums), then one block at a time to the
+    request with the lowest retained share, ties to the earlier request."""
+    import heapq
+
+    shares_list = [shares(s) for s in score_list]
+    order = [np.flatnonzero(~p)[np.argsort(-sh[~p], kind="stable")] for sh, p in zip(shares_list, pinned_list,
+                                                                                       strict=True)]
+    base = [float(sh[p].sum()) for sh, p in zip(shares_list, pinned_list, strict=True)]
+    prefix = [np.cumsum(sh[o]) for sh, o in zip(shares_list, order, strict=True)]
+    stacked = np.concatenate([pr + 2.0 * r for r, pr in enumerate(prefix)]) if prefix else np.zeros(0)
+    sizes = np.array([len(o) for o in order])
+    starts = np.concatenate(([0], np.cumsum(sizes)[:-1]))
+    offsets = 2.0 * np.arange(len(score_list))
+    base_a = np.array(base)
+
+    def extra(level: float) -> np.ndarray:
+        need = level - base_a
+        position = np.searchsorted(stacked, need - 1e-12 + offsets) - starts
+        return np.where(need <= 1e-12, 0, np.minimum(position + 1, sizes))
+
+    low, high = 0.0, 1.0
+    for _ in range(60):
+        mid = (low + high) / 2
+        if int(extra(mid).sum()) <= free:
+            low = mid
+        else:
+            high = mid
+    counts = [int(c) for c in extra(low)]
+    kept = [p.copy() for p in pinned_list]
+    for r, k in enumerate(counts):
+        kept[r][order[r][:k]] = True
+    leftover = free - sum(counts)
+    retained = [base[r] + (float(prefix[r][counts[r] - 1]) if counts[r] else 0.0) for r in range(len(score_list))]
+    heap = [(retained[r], r) for r in range(len(score_list)) if counts[r] < len(order[r])]
+    heapq.heapify(heap)
+    while leftover > 0 and heap:
+        level, r = heapq.heappop(heap)
+        block = order[r][counts[r]]
+        kept[r][block] = True
+        counts[r] += 1
+        leftover -= 1
+        if counts[r] < len(order[r]):
+            heapq.heappush(heap, (level + float(shares_list[r][block]), r))
+    return kept
+
+
 def allocate(score_list, budget: int, objective: str = "sum", pinned_list=None, weights=None) -> list[np.ndarray]:
     """Masks of kept blocks per request, at most ``budget`` in all (allocation.py:55-76)."""
     sizes = [len(s) for s in score_list]
@@ -85,6 +133,8 @@ def allocate(score_list, budget: int, objective: str = "sum", pinned_list=None, 
         return greedy(score_list, pinned_list, weights, budget - must)
     if objective == "uniform":
         return uniform(score_list, pinned_list, budget - must)
+    if objective == "maxmin":
+        return water_level(score_list, pinned_list, budget - must)
     raise ValueError(f"unknown objective {objective!r}")
 
 

@@ -26,6 +26,7 @@
 //   4. sum_kept_kernel over the candidates (ties above i*, rows tied at i*) and sum_quota_kernel, one
 //      CTA, which hands the ties at i* to the earliest rows and writes q_r.
 #include "ekv_common.cuh"
+#include "pairwise.cuh"
 #include "pins.cuh"
 
 namespace ekv {
@@ -34,8 +35,6 @@ constexpr int kSumThreads = 256;
 constexpr int kSumBins = 2048;
 constexpr int kSumPasses = 6;
 constexpr int kSumChunk = 2048;   // blocks of one row per CTA in the passes over every key
-constexpr int kMaxNodes = 1024;   // pairwise tree of up to 32768 values: at most 512 leaves (each > 64 values)
-constexpr int kMaxLevels = 16;
 constexpr int kSumMaxWidth = 32768;
 constexpr int kSumMaxRows = 1 << 17;  // a candidate's place is (row << 15) | block
 
@@ -126,27 +125,6 @@ __device__ __forceinline__ void digit_of(int pass, int& shift, unsigned long lon
   dmask = pass < 5 ? 2047ull : 255ull;
 }
 
-// numpy's pairwise_sum of one leaf (at most 128 values): eight accumulators, combined as
-// ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)), then the rest one by one; below 8 values a plain
-// loop from 0.
-__device__ double leaf_sum(const float* x, int len) {  // x: the row's scores in shared memory
-  if (len < 8) {
-    double res = 0.0;
-    for (int i = 0; i < len; ++i) res += clamped(x[i]);
-    return res;
-  }
-  double r[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) r[j] = clamped(x[j]);
-  int i = 8;
-  for (; i < len - (len % 8); i += 8)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) r[j] += clamped(x[i + j]);
-  double res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
-  for (; i < len; ++i) res += clamped(x[i]);
-  return res;
-}
-
 // Whether this CTA is the last of the grid to get here (after its writes are fenced).
 __device__ __forceinline__ bool last_cta(unsigned int* ticket, bool* s_last) {
   __threadfence();
@@ -203,20 +181,12 @@ __device__ void pick_digit(SumState* st, unsigned int* hist, int pass) {
   }
 }
 
-// One CTA per row: the total, the keys, the pins; the CTA that finishes last sets the budget.
-//
-// The total follows numpy's pairwise_sum tree: a segment of more than 128 values splits at
-// n2 = n / 2 rounded down to a multiple of 8, and its sum is sum(left) + sum(right). The tree is
-// built one level at a time (every node of a level splits in parallel and records its children),
-// the leaves are summed in parallel, and the levels are combined from the bottom up: the same
-// additions in the same order as numpy's recursion.
+// One CTA per row: the total (numpy's pairwise sum, pairwise.cuh), the keys, the pins; the CTA that
+// finishes last sets the budget.
 __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p) {
   extern __shared__ float s_x[];  // [width]: the row's scores
   __shared__ unsigned int s_hist[kSumBins];
-  __shared__ int s_lo[kMaxNodes], s_len[kMaxNodes], s_left[kMaxNodes];
-  __shared__ double s_val[kMaxNodes];
-  __shared__ int s_level[kMaxLevels + 2];
-  __shared__ int s_nodes, s_depth;
+  __shared__ PairwiseTree s_tree;
   __shared__ double s_total;
   __shared__ bool s_last;
   const int r = blockIdx.x, tid = threadIdx.x;
@@ -229,38 +199,8 @@ __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p
   for (int i = tid; i < kSumBins; i += kSumThreads) s_hist[i] = 0;
   if (request) {
     for (int i = tid; i < n; i += kSumThreads) s_x[i] = xg[i];
-    if (tid == 0) {
-      s_lo[0] = 0, s_len[0] = n, s_nodes = 1, s_level[0] = 0, s_level[1] = 1, s_depth = 1;
-    }
-    __syncthreads();
-    for (int d = 0; d < kMaxLevels; ++d) {  // split the level's nodes; children go after the level
-      const int a = s_level[d], b = s_level[d + 1];
-      if (a == b) break;
-      for (int i = a + tid; i < b; i += kSumThreads) {
-        const int lo = s_lo[i], len = s_len[i];
-        if (len <= 128) {
-          s_left[i] = -1;
-        } else {
-          int n2 = len / 2;
-          n2 -= n2 % 8;
-          const int c = atomicAdd(&s_nodes, 2);
-          s_lo[c] = lo, s_len[c] = n2, s_lo[c + 1] = lo + n2, s_len[c + 1] = len - n2;
-          s_left[i] = c;
-        }
-      }
-      __syncthreads();
-      if (tid == 0) s_level[d + 2] = s_nodes, s_depth = d + 1;
-      __syncthreads();
-    }
-    for (int i = tid; i < s_nodes; i += kSumThreads)
-      if (s_left[i] < 0) s_val[i] = leaf_sum(s_x + s_lo[i], s_len[i]);
-    __syncthreads();
-    for (int d = s_depth - 1; d >= 0; --d) {  // each inner node: left + right, deepest level first
-      for (int i = s_level[d] + tid; i < s_level[d + 1]; i += kSumThreads)
-        if (s_left[i] >= 0) s_val[i] = s_val[s_left[i]] + s_val[s_left[i] + 1];
-      __syncthreads();
-    }
-    if (tid == 0) s_total = s_val[0];
+    const double sum = block_pairwise_sum<kSumThreads>(s_tree, n, [&](int i) { return clamped(s_x[i]); });
+    if (tid == 0) s_total = sum;
     __syncthreads();
     const double total = s_total;
     unsigned long long* kr = p.keys + (int64_t)r * p.width;

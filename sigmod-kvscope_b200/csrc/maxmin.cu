@@ -1,0 +1,378 @@
+// The `maxmin` objective on the device: raise the smallest retained share of any request as far as one
+// shared budget allows, then spend what is left (observe/allocation.py:121-166, _water_level).
+//
+// The reference, per request r: shares s = max(score, 0) / total (float64, total by NumPy's pairwise
+// sum; equal shares without evidence), the unpinned blocks in order of decreasing share (equal shares:
+// the older block first), base_r = the pairwise sum of the pinned shares, prefix_r = the running sum
+// (np.cumsum) of the ordered shares. extra_r(level) = 0 when level - base_r <= 1e-12, else
+// min(searchsorted(prefix + 2 r', level - base_r - 1e-12 + 2 r') + 1, open_r), with r' the request's
+// index; 60 bisection steps on [0, 1] find the highest level whose extras fit the free budget, and
+// the rest of the budget goes one block at a time to the request with the lowest retained share
+// (ties: the earlier request). Here:
+//   mm_prep_kernel, one CTA per row: the total, the shares of the pinned blocks summed as NumPy sums
+//     them, the unpinned blocks ordered by a bitonic sort of (score, block) keys, their shares in that
+//     order; the CTA that finishes last sets the budget and each request's index.
+//   mm_cumsum_kernel, a thread per row: the running sums, one addition after another as np.cumsum.
+//   mm_level_kernel, one CTA: the bisection (a binary search per request and a reduction per step)
+//     and the leftover blocks through a binary heap in shared memory. The row quotas it writes make
+//     ekv_view_build (EKV_POLICY_UNIFORM: equal shares to the older block) keep exactly the reference's
+//     blocks.
+#include "ekv_common.cuh"
+#include "pairwise.cuh"
+#include "pins.cuh"
+
+namespace ekv {
+
+constexpr int kMmThreads = 1024;
+constexpr int kMmMaxWidth = 8192;
+constexpr int kMmMaxRows = 8192;
+constexpr int kMmBisection = 60;
+
+enum MmMode : int { kMmSelect = 0, kMmNone = 1, kMmAll = 2 };
+
+struct MmState {
+  long long must, blocks, total_open, free_;
+  int mode;
+  unsigned int ticket;
+};
+
+struct MmParams {
+  const float* scores;
+  int64_t score_s0;
+  const int32_t* row_blocks;
+  const int32_t* measured;
+  int recent, cap;
+  double fraction;
+  long long budget;
+  int rows, width;
+  int32_t* quota;
+  // workspace
+  MmState* state;
+  double* base;     // [rows] pinned share
+  int* row_m;       // [rows] unpinned blocks; -1 for a row that is not a request
+  int* req;         // [rows] index of the request among the requests
+  double* sorted;   // [rows][width] unpinned shares in decreasing order
+  double* prefix;   // [rows][width] their running sums
+};
+
+struct MmLayout {
+  size_t state, base, row_m, req, sorted, prefix, bytes;
+};
+
+MmLayout mm_layout(int rows, int width) {
+  MmLayout l{};
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o += round_up(bytes, 256);
+    return at;
+  };
+  l.state = take(sizeof(MmState));
+  l.base = take((size_t)rows * 8);
+  l.row_m = take((size_t)rows * 4);
+  l.req = take((size_t)rows * 4);
+  l.sorted = take((size_t)rows * width * 8);
+  l.prefix = take((size_t)rows * width * 8);
+  l.bytes = o;
+  return l;
+}
+
+__device__ __forceinline__ double mm_clamped(float s) { return s > 0.f ? (double)s : 0.0; }
+
+// max(score, 0) as an order-preserving uint32 (NaN as 0)
+__device__ __forceinline__ uint32_t mm_score_key(float s) { return s > 0.f ? __float_as_uint(s) : 0u; }
+
+// One CTA per row. Dynamic shared memory: the row's scores (float [width]) and the sort keys
+// (uint64 [next power of two >= width]).
+__global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
+  extern __shared__ __align__(16) unsigned char mm_smem[];
+  __shared__ PairwiseTree s_tree;
+  __shared__ bool s_last;
+  const int r = blockIdx.x, tid = threadIdx.x;
+  int n = p.row_blocks[r];
+  const bool request = n > p.cap && n > 0;
+  if (n > p.width) n = p.width;
+  float* s_x = reinterpret_cast<float*>(mm_smem);
+  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(mm_smem + ((size_t)p.width * 4 + 15) / 16 * 16);
+  const int ps = request ? pin_start(n, p.recent, p.measured, r) : 0;
+  const int m = ps > 1 ? ps - 1 : 0;  // unpinned blocks [1, ps)
+  if (request) {
+    const float* xg = p.scores + (int64_t)r * p.score_s0;
+    for (int i = tid; i < n; i += kMmThreads) s_x[i] = xg[i];
+    const double total = block_pairwise_sum<kMmThreads>(s_tree, n, [&](int i) { return mm_clamped(s_x[i]); });
+    const double equal = 1.0 / (double)(n > 1 ? n : 1);
+    auto share = [&](int i) { return total > 0.0 ? mm_clamped(s_x[i]) / total : equal; };
+    // the pinned blocks in index order: block 0 and [ps, n) (every block when ps == 0)
+    const int npin = ps >= 1 ? 1 + (n - ps) : n;
+    const double base = block_pairwise_sum<kMmThreads>(
+        s_tree, npin, [&](int j) { return share(ps >= 1 ? (j == 0 ? 0 : ps + j - 1) : j); });
+    // the unpinned blocks by decreasing share, equal shares by increasing block: ascending keys
+    // (~score key, block); the padding sorts last
+    int P = 1;
+    while (P < m) P <<= 1;
+    for (int j = tid; j < P; j += kMmThreads)
+      s_key[j] = j < m ? ((unsigned long long)(~mm_score_key(s_x[1 + j])) << 32) | (unsigned long long)(1 + j)
+                       : ~0ull;
+    __syncthreads();
+    for (int k = 2; k <= P; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = tid; i < P; i += kMmThreads) {
+          const int partner = i ^ j;
+          if (partner > i) {
+            const unsigned long long a = s_key[i], b = s_key[partner];
+            const bool up = (i & k) == 0;
+            if ((a > b) == up) s_key[i] = b, s_key[partner] = a;
+          }
+        }
+        __syncthreads();
+      }
+    }
+    double* sr = p.sorted + (int64_t)r * p.width;
+    for (int j = tid; j < m; j += kMmThreads) sr[j] = share((int)(s_key[j] & 0xffffffffu));
+    if (tid == 0) {
+      p.base[r] = base;
+      atomicAdd((unsigned long long*)&p.state->must, (unsigned long long)pin_count(n, ps));
+      atomicAdd((unsigned long long*)&p.state->blocks, (unsigned long long)n);
+      atomicAdd((unsigned long long*)&p.state->total_open, (unsigned long long)m);
+    }
+  }
+  if (tid == 0) p.row_m[r] = request ? m : -1;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&p.state->ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // the budget (controller.py:435-437), what to do with it (allocation.py:64-67) and each request's index
+  MmState* st = p.state;
+  if (tid == 0) {
+    const long long must = *(volatile long long*)&st->must, blocks = *(volatile long long*)&st->blocks;
+    long long budget = p.budget;
+    if (budget < 0) {
+      budget = (long long)ceil(p.fraction * (double)blocks);
+      if (budget < must) budget = must;
+    }
+    const long long free_ = budget - must;
+    st->free_ = free_;
+    st->mode = budget >= blocks ? kMmAll : (free_ <= 0 ? kMmNone : kMmSelect);
+    st->ticket = 0;
+  }
+  __shared__ int s_scan[kMmThreads / 32 + 1];
+  int carry = 0;
+  for (int b0 = 0; b0 < p.rows; b0 += kMmThreads) {
+    const int row = b0 + tid;
+    const int is_req = row < p.rows && __ldcg(p.row_m + row) >= 0;
+    int total = 0;
+    const int before = block_exclusive_scan<kMmThreads>(is_req, s_scan, &total);
+    if (row < p.rows) p.req[row] = carry + before;
+    carry += total;
+  }
+}
+
+// A thread per row: prefix[j] = prefix[j - 1] + sorted[j], one addition after another.
+__global__ void __launch_bounds__(128) mm_cumsum_kernel(const MmParams p) {
+  const int r = blockIdx.x * 128 + threadIdx.x;
+  if (r >= p.rows) return;
+  const int m = p.row_m[r];
+  const double* sr = p.sorted + (int64_t)r * p.width;
+  double* pr = p.prefix + (int64_t)r * p.width;
+  double acc = 0.0;
+  int j = 0;
+  for (; j + 8 <= m; j += 8) {  // eight loads in flight, the additions in order
+    double v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = sr[j + u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      acc = (j + u == 0) ? v[u] : acc + v[u];
+      pr[j + u] = acc;
+    }
+  }
+  for (; j < m; ++j) {
+    acc = j == 0 ? sr[j] : acc + sr[j];
+    pr[j] = acc;
+  }
+}
+
+// The blocks request r needs beyond its pins to retain `level` (allocation.py:146-150).
+__device__ __forceinline__ int mm_extra(const MmParams& p, int r, double level) {
+  const int m = p.row_m[r];
+  if (m < 0) return 0;
+  const double need = level - p.base[r];
+  if (need <= 1e-12) return 0;
+  const double offset = 2.0 * (double)p.req[r];
+  const double x = need - 1e-12 + offset;
+  const double* pr = p.prefix + (int64_t)r * p.width;
+  int lo = 0, hi = m;  // the first j with prefix[j] + offset >= x (searchsorted, side left)
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (pr[mid] + offset < x) lo = mid + 1; else hi = mid;
+  }
+  return lo + 1 < m ? lo + 1 : m;
+}
+
+// One CTA: the water level, the leftover blocks and the quotas. Dynamic shared memory: the heap
+// (double level and int request row per entry) and the counts, rows entries each.
+__global__ void __launch_bounds__(kMmThreads) mm_level_kernel(const MmParams p) {
+  extern __shared__ __align__(16) unsigned char lv_smem[];
+  double* h_level = reinterpret_cast<double*>(lv_smem);
+  int* h_row = reinterpret_cast<int*>(h_level + p.rows);
+  int* counts = h_row + p.rows;
+  __shared__ long long s_red[kMmThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const MmState* st = p.state;
+  const int mode = st->mode;
+  if (mode != kMmSelect) {
+    for (int r = tid; r < p.rows; r += kMmThreads) {
+      const int m = p.row_m[r];
+      p.quota[r] = m < 0 ? -1 : (mode == kMmAll ? m : 0);
+    }
+    return;
+  }
+  const long long free_ = st->free_;
+  auto total_extra = [&](double level) {
+    long long sum = 0;
+    for (int r = tid; r < p.rows; r += kMmThreads) sum += mm_extra(p, r, level);
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(kFullMask, sum, off);
+    __syncthreads();
+    if (lane == 0) s_red[warp] = sum;
+    __syncthreads();
+    long long t = 0;
+    for (int w = 0; w < kMmThreads / 32; ++w) t += s_red[w];
+    return t;
+  };
+  double low = 0.0, high = 1.0;
+  for (int it = 0; it < kMmBisection; ++it) {
+    const double mid = (low + high) / 2;
+    if (total_extra(mid) <= free_) low = mid; else high = mid;
+  }
+  long long used = 0;
+  for (int r = tid; r < p.rows; r += kMmThreads) {
+    counts[r] = mm_extra(p, r, low);
+    used += counts[r];
+  }
+  for (int off = 16; off > 0; off >>= 1) used += __shfl_xor_sync(kFullMask, used, off);
+  __syncthreads();
+  if (lane == 0) s_red[warp] = used;
+  __syncthreads();
+  if (tid == 0) {
+    long long leftover = free_;
+    for (int w = 0; w < kMmThreads / 32; ++w) leftover -= s_red[w];
+    // the requests that can still take a block, keyed by (retained share, request); a min-heap
+    auto less = [&](int a, int b) {
+      return h_level[a] < h_level[b] || (h_level[a] == h_level[b] && h_row[a] < h_row[b]);
+    };
+    auto swap = [&](int a, int b) {
+      const double l = h_level[a];
+      const int row = h_row[a];
+      h_level[a] = h_level[b], h_row[a] = h_row[b], h_level[b] = l, h_row[b] = row;
+    };
+    auto sift_down = [&](int i, int size) {
+      for (;;) {
+        const int a = 2 * i + 1, b = a + 1;
+        int best = i;
+        if (a < size && less(a, best)) best = a;
+        if (b < size && less(b, best)) best = b;
+        if (best == i) return;
+        swap(i, best);
+        i = best;
+      }
+    };
+    int size = 0;
+    for (int r = 0; r < p.rows; ++r) {
+      const int m = p.row_m[r];
+      if (m < 0 || counts[r] >= m) continue;
+      const int c = counts[r];
+      h_level[size] = p.base[r] + (c ? p.prefix[(int64_t)r * p.width + c - 1] : 0.0);
+      h_row[size] = r;
+      ++size;
+    }
+    for (int i = size / 2 - 1; i >= 0; --i) sift_down(i, size);
+    while (leftover > 0 && size > 0) {
+      const int r = h_row[0];
+      const double level = h_level[0];
+      const int c = counts[r]++;
+      --leftover;
+      if (counts[r] < p.row_m[r]) {  // back with its next block's share added (heappop then heappush)
+        h_level[0] = level + p.sorted[(int64_t)r * p.width + c];
+        sift_down(0, size);
+      } else {
+        --size;
+        if (size > 0) {
+          h_level[0] = h_level[size], h_row[0] = h_row[size];
+          sift_down(0, size);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  for (int r = tid; r < p.rows; r += kMmThreads) p.quota[r] = p.row_m[r] < 0 ? -1 : counts[r];
+}
+
+}  // namespace ekv
+
+using namespace ekv;
+
+extern "C" size_t ekv_allocate_maxmin_workspace_bytes(int rows, int width) {
+  if (rows <= 0 || width <= 0) return 0;
+  return mm_layout(rows, width).bytes;
+}
+
+extern "C" int ekv_allocate_maxmin(const float* scores, int64_t score_stride, const int32_t* row_blocks,
+                                   const int32_t* measured_blocks, int recent_blocks, int cap_above_blocks,
+                                   double budget_fraction, int64_t budget, int rows, int width, int32_t* quota,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (!scores || !row_blocks || !quota) return fail(EKV_EINVAL, "a required pointer is NULL");
+  if (rows <= 0 || width <= 0) return fail(EKV_EINVAL, "rows and width must be positive");
+  if (width > kMmMaxWidth) return fail(EKV_ENOTSUP, "width %d > %d", width, kMmMaxWidth);
+  if (rows > kMmMaxRows) return fail(EKV_ENOTSUP, "rows %d > %d", rows, kMmMaxRows);
+  if (score_stride < width) return fail(EKV_EINVAL, "score_stride %lld < width %d", (long long)score_stride, width);
+  if (recent_blocks < -1 || cap_above_blocks < -1) return fail(EKV_EINVAL, "invalid controller settings");
+  if (budget < 0 && !(budget_fraction > 0.0 && budget_fraction <= 1.0))
+    return fail(EKV_EINVAL, "the budget fraction must be in (0, 1]");
+  const MmLayout l = mm_layout(rows, width);
+  if (!workspace || workspace_bytes < l.bytes)
+    return fail(EKV_ERANGE, "the maxmin workspace holds %zu bytes, the call needs %zu", workspace_bytes, l.bytes);
+  if ((uintptr_t)workspace & 255) return fail(EKV_EINVAL, "the maxmin workspace must be 256-byte aligned");
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  MmParams p{};
+  p.scores = scores; p.score_s0 = score_stride; p.row_blocks = row_blocks; p.measured = measured_blocks;
+  p.recent = recent_blocks; p.cap = cap_above_blocks; p.fraction = budget_fraction; p.budget = (long long)budget;
+  p.rows = rows; p.width = width; p.quota = quota;
+  p.state = reinterpret_cast<MmState*>(base + l.state);
+  p.base = reinterpret_cast<double*>(base + l.base);
+  p.row_m = reinterpret_cast<int*>(base + l.row_m);
+  p.req = reinterpret_cast<int*>(base + l.req);
+  p.sorted = reinterpret_cast<double*>(base + l.sorted);
+  p.prefix = reinterpret_cast<double*>(base + l.prefix);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(base + l.state, 0, sizeof(MmState), s) != cudaSuccess)
+    return check_launch("cudaMemsetAsync(maxmin state)");
+  int sort_n = 1;
+  while (sort_n < width) sort_n <<= 1;
+  const size_t prep_smem = round_up((size_t)width * 4, 16) + (size_t)sort_n * 8;
+  const size_t level_smem = (size_t)rows * (8 + 4 + 4);
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
+    return check_launch("cudaGetDevice");
+  static size_t prep_set[kMaxDevices] = {}, level_set[kMaxDevices] = {};
+  if (prep_set[device] < prep_smem) {
+    if (cudaFuncSetAttribute(mm_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem) != cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(mm_prep_kernel)");
+    prep_set[device] = prep_smem;
+  }
+  if (level_set[device] < level_smem) {
+    if (cudaFuncSetAttribute(mm_level_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)level_smem) !=
+        cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(mm_level_kernel)");
+    level_set[device] = level_smem;
+  }
+  mm_prep_kernel<<<rows, kMmThreads, prep_smem, s>>>(p);
+  int rc = check_launch("mm_prep_kernel");
+  if (rc != EKV_OK) return rc;
+  mm_cumsum_kernel<<<(rows + 127) / 128, 128, 0, s>>>(p);
+  if ((rc = check_launch("mm_cumsum_kernel")) != EKV_OK) return rc;
+  mm_level_kernel<<<1, kMmThreads, level_smem, s>>>(p);
+  return check_launch("mm_level_kernel");
+}

@@ -1,0 +1,84 @@
+// numpy.add.reduce's pairwise summation of float64 values, reproduced bit for bit by one CTA.
+//
+// numpy sums a contiguous array of n values as pairwise_sum(a, n): below 8 values a plain loop from
+// 0.0; up to 128 values eight accumulators r[j] += a[i + j] over whole groups of 8, combined as
+// ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)), then the rest one by one; above 128 values
+// pairwise_sum(a, n2) + pairwise_sum(a + n2, n - n2) with n2 = n / 2 rounded down to a multiple of 8.
+// Here the tree is built one level at a time (every node of a level splits in parallel and records its
+// children), the leaves are summed in parallel, and the levels are combined from the bottom up: the
+// same additions in the same order as numpy's recursion.
+#pragma once
+
+#include "ekv_common.cuh"
+
+namespace ekv {
+
+constexpr int kPairwiseMaxNodes = 1024;  // up to 32768 values: at most 512 leaves of more than 64 values
+constexpr int kPairwiseMaxLevels = 16;
+
+struct PairwiseTree {  // shared-memory scratch of block_pairwise_sum
+  int lo[kPairwiseMaxNodes], len[kPairwiseMaxNodes], left[kPairwiseMaxNodes];
+  double val[kPairwiseMaxNodes];
+  int level[kPairwiseMaxLevels + 2];
+  int nodes, depth;
+};
+
+// One leaf of at most 128 values; value(i) gives the i-th value as a double.
+template <typename V>
+__device__ double pairwise_leaf(const V& value, int lo, int len) {
+  if (len < 8) {
+    double res = 0.0;
+    for (int i = 0; i < len; ++i) res += value(lo + i);
+    return res;
+  }
+  double r[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) r[j] = value(lo + j);
+  int i = 8;
+  for (; i < len - (len % 8); i += 8)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] += value(lo + i + j);
+  double res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+  for (; i < len; ++i) res += value(lo + i);
+  return res;
+}
+
+// The sum of value(0 .. n) (n <= 32768) as numpy computes it; every thread of the CTA calls it and
+// gets the sum. THREADS = blockDim.x.
+template <int THREADS, typename V>
+__device__ double block_pairwise_sum(PairwiseTree& t, int n, const V& value) {
+  const int tid = threadIdx.x;
+  __syncthreads();  // the scratch may still be read by an earlier call
+  if (tid == 0) t.lo[0] = 0, t.len[0] = n, t.nodes = 1, t.level[0] = 0, t.level[1] = 1, t.depth = 1;
+  __syncthreads();
+  for (int d = 0; d < kPairwiseMaxLevels; ++d) {  // split the level's nodes; children go after the level
+    const int a = t.level[d], b = t.level[d + 1];
+    if (a == b) break;
+    for (int i = a + tid; i < b; i += THREADS) {
+      const int lo = t.lo[i], len = t.len[i];
+      if (len <= 128) {
+        t.left[i] = -1;
+      } else {
+        int n2 = len / 2;
+        n2 -= n2 % 8;
+        const int c = atomicAdd(&t.nodes, 2);
+        t.lo[c] = lo, t.len[c] = n2, t.lo[c + 1] = lo + n2, t.len[c + 1] = len - n2;
+        t.left[i] = c;
+      }
+    }
+    __syncthreads();
+    if (tid == 0) t.level[d + 2] = t.nodes, t.depth = d + 1;
+    __syncthreads();
+  }
+  for (int i = tid; i < t.nodes; i += THREADS)
+    if (t.left[i] < 0) t.val[i] = pairwise_leaf(value, t.lo[i], t.len[i]);
+  __syncthreads();
+  for (int d = t.depth - 1; d >= 0; --d) {  // each inner node: left + right, deepest level first
+    for (int i = t.level[d] + tid; i < t.level[d + 1]; i += THREADS)
+      if (t.left[i] >= 0) t.val[i] = t.val[t.left[i]] + t.val[t.left[i] + 1];
+    __syncthreads();
+  }
+  return t.val[0];
+}
+
+}  // namespace ekv

@@ -29,7 +29,9 @@ import torch
 from .. import _lib
 
 Objective = Literal["sum", "maxmin", "uniform"]
-_POLICIES = {"sum": _lib.POLICY_SUM, "uniform": _lib.POLICY_UNIFORM, "newest": _lib.POLICY_NEWEST}
+# the view's ranking per objective: maxmin keeps each request's blocks by share, equal shares to the older block
+_POLICIES = {"sum": _lib.POLICY_SUM, "uniform": _lib.POLICY_UNIFORM, "newest": _lib.POLICY_NEWEST,
+             "maxmin": _lib.POLICY_UNIFORM}
 
 
 @dataclass(frozen=True)
@@ -104,6 +106,33 @@ def sum_quotas(
     return quota
 
 
+def maxmin_quotas(
+    scores: torch.Tensor,
+    row_blocks: torch.Tensor,
+    quota: torch.Tensor,
+    *,
+    measured: torch.Tensor | None,
+    recent_blocks: int,
+    cap_above_blocks: int,
+    budget: int = -1,
+    budget_fraction: float = 0.0,
+) -> torch.Tensor:
+    """The per-row quotas of the ``maxmin`` objective with one shared budget (``ekv_allocate_maxmin``), for a
+    view built with the ``uniform`` ranking. Arguments as ``sum_quotas``; no weights."""
+    rows, width = int(scores.shape[0]), int(scores.shape[1])
+    lib = _lib.load()
+    size = int(lib.ekv_allocate_maxmin_workspace_bytes(rows, width))
+    workspace = torch.empty(size + 256, dtype=torch.uint8, device=scores.device)
+    base = (workspace.data_ptr() + 255) // 256 * 256
+    rc = lib.ekv_allocate_maxmin(
+        scores.data_ptr(), scores.stride(0), row_blocks.data_ptr(), None if measured is None else measured.data_ptr(),
+        int(recent_blocks), int(cap_above_blocks), float(budget_fraction), int(budget), rows, width,
+        quota.data_ptr(), base, size, _lib.current_stream(),
+    )
+    _lib.check(rc, "ekv_allocate_maxmin")
+    return quota
+
+
 def allocate(requests: Sequence[Request], budget: int, objective: Objective = "sum") -> list[np.ndarray]:
     """Return, for each request, a bool mask of the blocks to keep. At most ``budget`` blocks are kept."""
     sizes = [len(r.scores) for r in requests]
@@ -121,8 +150,6 @@ def allocate(requests: Sequence[Request], budget: int, objective: Objective = "s
         raise ValueError(f"unknown objective {objective!r}")
     if objective in ("maxmin", "uniform") and any(r.weight != 1.0 for r in requests):
         raise ValueError(f"the {objective} objective does not use request weights")
-    if objective == "maxmin":
-        raise RuntimeError("the maxmin objective is not implemented on the device")
     width = max(sizes) if sizes else 0
     rows = len(requests)
     if rows == 0 or width == 0:
@@ -152,6 +179,9 @@ def allocate(requests: Sequence[Request], budget: int, objective: Objective = "s
         rc = lib.ekv_allocate_quotas(row_blocks.data_ptr(), measured.data_ptr(), -1, -1, 0.0, int(budget), None,
                                      _lib.POLICY_UNIFORM, rows, quota.data_ptr(), stream)
         _lib.check(rc, "ekv_allocate_quotas")
+    elif objective == "maxmin":
+        maxmin_quotas(scores_t, row_blocks, quota, measured=measured, recent_blocks=-1, cap_above_blocks=-1,
+                      budget=int(budget))
     else:
         weights = torch.tensor([float(r.weight) for r in requests], dtype=torch.float64).to(device)
         sum_quotas(scores_t, row_blocks, quota, measured=measured, recent_blocks=-1, cap_above_blocks=-1,

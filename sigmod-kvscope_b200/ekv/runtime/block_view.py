@@ -22,7 +22,9 @@ import torch
 from .. import _lib
 from .audit import AuditPlane
 
-_POLICIES = {"sum": _lib.POLICY_SUM, "uniform": _lib.POLICY_UNIFORM, "newest": _lib.POLICY_NEWEST}
+# the view's ranking per objective: maxmin keeps each request's blocks by share, equal shares to the older block
+_POLICIES = {"sum": _lib.POLICY_SUM, "uniform": _lib.POLICY_UNIFORM, "newest": _lib.POLICY_NEWEST,
+             "maxmin": _lib.POLICY_UNIFORM}
 
 
 class StatisticSwitch(Protocol):
@@ -143,6 +145,14 @@ def plan_view(
 
         sum_quotas(scores, row_blocks, quota, measured=measured, recent_blocks=recent_blocks,
                    cap_above_blocks=cap_above_blocks, budget_fraction=float(budget_fraction), weights=weights)
+    elif policy == "maxmin" and budget_fraction is not None:
+        # one budget: raise the lowest retained share first (allocation.py:121-166)
+        if scores is None:
+            raise ValueError("the maxmin objective ranks by scores")
+        from ..observe.allocation import maxmin_quotas
+
+        maxmin_quotas(scores, row_blocks, quota, measured=measured, recent_blocks=recent_blocks,
+                      cap_above_blocks=cap_above_blocks, budget_fraction=float(budget_fraction))
     else:
         rc = _lib.load().ekv_allocate_quotas(
             row_blocks.data_ptr(), _ptr(measured), int(recent_blocks), int(cap_above_blocks),

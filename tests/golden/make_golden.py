@@ -230,6 +230,39 @@ def view_cases():
     print("view_cases written")
 
 
+def maxmin_cases():
+    """allocate(..., "maxmin") (observe/allocation.py:121-166): requests with ties, without evidence, of one
+    block, and budgets from just above the pins to just below every block."""
+    rng = np.random.default_rng(47)
+    cases = {}
+    for i in range(50):
+        n_req = int(rng.integers(1, 12))
+        sizes = rng.integers(1, 60, n_req)
+        ties = i % 2 == 0
+        scores = [
+            (rng.integers(0, 4, n).astype(np.float32) if ties else rng.random(n).astype(np.float32)).astype(np.float64)
+            for n in sizes
+        ]
+        if i % 5 == 2:
+            scores[0][:] = 0.0  # no evidence: equal shares
+        recent = int(rng.integers(0, 4))
+        pinned = []
+        for n in sizes:
+            p = np.zeros(n, dtype=bool)
+            p[0] = True
+            p[max(0, n - 1 - recent):] = True
+            pinned.append(p)
+        must = sum(int(p.sum()) for p in pinned)
+        total = int(sizes.sum())
+        budget = int(rng.integers(must, total + 1))
+        masks = allocate([Request(scores=x, pinned=p) for x, p in zip(scores, pinned, strict=True)], budget, "maxmin")
+        cases[f"sizes{i}"], cases[f"scores{i}"] = sizes, np.concatenate(scores)
+        cases[f"recent{i}"], cases[f"budget{i}"] = np.int64(recent), np.int64(budget)
+        cases[f"mask{i}"] = np.concatenate(masks)
+    np.savez_compressed(os.path.join(HERE, "maxmin_cases.npz"), **cases)
+    print("maxmin_cases written")
+
+
 def slot_cases():
     """SlotCompactor.compact (runtime/sglang_compact.py:111-167) on SGLang-style CSR batches: the hand
     cases of the reference's own test (tests/test_sglang_view.py:80-104) and seeded random batches with
@@ -287,6 +320,7 @@ def all_cases():
     allocation_cases()
     view_cases()
     slot_cases()
+    maxmin_cases()
 
 
 if __name__ == "__main__":

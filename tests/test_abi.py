@@ -135,6 +135,11 @@ def test_other_entry_points_validate_before_launching(lib):
     assert lib.ekv_allocate_sum(*sum_args) == L.EINVAL  # a fraction above 1 with no explicit budget
     sum_args[7], sum_args[10] = 0.5, 40000
     assert lib.ekv_allocate_sum(*sum_args) == L.ENOTSUP  # wider than 32768
+    # the maxmin quotas: workspace and width are checked before anything is launched
+    mm_args = [fake, 8, fake, None, 4, 0, 0.5, -1, 2, 8, fake, None, 0, None]
+    assert lib.ekv_allocate_maxmin(*mm_args) == L.ERANGE  # no workspace
+    mm_args[11], mm_args[12], mm_args[9] = ctypes.c_void_p(0x1000), 1 << 30, 9000
+    assert lib.ekv_allocate_maxmin(*mm_args) == L.ENOTSUP  # wider than 8192
     # the SGLang compaction: entry size, pointers and strides
     slot_args = [fake, fake, 8, fake, 20, None, 1, 2, 2, 40, 16, 20, fake, fake, fake, 20, fake, fake, None]
     slot_args[2] = 3

@@ -112,6 +112,65 @@ def test_uniform_quotas_over_thousands_of_requests():
             np.testing.assert_array_equal(a, b, err_msg=f"trial {trial}, request {r}")
 
 
+def test_maxmin_matches_the_reference_and_the_oracle():
+    """The water level: the reference's own allocate(..., "maxmin") on 50 cases, then larger requests with
+    ties and requests without evidence against the oracle."""
+    from ekv.observe.allocation import Request, allocate
+
+    g = load_golden("maxmin_cases")
+    for i in range(50):
+        sizes = g[f"sizes{i}"]
+        bounds = np.concatenate([[0], np.cumsum(sizes)])
+        scores = [g[f"scores{i}"][bounds[j] : bounds[j + 1]] for j in range(len(sizes))]
+        pinned = [oa.controller_pins(int(n), int(g[f"recent{i}"])) for n in sizes]
+        masks = allocate([Request(scores=x, pinned=p) for x, p in zip(scores, pinned, strict=True)],
+                         int(g[f"budget{i}"]), "maxmin")
+        np.testing.assert_array_equal(np.concatenate(masks), g[f"mask{i}"], err_msg=f"case {i}")
+    rng = np.random.default_rng(59)
+    for trial in range(12):
+        n_req = int(rng.integers(2, 120))
+        sizes = rng.integers(1, 700, n_req)
+        if trial % 2:
+            scores = [rng.integers(0, 3, n).astype(np.float64) for n in sizes]
+        else:
+            scores = [(rng.random(n) ** 2).astype(np.float32).astype(np.float64) for n in sizes]
+        scores[0][:] = 0.0 if trial % 3 == 0 else scores[0]
+        pinned = [oa.controller_pins(int(n), int(rng.integers(0, 5))) for n in sizes]
+        must = sum(int(p.sum()) for p in pinned)
+        budget = int(rng.integers(must, int(sizes.sum())))
+        got = allocate([Request(scores=x, pinned=p) for x, p in zip(scores, pinned, strict=True)], budget, "maxmin")
+        want = oa.allocate(scores, budget, "maxmin", pinned)
+        for r, (a, b) in enumerate(zip(got, want, strict=True)):
+            np.testing.assert_array_equal(a, b, err_msg=f"trial {trial}, request {r}")
+
+
+def test_plan_view_maxmin_with_a_shared_budget_matches_the_controller():
+    from ekv.runtime.block_view import plan_view
+
+    rng = np.random.default_rng(67)
+    for trial in range(6):
+        rows, width = int(rng.integers(1, 80)), int(rng.integers(8, 600))
+        row_blocks = rng.integers(0, width + 1, rows).astype(np.int32)
+        lens = (row_blocks * 16 - rng.integers(0, 16, rows)).clip(0).astype(np.int32)
+        table = rng.integers(0, 1 << 20, (rows, width)).astype(np.int32)
+        scores = rng.dirichlet(np.full(width, 0.3), rows).astype(np.float32)
+        fraction = float(rng.choice([0.2, 0.5, 0.8]))
+        keep = oa.controller_keep(row_blocks, width, lambda r, n: scores[r, :n].astype(np.float64), fraction, "maxmin",
+                                  recent_blocks=4)
+        mask = torch.empty(rows, width, dtype=torch.uint8).cuda()
+        view, view_lens = plan_view(
+            torch.from_numpy(table).cuda(), torch.from_numpy(lens).cuda(), 16, torch.from_numpy(row_blocks).cuda(),
+            scores=torch.from_numpy(scores).cuda(), policy="maxmin", budget_fraction=fraction, recent_blocks=4,
+            mask_out=mask)
+        got_mask = mask.cpu().numpy()
+        for r in range(rows):
+            n = min(int(row_blocks[r]), width)
+            np.testing.assert_array_equal(got_mask[r, :n], keep[r, :n], err_msg=f"trial {trial} row {r}")
+        ref_view, ref_lens = ov.compact_block_table(table, lens, keep.astype(bool), 16)
+        np.testing.assert_array_equal(view.cpu().numpy(), ref_view, err_msg=f"trial {trial}")
+        np.testing.assert_array_equal(view_lens.cpu().numpy(), ref_lens, err_msg=f"trial {trial}")
+
+
 def test_sum_over_many_requests_against_the_oracle():
     """The global greedy: ties across requests (newer block, then earlier request), weights, requests
     without evidence, and budgets from just above the pins to just below every block."""

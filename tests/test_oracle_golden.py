@@ -198,3 +198,15 @@ def test_oracle_slot_compaction_matches_the_reference_kernels():
         np.testing.assert_array_equal(new_slots, g[f"new_slots{i}"], err_msg=f"case {i}")
         np.testing.assert_array_equal(lens, g[f"lens{i}"], err_msg=f"case {i}")
         np.testing.assert_array_equal(counts, g[f"counts{i}"], err_msg=f"case {i}")
+
+
+def test_oracle_maxmin_matches_the_reference_allocate():
+    """oracle.allocation.water_level against allocate(..., "maxmin") run by make_golden.py."""
+    g = load_golden("maxmin_cases")
+    for i in range(50):
+        sizes = g[f"sizes{i}"]
+        bounds = np.concatenate([[0], np.cumsum(sizes)])
+        scores = [g[f"scores{i}"][bounds[j] : bounds[j + 1]] for j in range(len(sizes))]
+        pinned = [oa.controller_pins(int(n), int(g[f"recent{i}"])) for n in sizes]
+        masks = oa.allocate(scores, int(g[f"budget{i}"]), "maxmin", pinned)
+        np.testing.assert_array_equal(np.concatenate(masks), g[f"mask{i}"], err_msg=f"case {i}")

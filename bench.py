@@ -272,6 +272,9 @@ def view_bench(rank: int, world: int, steps: int, warmup: int, dist_on: bool) ->
     def build_shared():  # the controller's default: `sum` with one budget over every row
         plan_view(t, ln, BLOCK, nn, scores=sc, policy="sum", budget_fraction=0.5, recent_blocks=4, out=out)
 
+    def build_maxmin():  # one budget: raise the lowest retained share first
+        plan_view(t, ln, BLOCK, nn, scores=sc, policy="maxmin", budget_fraction=0.5, recent_blocks=4, out=out)
+
     newest = torch.arange(width, dtype=torch.float32, device=dev).expand(len(nn), width).contiguous()
 
     def build_newest():  # keep-newest: scores = arange(n) under `uniform`, budget 0.5
@@ -306,7 +309,8 @@ def view_bench(rank: int, world: int, steps: int, warmup: int, dist_on: bool) ->
     result["sglang_us"] = round(result["sglang_us"] - result.pop("sglang_restore_us"), 2)
     result["sglang_entries"] = entries
     result["sglang_launches"] = 3
-    for key, fn, launches in (("us", build, 2), ("sum_shared_us", build_shared, 9), ("newest_us", build_newest, 2)):
+    for key, fn, launches in (("us", build, 2), ("sum_shared_us", build_shared, 9), ("maxmin_shared_us", build_maxmin, 4),
+                              ("newest_us", build_newest, 2)):
         graph = capture(fn)
         result[key] = round(timed(graph.replay, steps, warmup, dist_on) / steps * 1e6, 2)
         result[key.replace("us", "launches")] = launches

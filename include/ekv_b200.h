@@ -247,7 +247,7 @@ size_t ekv_allocate_maxmin_workspace_bytes(int rows, int width);
  * over one at a time to the request with the lowest retained share (ties: the earlier request). Rows,
  * pins, budget and quota as in ekv_allocate_sum (no weights: maxmin does not use them); the quotas are
  * for ekv_view_build with EKV_POLICY_UNIFORM (equal shares to the older block). width <= 8192,
- * rows <= 8192. Three kernels and one memset on `stream`, no host synchronisation.
+ * rows <= 4096. Three kernels and one memset on `stream`, no host synchronisation.
  */
 int ekv_allocate_maxmin(const float* scores, int64_t score_stride, const int32_t* row_blocks,
                         const int32_t* measured_blocks, int recent_blocks, int cap_above_blocks,

@@ -25,7 +25,7 @@ namespace ekv {
 
 constexpr int kMmThreads = 1024;
 constexpr int kMmMaxWidth = 8192;
-constexpr int kMmMaxRows = 8192;
+constexpr int kMmMaxRows = 4096;
 constexpr int kMmBisection = 60;
 
 enum MmMode : int { kMmSelect = 0, kMmNone = 1, kMmAll = 2 };
@@ -51,12 +51,14 @@ struct MmParams {
   double* base;     // [rows] pinned share
   int* row_m;       // [rows] unpinned blocks; -1 for a row that is not a request
   int* req;         // [rows] index of the request among the requests
-  double* sorted;   // [rows][width] unpinned shares in decreasing order
-  double* prefix;   // [rows][width] their running sums
+  double* sorted;   // [width][rows] unpinned shares in decreasing order (block-major: a warp's rows adjacent)
+  double* prefix;   // [width][rows] their running sums
+  int* lb_low;      // [rows] the search result at the bisection's low end
+  int* lb_high;     // [rows] ... and at its high end
 };
 
 struct MmLayout {
-  size_t state, base, row_m, req, sorted, prefix, bytes;
+  size_t state, base, row_m, req, lb_low, lb_high, sorted, prefix, bytes;
 };
 
 MmLayout mm_layout(int rows, int width) {
@@ -71,6 +73,8 @@ MmLayout mm_layout(int rows, int width) {
   l.base = take((size_t)rows * 8);
   l.row_m = take((size_t)rows * 4);
   l.req = take((size_t)rows * 4);
+  l.lb_low = take((size_t)rows * 4);
+  l.lb_high = take((size_t)rows * 4);
   l.sorted = take((size_t)rows * width * 8);
   l.prefix = take((size_t)rows * width * 8);
   l.bytes = o;
@@ -127,8 +131,7 @@ __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
         __syncthreads();
       }
     }
-    double* sr = p.sorted + (int64_t)r * p.width;
-    for (int j = tid; j < m; j += kMmThreads) sr[j] = share((int)(s_key[j] & 0xffffffffu));
+    for (int j = tid; j < m; j += kMmThreads) p.sorted[(int64_t)j * p.rows + r] = share((int)(s_key[j] & 0xffffffffu));
     if (tid == 0) {
       p.base[r] = base;
       atomicAdd((unsigned long long*)&p.state->must, (unsigned long long)pin_count(n, ps));
@@ -169,55 +172,68 @@ __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
   }
 }
 
-// A thread per row: prefix[j] = prefix[j - 1] + sorted[j], one addition after another.
-__global__ void __launch_bounds__(128) mm_cumsum_kernel(const MmParams p) {
-  const int r = blockIdx.x * 128 + threadIdx.x;
+// A thread per row: prefix[j] = prefix[j - 1] + sorted[j], one addition after another (block-major
+// arrays: a warp's loads and stores are contiguous).
+__global__ void __launch_bounds__(32) mm_cumsum_kernel(const MmParams p) {
+  const int r = blockIdx.x * 32 + threadIdx.x;
   if (r >= p.rows) return;
   const int m = p.row_m[r];
-  const double* sr = p.sorted + (int64_t)r * p.width;
-  double* pr = p.prefix + (int64_t)r * p.width;
-  double acc = 0.0;
-  int j = 0;
-  for (; j + 8 <= m; j += 8) {  // eight loads in flight, the additions in order
-    double v[8];
+  const int64_t R = p.rows;
+  constexpr int C = 16;  // values per chunk; the next chunk is loaded while this one is added
+  double acc = 0.0, cur[C], nxt[C];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = sr[j + u];
+  for (int u = 0; u < C; ++u) cur[u] = u < m ? p.sorted[u * R + r] : 0.0;
+  for (int j = 0; j < m; j += C) {
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      acc = (j + u == 0) ? v[u] : acc + v[u];
-      pr[j + u] = acc;
+    for (int u = 0; u < C; ++u) nxt[u] = j + C + u < m ? p.sorted[(j + C + u) * R + r] : 0.0;
+#pragma unroll
+    for (int u = 0; u < C; ++u) {
+      if (j + u < m) {
+        acc = (j + u == 0) ? cur[u] : acc + cur[u];
+        p.prefix[(j + u) * R + r] = acc;
+      }
     }
-  }
-  for (; j < m; ++j) {
-    acc = j == 0 ? sr[j] : acc + sr[j];
-    pr[j] = acc;
+#pragma unroll
+    for (int u = 0; u < C; ++u) cur[u] = nxt[u];
   }
 }
 
-// The blocks request r needs beyond its pins to retain `level` (allocation.py:146-150).
-__device__ __forceinline__ int mm_extra(const MmParams& p, int r, double level) {
-  const int m = p.row_m[r];
-  if (m < 0) return 0;
-  const double need = level - p.base[r];
-  if (need <= 1e-12) return 0;
-  const double offset = 2.0 * (double)p.req[r];
-  const double x = need - 1e-12 + offset;
-  const double* pr = p.prefix + (int64_t)r * p.width;
-  int lo = 0, hi = m;  // the first j with prefix[j] + offset >= x (searchsorted, side left)
+// searchsorted (side left) of x in request r's running sums, each plus the request's offset: the first
+// j with prefix[j] + offset >= x, known to lie in [lo, hi] (it grows with x).
+__device__ __forceinline__ int mm_search(const MmParams& p, int r, double x, double offset, int lo, int hi) {
   while (lo < hi) {
     const int mid = (lo + hi) >> 1;
-    if (pr[mid] + offset < x) lo = mid + 1; else hi = mid;
+    if (p.prefix[(int64_t)mid * p.rows + r] + offset < x) lo = mid + 1; else hi = mid;
   }
-  return lo + 1 < m ? lo + 1 : m;
+  return lo;
 }
 
-// One CTA: the water level, the leftover blocks and the quotas. Dynamic shared memory: the heap
-// (double level and int request row per entry) and the counts, rows entries each.
+// The blocks request r needs beyond its pins to retain `level` (allocation.py:146-150), and in *lb the
+// search result it comes from.
+__device__ __forceinline__ int mm_extra(const MmParams& p, int r, double level, int lo, int hi, int* lb) {
+  const int m = p.row_m[r];
+  *lb = lo;
+  if (m < 0) return 0;
+  const double need = level - p.base[r];
+  const double offset = 2.0 * (double)p.req[r];
+  *lb = mm_search(p, r, need - 1e-12 + offset, offset, lo, hi);
+  if (need <= 1e-12) return 0;
+  return *lb + 1 < m ? *lb + 1 : m;
+}
+
+constexpr int kMmAhead = 2;  // next shares per request staged in shared memory for the leftover blocks
+constexpr size_t kMmLevelBytesPerRow = 8 + 8 * kMmAhead + 4 * 3;
+
+// One CTA: the water level, the leftover blocks and the quotas. Dynamic shared memory per request: the
+// heap entry (double level, int row), the next kMmAhead shares, the count and the count at the start
+// of the leftover blocks.
 __global__ void __launch_bounds__(kMmThreads) mm_level_kernel(const MmParams p) {
   extern __shared__ __align__(16) unsigned char lv_smem[];
   double* h_level = reinterpret_cast<double*>(lv_smem);
-  int* h_row = reinterpret_cast<int*>(h_level + p.rows);
+  double* ahead = h_level + p.rows;  // [rows][kMmAhead]
+  int* h_row = reinterpret_cast<int*>(ahead + (size_t)p.rows * kMmAhead);
   int* counts = h_row + p.rows;
+  int* start = counts + p.rows;
   __shared__ long long s_red[kMmThreads / 32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const MmState* st = p.state;
@@ -230,30 +246,49 @@ __global__ void __launch_bounds__(kMmThreads) mm_level_kernel(const MmParams p) 
     return;
   }
   const long long free_ = st->free_;
-  auto total_extra = [&](double level) {
+  // each request's search result is monotone in the level: keep it at both ends of the bisection and
+  // search only between them
+  for (int r = tid; r < p.rows; r += kMmThreads) {
+    const int m = p.row_m[r];
+    p.lb_low[r] = 0;
+    p.lb_high[r] = m > 0 ? m : 0;
+  }
+  double low = 0.0, high = 1.0;
+  for (int it = 0; it < kMmBisection; ++it) {
+    const double mid = (low + high) / 2;
     long long sum = 0;
-    for (int r = tid; r < p.rows; r += kMmThreads) sum += mm_extra(p, r, level);
+    for (int r = tid; r < p.rows; r += kMmThreads) {
+      int lb;
+      sum += mm_extra(p, r, mid, p.lb_low[r], p.lb_high[r], &lb);
+      counts[r] = lb;  // (scratch: the search result at mid)
+    }
     for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(kFullMask, sum, off);
     __syncthreads();
     if (lane == 0) s_red[warp] = sum;
     __syncthreads();
     long long t = 0;
     for (int w = 0; w < kMmThreads / 32; ++w) t += s_red[w];
-    return t;
-  };
-  double low = 0.0, high = 1.0;
-  for (int it = 0; it < kMmBisection; ++it) {
-    const double mid = (low + high) / 2;
-    if (total_extra(mid) <= free_) low = mid; else high = mid;
+    const bool up = t <= free_;
+    for (int r = tid; r < p.rows; r += kMmThreads) (up ? p.lb_low : p.lb_high)[r] = counts[r];
+    if (up) low = mid; else high = mid;
   }
   long long used = 0;
   for (int r = tid; r < p.rows; r += kMmThreads) {
-    counts[r] = mm_extra(p, r, low);
+    int lb;
+    counts[r] = mm_extra(p, r, low, p.lb_low[r], p.lb_low[r], &lb);
     used += counts[r];
   }
   for (int off = 16; off > 0; off >>= 1) used += __shfl_xor_sync(kFullMask, used, off);
   __syncthreads();
   if (lane == 0) s_red[warp] = used;
+  // each request's retained share (its heap entry) and the shares of its next blocks, loaded in parallel
+  for (int r = tid; r < p.rows; r += kMmThreads) {
+    const int m = p.row_m[r], c = counts[r];
+    h_level[r] = m < 0 ? 0.0 : p.base[r] + (c ? p.prefix[(int64_t)(c - 1) * p.rows + r] : 0.0);
+    start[r] = c;
+#pragma unroll
+    for (int a = 0; a < kMmAhead; ++a) ahead[(size_t)r * kMmAhead + a] = c + a < m ? p.sorted[(int64_t)(c + a) * p.rows + r] : 0.0;
+  }
   __syncthreads();
   if (tid == 0) {
     long long leftover = free_;
@@ -278,12 +313,11 @@ __global__ void __launch_bounds__(kMmThreads) mm_level_kernel(const MmParams p) 
         i = best;
       }
     };
-    int size = 0;
+    int size = 0;  // the requests that can take a block, in order (an in-place compaction)
     for (int r = 0; r < p.rows; ++r) {
       const int m = p.row_m[r];
       if (m < 0 || counts[r] >= m) continue;
-      const int c = counts[r];
-      h_level[size] = p.base[r] + (c ? p.prefix[(int64_t)r * p.width + c - 1] : 0.0);
+      h_level[size] = h_level[r];
       h_row[size] = r;
       ++size;
     }
@@ -294,7 +328,8 @@ __global__ void __launch_bounds__(kMmThreads) mm_level_kernel(const MmParams p) 
       const int c = counts[r]++;
       --leftover;
       if (counts[r] < p.row_m[r]) {  // back with its next block's share added (heappop then heappush)
-        h_level[0] = level + p.sorted[(int64_t)r * p.width + c];
+        const int a = c - start[r];
+        h_level[0] = level + (a < kMmAhead ? ahead[(size_t)r * kMmAhead + a] : p.sorted[(int64_t)c * p.rows + r]);
         sift_down(0, size);
       } else {
         --size;
@@ -345,6 +380,8 @@ extern "C" int ekv_allocate_maxmin(const float* scores, int64_t score_stride, co
   p.row_m = reinterpret_cast<int*>(base + l.row_m);
   p.req = reinterpret_cast<int*>(base + l.req);
   p.sorted = reinterpret_cast<double*>(base + l.sorted);
+  p.lb_low = reinterpret_cast<int*>(base + l.lb_low);
+  p.lb_high = reinterpret_cast<int*>(base + l.lb_high);
   p.prefix = reinterpret_cast<double*>(base + l.prefix);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(base + l.state, 0, sizeof(MmState), s) != cudaSuccess)
@@ -352,7 +389,7 @@ extern "C" int ekv_allocate_maxmin(const float* scores, int64_t score_stride, co
   int sort_n = 1;
   while (sort_n < width) sort_n <<= 1;
   const size_t prep_smem = round_up((size_t)width * 4, 16) + (size_t)sort_n * 8;
-  const size_t level_smem = (size_t)rows * (8 + 4 + 4);
+  const size_t level_smem = (size_t)rows * kMmLevelBytesPerRow;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
     return check_launch("cudaGetDevice");
@@ -371,7 +408,7 @@ extern "C" int ekv_allocate_maxmin(const float* scores, int64_t score_stride, co
   mm_prep_kernel<<<rows, kMmThreads, prep_smem, s>>>(p);
   int rc = check_launch("mm_prep_kernel");
   if (rc != EKV_OK) return rc;
-  mm_cumsum_kernel<<<(rows + 127) / 128, 128, 0, s>>>(p);
+  mm_cumsum_kernel<<<(rows + 31) / 32, 32, 0, s>>>(p);
   if ((rc = check_launch("mm_cumsum_kernel")) != EKV_OK) return rc;
   mm_level_kernel<<<1, kMmThreads, level_smem, s>>>(p);
   return check_launch("mm_level_kernel");

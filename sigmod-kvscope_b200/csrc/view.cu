@@ -343,7 +343,16 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
   if (by_threshold) {
     cp_async_wait<1>();  // the shares have landed (the table may still be in flight)
     __syncthreads();
-    for (int b = 1 + threadIdx.x; b < ps; b += kViewThreads) keys[b] = share_key(__uint_as_float(keys[b]));
+    // keys are handled four at a time (16-byte shared loads); position 0 and positions from ps on are
+    // not keys
+    const int groups = (ps + 3) >> 2;
+    uint4* keys4 = reinterpret_cast<uint4*>(keys);
+    for (int g = threadIdx.x; g < groups; g += kViewThreads) {
+      uint4 v = keys4[g];
+      v.x = share_key(__uint_as_float(v.x)), v.y = share_key(__uint_as_float(v.y));
+      v.z = share_key(__uint_as_float(v.z)), v.w = share_key(__uint_as_float(v.w));
+      keys4[g] = v;
+    }
     reinterpret_cast<int4*>(s_hist)[threadIdx.x] = make_int4(0, 0, 0, 0);
     __syncthreads();
     int k = q;
@@ -351,9 +360,15 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
     for (int pass = 0; pass < 3; ++pass) {
       const int shift = pass == 0 ? 20 : (pass == 1 ? 9 : 0);
       const uint32_t dmask = pass == 2 ? 511u : 2047u;
-      for (int b = 1 + threadIdx.x; b < ps; b += kViewThreads) {
-        const uint32_t key = keys[b];
-        if ((key & pmask) == prefix) atomicAdd(&s_hist[(key >> shift) & dmask], 1);
+      for (int g = threadIdx.x; g < groups; g += kViewThreads) {
+        const uint4 v = keys4[g];
+        const uint32_t kv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int b = 4 * g + j;
+          const bool in = b >= 1 && b < ps && (kv[j] & pmask) == prefix;
+          if (in) atomicAdd(&s_hist[(kv[j] >> shift) & dmask], 1);
+        }
       }
       __syncthreads();
       const int4 h = reinterpret_cast<const int4*>(s_hist)[threadIdx.x];
@@ -408,6 +423,17 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
 
   // ---- pass 1: the final keep flag of every laid-out position, as one ballot per iteration ---------
   int kept_count = 0, eq_seen = eq_base;
+  if (rank_mode && by_threshold && !ties && mrow == nullptr && rrow == nullptr && !full) {
+    // the common case: a key at or above the threshold is kept; outside [1, open_hi) every block is
+    for (int i = 0; i < iters; ++i) {
+      const int b = wbase + 32 * i + lane;
+      const uint32_t key = (b >= 1 && b < open_hi) ? keys[b] & pmask : 0xffffffffu;
+      const bool keep = (key >= prefix || b == 0 || b == blocks - 1) && b < blocks && b < W;
+      const uint32_t bits = __ballot_sync(kFullMask, keep);
+      if (lane == 0) s_bits[warp][i] = bits;
+      kept_count += __popc(bits);
+    }
+  } else
   for (int i = 0; i < iters; ++i) {
     const int b = wbase + 32 * i + lane;
     const bool in_row = b < W;

@@ -207,17 +207,10 @@ __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p
     int shift0;
     unsigned long long dmask0;
     digit_of(0, shift0, dmask0);
-    for (int base = 1; base < ps; base += kSumThreads) {  // the keys and pass 0 of the select
-      const int b = base + tid;  // (warp-uniform trip count)
-      unsigned int digit = kSumBins;
-      if (b < ps) {
-        const unsigned long long key = gain_key(s_x[b], total, w, n);
-        kr[b] = key;
-        digit = (unsigned int)((key >> shift0) & dmask0);
-      }
-      // the keys of a row share a few exponents: one shared-memory atomic per digit and warp
-      const unsigned int same = __match_any_sync(kFullMask, digit);
-      if (digit < kSumBins && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&s_hist[digit], __popc(same));
+    for (int b = 1 + tid; b < ps; b += kSumThreads) {  // the keys and pass 0 of the select
+      const unsigned long long key = gain_key(s_x[b], total, w, n);
+      kr[b] = key;
+      atomicAdd(&s_hist[(key >> shift0) & dmask0], 1u);
     }
   }
   __syncthreads();

@@ -416,3 +416,41 @@ def test_one_step_launch_equals_per_layer_launches():
     L.check(rc, "ekv_audit_step")
     torch.cuda.synchronize()
     assert torch.equal(torch.nan_to_num(run.share, 3.0), torch.nan_to_num(step.share, 3.0))
+
+
+def test_long_context_rows_match_the_c_oracle():
+    """Rows of 32k to 128k tokens in an 8192-block table (the long-context shape): every cell against the C
+    restatement of the reference kernel, the shares against the oracle's normalisation."""
+    from oracle import cpu as ocpu
+
+    rows, q_heads, kv_heads, width = 6, 32, 8, 8192
+    rng = np.random.default_rng(13)
+    lens = rng.integers(32768, 131073, rows)
+    lens[0], lens[1] = 131072, 32769  # the widest row, and a tail block of one token
+    blocks = -(-lens // 16)
+    pool = int(blocks.sum()) + 7
+    ids = rng.permutation(pool)[: int(blocks.sum())].astype(np.int32)
+    table = np.zeros((rows, width), dtype=np.int32)
+    start = 0
+    for r in range(rows):
+        table[r, : blocks[r]] = ids[start : start + blocks[r]]
+        start += blocks[r]
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    q = torch.randn(rows + 3, q_heads, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    k = torch.randn(pool, 16, kv_heads, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    qrow = rng.permutation(rows + 3)[:rows].astype(np.int32)
+    run = launch(q, k, torch.from_numpy(table), torch.from_numpy(lens.astype(np.int32)), torch.from_numpy(qrow),
+                 [1] * rows, True, 1, 0, 4)
+    assert int(run.status.item()) == 0
+    ref = oaud.new_table(1, rows, width, 4)
+    q16 = q.cpu().view(torch.int16).numpy().view(np.uint16)
+    k16 = k.cpu().view(torch.int16).numpy().view(np.uint16)
+    ocpu.tile_lse(q16, k16, "bf16", table, lens.astype(np.int32), qrow, np.ones(rows, dtype=np.uint8), 1, ref,
+                  1 / math.sqrt(128), 0, 0, 16, 2)
+    got = run.lse.cpu().numpy()
+    w = ~np.isnan(ref)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    np.testing.assert_allclose(got[w], ref[w], **LSE_TOL)
+    u = osh.log_weights(ref, 1, np.arange(rows), 2)
+    share = run.share.cpu().numpy().astype(np.float64)
+    np.testing.assert_allclose(share, osh.normalize(u, blocks, 2), **SHARE_TOL)

@@ -276,6 +276,25 @@ def view_bench(rank: int, world: int, steps: int, warmup: int, dist_on: bool) ->
         plan_view(t, ln, BLOCK, nn, scores=sc, policy="maxmin", budget_fraction=0.5, recent_blocks=4, out=out)
 
     newest = torch.arange(width, dtype=torch.float32, device=dev).expand(len(nn), width).contiguous()
+    # float64 scores, as the controller smooths them: 0.5 * older shares + 0.5 * the latest audit's
+    older = torch.distributions.Dirichlet(torch.full((width,), 0.3, dtype=torch.float64)).sample((rows_total,))
+    sc64 = (0.5 * older[mine].to(dev) + 0.5 * sc.double()).contiguous()
+
+    def build_shared64():  # the controller's default over float64 shares, ranked by the float64 gains
+        plan_view(t, ln, BLOCK, nn, scores=sc64, policy="sum", budget_fraction=0.5, recent_blocks=4, out=out)
+
+    # the controller's decide stage on the device: fold an audit of every row into the per-request ledger,
+    # then the committed keep mask of every row (one host synchronisation: the evidence bytes)
+    from ekv.observe.controller import ShareLedger
+
+    ledger = ShareLedger(width, capacity=len(nn))
+    req_keys = np.arange(1, len(nn) + 1, dtype=np.uint64) + np.uint64(rank * rows_total)
+    req_lens = nn.cpu().numpy().astype(np.int64)
+    ledger.absorb(sc, req_keys, req_lens)
+
+    def controller_tick():
+        ledger.absorb(sc, req_keys, req_lens)
+        ledger.keep_mask(req_keys, req_lens, budget_fraction=0.5, objective="sum", recent_blocks=4)
 
     def build_newest():  # keep-newest: scores = arange(n) under `uniform`, budget 0.5
         plan_view(t, ln, BLOCK, nn, scores=newest, policy="uniform", budget_fraction=0.5, recent_blocks=0, out=out)
@@ -309,12 +328,15 @@ def view_bench(rank: int, world: int, steps: int, warmup: int, dist_on: bool) ->
     result["sglang_us"] = round(result["sglang_us"] - result.pop("sglang_restore_us"), 2)
     result["sglang_entries"] = entries
     result["sglang_launches"] = 3
-    for key, fn, launches in (("us", build, 2), ("sum_shared_us", build_shared, 9), ("maxmin_shared_us", build_maxmin, 4),
-                              ("newest_us", build_newest, 2)):
+    for key, fn, launches in (("us", build, 2), ("sum_shared_us", build_shared, 10), ("maxmin_shared_us", build_maxmin, 4),
+                              ("newest_us", build_newest, 2), ("sum_shared_f64_us", build_shared64, 10)):
         graph = capture(fn)
         result[key] = round(timed(graph.replay, steps, warmup, dist_on) / steps * 1e6, 2)
         result[key.replace("us", "launches")] = launches
         del graph
+    # not capturable (the fold reads its evidence bytes back): timed as called, host work included
+    result["controller_tick_us"] = round(timed(controller_tick, steps, warmup, dist_on) / steps * 1e6, 2)
+    result["controller_tick_launches"] = 11
     return result
 
 

@@ -210,13 +210,15 @@ int ekv_share_finalize(const float* share_acc, const int32_t* contributors, cons
  * as the controller computes it -- split by `uniform` quotas with largest remainders (objective
  * EKV_POLICY_UNIFORM or EKV_POLICY_NEWEST). With row_fraction != NULL (float64 [rows]) every row is
  * its own allocate() call with budget max(pins, ceil(row_fraction[r] * row_blocks[r])) (any
- * objective). quota [rows] int32: the unpinned blocks to keep, or -1 for a row that is not measured
+ * objective). A measured row of more than `width` blocks (width > 0) takes part with width of them,
+ * as the controller's n = min(length, row_width) (controller.py:414); width = 0 sets no limit.
+ * quota [rows] int32: the unpinned blocks to keep, or -1 for a row that is not measured
  * (it reads in full). One CTA; rows <= 8192 for a shared budget, <= 65536 otherwise.
  */
 int ekv_allocate_quotas(const int32_t* row_blocks, const int32_t* measured_blocks,
                         int recent_blocks, int cap_above_blocks, double budget_fraction,
                         int64_t budget, const double* row_fraction, int objective, int rows,
-                        int32_t* quota, void* stream);
+                        int width, int32_t* quota, void* stream);
 
 /*
  * ekv_decode_view -- DecodeView.build on the device: keep algebra, compaction and read counters in one
@@ -296,6 +298,65 @@ int ekv_allocate_sum(const float* scores, int64_t score_stride, const double* we
                      const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,
                      int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
                      int32_t* quota, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * ekv_allocate_sum_f64 -- ekv_allocate_sum over float64 scores, which float32 need not hold
+ * (the controller's smoothed shares, observe/controller.py:340-343).
+ *
+ * Row r's scores are scores[score_rows[r]][0..n) (score_rows may be NULL: row r), so a ledger of shares
+ * per request (ekv_ledger_absorb) is read in place. The quotas are for ekv_view_build_f64 with
+ * EKV_POLICY_SUM, the same weights and the same pins. width <= 16384. Same workspace as ekv_allocate_sum.
+ */
+int ekv_allocate_sum_f64(const double* scores, int64_t score_stride, const int32_t* score_rows,
+                         const double* weights, const int32_t* row_blocks, const int32_t* measured_blocks,
+                         int recent_blocks, int cap_above_blocks, double budget_fraction, int64_t budget,
+                         int rows, int width, int32_t* quota, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/*
+ * ekv_allocate_maxmin_f64 -- ekv_allocate_maxmin over float64 scores; score_rows as in
+ * ekv_allocate_sum_f64. The quotas are for ekv_view_build_f64 with EKV_POLICY_UNIFORM. width <= 8192,
+ * rows <= 4096. Same workspace as ekv_allocate_maxmin.
+ */
+int ekv_allocate_maxmin_f64(const double* scores, int64_t score_stride, const int32_t* score_rows,
+                            const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,
+                            int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
+                            int32_t* quota, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * ekv_view_build_f64 -- ekv_view_build in ranking mode over float64 scores.
+ *
+ * A request's unpinned blocks are ranked by the float64 value the reference ranks: its gain
+ * weight * share (EKV_POLICY_SUM, allocation.py:107) or its share (EKV_POLICY_UNIFORM, :89; weights
+ * then must be NULL or 1), share = max(score, 0) / total with total NumPy's pairwise sum of the
+ * request's clamped scores (1 / n when it is not positive, :46-52); distinct scores with equal shares
+ * tie. scores[score_rows[r]] (score_rows may be NULL: row r), weights [rows] float64 (NULL: 1.0).
+ * view == NULL writes mask_out only (the controller's committed mask, controller.py:401, :445): table,
+ * seq_lens and view_lens are then not read. width <= 16384.
+ */
+int ekv_view_build_f64(const int32_t* table, int64_t table_stride, const int32_t* seq_lens,
+                       const int32_t* row_blocks, const int32_t* quota, const int32_t* measured_blocks,
+                       int recent_blocks, const double* scores, int64_t score_stride, const int32_t* score_rows,
+                       const double* weights, int policy, const uint8_t* full_rows, const uint8_t* released,
+                       int64_t released_stride, int rows, int width, int block_size, int32_t* view,
+                       int64_t view_stride, int32_t* view_lens, uint8_t* mask_out, int64_t mask_stride,
+                       void* stream);
+
+/*
+ * ekv_ledger_absorb -- fold one audit's shares into the per-request shares (Controller._absorb_audit,
+ * observe/controller.py:332-345).
+ *
+ * fresh [rows][fresh_stride] (float32, or float64 when fresh_f64 != 0) is the audit's share of each row.
+ * Row r belongs to the request whose shares are ledger row slot[r] (float64 [ledger_rows][ledger_stride]);
+ * slot[r] < 0 (or >= ledger_rows) skips the row. A row with no value other than NaN carries no evidence:
+ * evidence[r] = 0 and the ledger is left alone. Otherwise evidence[r] = 1 and the ledger row becomes
+ * nan_to_num(fresh[r]) (blend[r] == 0: a request with no shares yet) or
+ * decay * ledger + (1 - decay) * nan_to_num(fresh[r]), rounded as NumPy rounds it. decay in [0, 1).
+ * The slots of one call must be distinct. One kernel, no host synchronisation.
+ */
+int ekv_ledger_absorb(const void* fresh, int fresh_f64, int64_t fresh_stride, const int32_t* slot,
+                      const uint8_t* blend, double decay, int rows, int width, double* ledger,
+                      int64_t ledger_stride, int ledger_rows, uint8_t* evidence, void* stream);
 
 /*
  * ekv_view_build -- the per-row keep decision and the compacted block-table view, in one kernel.

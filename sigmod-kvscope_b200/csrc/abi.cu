@@ -30,4 +30,4 @@ int check_launch(const char* what) {
 
 extern "C" const char* ekv_last_error_string(void) { return ekv::g_error; }
 
-extern "C" int ekv_abi_version(void) { return 3; }
+extern "C" int ekv_abi_version(void) { return 4; }

@@ -52,8 +52,9 @@ struct SumState {
 };
 
 struct SumParams {
-  const float* scores;
+  const void* scores;          // float or double [.][score_s0] (sum_prep_kernel<float> / <double>)
   int64_t score_s0;
+  const int32_t* score_rows;   // may be NULL: row r's scores are scores row score_rows[r]
   const double* weights;
   const int32_t* row_blocks;
   const int32_t* measured;
@@ -111,12 +112,14 @@ SumLayout sum_layout(int rows, int width) {
 
 // max(score, 0) in float64; NaN counts as 0, as the controller passes it (observe/controller.py:337).
 __device__ __forceinline__ double clamped(float s) { return s > 0.f ? (double)s : 0.0; }
+__device__ __forceinline__ double clamped(double s) { return s > 0.0 ? s : 0.0; }
 
 // The order-preserving key of request r's gain at a block with score s: the bits of the
-// non-negative float64 gain (0 for a gain of +-0).
-__device__ __forceinline__ unsigned long long gain_key(float s, double total, double w, int n) {
-  const double share = total > 0.0 ? clamped(s) / total : 1.0 / (double)(n > 1 ? n : 1);
-  const double g = w * share;
+// non-negative float64 gain (0 for a gain of +-0), each operation rounded as NumPy rounds it.
+template <typename S>
+__device__ __forceinline__ unsigned long long gain_key(S s, double total, double w, int n) {
+  const double share = total > 0.0 ? __ddiv_rn(clamped(s), total) : __ddiv_rn(1.0, (double)(n > 1 ? n : 1));
+  const double g = __dmul_rn(w, share);
   return g > 0.0 ? (unsigned long long)__double_as_longlong(g) : 0ull;
 }
 
@@ -183,8 +186,10 @@ __device__ void pick_digit(SumState* st, unsigned int* hist, int pass) {
 
 // One CTA per row: the total (numpy's pairwise sum, pairwise.cuh), the keys, the pins; the CTA that
 // finishes last sets the budget.
+template <typename S>
 __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p) {
-  extern __shared__ float s_x[];  // [width]: the row's scores
+  extern __shared__ __align__(16) unsigned char sum_smem[];
+  S* s_x = reinterpret_cast<S*>(sum_smem);  // [width]: the row's scores
   __shared__ unsigned int s_hist[kSumBins];
   __shared__ PairwiseTree s_tree;
   __shared__ double s_total;
@@ -193,7 +198,7 @@ __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p
   int n = p.row_blocks[r];
   const bool request = n > p.cap && n > 0;
   if (n > p.width) n = p.width;
-  const float* xg = p.scores + (int64_t)r * p.score_s0;
+  const S* xg = static_cast<const S*>(p.scores) + (p.score_rows != nullptr ? (int64_t)p.score_rows[r] : (int64_t)r) * p.score_s0;
   const int ps = request ? pin_start(n, p.recent, p.measured, r) : 0;
   const double w = p.weights ? p.weights[r] : 1.0;
   for (int i = tid; i < kSumBins; i += kSumThreads) s_hist[i] = 0;
@@ -457,14 +462,16 @@ extern "C" size_t ekv_allocate_sum_workspace_bytes(int rows, int width) {
   return sum_layout(rows, width).bytes;
 }
 
-extern "C" int ekv_allocate_sum(const float* scores, int64_t score_stride, const double* weights,
-                                const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,
-                                int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
-                                int32_t* quota, void* workspace, size_t workspace_bytes, void* stream) {
+template <typename S>
+static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* score_rows, const double* weights,
+                        const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,
+                        int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
+                        int32_t* quota, void* workspace, size_t workspace_bytes, void* stream) {
+  constexpr int max_width = sizeof(S) == 8 ? kSumMaxWidth / 2 : kSumMaxWidth;  // the prep kernel stages a row
   clear_error();
   if (!scores || !row_blocks || !quota) return fail(EKV_EINVAL, "a required pointer is NULL");
   if (rows <= 0 || width <= 0) return fail(EKV_EINVAL, "rows and width must be positive");
-  if (width > kSumMaxWidth) return fail(EKV_ENOTSUP, "width %d > %d", width, kSumMaxWidth);
+  if (width > max_width) return fail(EKV_ENOTSUP, "width %d > %d", width, max_width);
   if (rows > kSumMaxRows) return fail(EKV_ENOTSUP, "rows %d > %d", rows, kSumMaxRows);
   if (score_stride < width) return fail(EKV_EINVAL, "score_stride %lld < width %d", (long long)score_stride, width);
   if (recent_blocks < -1 || cap_above_blocks < -1) return fail(EKV_EINVAL, "invalid controller settings");
@@ -476,7 +483,7 @@ extern "C" int ekv_allocate_sum(const float* scores, int64_t score_stride, const
   if ((uintptr_t)workspace & 255) return fail(EKV_EINVAL, "the sum workspace must be 256-byte aligned");
   uint8_t* base = static_cast<uint8_t*>(workspace);
   SumParams p{};
-  p.scores = scores; p.score_s0 = score_stride; p.weights = weights; p.row_blocks = row_blocks;
+  p.scores = scores; p.score_s0 = score_stride; p.score_rows = score_rows; p.weights = weights; p.row_blocks = row_blocks;
   p.measured = measured_blocks; p.recent = recent_blocks; p.cap = cap_above_blocks;
   p.fraction = budget_fraction; p.budget = (long long)budget; p.rows = rows; p.width = width; p.quota = quota;
   p.state = reinterpret_cast<SumState*>(base + l.state);
@@ -498,15 +505,15 @@ extern "C" int ekv_allocate_sum(const float* scores, int64_t score_stride, const
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
     return check_launch("cudaDeviceGetAttribute");
-  const size_t prep_smem = (size_t)width * sizeof(float);
+  const size_t prep_smem = (size_t)width * sizeof(S);
   static size_t configured[kMaxDevices] = {};
   if (configured[device] < prep_smem) {
-    if (cudaFuncSetAttribute(sum_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem) !=
+    if (cudaFuncSetAttribute(sum_prep_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem) !=
         cudaSuccess)
       return check_launch("cudaFuncSetAttribute(sum_prep_kernel)");
     configured[device] = prep_smem;
   }
-  sum_prep_kernel<<<rows, kSumThreads, prep_smem, s>>>(p);
+  sum_prep_kernel<S><<<rows, kSumThreads, prep_smem, s>>>(p);
   int rc = check_launch("sum_prep_kernel");
   if (rc == EKV_OK) {
     sum_keys_pass_kernel<<<dim3(cdiv(width, kSumChunk), rows), kSumThreads, 0, s>>>(p);
@@ -524,4 +531,23 @@ extern "C" int ekv_allocate_sum(const float* scores, int64_t score_stride, const
   if ((rc = check_launch("sum_kept_kernel")) != EKV_OK) return rc;
   sum_quota_kernel<<<1, 1024, 0, s>>>(p);
   return check_launch("sum_quota_kernel");
+}
+
+extern "C" int ekv_allocate_sum(const float* scores, int64_t score_stride, const double* weights,
+                                const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,
+                                int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
+                                int32_t* quota, void* workspace, size_t workspace_bytes, void* stream) {
+  return allocate_sum<float>(scores, score_stride, nullptr, weights, row_blocks, measured_blocks, recent_blocks,
+                             cap_above_blocks, budget_fraction, budget, rows, width, quota, workspace,
+                             workspace_bytes, stream);
+}
+
+extern "C" int ekv_allocate_sum_f64(const double* scores, int64_t score_stride, const int32_t* score_rows,
+                                    const double* weights, const int32_t* row_blocks, const int32_t* measured_blocks,
+                                    int recent_blocks, int cap_above_blocks, double budget_fraction, int64_t budget,
+                                    int rows, int width, int32_t* quota, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  return allocate_sum<double>(scores, score_stride, score_rows, weights, row_blocks, measured_blocks,
+                              recent_blocks, cap_above_blocks, budget_fraction, budget, rows, width, quota,
+                              workspace, workspace_bytes, stream);
 }

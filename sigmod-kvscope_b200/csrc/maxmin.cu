@@ -37,8 +37,9 @@ struct MmState {
 };
 
 struct MmParams {
-  const float* scores;
+  const void* scores;          // float or double [.][score_s0] (mm_prep_kernel<float> / <double>)
   int64_t score_s0;
+  const int32_t* score_rows;   // may be NULL: row r's scores are scores row score_rows[r]
   const int32_t* row_blocks;
   const int32_t* measured;
   int recent, cap;
@@ -82,41 +83,70 @@ MmLayout mm_layout(int rows, int width) {
 }
 
 __device__ __forceinline__ double mm_clamped(float s) { return s > 0.f ? (double)s : 0.0; }
+__device__ __forceinline__ double mm_clamped(double s) { return s > 0.0 ? s : 0.0; }
+
+__host__ __device__ __forceinline__ int mm_sort_n(int width) {
+  int n = 1;
+  while (n < width) n <<= 1;
+  return n;
+}
+
+// Shared memory of mm_prep_kernel<S>: the row's scores, the sort keys (uint64 [mm_sort_n(width)]) and,
+// for float64 scores, the block of each key (uint32 [mm_sort_n(width)]).
+template <typename S>
+__host__ __device__ __forceinline__ size_t mm_prep_smem(int width) {
+  const size_t scores = ((size_t)width * sizeof(S) + 15) / 16 * 16;
+  return scores + (size_t)mm_sort_n(width) * (sizeof(S) == 8 ? 12 : 8);
+}
 
 // max(score, 0) as an order-preserving uint32 (NaN as 0)
 __device__ __forceinline__ uint32_t mm_score_key(float s) { return s > 0.f ? __float_as_uint(s) : 0u; }
 
-// One CTA per row. Dynamic shared memory: the row's scores (float [width]) and the sort keys
-// (uint64 [next power of two >= width]).
+// One CTA per row. Float32 scores sort one uint64 per block, (~score bits, block): for scores that
+// float32 holds, the order of the scores is the order of the shares. Float64 scores sort pairs
+// (~share bits, block), the share being the very float64 value the reference orders
+// (allocation.py:129): distinct scores can give equal shares.
+template <typename S>
 __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
   extern __shared__ __align__(16) unsigned char mm_smem[];
   __shared__ PairwiseTree s_tree;
   __shared__ bool s_last;
+  constexpr bool kWide = sizeof(S) == 8;
   const int r = blockIdx.x, tid = threadIdx.x;
   int n = p.row_blocks[r];
   const bool request = n > p.cap && n > 0;
   if (n > p.width) n = p.width;
-  float* s_x = reinterpret_cast<float*>(mm_smem);
-  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(mm_smem + ((size_t)p.width * 4 + 15) / 16 * 16);
+  S* s_x = reinterpret_cast<S*>(mm_smem);
+  unsigned long long* s_key =
+      reinterpret_cast<unsigned long long*>(mm_smem + ((size_t)p.width * sizeof(S) + 15) / 16 * 16);
+  uint32_t* s_blk = reinterpret_cast<uint32_t*>(s_key + mm_sort_n(p.width));  // float64 scores only
   const int ps = request ? pin_start(n, p.recent, p.measured, r) : 0;
   const int m = ps > 1 ? ps - 1 : 0;  // unpinned blocks [1, ps)
   if (request) {
-    const float* xg = p.scores + (int64_t)r * p.score_s0;
+    const S* xg = static_cast<const S*>(p.scores) +
+                  (p.score_rows != nullptr ? (int64_t)p.score_rows[r] : (int64_t)r) * p.score_s0;
     for (int i = tid; i < n; i += kMmThreads) s_x[i] = xg[i];
     const double total = block_pairwise_sum<kMmThreads>(s_tree, n, [&](int i) { return mm_clamped(s_x[i]); });
-    const double equal = 1.0 / (double)(n > 1 ? n : 1);
-    auto share = [&](int i) { return total > 0.0 ? mm_clamped(s_x[i]) / total : equal; };
+    const double equal = __ddiv_rn(1.0, (double)(n > 1 ? n : 1));
+    auto share = [&](int i) { return total > 0.0 ? __ddiv_rn(mm_clamped(s_x[i]), total) : equal; };
     // the pinned blocks in index order: block 0 and [ps, n) (every block when ps == 0)
     const int npin = ps >= 1 ? 1 + (n - ps) : n;
     const double base = block_pairwise_sum<kMmThreads>(
         s_tree, npin, [&](int j) { return share(ps >= 1 ? (j == 0 ? 0 : ps + j - 1) : j); });
-    // the unpinned blocks by decreasing share, equal shares by increasing block: ascending keys
-    // (~score key, block); the padding sorts last
+    // the unpinned blocks by decreasing share, equal shares by increasing block: ascending keys; the
+    // padding sorts last
     int P = 1;
     while (P < m) P <<= 1;
-    for (int j = tid; j < P; j += kMmThreads)
-      s_key[j] = j < m ? ((unsigned long long)(~mm_score_key(s_x[1 + j])) << 32) | (unsigned long long)(1 + j)
-                       : ~0ull;
+    if constexpr (kWide) {
+      for (int j = tid; j < P; j += kMmThreads) {
+        s_key[j] = j < m ? ~(unsigned long long)__double_as_longlong(share(1 + j)) : ~0ull;
+        s_blk[j] = j < m ? (uint32_t)(1 + j) : 0xffffffffu;
+      }
+    } else {
+      for (int j = tid; j < P; j += kMmThreads)
+        s_key[j] = j < m ? ((unsigned long long)(~mm_score_key(s_x[1 + j])) << 32) | (unsigned long long)(1 + j)
+                         : ~0ull;
+    }
     __syncthreads();
     for (int k = 2; k <= P; k <<= 1) {
       for (int j = k >> 1; j > 0; j >>= 1) {
@@ -125,13 +155,22 @@ __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
           if (partner > i) {
             const unsigned long long a = s_key[i], b = s_key[partner];
             const bool up = (i & k) == 0;
-            if ((a > b) == up) s_key[i] = b, s_key[partner] = a;
+            if constexpr (kWide) {
+              const uint32_t ai = s_blk[i], bi = s_blk[partner];
+              if ((a > b || (a == b && ai > bi)) == up) s_key[i] = b, s_key[partner] = a, s_blk[i] = bi, s_blk[partner] = ai;
+            } else {
+              if ((a > b) == up) s_key[i] = b, s_key[partner] = a;
+            }
           }
         }
         __syncthreads();
       }
     }
-    for (int j = tid; j < m; j += kMmThreads) p.sorted[(int64_t)j * p.rows + r] = share((int)(s_key[j] & 0xffffffffu));
+    if constexpr (kWide) {
+      for (int j = tid; j < m; j += kMmThreads) p.sorted[(int64_t)j * p.rows + r] = share((int)s_blk[j]);
+    } else {
+      for (int j = tid; j < m; j += kMmThreads) p.sorted[(int64_t)j * p.rows + r] = share((int)(s_key[j] & 0xffffffffu));
+    }
     if (tid == 0) {
       p.base[r] = base;
       atomicAdd((unsigned long long*)&p.state->must, (unsigned long long)pin_count(n, ps));
@@ -353,10 +392,11 @@ extern "C" size_t ekv_allocate_maxmin_workspace_bytes(int rows, int width) {
   return mm_layout(rows, width).bytes;
 }
 
-extern "C" int ekv_allocate_maxmin(const float* scores, int64_t score_stride, const int32_t* row_blocks,
-                                   const int32_t* measured_blocks, int recent_blocks, int cap_above_blocks,
-                                   double budget_fraction, int64_t budget, int rows, int width, int32_t* quota,
-                                   void* workspace, size_t workspace_bytes, void* stream) {
+template <typename S>
+static int allocate_maxmin(const S* scores, int64_t score_stride, const int32_t* score_rows,
+                           const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,
+                           int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
+                           int32_t* quota, void* workspace, size_t workspace_bytes, void* stream) {
   clear_error();
   if (!scores || !row_blocks || !quota) return fail(EKV_EINVAL, "a required pointer is NULL");
   if (rows <= 0 || width <= 0) return fail(EKV_EINVAL, "rows and width must be positive");
@@ -372,7 +412,8 @@ extern "C" int ekv_allocate_maxmin(const float* scores, int64_t score_stride, co
   if ((uintptr_t)workspace & 255) return fail(EKV_EINVAL, "the maxmin workspace must be 256-byte aligned");
   uint8_t* base = static_cast<uint8_t*>(workspace);
   MmParams p{};
-  p.scores = scores; p.score_s0 = score_stride; p.row_blocks = row_blocks; p.measured = measured_blocks;
+  p.scores = scores; p.score_s0 = score_stride; p.score_rows = score_rows; p.row_blocks = row_blocks;
+  p.measured = measured_blocks;
   p.recent = recent_blocks; p.cap = cap_above_blocks; p.fraction = budget_fraction; p.budget = (long long)budget;
   p.rows = rows; p.width = width; p.quota = quota;
   p.state = reinterpret_cast<MmState*>(base + l.state);
@@ -386,16 +427,14 @@ extern "C" int ekv_allocate_maxmin(const float* scores, int64_t score_stride, co
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(base + l.state, 0, sizeof(MmState), s) != cudaSuccess)
     return check_launch("cudaMemsetAsync(maxmin state)");
-  int sort_n = 1;
-  while (sort_n < width) sort_n <<= 1;
-  const size_t prep_smem = round_up((size_t)width * 4, 16) + (size_t)sort_n * 8;
+  const size_t prep_smem = mm_prep_smem<S>(width);
   const size_t level_smem = (size_t)rows * kMmLevelBytesPerRow;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
     return check_launch("cudaGetDevice");
   static size_t prep_set[kMaxDevices] = {}, level_set[kMaxDevices] = {};
   if (prep_set[device] < prep_smem) {
-    if (cudaFuncSetAttribute(mm_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(mm_prep_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(mm_prep_kernel)");
     prep_set[device] = prep_smem;
   }
@@ -405,11 +444,30 @@ extern "C" int ekv_allocate_maxmin(const float* scores, int64_t score_stride, co
       return check_launch("cudaFuncSetAttribute(mm_level_kernel)");
     level_set[device] = level_smem;
   }
-  mm_prep_kernel<<<rows, kMmThreads, prep_smem, s>>>(p);
+  mm_prep_kernel<S><<<rows, kMmThreads, prep_smem, s>>>(p);
   int rc = check_launch("mm_prep_kernel");
   if (rc != EKV_OK) return rc;
   mm_cumsum_kernel<<<(rows + 31) / 32, 32, 0, s>>>(p);
   if ((rc = check_launch("mm_cumsum_kernel")) != EKV_OK) return rc;
   mm_level_kernel<<<1, kMmThreads, level_smem, s>>>(p);
   return check_launch("mm_level_kernel");
+}
+
+extern "C" int ekv_allocate_maxmin(const float* scores, int64_t score_stride, const int32_t* row_blocks,
+                                   const int32_t* measured_blocks, int recent_blocks, int cap_above_blocks,
+                                   double budget_fraction, int64_t budget, int rows, int width, int32_t* quota,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  return allocate_maxmin<float>(scores, score_stride, nullptr, row_blocks, measured_blocks, recent_blocks,
+                                cap_above_blocks, budget_fraction, budget, rows, width, quota, workspace,
+                                workspace_bytes, stream);
+}
+
+extern "C" int ekv_allocate_maxmin_f64(const double* scores, int64_t score_stride, const int32_t* score_rows,
+                                       const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,
+                                       int cap_above_blocks, double budget_fraction, int64_t budget, int rows,
+                                       int width, int32_t* quota, void* workspace, size_t workspace_bytes,
+                                       void* stream) {
+  return allocate_maxmin<double>(scores, score_stride, score_rows, row_blocks, measured_blocks, recent_blocks,
+                                 cap_above_blocks, budget_fraction, budget, rows, width, quota, workspace,
+                                 workspace_bytes, stream);
 }

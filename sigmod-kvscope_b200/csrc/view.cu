@@ -11,6 +11,7 @@
 // them, both in their original order: the stable partition of compact_block_table
 // (runtime/block_view.py:52).
 #include "ekv_common.cuh"
+#include "pairwise.cuh"
 #include "pins.cuh"
 
 namespace ekv {
@@ -24,9 +25,12 @@ struct QuotaParams {
   double fraction;
   long long budget;  // >= 0: the shared budget as given; < 0: from `fraction`
   const double* row_fraction;
-  int rows;
+  int rows, width;  // width > 0: a request holds min(row_blocks, width) blocks
   int32_t* quota;
 };
+
+// The blocks of a request of row_blocks blocks: its length, at most the row width (controller.py:414).
+__device__ __forceinline__ int request_blocks(int n, int width) { return width > 0 && n > width ? width : n; }
 
 constexpr int kQuotaThreads = 1024;
 constexpr int kQuotaMaxRows = 8192;  // rows of one shared budget (shared-memory remainders)
@@ -49,11 +53,12 @@ __global__ void __launch_bounds__(kQuotaThreads) quota_kernel(const QuotaParams 
   if (p.row_fraction != nullptr) {
     // Every row is its own allocate() call (allocation.py:55-76) with its own budget.
     for (int r = threadIdx.x; r < R; r += kQuotaThreads) {
-      const int n = p.row_blocks[r];
+      int n = p.row_blocks[r];
       if (n <= p.cap || n <= 0) {
         p.quota[r] = -1;
         continue;
       }
+      n = request_blocks(n, p.width);
       const int ps = pin_start(n, p.recent, p.measured, r);
       const int pins = pin_count(n, ps);
       const int open = ps > 1 ? ps - 1 : 0;
@@ -66,8 +71,9 @@ __global__ void __launch_bounds__(kQuotaThreads) quota_kernel(const QuotaParams 
   // One budget for all measured rows (controller.py:398-451), split by _uniform (allocation.py:79-91).
   long long total = 0, floor_ = 0, total_open = 0;
   for (int r = threadIdx.x; r < R; r += kQuotaThreads) {
-    const int n = p.row_blocks[r];
+    int n = p.row_blocks[r];
     if (n <= p.cap || n <= 0) continue;
+    n = request_blocks(n, p.width);
     const int ps = pin_start(n, p.recent, p.measured, r);
     total += n;
     floor_ += pin_count(n, ps);
@@ -85,12 +91,13 @@ __global__ void __launch_bounds__(kQuotaThreads) quota_kernel(const QuotaParams 
   const long long free_ = budget - floor_;
   long long assigned = 0;
   for (int r = threadIdx.x; r < R; r += kQuotaThreads) {
-    const int n = p.row_blocks[r];
+    int n = p.row_blocks[r];
     s_rem[r] = -1.0;  // not a request
     if (n <= p.cap || n <= 0) {
       p.quota[r] = -1;
       continue;
     }
+    n = request_blocks(n, p.width);
     const int ps = pin_start(n, p.recent, p.measured, r);
     const int open = ps > 1 ? ps - 1 : 0;
     if (keep_all) {
@@ -181,8 +188,10 @@ struct ViewParams {
   const int32_t* quota;
   const int32_t* measured;
   int recent;
-  const float* scores;
+  const void* scores;          // float [rows][score_s0] (view_kernel<uint32_t>) or double (<unsigned long long>)
   int64_t score_s0;
+  const int32_t* score_rows;   // may be NULL: row r ranks scores row score_rows[r] instead of r
+  const double* weights;       // may be NULL (1.0): the request weights of the float64 gain keys
   int policy;
   const uint8_t* keep;
   int64_t keep_s0;
@@ -254,8 +263,8 @@ __device__ __forceinline__ uint32_t lanes_below() {
   return m;
 }
 
-// Exclusive scan of one count per warp (warp 0 scans); returns this warp's base and sets *total.
-__device__ __forceinline__ int warp_bases(int count, int* s_w, int* total) {
+// Exclusive scan of one count per warp (warp 0 scans): {this warp's base, the total}.
+__device__ __forceinline__ int2 warp_bases(int count, int* s_w) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __syncthreads();
   if (lane == 0) s_w[warp] = count;
@@ -271,51 +280,102 @@ __device__ __forceinline__ int warp_bases(int count, int* s_w, int* total) {
     if (lane == kViewWarps - 1) s_w[kViewWarps] = inc;
   }
   __syncthreads();
-  *total = s_w[kViewWarps];
-  return s_w[warp];
+  return make_int2(s_w[warp], s_w[kViewWarps]);
+}
+
+// The order keys of the ranking. Float32 scores: the bits of max(score, 0), three digits (bits 30-20,
+// 19-9, 8-0; bit 31 is always clear). Float64 scores: the bits of the non-negative float64
+// weight * share, share = max(score, 0) / total (total: NumPy's pairwise sum of the row's clamped
+// scores; 1 / n when it is not positive), the very value the reference ranks (allocation.py:46-52,
+// :89, :107), six digits (bits 62-52, 51-41, 40-30, 29-19, 18-8, 7-0).
+template <typename K>
+struct ViewKey;
+template <>
+struct ViewKey<uint32_t> {
+  static constexpr int kPasses = 3;
+  __device__ static void digit(int pass, int& shift, uint32_t& dmask) {
+    shift = pass == 0 ? 20 : (pass == 1 ? 9 : 0);
+    dmask = pass == 2 ? 511u : 2047u;
+  }
+  // keys 4g .. 4g + 3 (one 16-byte shared load)
+  __device__ static void load4(const uint32_t* keys, int g, uint32_t (&kv)[4]) {
+    const uint4 v = reinterpret_cast<const uint4*>(keys)[g];
+    kv[0] = v.x, kv[1] = v.y, kv[2] = v.z, kv[3] = v.w;
+  }
+};
+template <>
+struct ViewKey<unsigned long long> {
+  static constexpr int kPasses = 6;
+  __device__ static void digit(int pass, int& shift, unsigned long long& dmask) {
+    shift = pass < 5 ? 52 - 11 * pass : 0;
+    dmask = pass < 5 ? 2047ull : 255ull;
+  }
+  __device__ static void load4(const unsigned long long* keys, int g, unsigned long long (&kv)[4]) {
+    const ulonglong2 a = reinterpret_cast<const ulonglong2*>(keys)[2 * g];
+    const ulonglong2 b = reinterpret_cast<const ulonglong2*>(keys)[2 * g + 1];
+    kv[0] = a.x, kv[1] = a.y, kv[2] = b.x, kv[3] = b.y;
+  }
+};
+
+// The gain key of one block of a float64 row: bits of weight * (max(s, 0) / total) in float64, each
+// operation rounded on its own as NumPy rounds it (NaN counts as 0).
+__device__ __forceinline__ unsigned long long share_key64(double s, double total, double w, int n) {
+  const double c = s > 0.0 ? s : 0.0;
+  const double share = total > 0.0 ? __ddiv_rn(c, total) : __ddiv_rn(1.0, (double)(n > 1 ? n : 1));
+  const double g = __dmul_rn(w, share);
+  return g > 0.0 ? (unsigned long long)__double_as_longlong(g) : 0ull;
+}
+
+template <typename K>
+__host__ __device__ constexpr size_t view_smem_bytes(int width) {
+  // keys (the staged scores, then the keys, then the view row) + the table row (+ the pairwise-sum tree)
+  return (size_t)((width + kViewThreads - 1) / kViewThreads * kViewThreads) * (sizeof(K) + 4) +
+         (sizeof(K) == 8 ? sizeof(PairwiseTree) : 0);
 }
 
 // One CTA per row.
 //
-// The ranking: the q-th largest key among positions [1, ps) by a three-pass MSB radix select (digits
-// of bits 30-20, 19-9 and 8-0; bit 31 of a key is always clear). Thread t owns histogram bins
-// [4t, 4t + 4): it reads them for the scan and clears them for the next pass in the same step. If
-// the chosen bin holds exactly the keys still wanted, every key with that prefix is kept and the
-// select stops early. The equal-key count comes from the last histogram, so the scan that ranks
-// equal keys by position runs only when some of them must be dropped.
+// The ranking: the q-th largest key among positions [1, ps) by an MSB radix select over the digits
+// of ViewKey<K>. Thread t owns histogram bins [4t, 4t + 4): it reads them for the scan and clears them
+// for the next pass in the same step. If the chosen bin holds exactly the keys still wanted, every key
+// with that prefix is kept and the select stops early. The equal-key count comes from the last
+// histogram, so the scan that ranks equal keys by position runs only when some of them must be dropped.
 //
 // The layout: only positions [0, min(blocks, width)) can be kept, so those are laid out warp-striped
 // (warp w owns [w * 32 * iters, (w + 1) * 32 * iters), lane l of iteration i holds base + 32 * i + l,
 // so a ballot per iteration orders a warp's positions), and the rest of the row, never kept, keeps its
 // place: the view there is the table. With mask_out the layout covers the whole width, as every
-// position's committed flag is written.
+// position's committed flag is written; with no view (mask_out only) the kernel ends there.
+template <typename K>
 __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) {
-  extern __shared__ __align__(16) uint32_t smem_view[];
+  extern __shared__ __align__(16) unsigned char smem_view[];
   __shared__ __align__(16) int s_hist[kViewBins];
   __shared__ int s_w[kViewWarps + 1];
   __shared__ int s_pick[3];
   __shared__ uint32_t s_bits[kViewWarps][kViewMaxIters];  // each warp's keep ballots, per iteration
+  constexpr bool kWide = sizeof(K) == 8;
   const int r = blockIdx.x;
   const int W = p.width, BS = p.block_size;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int w_pad = (W + kViewThreads - 1) / kViewThreads * kViewThreads;
-  uint32_t* keys = smem_view;                                      // [w_pad]: shares -> keys -> view row
-  int32_t* trow_s = reinterpret_cast<int32_t*>(smem_view + w_pad);  // [w_pad]: the table row
+  K* keys = reinterpret_cast<K*>(smem_view);                                       // [w_pad]
+  int32_t* trow_s = reinterpret_cast<int32_t*>(smem_view + (size_t)w_pad * sizeof(K));  // [w_pad]: the table row
 
-  const int seq = p.seq_lens[r];
+  const bool has_view = p.view != nullptr;
+  const int seq = p.seq_lens != nullptr ? p.seq_lens[r] : 0;
   const int blocks = seq > 0 ? (seq + BS - 1) / BS : 0;
   uint8_t* mrow = p.mask_out ? p.mask_out + (int64_t)r * p.mask_s0 : nullptr;
   const int live = mrow != nullptr ? W : (blocks < W ? blocks : W);
   const int iters = (live + kViewThreads - 1) / kViewThreads;
   const int wbase = warp * 32 * iters;
-  const int laid = iters * kViewThreads < W ? iters * kViewThreads : W;  // positions [0, laid) laid out
+  const int laid = !has_view ? 0 : (iters * kViewThreads < W ? iters * kViewThreads : W);  // positions laid out
 
   // ---- the row's committed mask: pins + selection (ranking mode) or the given mask ---------------
   const bool rank_mode = p.keep == nullptr;
-  int ps = 0, q = 0, open_hi = 1;  // the selection applies to positions [1, open_hi)
+  int ps = 0, q = 0, open_hi = 1, n_a = 0;  // the selection applies to positions [1, open_hi)
   bool by_threshold = false, newest = false;
   if (rank_mode) {
-    int n_a = p.row_blocks[r];
+    n_a = p.row_blocks[r];
     n_a = n_a < 0 ? 0 : (n_a > W ? W : n_a);
     q = p.quota[r];
     if (q >= 0 && n_a > 0) {
@@ -331,43 +391,64 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
     }
   }
   if (by_threshold) {
-    stage_words(keys, reinterpret_cast<const uint32_t*>(p.scores + (int64_t)r * p.score_s0), ps);
+    const int64_t srow = p.score_rows != nullptr ? (int64_t)p.score_rows[r] : (int64_t)r;
+    if (kWide) {  // every score of the request: the total needs them all
+      stage_words(reinterpret_cast<uint32_t*>(keys),
+                  reinterpret_cast<const uint32_t*>(static_cast<const double*>(p.scores) + srow * p.score_s0), 2 * n_a);
+    } else {
+      stage_words(reinterpret_cast<uint32_t*>(keys),
+                  reinterpret_cast<const uint32_t*>(static_cast<const float*>(p.scores) + srow * p.score_s0), ps);
+    }
     cp_async_commit();
   }
-  const int32_t* trow = p.table + (int64_t)r * p.table_s0;
+  // (address arithmetic only: without a view, laid is 0 and the table is never read)
+  const int32_t* trow = reinterpret_cast<const int32_t*>(reinterpret_cast<uintptr_t>(p.table) +
+                                                         (uintptr_t)((int64_t)r * p.table_s0 * 4));
   stage_words(reinterpret_cast<uint32_t*>(trow_s), reinterpret_cast<const uint32_t*>(trow), laid);
   cp_async_commit();
 
-  uint32_t prefix = 0, pmask = 0;
+  K prefix = 0, pmask = 0;
   int k_eq = 0, eq_total = 0;
   if (by_threshold) {
-    cp_async_wait<1>();  // the shares have landed (the table may still be in flight)
+    cp_async_wait<1>();  // the scores have landed (the table may still be in flight)
     __syncthreads();
-    // keys are handled four at a time (16-byte shared loads); position 0 and positions from ps on are
-    // not keys
+    // keys are handled four at a time; position 0 and positions from ps on are not keys
     const int groups = (ps + 3) >> 2;
-    uint4* keys4 = reinterpret_cast<uint4*>(keys);
-    for (int g = threadIdx.x; g < groups; g += kViewThreads) {
-      uint4 v = keys4[g];
-      v.x = share_key(__uint_as_float(v.x)), v.y = share_key(__uint_as_float(v.y));
-      v.z = share_key(__uint_as_float(v.z)), v.w = share_key(__uint_as_float(v.w));
-      keys4[g] = v;
+    if constexpr (kWide) {
+      const double* s_x = reinterpret_cast<const double*>(keys);
+      PairwiseTree& tree = *reinterpret_cast<PairwiseTree*>(smem_view + (size_t)w_pad * (sizeof(K) + 4));
+      const double total = block_pairwise_sum<kViewThreads>(tree, n_a, [&](int i) {
+        const double s = s_x[i];
+        return s > 0.0 ? s : 0.0;
+      });
+      const double w = p.weights != nullptr ? p.weights[r] : 1.0;
+      for (int b = threadIdx.x; b < 4 * groups; b += kViewThreads)  // in place: each thread its own positions
+        keys[b] = b < ps ? share_key64(s_x[b], total, w, n_a) : 0ull;
+    } else {
+      uint4* keys4 = reinterpret_cast<uint4*>(keys);
+      for (int g = threadIdx.x; g < groups; g += kViewThreads) {
+        uint4 v = keys4[g];
+        v.x = share_key(__uint_as_float(v.x)), v.y = share_key(__uint_as_float(v.y));
+        v.z = share_key(__uint_as_float(v.z)), v.w = share_key(__uint_as_float(v.w));
+        keys4[g] = v;
+      }
     }
     reinterpret_cast<int4*>(s_hist)[threadIdx.x] = make_int4(0, 0, 0, 0);
     __syncthreads();
     int k = q;
 #pragma unroll 1
-    for (int pass = 0; pass < 3; ++pass) {
-      const int shift = pass == 0 ? 20 : (pass == 1 ? 9 : 0);
-      const uint32_t dmask = pass == 2 ? 511u : 2047u;
+    for (int pass = 0; pass < ViewKey<K>::kPasses; ++pass) {
+      int shift;
+      K dmask;
+      ViewKey<K>::digit(pass, shift, dmask);
       for (int g = threadIdx.x; g < groups; g += kViewThreads) {
-        const uint4 v = keys4[g];
-        const uint32_t kv[4] = {v.x, v.y, v.z, v.w};
+        K kv[4];
+        ViewKey<K>::load4(keys, g, kv);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int b = 4 * g + j;
           const bool in = b >= 1 && b < ps && (kv[j] & pmask) == prefix;
-          if (in) atomicAdd(&s_hist[(kv[j] >> shift) & dmask], 1);
+          if (in) atomicAdd(&s_hist[(int)((kv[j] >> shift) & dmask)], 1);
         }
       }
       __syncthreads();
@@ -393,7 +474,7 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
       if (gt < k && gt + h.x >= k) s_pick[0] = bin, s_pick[1] = gt, s_pick[2] = h.x;
       __syncthreads();
       k -= s_pick[1];
-      prefix |= (uint32_t)s_pick[0] << shift;
+      prefix |= (K)s_pick[0] << shift;
       pmask |= dmask << shift;
       eq_total = s_pick[2];  // the keys with the chosen prefix
       if (eq_total == k) break;  // all of them are kept: the prefix is the threshold
@@ -412,8 +493,7 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
       const bool eq = b >= 1 && b < ps && (keys[b] & pmask) == prefix;
       cnt += __popc(__ballot_sync(kFullMask, eq));
     }
-    int unused = 0;
-    eq_base = warp_bases(cnt, s_w, &unused);
+    eq_base = warp_bases(cnt, s_w).x;
   }
 
   const uint8_t flags = p.full_rows != nullptr ? p.full_rows[r] : 0;
@@ -427,7 +507,7 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
     // the common case: a key at or above the threshold is kept; outside [1, open_hi) every block is
     for (int i = 0; i < iters; ++i) {
       const int b = wbase + 32 * i + lane;
-      const uint32_t key = (b >= 1 && b < open_hi) ? keys[b] & pmask : 0xffffffffu;
+      const K key = (b >= 1 && b < open_hi) ? keys[b] & pmask : ~(K)0;
       const bool keep = (key >= prefix || b == 0 || b == blocks - 1) && b < blocks && b < W;
       const uint32_t bits = __ballot_sync(kFullMask, keep);
       if (lane == 0) s_bits[warp][i] = bits;
@@ -444,7 +524,7 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
       if (newest) {
         c = b >= ps - q;
       } else if (by_threshold) {
-        const uint32_t key = keys[b] & pmask;
+        const K key = keys[b] & pmask;
         c = key > prefix || (key == prefix && !ties);  // every equal key is kept unless too many
       } else {
         c = false;  // nothing selected
@@ -467,13 +547,13 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
     if (lane == 0) s_bits[warp][i] = bits;
     kept_count += __popc(bits);
   }
-  int kept_total = 0;
-  const int kept_base = warp_bases(kept_count, s_w, &kept_total);  // (its barrier also ends every key read)
+  const int2 kb = warp_bases(kept_count, s_w);  // (its barrier also ends every key read)
+  const int kept_base = kb.x, kept_total = kb.y;
 
   // ---- pass 2: kept ids first, then the others, both in position order, into shared memory -------
   cp_async_wait<0>();
   __syncthreads();  // the table row has landed
-  uint32_t* out = keys;
+  uint32_t* out = reinterpret_cast<uint32_t*>(keys);
   int kept = kept_base;
   for (int i = 0; i < iters; ++i) {
     const int b = wbase + 32 * i + lane;
@@ -488,8 +568,8 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
   __syncthreads();
   int32_t* vrow = p.view + (int64_t)r * p.view_s0;
   copy_words(vrow, reinterpret_cast<const int32_t*>(out), 0, laid);
-  copy_words(vrow, trow, laid, W);  // past the laid-out positions nothing is kept: the view is the table
-  if (threadIdx.x == 0) {
+  if (has_view) copy_words(vrow, trow, laid, W);  // past the laid-out positions nothing is kept: the view is the table
+  if (threadIdx.x == 0 && has_view) {
     const int last = seq - (blocks - 1) * BS;
     const int view_len = blocks > 0 ? (kept_total - 1) * BS + last : 0;
     p.view_lens[r] = view_len;
@@ -508,19 +588,19 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
   }
 }
 
+template <typename K>
 int launch_view(const ViewParams& p, cudaStream_t stream) {
-  const size_t w_pad = (size_t)(p.width + kViewThreads - 1) / kViewThreads * kViewThreads;
-  const size_t smem = 2 * w_pad * sizeof(uint32_t);
+  const size_t smem = view_smem_bytes<K>(p.width);
   static size_t configured[kMaxDevices] = {};
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
     return check_launch("cudaGetDevice");
   if (configured[device] < smem) {
-    if (cudaFuncSetAttribute(view_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(view_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(view_kernel)");
     configured[device] = smem;
   }
-  view_kernel<<<p.rows, kViewThreads, smem, stream>>>(p);
+  view_kernel<K><<<p.rows, kViewThreads, smem, stream>>>(p);
   return check_launch("view_kernel");
 }
 
@@ -531,10 +611,10 @@ using namespace ekv;
 extern "C" int ekv_allocate_quotas(const int32_t* row_blocks, const int32_t* measured_blocks,
                                    int recent_blocks, int cap_above_blocks, double budget_fraction,
                                    int64_t budget, const double* row_fraction, int objective,
-                                   int rows, int32_t* quota, void* stream) {
+                                   int rows, int width, int32_t* quota, void* stream) {
   clear_error();
   if (!row_blocks || !quota) return fail(EKV_EINVAL, "a required pointer is NULL");
-  if (rows <= 0) return fail(EKV_EINVAL, "rows must be positive");
+  if (rows <= 0 || width < 0) return fail(EKV_EINVAL, "rows must be positive and width not negative");
   if (recent_blocks < -1 || cap_above_blocks < -1) return fail(EKV_EINVAL, "invalid controller settings");
   if (objective != EKV_POLICY_SUM && objective != EKV_POLICY_UNIFORM && objective != EKV_POLICY_NEWEST)
     return fail(EKV_EINVAL, "unknown objective %d", objective);
@@ -560,7 +640,7 @@ extern "C" int ekv_allocate_quotas(const int32_t* row_blocks, const int32_t* mea
     configured[device] = true;
   }
   QuotaParams p{row_blocks, measured_blocks, recent_blocks, cap_above_blocks, budget_fraction,
-                (long long)budget, row_fraction, rows, quota};
+                (long long)budget, row_fraction, rows, width, quota};
   quota_kernel<<<1, kQuotaThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("quota_kernel");
 }
@@ -593,10 +673,10 @@ extern "C" int ekv_view_build(const int32_t* table, int64_t table_stride, const 
   if (released && released_stride < width) return fail(EKV_EINVAL, "released_stride < width");
   if (mask_out && mask_stride < width) return fail(EKV_EINVAL, "mask_stride < width");
   ViewParams p{table,   table_stride, seq_lens, row_blocks, quota,      measured_blocks,
-               recent_blocks, scores, score_stride, policy, keep,      keep_stride,
+               recent_blocks, scores, score_stride, nullptr, nullptr, policy, keep,      keep_stride,
                full_rows, released, released_stride, rows, width,     block_size,
                view,    view_stride,  view_lens, mask_out,  mask_stride, nullptr, 0};
-  return launch_view(p, static_cast<cudaStream_t>(stream));
+  return launch_view<uint32_t>(p, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ekv_compact_block_table(const int32_t* table, int64_t table_stride,
@@ -627,8 +707,37 @@ extern "C" int ekv_decode_view(const int32_t* table, int64_t table_stride, const
   if (table_stride < width || view_stride < width || keep_stride < width)
     return fail(EKV_EINVAL, "a row stride is below the width");
   if (released && released_stride < width) return fail(EKV_EINVAL, "released_stride < width");
-  ViewParams p{table, table_stride, seq_lens, nullptr, nullptr, nullptr, 0, nullptr, 0, EKV_POLICY_UNIFORM,
+  ViewParams p{table, table_stride, seq_lens, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, nullptr, EKV_POLICY_UNIFORM,
                keep,  keep_stride,  row_flags, released, released_stride, rows, width, block_size,
                view,  view_stride,  view_lens, nullptr, 0, reinterpret_cast<long long*>(counts), expired != 0};
-  return launch_view(p, static_cast<cudaStream_t>(stream));
+  return launch_view<uint32_t>(p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ekv_view_build_f64(const int32_t* table, int64_t table_stride, const int32_t* seq_lens,
+                                  const int32_t* row_blocks, const int32_t* quota, const int32_t* measured_blocks,
+                                  int recent_blocks, const double* scores, int64_t score_stride,
+                                  const int32_t* score_rows, const double* weights, int policy,
+                                  const uint8_t* full_rows, const uint8_t* released, int64_t released_stride,
+                                  int rows, int width, int block_size, int32_t* view, int64_t view_stride,
+                                  int32_t* view_lens, uint8_t* mask_out, int64_t mask_stride, void* stream) {
+  clear_error();
+  if (!row_blocks || !quota) return fail(EKV_EINVAL, "a required pointer is NULL");
+  if (view == nullptr ? mask_out == nullptr : (!table || !seq_lens || !view_lens))
+    return fail(EKV_EINVAL, "a view needs table, seq_lens, view and view_lens; without one, mask_out is required");
+  if (rows <= 0 || width <= 0 || block_size <= 0)
+    return fail(EKV_EINVAL, "rows, width and block_size must be positive");
+  if (width > kViewMaxWidth) return fail(EKV_ENOTSUP, "width %d > %d (a view row is staged in shared memory)", width, kViewMaxWidth);
+  if (view != nullptr && (table_stride < width || view_stride < width)) return fail(EKV_EINVAL, "a row stride is below the width");
+  if (policy != EKV_POLICY_SUM && policy != EKV_POLICY_UNIFORM && policy != EKV_POLICY_NEWEST)
+    return fail(EKV_EINVAL, "unknown policy %d", policy);
+  if (policy != EKV_POLICY_NEWEST && (!scores || score_stride < width))
+    return fail(EKV_EINVAL, "ranking by shares needs scores with a row stride >= width");
+  if (recent_blocks < -1) return fail(EKV_EINVAL, "recent_blocks must be >= -1");
+  if (released && released_stride < width) return fail(EKV_EINVAL, "released_stride < width");
+  if (mask_out && mask_stride < width) return fail(EKV_EINVAL, "mask_stride < width");
+  ViewParams p{table,   table_stride, seq_lens, row_blocks, quota,      measured_blocks,
+               recent_blocks, scores, score_stride, score_rows, weights, policy, nullptr, 0,
+               full_rows, released, released_stride, rows, width,     block_size,
+               view,    view_stride,  view_lens, mask_out,  mask_stride, nullptr, 0};
+  return launch_view<unsigned long long>(p, static_cast<cudaStream_t>(stream));
 }

@@ -74,7 +74,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i32, [_p, _i32, _i32, _i32, _i32, _p, _i32, _i32, _p, _p, _p]
     ),
     "ekv_share_finalize": (_i32, [_p, _p, _p, _i32, _i32, _i32, _p, _p]),
-    "ekv_allocate_quotas": (_i32, [_p, _p, _i32, _i32, _f64, _i64, _p, _i32, _i32, _p, _p]),
+    "ekv_allocate_quotas": (_i32, [_p, _p, _i32, _i32, _f64, _i64, _p, _i32, _i32, _i32, _p, _p]),
     "ekv_allocate_sum_workspace_bytes": (ctypes.c_size_t, [_i32, _i32]),
     "ekv_allocate_maxmin_workspace_bytes": (ctypes.c_size_t, [_i32, _i32]),
     "ekv_allocate_maxmin": (_i32, [_p, _i64, _p, _p, _i32, _i32, _f64, _i64, _i32, _i32, _p, _p, ctypes.c_size_t, _p]),
@@ -82,6 +82,18 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ekv_slot_compact": (_i32, [_p, _p, _i32, _p, _i64, _p, _i32, _i32, _i32, _i64, _i32, _i32, _p, _p, _p, _i64,
                                 _p, _p, _p]),
     "ekv_allocate_sum": (_i32, [_p, _i64, _p, _p, _p, _i32, _i32, _f64, _i64, _i32, _i32, _p, _p, ctypes.c_size_t, _p]),
+    "ekv_allocate_sum_f64": (
+        _i32, [_p, _i64, _p, _p, _p, _p, _i32, _i32, _f64, _i64, _i32, _i32, _p, _p, ctypes.c_size_t, _p],
+    ),
+    "ekv_allocate_maxmin_f64": (
+        _i32, [_p, _i64, _p, _p, _p, _i32, _i32, _f64, _i64, _i32, _i32, _p, _p, ctypes.c_size_t, _p],
+    ),
+    "ekv_view_build_f64": (
+        _i32,
+        [_p, _i64, _p, _p, _p, _p, _i32, _p, _i64, _p, _p, _i32, _p, _p, _i64,
+         _i32, _i32, _i32, _p, _i64, _p, _p, _i64, _p],
+    ),
+    "ekv_ledger_absorb": (_i32, [_p, _i32, _i64, _p, _p, _f64, _i32, _i32, _p, _i64, _i32, _p, _p]),
     "ekv_view_build": (
         _i32,
         [_p, _i64, _p, _p, _p, _p, _i32, _p, _i64, _i32, _p, _i64, _p, _p, _i64,

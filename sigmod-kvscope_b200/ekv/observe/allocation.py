@@ -5,16 +5,19 @@ keep their names, signature, pins, validation and tie rules. ``uniform`` gives e
 same fraction of its unpinned blocks by largest remainder (equal remainders to the earlier request)
 and keeps each request's best blocks by its own shares, equal shares to the older block
 (allocation.py:79-91). ``sum`` keeps the unpinned blocks with the largest weighted share over all
-requests, equal gains to the newer block, then to the earlier request (:94-118). The quotas run in
-the sm_100a kernels ``ekv_allocate_quotas`` (uniform) and ``ekv_allocate_sum`` (sum: a global
-radix select over the float64 gains, with each request's total summed as NumPy sums it), the
-per-request top-k selection in ``ekv_view_build``.
+requests, equal gains to the newer block, then to the earlier request (:94-118). ``maxmin`` raises
+the smallest retained share as far as the budget allows (:121-166). The quotas run in the sm_100a
+kernels ``ekv_allocate_quotas`` (uniform), ``ekv_allocate_sum`` (sum: a global radix select over the
+float64 gains, with each request's total summed as NumPy sums it) and ``ekv_allocate_maxmin`` (the
+water level), the per-request top-k selection in ``ekv_view_build``.
 
-Device ranking compares max(score, 0) as float32 within a request. For float32-exact scores that is
-the reference's ranking by float64 shares exactly: dividing distinct float32 values by the same total
-(and multiplying by one weight) keeps them distinct and ordered, and equal values stay equal. Scores
-that float32 cannot hold exactly, negative weights and ``maxmin`` are not implemented on the device
-and raise ``RuntimeError``; NaN scores count as 0, as the controller passes them (controller.py:337).
+``allocate`` ranks the float64 values the reference ranks: the share max(score, 0) / total, or the
+gain weight * share for ``sum``, each rounded as NumPy rounds it, with the total summed as NumPy's
+pairwise sum (``ekv_allocate_sum_f64``, ``ekv_allocate_maxmin_f64``, ``ekv_view_build_f64``); distinct
+scores whose shares round to one value tie, as they do in the reference. ``sum_quotas``,
+``maxmin_quotas`` and the view also run on float32 scores, whose order is then the order of the shares.
+Negative request weights raise ``RuntimeError``; NaN scores count as 0, as the controller passes them
+(controller.py:337).
 """
 
 from __future__ import annotations
@@ -74,6 +77,16 @@ def _pin_start(pinned: np.ndarray) -> int:
     return tail
 
 
+def _score_layout(scores: torch.Tensor, row_blocks: torch.Tensor, score_rows: torch.Tensor | None) -> tuple[int, int]:
+    """(rows, width) of a quota call: one row per ``row_blocks`` entry; ``score_rows`` maps them to score rows."""
+    if scores.dtype not in (torch.float32, torch.float64) or scores.ndim != 2 or scores.stride(1) != 1:
+        raise ValueError("scores must be float32 or float64 [rows, width] with contiguous rows")
+    if score_rows is not None and scores.dtype != torch.float64:
+        raise ValueError("score_rows needs float64 scores")
+    rows = int(row_blocks.shape[0]) if score_rows is not None else int(scores.shape[0])
+    return rows, int(scores.shape[1])
+
+
 def sum_quotas(
     scores: torch.Tensor,
     row_blocks: torch.Tensor,
@@ -85,24 +98,32 @@ def sum_quotas(
     budget: int = -1,
     budget_fraction: float = 0.0,
     weights: torch.Tensor | None = None,
+    score_rows: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """The per-row quotas of the ``sum`` objective with one shared budget (``ekv_allocate_sum``).
 
-    ``scores`` float32 [rows, width] on the device, ``row_blocks`` int32 [rows], ``quota`` int32 [rows]
-    (out), ``weights`` float64 [rows] or None; ``budget`` >= 0 as given, else from
+    ``scores`` float32 or float64 [., width] on the device, ``row_blocks`` int32 [rows], ``quota`` int32
+    [rows] (out), ``weights`` float64 [rows] or None; ``score_rows`` (int32 [rows], float64 scores only)
+    reads row r's scores from row ``score_rows[r]``. ``budget`` >= 0 as given, else from
     ``budget_fraction`` as the controller computes it. No host synchronisation.
     """
-    rows, width = int(scores.shape[0]), int(scores.shape[1])
+    rows, width = _score_layout(scores, row_blocks, score_rows)
     lib = _lib.load()
     size = int(lib.ekv_allocate_sum_workspace_bytes(rows, width))
     workspace = torch.empty(size + 256, dtype=torch.uint8, device=scores.device)
     base = (workspace.data_ptr() + 255) // 256 * 256
-    rc = lib.ekv_allocate_sum(
-        scores.data_ptr(), scores.stride(0), None if weights is None else weights.data_ptr(), row_blocks.data_ptr(),
+    common = (
+        None if weights is None else weights.data_ptr(), row_blocks.data_ptr(),
         None if measured is None else measured.data_ptr(), int(recent_blocks), int(cap_above_blocks),
         float(budget_fraction), int(budget), rows, width, quota.data_ptr(), base, size, _lib.current_stream(),
     )
-    _lib.check(rc, "ekv_allocate_sum")
+    if scores.dtype == torch.float64:
+        rows_ptr = None if score_rows is None else score_rows.data_ptr()
+        rc = lib.ekv_allocate_sum_f64(scores.data_ptr(), scores.stride(0), rows_ptr, *common)
+        _lib.check(rc, "ekv_allocate_sum_f64")
+    else:
+        rc = lib.ekv_allocate_sum(scores.data_ptr(), scores.stride(0), *common)
+        _lib.check(rc, "ekv_allocate_sum")
     return quota
 
 
@@ -116,20 +137,27 @@ def maxmin_quotas(
     cap_above_blocks: int,
     budget: int = -1,
     budget_fraction: float = 0.0,
+    score_rows: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """The per-row quotas of the ``maxmin`` objective with one shared budget (``ekv_allocate_maxmin``), for a
     view built with the ``uniform`` ranking. Arguments as ``sum_quotas``; no weights."""
-    rows, width = int(scores.shape[0]), int(scores.shape[1])
+    rows, width = _score_layout(scores, row_blocks, score_rows)
     lib = _lib.load()
     size = int(lib.ekv_allocate_maxmin_workspace_bytes(rows, width))
     workspace = torch.empty(size + 256, dtype=torch.uint8, device=scores.device)
     base = (workspace.data_ptr() + 255) // 256 * 256
-    rc = lib.ekv_allocate_maxmin(
-        scores.data_ptr(), scores.stride(0), row_blocks.data_ptr(), None if measured is None else measured.data_ptr(),
-        int(recent_blocks), int(cap_above_blocks), float(budget_fraction), int(budget), rows, width,
-        quota.data_ptr(), base, size, _lib.current_stream(),
+    common = (
+        row_blocks.data_ptr(), None if measured is None else measured.data_ptr(), int(recent_blocks),
+        int(cap_above_blocks), float(budget_fraction), int(budget), rows, width, quota.data_ptr(), base, size,
+        _lib.current_stream(),
     )
-    _lib.check(rc, "ekv_allocate_maxmin")
+    if scores.dtype == torch.float64:
+        rows_ptr = None if score_rows is None else score_rows.data_ptr()
+        rc = lib.ekv_allocate_maxmin_f64(scores.data_ptr(), scores.stride(0), rows_ptr, *common)
+        _lib.check(rc, "ekv_allocate_maxmin_f64")
+    else:
+        rc = lib.ekv_allocate_maxmin(scores.data_ptr(), scores.stride(0), *common)
+        _lib.check(rc, "ekv_allocate_maxmin")
     return quota
 
 
@@ -154,18 +182,12 @@ def allocate(requests: Sequence[Request], budget: int, objective: Objective = "s
     rows = len(requests)
     if rows == 0 or width == 0:
         return [p.copy() for p in pinned]
-    scores = np.zeros((rows, width), dtype=np.float32)
+    if objective == "sum" and any(not r.weight >= 0.0 or not np.isfinite(r.weight) for r in requests):
+        raise RuntimeError("negative or non-finite request weights are not supported on the device")
+    scores = np.zeros((rows, width), dtype=np.float64)
     for r, req in enumerate(requests):
         s = np.asarray(req.scores, dtype=np.float64)
-        finite = ~np.isnan(s)
-        s32 = np.where(finite, s, 0.0).astype(np.float32)
-        if not np.array_equal(s32.astype(np.float64)[finite], s[finite]):
-            raise RuntimeError("the device ranking needs scores that float32 holds exactly")
-        if objective == "sum" and req.weight < 0.0:
-            raise RuntimeError("negative request weights are not supported on the device")
-        if objective == "sum" and req.weight == 0.0:
-            s32[:] = 0.0  # every gain is 0: all tie
-        scores[r, : sizes[r]] = s32
+        scores[r, : sizes[r]] = np.where(np.isnan(s), 0.0, s)
     # pins {0} | [pin_start, n): passed as the "measured" start, with no recent pins of their own
     pin_starts = torch.tensor([_pin_start(p) for p in pinned], dtype=torch.int32)
     device = torch.device("cuda", torch.cuda.current_device())
@@ -175,9 +197,10 @@ def allocate(requests: Sequence[Request], budget: int, objective: Objective = "s
     measured = pin_starts.to(device)
     quota = torch.empty(rows, dtype=torch.int32, device=device)
     scores_t = torch.from_numpy(scores).to(device)
+    weights = None
     if objective == "uniform":
         rc = lib.ekv_allocate_quotas(row_blocks.data_ptr(), measured.data_ptr(), -1, -1, 0.0, int(budget), None,
-                                     _lib.POLICY_UNIFORM, rows, quota.data_ptr(), stream)
+                                     _lib.POLICY_UNIFORM, rows, width, quota.data_ptr(), stream)
         _lib.check(rc, "ekv_allocate_quotas")
     elif objective == "maxmin":
         maxmin_quotas(scores_t, row_blocks, quota, measured=measured, recent_blocks=-1, cap_above_blocks=-1,
@@ -186,16 +209,12 @@ def allocate(requests: Sequence[Request], budget: int, objective: Objective = "s
         weights = torch.tensor([float(r.weight) for r in requests], dtype=torch.float64).to(device)
         sum_quotas(scores_t, row_blocks, quota, measured=measured, recent_blocks=-1, cap_above_blocks=-1,
                    budget=int(budget), weights=weights)
-    table = torch.zeros(rows, width, dtype=torch.int32, device=device)
-    lens = torch.zeros(rows, dtype=torch.int32, device=device)
-    view = torch.empty(rows, width, dtype=torch.int32, device=device)
-    view_lens = torch.empty(rows, dtype=torch.int32, device=device)
     mask = torch.empty(rows, width, dtype=torch.uint8, device=device)
-    rc = lib.ekv_view_build(
-        table.data_ptr(), width, lens.data_ptr(), row_blocks.data_ptr(), quota.data_ptr(), measured.data_ptr(),
-        -1, scores_t.data_ptr(), width, _POLICIES[objective], None, 0, None, None, 0, rows, width, 16,
-        view.data_ptr(), width, view_lens.data_ptr(), mask.data_ptr(), width, stream,
+    rc = lib.ekv_view_build_f64(
+        None, 0, None, row_blocks.data_ptr(), quota.data_ptr(), measured.data_ptr(), -1, scores_t.data_ptr(),
+        width, None, None if weights is None else weights.data_ptr(), _POLICIES[objective], None, None, 0, rows,
+        width, 16, None, 0, None, mask.data_ptr(), width, stream,
     )
-    _lib.check(rc, "ekv_view_build")
+    _lib.check(rc, "ekv_view_build_f64")
     out = mask.cpu().numpy().astype(bool)
     return [out[r, : sizes[r]].copy() for r in range(rows)]

@@ -1,0 +1,316 @@
+"""The controller's decide stage on the device: ingest of the statistic, smoothing, and the keep mask.
+
+The reference controller (observe/controller.py) copies the statistic of the audited rows out of the
+serving process over IPC, one cudaMemcpy per (plane, layer, run of rows) (TileShareSource.read,
+:111-136, with read_tile_rows, observe/tile_shares.py:129-173), normalises it with NumPy, folds it
+into a float64 share vector per request key (Controller._absorb_audit, :332-345) and builds the keep
+mask of every row with ``allocate`` (Controller._allocate, :398-451). Here the data stay on the GPU:
+
+* ``DeviceShareSource`` opens the serving process's statistic table through the IPC handle its
+  descriptor line publishes (the format RecordingPlane writes, runtime/audit_kernel.py:162-180) and
+  returns the shares [live_rows, width] (float32, on the device) in one kernel (ekv_normalize_tile_lse).
+* ``ShareLedger`` holds one float64 row per request (the reference's ``shares`` dict) and folds a new
+  audit into it with ``ekv_ledger_absorb``: same evidence rule, same NaN handling, same rounding.
+* ``ShareLedger.keep_mask`` computes the mask Controller._allocate commits, from the ledger in place
+  (``ekv_allocate_sum_f64`` / ``ekv_allocate_quotas`` / ``ekv_allocate_maxmin_f64`` and
+  ``ekv_view_build_f64``), bit-exact with the reference for the same shares.
+
+Only the request-key bookkeeping (which ledger row holds which request, which blocks the last audit
+measured) stays on the host, as small dicts; the one host synchronisation per absorbed audit reads one
+evidence byte per row. The mailbox, leases, audit requests, step-time target and block release are
+the controller's control plane and are not rebuilt: ``keep_mask`` covers a controller with
+``release_after`` = 0 and measured shares (no fixed scoring rule).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from collections.abc import Callable, Sequence
+
+import numpy as np
+import torch
+
+from .. import _lib
+from ..runtime.audit import _cudart
+from .allocation import Objective, maxmin_quotas, sum_quotas
+from .tile_shares import _AGGREGATES, Aggregate, _check_aggregate
+
+_CUDA_IPC_LAZY_ENABLE_PEER_ACCESS = 1
+_CUDA_MEMCPY_DEVICE_TO_HOST = 2
+
+
+class _IpcMemHandle(ctypes.Structure):
+    """cudaIpcMemHandle_t: 64 opaque bytes, passed by value to cudaIpcOpenMemHandle."""
+
+    _fields_ = [("reserved", ctypes.c_ubyte * 64)]
+
+
+def audit_row_blocks(audit_keys: np.ndarray, keys: np.ndarray, lengths: np.ndarray,
+                     cap_above_blocks: int) -> tuple[int, np.ndarray]:
+    """(live, row_blocks) of a completed audit (observe/controller.py:319-323): the rows up to the last
+    audited one, each with its request's current length in blocks looked up by key (the batch may have
+    been reordered since the audit), 0 for a request that has finished or is at or below the cap."""
+    audit_keys = np.asarray(audit_keys, dtype=np.uint64)
+    audited = np.flatnonzero(audit_keys)
+    live = int(audited[-1]) + 1 if audited.size else 0
+    current = {int(k): int(n) for k, n in zip(np.asarray(keys, dtype=np.uint64).tolist(), lengths) if int(k)}
+    row_blocks = np.array([current.get(int(audit_keys[row]), 0) for row in range(live)], dtype=np.int64)
+    row_blocks[row_blocks <= cap_above_blocks] = 0
+    return live, row_blocks
+
+
+class DeviceShareSource:
+    """The attention share of the live rows, read on the device from a serving process's table.
+
+    The device counterpart of TileShareSource (observe/controller.py:92-136): the same descriptor entry
+    (``share_descriptor(pid)``) and the same ``read(live_rows, row_blocks)``, but the result is a float32
+    tensor [live_rows, width] on this process's current device, NaN for rows without evidence (rows of 0
+    blocks are not read). For the serving process itself the device addresses are used directly; another
+    process opens the IPC handles once."""
+
+    def __init__(self, entry: dict[str, int | str], pid: int, aggregate: Aggregate = "mean") -> None:
+        _check_aggregate(aggregate)
+        self.aggregate = aggregate
+        self.rows = int(entry["max_rows"])
+        self.width = int(entry["ncap"])
+        self.group_rows = int(entry["tile_lse_group_rows"])
+        self.max_layers = int(entry["tile_lse_layers"])
+        self.tile_blocks = int(entry["attn_share_tile_blocks"])
+        self._cuda = _cudart()
+        self._opened: list[int] = []
+        if pid == os.getpid():
+            self.base = int(entry["tile_lse_dev"])
+            self.table = int(entry["layer_table_dev"])
+        else:
+            self.base = self._open(str(entry["tile_lse_ipc"]))
+            self.table = self._open(str(entry["layer_table_ipc"]))
+        self.device = torch.device("cuda", torch.cuda.current_device())
+
+    def _open(self, handle_hex: str) -> int:
+        handle = _IpcMemHandle.from_buffer_copy(bytes.fromhex(handle_hex))
+        pointer = ctypes.c_void_p()
+        rc = self._cuda.cudaIpcOpenMemHandle(ctypes.byref(pointer), handle, ctypes.c_uint(_CUDA_IPC_LAZY_ENABLE_PEER_ACCESS))
+        if rc != 0 or pointer.value is None:
+            raise RuntimeError(f"cudaIpcOpenMemHandle failed with code {rc}")
+        self._opened.append(pointer.value)
+        return pointer.value
+
+    def close(self) -> None:
+        for address in self._opened:
+            self._cuda.cudaIpcCloseMemHandle(ctypes.c_void_p(address))
+        self._opened.clear()
+
+    def layers(self) -> int:
+        """The layers the serving process has filled in its layer table (reference :122-125)."""
+        raw = (ctypes.c_uint64 * self.max_layers)()
+        rc = self._cuda.cudaMemcpy(raw, ctypes.c_void_p(self.table), ctypes.c_size_t(self.max_layers * 8),
+                                   _CUDA_MEMCPY_DEVICE_TO_HOST)
+        if rc != 0:
+            raise RuntimeError(f"cudaMemcpy of the layer table failed with code {rc}")
+        return int(np.count_nonzero(np.frombuffer(raw, dtype=np.uint64)))
+
+    def read(self, live_rows: int, row_blocks: np.ndarray) -> torch.Tensor:
+        layers = self.layers()
+        if layers == 0:
+            raise RuntimeError("the layer table is empty: the serving process has not filled it")
+        live = int(live_rows)
+        out = torch.full((max(live, 0), self.width), float("nan"), dtype=torch.float32, device=self.device)
+        if live <= 0:
+            return out
+        blocks = np.asarray(row_blocks)[:live].astype(np.int64)
+        if not (blocks > 0).any():
+            return out
+        # rows of 0 blocks have no evidence: a row id outside the table makes the kernel write NaN
+        ids = np.where(blocks > 0, np.arange(live), -1).astype(np.int32)
+        ids_t = torch.from_numpy(ids).to(self.device)
+        rb_t = torch.from_numpy(np.clip(blocks, -1, 2**31 - 1).astype(np.int32)).to(self.device)
+        rc = _lib.load().ekv_normalize_tile_lse(
+            self.base, self.max_layers, layers, self.rows, self.width, self.group_rows, ids_t.data_ptr(),
+            rb_t.data_ptr(), live, self.tile_blocks, _AGGREGATES[self.aggregate], out.data_ptr(), None,
+            _lib.current_stream(),
+        )
+        _lib.check(rc, "ekv_normalize_tile_lse")
+        return out
+
+
+class ShareLedger:
+    """The smoothed float64 share of every block of every measured request, one device row per request.
+
+    ``absorb`` is the fold of Controller._absorb_audit (observe/controller.py:332-345); ``slots`` and
+    ``measured`` are the reference's ``shares`` keys (as ledger rows) and ``measured`` dict; ``forget``
+    is the shares part of _forget_departed (:347-359); ``keep_mask`` is Controller._allocate's keep mask
+    (:398-451) with no released blocks."""
+
+    def __init__(self, width: int, capacity: int = 256, *, share_decay: float = 0.5, device=None) -> None:
+        if width <= 0 or capacity <= 0:
+            raise ValueError("the ledger needs a positive width and capacity")
+        if not 0.0 <= share_decay < 1.0:
+            raise ValueError("invalid controller settings")
+        self.width = int(width)
+        self.decay = float(share_decay)
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.table = torch.zeros(int(capacity), self.width, dtype=torch.float64, device=self.device)
+        self.slots: dict[int, int] = {}  # request key -> ledger row
+        self.measured: dict[int, int] = {}  # request key -> blocks the latest audit covered
+        self._free = list(range(int(capacity) - 1, -1, -1))
+        self.evidence_version = 0
+
+    # -- bookkeeping ---------------------------------------------------------------------------------
+
+    def _take_slot(self) -> int:
+        if not self._free:  # grow: the rows keep their slots
+            old = self.table.shape[0]
+            grown = torch.zeros(2 * old, self.width, dtype=torch.float64, device=self.device)
+            grown[:old].copy_(self.table)
+            self.table = grown
+            self._free = list(range(2 * old - 1, old - 1, -1))
+        return self._free.pop()
+
+    def __contains__(self, key: int) -> bool:
+        return int(key) in self.slots
+
+    def shares(self, key: int) -> np.ndarray:
+        """The request's smoothed shares (float64 [width]), copied to the host."""
+        return self.table[self.slots[int(key)]].cpu().numpy()
+
+    def forget(self, present_keys: Sequence[int] | np.ndarray) -> None:
+        """Drop the requests that are no longer in the batch (observe/controller.py:347-359)."""
+        present = {int(k) for k in np.asarray(present_keys, dtype=np.uint64).tolist() if int(k)}
+        for key in set(self.slots) - present:
+            self._free.append(self.slots.pop(key))
+            self.measured.pop(key, None)
+
+    # -- the fold of one audit -----------------------------------------------------------------------
+
+    def absorb(self, fresh: torch.Tensor, audit_keys: np.ndarray, row_blocks: np.ndarray) -> list[int]:
+        """Fold one audit's shares ``fresh`` [live, width] (float32 or float64, on the device; NaN without
+        evidence) into the requests ``audit_keys[row]`` (0: no request). ``row_blocks[row]`` is the
+        request's length in blocks, which becomes its ``measured`` count. Returns the keys that received
+        evidence, in row order."""
+        if fresh.ndim != 2 or fresh.shape[1] != self.width or not fresh.is_cuda:
+            raise ValueError(f"fresh shares must be a device tensor [rows, {self.width}]")
+        if fresh.dtype not in (torch.float32, torch.float64) or fresh.stride(1) != 1:
+            raise ValueError("fresh shares must be float32 or float64 with contiguous rows")
+        live = int(fresh.shape[0])
+        keys = np.asarray(audit_keys, dtype=np.uint64)[:live].tolist()
+        blocks = np.asarray(row_blocks)[:live]
+        # a key met twice folds twice, in row order (rounds of first occurrences, second, ...)
+        rounds: list[list[int]] = []
+        seen: dict[int, int] = {}
+        for row, key in enumerate(keys):
+            if key:
+                k = seen.get(key, 0)
+                seen[key] = k + 1
+                if k == len(rounds):
+                    rounds.append([])
+                rounds[k].append(row)
+        updated: list[tuple[int, int]] = []
+        lib = _lib.load()
+        stream = _lib.current_stream()
+        for rows in rounds:
+            slot = np.full(live, -1, dtype=np.int32)
+            blend = np.zeros(live, dtype=np.uint8)
+            tentative: dict[int, int] = {}
+            for row in rows:
+                key = keys[row]
+                if key in self.slots:
+                    slot[row], blend[row] = self.slots[key], 1
+                else:
+                    slot[row] = tentative[row] = self._take_slot()
+            evidence = torch.empty(live, dtype=torch.uint8, device=self.device)
+            slot_t = torch.from_numpy(slot).to(self.device)
+            blend_t = torch.from_numpy(blend).to(self.device)
+            rc = lib.ekv_ledger_absorb(
+                fresh.data_ptr(), int(fresh.dtype == torch.float64), fresh.stride(0), slot_t.data_ptr(),
+                blend_t.data_ptr(), self.decay, live, self.width, self.table.data_ptr(), self.table.stride(0),
+                self.table.shape[0], evidence.data_ptr(), stream,
+            )
+            _lib.check(rc, "ekv_ledger_absorb")
+            has = evidence.cpu().numpy()
+            for row in rows:
+                key = keys[row]
+                if has[row]:
+                    if row in tentative:
+                        self.slots[key] = tentative[row]
+                    self.measured[key] = int(blocks[row])
+                    self.evidence_version += 1
+                    updated.append((row, key))
+                elif row in tentative:
+                    self._free.append(tentative[row])
+        return [key for _, key in sorted(updated)]
+
+    # -- the committed keep mask ---------------------------------------------------------------------
+
+    def keep_mask(
+        self,
+        keys: np.ndarray,
+        lengths: np.ndarray,
+        *,
+        budget_fraction: float,
+        objective: Objective = "sum",
+        recent_blocks: int = 4,
+        cap_above_blocks: int = 0,
+        weight: Callable[[int], float] | None = None,
+    ) -> torch.Tensor:
+        """The keep mask uint8 [rows, width] (on the device) of Controller._allocate for the rows' request
+        ``keys`` and ``lengths`` (blocks): measured rows (longer than ``cap_above_blocks``, with shares)
+        keep their pins and their share of one budget, max(pins, ceil(budget_fraction * blocks)); every
+        other row, and every position past a request's length, keeps all."""
+        if objective not in ("sum", "maxmin", "uniform"):
+            raise ValueError(f"unknown objective {objective!r}")
+        if not 0.0 < budget_fraction <= 1.0:
+            raise ValueError("the budget fraction must be in (0, 1]")
+        keys_l = np.asarray(keys, dtype=np.uint64).tolist()
+        lengths = np.asarray(lengths).astype(np.int64)
+        rows = len(keys_l)
+        W = self.width
+        row_blocks = np.zeros(rows, dtype=np.int32)
+        measured = np.zeros(rows, dtype=np.int32)
+        score_rows = np.zeros(rows, dtype=np.int32)
+        weights = np.ones(rows, dtype=np.float64)
+        for row, key in enumerate(keys_l):
+            n = int(lengths[row])
+            if n > cap_above_blocks and key and key in self.slots:
+                row_blocks[row] = min(n, 2**31 - 1)
+                measured[row] = min(self.measured[key], 2**31 - 1)
+                score_rows[row] = self.slots[key]
+                if weight is not None:
+                    weights[row] = float(weight(key))
+        if objective != "sum" and np.any(weights != 1.0):
+            raise ValueError(f"the {objective} objective does not use request weights")
+        if objective == "sum" and (np.any(weights < 0.0) or not np.all(np.isfinite(weights))):
+            raise RuntimeError("negative or non-finite request weights are not supported on the device")
+        dev = self.device
+        lib = _lib.load()
+        stream = _lib.current_stream()
+        rb_t = torch.from_numpy(row_blocks).to(dev)
+        ms_t = torch.from_numpy(measured).to(dev)
+        sr_t = torch.from_numpy(score_rows).to(dev)
+        quota = torch.empty(rows, dtype=torch.int32, device=dev)
+        w_t = None
+        if objective == "sum":
+            w_t = torch.from_numpy(weights).to(dev)
+            sum_quotas(self.table, rb_t, quota, measured=ms_t, recent_blocks=recent_blocks,
+                       cap_above_blocks=cap_above_blocks, budget_fraction=budget_fraction, weights=w_t,
+                       score_rows=sr_t)
+            policy = _lib.POLICY_SUM
+        elif objective == "maxmin":
+            maxmin_quotas(self.table, rb_t, quota, measured=ms_t, recent_blocks=recent_blocks,
+                          cap_above_blocks=cap_above_blocks, budget_fraction=budget_fraction, score_rows=sr_t)
+            policy = _lib.POLICY_UNIFORM
+        else:
+            rc = lib.ekv_allocate_quotas(rb_t.data_ptr(), ms_t.data_ptr(), int(recent_blocks), int(cap_above_blocks),
+                                         float(budget_fraction), -1, None, _lib.POLICY_UNIFORM, rows, W,
+                                         quota.data_ptr(), stream)
+            _lib.check(rc, "ekv_allocate_quotas")
+            policy = _lib.POLICY_UNIFORM
+        mask = torch.empty(rows, W, dtype=torch.uint8, device=dev)
+        rc = lib.ekv_view_build_f64(
+            None, 0, None, rb_t.data_ptr(), quota.data_ptr(), ms_t.data_ptr(), int(recent_blocks),
+            self.table.data_ptr(), self.table.stride(0), sr_t.data_ptr(), None if w_t is None else w_t.data_ptr(),
+            policy, None, None, 0, rows, W, 16, None, 0, None, mask.data_ptr(), W, stream,
+        )
+        _lib.check(rc, "ekv_view_build_f64")
+        return mask
+

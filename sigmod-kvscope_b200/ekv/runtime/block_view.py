@@ -55,6 +55,7 @@ def _view_build(
     policy: str = "uniform",
     out: tuple[torch.Tensor, torch.Tensor] | None = None,
     mask_out: torch.Tensor | None = None,
+    weights: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     rows, width = int(table.shape[0]), int(table.shape[1])
     if table.dtype != torch.int32 or seq_lens.dtype != torch.int32:
@@ -75,6 +76,18 @@ def _view_build(
         return t if t.stride(-1) == 1 else t.contiguous()
 
     keep, full_rows, released = u8(keep), u8(full_rows), u8(released)
+    if scores is not None and scores.dtype == torch.float64 and keep is None:
+        # float64 scores: ranked by the float64 share (or weighted gain) itself
+        rc = _lib.load().ekv_view_build_f64(
+            table.data_ptr(), table.stride(0), seq_lens.data_ptr(), _ptr(row_blocks), _ptr(quota), _ptr(measured),
+            int(recent_blocks), scores.data_ptr(), scores.stride(0), None,
+            _ptr(weights) if policy == "sum" else None, _POLICIES[policy],
+            _ptr(full_rows), _ptr(released), released.stride(0) if released is not None else 0, rows, width,
+            int(block_size), view.data_ptr(), view.stride(0), view_lens.data_ptr(), _ptr(mask_out),
+            mask_out.stride(0) if mask_out is not None else 0, _lib.current_stream(),
+        )
+        _lib.check(rc, "ekv_view_build_f64")
+        return view, view_lens
     rc = _lib.load().ekv_view_build(
         table.data_ptr(), table.stride(0), seq_lens.data_ptr(), _ptr(row_blocks), _ptr(quota), _ptr(measured),
         int(recent_blocks), _ptr(scores), scores.stride(0) if scores is not None else 0, _POLICIES[policy],
@@ -127,8 +140,9 @@ def plan_view(
     Rows at or below ``cap_above_blocks`` read in full. With ``budget_fraction`` the measured rows
     share the budget max(pins, ceil(fraction * blocks)) (controller.py:398-451), split by uniform
     quotas, or under ``sum`` by the global greedy over the weighted shares (``weights`` float64
-    [rows], None for 1.0; a row of weight 0 must pass zero scores); with ``row_fraction`` (float64
-    [rows]) each row is its own allocate() call. ``policy`` "uniform"/"sum" ranks by ``scores`` (float32 [rows, width], the device shares),
+    [rows], None for 1.0; with float32 scores a row of weight 0 must pass zero scores); with
+    ``row_fraction`` (float64 [rows]) each row is its own allocate() call. ``policy`` "uniform"/"sum"
+    ranks by ``scores`` (float32 [rows, width], the device shares, or float64: the smoothed shares),
     "newest" keeps the newest blocks (the daemon's recency rule). ``mask_out`` receives the mask the
     controller commits.
     """
@@ -156,14 +170,14 @@ def plan_view(
     else:
         rc = _lib.load().ekv_allocate_quotas(
             row_blocks.data_ptr(), _ptr(measured), int(recent_blocks), int(cap_above_blocks),
-            float(budget_fraction or 0.0), -1, _ptr(row_fraction), objective, rows, quota.data_ptr(),
-            _lib.current_stream(),
+            float(budget_fraction or 0.0), -1, _ptr(row_fraction), objective, rows, int(table.shape[1]),
+            quota.data_ptr(), _lib.current_stream(),
         )
         _lib.check(rc, "ekv_allocate_quotas")
     return _view_build(
         table, seq_lens, block_size, row_blocks=row_blocks, quota=quota, measured=measured,
         recent_blocks=recent_blocks, scores=scores, policy=policy, released=released, full_rows=full_rows,
-        mask_out=mask_out, out=out,
+        mask_out=mask_out, out=out, weights=weights,
     )
 
 

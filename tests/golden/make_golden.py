@@ -12,7 +12,10 @@ It imports the reference read-only and runs, on CPU:
   * ``allocate`` (observe/allocation.py) with the pins and budget of Controller._allocate;
   * ``compact_block_table`` (runtime/block_view.py:36-56);
   * ``SlotCompactor.compact`` (runtime/sglang_compact.py), the SGLang CSR compaction, both Triton
-    kernels under the interpreter.
+    kernels under the interpreter;
+  * ``allocate`` on float64 scores whose shares round together (``float64_cases``);
+  * ``Controller._absorb_audit`` and ``Controller._allocate`` (observe/controller.py) over a sequence
+    of audits, with stand-ins for the mailbox writer and the share source (``controller_cases``).
 Inputs are seeded; the fixtures hold inputs and outputs, so the tests never need the reference.
 """
 
@@ -311,6 +314,164 @@ def slot_cases():
     print("slot_cases written")
 
 
+def _near_ties(rng, n):
+    """float64 scores with runs of adjacent doubles, whose shares often round to one value."""
+    base = rng.random(n) * 10.0 ** rng.integers(-3, 2)
+    runs = rng.integers(1, 5, n)
+    out = []
+    for x, k in zip(base.tolist(), runs.tolist(), strict=True):
+        for _ in range(k):
+            out.append(x)
+            x = float(np.nextafter(x, np.inf))
+    return np.array(out[:n])
+
+
+def float64_cases():
+    """allocate() on float64 scores: adjacent doubles (distinct scores with equal shares), weights that
+    merge gains, negative scores, exact float32 values and requests without evidence."""
+    rng = np.random.default_rng(53)
+    cases = {}
+    for i in range(90):
+        n_req = int(rng.integers(1, 9))
+        sizes = rng.integers(1, 120, n_req)
+        kind = i % 3
+        scores = []
+        for n in sizes:
+            if kind == 0:
+                x = _near_ties(rng, n)
+            elif kind == 1:
+                x = rng.dirichlet(np.full(n, 0.3)) if n > 1 else rng.random(1)
+            else:
+                x = np.where(rng.random(n) < 0.5, _near_ties(rng, n), rng.integers(-1, 3, n).astype(np.float64))
+            scores.append(x)
+        if i % 11 == 4:
+            scores[0][:] = 0.0  # no evidence: equal shares
+        objective = ("sum", "uniform", "maxmin")[(i // 3) % 3]
+        weights = np.ones(n_req)
+        if objective == "sum":
+            weights = rng.choice([1.0, 0.3, 1.7, 2.0, 0.0, 1.0 / 3.0], n_req)
+        recent = int(rng.integers(0, 5))
+        pinned = []
+        for n in sizes:
+            p = np.zeros(n, dtype=bool)
+            p[0] = True
+            p[max(0, n - 1 - recent):] = True
+            pinned.append(p)
+        must = sum(int(p.sum()) for p in pinned)
+        total = int(sizes.sum())
+        budget = int(rng.integers(must, total + 1))
+        requests = [Request(scores=x, weight=float(w), pinned=p) for x, w, p in zip(scores, weights, pinned, strict=True)]
+        masks = allocate(requests, budget, objective)
+        cases[f"sizes{i}"], cases[f"scores{i}"], cases[f"weights{i}"] = sizes, np.concatenate(scores), weights
+        cases[f"recent{i}"], cases[f"budget{i}"] = np.int64(recent), np.int64(budget)
+        cases[f"objective{i}"] = objective
+        cases[f"mask{i}"] = np.concatenate(masks)
+    np.savez_compressed(os.path.join(HERE, "float64_cases.npz"), **cases)
+    print("float64_cases written")
+
+
+class _Box:
+    def __init__(self, rows, width):
+        self.max_rows, self.row_width = rows, width
+        self.record = (0, 0, np.zeros(rows, dtype=np.uint64))
+
+    def audit_record(self):
+        return self.record
+
+
+class _Writer:
+    def __init__(self, rows, width):
+        self.box = _Box(rows, width)
+
+    def ack_audit(self, done):
+        pass
+
+
+class _Source:
+    """Serves a prepared share matrix, NaN for the rows of 0 blocks as TileShareSource.read leaves them."""
+
+    def __init__(self):
+        self.fresh = None
+
+    def read(self, live_rows, row_blocks):
+        out = self.fresh[:live_rows].copy()
+        out[np.asarray(row_blocks)[:live_rows] <= 0] = np.nan
+        return out
+
+
+def controller_cases():
+    """Controller._absorb_audit then _forget_departed then _allocate (observe/controller.py:311-451), as a
+    tick runs them, over a sequence of audits: requests that come, grow, are audited again (their shares
+    blended), have no evidence, are at or below the length cap, and leave. One controller per objective."""
+    from observe.controller import Controller, Settings
+
+    rows, width = 20, 64
+    rng = np.random.default_rng(61)
+    pool = rng.integers(1, 2**63, 40, dtype=np.uint64)
+    cases = {"rows": np.int64(rows), "width": np.int64(width)}
+    setups = [("sum", 0.4, 4, 0.5, 0), ("uniform", 0.3, 2, 0.25, 8), ("maxmin", 0.5, 3, 0.5, 4), ("sum", 0.25, 0, 0.0, 16)]
+
+    def weight(key):
+        return 1.0 + 0.25 * (int(key) % 4) - (0.5 if int(key) % 7 == 0 else 0.0)
+
+    steps = 10
+    cases["steps"] = np.int64(steps)
+    cases["setups"] = np.array([f"{o},{f},{r},{d},{c}" for o, f, r, d, c in setups])
+    controllers = []
+    for objective, fraction, recent, decay, cap in setups:
+        settings = Settings(budget_fraction=fraction, objective=objective, recent_blocks=recent, share_decay=decay,
+                            cap_above_blocks=cap)
+        writer, source = _Writer(rows, width), _Source()
+        controllers.append((Controller(writer, source, settings, weight=weight if objective == "sum" else None),
+                            writer, source))
+    present = list(pool[:14])
+    length = {int(k): int(rng.integers(1, 60)) for k in pool}
+    for step in range(steps):
+        # the batch: some requests leave, some arrive, every request grows
+        if step:
+            for _ in range(int(rng.integers(0, 3))):
+                if present:
+                    present.pop(int(rng.integers(0, len(present))))
+            for k in pool[rng.permutation(len(pool))[: int(rng.integers(0, 4))]]:
+                if k not in present and len(present) < rows:
+                    present.append(k)
+        for k in present:
+            length[int(k)] = min(width + 20, length[int(k)] + int(rng.integers(0, 6)))
+        keys = np.zeros(rows, dtype=np.uint64)
+        lengths = np.zeros(rows, dtype=np.int64)
+        slots = rng.permutation(rows)[: len(present)]
+        for k, r in zip(present, slots, strict=True):
+            keys[r], lengths[r] = k, length[int(k)]
+        # the audit: a subset of the rows (by key), in an order of its own
+        audit_keys = np.zeros(rows, dtype=np.uint64)
+        audited = [k for k in present if rng.random() < 0.7]
+        for k, r in zip(audited, rng.permutation(rows)[: len(audited)], strict=True):
+            audit_keys[r] = k
+        fresh = np.full((rows, width), np.nan)
+        for r in range(rows):
+            if rng.random() < 0.15:
+                continue  # no evidence for this row
+            x = rng.dirichlet(np.full(width, 0.4))
+            if rng.random() < 0.3:
+                x[rng.random(width) < 0.2] = np.nan  # cells without data
+            fresh[r] = x
+        cases[f"keys{step}"], cases[f"lengths{step}"] = keys, lengths
+        cases[f"audit_keys{step}"], cases[f"fresh{step}"] = audit_keys, fresh
+        for c, (controller, writer, source) in enumerate(controllers):
+            writer.box.record = (step + 1, step + 1, audit_keys)
+            source.fresh = fresh
+            controller._absorb_audit(keys, lengths)
+            controller._forget_departed(keys)
+            keep, _release = controller._allocate(keys, lengths)
+            cases[f"keep{c}_{step}"] = keep
+            ks = sorted(controller.shares)
+            cases[f"share_keys{c}_{step}"] = np.array(ks, dtype=np.uint64)
+            cases[f"shares{c}_{step}"] = np.array([controller.shares[k] for k in ks]).reshape(len(ks), width)
+            cases[f"measured{c}_{step}"] = np.array([controller.measured[k] for k in ks], dtype=np.int64)
+    np.savez_compressed(os.path.join(HERE, "controller_cases.npz"), **cases)
+    print("controller_cases written")
+
+
 def all_cases():
     audit_case("audit_cfg1_fp16", 0, rows=4, q_heads=8, kv_heads=2, layers=1, len_lo=100, len_hi=600, pool=256, dtype="fp16")
     audit_case("audit_layers_fp16", 1, rows=6, q_heads=8, kv_heads=2, layers=3, len_lo=1, len_hi=300, pool=256,
@@ -321,6 +482,8 @@ def all_cases():
     view_cases()
     slot_cases()
     maxmin_cases()
+    float64_cases()
+    controller_cases()
 
 
 if __name__ == "__main__":

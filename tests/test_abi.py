@@ -113,9 +113,9 @@ def test_other_entry_points_validate_before_launching(lib):
     assert lib.ekv_normalize_tile_lse(fake, 1, 1, 1, 1, 1, fake, fake, 0, 2, 0, fake, None, None) == L.OK  # no rows
     assert lib.ekv_normalize_log_weights(fake, 1, 1, 1, 1, fake, 0, 0, fake, None, None) == L.EINVAL
     assert lib.ekv_share_finalize(None, fake, None, 1, 1, 0, fake, None) == L.EINVAL
-    assert lib.ekv_allocate_quotas(fake, None, 4, 0, 0.5, -1, None, L.POLICY_SUM, 4, fake, None) == L.ENOTSUP
-    assert lib.ekv_allocate_quotas(fake, None, 4, 0, 1.5, -1, None, L.POLICY_UNIFORM, 4, fake, None) == L.EINVAL
-    assert lib.ekv_allocate_quotas(fake, None, 4, 0, 0.5, -1, None, L.POLICY_UNIFORM, 9000, fake, None) == L.ENOTSUP
+    assert lib.ekv_allocate_quotas(fake, None, 4, 0, 0.5, -1, None, L.POLICY_SUM, 4, 0, fake, None) == L.ENOTSUP
+    assert lib.ekv_allocate_quotas(fake, None, 4, 0, 1.5, -1, None, L.POLICY_UNIFORM, 4, 0, fake, None) == L.EINVAL
+    assert lib.ekv_allocate_quotas(fake, None, 4, 0, 0.5, -1, None, L.POLICY_UNIFORM, 9000, 0, fake, None) == L.ENOTSUP
     view_args = [fake, 8, fake, fake, fake, None, 0, None, 8, L.POLICY_SUM, None, 0, None, None, 0, 2, 8, 16,
                  fake, 8, fake, None, 0, None]
     assert lib.ekv_view_build(*view_args) == L.EINVAL  # ranking by shares without scores
@@ -140,6 +140,27 @@ def test_other_entry_points_validate_before_launching(lib):
     assert lib.ekv_allocate_maxmin(*mm_args) == L.ERANGE  # no workspace
     mm_args[11], mm_args[12], mm_args[9] = ctypes.c_void_p(0x1000), 1 << 30, 9000
     assert lib.ekv_allocate_maxmin(*mm_args) == L.ENOTSUP  # wider than 8192
+    # the float64 entry points
+    sum64 = [fake, 8, None, None, fake, None, 4, 0, 0.5, -1, 2, 8, fake, ctypes.c_void_p(0x1000), ws, None]
+    sum64[11] = 20000
+    assert lib.ekv_allocate_sum_f64(*sum64) == L.ENOTSUP  # a float64 row is staged whole: wider than 16384
+    sum64[11], sum64[13] = 8, None
+    assert lib.ekv_allocate_sum_f64(*sum64) == L.ERANGE  # no workspace
+    mm64 = [fake, 4, None, fake, None, 4, 0, 0.5, -1, 2, 8, fake, ctypes.c_void_p(0x1000), 1 << 30, None]
+    assert lib.ekv_allocate_maxmin_f64(*mm64) == L.EINVAL  # score stride below the width
+    v64 = [None, 0, None, fake, fake, None, 0, fake, 8, None, None, L.POLICY_SUM, None, None, 0, 2, 8, 16,
+           None, 0, None, None, 0, None]
+    assert lib.ekv_view_build_f64(*v64) == L.EINVAL  # neither a view nor a mask
+    v64[21], v64[22] = fake, 8
+    v64[8] = 4
+    assert lib.ekv_view_build_f64(*v64) == L.EINVAL  # score stride below the width
+    v64[8], v64[11] = 8, 7
+    assert lib.ekv_view_build_f64(*v64) == L.EINVAL  # unknown policy
+    ledger = [fake, 1, 8, fake, fake, 0.5, 2, 8, fake, 8, 4, fake, None]
+    ledger[5] = 1.0
+    assert lib.ekv_ledger_absorb(*ledger) == L.EINVAL  # a decay of 1 keeps nothing new
+    ledger[5], ledger[9] = 0.5, 4
+    assert lib.ekv_ledger_absorb(*ledger) == L.EINVAL  # ledger stride below the width
     # the SGLang compaction: entry size, pointers and strides
     slot_args = [fake, fake, 8, fake, 20, None, 1, 2, 2, 40, 16, 20, fake, fake, fake, 20, fake, fake, None]
     slot_args[2] = 3
@@ -166,4 +187,4 @@ def test_step_and_stash_validate_before_launching(lib):
 
 
 def test_abi_version(lib):
-    assert lib.ekv_abi_version() == 3
+    assert lib.ekv_abi_version() == 4

@@ -210,3 +210,54 @@ def test_oracle_maxmin_matches_the_reference_allocate():
         pinned = [oa.controller_pins(int(n), int(g[f"recent{i}"])) for n in sizes]
         masks = oa.allocate(scores, int(g[f"budget{i}"]), "maxmin", pinned)
         np.testing.assert_array_equal(np.concatenate(masks), g[f"mask{i}"], err_msg=f"case {i}")
+
+
+def test_oracle_float64_allocation_matches_the_reference():
+    """Every objective on float64 scores whose shares (and weighted gains) round together."""
+    g = load_golden("float64_cases")
+    for i in range(90):
+        sizes = g[f"sizes{i}"]
+        bounds = np.concatenate([[0], np.cumsum(sizes)])
+        scores = [g[f"scores{i}"][bounds[j] : bounds[j + 1]] for j in range(len(sizes))]
+        pinned = [oa.controller_pins(int(n), int(g[f"recent{i}"])) for n in sizes]
+        masks = oa.allocate(scores, int(g[f"budget{i}"]), str(g[f"objective{i}"]), pinned, list(g[f"weights{i}"]))
+        np.testing.assert_array_equal(np.concatenate(masks), g[f"mask{i}"], err_msg=f"case {i}")
+
+
+def controller_setups(g):
+    out = []
+    for text in g["setups"]:
+        objective, fraction, recent, decay, cap = str(text).split(",")
+        out.append((objective, float(fraction), int(recent), float(decay), int(cap)))
+    return out
+
+
+def controller_weight(key):
+    """The request weights make_golden.py gives the reference controller (sum objective only)."""
+    return 1.0 + 0.25 * (int(key) % 4) - (0.5 if int(key) % 7 == 0 else 0.0)
+
+
+def test_oracle_controller_matches_the_reference_sequence():
+    """oracle.controller.Ledger against the reference Controller over a sequence of audits: the smoothed
+    shares, the measured lengths and the committed keep mask after every audit, bit for bit."""
+    from oracle import controller as oc
+
+    g = load_golden("controller_cases")
+    width = int(g["width"])
+    for c, (objective, fraction, recent, decay, cap) in enumerate(controller_setups(g)):
+        ledger = oc.Ledger(width, decay)
+        for step in range(int(g["steps"])):
+            keys, lengths, audit_keys = g[f"keys{step}"], g[f"lengths{step}"], g[f"audit_keys{step}"]
+            live, row_blocks = oc.audit_row_blocks(audit_keys, keys, lengths, cap)
+            fresh = g[f"fresh{step}"][:live].copy()
+            fresh[row_blocks <= 0] = np.nan
+            ledger.absorb(fresh, audit_keys, row_blocks)
+            ledger.forget(keys)
+            keep = ledger.keep(keys, lengths, width, fraction, objective, recent, cap,
+                               controller_weight if objective == "sum" else None)
+            ks = sorted(ledger.shares)
+            np.testing.assert_array_equal(np.array(ks, dtype=np.uint64), g[f"share_keys{c}_{step}"])
+            got = np.array([ledger.shares[k] for k in ks]).reshape(len(ks), width)
+            np.testing.assert_array_equal(got, g[f"shares{c}_{step}"], err_msg=f"setup {c} step {step}")
+            np.testing.assert_array_equal([ledger.measured[k] for k in ks], g[f"measured{c}_{step}"])
+            np.testing.assert_array_equal(keep, g[f"keep{c}_{step}"], err_msg=f"setup {c} step {step}")

@@ -212,126 +212,297 @@ __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
 }
 
 // A thread per row: prefix[j] = prefix[j - 1] + sorted[j], one addition after another (block-major
-// arrays: a warp's loads and stores are contiguous).
+// arrays: a warp's loads and stores are contiguous). The additions of a row are a dependent chain, so
+// the loads run far ahead of it: each lane copies its own row's next shares into a ring of shared-memory
+// stages with cp.async (8 bytes per copy, 256 bytes per warp instruction) and reads back only what it
+// copied itself, so no barrier is needed.
+constexpr int kCsChunk = 32;   // shares of a row per stage
+constexpr int kCsStages = 8;   // stages in the ring: 7 in flight while one is added up
+constexpr size_t kCsSmem = (size_t)kCsStages * kCsChunk * 32 * sizeof(double);
+
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
 __global__ void __launch_bounds__(32) mm_cumsum_kernel(const MmParams p) {
-  const int r = blockIdx.x * 32 + threadIdx.x;
-  if (r >= p.rows) return;
-  const int m = p.row_m[r];
+  extern __shared__ __align__(16) double cs_ring[];  // [kCsStages][kCsChunk][32]
+  const int lane = threadIdx.x;
+  const int r = blockIdx.x * 32 + lane;
+  const int m = r < p.rows ? p.row_m[r] : 0;
   const int64_t R = p.rows;
-  constexpr int C = 16;  // values per chunk; the next chunk is loaded while this one is added
-  double acc = 0.0, cur[C], nxt[C];
+  int most = m;
+  for (int off = 16; off > 0; off >>= 1) most = max(most, __shfl_xor_sync(kFullMask, most, off));
+  const int chunks = most > 0 ? (most + kCsChunk - 1) / kCsChunk : 0;
+  const double* src = p.sorted + (r < p.rows ? r : 0);
+  double* dst = p.prefix + (r < p.rows ? r : 0);
+  double* ring = cs_ring + lane;
+  // chunk c: this lane's shares c * kCsChunk + u, u < kCsChunk, into stage c % kCsStages
+  auto issue = [&](int c) {
+    if (c < chunks) {
+      const int left = m - c * kCsChunk;
+      const double* g = src + (int64_t)c * kCsChunk * R;
+      double* sh = ring + (c % kCsStages) * kCsChunk * 32;
+      if (left >= kCsChunk) {
 #pragma unroll
-  for (int u = 0; u < C; ++u) cur[u] = u < m ? p.sorted[u * R + r] : 0.0;
-  for (int j = 0; j < m; j += C) {
-#pragma unroll
-    for (int u = 0; u < C; ++u) nxt[u] = j + C + u < m ? p.sorted[(j + C + u) * R + r] : 0.0;
-#pragma unroll
-    for (int u = 0; u < C; ++u) {
-      if (j + u < m) {
-        acc = (j + u == 0) ? cur[u] : acc + cur[u];
-        p.prefix[(j + u) * R + r] = acc;
+        for (int u = 0; u < kCsChunk; ++u) cp_async8(sh + u * 32, g + u * R);
+      } else {
+        for (int u = 0; u < left; ++u) cp_async8(sh + u * 32, g + u * R);
       }
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");  // an empty group keeps the count in step
+  };
+  for (int c = 0; c < kCsStages - 1; ++c) issue(c);
+  // np.cumsum: out[0] = a[0], out[j] = out[j - 1] + a[j]; the shares are +0 or positive, so starting
+  // from +0 gives out[0] bit for bit
+  double acc = 0.0;
+  for (int c = 0; c < chunks; ++c) {
+    issue(c + kCsStages - 1);
+    asm volatile("cp.async.wait_group %0;" ::"n"(kCsStages - 1) : "memory");  // chunk c has landed
+    const double* sh = ring + (c % kCsStages) * kCsChunk * 32;
+    double* g = dst + (int64_t)c * kCsChunk * R;
+    const int left = m - c * kCsChunk;
+    if (left >= kCsChunk) {
 #pragma unroll
-    for (int u = 0; u < C; ++u) cur[u] = nxt[u];
+      for (int u = 0; u < kCsChunk; ++u) {
+        acc = __dadd_rn(acc, sh[u * 32]);
+        g[u * R] = acc;
+      }
+    } else {
+      for (int u = 0; u < left; ++u) {
+        acc = __dadd_rn(acc, sh[u * 32]);
+        g[u * R] = acc;
+      }
+    }
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
-// searchsorted (side left) of x in request r's running sums, each plus the request's offset: the first
-// j with prefix[j] + offset >= x, known to lie in [lo, hi] (it grows with x).
-__device__ __forceinline__ int mm_search(const MmParams& p, int r, double x, double offset, int lo, int hi) {
-  while (lo < hi) {
-    const int mid = (lo + hi) >> 1;
-    if (p.prefix[(int64_t)mid * p.rows + r] + offset < x) lo = mid + 1; else hi = mid;
-  }
-  return lo;
-}
-
-// The blocks request r needs beyond its pins to retain `level` (allocation.py:146-150), and in *lb the
-// search result it comes from.
-__device__ __forceinline__ int mm_extra(const MmParams& p, int r, double level, int lo, int hi, int* lb) {
-  const int m = p.row_m[r];
-  *lb = lo;
-  if (m < 0) return 0;
-  const double need = level - p.base[r];
-  const double offset = 2.0 * (double)p.req[r];
-  *lb = mm_search(p, r, need - 1e-12 + offset, offset, lo, hi);
-  if (need <= 1e-12) return 0;
-  return *lb + 1 < m ? *lb + 1 : m;
-}
-
+// The water level by bisection, several steps per round: the 2^S - 1 levels the next S steps can
+// probe (a binary tree: a step that fits the budget raises `low`, else it lowers `high`) are evaluated
+// together, then the path through them is taken. Each evaluation is, per request, the searchsorted of
+// allocation.py:146-150 -- the first j with prefix[j] + offset >= x -- confined to the request's
+// results at the round's two ends (the result grows with the level), the 2^S - 1 searches of a request
+// interleaved so their loads overlap.
+constexpr int kMmSpec = 3;
+constexpr int kMmNodes = (1 << kMmSpec) - 1;
+constexpr int kMmLevelThreads = 512;
 constexpr int kMmAhead = 2;  // next shares per request staged in shared memory for the leftover blocks
-constexpr size_t kMmLevelBytesPerRow = 8 + 8 * kMmAhead + 4 * 3;
+constexpr int kMmFewLeftovers = 64;  // up to this many leftover blocks: argmin per block, no heap
 
-// One CTA: the water level, the leftover blocks and the quotas. Dynamic shared memory per request: the
-// heap entry (double level, int row), the next kMmAhead shares, the count and the count at the start
-// of the leftover blocks.
-__global__ void __launch_bounds__(kMmThreads) mm_level_kernel(const MmParams p) {
+// Shared memory of mm_level_kernel, per request: counts and blocks (kept throughout), then either the
+// bisection's state or the leftover heap.
+struct MmLevelSmem {
+  size_t counts, m, u, base, off, lo, hi, lbs, level, ahead, row, start, bytes;
+};
+
+__host__ __device__ inline MmLevelSmem mm_level_smem(int rows) {
+  MmLevelSmem l{};
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o += (bytes + 15) / 16 * 16;
+    return at;
+  };
+  l.counts = take((size_t)rows * 4);
+  l.m = take((size_t)rows * 4);
+  l.u = o;  // the union
+  l.base = take((size_t)rows * 8);
+  l.off = take((size_t)rows * 8);
+  l.lo = take((size_t)rows * 4);
+  l.hi = take((size_t)rows * 4);
+  l.lbs = take((size_t)rows * kMmNodes * 2);
+  const size_t bisection_end = o;
+  o = l.u;
+  l.level = take((size_t)rows * 8);
+  l.ahead = take((size_t)rows * 8 * kMmAhead);
+  l.row = take((size_t)rows * 4);
+  l.start = take((size_t)rows * 4);
+  l.bytes = o > bisection_end ? o : bisection_end;
+  return l;
+}
+
+// One CTA: the water level, the leftover blocks and the quotas.
+__global__ void __launch_bounds__(kMmLevelThreads) mm_level_kernel(const MmParams p) {
   extern __shared__ __align__(16) unsigned char lv_smem[];
-  double* h_level = reinterpret_cast<double*>(lv_smem);
-  double* ahead = h_level + p.rows;  // [rows][kMmAhead]
-  int* h_row = reinterpret_cast<int*>(ahead + (size_t)p.rows * kMmAhead);
-  int* counts = h_row + p.rows;
-  int* start = counts + p.rows;
-  __shared__ long long s_red[kMmThreads / 32];
+  const MmLevelSmem L = mm_level_smem(p.rows);
+  int* counts = reinterpret_cast<int*>(lv_smem + L.counts);
+  int* s_m = reinterpret_cast<int*>(lv_smem + L.m);
+  double* s_base = reinterpret_cast<double*>(lv_smem + L.base);
+  double* s_off = reinterpret_cast<double*>(lv_smem + L.off);
+  int* s_lo = reinterpret_cast<int*>(lv_smem + L.lo);
+  int* s_hi = reinterpret_cast<int*>(lv_smem + L.hi);
+  uint16_t* s_lbs = reinterpret_cast<uint16_t*>(lv_smem + L.lbs);
+  double* h_level = reinterpret_cast<double*>(lv_smem + L.level);
+  double* ahead = reinterpret_cast<double*>(lv_smem + L.ahead);  // [rows][kMmAhead]
+  int* h_row = reinterpret_cast<int*>(lv_smem + L.row);
+  int* start = reinterpret_cast<int*>(lv_smem + L.start);
+  __shared__ long long s_red[kMmLevelThreads / 32][kMmNodes];
+  __shared__ long long s_tot[kMmNodes];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const MmState* st = p.state;
   const int mode = st->mode;
   if (mode != kMmSelect) {
-    for (int r = tid; r < p.rows; r += kMmThreads) {
+    for (int r = tid; r < p.rows; r += kMmLevelThreads) {
       const int m = p.row_m[r];
       p.quota[r] = m < 0 ? -1 : (mode == kMmAll ? m : 0);
     }
     return;
   }
   const long long free_ = st->free_;
-  // each request's search result is monotone in the level: keep it at both ends of the bisection and
-  // search only between them
-  for (int r = tid; r < p.rows; r += kMmThreads) {
+  const int64_t R = p.rows;
+  for (int r = tid; r < p.rows; r += kMmLevelThreads) {
     const int m = p.row_m[r];
-    p.lb_low[r] = 0;
-    p.lb_high[r] = m > 0 ? m : 0;
+    s_m[r] = m;
+    s_base[r] = p.base[r];
+    s_off[r] = 2.0 * (double)p.req[r];
+    s_lo[r] = 0;
+    s_hi[r] = m > 0 ? m : 0;
   }
+  __syncthreads();
   double low = 0.0, high = 1.0;
-  for (int it = 0; it < kMmBisection; ++it) {
-    const double mid = (low + high) / 2;
-    long long sum = 0;
-    for (int r = tid; r < p.rows; r += kMmThreads) {
-      int lb;
-      sum += mm_extra(p, r, mid, p.lb_low[r], p.lb_high[r], &lb);
-      counts[r] = lb;  // (scratch: the search result at mid)
+  for (int round = 0; round < kMmBisection / kMmSpec; ++round) {
+    // the levels of the tree: node n's children are 2n + 1 (its level did not fit: high = mid) and
+    // 2n + 2 (it fit: low = mid); every thread builds the same tree
+    double lo_v[kMmNodes], hi_v[kMmNodes], mid[kMmNodes];
+    lo_v[0] = low, hi_v[0] = high;
+#pragma unroll
+    for (int n = 0; n < kMmNodes; ++n) {
+      mid[n] = (lo_v[n] + hi_v[n]) / 2;
+      if (2 * n + 2 < kMmNodes) {
+        lo_v[2 * n + 1] = lo_v[n], hi_v[2 * n + 1] = mid[n];
+        lo_v[2 * n + 2] = mid[n], hi_v[2 * n + 2] = hi_v[n];
+      }
     }
-    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(kFullMask, sum, off);
+    long long sum[kMmNodes];
+#pragma unroll
+    for (int n = 0; n < kMmNodes; ++n) sum[n] = 0;
+    for (int r = tid; r < p.rows; r += kMmLevelThreads) {
+      const int m = s_m[r];
+      if (m < 0) continue;
+      const double base = s_base[r], off = s_off[r];
+      int lo[kMmNodes], hi[kMmNodes];
+      double x[kMmNodes];
+#pragma unroll
+      for (int n = 0; n < kMmNodes; ++n) {
+        lo[n] = s_lo[r], hi[n] = s_hi[r];
+        x[n] = (mid[n] - base) - 1e-12 + off;
+      }
+      for (;;) {  // the searches side by side, one load each per step
+        double v[kMmNodes];
+        int md[kMmNodes];
+        bool active = false;
+#pragma unroll
+        for (int n = 0; n < kMmNodes; ++n) {
+          md[n] = (lo[n] + hi[n]) >> 1;
+          if (lo[n] < hi[n]) v[n] = p.prefix[(int64_t)md[n] * R + r], active = true;
+        }
+        if (!active) break;
+#pragma unroll
+        for (int n = 0; n < kMmNodes; ++n) {
+          if (lo[n] < hi[n]) {
+            if (v[n] + off < x[n]) lo[n] = md[n] + 1; else hi[n] = md[n];
+          }
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < kMmNodes; ++n) {
+        s_lbs[(size_t)r * kMmNodes + n] = (uint16_t)lo[n];
+        const double need = mid[n] - base;
+        sum[n] += need <= 1e-12 ? 0 : (lo[n] + 1 < m ? lo[n] + 1 : m);
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < kMmNodes; ++n)
+      for (int off = 16; off > 0; off >>= 1) sum[n] += __shfl_xor_sync(kFullMask, sum[n], off);
+    if (lane == 0)
+#pragma unroll
+      for (int n = 0; n < kMmNodes; ++n) s_red[warp][n] = sum[n];
     __syncthreads();
-    if (lane == 0) s_red[warp] = sum;
+    if (tid < kMmNodes) {
+      long long t = 0;
+      for (int w = 0; w < kMmLevelThreads / 32; ++w) t += s_red[w][tid];
+      s_tot[tid] = t;
+    }
     __syncthreads();
-    long long t = 0;
-    for (int w = 0; w < kMmThreads / 32; ++w) t += s_red[w];
-    const bool up = t <= free_;
-    for (int r = tid; r < p.rows; r += kMmThreads) (up ? p.lb_low : p.lb_high)[r] = counts[r];
-    if (up) low = mid; else high = mid;
+    int n = 0, lo_node = -1, hi_node = -1;
+    for (int d = 0; d < kMmSpec; ++d) {
+      double level = mid[0];  // mid[n] without indexing a register array at run time
+#pragma unroll
+      for (int k = 1; k < kMmNodes; ++k) level = k == n ? mid[k] : level;
+      if (s_tot[n] <= free_) {
+        low = level, lo_node = n, n = 2 * n + 2;
+      } else {
+        high = level, hi_node = n, n = 2 * n + 1;
+      }
+    }
+    for (int r = tid; r < p.rows; r += kMmLevelThreads) {
+      if (s_m[r] < 0) continue;
+      if (lo_node >= 0) s_lo[r] = s_lbs[(size_t)r * kMmNodes + lo_node];
+      if (hi_node >= 0) s_hi[r] = s_lbs[(size_t)r * kMmNodes + hi_node];
+    }
+    // (the next round's first barrier comes after every thread's last read of s_tot and s_lbs here)
   }
   long long used = 0;
-  for (int r = tid; r < p.rows; r += kMmThreads) {
-    int lb;
-    counts[r] = mm_extra(p, r, low, p.lb_low[r], p.lb_low[r], &lb);
-    used += counts[r];
+  for (int r = tid; r < p.rows; r += kMmLevelThreads) {  // the blocks each request takes at `low`
+    const int m = s_m[r];
+    int c = 0;
+    if (m >= 0) {
+      const double need = low - s_base[r];
+      c = need <= 1e-12 ? 0 : (s_lo[r] + 1 < m ? s_lo[r] + 1 : m);
+    }
+    counts[r] = c;
+    used += c;
   }
   for (int off = 16; off > 0; off >>= 1) used += __shfl_xor_sync(kFullMask, used, off);
-  __syncthreads();
-  if (lane == 0) s_red[warp] = used;
+  if (lane == 0) s_red[warp][0] = used;
+  __syncthreads();  // the bisection's state is dead from here: the heap takes its place
   // each request's retained share (its heap entry) and the shares of its next blocks, loaded in parallel
-  for (int r = tid; r < p.rows; r += kMmThreads) {
-    const int m = p.row_m[r], c = counts[r];
-    h_level[r] = m < 0 ? 0.0 : p.base[r] + (c ? p.prefix[(int64_t)(c - 1) * p.rows + r] : 0.0);
+  for (int r = tid; r < p.rows; r += kMmLevelThreads) {
+    const int m = s_m[r], c = counts[r];
+    h_level[r] = m < 0 ? 0.0 : p.base[r] + (c ? p.prefix[(int64_t)(c - 1) * R + r] : 0.0);
     start[r] = c;
 #pragma unroll
-    for (int a = 0; a < kMmAhead; ++a) ahead[(size_t)r * kMmAhead + a] = c + a < m ? p.sorted[(int64_t)(c + a) * p.rows + r] : 0.0;
+    for (int a = 0; a < kMmAhead; ++a) ahead[(size_t)r * kMmAhead + a] = c + a < m ? p.sorted[(int64_t)(c + a) * R + r] : 0.0;
   }
   __syncthreads();
-  if (tid == 0) {
-    long long leftover = free_;
-    for (int w = 0; w < kMmThreads / 32; ++w) leftover -= s_red[w];
+  long long leftover = free_;
+  for (int w = 0; w < kMmLevelThreads / 32; ++w) leftover -= s_red[w][0];
+  if (leftover > 0 && leftover <= kMmFewLeftovers) {
+    // a few blocks left over: each goes to the request of lowest (retained share, index) that can take
+    // one, found by a block-wide argmin (heappop of allocation.py:160-166, without building the heap)
+    __shared__ double s_best_level[kMmLevelThreads / 32];
+    __shared__ int s_best_row[kMmLevelThreads / 32];
+    for (long long k = 0; k < leftover; ++k) {
+      double best = 0.0;
+      int best_row = -1;
+      for (int r = tid; r < p.rows; r += kMmLevelThreads) {
+        const int m = s_m[r];
+        if (m < 0 || counts[r] >= m) continue;
+        if (best_row < 0 || h_level[r] < best) best = h_level[r], best_row = r;  // rows ascend: ties keep the lower
+      }
+      for (int off = 16; off > 0; off >>= 1) {
+        const double ol = __shfl_xor_sync(kFullMask, best, off);
+        const int orow = __shfl_xor_sync(kFullMask, best_row, off);
+        if (orow >= 0 && (best_row < 0 || ol < best || (ol == best && orow < best_row))) best = ol, best_row = orow;
+      }
+      if (lane == 0) s_best_level[warp] = best, s_best_row[warp] = best_row;
+      __syncthreads();
+      if (tid == 0) {
+        for (int w = 1; w < kMmLevelThreads / 32; ++w) {
+          const double ol = s_best_level[w];
+          const int orow = s_best_row[w];
+          if (orow >= 0 && (best_row < 0 || ol < best || (ol == best && orow < best_row))) best = ol, best_row = orow;
+        }
+        if (best_row >= 0) {
+          const int c = counts[best_row]++;
+          const int a = c - start[best_row];
+          h_level[best_row] = best + (a < kMmAhead ? ahead[(size_t)best_row * kMmAhead + a]
+                                                   : p.sorted[(int64_t)c * R + best_row]);
+        }
+      }
+      __syncthreads();
+    }
+  } else if (leftover > 0 && tid == 0) {
     // the requests that can still take a block, keyed by (retained share, request); a min-heap
     auto less = [&](int a, int b) {
       return h_level[a] < h_level[b] || (h_level[a] == h_level[b] && h_row[a] < h_row[b]);
@@ -354,7 +525,7 @@ __global__ void __launch_bounds__(kMmThreads) mm_level_kernel(const MmParams p) 
     };
     int size = 0;  // the requests that can take a block, in order (an in-place compaction)
     for (int r = 0; r < p.rows; ++r) {
-      const int m = p.row_m[r];
+      const int m = s_m[r];
       if (m < 0 || counts[r] >= m) continue;
       h_level[size] = h_level[r];
       h_row[size] = r;
@@ -366,7 +537,7 @@ __global__ void __launch_bounds__(kMmThreads) mm_level_kernel(const MmParams p) 
       const double level = h_level[0];
       const int c = counts[r]++;
       --leftover;
-      if (counts[r] < p.row_m[r]) {  // back with its next block's share added (heappop then heappush)
+      if (counts[r] < s_m[r]) {  // back with its next block's share added (heappop then heappush)
         const int a = c - start[r];
         h_level[0] = level + (a < kMmAhead ? ahead[(size_t)r * kMmAhead + a] : p.sorted[(int64_t)c * p.rows + r]);
         sift_down(0, size);
@@ -380,7 +551,7 @@ __global__ void __launch_bounds__(kMmThreads) mm_level_kernel(const MmParams p) 
     }
   }
   __syncthreads();
-  for (int r = tid; r < p.rows; r += kMmThreads) p.quota[r] = p.row_m[r] < 0 ? -1 : counts[r];
+  for (int r = tid; r < p.rows; r += kMmLevelThreads) p.quota[r] = s_m[r] < 0 ? -1 : counts[r];
 }
 
 }  // namespace ekv
@@ -428,11 +599,17 @@ static int allocate_maxmin(const S* scores, int64_t score_stride, const int32_t*
   if (cudaMemsetAsync(base + l.state, 0, sizeof(MmState), s) != cudaSuccess)
     return check_launch("cudaMemsetAsync(maxmin state)");
   const size_t prep_smem = mm_prep_smem<S>(width);
-  const size_t level_smem = (size_t)rows * kMmLevelBytesPerRow;
+  const size_t level_smem = mm_level_smem(rows).bytes;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
     return check_launch("cudaGetDevice");
   static size_t prep_set[kMaxDevices] = {}, level_set[kMaxDevices] = {};
+  static bool cumsum_set[kMaxDevices] = {};
+  if (!cumsum_set[device]) {
+    if (cudaFuncSetAttribute(mm_cumsum_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCsSmem) != cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(mm_cumsum_kernel)");
+    cumsum_set[device] = true;
+  }
   if (prep_set[device] < prep_smem) {
     if (cudaFuncSetAttribute(mm_prep_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(mm_prep_kernel)");
@@ -447,9 +624,9 @@ static int allocate_maxmin(const S* scores, int64_t score_stride, const int32_t*
   mm_prep_kernel<S><<<rows, kMmThreads, prep_smem, s>>>(p);
   int rc = check_launch("mm_prep_kernel");
   if (rc != EKV_OK) return rc;
-  mm_cumsum_kernel<<<(rows + 31) / 32, 32, 0, s>>>(p);
+  mm_cumsum_kernel<<<(rows + 31) / 32, 32, kCsSmem, s>>>(p);
   if ((rc = check_launch("mm_cumsum_kernel")) != EKV_OK) return rc;
-  mm_level_kernel<<<1, kMmThreads, level_smem, s>>>(p);
+  mm_level_kernel<<<1, kMmLevelThreads, level_smem, s>>>(p);
   return check_launch("mm_level_kernel");
 }
 

@@ -144,6 +144,55 @@ def test_maxmin_matches_the_reference_and_the_oracle():
             np.testing.assert_array_equal(a, b, err_msg=f"trial {trial}, request {r}")
 
 
+def water_leftover(scores, pinned, budget):
+    """Blocks the water level leaves over for the heap (allocation.py:121-160), as the oracle computes it."""
+    shares = [oa.shares(s) for s in scores]
+    order = [np.flatnonzero(~p)[np.argsort(-shares[r][~p], kind="stable")] for r, p in enumerate(pinned)]
+    base = np.array([float(shares[r][p].sum()) for r, p in enumerate(pinned)])
+    prefix = [np.cumsum(shares[r][order[r]]) for r in range(len(scores))]
+    stacked = np.concatenate([p + 2.0 * r for r, p in enumerate(prefix)])
+    sizes = np.array([len(o) for o in order])
+    starts = np.concatenate(([0], np.cumsum(sizes)[:-1]))
+    offsets = 2.0 * np.arange(len(scores))
+    free = budget - sum(int(p.sum()) for p in pinned)
+
+    def extra(level):
+        need = level - base
+        position = np.searchsorted(stacked, need - 1e-12 + offsets) - starts
+        return np.where(need <= 1e-12, 0, np.minimum(position + 1, sizes))
+
+    low, high = 0.0, 1.0
+    for _ in range(60):
+        mid = (low + high) / 2
+        if int(extra(mid).sum()) <= free:
+            low = mid
+        else:
+            high = mid
+    return free - int(extra(low).sum())
+
+
+def test_maxmin_leftover_blocks_by_argmin_and_by_heap():
+    """Requests that reach the water level together leave blocks over: a few go out one block-wide argmin
+    at a time, many through the heap; both give the reference's order (lowest retained share, then the
+    earlier request)."""
+    from ekv.observe.allocation import Request, allocate
+
+    rng = np.random.default_rng(71)
+    one = rng.random(50)
+    scores = [one.copy() for _ in range(240)]
+    pinned = [oa.controller_pins(len(x), 2) for x in scores]
+    must = sum(int(p.sum()) for p in pinned)
+    seen = set()
+    for budget in range(must + 2400, must + 2640, 9):
+        left = water_leftover(scores, pinned, budget)
+        seen.add("none" if left == 0 else ("few" if left <= 64 else "many"))
+        got = allocate([Request(scores=x, pinned=p) for x, p in zip(scores, pinned, strict=True)], budget, "maxmin")
+        want = oa.allocate(scores, budget, "maxmin", pinned)
+        for r, (a, b) in enumerate(zip(got, want, strict=True)):
+            np.testing.assert_array_equal(a, b, err_msg=f"budget {budget} ({left} left over), request {r}")
+    assert {"few", "many"} <= seen, seen
+
+
 def test_plan_view_maxmin_with_a_shared_budget_matches_the_controller():
     from ekv.runtime.block_view import plan_view
 

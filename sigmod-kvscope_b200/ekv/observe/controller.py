@@ -26,7 +26,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from collections.abc import Callable, Sequence
+from collections.abc import Callable, Mapping, Sequence
 
 import numpy as np
 import torch
@@ -36,6 +36,7 @@ from ..runtime.audit import _cudart
 from .allocation import Objective, maxmin_quotas, sum_quotas
 from .tile_shares import _AGGREGATES, Aggregate, _check_aggregate
 
+_TORCH_DTYPES = {np.dtype(np.int32): torch.int32, np.dtype(np.uint8): torch.uint8, np.dtype(np.float64): torch.float64}
 _CUDA_IPC_LAZY_ENABLE_PEER_ACCESS = 1
 _CUDA_MEMCPY_DEVICE_TO_HOST = 2
 
@@ -134,13 +135,30 @@ class DeviceShareSource:
         return out
 
 
+class _MeasuredView(Mapping):
+    """request key -> blocks its latest audit covered (the reference's ``measured`` dict), read-only."""
+
+    def __init__(self, ledger: "ShareLedger") -> None:
+        self._ledger = ledger
+
+    def __getitem__(self, key: int) -> int:
+        return int(self._ledger._measured[self._ledger.slots[int(key)]])
+
+    def __iter__(self):
+        return iter(self._ledger.slots)
+
+    def __len__(self) -> int:
+        return len(self._ledger.slots)
+
+
 class ShareLedger:
     """The smoothed float64 share of every block of every measured request, one device row per request.
 
     ``absorb`` is the fold of Controller._absorb_audit (observe/controller.py:332-345); ``slots`` and
     ``measured`` are the reference's ``shares`` keys (as ledger rows) and ``measured`` dict; ``forget``
     is the shares part of _forget_departed (:347-359); ``keep_mask`` is Controller._allocate's keep mask
-    (:398-451) with no released blocks."""
+    (:398-451) with no released blocks. The per-row bookkeeping is vectorised (a sorted key index, one
+    pinned host-to-device copy per call), so a tick over a thousand requests costs launches, not Python."""
 
     def __init__(self, width: int, capacity: int = 256, *, share_decay: float = 0.5, device=None) -> None:
         if width <= 0 or capacity <= 0:
@@ -152,20 +170,51 @@ class ShareLedger:
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.table = torch.zeros(int(capacity), self.width, dtype=torch.float64, device=self.device)
         self.slots: dict[int, int] = {}  # request key -> ledger row
-        self.measured: dict[int, int] = {}  # request key -> blocks the latest audit covered
+        self._measured = np.zeros(int(capacity), dtype=np.int64)  # ledger row -> blocks its audit covered
+        self.measured = _MeasuredView(self)
         self._free = list(range(int(capacity) - 1, -1, -1))
+        self._index: tuple[np.ndarray, np.ndarray] | None = None  # sorted keys and their rows
         self.evidence_version = 0
 
     # -- bookkeeping ---------------------------------------------------------------------------------
 
-    def _take_slot(self) -> int:
-        if not self._free:  # grow: the rows keep their slots
+    def _take_slots(self, count: int) -> np.ndarray:
+        while len(self._free) < count:  # grow: the rows keep their slots
             old = self.table.shape[0]
             grown = torch.zeros(2 * old, self.width, dtype=torch.float64, device=self.device)
             grown[:old].copy_(self.table)
             self.table = grown
-            self._free = list(range(2 * old - 1, old - 1, -1))
-        return self._free.pop()
+            self._measured = np.concatenate([self._measured, np.zeros(old, dtype=np.int64)])
+            self._free = list(range(2 * old - 1, old - 1, -1)) + self._free
+        taken = self._free[len(self._free) - count:][::-1]
+        del self._free[len(self._free) - count:]
+        return np.asarray(taken, dtype=np.int32)
+
+    def _slot_of(self, keys: np.ndarray) -> np.ndarray:
+        """The ledger row of each key, -1 for key 0 and for keys without shares."""
+        if self._index is None:
+            k = np.fromiter(self.slots.keys(), dtype=np.uint64, count=len(self.slots))
+            v = np.fromiter(self.slots.values(), dtype=np.int32, count=len(self.slots))
+            order = np.argsort(k)
+            self._index = (k[order], v[order])
+        sorted_keys, rows = self._index
+        if sorted_keys.size == 0:
+            return np.full(len(keys), -1, dtype=np.int32)
+        at = np.minimum(np.searchsorted(sorted_keys, keys), sorted_keys.size - 1)
+        return np.where((sorted_keys[at] == keys) & (keys != 0), rows[at], -1).astype(np.int32)
+
+    def _to_device(self, *arrays: np.ndarray) -> list[torch.Tensor]:
+        """The arrays on the device through one pinned buffer and one asynchronous copy (8-byte aligned)."""
+        offsets, total = [], 0
+        for a in arrays:
+            offsets.append(total)
+            total += (a.nbytes + 7) // 8 * 8
+        host = torch.empty(max(total, 8), dtype=torch.uint8, pin_memory=True)
+        view = host.numpy()
+        for a, o in zip(arrays, offsets, strict=True):
+            view[o : o + a.nbytes] = np.ascontiguousarray(a).view(np.uint8).reshape(-1)
+        dev = host.to(self.device, non_blocking=True)
+        return [dev[o : o + a.nbytes].view(_TORCH_DTYPES[a.dtype]) for a, o in zip(arrays, offsets, strict=True)]
 
     def __contains__(self, key: int) -> bool:
         return int(key) in self.slots
@@ -176,10 +225,14 @@ class ShareLedger:
 
     def forget(self, present_keys: Sequence[int] | np.ndarray) -> None:
         """Drop the requests that are no longer in the batch (observe/controller.py:347-359)."""
-        present = {int(k) for k in np.asarray(present_keys, dtype=np.uint64).tolist() if int(k)}
-        for key in set(self.slots) - present:
+        if not self.slots:
+            return
+        held = np.fromiter(self.slots.keys(), dtype=np.uint64, count=len(self.slots))
+        gone = held[~np.isin(held, np.asarray(present_keys, dtype=np.uint64))]
+        for key in gone.tolist():
             self._free.append(self.slots.pop(key))
-            self.measured.pop(key, None)
+        if gone.size:
+            self._index = None
 
     # -- the fold of one audit -----------------------------------------------------------------------
 
@@ -193,52 +246,55 @@ class ShareLedger:
         if fresh.dtype not in (torch.float32, torch.float64) or fresh.stride(1) != 1:
             raise ValueError("fresh shares must be float32 or float64 with contiguous rows")
         live = int(fresh.shape[0])
-        keys = np.asarray(audit_keys, dtype=np.uint64)[:live].tolist()
-        blocks = np.asarray(row_blocks)[:live]
-        # a key met twice folds twice, in row order (rounds of first occurrences, second, ...)
-        rounds: list[list[int]] = []
-        seen: dict[int, int] = {}
-        for row, key in enumerate(keys):
-            if key:
-                k = seen.get(key, 0)
-                seen[key] = k + 1
-                if k == len(rounds):
-                    rounds.append([])
-                rounds[k].append(row)
-        updated: list[tuple[int, int]] = []
-        lib = _lib.load()
-        stream = _lib.current_stream()
-        for rows in rounds:
-            slot = np.full(live, -1, dtype=np.int32)
-            blend = np.zeros(live, dtype=np.uint8)
-            tentative: dict[int, int] = {}
-            for row in rows:
-                key = keys[row]
-                if key in self.slots:
-                    slot[row], blend[row] = self.slots[key], 1
-                else:
-                    slot[row] = tentative[row] = self._take_slot()
-            evidence = torch.empty(live, dtype=torch.uint8, device=self.device)
-            slot_t = torch.from_numpy(slot).to(self.device)
-            blend_t = torch.from_numpy(blend).to(self.device)
-            rc = lib.ekv_ledger_absorb(
-                fresh.data_ptr(), int(fresh.dtype == torch.float64), fresh.stride(0), slot_t.data_ptr(),
-                blend_t.data_ptr(), self.decay, live, self.width, self.table.data_ptr(), self.table.stride(0),
-                self.table.shape[0], evidence.data_ptr(), stream,
-            )
-            _lib.check(rc, "ekv_ledger_absorb")
-            has = evidence.cpu().numpy()
-            for row in rows:
-                key = keys[row]
-                if has[row]:
-                    if row in tentative:
-                        self.slots[key] = tentative[row]
-                    self.measured[key] = int(blocks[row])
-                    self.evidence_version += 1
-                    updated.append((row, key))
-                elif row in tentative:
-                    self._free.append(tentative[row])
-        return [key for _, key in sorted(updated)]
+        keys = np.asarray(audit_keys, dtype=np.uint64)[:live]
+        blocks = np.asarray(row_blocks)[:live].astype(np.int64)
+        present = np.flatnonzero(keys)
+        if present.size == 0:
+            return []
+        # a key met twice folds twice, in row order: rows are folded in rounds of first occurrences,
+        # second occurrences, ...
+        order = np.argsort(keys[present], kind="stable")
+        sorted_keys = keys[present][order]
+        first = np.ones(present.size, dtype=bool)
+        first[1:] = sorted_keys[1:] != sorted_keys[:-1]
+        group_start = np.maximum.accumulate(np.where(first, np.arange(present.size), 0))
+        occurrence = np.empty(present.size, dtype=np.int64)
+        occurrence[order] = np.arange(present.size) - group_start
+        updated: list[np.ndarray] = []
+        for k in range(int(occurrence.max()) + 1):
+            rows = present[occurrence == k]
+            updated.append(self._fold(fresh, live, keys, blocks, rows))
+        got = np.sort(np.concatenate(updated))
+        return keys[got].tolist()
+
+    def _fold(self, fresh: torch.Tensor, live: int, keys: np.ndarray, blocks: np.ndarray, rows: np.ndarray) -> np.ndarray:
+        """One kernel over the rows ``rows`` (distinct keys); returns the rows that had evidence."""
+        slot = np.full(live, -1, dtype=np.int32)
+        slot[rows] = self._slot_of(keys[rows])
+        blend = (slot >= 0).astype(np.uint8)
+        new = rows[slot[rows] < 0]
+        if new.size:
+            slot[new] = self._take_slots(new.size)
+        slot_t, blend_t = self._to_device(slot, blend)
+        evidence = torch.empty(live, dtype=torch.uint8, device=self.device)
+        rc = _lib.load().ekv_ledger_absorb(
+            fresh.data_ptr(), int(fresh.dtype == torch.float64), fresh.stride(0), slot_t.data_ptr(),
+            blend_t.data_ptr(), self.decay, live, self.width, self.table.data_ptr(), self.table.stride(0),
+            self.table.shape[0], evidence.data_ptr(), _lib.current_stream(),
+        )
+        _lib.check(rc, "ekv_ledger_absorb")
+        has = evidence.cpu().numpy().astype(bool)
+        got = rows[has[rows]]
+        if new.size:
+            kept_new = new[has[new]]
+            self._free.extend(slot[new[~has[new]]].tolist())
+            for row in kept_new.tolist():
+                self.slots[int(keys[row])] = int(slot[row])
+            if kept_new.size:
+                self._index = None
+        self._measured[slot[got]] = blocks[got]
+        self.evidence_version += int(got.size)
+        return got
 
     # -- the committed keep mask ---------------------------------------------------------------------
 
@@ -261,22 +317,20 @@ class ShareLedger:
             raise ValueError(f"unknown objective {objective!r}")
         if not 0.0 < budget_fraction <= 1.0:
             raise ValueError("the budget fraction must be in (0, 1]")
-        keys_l = np.asarray(keys, dtype=np.uint64).tolist()
+        keys = np.asarray(keys, dtype=np.uint64)
         lengths = np.asarray(lengths).astype(np.int64)
-        rows = len(keys_l)
+        rows = len(keys)
         W = self.width
-        row_blocks = np.zeros(rows, dtype=np.int32)
-        measured = np.zeros(rows, dtype=np.int32)
-        score_rows = np.zeros(rows, dtype=np.int32)
+        slot = self._slot_of(keys)
+        chosen = (lengths > cap_above_blocks) & (keys != 0) & (slot >= 0)
+        big = 2**31 - 1
+        row_blocks = np.where(chosen, np.minimum(lengths, big), 0).astype(np.int32)
+        measured = np.where(chosen, np.minimum(self._measured[np.maximum(slot, 0)], big), 0).astype(np.int32)
+        score_rows = np.where(chosen, slot, 0).astype(np.int32)
         weights = np.ones(rows, dtype=np.float64)
-        for row, key in enumerate(keys_l):
-            n = int(lengths[row])
-            if n > cap_above_blocks and key and key in self.slots:
-                row_blocks[row] = min(n, 2**31 - 1)
-                measured[row] = min(self.measured[key], 2**31 - 1)
-                score_rows[row] = self.slots[key]
-                if weight is not None:
-                    weights[row] = float(weight(key))
+        if weight is not None:
+            picked = np.flatnonzero(chosen)
+            weights[picked] = [float(weight(k)) for k in keys[picked].tolist()]
         if objective != "sum" and np.any(weights != 1.0):
             raise ValueError(f"the {objective} objective does not use request weights")
         if objective == "sum" and (np.any(weights < 0.0) or not np.all(np.isfinite(weights))):
@@ -284,13 +338,9 @@ class ShareLedger:
         dev = self.device
         lib = _lib.load()
         stream = _lib.current_stream()
-        rb_t = torch.from_numpy(row_blocks).to(dev)
-        ms_t = torch.from_numpy(measured).to(dev)
-        sr_t = torch.from_numpy(score_rows).to(dev)
+        rb_t, ms_t, sr_t, w_t = self._to_device(row_blocks, measured, score_rows, weights)
         quota = torch.empty(rows, dtype=torch.int32, device=dev)
-        w_t = None
         if objective == "sum":
-            w_t = torch.from_numpy(weights).to(dev)
             sum_quotas(self.table, rb_t, quota, measured=ms_t, recent_blocks=recent_blocks,
                        cap_above_blocks=cap_above_blocks, budget_fraction=budget_fraction, weights=w_t,
                        score_rows=sr_t)
@@ -308,9 +358,9 @@ class ShareLedger:
         mask = torch.empty(rows, W, dtype=torch.uint8, device=dev)
         rc = lib.ekv_view_build_f64(
             None, 0, None, rb_t.data_ptr(), quota.data_ptr(), ms_t.data_ptr(), int(recent_blocks),
-            self.table.data_ptr(), self.table.stride(0), sr_t.data_ptr(), None if w_t is None else w_t.data_ptr(),
-            policy, None, None, 0, rows, W, 16, None, 0, None, mask.data_ptr(), W, stream,
+            self.table.data_ptr(), self.table.stride(0), sr_t.data_ptr(),
+            w_t.data_ptr() if objective == "sum" else None, policy, None, None, 0, rows, W, 16, None, 0, None,
+            mask.data_ptr(), W, stream,
         )
         _lib.check(rc, "ekv_view_build_f64")
         return mask
-

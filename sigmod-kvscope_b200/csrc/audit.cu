@@ -605,7 +605,7 @@ __device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, i
   __syncwarp();
 
   // 2. every tile's share, summed (mean) or maxed (max) over the query rows: exp(u - lse) =
-  // exp(m + log(l) - (M + log S)); the blocks of a partial last tile get its weight back,
+  // exp(m + log(l) - (M + log S)) = l * exp(m - lse); the blocks of a partial last tile get its weight back,
   // exp(u + log(TB / tail) - lse) = exp(u - lse) * TB / tail
   const bool agg_max = p.aggregate == EKV_AGG_MAX;
   const int tail = n % TB;
@@ -629,8 +629,9 @@ __device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, i
       }
 #pragma unroll
       for (int u = 0; u < kShareBatch; ++u) {
-        const float x = mv[u] + logf(lv[u]);
-        const float sh = x > -INFINITY ? __expf(x - lse) : 0.f;  // NaN cells fail the test: no share
+        // exp(m + log(l) - lse) as l * exp(m - lse): no logarithm per cell; a cell without data (m = -inf,
+        // l = 0) or never written (NaN) fails the test and has no share
+        const float sh = (mv[u] > -INFINITY && lv[u] > 0.f) ? lv[u] * __expf(mv[u] - lse) : 0.f;
         e[u] = agg_max ? fmaxf(e[u], sh) : e[u] + sh;
       }
     }

@@ -385,6 +385,20 @@ int ekv_view_build(const int32_t* table, int64_t table_stride, const int32_t* se
                    uint8_t* mask_out, int64_t mask_stride, void* stream);
 
 /*
+ * ekv_view_build_fractions -- ekv_allocate_quotas with per-row budgets (row_fraction) followed by
+ * ekv_view_build in ranking mode, in one kernel: each measured row (row_blocks[r] > cap_above_blocks
+ * and > 0) is its own allocate() call with budget max(pins, ceil(row_fraction[r] * n)), n =
+ * min(row_blocks[r], width); other rows read in full. Arguments as in those two calls.
+ */
+int ekv_view_build_fractions(const int32_t* table, int64_t table_stride, const int32_t* seq_lens,
+                             const int32_t* row_blocks, const double* row_fraction,
+                             const int32_t* measured_blocks, int recent_blocks, int cap_above_blocks,
+                             const float* scores, int64_t score_stride, int policy, const uint8_t* full_rows,
+                             const uint8_t* released, int64_t released_stride, int rows, int width,
+                             int block_size, int32_t* view, int64_t view_stride, int32_t* view_lens,
+                             uint8_t* mask_out, int64_t mask_stride, void* stream);
+
+/*
  * ekv_compact_block_table -- compact_block_table (runtime/block_view.py:36-56) on the device:
  * ekv_view_build in mask mode with no full rows and no released blocks.
  */

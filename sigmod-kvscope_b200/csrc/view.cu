@@ -207,6 +207,9 @@ struct ViewParams {
   // the read counters of a decode view (ekv_decode_view): full_rows then carries packed row flags
   long long* counts;
   int expired;
+  // per-row budgets computed in the kernel (ekv_view_build_fractions) instead of read from quota
+  const double* row_fraction;
+  int cap;
 };
 
 // Row flags of ekv_decode_view (full_rows): the row reads every block / decodes / is audited.
@@ -376,8 +379,21 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
   bool by_threshold = false, newest = false;
   if (rank_mode) {
     n_a = p.row_blocks[r];
+    const bool request = n_a > p.cap && n_a > 0;
     n_a = n_a < 0 ? 0 : (n_a > W ? W : n_a);
-    q = p.quota[r];
+    if (p.row_fraction != nullptr) {
+      // the quota of ekv_allocate_quotas for a row that is its own allocate() call, computed here
+      q = -1;
+      if (request) {
+        const int ps0 = pin_start(n_a, p.recent, p.measured, r);
+        const int pins = pin_count(n_a, ps0);
+        long long budget = (long long)ceil(p.row_fraction[r] * (double)n_a);
+        if (budget < pins) budget = pins;
+        q = budget >= n_a ? (ps0 > 1 ? ps0 - 1 : 0) : (int)(budget - pins);
+      }
+    } else {
+      q = p.quota[r];
+    }
     if (q >= 0 && n_a > 0) {
       ps = pin_start(n_a, p.recent, p.measured, r);
       const int n_open = ps > 1 ? ps - 1 : 0;
@@ -675,7 +691,7 @@ extern "C" int ekv_view_build(const int32_t* table, int64_t table_stride, const 
   ViewParams p{table,   table_stride, seq_lens, row_blocks, quota,      measured_blocks,
                recent_blocks, scores, score_stride, nullptr, nullptr, policy, keep,      keep_stride,
                full_rows, released, released_stride, rows, width,     block_size,
-               view,    view_stride,  view_lens, mask_out,  mask_stride, nullptr, 0};
+               view,    view_stride,  view_lens, mask_out,  mask_stride, nullptr, 0, nullptr, -1};
   return launch_view<uint32_t>(p, static_cast<cudaStream_t>(stream));
 }
 
@@ -709,7 +725,8 @@ extern "C" int ekv_decode_view(const int32_t* table, int64_t table_stride, const
   if (released && released_stride < width) return fail(EKV_EINVAL, "released_stride < width");
   ViewParams p{table, table_stride, seq_lens, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, nullptr, EKV_POLICY_UNIFORM,
                keep,  keep_stride,  row_flags, released, released_stride, rows, width, block_size,
-               view,  view_stride,  view_lens, nullptr, 0, reinterpret_cast<long long*>(counts), expired != 0};
+               view,  view_stride,  view_lens, nullptr, 0, reinterpret_cast<long long*>(counts), expired != 0,
+               nullptr, -1};
   return launch_view<uint32_t>(p, static_cast<cudaStream_t>(stream));
 }
 
@@ -738,6 +755,34 @@ extern "C" int ekv_view_build_f64(const int32_t* table, int64_t table_stride, co
   ViewParams p{table,   table_stride, seq_lens, row_blocks, quota,      measured_blocks,
                recent_blocks, scores, score_stride, score_rows, weights, policy, nullptr, 0,
                full_rows, released, released_stride, rows, width,     block_size,
-               view,    view_stride,  view_lens, mask_out,  mask_stride, nullptr, 0};
+               view,    view_stride,  view_lens, mask_out,  mask_stride, nullptr, 0, nullptr, -1};
   return launch_view<unsigned long long>(p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ekv_view_build_fractions(const int32_t* table, int64_t table_stride, const int32_t* seq_lens,
+                                        const int32_t* row_blocks, const double* row_fraction,
+                                        const int32_t* measured_blocks, int recent_blocks, int cap_above_blocks,
+                                        const float* scores, int64_t score_stride, int policy,
+                                        const uint8_t* full_rows, const uint8_t* released, int64_t released_stride,
+                                        int rows, int width, int block_size, int32_t* view, int64_t view_stride,
+                                        int32_t* view_lens, uint8_t* mask_out, int64_t mask_stride, void* stream) {
+  clear_error();
+  if (!table || !seq_lens || !view || !view_lens || !row_blocks || !row_fraction)
+    return fail(EKV_EINVAL, "a required pointer is NULL");
+  if (rows <= 0 || width <= 0 || block_size <= 0)
+    return fail(EKV_EINVAL, "rows, width and block_size must be positive");
+  if (width > kViewMaxWidth) return fail(EKV_ENOTSUP, "width %d > %d (a view row is staged in shared memory)", width, kViewMaxWidth);
+  if (table_stride < width || view_stride < width) return fail(EKV_EINVAL, "a row stride is below the width");
+  if (policy != EKV_POLICY_SUM && policy != EKV_POLICY_UNIFORM && policy != EKV_POLICY_NEWEST)
+    return fail(EKV_EINVAL, "unknown policy %d", policy);
+  if (policy != EKV_POLICY_NEWEST && (!scores || score_stride < width))
+    return fail(EKV_EINVAL, "ranking by shares needs scores with a row stride >= width");
+  if (recent_blocks < -1 || cap_above_blocks < -1) return fail(EKV_EINVAL, "invalid controller settings");
+  if (released && released_stride < width) return fail(EKV_EINVAL, "released_stride < width");
+  if (mask_out && mask_stride < width) return fail(EKV_EINVAL, "mask_stride < width");
+  ViewParams p{table,   table_stride, seq_lens, row_blocks, nullptr,    measured_blocks,
+               recent_blocks, scores, score_stride, nullptr, nullptr, policy, nullptr, 0,
+               full_rows, released, released_stride, rows, width,     block_size,
+               view,    view_stride,  view_lens, mask_out,  mask_stride, nullptr, 0, row_fraction, cap_above_blocks};
+  return launch_view<uint32_t>(p, static_cast<cudaStream_t>(stream));
 }

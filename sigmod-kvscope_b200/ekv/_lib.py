@@ -99,6 +99,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _i64, _p, _p, _p, _p, _i32, _p, _i64, _i32, _p, _i64, _p, _p, _i64,
          _i32, _i32, _i32, _p, _i64, _p, _p, _i64, _p],
     ),
+    "ekv_view_build_fractions": (
+        _i32,
+        [_p, _i64, _p, _p, _p, _p, _i32, _i32, _p, _i64, _i32, _p, _p, _i64,
+         _i32, _i32, _i32, _p, _i64, _p, _p, _i64, _p],
+    ),
     "ekv_compact_block_table": (_i32, [_p, _i64, _p, _p, _i64, _i32, _i32, _i32, _p, _i64, _p, _p]),
 }
 

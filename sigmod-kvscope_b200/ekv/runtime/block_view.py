@@ -149,6 +149,29 @@ def plan_view(
     if (budget_fraction is None) == (row_fraction is None):
         raise ValueError("give a shared budget fraction or per-row fractions, not both and not neither")
     rows = int(table.shape[0])
+    if row_fraction is not None and (scores is None or scores.dtype == torch.float32) and policy in ("sum", "uniform", "newest"):
+        # per-row budgets: the quotas and the view in one kernel
+        if table.dtype != torch.int32 or seq_lens.dtype != torch.int32 or table.stride(1) != 1:
+            raise ValueError("the block table (rows contiguous) and the lengths must be int32")
+        if policy != "newest" and scores is None:
+            raise ValueError(f"the {policy} objective ranks by scores")
+        width = int(table.shape[1])
+        view, view_lens = out if out is not None else (
+            torch.empty(rows, width, dtype=torch.int32, device=table.device),
+            torch.empty(rows, dtype=torch.int32, device=table.device),
+        )
+        if rows == 0:
+            return view, view_lens
+        rc = _lib.load().ekv_view_build_fractions(
+            table.data_ptr(), table.stride(0), seq_lens.data_ptr(), row_blocks.data_ptr(), row_fraction.data_ptr(),
+            _ptr(measured), int(recent_blocks), int(cap_above_blocks), _ptr(scores),
+            scores.stride(0) if scores is not None else 0, _POLICIES[policy], _ptr(full_rows), _ptr(released),
+            released.stride(0) if released is not None else 0, rows, width, int(block_size), view.data_ptr(),
+            view.stride(0), view_lens.data_ptr(), _ptr(mask_out), mask_out.stride(0) if mask_out is not None else 0,
+            _lib.current_stream(),
+        )
+        _lib.check(rc, "ekv_view_build_fractions")
+        return view, view_lens
     quota = torch.empty(rows, dtype=torch.int32, device=table.device)
     objective = _POLICIES[policy]
     if policy == "sum" and budget_fraction is not None:

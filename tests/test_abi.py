@@ -161,6 +161,14 @@ def test_other_entry_points_validate_before_launching(lib):
     assert lib.ekv_ledger_absorb(*ledger) == L.EINVAL  # a decay of 1 keeps nothing new
     ledger[5], ledger[9] = 0.5, 4
     assert lib.ekv_ledger_absorb(*ledger) == L.EINVAL  # ledger stride below the width
+    frac = [fake, 8, fake, fake, fake, None, 0, 0, fake, 8, L.POLICY_SUM, None, None, 0, 2, 8, 16, fake, 8, fake,
+            None, 0, None]
+    frac[4] = None
+    assert lib.ekv_view_build_fractions(*frac) == L.EINVAL  # no fractions
+    frac[4], frac[7] = fake, -2
+    assert lib.ekv_view_build_fractions(*frac) == L.EINVAL  # a cap below -1
+    frac[7], frac[15] = 0, 20000
+    assert lib.ekv_view_build_fractions(*frac) == L.ENOTSUP  # wider than 16384
     # the SGLang compaction: entry size, pointers and strides
     slot_args = [fake, fake, 8, fake, 20, None, 1, 2, 2, 40, 16, 20, fake, fake, fake, 20, fake, fake, None]
     slot_args[2] = 3

@@ -426,6 +426,44 @@ def test_view_stress_rows_match_the_oracle(policy):
     np.testing.assert_array_equal(view_lens.cpu().numpy(), ref_lens)
 
 
+@pytest.mark.parametrize("policy", ["sum", "uniform", "newest"])
+def test_per_row_budgets_in_one_kernel_match_the_two_launch_path(policy):
+    """ekv_view_build_fractions (quotas computed in the view kernel) against ekv_allocate_quotas followed by
+    ekv_view_build: length caps, measured suffixes, recent pins, rows longer than the table, empty rows,
+    full rows and released blocks, bit for bit."""
+    import ekv._lib as L
+    from ekv.runtime.block_view import _view_build, plan_view
+
+    rng = np.random.default_rng({"sum": 3, "uniform": 4, "newest": 5}[policy])
+    rows, width, cap, recent = 300, 1000, 16, 3
+    row_blocks = rng.integers(0, 1100, rows).astype(np.int32)
+    row_blocks[::13] = 0
+    measured = (row_blocks - rng.integers(0, 40, rows)).clip(0).astype(np.int32)
+    lens = (np.minimum(row_blocks, width) * 16 - rng.integers(0, 16, rows)).clip(0).astype(np.int32)
+    table = rng.integers(0, 1 << 20, (rows, width)).astype(np.int32)
+    scores = np.round(rng.dirichlet(np.full(width, 0.3), rows), 4).astype(np.float32)
+    fraction = rng.uniform(0.1, 1.0, rows)
+    full = (rng.random(rows) < 0.1).astype(np.uint8)
+    released = (rng.random((rows, width)) < 0.05).astype(np.uint8)
+    dev = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    args = dict(scores=dev(scores) if policy != "newest" else None, measured=dev(measured), recent_blocks=recent,
+                full_rows=dev(full), released=dev(released))
+    mask1 = torch.empty(rows, width, dtype=torch.uint8).cuda()
+    view1, lens1 = plan_view(dev(table), dev(lens), 16, dev(row_blocks), policy=policy, row_fraction=dev(fraction),
+                             cap_above_blocks=cap, mask_out=mask1, **args)
+    quota = torch.empty(rows, dtype=torch.int32).cuda()
+    rb, fr = dev(row_blocks), dev(fraction)  # held: the launches read them after this line
+    rc = L.load().ekv_allocate_quotas(rb.data_ptr(), args["measured"].data_ptr(), recent, cap, 0.0, -1, fr.data_ptr(),
+                                      L.POLICY_SUM, rows, width, quota.data_ptr(), L.current_stream())
+    L.check(rc, "ekv_allocate_quotas")
+    mask2 = torch.empty(rows, width, dtype=torch.uint8).cuda()
+    view2, lens2 = _view_build(dev(table), dev(lens), 16, row_blocks=rb, quota=quota, policy=policy, mask_out=mask2,
+                               **args)
+    np.testing.assert_array_equal(mask1.cpu().numpy(), mask2.cpu().numpy())
+    np.testing.assert_array_equal(view1.cpu().numpy(), view2.cpu().numpy())
+    np.testing.assert_array_equal(lens1.cpu().numpy(), lens2.cpu().numpy())
+
+
 def test_full_size_view_stress_properties():
     """1024 rows x 8192: the view is a permutation of the row, kept ids come first in their original
     order, the kept count is pins + quota, and the length formula holds."""

@@ -478,8 +478,15 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
       }
       if (lane == 0) s_w[warp] = above;
       __syncthreads();
-      int gt = above - sum;  // keys in higher bins
-      for (int w2 = warp + 1; w2 < kViewWarps; ++w2) gt += s_w[w2];
+      // keys in higher bins: the rest of this warp's plus every later warp's (a suffix sum of the warp
+      // totals by shuffles: lane j holds the total of warps j .. kViewWarps - 1)
+      int later = lane < kViewWarps ? s_w[lane] : 0;
+      for (int off = 1; off < kViewWarps; off <<= 1) {
+        const int v = __shfl_down_sync(kFullMask, later, off);
+        if (lane + off < kViewWarps) later += v;
+      }
+      later = __shfl_sync(kFullMask, later, (warp + 1) & 31);
+      int gt = above - sum + (warp + 1 < kViewWarps ? later : 0);
       const int bin = 4 * threadIdx.x;
       if (gt < k && gt + h.w >= k) s_pick[0] = bin + 3, s_pick[1] = gt, s_pick[2] = h.w;
       gt += h.w;

@@ -542,17 +542,22 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
   }
 }
 
-// ---- the share kernel: one warp per (layer, row) ---------------------------------------------------------
+// ---- the share kernel: one CTA of kShareWarps warps per (layer, row) ---------------------------------
 
 constexpr int kShareWarps = 4;
+constexpr int kShareThreads = kShareWarps * 32;
 constexpr int kShareBatch = 8;  // tiles whose cells a lane loads before it uses any
 
 // The block shares of layer L of row r (n blocks) from the cells of the row's tiles, into
-// share_layer[L][r][:n], and the number of query rows with data into contrib_layer[L][r]. Lane l
-// takes query row kl + 32 a (kl = l % lanes_q) of tiles rep, rep + reps, ... (rep = l / lanes_q),
-// lanes_q being the query rows rounded up to a power of two (at most 32).
-__device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, int n, float* w_lse, int* w_has) {
-  const int lane = threadIdx.x & 31;
+// share_layer[L][r][:n], and the number of query rows with data into contrib_layer[L][r]. Thread t
+// takes query row kl + 32 a (kl = t % lanes_q) of tiles rep, rep + reps, ... (rep = t / lanes_q,
+// reps = kShareThreads / lanes_q), lanes_q being the query rows rounded up to a power of two (at most
+// 32). The log totals are merged over a thread's tiles in order, over the replicas of a warp by
+// xor-shuffles (lse_merge is commutative: both partners hold the same result), then over the warps in
+// warp order: the same order on every launch.
+__device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, int n, float* s_lse, int* s_has,
+                                           float (*s_wm)[kMaxQ], float (*s_ws)[kMaxQ], int* s_count) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int Q = p.Q, TB = p.tile_blocks;
   const int n_tiles = (n + TB - 1) / TB;
   const size_t lr = (size_t)L * p.rows + r;
@@ -562,15 +567,13 @@ __device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, i
   int qp = 1;
   while (qp < Q) qp <<= 1;
   const int lanes_q = qp < 32 ? qp : 32;
-  const int reps = 32 / lanes_q;
-  const int kpl = qp > 32 ? qp / 32 : 1;  // query rows per lane (kMaxQ = 128: at most 4)
-  const int kl = lane % lanes_q, rep = lane / lanes_q;
+  const int reps = kShareThreads / lanes_q;
+  const int kpl = qp > 32 ? qp / 32 : 1;  // query rows per thread (kMaxQ = 128: at most 4)
+  const int kl = lane % lanes_q, rep = tid / lanes_q;
   const int steps = (n_tiles + reps - 1) / reps;
 
-  // 1. the log total of each query row: (max, sum) merged over the tiles in order, then over the
-  // replicas (lse_merge is commutative: both partners of a shuffle hold the same result)
+  // 1. the log total of each query row
   const float log_tb = logf((float)TB);
-  int has = 0;
   for (int a = 0; a < kpl; ++a) {
     const int k = kl + 32 * a;
     const bool active = k < Q;
@@ -593,20 +596,27 @@ __device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, i
       const float m2 = __shfl_xor_sync(kFullMask, M, off), s2 = __shfl_xor_sync(kFullMask, S, off);
       lse_merge(M, S, m2, s2);
     }
-    if (rep == 0 && active) {
-      const bool h = M > -INFINITY;
-      w_has[k] = h;
-      w_lse[k] = h ? M + logf(S) + log_tb : 0.f;  // log of the sum over blocks of exp(u), plus log(TB)
-      has += h;
-    }
+    if (lane < lanes_q && active) s_wm[warp][k] = M, s_ws[warp][k] = S;
   }
-  for (int off = 16; off > 0; off >>= 1) has += __shfl_xor_sync(kFullMask, has, off);
-  if (lane == 0) p.contrib_layer[lr] = has;
-  __syncwarp();
+  __syncthreads();
+  if (tid < Q) {  // over the warps, in warp order
+    float M = s_wm[0][tid], S = s_ws[0][tid];
+    for (int w = 1; w < kShareWarps; ++w) lse_merge(M, S, s_wm[w][tid], s_ws[w][tid]);
+    const bool h = M > -INFINITY;
+    s_has[tid] = h;
+    s_lse[tid] = h ? M + logf(S) + log_tb : 0.f;  // log of the sum over blocks of exp(u), plus log(TB)
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int has = 0;
+    for (int k = lane; k < Q; k += 32) has += s_has[k];
+    for (int off = 16; off > 0; off >>= 1) has += __shfl_xor_sync(kFullMask, has, off);
+    if (lane == 0) p.contrib_layer[lr] = has, *s_count = has;
+  }
 
   // 2. every tile's share, summed (mean) or maxed (max) over the query rows: exp(u - lse) =
-  // exp(m + log(l) - (M + log S)) = l * exp(m - lse); the blocks of a partial last tile get its weight back,
-  // exp(u + log(TB / tail) - lse) = exp(u - lse) * TB / tail
+  // exp(m + log(l) - (M + log S)) = l * exp(m - lse); the blocks of a partial last tile get its weight
+  // back, exp(u + log(TB / tail) - lse) = exp(u - lse) * TB / tail
   const bool agg_max = p.aggregate == EKV_AGG_MAX;
   const int tail = n % TB;
   float* sl = p.share_layer + lr * p.width;
@@ -616,8 +626,8 @@ __device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, i
     for (int u = 0; u < kShareBatch; ++u) e[u] = 0.f;
     for (int a = 0; a < kpl; ++a) {
       const int k = kl + 32 * a;
-      const bool active = k < Q && w_has[k < Q ? k : 0];
-      const float lse = active ? w_lse[k] : 0.f;
+      const bool active = k < Q && s_has[k < Q ? k : 0];
+      const float lse = active ? s_lse[k] : 0.f;
       float mv[kShareBatch], lv[kShareBatch];
 #pragma unroll
       for (int u = 0; u < kShareBatch; ++u) {
@@ -629,8 +639,7 @@ __device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, i
       }
 #pragma unroll
       for (int u = 0; u < kShareBatch; ++u) {
-        // exp(m + log(l) - lse) as l * exp(m - lse): no logarithm per cell; a cell without data (m = -inf,
-        // l = 0) or never written (NaN) fails the test and has no share
+        // a cell without data (m = -inf, l = 0) or never written (NaN) fails the test and has no share
         const float sh = (mv[u] > -INFINITY && lv[u] > 0.f) ? lv[u] * __expf(mv[u] - lse) : 0.f;
         e[u] = agg_max ? fmaxf(e[u], sh) : e[u] + sh;
       }
@@ -651,21 +660,22 @@ __device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, i
   }
 }
 
-// Grid: (layers [layer0, layer0 + n_layers)) x rows pairs, kShareWarps per CTA.
-__global__ void __launch_bounds__(kShareWarps * 32) share_kernel(const AuditParams p) {
-  __shared__ float s_lse[kShareWarps][kMaxQ];
-  __shared__ int s_has[kShareWarps][kMaxQ];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Grid: one CTA per (layer, row) pair of the layers [layer0, layer0 + n_layers).
+__global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams p) {
+  __shared__ float s_lse[kMaxQ];
+  __shared__ int s_has[kMaxQ];
+  __shared__ float s_wm[kShareWarps][kMaxQ], s_ws[kShareWarps][kMaxQ];
+  __shared__ int s_count;
   if (*p.flag == 0) return;  // nothing was recorded this step
-  const long long pair = (long long)blockIdx.x * kShareWarps + warp;
+  const long long pair = blockIdx.x;
   if (pair >= (long long)p.n_layers * p.rows) return;
   const int L = p.layer0 + (int)(pair / p.rows), r = (int)(pair % p.rows);
   const RowInfo ri = row_info(p, r, false);
   if (ri.n_chunks == 0) {  // the row records nothing: no contributors
-    if (lane == 0) p.contrib_layer[(size_t)L * p.rows + r] = 0;
+    if (threadIdx.x == 0) p.contrib_layer[(size_t)L * p.rows + r] = 0;
     return;
   }
-  share_task(p, L, r, ri.n_blocks, s_lse[warp], s_has[warp]);
+  share_task(p, L, r, ri.n_blocks, s_lse, s_has, s_wm, s_ws, &s_count);
 }
 
 // ---- the combine kernel: a row's layers into its final share --------------------------------------------
@@ -807,7 +817,7 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
   ps.layer0 = share0;
   ps.n_layers = share_layers;
   const long long pairs = (long long)share_layers * p.rows;
-  share_kernel<<<(unsigned)((pairs + kShareWarps - 1) / kShareWarps), kShareWarps * 32, 0, stream>>>(ps);
+  share_kernel<<<(unsigned)pairs, kShareThreads, 0, stream>>>(ps);
   rc = check_launch("share_kernel");
   if (rc != EKV_OK) return rc;
   combine_kernel<<<dim3(cdiv(p.width, kCombineThreads), p.rows), kCombineThreads, 0, stream>>>(ps);

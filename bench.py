@@ -466,6 +466,10 @@ def main() -> None:
     if dist_on:
         from datetime import timedelta
 
+        # NCCL's version banner goes to stdout, where the one JSON line goes: keep NCCL at warnings unless
+        # a more verbose level was asked for
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     import ekv.build
 

@@ -190,3 +190,27 @@ def test_device_share_source_reads_another_process_over_ipc(tmp_path, monkeypatc
     assert result.returncode == 0, result.stderr[-2000:]
     np.testing.assert_array_equal(np.load(out), expect)
     assert json.loads(result.stdout.strip().splitlines()[-1]) == layers
+
+
+@pytest.mark.parametrize("objective,width", [("sum", 16384), ("uniform", 16384), ("maxmin", 8192)])
+def test_float64_allocation_at_the_widest_rows(objective, width):
+    """The float64 paths at their width limits (a row of scores staged whole in shared memory: 16384
+    blocks for the view and `sum`, 8192 for `maxmin`), against the oracle."""
+    from ekv.observe.allocation import Request, allocate
+
+    rng = np.random.default_rng(width + len(objective))
+    sizes = [width, width - 3, 1, 2, width // 3, 700]
+    scores = []
+    for n in sizes:
+        x = np.repeat(rng.random((n + 3) // 4) ** 2, 4)[:n]
+        x[1::4] = np.nextafter(x[1::4], np.inf)  # adjacent doubles: shares that round together
+        scores.append(x)
+    weights = [1.0, 0.3, 2.0, 1.0, 1.0 / 3.0, 1.7] if objective == "sum" else [1.0] * len(sizes)
+    pinned = [oa.controller_pins(n, 4, n - 20) for n in sizes]
+    must = sum(int(p.sum()) for p in pinned)
+    for budget in (must, must + 5000, sum(sizes) - 7):
+        got = allocate([Request(scores=x, weight=w, pinned=p) for x, w, p in zip(scores, weights, pinned, strict=True)],
+                       budget, objective)
+        want = oa.allocate(scores, budget, objective, pinned, weights)
+        for r, (a, b) in enumerate(zip(got, want, strict=True)):
+            np.testing.assert_array_equal(a, b, err_msg=f"budget {budget}, request {r}")

@@ -305,13 +305,16 @@ int ekv_allocate_sum(const float* scores, int64_t score_stride, const double* we
  *
  * Row r's scores are scores[score_rows[r]][0..n) (score_rows may be NULL: row r), so a ledger of shares
  * per request (ekv_ledger_absorb) is read in place. The quotas are for ekv_view_build_f64 with
- * EKV_POLICY_SUM, the same weights and the same pins. width <= 16384. Same workspace as ekv_allocate_sum.
+ * EKV_POLICY_SUM, the same weights and the same pins. mask_out (may be NULL; uint8 [rows][mask_stride])
+ * receives the committed mask straight from the threshold -- the pins, the blocks past a request and
+ * every row that is not a request kept -- with no view launch: the mask ekv_view_build_f64 would write.
+ * width <= 16384. Same workspace as ekv_allocate_sum.
  */
 int ekv_allocate_sum_f64(const double* scores, int64_t score_stride, const int32_t* score_rows,
                          const double* weights, const int32_t* row_blocks, const int32_t* measured_blocks,
                          int recent_blocks, int cap_above_blocks, double budget_fraction, int64_t budget,
-                         int rows, int width, int32_t* quota, void* workspace, size_t workspace_bytes,
-                         void* stream);
+                         int rows, int width, int32_t* quota, uint8_t* mask_out, int64_t mask_stride,
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * ekv_allocate_maxmin_f64 -- ekv_allocate_maxmin over float64 scores; score_rows as in

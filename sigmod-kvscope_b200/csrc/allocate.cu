@@ -63,6 +63,8 @@ struct SumParams {
   long long budget;
   int rows, width;
   int32_t* quota;
+  uint8_t* mask_out;  // may be NULL: the committed mask [rows][mask_s0], written straight from the threshold
+  int64_t mask_s0;
   // workspace
   SumState* state;
   unsigned int* hist;        // [kSumBins]
@@ -448,8 +450,45 @@ __global__ void __launch_bounds__(1024) sum_quota_kernel(const SumParams p) {
       const int ps = p.row_ps[r];
       p.quota[r] = mode == kSumAll ? (ps > 1 ? ps - 1 : 0) : 0;
     } else {
-      p.quota[r] = p.row_above[r] + p.row_kept[r] + (at && before < m ? 1 : 0);
+      const int take = at && before < m ? 1 : 0;
+      p.quota[r] = p.row_above[r] + p.row_kept[r] + take;
+      p.row_at[r] = take;  // from here on: the row's tie at i* is taken (sum_mask_kernel)
     }
+  }
+}
+
+// The committed mask straight from the threshold, without ranking any row: block b of request r is
+// kept when it is pinned (block 0 and [ps, n)), past the request, or unpinned with a gain key above the
+// threshold, or equal to it at an index above i*, or at i* when the row's tie there is taken. Grid
+// (width / kSumMaskSpan, rows); four positions per thread.
+constexpr int kSumMaskSpan = 4 * kSumThreads;
+__global__ void __launch_bounds__(kSumThreads) sum_mask_kernel(const SumParams p) {
+  const int r = blockIdx.y;
+  const SumState* st = p.state;
+  const int mode = st->mode;
+  const unsigned long long prefix = st->prefix, mask = st->mask;
+  const int istar = st->istar;
+  const int n = p.row_n[r], ps = p.row_ps[r];
+  const bool take = p.row_at[r] != 0;
+  const unsigned long long* kr = p.keys + (int64_t)r * p.width;
+  uint8_t* out = p.mask_out + (int64_t)r * p.mask_s0;
+  const int b0 = blockIdx.x * kSumMaskSpan + 4 * threadIdx.x;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int b = b0 + j;
+    if (b >= p.width) break;
+    bool keep = true;  // not a request, a pin, or past the request
+    if (n > 0 && b >= 1 && b < ps) {
+      if (mode == kSumAll) {
+        keep = true;
+      } else if (mode == kSumNone) {
+        keep = false;
+      } else {
+        const unsigned long long km = kr[b] & mask;
+        keep = km > prefix || (km == prefix && (b > istar || (b == istar && take)));
+      }
+    }
+    out[b] = keep ? 1 : 0;
   }
 }
 
@@ -466,7 +505,8 @@ template <typename S>
 static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* score_rows, const double* weights,
                         const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,
                         int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
-                        int32_t* quota, void* workspace, size_t workspace_bytes, void* stream) {
+                        int32_t* quota, uint8_t* mask_out, int64_t mask_stride, void* workspace,
+                        size_t workspace_bytes, void* stream) {
   constexpr int max_width = sizeof(S) == 8 ? kSumMaxWidth / 2 : kSumMaxWidth;  // the prep kernel stages a row
   clear_error();
   if (!scores || !row_blocks || !quota) return fail(EKV_EINVAL, "a required pointer is NULL");
@@ -474,6 +514,7 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
   if (width > max_width) return fail(EKV_ENOTSUP, "width %d > %d", width, max_width);
   if (rows > kSumMaxRows) return fail(EKV_ENOTSUP, "rows %d > %d", rows, kSumMaxRows);
   if (score_stride < width) return fail(EKV_EINVAL, "score_stride %lld < width %d", (long long)score_stride, width);
+  if (mask_out && mask_stride < width) return fail(EKV_EINVAL, "mask_stride %lld < width %d", (long long)mask_stride, width);
   if (recent_blocks < -1 || cap_above_blocks < -1) return fail(EKV_EINVAL, "invalid controller settings");
   if (budget < 0 && !(budget_fraction > 0.0 && budget_fraction <= 1.0))
     return fail(EKV_EINVAL, "the budget fraction must be in (0, 1]");
@@ -486,6 +527,7 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
   p.scores = scores; p.score_s0 = score_stride; p.score_rows = score_rows; p.weights = weights; p.row_blocks = row_blocks;
   p.measured = measured_blocks; p.recent = recent_blocks; p.cap = cap_above_blocks;
   p.fraction = budget_fraction; p.budget = (long long)budget; p.rows = rows; p.width = width; p.quota = quota;
+  p.mask_out = mask_out; p.mask_s0 = mask_stride;
   p.state = reinterpret_cast<SumState*>(base + l.state);
   p.hist = reinterpret_cast<unsigned int*>(base + l.hist);
   p.ties = reinterpret_cast<unsigned int*>(base + l.ties);
@@ -530,7 +572,9 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
   sum_kept_kernel<<<cand_grid, kSumThreads, 0, s>>>(p);
   if ((rc = check_launch("sum_kept_kernel")) != EKV_OK) return rc;
   sum_quota_kernel<<<1, 1024, 0, s>>>(p);
-  return check_launch("sum_quota_kernel");
+  if ((rc = check_launch("sum_quota_kernel")) != EKV_OK || mask_out == nullptr) return rc;
+  sum_mask_kernel<<<dim3(cdiv(width, kSumMaskSpan), rows), kSumThreads, 0, s>>>(p);
+  return check_launch("sum_mask_kernel");
 }
 
 extern "C" int ekv_allocate_sum(const float* scores, int64_t score_stride, const double* weights,
@@ -538,16 +582,16 @@ extern "C" int ekv_allocate_sum(const float* scores, int64_t score_stride, const
                                 int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
                                 int32_t* quota, void* workspace, size_t workspace_bytes, void* stream) {
   return allocate_sum<float>(scores, score_stride, nullptr, weights, row_blocks, measured_blocks, recent_blocks,
-                             cap_above_blocks, budget_fraction, budget, rows, width, quota, workspace,
+                             cap_above_blocks, budget_fraction, budget, rows, width, quota, nullptr, 0, workspace,
                              workspace_bytes, stream);
 }
 
 extern "C" int ekv_allocate_sum_f64(const double* scores, int64_t score_stride, const int32_t* score_rows,
                                     const double* weights, const int32_t* row_blocks, const int32_t* measured_blocks,
                                     int recent_blocks, int cap_above_blocks, double budget_fraction, int64_t budget,
-                                    int rows, int width, int32_t* quota, void* workspace, size_t workspace_bytes,
-                                    void* stream) {
+                                    int rows, int width, int32_t* quota, uint8_t* mask_out, int64_t mask_stride,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
   return allocate_sum<double>(scores, score_stride, score_rows, weights, row_blocks, measured_blocks,
                               recent_blocks, cap_above_blocks, budget_fraction, budget, rows, width, quota,
-                              workspace, workspace_bytes, stream);
+                              mask_out, mask_stride, workspace, workspace_bytes, stream);
 }

@@ -83,7 +83,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                 _p, _p, _p]),
     "ekv_allocate_sum": (_i32, [_p, _i64, _p, _p, _p, _i32, _i32, _f64, _i64, _i32, _i32, _p, _p, ctypes.c_size_t, _p]),
     "ekv_allocate_sum_f64": (
-        _i32, [_p, _i64, _p, _p, _p, _p, _i32, _i32, _f64, _i64, _i32, _i32, _p, _p, ctypes.c_size_t, _p],
+        _i32, [_p, _i64, _p, _p, _p, _p, _i32, _i32, _f64, _i64, _i32, _i32, _p, _p, _i64, _p, ctypes.c_size_t, _p],
     ),
     "ekv_allocate_maxmin_f64": (
         _i32, [_p, _i64, _p, _p, _p, _i32, _i32, _f64, _i64, _i32, _i32, _p, _p, ctypes.c_size_t, _p],

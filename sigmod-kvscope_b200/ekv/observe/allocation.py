@@ -99,13 +99,15 @@ def sum_quotas(
     budget_fraction: float = 0.0,
     weights: torch.Tensor | None = None,
     score_rows: torch.Tensor | None = None,
+    mask_out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """The per-row quotas of the ``sum`` objective with one shared budget (``ekv_allocate_sum``).
 
     ``scores`` float32 or float64 [., width] on the device, ``row_blocks`` int32 [rows], ``quota`` int32
     [rows] (out), ``weights`` float64 [rows] or None; ``score_rows`` (int32 [rows], float64 scores only)
-    reads row r's scores from row ``score_rows[r]``. ``budget`` >= 0 as given, else from
-    ``budget_fraction`` as the controller computes it. No host synchronisation.
+    reads row r's scores from row ``score_rows[r]``; ``mask_out`` (uint8 [rows, width], float64 scores
+    only) receives the committed keep mask straight from the threshold. ``budget`` >= 0 as given, else
+    from ``budget_fraction`` as the controller computes it. No host synchronisation.
     """
     rows, width = _score_layout(scores, row_blocks, score_rows)
     lib = _lib.load()
@@ -119,9 +121,12 @@ def sum_quotas(
     )
     if scores.dtype == torch.float64:
         rows_ptr = None if score_rows is None else score_rows.data_ptr()
-        rc = lib.ekv_allocate_sum_f64(scores.data_ptr(), scores.stride(0), rows_ptr, *common)
+        mask = (None, 0) if mask_out is None else (mask_out.data_ptr(), mask_out.stride(0))
+        rc = lib.ekv_allocate_sum_f64(scores.data_ptr(), scores.stride(0), rows_ptr, *common[:10], *mask, *common[10:])
         _lib.check(rc, "ekv_allocate_sum_f64")
     else:
+        if mask_out is not None:
+            raise ValueError("the mask straight from the threshold is written for float64 scores")
         rc = lib.ekv_allocate_sum(scores.data_ptr(), scores.stride(0), *common)
         _lib.check(rc, "ekv_allocate_sum")
     return quota
@@ -197,7 +202,6 @@ def allocate(requests: Sequence[Request], budget: int, objective: Objective = "s
     measured = pin_starts.to(device)
     quota = torch.empty(rows, dtype=torch.int32, device=device)
     scores_t = torch.from_numpy(scores).to(device)
-    weights = None
     if objective == "uniform":
         rc = lib.ekv_allocate_quotas(row_blocks.data_ptr(), measured.data_ptr(), -1, -1, 0.0, int(budget), None,
                                      _lib.POLICY_UNIFORM, rows, width, quota.data_ptr(), stream)
@@ -205,16 +209,17 @@ def allocate(requests: Sequence[Request], budget: int, objective: Objective = "s
     elif objective == "maxmin":
         maxmin_quotas(scores_t, row_blocks, quota, measured=measured, recent_blocks=-1, cap_above_blocks=-1,
                       budget=int(budget))
-    else:
+    mask = torch.empty(rows, width, dtype=torch.uint8, device=device)
+    if objective == "sum":  # the mask straight from the global threshold
         weights = torch.tensor([float(r.weight) for r in requests], dtype=torch.float64).to(device)
         sum_quotas(scores_t, row_blocks, quota, measured=measured, recent_blocks=-1, cap_above_blocks=-1,
-                   budget=int(budget), weights=weights)
-    mask = torch.empty(rows, width, dtype=torch.uint8, device=device)
-    rc = lib.ekv_view_build_f64(
-        None, 0, None, row_blocks.data_ptr(), quota.data_ptr(), measured.data_ptr(), -1, scores_t.data_ptr(),
-        width, None, None if weights is None else weights.data_ptr(), _POLICIES[objective], None, None, 0, rows,
-        width, 16, None, 0, None, mask.data_ptr(), width, stream,
-    )
-    _lib.check(rc, "ekv_view_build_f64")
+                   budget=int(budget), weights=weights, mask_out=mask)
+    else:
+        rc = lib.ekv_view_build_f64(
+            None, 0, None, row_blocks.data_ptr(), quota.data_ptr(), measured.data_ptr(), -1, scores_t.data_ptr(),
+            width, None, None, _POLICIES[objective], None, None, 0, rows, width, 16, None, 0, None,
+            mask.data_ptr(), width, stream,
+        )
+        _lib.check(rc, "ekv_view_build_f64")
     out = mask.cpu().numpy().astype(bool)
     return [out[r, : sizes[r]].copy() for r in range(rows)]

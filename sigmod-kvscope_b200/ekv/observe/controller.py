@@ -340,12 +340,13 @@ class ShareLedger:
         stream = _lib.current_stream()
         rb_t, ms_t, sr_t, w_t = self._to_device(row_blocks, measured, score_rows, weights)
         quota = torch.empty(rows, dtype=torch.int32, device=dev)
-        if objective == "sum":
+        mask = torch.empty(rows, W, dtype=torch.uint8, device=dev)
+        if objective == "sum":  # the mask comes straight from the global threshold: no ranking per row
             sum_quotas(self.table, rb_t, quota, measured=ms_t, recent_blocks=recent_blocks,
                        cap_above_blocks=cap_above_blocks, budget_fraction=budget_fraction, weights=w_t,
-                       score_rows=sr_t)
-            policy = _lib.POLICY_SUM
-        elif objective == "maxmin":
+                       score_rows=sr_t, mask_out=mask)
+            return mask
+        if objective == "maxmin":
             maxmin_quotas(self.table, rb_t, quota, measured=ms_t, recent_blocks=recent_blocks,
                           cap_above_blocks=cap_above_blocks, budget_fraction=budget_fraction, score_rows=sr_t)
             policy = _lib.POLICY_UNIFORM
@@ -355,12 +356,10 @@ class ShareLedger:
                                          quota.data_ptr(), stream)
             _lib.check(rc, "ekv_allocate_quotas")
             policy = _lib.POLICY_UNIFORM
-        mask = torch.empty(rows, W, dtype=torch.uint8, device=dev)
         rc = lib.ekv_view_build_f64(
             None, 0, None, rb_t.data_ptr(), quota.data_ptr(), ms_t.data_ptr(), int(recent_blocks),
-            self.table.data_ptr(), self.table.stride(0), sr_t.data_ptr(),
-            w_t.data_ptr() if objective == "sum" else None, policy, None, None, 0, rows, W, 16, None, 0, None,
-            mask.data_ptr(), W, stream,
+            self.table.data_ptr(), self.table.stride(0), sr_t.data_ptr(), None, policy, None, None, 0, rows, W, 16,
+            None, 0, None, mask.data_ptr(), W, stream,
         )
         _lib.check(rc, "ekv_view_build_f64")
         return mask

@@ -141,10 +141,12 @@ def test_other_entry_points_validate_before_launching(lib):
     mm_args[11], mm_args[12], mm_args[9] = ctypes.c_void_p(0x1000), 1 << 30, 9000
     assert lib.ekv_allocate_maxmin(*mm_args) == L.ENOTSUP  # wider than 8192
     # the float64 entry points
-    sum64 = [fake, 8, None, None, fake, None, 4, 0, 0.5, -1, 2, 8, fake, ctypes.c_void_p(0x1000), ws, None]
+    sum64 = [fake, 8, None, None, fake, None, 4, 0, 0.5, -1, 2, 8, fake, None, 0, ctypes.c_void_p(0x1000), ws, None]
     sum64[11] = 20000
     assert lib.ekv_allocate_sum_f64(*sum64) == L.ENOTSUP  # a float64 row is staged whole: wider than 16384
-    sum64[11], sum64[13] = 8, None
+    sum64[11], sum64[13], sum64[14] = 8, fake, 4
+    assert lib.ekv_allocate_sum_f64(*sum64) == L.EINVAL  # mask stride below the width
+    sum64[13], sum64[14], sum64[15] = None, 0, None
     assert lib.ekv_allocate_sum_f64(*sum64) == L.ERANGE  # no workspace
     mm64 = [fake, 4, None, fake, None, 4, 0, 0.5, -1, 2, 8, fake, ctypes.c_void_p(0x1000), 1 << 30, None]
     assert lib.ekv_allocate_maxmin_f64(*mm64) == L.EINVAL  # score stride below the width

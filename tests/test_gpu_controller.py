@@ -140,6 +140,15 @@ def test_float64_views_at_scale_match_the_oracle(objective):
     for r, m in zip(chosen, masks, strict=True):
         keep[r, : len(m)] = m
     np.testing.assert_array_equal(mask.cpu().numpy(), keep)
+    if objective == "sum":  # the same mask straight from the global threshold, with no view launch
+        from ekv.observe.allocation import sum_quotas
+
+        direct = torch.empty(rows, width, dtype=torch.uint8, device="cuda")
+        quota = torch.empty(rows, dtype=torch.int32, device="cuda")
+        sc, rb, ms, wt = (torch.from_numpy(x).cuda() for x in (scores, blocks, measured, weights))
+        sum_quotas(sc, rb, quota, measured=ms, recent_blocks=recent, cap_above_blocks=cap, budget_fraction=fraction,
+                   weights=wt, mask_out=direct)
+        np.testing.assert_array_equal(direct.cpu().numpy(), keep)
     ref_view, ref_lens = ov.compact_block_table(table, seq, keep.astype(bool), 16)
     np.testing.assert_array_equal(view.cpu().numpy(), ref_view)
     np.testing.assert_array_equal(view_lens.cpu().numpy(), ref_lens)

@@ -158,8 +158,10 @@ def controller_keep(
     recent_blocks: int = 4,
     cap_above_blocks: int = 0,
     measured: np.ndarray | None = None,
+    weights: np.ndarray | None = None,
 ) -> np.ndarray:
-    """The keep mask uint8 [rows, width] the controller commits; ``scores_of(row, n)`` gives a row's scores."""
+    """The keep mask uint8 [rows, width] the controller commits; ``scores_of(row, n)`` gives a row's scores,
+    ``weights[row]`` its request weight (None: 1.0)."""
     rows = len(row_blocks)
     keep = np.ones((rows, width), dtype=np.uint8)
     chosen = [r for r in range(rows) if int(row_blocks[r]) > cap_above_blocks and int(row_blocks[r]) > 0]
@@ -173,7 +175,8 @@ def controller_keep(
     total = sum(len(s) for s in score_list)
     floor = sum(int(p.sum()) for p in pinned_list)
     budget = max(floor, int(math.ceil(budget_fraction * total)))
-    for r, mask in zip(chosen, allocate(score_list, budget, objective, pinned_list), strict=True):
+    w = None if weights is None else [float(weights[r]) for r in chosen]
+    for r, mask in zip(chosen, allocate(score_list, budget, objective, pinned_list, w), strict=True):
         keep[r, : len(mask)] = mask
     return keep
 

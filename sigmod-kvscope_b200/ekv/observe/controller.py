@@ -12,8 +12,9 @@ mask of every row with ``allocate`` (Controller._allocate, :398-451). Here the d
 * ``ShareLedger`` holds one float64 row per request (the reference's ``shares`` dict) and folds a new
   audit into it with ``ekv_ledger_absorb``: same evidence rule, same NaN handling, same rounding.
 * ``ShareLedger.keep_mask`` computes the mask Controller._allocate commits, from the ledger in place
-  (``ekv_allocate_sum_f64`` / ``ekv_allocate_quotas`` / ``ekv_allocate_maxmin_f64`` and
-  ``ekv_view_build_f64``), bit-exact with the reference for the same shares.
+  (``ekv_allocate_sum_f64`` with the mask straight from its threshold, or ``ekv_allocate_quotas`` /
+  ``ekv_allocate_maxmin_f64`` and ``ekv_view_build_f64``), bit-exact with the reference for the same
+  shares; ``fixed_keep_mask`` does the same for a controller with a fixed scoring rule.
 
 Only the request-key bookkeeping (which ledger row holds which request, which blocks the last audit
 measured) stays on the host, as small dicts; the one host synchronisation per absorbed audit reads one
@@ -135,6 +136,102 @@ class DeviceShareSource:
         return out
 
 
+def _to_device(device: torch.device, *arrays: np.ndarray) -> list[torch.Tensor]:
+    """The arrays on the device through one pinned buffer and one asynchronous copy (8-byte aligned)."""
+    offsets, total = [], 0
+    for a in arrays:
+        offsets.append(total)
+        total += (a.nbytes + 7) // 8 * 8
+    host = torch.empty(max(total, 8), dtype=torch.uint8, pin_memory=True)
+    view = host.numpy()
+    for a, o in zip(arrays, offsets, strict=True):
+        view[o : o + a.nbytes] = np.ascontiguousarray(a).view(np.uint8).reshape(-1)
+    dev = host.to(device, non_blocking=True)
+    return [dev[o : o + a.nbytes].view(_TORCH_DTYPES[a.dtype]) for a, o in zip(arrays, offsets, strict=True)]
+
+
+def _check_weights(objective: str, weights: np.ndarray) -> None:
+    if objective not in ("sum", "maxmin", "uniform"):
+        raise ValueError(f"unknown objective {objective!r}")
+    if objective != "sum" and np.any(weights != 1.0):
+        raise ValueError(f"the {objective} objective does not use request weights")
+    if objective == "sum" and (np.any(weights < 0.0) or not np.all(np.isfinite(weights))):
+        raise RuntimeError("negative or non-finite request weights are not supported on the device")
+
+
+def _committed_mask(scores: torch.Tensor, score_rows: torch.Tensor | None, row_blocks: torch.Tensor,
+                    measured: torch.Tensor | None, weights: torch.Tensor, objective: str, budget_fraction: float,
+                    recent_blocks: int, cap_above_blocks: int) -> torch.Tensor:
+    """The keep mask uint8 [rows, width] of one budget over the rows' float64 scores (Controller._allocate)."""
+    rows, width = int(row_blocks.shape[0]), int(scores.shape[1])
+    dev = scores.device
+    quota = torch.empty(rows, dtype=torch.int32, device=dev)
+    mask = torch.empty(rows, width, dtype=torch.uint8, device=dev)
+    if objective == "sum":  # the mask comes straight from the global threshold: no ranking per row
+        sum_quotas(scores, row_blocks, quota, measured=measured, recent_blocks=recent_blocks,
+                   cap_above_blocks=cap_above_blocks, budget_fraction=budget_fraction, weights=weights,
+                   score_rows=score_rows, mask_out=mask)
+        return mask
+    lib = _lib.load()
+    stream = _lib.current_stream()
+    if objective == "maxmin":
+        maxmin_quotas(scores, row_blocks, quota, measured=measured, recent_blocks=recent_blocks,
+                      cap_above_blocks=cap_above_blocks, budget_fraction=budget_fraction, score_rows=score_rows)
+    else:
+        rc = lib.ekv_allocate_quotas(row_blocks.data_ptr(), None if measured is None else measured.data_ptr(),
+                                     int(recent_blocks), int(cap_above_blocks), float(budget_fraction), -1, None,
+                                     _lib.POLICY_UNIFORM, rows, width, quota.data_ptr(), stream)
+        _lib.check(rc, "ekv_allocate_quotas")
+    rc = lib.ekv_view_build_f64(
+        None, 0, None, row_blocks.data_ptr(), quota.data_ptr(), None if measured is None else measured.data_ptr(),
+        int(recent_blocks), scores.data_ptr(), scores.stride(0), None if score_rows is None else score_rows.data_ptr(),
+        None, _lib.POLICY_UNIFORM, None, None, 0, rows, width, 16, None, 0, None, mask.data_ptr(), width, stream,
+    )
+    _lib.check(rc, "ekv_view_build_f64")
+    return mask
+
+
+def fixed_keep_mask(
+    keys: np.ndarray,
+    lengths: np.ndarray,
+    scores_of: Callable[[int], np.ndarray],
+    *,
+    width: int,
+    budget_fraction: float,
+    objective: Objective = "sum",
+    recent_blocks: int = 4,
+    cap_above_blocks: int = 0,
+    weight: Callable[[int], float] | None = None,
+    device=None,
+) -> torch.Tensor:
+    """The keep mask uint8 [rows, width] of a controller with a fixed scoring rule instead of measured
+    shares (observe/controller.py:148-160, :411-417): every row longer than ``cap_above_blocks`` with a
+    request is one request of ``scores_of(n)`` scores (n = min(length, width)), pinned at block 0 and its
+    newest ``recent_blocks`` + 1 blocks, under one budget max(pins, ceil(budget_fraction * blocks))."""
+    if not 0.0 < budget_fraction <= 1.0:
+        raise ValueError("the budget fraction must be in (0, 1]")
+    keys = np.asarray(keys, dtype=np.uint64)
+    lengths = np.asarray(lengths).astype(np.int64)
+    rows = len(keys)
+    chosen = (lengths > cap_above_blocks) & (keys != 0)
+    scores = np.zeros((rows, width), dtype=np.float64)
+    weights = np.ones(rows, dtype=np.float64)
+    for r in np.flatnonzero(chosen).tolist():
+        n = int(min(lengths[r], width))
+        x = np.asarray(scores_of(n), dtype=np.float64)
+        if x.shape != (n,):
+            raise ValueError(f"the scoring rule gave {x.shape} scores for {n} blocks")
+        scores[r, :n] = np.where(np.isnan(x), 0.0, x)
+        if weight is not None:
+            weights[r] = float(weight(int(keys[r])))
+    _check_weights(objective, weights)
+    row_blocks = np.where(chosen, np.minimum(lengths, 2**31 - 1), 0).astype(np.int32)
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    sc_t, rb_t, w_t = _to_device(dev, scores, row_blocks, weights)
+    return _committed_mask(sc_t.view(rows, width), None, rb_t, None, w_t, objective, budget_fraction,
+                           recent_blocks, cap_above_blocks)
+
+
 class _MeasuredView(Mapping):
     """request key -> blocks its latest audit covered (the reference's ``measured`` dict), read-only."""
 
@@ -203,19 +300,6 @@ class ShareLedger:
         at = np.minimum(np.searchsorted(sorted_keys, keys), sorted_keys.size - 1)
         return np.where((sorted_keys[at] == keys) & (keys != 0), rows[at], -1).astype(np.int32)
 
-    def _to_device(self, *arrays: np.ndarray) -> list[torch.Tensor]:
-        """The arrays on the device through one pinned buffer and one asynchronous copy (8-byte aligned)."""
-        offsets, total = [], 0
-        for a in arrays:
-            offsets.append(total)
-            total += (a.nbytes + 7) // 8 * 8
-        host = torch.empty(max(total, 8), dtype=torch.uint8, pin_memory=True)
-        view = host.numpy()
-        for a, o in zip(arrays, offsets, strict=True):
-            view[o : o + a.nbytes] = np.ascontiguousarray(a).view(np.uint8).reshape(-1)
-        dev = host.to(self.device, non_blocking=True)
-        return [dev[o : o + a.nbytes].view(_TORCH_DTYPES[a.dtype]) for a, o in zip(arrays, offsets, strict=True)]
-
     def __contains__(self, key: int) -> bool:
         return int(key) in self.slots
 
@@ -275,7 +359,7 @@ class ShareLedger:
         new = rows[slot[rows] < 0]
         if new.size:
             slot[new] = self._take_slots(new.size)
-        slot_t, blend_t = self._to_device(slot, blend)
+        slot_t, blend_t = _to_device(self.device, slot, blend)
         evidence = torch.empty(live, dtype=torch.uint8, device=self.device)
         rc = _lib.load().ekv_ledger_absorb(
             fresh.data_ptr(), int(fresh.dtype == torch.float64), fresh.stride(0), slot_t.data_ptr(),
@@ -320,7 +404,6 @@ class ShareLedger:
         keys = np.asarray(keys, dtype=np.uint64)
         lengths = np.asarray(lengths).astype(np.int64)
         rows = len(keys)
-        W = self.width
         slot = self._slot_of(keys)
         chosen = (lengths > cap_above_blocks) & (keys != 0) & (slot >= 0)
         big = 2**31 - 1
@@ -331,35 +414,7 @@ class ShareLedger:
         if weight is not None:
             picked = np.flatnonzero(chosen)
             weights[picked] = [float(weight(k)) for k in keys[picked].tolist()]
-        if objective != "sum" and np.any(weights != 1.0):
-            raise ValueError(f"the {objective} objective does not use request weights")
-        if objective == "sum" and (np.any(weights < 0.0) or not np.all(np.isfinite(weights))):
-            raise RuntimeError("negative or non-finite request weights are not supported on the device")
-        dev = self.device
-        lib = _lib.load()
-        stream = _lib.current_stream()
-        rb_t, ms_t, sr_t, w_t = self._to_device(row_blocks, measured, score_rows, weights)
-        quota = torch.empty(rows, dtype=torch.int32, device=dev)
-        mask = torch.empty(rows, W, dtype=torch.uint8, device=dev)
-        if objective == "sum":  # the mask comes straight from the global threshold: no ranking per row
-            sum_quotas(self.table, rb_t, quota, measured=ms_t, recent_blocks=recent_blocks,
-                       cap_above_blocks=cap_above_blocks, budget_fraction=budget_fraction, weights=w_t,
-                       score_rows=sr_t, mask_out=mask)
-            return mask
-        if objective == "maxmin":
-            maxmin_quotas(self.table, rb_t, quota, measured=ms_t, recent_blocks=recent_blocks,
-                          cap_above_blocks=cap_above_blocks, budget_fraction=budget_fraction, score_rows=sr_t)
-            policy = _lib.POLICY_UNIFORM
-        else:
-            rc = lib.ekv_allocate_quotas(rb_t.data_ptr(), ms_t.data_ptr(), int(recent_blocks), int(cap_above_blocks),
-                                         float(budget_fraction), -1, None, _lib.POLICY_UNIFORM, rows, W,
-                                         quota.data_ptr(), stream)
-            _lib.check(rc, "ekv_allocate_quotas")
-            policy = _lib.POLICY_UNIFORM
-        rc = lib.ekv_view_build_f64(
-            None, 0, None, rb_t.data_ptr(), quota.data_ptr(), ms_t.data_ptr(), int(recent_blocks),
-            self.table.data_ptr(), self.table.stride(0), sr_t.data_ptr(), None, policy, None, None, 0, rows, W, 16,
-            None, 0, None, mask.data_ptr(), W, stream,
-        )
-        _lib.check(rc, "ekv_view_build_f64")
-        return mask
+        _check_weights(objective, weights)
+        rb_t, ms_t, sr_t, w_t = _to_device(self.device, row_blocks, measured, score_rows, weights)
+        return _committed_mask(self.table, sr_t, rb_t, ms_t, w_t, objective, budget_fraction, recent_blocks,
+                               cap_above_blocks)

@@ -468,6 +468,16 @@ def controller_cases():
             cases[f"share_keys{c}_{step}"] = np.array(ks, dtype=np.uint64)
             cases[f"shares{c}_{step}"] = np.array([controller.shares[k] for k in ks]).reshape(len(ks), width)
             cases[f"measured{c}_{step}"] = np.array([controller.measured[k] for k in ks], dtype=np.int64)
+    # a controller with a fixed scoring rule instead of measured shares (observe/controller.py:148-160,
+    # :411-417): float64 scores no float32 holds, weights, recent pins and a length cap
+    def fixed(n):
+        return np.sin(np.arange(n) * 0.37) + 1.0
+
+    settings = Settings(budget_fraction=0.35, objective="sum", recent_blocks=2, cap_above_blocks=4)
+    fixed_ctl = Controller(_Writer(rows, width), None, settings, weight=weight, scores=fixed)
+    for step in range(steps):
+        keep, _release = fixed_ctl._allocate(cases[f"keys{step}"], cases[f"lengths{step}"])
+        cases[f"fixed_keep{step}"] = keep
     np.savez_compressed(os.path.join(HERE, "controller_cases.npz"), **cases)
     print("controller_cases written")
 

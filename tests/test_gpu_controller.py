@@ -223,3 +223,29 @@ def test_float64_allocation_at_the_widest_rows(objective, width):
         want = oa.allocate(scores, budget, objective, pinned, weights)
         for r, (a, b) in enumerate(zip(got, want, strict=True)):
             np.testing.assert_array_equal(a, b, err_msg=f"budget {budget}, request {r}")
+
+
+def test_fixed_scoring_rule_follows_the_reference_controller():
+    """A controller with a fixed scoring rule (float64 scores no float32 holds, weights, recent pins, a
+    length cap), step after step, against the reference Controller; and the other objectives against the
+    oracle."""
+    from ekv.observe.controller import fixed_keep_mask
+
+    g = load_golden("controller_cases")
+    width = int(g["width"])
+
+    def rule(n):
+        return np.sin(np.arange(n) * 0.37) + 1.0
+
+    for step in range(int(g["steps"])):
+        keys, lengths = g[f"keys{step}"], g[f"lengths{step}"]
+        keep = fixed_keep_mask(keys, lengths, rule, width=width, budget_fraction=0.35, objective="sum",
+                               recent_blocks=2, cap_above_blocks=4, weight=controller_weight)
+        np.testing.assert_array_equal(keep.cpu().numpy(), g[f"fixed_keep{step}"], err_msg=f"step {step}")
+        row_blocks = np.where(keys != 0, lengths, 0)
+        for objective in ("maxmin", "uniform"):
+            keep = fixed_keep_mask(keys, lengths, rule, width=width, budget_fraction=0.35, objective=objective,
+                                   recent_blocks=2, cap_above_blocks=4)
+            want = oa.controller_keep(row_blocks, width, lambda r, n: rule(n), 0.35, objective, recent_blocks=2,
+                                      cap_above_blocks=4)
+            np.testing.assert_array_equal(keep.cpu().numpy(), want, err_msg=f"step {step} {objective}")

@@ -261,3 +261,17 @@ def test_oracle_controller_matches_the_reference_sequence():
             np.testing.assert_array_equal(got, g[f"shares{c}_{step}"], err_msg=f"setup {c} step {step}")
             np.testing.assert_array_equal([ledger.measured[k] for k in ks], g[f"measured{c}_{step}"])
             np.testing.assert_array_equal(keep, g[f"keep{c}_{step}"], err_msg=f"setup {c} step {step}")
+
+
+def test_oracle_fixed_scoring_controller_matches_the_reference():
+    """A controller with a fixed scoring rule (no measured shares): every row longer than the cap is a
+    request of fixed(n) scores with the recent pins, weighted, under one budget."""
+    g = load_golden("controller_cases")
+    width = int(g["width"])
+    for step in range(int(g["steps"])):
+        keys, lengths = g[f"keys{step}"], g[f"lengths{step}"]
+        row_blocks = np.where(keys != 0, lengths, 0)
+        weights = np.array([controller_weight(k) for k in keys])
+        keep = oa.controller_keep(row_blocks, width, lambda r, n: np.sin(np.arange(n) * 0.37) + 1.0, 0.35, "sum",
+                                  recent_blocks=2, cap_above_blocks=4, weights=weights)
+        np.testing.assert_array_equal(keep, g[f"fixed_keep{step}"], err_msg=f"step {step}")

@@ -184,6 +184,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
   __shared__ long long s_queue[kWarps][kItemQueue];  // each warp's items in the order it took them
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  chain_wait();  // the query stash, the tensor maps and the item counter come from the launches before
   if (*p.flag == 0) return;  // the statistic is off: nothing is recorded (:64)
 
   // ---- the rows of the step and the items -----------------------------------------------------
@@ -725,6 +726,8 @@ __global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams 
   __shared__ int s_has[kMaxQ];
   __shared__ float s_wm[kShareWarps][kMaxQ], s_ws[kShareWarps][kMaxQ];
   __shared__ int s_count;
+  chain_release();
+  chain_wait();  // the record kernel's cells
   if (*p.flag == 0) return;  // nothing was recorded this step
   const long long pair = blockIdx.x;
   if (pair >= (long long)p.n_layers * p.rows) return;
@@ -749,6 +752,8 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditPar
   __shared__ float s_red[kCombineThreads / 32];
   __shared__ int s_last;
   const int r = blockIdx.y, tid = threadIdx.x;
+  chain_release();
+  chain_wait();  // the share kernel's layer shares
   if (*p.flag == 0) return;  // nothing was recorded this step
   const RowInfo ri = row_info(p, r, false);
   float* out = p.share_out + (size_t)r * p.width;
@@ -818,6 +823,8 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditPar
 // (a misaligned address is left out; the record kernel skips that layer's copies and reports them).
 __global__ void __launch_bounds__(128) kmap_kernel(const __grid_constant__ CUtensorMap tmpl, const uint64_t* k_layers,
                                                    int layer0, int n_layers, CUtensorMap* maps, uint32_t* item_counter) {
+  chain_release();  // the record kernel may set up its rows meanwhile
+  chain_wait();
   if (threadIdx.x == 0) *item_counter = 0u;  // the record kernel's dynamic items start again
   for (int i = threadIdx.x; i < n_layers; i += blockDim.x) {
     CUtensorMap* map = maps + layer0 + i;
@@ -864,22 +871,22 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
     smem_of[device] = smem;
   }
   if (p.kmaps != nullptr) {
-    kmap_kernel<<<1, 128, 0, stream>>>(p.kmap0, p.k_layers, p.layer0, p.n_layers, const_cast<CUtensorMap*>(p.kmaps),
-                                       p.item_counter);
+    launch_chained(kmap_kernel, dim3(1), dim3(128), 0, stream, p.kmap0, p.k_layers, p.layer0, p.n_layers,
+                   const_cast<CUtensorMap*>(p.kmaps), p.item_counter);
     const int rc = check_launch("kmap_kernel");
     if (rc != EKV_OK) return rc;
   }
-  kernel<<<grid_of[device], kWarps * 32, smem, stream>>>(p);
+  launch_chained(kernel, dim3(grid_of[device]), dim3(kWarps * 32), smem, stream, p);
   int rc = check_launch("record_kernel");
   if (rc != EKV_OK || !finalize || p.share_out == nullptr) return rc;
   AuditParams ps = p;
   ps.layer0 = share0;
   ps.n_layers = share_layers;
   const long long pairs = (long long)share_layers * p.rows;
-  share_kernel<<<(unsigned)pairs, kShareThreads, 0, stream>>>(ps);
+  launch_chained(share_kernel, dim3((unsigned)pairs), dim3(kShareThreads), 0, stream, ps);
   rc = check_launch("share_kernel");
   if (rc != EKV_OK) return rc;
-  combine_kernel<<<dim3(cdiv(p.width, kCombineThreads), p.rows), kCombineThreads, 0, stream>>>(ps);
+  launch_chained(combine_kernel, dim3(cdiv(p.width, kCombineThreads), p.rows), dim3(kCombineThreads), 0, stream, ps);
   return check_launch("combine_kernel");
 }
 
@@ -1007,6 +1014,8 @@ __global__ void __launch_bounds__(256) stash_kernel(const uint8_t* q, int64_t q_
                                                     const int32_t* qrow, int rows, int64_t q_tokens,
                                                     int first_head, int heads_x_g, uint8_t* stash,
                                                     uint32_t* status) {
+  chain_release();
+  chain_wait();  // the query may come from the launch before this one
   constexpr int kChunks = 2 * D / 16;  // 16-byte pieces of one query row
   const long long total = (long long)rows * heads_x_g * kChunks;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -1041,9 +1050,9 @@ extern "C" int ekv_audit_stash(const void* q, int64_t q_stride_token, int64_t q_
     return fail(EKV_EINVAL, "the query and the stash must be 16-byte aligned with strides of whole 16-byte units");
   const long long pieces = (long long)rows * heads * group_rows * (2 * 128 / 16);
   const int blocks = (int)((pieces + 255) / 256 < 1024 ? (pieces + 255) / 256 : 1024);
-  stash_kernel<128><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(q), q_stride_token, q_stride_head, qrow, rows, q_tokens, group * group_rows,
-      heads * group_rows, static_cast<uint8_t*>(stash), status);
+  launch_chained(stash_kernel<128>, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                 static_cast<const uint8_t*>(q), q_stride_token, q_stride_head, qrow, rows, q_tokens,
+                 group * group_rows, heads * group_rows, static_cast<uint8_t*>(stash), status);
   return check_launch("stash_kernel");
 }
 

@@ -30,6 +30,30 @@ inline int cdiv(int a, int b) { return (a + b - 1) / b; }
 // ---- device: small utilities -------------------------------------------------------------------
 
 constexpr uint32_t kFullMask = 0xffffffffu;
+
+// ---- chained launches (programmatic dependent launch) ----------------------------------------------
+// A kernel launched with launch_chained may start while the kernel before it in the stream is still
+// finishing; it calls chain_wait() before it reads anything an earlier launch wrote (the wait returns
+// once that launch has completed and its writes are visible), and chain_release() once the next
+// chained launch may start. Without the launch attribute both are no-ops.
+__device__ __forceinline__ void chain_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void chain_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                  Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
 // A bounded wait gives up after this many SM clock cycles (about a second at 1.9 GHz).
 constexpr long long kWaitLimitCycles = 2000000000ll;
 

@@ -190,6 +190,8 @@ __device__ void pick_digit(SumState* st, unsigned int* hist, int pass) {
 // finishes last sets the budget.
 template <typename S>
 __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p) {
+  chain_release();
+  chain_wait();  // what the launch before this one wrote
   extern __shared__ __align__(16) unsigned char sum_smem[];
   S* s_x = reinterpret_cast<S*>(sum_smem);  // [width]: the row's scores
   __shared__ unsigned int s_hist[kSumBins];
@@ -263,6 +265,8 @@ __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p
 // Pass 1 over every key: grid (width / kSumChunk, rows). It counts each row's keys above the digit of
 // pass 0 and moves the keys of that digit to the candidates (each CTA's in one piece).
 __global__ void __launch_bounds__(kSumThreads) sum_keys_pass_kernel(const SumParams p) {
+  chain_release();
+  chain_wait();  // what the launch before this one wrote
   constexpr int pass = 1;
   __shared__ unsigned int s_hist[kSumBins];
   __shared__ unsigned long long s_ckey[kSumChunk];  // this CTA's candidates, moved out in one piece
@@ -332,6 +336,8 @@ __global__ void __launch_bounds__(kSumThreads) sum_keys_pass_kernel(const SumPar
 
 // Passes 2-5 over the candidates (the keys with pass 0's digit).
 __global__ void __launch_bounds__(kSumThreads) sum_cand_pass_kernel(const SumParams p, int pass) {
+  chain_release();
+  chain_wait();  // what the launch before this one wrote
   __shared__ unsigned int s_hist[kSumBins];
   __shared__ bool s_last;
   const int tid = threadIdx.x;
@@ -359,6 +365,8 @@ __global__ void __launch_bounds__(kSumThreads) sum_cand_pass_kernel(const SumPar
 // Over the candidates: keys above the threshold per row, ties per block index; the CTA that
 // finishes last finds i*, the lowest block index of the ties taken, and m, the ties taken there.
 __global__ void __launch_bounds__(kSumThreads) sum_ties_kernel(const SumParams p) {
+  chain_release();
+  chain_wait();  // what the launch before this one wrote
   __shared__ long long s_w[kSumThreads / 32];
   __shared__ bool s_last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -410,6 +418,8 @@ __global__ void __launch_bounds__(kSumThreads) sum_ties_kernel(const SumParams p
 
 // Over the candidates: each row's ties above i* and whether it ties at i*.
 __global__ void __launch_bounds__(kSumThreads) sum_kept_kernel(const SumParams p) {
+  chain_release();
+  chain_wait();  // what the launch before this one wrote
   const int tid = threadIdx.x;
   const SumState* st = p.state;
   if (st->mode != kSumSelect) return;
@@ -429,6 +439,8 @@ __global__ void __launch_bounds__(kSumThreads) sum_kept_kernel(const SumParams p
 
 // One CTA: the quotas; the m ties at i* go to the earliest rows that tie there.
 __global__ void __launch_bounds__(1024) sum_quota_kernel(const SumParams p) {
+  chain_release();
+  chain_wait();  // what the launch before this one wrote
   __shared__ int s_scan[1024 / 32 + 1];
   const int tid = threadIdx.x;
   const SumState* st = p.state;
@@ -463,6 +475,8 @@ __global__ void __launch_bounds__(1024) sum_quota_kernel(const SumParams p) {
 // (width / kSumMaskSpan, rows); four positions per thread.
 constexpr int kSumMaskSpan = 4 * kSumThreads;
 __global__ void __launch_bounds__(kSumThreads) sum_mask_kernel(const SumParams p) {
+  chain_release();
+  chain_wait();  // what the launch before this one wrote
   const int r = blockIdx.y;
   const SumState* st = p.state;
   const int mode = st->mode;
@@ -555,25 +569,25 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
       return check_launch("cudaFuncSetAttribute(sum_prep_kernel)");
     configured[device] = prep_smem;
   }
-  sum_prep_kernel<S><<<rows, kSumThreads, prep_smem, s>>>(p);
+  launch_chained(sum_prep_kernel<S>, dim3(rows), dim3(kSumThreads), prep_smem, s, p);
   int rc = check_launch("sum_prep_kernel");
   if (rc == EKV_OK) {
-    sum_keys_pass_kernel<<<dim3(cdiv(width, kSumChunk), rows), kSumThreads, 0, s>>>(p);
+    launch_chained(sum_keys_pass_kernel, dim3(cdiv(width, kSumChunk), rows), dim3(kSumThreads), 0, s, p);
     rc = check_launch("sum_keys_pass_kernel");
   }
   const int cand_grid = 2 * sms;
   for (int pass = 2; pass < kSumPasses && rc == EKV_OK; ++pass) {
-    sum_cand_pass_kernel<<<cand_grid, kSumThreads, 0, s>>>(p, pass);
+    launch_chained(sum_cand_pass_kernel, dim3(cand_grid), dim3(kSumThreads), 0, s, p, pass);
     rc = check_launch("sum_cand_pass_kernel");
   }
   if (rc != EKV_OK) return rc;
-  sum_ties_kernel<<<cand_grid, kSumThreads, 0, s>>>(p);
+  launch_chained(sum_ties_kernel, dim3(cand_grid), dim3(kSumThreads), 0, s, p);
   if ((rc = check_launch("sum_ties_kernel")) != EKV_OK) return rc;
-  sum_kept_kernel<<<cand_grid, kSumThreads, 0, s>>>(p);
+  launch_chained(sum_kept_kernel, dim3(cand_grid), dim3(kSumThreads), 0, s, p);
   if ((rc = check_launch("sum_kept_kernel")) != EKV_OK) return rc;
-  sum_quota_kernel<<<1, 1024, 0, s>>>(p);
+  launch_chained(sum_quota_kernel, dim3(1), dim3(1024), 0, s, p);
   if ((rc = check_launch("sum_quota_kernel")) != EKV_OK || mask_out == nullptr) return rc;
-  sum_mask_kernel<<<dim3(cdiv(width, kSumMaskSpan), rows), kSumThreads, 0, s>>>(p);
+  launch_chained(sum_mask_kernel, dim3(cdiv(width, kSumMaskSpan), rows), dim3(kSumThreads), 0, s, p);
   return check_launch("sum_mask_kernel");
 }
 

@@ -108,6 +108,8 @@ __device__ __forceinline__ uint32_t mm_score_key(float s) { return s > 0.f ? __f
 // (allocation.py:129): distinct scores can give equal shares.
 template <typename S>
 __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
+  chain_release();
+  chain_wait();  // what the launch before this one wrote
   extern __shared__ __align__(16) unsigned char mm_smem[];
   __shared__ PairwiseTree s_tree;
   __shared__ bool s_last;
@@ -225,6 +227,8 @@ __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
 }
 
 __global__ void __launch_bounds__(32) mm_cumsum_kernel(const MmParams p) {
+  chain_release();
+  chain_wait();  // what the launch before this one wrote
   extern __shared__ __align__(16) double cs_ring[];  // [kCsStages][kCsChunk][32]
   const int lane = threadIdx.x;
   const int r = blockIdx.x * 32 + lane;
@@ -323,6 +327,8 @@ __host__ __device__ inline MmLevelSmem mm_level_smem(int rows) {
 
 // One CTA: the water level, the leftover blocks and the quotas.
 __global__ void __launch_bounds__(kMmLevelThreads) mm_level_kernel(const MmParams p) {
+  chain_release();
+  chain_wait();  // what the launch before this one wrote
   extern __shared__ __align__(16) unsigned char lv_smem[];
   const MmLevelSmem L = mm_level_smem(p.rows);
   int* counts = reinterpret_cast<int*>(lv_smem + L.counts);
@@ -621,12 +627,12 @@ static int allocate_maxmin(const S* scores, int64_t score_stride, const int32_t*
       return check_launch("cudaFuncSetAttribute(mm_level_kernel)");
     level_set[device] = level_smem;
   }
-  mm_prep_kernel<S><<<rows, kMmThreads, prep_smem, s>>>(p);
+  launch_chained(mm_prep_kernel<S>, dim3(rows), dim3(kMmThreads), prep_smem, s, p);
   int rc = check_launch("mm_prep_kernel");
   if (rc != EKV_OK) return rc;
-  mm_cumsum_kernel<<<(rows + 31) / 32, 32, kCsSmem, s>>>(p);
+  launch_chained(mm_cumsum_kernel, dim3((rows + 31) / 32), dim3(32), kCsSmem, s, p);
   if ((rc = check_launch("mm_cumsum_kernel")) != EKV_OK) return rc;
-  mm_level_kernel<<<1, kMmLevelThreads, level_smem, s>>>(p);
+  launch_chained(mm_level_kernel, dim3(1), dim3(kMmLevelThreads), level_smem, s, p);
   return check_launch("mm_level_kernel");
 }
 

@@ -47,6 +47,8 @@ __device__ __forceinline__ long long block_sum_ll(long long v, long long* scratc
 }
 
 __global__ void __launch_bounds__(kQuotaThreads) quota_kernel(const QuotaParams p) {
+  chain_release();
+  chain_wait();  // what the launch before this one wrote
   extern __shared__ double s_rem[];  // [rows] remainders of the shared-budget split
   __shared__ long long s_red[kQuotaThreads / 32];
   const int R = p.rows;
@@ -351,6 +353,8 @@ __host__ __device__ constexpr size_t view_smem_bytes(int width) {
 // position's committed flag is written; with no view (mask_out only) the kernel ends there.
 template <typename K>
 __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) {
+  chain_release();
+  chain_wait();  // what the launch before this one wrote
   extern __shared__ __align__(16) unsigned char smem_view[];
   __shared__ __align__(16) int s_hist[kViewBins];
   __shared__ int s_w[kViewWarps + 1];
@@ -623,7 +627,7 @@ int launch_view(const ViewParams& p, cudaStream_t stream) {
       return check_launch("cudaFuncSetAttribute(view_kernel)");
     configured[device] = smem;
   }
-  view_kernel<K><<<p.rows, kViewThreads, smem, stream>>>(p);
+  launch_chained(view_kernel<K>, dim3(p.rows), dim3(kViewThreads), smem, stream, p);
   return check_launch("view_kernel");
 }
 
@@ -664,7 +668,7 @@ extern "C" int ekv_allocate_quotas(const int32_t* row_blocks, const int32_t* mea
   }
   QuotaParams p{row_blocks, measured_blocks, recent_blocks, cap_above_blocks, budget_fraction,
                 (long long)budget, row_fraction, rows, width, quota};
-  quota_kernel<<<1, kQuotaThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  launch_chained(quota_kernel, dim3(1), dim3(kQuotaThreads), smem, static_cast<cudaStream_t>(stream), p);
   return check_launch("quota_kernel");
 }
 

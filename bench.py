@@ -466,11 +466,19 @@ def main() -> None:
     if dist_on:
         from datetime import timedelta
 
-        # NCCL's version banner goes to stdout, where the one JSON line goes: keep NCCL at warnings unless
-        # a more verbose level was asked for
-        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-            os.environ["NCCL_DEBUG"] = "WARN"
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        # the communicator's set-up may print a version banner on the process's stdout, where the one JSON
+        # line goes: send file descriptor 1 to stderr until the first collective has run
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     import ekv.build
 
     ekv.build.build()

@@ -52,8 +52,10 @@ CONFIGS = {
 }
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one record-kernel launch (an audit step of all 32
-# layers) of the llama8b workload, from an ncu capture of that launch.
-NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"llama8b": 2458.654e6 + 8.595e6}
+# layers) of the llama8b workload: an ncu capture of the same launch over 8 layers (`--layers 8
+# --pools 1`: one 2.6 GB pool, every layer a head of its own) scaled by 4, the traffic growing with the
+# layers (every layer reads its own keys once).
+NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"llama8b": 4 * (614.871e6 + 5.805e6)}
 
 
 def lengths(spec, rows: int, rng: np.random.Generator) -> np.ndarray:
@@ -161,9 +163,13 @@ class Workload:
         self.table_host = table
         dev = torch.device("cuda", torch.cuda.current_device())
         gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+        # reference mode: a layer audits one KV head, head layer % kv_heads (the reference's rule), so
+        # ceil(layers / kv_heads) pools give every layer keys of its own, as a model's layers have; all-heads
+        # mode reads every head of a layer's pool and cycles over the configured pools
+        n_pools = cfg["pools"] if mode == "all-heads" or cfg.get("pools_fixed") else -(-self.layers // self.kv_local)
         self.caches = [
             torch.randn(pool, 2, BLOCK, self.kv_local, HEAD_DIM, device=dev, generator=gen, dtype=torch.bfloat16)
-            for _ in range(cfg["pools"])
+            for _ in range(n_pools)
         ]
         tokens = self.rows
         self.queries = [  # every layer's query of the step, resident in HBM
@@ -179,8 +185,15 @@ class Workload:
     def units_per_step(self) -> int:
         return int(self.lens.astype(np.int64).sum()) * self.layers * self.heads
 
+    def cache(self, layer: int) -> torch.Tensor:
+        """The KV pool of a layer. In reference mode layer l reads head l % kv_heads of pool
+        l // kv_heads: no two layers read the same keys, so no read is served from L2 by another layer's."""
+        if self.heads > 1 or self.cfg.get("pools_fixed"):
+            return self.caches[layer % len(self.caches)]
+        return self.caches[(layer // self.kv_local) % len(self.caches)]
+
     def keys(self, layer: int) -> torch.Tensor:
-        return self.caches[layer % len(self.caches)][:, 0]
+        return self.cache(layer)[:, 0]
 
     def query(self, layer: int) -> torch.Tensor:
         return self.queries[layer]
@@ -191,7 +204,7 @@ def make_plane(w: Workload, deferred: bool):
 
     os.environ.setdefault("EKV_RUNTIME_DIR", tempfile.mkdtemp(prefix="ekv_bench_"))
     plane = RecordingPlane(w.layers, w.rows, w.width, w.group_rows, BLOCK, heads=w.heads, deferred=deferred)
-    plane.attach([w.caches[layer % len(w.caches)].data_ptr() for layer in range(w.layers)])
+    plane.attach([w.cache(layer).data_ptr() for layer in range(w.layers)])
     plane.select(w.select, w.qrow)
     plane.set(True)
     return plane
@@ -207,7 +220,7 @@ def audit_step(plane, w: Workload) -> None:
 def audit_step_resident(plane, w: Workload, shares: bool = True) -> None:
     """One audit step from queries resident per layer: one launch of every layer (record_step)."""
     plane.record_step(w.table, w.lens_t, [w.query(layer) for layer in range(w.layers)],
-                      [w.caches[layer % len(w.caches)] for layer in range(w.layers)], w.scale, shares=shares)
+                      [w.cache(layer) for layer in range(w.layers)], w.scale, shares=shares)
 
 
 def capture(fn) -> torch.cuda.CUDAGraph:
@@ -443,15 +456,21 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the timed CPU sample")
     ap.add_argument("--no-view", action="store_true", help="skip the block-view build timing")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end timing")
-    ap.add_argument("--pools", type=int, default=None, help="distinct KV pools cycled over the layers")
+    ap.add_argument("--pools", type=int, default=None,
+                    help="a fixed number of KV pools cycled over the layers (default: reference mode gives every "
+                         "layer keys of its own)")
+    ap.add_argument("--layers", type=int, default=None, help="audit this many layers instead of the model's")
     ap.add_argument("--record", choices=["deferred", "per-layer"], default="deferred",
                     help="RecordingPlane mode: every layer in one launch after the last, or a launch per layer")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     cfg = dict(CONFIGS[args.config])
-    if args.pools:
+    if args.layers:  # fewer layers (profiling: with one pool, every layer still reads a head of its own)
+        cfg["layers"] = args.layers
+    if args.pools:  # a fixed number of pools, cycled over the layers (profiling: a few GB on the device)
         cfg["pools"] = args.pools
+        cfg["pools_fixed"] = True
     if args.impl == "reference":
         reference_arm(args, cfg)
         return
@@ -562,6 +581,7 @@ def main() -> None:
     if rank != 0:
         return
     traffic = NCU_TRAFFIC_PER_LAUNCH.get(args.config) if (args.mode == "reference" and args.record == "deferred"
+                                                          and not args.layers and not args.pools
                                                           and world == 1) else None
     line = {
         "metric": "audited KV tokens/s", "value": value, "unit": "audited KV tokens/s", "n_gpus": world,
@@ -572,7 +592,7 @@ def main() -> None:
                    "layers": w.layers,
                    "q_heads": cfg["q_heads"], "kv_heads": cfg["kv_heads"], "kv_heads_per_gpu": w.kv_local,
                    "audited_heads_per_layer_per_gpu": w.heads, "block_size": BLOCK, "tile_blocks": TILE_BLOCKS,
-                   "mean_len": float(w.lens.mean()), "width": w.width, "pools": cfg["pools"],
+                   "mean_len": float(w.lens.mean()), "width": w.width, "pools": len(w.caches),
                    "l2": f"inputs larger than L2: {units_rank / w.layers * 256 / 1e6:.0f} MB of keys per launch",
                    "parallelism": f"tp{world} (KV heads)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,

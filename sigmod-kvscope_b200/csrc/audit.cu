@@ -178,82 +178,35 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
   int* s_blocks = prefix + p.rows + 1;                                     // [rows]
   int* s_len = s_blocks + p.rows;                                          // [rows]
   int* s_tok = s_len + p.rows;                                             // [rows]
-  int* s_class_rows = s_tok + p.rows;                                      // [rows]: rows by last-chunk size
   __shared__ int s_scan[kWarps + 1];
-  __shared__ int s_class_count[kChunkTiles], s_class_start[kChunkTiles], s_class_fill[kChunkTiles];
   __shared__ long long s_queue[kWarps][kItemQueue];  // each warp's items in the order it took them
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   chain_wait();  // the query stash, the tensor maps and the item counter come from the launches before
   if (*p.flag == 0) return;  // the statistic is off: nothing is recorded (:64)
 
-  // ---- the rows of the step and the items -----------------------------------------------------
-  // With a counter (the items of a whole step go to whichever warp is free), full chunks (kChunkTiles
-  // tiles) of every (layer, head) come first, then each row's last, partial chunk, largest first: the
-  // items handed out last are the shortest, so the warps finish close together. prefix[r]: the full
-  // chunks of the rows before r; s_class_rows: the rows whose last chunk has s tiles, s from
-  // kChunkTiles - 1 down to 1. Without a counter (a launch with fewer items than warps) every chunk of a
-  // row is one item in row order: prefix[r] counts all chunks.
-  const bool by_size = p.item_counter != nullptr;
-  if (threadIdx.x < kChunkTiles) s_class_count[threadIdx.x] = 0, s_class_fill[threadIdx.x] = 0;
-  __syncthreads();
+  // ---- the rows of the step and the items: chunks per row, prefix-summed in shared memory --------
   {
     int carry = 0;
     for (int base = 0; base < p.rows; base += kWarps * 32) {
       const int r = base + threadIdx.x;
       RowInfo ri{0, 0, 0, 0};
-      int full = 0;
       if (r < p.rows) {
         ri = row_info(p, r, blockIdx.x == 0);
         s_blocks[r] = ri.n_blocks;
         s_len[r] = ri.len;
         s_tok[r] = ri.n_chunks ? p.qrow[r] : 0;
-        full = !by_size ? ri.n_chunks : (ri.n_chunks ? ri.n_tiles / kChunkTiles : 0);
-        const int part = by_size && ri.n_chunks ? ri.n_tiles % kChunkTiles : 0;
-        if (part) atomicAdd(&s_class_count[part], 1);
       }
       int total = 0;
-      const int before = block_exclusive_scan<kWarps * 32>(full, s_scan, &total);
+      const int before = block_exclusive_scan<kWarps * 32>(ri.n_chunks, s_scan, &total);
       if (r < p.rows) prefix[r] = carry + before;
       carry += total;
     }
-    if (threadIdx.x == 0) {
-      prefix[p.rows] = carry;
-      int at = 0;
-      for (int c = kChunkTiles - 1; c >= 1; --c) s_class_start[c] = at, at += s_class_count[c];
-    }
+    if (threadIdx.x == 0) prefix[p.rows] = carry;
     __syncthreads();
-    // the rows of each class in increasing order: every CTA must map an item to the same row
-    __shared__ int s_wcount[kWarps][kChunkTiles];
-    for (int base = 0; by_size && base < p.rows; base += kWarps * 32) {
-      const int r = base + threadIdx.x;
-      const int nb = r < p.rows ? s_blocks[r] : 0;  // 0 for a row that records nothing
-      const int part = nb > 0 ? ((nb + p.tile_blocks - 1) / p.tile_blocks) % kChunkTiles : 0;
-      int rank = 0;
-#pragma unroll
-      for (int c = 1; c < kChunkTiles; ++c) {
-        const uint32_t b = __ballot_sync(kFullMask, part == c);
-        if (lane == 0) s_wcount[warp][c] = __popc(b);
-        if (part == c) rank = __popc(b & ((1u << lane) - 1u));
-      }
-      __syncthreads();
-      if (part) {
-        int at = s_class_start[part] + s_class_fill[part] + rank;
-        for (int w = 0; w < warp; ++w) at += s_wcount[w][part];
-        s_class_rows[at] = r;
-      }
-      __syncthreads();
-      if (threadIdx.x >= 1 && threadIdx.x < kChunkTiles)
-        for (int w = 0; w < kWarps; ++w) s_class_fill[threadIdx.x] += s_wcount[w][threadIdx.x];
-      __syncthreads();
-    }
   }
-  const int full_per_lh = prefix[p.rows];
-  const long long lhs = (long long)p.heads * p.n_layers;
-  const long long full_items = (long long)full_per_lh * lhs;
-  int part_rows = 0;
-  for (int c = 1; c < kChunkTiles; ++c) part_rows += s_class_count[c];
-  const long long total_items = full_items + (long long)part_rows * lhs;
+  const int chunks_per_lh = prefix[p.rows];
+  const long long total_items = (long long)chunks_per_lh * p.heads * p.n_layers;
   const long long workers = (long long)gridDim.x * kWarps;
   const long long worker = (long long)blockIdx.x * kWarps + warp;
   uint32_t* const ctr = p.item_counter;
@@ -290,31 +243,19 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
   auto decode = [&](long long item, Cursor& c) {
     c.item = item;
     if (item >= total_items) return;
-    long long lh;
-    if (item < full_items) {  // a full chunk (every chunk without a counter): (layer, head), row, chunk
-      lh = item / full_per_lh;
-      const int idx = (int)(item - lh * full_per_lh);
-      int lo = 0, hi = p.rows;  // the last row with prefix[row] <= idx
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (prefix[mid] <= idx) lo = mid; else hi = mid;
-      }
-      c.row = lo;
-      c.t0 = c.t = (idx - prefix[lo]) * kChunkTiles;
-      c.t_end = by_size ? c.t + kChunkTiles : min(c.t + kChunkTiles, (s_blocks[lo] + p.tile_blocks - 1) / p.tile_blocks);
-    } else {  // a last, partial chunk: the size class, then (layer, head) and the row in the class
-      long long k = item - full_items;
-      int cls = kChunkTiles - 1;
-      while (k >= (long long)s_class_count[cls] * lhs) k -= (long long)s_class_count[cls] * lhs, --cls;
-      lh = k / s_class_count[cls];
-      const int row = s_class_rows[s_class_start[cls] + (int)(k - lh * s_class_count[cls])];
-      const int n_tiles = (s_blocks[row] + p.tile_blocks - 1) / p.tile_blocks;
-      c.row = row;
-      c.t0 = c.t = n_tiles - cls;
-      c.t_end = n_tiles;
+    const long long lh = item / chunks_per_lh;
+    const int idx = (int)(item - lh * chunks_per_lh);
+    int lo = 0, hi = p.rows;  // the last row with prefix[row] <= idx
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (prefix[mid] <= idx) lo = mid; else hi = mid;
     }
+    c.row = lo;
     c.layer = p.layer0 + (int)(lh / p.heads);
     c.head = (int)(lh % p.heads);
+    const int n_tiles = (s_blocks[lo] + p.tile_blocks - 1) / p.tile_blocks;
+    c.t0 = c.t = (idx - prefix[lo]) * kChunkTiles;
+    c.t_end = min(c.t + kChunkTiles, n_tiles);
   };
 
   // the block ids of an item: lane i holds blocks t0 * tile_blocks + i and + 32 + i
@@ -848,7 +789,7 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
   using Lay = Layout<D>;
   constexpr int STAGES = Ring<TT>::kStages;
   constexpr size_t fixed = 1024 + (size_t)kWarps * STAGES * TT * 2 * Lay::kHalfRow + kWarps * STAGES * (8 + 4);
-  const size_t smem = fixed + (size_t)(5 * p.rows + 1) * 4;
+  const size_t smem = fixed + (size_t)(4 * p.rows + 1) * 4;
   static int grid_of[kMaxDevices] = {};
   static size_t smem_of[kMaxDevices] = {};
   int device = 0;

@@ -557,7 +557,7 @@ constexpr int kShareBatch = 8;  // tiles whose cells a lane loads before it uses
 // xor-shuffles (lse_merge is commutative: both partners hold the same result), then over the warps in
 // warp order: the same order on every launch.
 __device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, int n, float* s_lse, int* s_has,
-                                           float (*s_wm)[kMaxQ], float (*s_ws)[kMaxQ], int* s_count) {
+                                           float (*s_wm)[kMaxQ], float (*s_ws)[kMaxQ]) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int Q = p.Q, TB = p.tile_blocks;
   const int n_tiles = (n + TB - 1) / TB;
@@ -612,7 +612,7 @@ __device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, i
     int has = 0;
     for (int k = lane; k < Q; k += 32) has += s_has[k];
     for (int off = 16; off > 0; off >>= 1) has += __shfl_xor_sync(kFullMask, has, off);
-    if (lane == 0) p.contrib_layer[lr] = has, *s_count = has;
+    if (lane == 0) p.contrib_layer[lr] = has;
   }
 
   // 2. every tile's share, summed (mean) or maxed (max) over the query rows: exp(u - lse) =
@@ -666,7 +666,6 @@ __global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams 
   __shared__ float s_lse[kMaxQ];
   __shared__ int s_has[kMaxQ];
   __shared__ float s_wm[kShareWarps][kMaxQ], s_ws[kShareWarps][kMaxQ];
-  __shared__ int s_count;
   chain_release();
   chain_wait();  // the record kernel's cells
   if (*p.flag == 0) return;  // nothing was recorded this step
@@ -678,7 +677,7 @@ __global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams 
     if (threadIdx.x == 0) p.contrib_layer[(size_t)L * p.rows + r] = 0;
     return;
   }
-  share_task(p, L, r, ri.n_blocks, s_lse, s_has, s_wm, s_ws, &s_count);
+  share_task(p, L, r, ri.n_blocks, s_lse, s_has, s_wm, s_ws);
 }
 
 // ---- the combine kernel: a row's layers into its final share --------------------------------------------

@@ -6,8 +6,8 @@ meaning. SGLang's decode kernel reads request ``r`` from ``slots[indptr[r]:indpt
 slot per entry; the view groups ``block_tokens`` consecutive entries into a block and keeps some
 blocks (the first and last always; all of them when the policy is not live, when the row is audited,
 and for the rows a CUDA graph adds from ``n_real`` on). The work runs in the sm_100a kernels of
-``ekv_slot_compact``: a plan kernel whose warps take rows in parallel (the reference walks the rows
-in one Triton program), a gather of every new entry, and the copy back into the engine's buffers.
+``ekv_slot_compact``: a warp per row (the reference walks the rows in one Triton program), a scan of
+the new lengths, a gather of every new entry, and the copy back into the engine's buffers.
 """
 
 from __future__ import annotations

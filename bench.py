@@ -176,8 +176,11 @@ class Workload:
             torch.randn(tokens, self.kv_local * self.group_rows, HEAD_DIM, device=dev, generator=gen,
                         dtype=torch.bfloat16) for _ in range(self.layers)
         ]
-        self.table = torch.from_numpy(table).to(dev)
-        self.lens_t = torch.from_numpy(self.lens).to(dev)
+        # the engine's step inputs, block table then lengths, in one buffer that one copy fills
+        self.inputs_host = np.concatenate([table.ravel(), self.lens])
+        self.inputs = torch.from_numpy(self.inputs_host).to(dev)
+        self.table = self.inputs[: table.size].view(self.rows, self.width)
+        self.lens_t = self.inputs[table.size :]
         self.qrow = np.arange(self.rows, dtype=np.int32)
         self.select = np.ones(self.rows, dtype=bool)
         self.scale = 1.0 / math.sqrt(HEAD_DIM)
@@ -548,28 +551,32 @@ def main() -> None:
     peak, peak_kind = measured_peak()
 
     # e2e: the step's host inputs in from pinned memory, the shares out, every step
-    pinned_table = torch.from_numpy(w.table_host).pin_memory()
-    pinned_lens = torch.from_numpy(w.lens).pin_memory()
-    pinned_sel = torch.from_numpy(w.select.astype(np.uint8)).pin_memory()
-    pinned_tok = torch.from_numpy(w.qrow).pin_memory()
-    out_host = torch.empty(share.shape, dtype=share.dtype).pin_memory()
+    # (the engine's block table and lengths: one copy; the selection: RecordingPlane.select, one copy)
+    # Each step's shares land in one of two pinned buffers; the host waits for a step's shares after it
+    # has queued the next step, so the GPU does not idle while the host issues a step.
+    pinned_inputs = torch.from_numpy(w.inputs_host).pin_memory()
+    out_host = [torch.empty(share.shape, dtype=share.dtype).pin_memory() for _ in range(2)]
+    out_ready = [torch.cuda.Event(), torch.cuda.Event()]
+    issued = [0]
 
     api_graph = capture(lambda: audit_step(plane, w)) if args.record == "deferred" else graph
 
     def e2e_step():
-        w.table.copy_(pinned_table, non_blocking=True)
-        w.lens_t.copy_(pinned_lens, non_blocking=True)
-        plane._select.copy_(pinned_sel, non_blocking=True)
-        plane._token.copy_(pinned_tok, non_blocking=True)
+        i = issued[0]
+        issued[0] += 1
+        w.inputs.copy_(pinned_inputs, non_blocking=True)
+        plane.select(w.select, w.qrow)
         api_graph.replay()
         if dist_on:
             allreduce_shares(share)
-        out_host.copy_(share, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        out_host[i % 2].copy_(share, non_blocking=True)
+        out_ready[i % 2].record()
+        if i > 0:
+            out_ready[(i - 1) % 2].synchronize()  # the previous step's shares are on the host
 
     e2e_seconds = timed(e2e_step, args.steps, args.warmup, dist_on) if not args.no_e2e else float("nan")
-    h2d = pinned_table.nbytes + pinned_lens.nbytes + pinned_sel.nbytes + pinned_tok.nbytes
-    d2h = out_host.nbytes
+    h2d = pinned_inputs.nbytes + 5 * w.rows  # select(): a token row (int32) and a flag per row
+    d2h = out_host[0].nbytes
     view = None if args.no_view else view_bench(rank, world, args.steps, args.warmup, dist_on)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -603,9 +610,11 @@ def main() -> None:
                              "layer); CUDA events over its own timed launches"},
         "e2e": {"value": units_all * args.steps / e2e_seconds, "unit": "audited KV tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "note": "RecordingPlane.record per layer (a query stash per layer, one launch of every layer "
-                        "after the last) in a CUDA graph; block table, lengths, selection, query rows in from "
-                        "pinned host memory, shares out; KV cache resident"},
+                "note": "RecordingPlane.select (one copy from pinned staging), then RecordingPlane.record per "
+                        "layer (a query stash per layer, one launch of every layer after the last) in a CUDA "
+                        "graph; the block table and lengths in by one copy from pinned host memory, shares "
+                        "out to pinned memory, the host waiting for them after queueing the next step; KV "
+                        "cache resident"},
         # per step: the descriptor, record, share and combine kernels (deferred), or a record kernel
         # per layer plus the share and combine kernels (per-layer)
         "gpu_launches": args.steps * (4 if args.record == "deferred" else w.layers + 2),

@@ -88,8 +88,15 @@ class RecordingPlane(AuditPlane):
         self._cuda.cudaMemset(ctypes.c_void_p(self._table_dev), 0, ctypes.c_size_t(layers * 8))
         device = torch.device("cuda", torch.cuda.current_device())
         self._device = device
-        self._select = torch.zeros(rows, dtype=torch.uint8, device=device)
-        self._token = torch.zeros(rows, dtype=torch.int32, device=device)
+        # the selection: query token rows then audited flags, one device buffer that one copy fills
+        self._inputs = torch.zeros(5 * rows, dtype=torch.uint8, device=device)
+        self._token = self._inputs[: 4 * rows].view(torch.int32)
+        self._select = self._inputs[4 * rows :]
+        self._inputs_host = np.zeros(5 * rows, dtype=np.uint8)  # what the device buffer holds
+        # two pinned staging buffers, each reused once the copy from it has run
+        self._staging = [torch.zeros(5 * rows, dtype=torch.uint8).pin_memory() for _ in range(2)]
+        self._staged = [torch.cuda.Event(), torch.cuda.Event()]
+        self._stage = 0
         # the fused share: final shares and contributors, and the kernel's workspace
         self._contributors = torch.zeros(rows, dtype=torch.int32, device=device)
         self._share = torch.full((rows, width), float("nan"), dtype=torch.float32, device=device)
@@ -169,9 +176,26 @@ class RecordingPlane(AuditPlane):
 
     def select(self, audited: np.ndarray, token_start: np.ndarray) -> None:
         """Choose the rows to record in the next step, and the token index of each row's query."""
+        audited = np.asarray(audited)
         rows = len(audited)
-        self._select[:rows].copy_(torch.from_numpy(np.asarray(audited).astype(np.uint8)))
-        self._token[:rows].copy_(torch.from_numpy(np.asarray(token_start).astype(np.int32)))
+        try:  # the shapes torch's copy into the first `rows` rows accepts
+            if rows > self.rows:
+                raise ValueError
+            token_start = np.broadcast_to(np.asarray(token_start), (rows,))
+        except ValueError:
+            raise RuntimeError(
+                f"{rows} audited flags and {np.shape(token_start)} token rows for a plane of {self.rows} rows"
+            ) from None
+        host = self._inputs_host
+        host[: 4 * self.rows].view(np.int32)[:rows] = token_start.astype(np.int32)
+        host[4 * self.rows : 4 * self.rows + rows] = audited.astype(np.uint8)
+        # one asynchronous copy on the current stream from a pinned buffer whose last copy has run
+        i = self._stage
+        self._staged[i].synchronize()
+        self._staging[i].numpy()[:] = host
+        self._inputs.copy_(self._staging[i], non_blocking=True)
+        self._staged[i].record()
+        self._stage = 1 - i
 
     def record(
         self,

@@ -454,3 +454,23 @@ def test_long_context_rows_match_the_c_oracle():
     u = osh.log_weights(ref, 1, np.arange(rows), 2)
     share = run.share.cpu().numpy().astype(np.float64)
     np.testing.assert_allclose(share, osh.normalize(u, blocks, 2), **SHARE_TOL)
+
+
+def test_select_is_one_ordered_copy_per_call(runtime_dir):
+    """select() stages both arrays in pinned memory and copies them on the current stream: calls in a
+    row land in order, a shorter selection leaves the later rows as they were, and shapes torch's
+    copy would refuse raise RuntimeError, as the reference's select does."""
+    from ekv.runtime.audit_kernel import RecordingPlane
+
+    rows = 6
+    plane = RecordingPlane(2, rows, 4, 4, 16)
+    for i in range(5):  # more calls than staging buffers, without a synchronisation between them
+        plane.select(np.arange(rows) % 2 == i % 2, np.arange(rows) + 10 * i)
+    plane.select(np.array([True, True]), np.array([7, 8]))
+    torch.cuda.synchronize()
+    assert plane._token.cpu().tolist() == [7, 8, 42, 43, 44, 45]
+    assert plane._select.cpu().tolist() == [1, 1, 1, 0, 1, 0]
+    with pytest.raises(RuntimeError):
+        plane.select(np.ones(rows + 1, dtype=bool), np.arange(rows + 1))
+    with pytest.raises(RuntimeError):
+        plane.select(np.ones(3, dtype=bool), np.arange(2))

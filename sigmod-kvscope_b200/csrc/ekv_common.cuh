@@ -57,6 +57,13 @@ inline cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 bloc
 // A bounded wait gives up after this many SM clock cycles (about a second at 1.9 GHz).
 constexpr long long kWaitLimitCycles = 2000000000ll;
 
+// The lanes of this warp below this one, as a mask.
+__device__ __forceinline__ uint32_t lanes_below() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

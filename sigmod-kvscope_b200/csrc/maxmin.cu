@@ -10,13 +10,16 @@
 // the rest of the budget goes one block at a time to the request with the lowest retained share
 // (ties: the earlier request). Here:
 //   mm_prep_kernel, one CTA per row: the total, the shares of the pinned blocks summed as NumPy sums
-//     them, the unpinned blocks ordered by a bitonic sort of (score, block) keys, their shares in that
-//     order; the CTA that finishes last sets the budget and each request's index.
+//     them, the unpinned blocks ordered by a stable radix sort of their share keys (equal keys keep the
+//     older block first), their shares in that order; the CTA that finishes last sets the budget and
+//     each request's index.
 //   mm_cumsum_kernel, a thread per row: the running sums, one addition after another as np.cumsum.
 //   mm_level_kernel, one CTA: the bisection (a binary search per request and a reduction per step)
 //     and the leftover blocks through a binary heap in shared memory. The row quotas it writes make
 //     ekv_view_build (EKV_POLICY_UNIFORM: equal shares to the older block) keep exactly the reference's
 //     blocks.
+#include <type_traits>
+
 #include "ekv_common.cuh"
 #include "pairwise.cuh"
 #include "pins.cuh"
@@ -85,18 +88,89 @@ MmLayout mm_layout(int rows, int width) {
 __device__ __forceinline__ double mm_clamped(float s) { return s > 0.f ? (double)s : 0.0; }
 __device__ __forceinline__ double mm_clamped(double s) { return s > 0.0 ? s : 0.0; }
 
+constexpr int kMmSortItems = kMmMaxWidth / kMmThreads;  // keys a thread holds in a sort pass
+constexpr int kMmDigits = 256;                            // 8-bit digits
+constexpr int kMmWarps = kMmThreads / 32;
+constexpr int kMmScanWarps = 8;                                   // counts of one digit a thread scans
+constexpr int kMmDigitThreads = kMmWarps / kMmScanWarps;          // threads per digit in the scan
+static_assert(kMmDigitThreads * kMmDigits == kMmThreads, "the count scan gives every thread 8 warps of a digit");
+
+// Keys of a row's sort: a multiple of kMmThreads covering the width.
 __host__ __device__ __forceinline__ int mm_sort_n(int width) {
-  int n = 1;
-  while (n < width) n <<= 1;
-  return n;
+  return (width + kMmThreads - 1) / kMmThreads * kMmThreads;
 }
 
-// Shared memory of mm_prep_kernel<S>: the row's scores, the sort keys (uint64 [mm_sort_n(width)]) and,
-// for float64 scores, the block of each key (uint32 [mm_sort_n(width)]).
+// Shared memory of mm_prep_kernel<S>: the row's scores, then the sort keys (uint32 for float32 scores,
+// uint64 for float64, [mm_sort_n(width)]), the block of each key (uint16) and the digit counts of
+// every warp (uint16 [warps][256]); the pairwise sums' scratch, used before the sort, lies over these.
 template <typename S>
 __host__ __device__ __forceinline__ size_t mm_prep_smem(int width) {
   const size_t scores = ((size_t)width * sizeof(S) + 15) / 16 * 16;
-  return scores + (size_t)mm_sort_n(width) * (sizeof(S) == 8 ? 12 : 8);
+  const size_t keys = (size_t)mm_sort_n(width) * sizeof(S);
+  const size_t blocks = ((size_t)mm_sort_n(width) * 2 + 15) / 16 * 16;
+  const size_t sort = keys + blocks + (size_t)kMmWarps * kMmDigits * 2;
+  return scores + (sort > sizeof(PairwiseTree) ? sort : sizeof(PairwiseTree));
+}
+
+// Stable ascending sort of the keys s_key[0, kMmThreads * items) with their blocks s_blk, in shared memory:
+// least significant digit first, 8 bits a pass. Warp w holds elements [w * 32 * items, (w + 1) * 32 *
+// items), item k of lane l being element w * 32 * items + 32 k + l; a warp ranks its items in element
+// order (items in order, lanes with the same digit by match.any), the counts of every (digit, warp)
+// are scanned digit-major, warp-minor, and every key goes to its digit's start + the count of
+// earlier equal digits: a stable pass.
+template <typename K>
+__device__ void mm_radix_sort(K* s_key, uint16_t* s_blk, uint16_t* s_cnt, int* s_scan, int items) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int span = 32 * items;
+  uint16_t* wcnt = s_cnt + warp * kMmDigits;  // this warp's counts
+  for (int shift = 0; shift < 8 * (int)sizeof(K); shift += 8) {
+    K key[kMmSortItems];
+    uint32_t item[kMmSortItems];  // the key's block (low half), then its rank in the warp's digit (high)
+#pragma unroll
+    for (int k = 0; k < kMmSortItems; ++k) {
+      if (k < items) {
+        const int e = warp * span + 32 * k + lane;
+        key[k] = s_key[e];
+        item[k] = s_blk[e];
+      }
+    }
+    for (int i = tid; i < kMmWarps * kMmDigits; i += kMmThreads) s_cnt[i] = 0;
+    __syncthreads();  // every key read, every count zero
+#pragma unroll
+    for (int k = 0; k < kMmSortItems; ++k) {
+      if (k < items) {
+        const unsigned d = (unsigned)(key[k] >> shift) & (kMmDigits - 1);
+        const uint32_t peers = __match_any_sync(kFullMask, d);
+        const int below = __popc(peers & lanes_below());
+        const int seen = wcnt[d];
+        item[k] |= (uint32_t)(seen + below) << 16;
+        __syncwarp();
+        if (below == 0) wcnt[d] = (uint16_t)(seen + __popc(peers));
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    // thread t: the counts of 8 warps of one digit, in the digit-major order of the scan
+    const int d = tid / kMmDigitThreads, w0 = (tid % kMmDigitThreads) * kMmScanWarps;
+    int c[kMmScanWarps], sum = 0;
+#pragma unroll
+    for (int i = 0; i < kMmScanWarps; ++i) c[i] = s_cnt[(w0 + i) * kMmDigits + d], sum += c[i];
+    int total = 0;
+    int at = block_exclusive_scan<kMmThreads>(sum, s_scan, &total);
+#pragma unroll
+    for (int i = 0; i < kMmScanWarps; ++i) s_cnt[(w0 + i) * kMmDigits + d] = (uint16_t)at, at += c[i];
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kMmSortItems; ++k) {
+      if (k < items) {
+        const unsigned dk = (unsigned)(key[k] >> shift) & (kMmDigits - 1);
+        const int pos = wcnt[dk] + (int)(item[k] >> 16);
+        s_key[pos] = key[k];
+        s_blk[pos] = (uint16_t)item[k];
+      }
+    }
+    __syncthreads();
+  }
 }
 
 // max(score, 0) as an order-preserving uint32 (NaN as 0)
@@ -111,17 +185,20 @@ __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
   chain_release();
   chain_wait();  // what the launch before this one wrote
   extern __shared__ __align__(16) unsigned char mm_smem[];
-  __shared__ PairwiseTree s_tree;
   __shared__ bool s_last;
   constexpr bool kWide = sizeof(S) == 8;
   const int r = blockIdx.x, tid = threadIdx.x;
   int n = p.row_blocks[r];
   const bool request = n > p.cap && n > 0;
   if (n > p.width) n = p.width;
+  using Key = typename std::conditional<sizeof(S) == 8, unsigned long long, uint32_t>::type;
+  const int N = mm_sort_n(p.width);
   S* s_x = reinterpret_cast<S*>(mm_smem);
-  unsigned long long* s_key =
-      reinterpret_cast<unsigned long long*>(mm_smem + ((size_t)p.width * sizeof(S) + 15) / 16 * 16);
-  uint32_t* s_blk = reinterpret_cast<uint32_t*>(s_key + mm_sort_n(p.width));  // float64 scores only
+  Key* s_key = reinterpret_cast<Key*>(mm_smem + ((size_t)p.width * sizeof(S) + 15) / 16 * 16);
+  uint16_t* s_blk = reinterpret_cast<uint16_t*>(s_key + N);
+  uint16_t* s_cnt = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(s_blk) + ((size_t)N * 2 + 15) / 16 * 16);
+  __shared__ int s_scan[kMmThreads / 32 + 1];
+  PairwiseTree& s_tree = *reinterpret_cast<PairwiseTree*>(s_key);  // until the keys are written
   const int ps = request ? pin_start(n, p.recent, p.measured, r) : 0;
   const int m = ps > 1 ? ps - 1 : 0;  // unpinned blocks [1, ps)
   if (request) {
@@ -135,44 +212,21 @@ __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
     const int npin = ps >= 1 ? 1 + (n - ps) : n;
     const double base = block_pairwise_sum<kMmThreads>(
         s_tree, npin, [&](int j) { return share(ps >= 1 ? (j == 0 ? 0 : ps + j - 1) : j); });
-    // the unpinned blocks by decreasing share, equal shares by increasing block: ascending keys; the
-    // padding sorts last
-    int P = 1;
-    while (P < m) P <<= 1;
-    if constexpr (kWide) {
-      for (int j = tid; j < P; j += kMmThreads) {
+    __syncthreads();  // every thread has the sums: the keys may overwrite the scratch
+    // the unpinned blocks by decreasing share, equal shares by increasing block: ascending keys in
+    // block order through a stable sort; the padding (all ones) sorts last
+    const int items = (m + kMmThreads - 1) / kMmThreads;
+    for (int j = tid; j < items * kMmThreads; j += kMmThreads) {
+      if constexpr (kWide) {
         s_key[j] = j < m ? ~(unsigned long long)__double_as_longlong(share(1 + j)) : ~0ull;
-        s_blk[j] = j < m ? (uint32_t)(1 + j) : 0xffffffffu;
+      } else {
+        s_key[j] = j < m ? ~mm_score_key(s_x[1 + j]) : ~0u;
       }
-    } else {
-      for (int j = tid; j < P; j += kMmThreads)
-        s_key[j] = j < m ? ((unsigned long long)(~mm_score_key(s_x[1 + j])) << 32) | (unsigned long long)(1 + j)
-                         : ~0ull;
+      s_blk[j] = (uint16_t)(j < m ? 1 + j : 0);
     }
     __syncthreads();
-    for (int k = 2; k <= P; k <<= 1) {
-      for (int j = k >> 1; j > 0; j >>= 1) {
-        for (int i = tid; i < P; i += kMmThreads) {
-          const int partner = i ^ j;
-          if (partner > i) {
-            const unsigned long long a = s_key[i], b = s_key[partner];
-            const bool up = (i & k) == 0;
-            if constexpr (kWide) {
-              const uint32_t ai = s_blk[i], bi = s_blk[partner];
-              if ((a > b || (a == b && ai > bi)) == up) s_key[i] = b, s_key[partner] = a, s_blk[i] = bi, s_blk[partner] = ai;
-            } else {
-              if ((a > b) == up) s_key[i] = b, s_key[partner] = a;
-            }
-          }
-        }
-        __syncthreads();
-      }
-    }
-    if constexpr (kWide) {
-      for (int j = tid; j < m; j += kMmThreads) p.sorted[(int64_t)j * p.rows + r] = share((int)s_blk[j]);
-    } else {
-      for (int j = tid; j < m; j += kMmThreads) p.sorted[(int64_t)j * p.rows + r] = share((int)(s_key[j] & 0xffffffffu));
-    }
+    if (items > 0) mm_radix_sort<Key>(s_key, s_blk, s_cnt, s_scan, items);
+    for (int j = tid; j < m; j += kMmThreads) p.sorted[(int64_t)j * p.rows + r] = share((int)s_blk[j]);
     if (tid == 0) {
       p.base[r] = base;
       atomicAdd((unsigned long long*)&p.state->must, (unsigned long long)pin_count(n, ps));
@@ -201,7 +255,6 @@ __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
     st->mode = budget >= blocks ? kMmAll : (free_ <= 0 ? kMmNone : kMmSelect);
     st->ticket = 0;
   }
-  __shared__ int s_scan[kMmThreads / 32 + 1];
   int carry = 0;
   for (int b0 = 0; b0 < p.rows; b0 += kMmThreads) {
     const int row = b0 + tid;

@@ -262,11 +262,6 @@ __device__ __forceinline__ void copy_words(int32_t* dst, const int32_t* src, int
   for (int j = i + threadIdx.x; j < hi; j += kViewThreads) dst[j] = src[j];
 }
 
-__device__ __forceinline__ uint32_t lanes_below() {
-  uint32_t m;
-  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
-  return m;
-}
 
 // Exclusive scan of one count per warp (warp 0 scans): {this warp's base, the total}.
 __device__ __forceinline__ int2 warp_bases(int count, int* s_w) {

@@ -90,10 +90,14 @@ __device__ __forceinline__ double mm_clamped(double s) { return s > 0.0 ? s : 0.
 
 constexpr int kMmSortItems = kMmMaxWidth / kMmThreads;  // keys a thread holds in a sort pass
 constexpr int kMmDigits = 256;                            // 8-bit digits
+// A warp's digit counts (uint16) take kMmCountStride entries: rows two entries longer than the digits
+// put the 8 warps x 4 digit pairs that a warp of the count scan reads in 32 different banks.
+constexpr int kMmCountStride = kMmDigits + 2;
 constexpr int kMmWarps = kMmThreads / 32;
 constexpr int kMmScanWarps = 8;                                   // counts of one digit a thread scans
 constexpr int kMmDigitThreads = kMmWarps / kMmScanWarps;          // threads per digit in the scan
 static_assert(kMmDigitThreads * kMmDigits == kMmThreads, "the count scan gives every thread 8 warps of a digit");
+static_assert(kMmWarps <= 32, "a warp scans the warp totals");
 
 // Keys of a row's sort: a multiple of kMmThreads covering the width.
 __host__ __device__ __forceinline__ int mm_sort_n(int width) {
@@ -102,27 +106,27 @@ __host__ __device__ __forceinline__ int mm_sort_n(int width) {
 
 // Shared memory of mm_prep_kernel<S>: the row's scores, then the sort keys (uint32 for float32 scores,
 // uint64 for float64, [mm_sort_n(width)]), the block of each key (uint16) and the digit counts of
-// every warp (uint16 [warps][256]); the pairwise sums' scratch, used before the sort, lies over these.
+// every warp (uint16 [warps][kMmCountStride]); the pairwise sums' scratch, used before the sort, lies over these.
 template <typename S>
 __host__ __device__ __forceinline__ size_t mm_prep_smem(int width) {
   const size_t scores = ((size_t)width * sizeof(S) + 15) / 16 * 16;
   const size_t keys = (size_t)mm_sort_n(width) * sizeof(S);
   const size_t blocks = ((size_t)mm_sort_n(width) * 2 + 15) / 16 * 16;
-  const size_t sort = keys + blocks + (size_t)kMmWarps * kMmDigits * 2;
+  const size_t sort = keys + blocks + (size_t)kMmWarps * kMmCountStride * 2;
   return scores + (sort > sizeof(PairwiseTree) ? sort : sizeof(PairwiseTree));
 }
 
 // Stable ascending sort of the keys s_key[0, kMmThreads * items) with their blocks s_blk, in shared memory:
 // least significant digit first, 8 bits a pass. Warp w holds elements [w * 32 * items, (w + 1) * 32 *
 // items), item k of lane l being element w * 32 * items + 32 k + l; a warp ranks its items in element
-// order (items in order, lanes with the same digit by match.any), the counts of every (digit, warp)
+// order (items in order, lanes with the same digit by eight ballots), the counts of every (digit, warp)
 // are scanned digit-major, warp-minor, and every key goes to its digit's start + the count of
 // earlier equal digits: a stable pass.
 template <typename K>
 __device__ void mm_radix_sort(K* s_key, uint16_t* s_blk, uint16_t* s_cnt, int* s_scan, int items) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int span = 32 * items;
-  uint16_t* wcnt = s_cnt + warp * kMmDigits;  // this warp's counts
+  uint16_t* wcnt = s_cnt + warp * kMmCountStride;  // this warp's counts
   for (int shift = 0; shift < 8 * (int)sizeof(K); shift += 8) {
     K key[kMmSortItems];
     uint32_t item[kMmSortItems];  // the key's block (low half), then its rank in the warp's digit (high)
@@ -134,13 +138,18 @@ __device__ void mm_radix_sort(K* s_key, uint16_t* s_blk, uint16_t* s_cnt, int* s
         item[k] = s_blk[e];
       }
     }
-    for (int i = tid; i < kMmWarps * kMmDigits; i += kMmThreads) s_cnt[i] = 0;
+    for (int i = tid; i < kMmWarps * kMmCountStride; i += kMmThreads) s_cnt[i] = 0;
     __syncthreads();  // every key read, every count zero
 #pragma unroll
     for (int k = 0; k < kMmSortItems; ++k) {
       if (k < items) {
         const unsigned d = (unsigned)(key[k] >> shift) & (kMmDigits - 1);
-        const uint32_t peers = __match_any_sync(kFullMask, d);
+        uint32_t peers = kFullMask;  // the lanes with this digit: eight ballots (faster than match.any)
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+          const uint32_t bal = __ballot_sync(kFullMask, (d >> b) & 1u);
+          peers &= ((d >> b) & 1u) ? bal : ~bal;
+        }
         const int below = __popc(peers & lanes_below());
         const int seen = wcnt[d];
         item[k] |= (uint32_t)(seen + below) << 16;
@@ -154,11 +163,20 @@ __device__ void mm_radix_sort(K* s_key, uint16_t* s_blk, uint16_t* s_cnt, int* s
     const int d = tid / kMmDigitThreads, w0 = (tid % kMmDigitThreads) * kMmScanWarps;
     int c[kMmScanWarps], sum = 0;
 #pragma unroll
-    for (int i = 0; i < kMmScanWarps; ++i) c[i] = s_cnt[(w0 + i) * kMmDigits + d], sum += c[i];
-    int total = 0;
-    int at = block_exclusive_scan<kMmThreads>(sum, s_scan, &total);
+    for (int i = 0; i < kMmScanWarps; ++i) c[i] = s_cnt[(w0 + i) * kMmCountStride + d], sum += c[i];
+    // the exclusive prefix of `sum` over the threads: a warp scan, then every warp scans the warp totals
+    int inc = sum;
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(kFullMask, inc, off);
+      if (lane >= off) inc += v;
+    }
+    if (lane == 31) s_scan[warp] = inc;
+    __syncthreads();
+    int before = lane < warp ? s_scan[lane] : 0;  // the totals of the warps before this one
+    for (int off = 16; off > 0; off >>= 1) before += __shfl_xor_sync(kFullMask, before, off);
+    int at = before + inc - sum;
 #pragma unroll
-    for (int i = 0; i < kMmScanWarps; ++i) s_cnt[(w0 + i) * kMmDigits + d] = (uint16_t)at, at += c[i];
+    for (int i = 0; i < kMmScanWarps; ++i) s_cnt[(w0 + i) * kMmCountStride + d] = (uint16_t)at, at += c[i];
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < kMmSortItems; ++k) {
@@ -432,42 +450,61 @@ __global__ void __launch_bounds__(kMmLevelThreads) mm_level_kernel(const MmParam
         lo_v[2 * n + 2] = mid[n], hi_v[2 * n + 2] = hi_v[n];
       }
     }
-    long long sum[kMmNodes];
+    int sum[kMmNodes];  // at most 4096 requests x 8192 blocks
 #pragma unroll
     for (int n = 0; n < kMmNodes; ++n) sum[n] = 0;
-    for (int r = tid; r < p.rows; r += kMmLevelThreads) {
-      const int m = s_m[r];
-      if (m < 0) continue;
-      const double base = s_base[r], off = s_off[r];
-      int lo[kMmNodes], hi[kMmNodes];
-      double x[kMmNodes];
+    // two requests a thread, r0 and r0 + kMmLevelThreads, their 2 x kMmNodes searches side by side
+    for (int r0 = tid; r0 < p.rows; r0 += 2 * kMmLevelThreads) {
+      int rq[2], mq[2];
+      double base[2], off[2];
+      uint32_t lh[2][kMmNodes];  // the search's bounds: lo | hi << 16 (both at most 8192)
 #pragma unroll
-      for (int n = 0; n < kMmNodes; ++n) {
-        lo[n] = s_lo[r], hi[n] = s_hi[r];
-        x[n] = (mid[n] - base) - 1e-12 + off;
+      for (int q = 0; q < 2; ++q) {
+        const int r = r0 + q * kMmLevelThreads;
+        rq[q] = r < p.rows ? r : r0;
+        mq[q] = r < p.rows ? s_m[r] : -1;
+        base[q] = s_base[rq[q]], off[q] = s_off[rq[q]];
+        const uint32_t b = mq[q] >= 0 ? (uint32_t)s_lo[rq[q]] | ((uint32_t)s_hi[rq[q]] << 16) : 0u;
+#pragma unroll
+        for (int n = 0; n < kMmNodes; ++n) lh[q][n] = b;
       }
-      for (;;) {  // the searches side by side, one load each per step
-        double v[kMmNodes];
-        int md[kMmNodes];
+      for (;;) {  // one load per open search per step
+        // (the search targets are recomputed each step rather than held: 14 more doubles would spill)
+        asm volatile("" : "+d"(base[0]), "+d"(base[1]), "+d"(off[0]), "+d"(off[1]));
+        double v[2][kMmNodes];
         bool active = false;
 #pragma unroll
-        for (int n = 0; n < kMmNodes; ++n) {
-          md[n] = (lo[n] + hi[n]) >> 1;
-          if (lo[n] < hi[n]) v[n] = p.prefix[(int64_t)md[n] * R + r], active = true;
-        }
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+          for (int n = 0; n < kMmNodes; ++n) {
+            const int lo = (int)(lh[q][n] & 0xffffu), hi = (int)(lh[q][n] >> 16);
+            if (lo < hi) v[q][n] = p.prefix[(int64_t)((lo + hi) >> 1) * R + rq[q]], active = true;
+          }
         if (!active) break;
 #pragma unroll
-        for (int n = 0; n < kMmNodes; ++n) {
-          if (lo[n] < hi[n]) {
-            if (v[n] + off < x[n]) lo[n] = md[n] + 1; else hi[n] = md[n];
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+          for (int n = 0; n < kMmNodes; ++n) {
+            const int lo = (int)(lh[q][n] & 0xffffu), hi = (int)(lh[q][n] >> 16);
+            if (lo < hi) {  // searchsorted's test, prefix + 2 r' < level - base - 1e-12 + 2 r'
+              const int md = (lo + hi) >> 1;
+              const double x = (mid[n] - base[q]) - 1e-12 + off[q];
+              lh[q][n] = v[q][n] + off[q] < x ? (uint32_t)(md + 1) | ((uint32_t)hi << 16)
+                                              : (uint32_t)lo | ((uint32_t)md << 16);
+            }
           }
-        }
       }
 #pragma unroll
-      for (int n = 0; n < kMmNodes; ++n) {
-        s_lbs[(size_t)r * kMmNodes + n] = (uint16_t)lo[n];
-        const double need = mid[n] - base;
-        sum[n] += need <= 1e-12 ? 0 : (lo[n] + 1 < m ? lo[n] + 1 : m);
+      for (int q = 0; q < 2; ++q) {
+        if (mq[q] < 0) continue;
+        const int r = rq[q], m = mq[q];
+#pragma unroll
+        for (int n = 0; n < kMmNodes; ++n) {
+          const int lo = (int)(lh[q][n] & 0xffffu);
+          s_lbs[(size_t)r * kMmNodes + n] = (uint16_t)lo;
+          const double need = mid[n] - base[q];
+          sum[n] += need <= 1e-12 ? 0 : (lo + 1 < m ? lo + 1 : m);
+        }
       }
     }
 #pragma unroll

@@ -14,8 +14,10 @@
 //     older block first), their shares in that order; the CTA that finishes last sets the budget and
 //     each request's index.
 //   mm_cumsum_kernel, a thread per row: the running sums, one addition after another as np.cumsum.
-//   mm_level_kernel, one CTA: the bisection (a binary search per request and a reduction per step)
-//     and the leftover blocks through a binary heap in shared memory. The row quotas it writes make
+//   mm_wide_kernel, a thread per (request, level): the first bisection steps' levels evaluated over
+//     every SM (the searches then span whole rows: one SM's loads would be the bottleneck).
+//   mm_level_kernel, one CTA: the rest of the bisection (a binary search per request and a reduction
+//     per step) and the leftover blocks through a binary heap in shared memory. The row quotas it writes make
 //     ekv_view_build (EKV_POLICY_UNIFORM: equal shares to the older block) keep exactly the reference's
 //     blocks.
 #include <type_traits>
@@ -33,10 +35,14 @@ constexpr int kMmBisection = 60;
 
 enum MmMode : int { kMmSelect = 0, kMmNone = 1, kMmAll = 2 };
 
+constexpr int kMmWideSteps = 6;                            // bisection steps of mm_wide_kernel
+constexpr int kMmWideNodes = (1 << kMmWideSteps) - 1;      // the levels they can probe
+
 struct MmState {
   long long must, blocks, total_open, free_;
   int mode;
   unsigned int ticket;
+  long long wide[kMmWideNodes];  // blocks the requests take at each of mm_wide_kernel's levels
 };
 
 struct MmParams {
@@ -57,12 +63,11 @@ struct MmParams {
   int* req;         // [rows] index of the request among the requests
   double* sorted;   // [width][rows] unpinned shares in decreasing order (block-major: a warp's rows adjacent)
   double* prefix;   // [width][rows] their running sums
-  int* lb_low;      // [rows] the search result at the bisection's low end
-  int* lb_high;     // [rows] ... and at its high end
+  uint16_t* wide_lbs;  // [kMmWideNodes][rows] each request's search result at mm_wide_kernel's levels
 };
 
 struct MmLayout {
-  size_t state, base, row_m, req, lb_low, lb_high, sorted, prefix, bytes;
+  size_t state, base, row_m, req, wide_lbs, sorted, prefix, bytes;
 };
 
 MmLayout mm_layout(int rows, int width) {
@@ -77,8 +82,7 @@ MmLayout mm_layout(int rows, int width) {
   l.base = take((size_t)rows * 8);
   l.row_m = take((size_t)rows * 4);
   l.req = take((size_t)rows * 4);
-  l.lb_low = take((size_t)rows * 4);
-  l.lb_high = take((size_t)rows * 4);
+  l.wide_lbs = take((size_t)rows * kMmWideNodes * 2);
   l.sorted = take((size_t)rows * width * 8);
   l.prefix = take((size_t)rows * width * 8);
   l.bytes = o;
@@ -360,6 +364,7 @@ __global__ void __launch_bounds__(32) mm_cumsum_kernel(const MmParams p) {
 // interleaved so their loads overlap.
 constexpr int kMmSpec = 3;
 constexpr int kMmNodes = (1 << kMmSpec) - 1;
+static_assert((kMmBisection - kMmWideSteps) % kMmSpec == 0, "whole rounds after the wide steps");
 constexpr int kMmLevelThreads = 512;
 constexpr int kMmAhead = 2;  // next shares per request staged in shared memory for the leftover blocks
 constexpr int kMmFewLeftovers = 64;  // up to this many leftover blocks: argmin per block, no heap
@@ -394,6 +399,55 @@ __host__ __device__ inline MmLevelSmem mm_level_smem(int rows) {
   l.start = take((size_t)rows * 4);
   l.bytes = o > bisection_end ? o : bisection_end;
   return l;
+}
+
+// Level of node n of the first kMmWideSteps steps' tree (node 0 the first step's level; node n's
+// children 2n + 1 when its level does not fit the budget, so `high` falls to it, and 2n + 2 when it
+// fits and `low` rises to it): the midpoints the sequential bisection computes on that path.
+__device__ __forceinline__ double mm_wide_level(int n) {
+  const int depth = 31 - __clz(n + 1);
+  double lo = 0.0, hi = 1.0;
+  for (int d = 0; d < depth; ++d) {
+    const double mid = (lo + hi) / 2;
+    if (((n + 1) >> (depth - d - 1)) & 1) lo = mid; else hi = mid;  // an even child: the level fit
+  }
+  return (lo + hi) / 2;
+}
+
+constexpr int kMmWideThreads = 256;
+
+// Grid (requests / kMmWideThreads, kMmWideNodes): thread (r, n) runs request r's search at node n's
+// level over its whole row, keeps the result for mm_level_kernel and adds the request's blocks to the
+// node's total.
+__global__ void __launch_bounds__(kMmWideThreads) mm_wide_kernel(const MmParams p) {
+  chain_release();
+  chain_wait();  // the running sums
+  __shared__ long long s_part[kMmWideThreads / 32];
+  if (p.state->mode != kMmSelect) return;
+  const int n = blockIdx.y, r = blockIdx.x * kMmWideThreads + threadIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const double level = mm_wide_level(n);
+  long long take = 0;
+  const int m = r < p.rows ? p.row_m[r] : -1;
+  if (m >= 0) {
+    const double base = p.base[r], off = 2.0 * (double)p.req[r];
+    const double x = (level - base) - 1e-12 + off;
+    int lo = 0, hi = m;
+    while (lo < hi) {  // the first j with prefix[j] + off >= x
+      const int md = (lo + hi) >> 1;
+      if (p.prefix[(int64_t)md * p.rows + r] + off < x) lo = md + 1; else hi = md;
+    }
+    p.wide_lbs[(size_t)n * p.rows + r] = (uint16_t)lo;
+    take = level - base <= 1e-12 ? 0 : (lo + 1 < m ? lo + 1 : m);
+  }
+  for (int o = 16; o > 0; o >>= 1) take += __shfl_xor_sync(kFullMask, take, o);
+  if (lane == 0) s_part[warp] = take;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    long long t = 0;
+    for (int w = 0; w < kMmWideThreads / 32; ++w) t += s_part[w];
+    atomicAdd(reinterpret_cast<unsigned long long*>(&p.state->wide[n]), (unsigned long long)t);
+  }
 }
 
 // One CTA: the water level, the leftover blocks and the quotas.
@@ -432,12 +486,26 @@ __global__ void __launch_bounds__(kMmLevelThreads) mm_level_kernel(const MmParam
     s_m[r] = m;
     s_base[r] = p.base[r];
     s_off[r] = 2.0 * (double)p.req[r];
-    s_lo[r] = 0;
-    s_hi[r] = m > 0 ? m : 0;
+  }
+  // the first kMmWideSteps steps: the path through mm_wide_kernel's levels, and each request's search
+  // results at the path's two ends
+  double low = 0.0, high = 1.0;
+  int wide_lo = -1, wide_hi = -1;
+  for (int d = 0, n = 0; d < kMmWideSteps; ++d) {
+    const double level = mm_wide_level(n);
+    if (__ldcg(&st->wide[n]) <= free_) {
+      low = level, wide_lo = n, n = 2 * n + 2;
+    } else {
+      high = level, wide_hi = n, n = 2 * n + 1;
+    }
+  }
+  for (int r = tid; r < p.rows; r += kMmLevelThreads) {
+    const int m = s_m[r];
+    s_lo[r] = m >= 0 && wide_lo >= 0 ? p.wide_lbs[(size_t)wide_lo * p.rows + r] : 0;
+    s_hi[r] = m >= 0 && wide_hi >= 0 ? p.wide_lbs[(size_t)wide_hi * p.rows + r] : (m > 0 ? m : 0);
   }
   __syncthreads();
-  double low = 0.0, high = 1.0;
-  for (int round = 0; round < kMmBisection / kMmSpec; ++round) {
+  for (int round = 0; round < (kMmBisection - kMmWideSteps) / kMmSpec; ++round) {
     // the levels of the tree: node n's children are 2n + 1 (its level did not fit: high = mid) and
     // 2n + 2 (it fit: low = mid); every thread builds the same tree
     double lo_v[kMmNodes], hi_v[kMmNodes], mid[kMmNodes];
@@ -688,8 +756,7 @@ static int allocate_maxmin(const S* scores, int64_t score_stride, const int32_t*
   p.row_m = reinterpret_cast<int*>(base + l.row_m);
   p.req = reinterpret_cast<int*>(base + l.req);
   p.sorted = reinterpret_cast<double*>(base + l.sorted);
-  p.lb_low = reinterpret_cast<int*>(base + l.lb_low);
-  p.lb_high = reinterpret_cast<int*>(base + l.lb_high);
+  p.wide_lbs = reinterpret_cast<uint16_t*>(base + l.wide_lbs);
   p.prefix = reinterpret_cast<double*>(base + l.prefix);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(base + l.state, 0, sizeof(MmState), s) != cudaSuccess)
@@ -722,6 +789,9 @@ static int allocate_maxmin(const S* scores, int64_t score_stride, const int32_t*
   if (rc != EKV_OK) return rc;
   launch_chained(mm_cumsum_kernel, dim3((rows + 31) / 32), dim3(32), kCsSmem, s, p);
   if ((rc = check_launch("mm_cumsum_kernel")) != EKV_OK) return rc;
+  launch_chained(mm_wide_kernel, dim3((rows + kMmWideThreads - 1) / kMmWideThreads, kMmWideNodes), dim3(kMmWideThreads),
+                 0, s, p);
+  if ((rc = check_launch("mm_wide_kernel")) != EKV_OK) return rc;
   launch_chained(mm_level_kernel, dim3(1), dim3(kMmLevelThreads), level_smem, s, p);
   return check_launch("mm_level_kernel");
 }

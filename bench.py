@@ -344,7 +344,7 @@ def view_bench(rank: int, world: int, steps: int, warmup: int, dist_on: bool) ->
     result["sglang_us"] = round(result["sglang_us"] - result.pop("sglang_restore_us"), 2)
     result["sglang_entries"] = entries
     result["sglang_launches"] = 4
-    for key, fn, launches in (("us", build, 1), ("sum_shared_us", build_shared, 10), ("maxmin_shared_us", build_maxmin, 4),
+    for key, fn, launches in (("us", build, 1), ("sum_shared_us", build_shared, 10), ("maxmin_shared_us", build_maxmin, 6),
                               ("newest_us", build_newest, 2), ("sum_shared_f64_us", build_shared64, 10)):
         graph = capture(fn)
         result[key] = round(timed(graph.replay, steps, warmup, dist_on) / steps * 1e6, 2)

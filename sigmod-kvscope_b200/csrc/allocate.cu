@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p
   const double w = p.weights ? p.weights[r] : 1.0;
   for (int i = tid; i < kSumBins; i += kSumThreads) s_hist[i] = 0;
   if (request) {
-    for (int i = tid; i < n; i += kSumThreads) s_x[i] = xg[i];
+    stage_row<kSumThreads>(s_x, xg, n);
     const double sum = block_pairwise_sum<kSumThreads>(s_tree, n, [&](int i) { return clamped(s_x[i]); });
     if (tid == 0) s_total = sum;
     __syncthreads();
@@ -293,10 +293,18 @@ __global__ void __launch_bounds__(kSumThreads) sum_keys_pass_kernel(const SumPar
   const int lo = 1 + blockIdx.x * kSumChunk, hi = min(lo + kSumChunk, ps);
   int above = 0;
   if (n > 0) {
-    for (int base = lo; base < hi; base += kSumThreads) {  // warp-uniform trip count
-      const int b = base + tid;
+    constexpr int kPer = kSumChunk / kSumThreads;  // keys a thread reads, all loads issued first
+    unsigned long long keys[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int b = lo + j * kSumThreads + tid;
+      keys[j] = b < hi ? kr[b] : 0ull;
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {  // warp-uniform trip count
+      const int b = lo + j * kSumThreads + tid;
       const bool in = b < hi;
-      const unsigned long long key = in ? kr[b] : 0ull;
+      const unsigned long long key = keys[j];
       // the prefix is pass 0's digit
       const unsigned long long top = key & (dmask0 << shift0);
       const bool cand = in && top == (prefix & (dmask0 << shift0));

@@ -723,7 +723,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditPar
     if (contributors == 0) {
       v = NAN;
     } else if (b < n) {
-      constexpr int U = 8;  // layers loaded before any is added, then added in layer order
+      constexpr int U = 32;  // layers loaded before any is added, then added in layer order
       for (int k0 = la; k0 < lb; k0 += U) {
         float x[U];
 #pragma unroll

@@ -68,6 +68,41 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Asynchronous global -> shared copies (cp.async): 4 and 8 bytes through L1, 16 bytes around it.
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// dst[0, n) = src[0, n) (elements of 4 or 8 bytes) into shared memory by every thread of the CTA, all
+// copies in flight at once (16 bytes a copy where both ends are 16-byte aligned); returns after a
+// barrier, with the row visible to the whole CTA.
+template <int THREADS, typename T>
+__device__ __forceinline__ void stage_row(T* dst, const T* src, int n) {
+  static_assert(sizeof(T) == 4 || sizeof(T) == 8, "4- or 8-byte elements");
+  constexpr int kPer = 16 / sizeof(T);
+  int done = 0;
+  if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+    done = n / kPer * kPer;
+    for (int i = kPer * threadIdx.x; i < done; i += kPer * THREADS) cp_async16(dst + i, src + i);
+  }
+  for (int i = done + threadIdx.x; i < n; i += THREADS) {
+    if constexpr (sizeof(T) == 4) cp_async4(dst + i, src + i); else cp_async8(dst + i, src + i);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+}
+
+
 __device__ __forceinline__ void set_status(uint32_t* status, uint32_t bits) {
   if (status != nullptr) atomicOr(status, bits);
 }

@@ -14,8 +14,9 @@
 //     older block first), their shares in that order; the CTA that finishes last sets the budget and
 //     each request's index.
 //   mm_cumsum_kernel, a thread per row: the running sums, one addition after another as np.cumsum.
-//   mm_wide_kernel, a thread per (request, level): the first bisection steps' levels evaluated over
-//     every SM (the searches then span whole rows: one SM's loads would be the bottleneck).
+//   mm_wide_kernel, a thread per (request, level), in stages of six steps: the first bisection steps'
+//     levels evaluated over every SM (their searches span most of a row: one SM's loads would be the
+//     bottleneck).
 //   mm_level_kernel, one CTA: the rest of the bisection (a binary search per request and a reduction
 //     per step) and the leftover blocks through a binary heap in shared memory. The row quotas it writes make
 //     ekv_view_build (EKV_POLICY_UNIFORM: equal shares to the older block) keep exactly the reference's
@@ -35,14 +36,15 @@ constexpr int kMmBisection = 60;
 
 enum MmMode : int { kMmSelect = 0, kMmNone = 1, kMmAll = 2 };
 
-constexpr int kMmWideSteps = 6;                            // bisection steps of mm_wide_kernel
+constexpr int kMmWideSteps = 6;                            // bisection steps of one mm_wide_kernel stage
 constexpr int kMmWideNodes = (1 << kMmWideSteps) - 1;      // the levels they can probe
+constexpr int kMmWideStages = 2;                           // stages before the single CTA's rounds
 
 struct MmState {
   long long must, blocks, total_open, free_;
   int mode;
   unsigned int ticket;
-  long long wide[kMmWideNodes];  // blocks the requests take at each of mm_wide_kernel's levels
+  long long wide[kMmWideStages * kMmWideNodes];  // blocks the requests take at each wide level
 };
 
 struct MmParams {
@@ -63,7 +65,7 @@ struct MmParams {
   int* req;         // [rows] index of the request among the requests
   double* sorted;   // [width][rows] unpinned shares in decreasing order (block-major: a warp's rows adjacent)
   double* prefix;   // [width][rows] their running sums
-  uint16_t* wide_lbs;  // [kMmWideNodes][rows] each request's search result at mm_wide_kernel's levels
+  uint16_t* wide_lbs;  // [kMmWideStages * kMmWideNodes][rows] each request's search result at the wide levels
 };
 
 struct MmLayout {
@@ -82,7 +84,7 @@ MmLayout mm_layout(int rows, int width) {
   l.base = take((size_t)rows * 8);
   l.row_m = take((size_t)rows * 4);
   l.req = take((size_t)rows * 4);
-  l.wide_lbs = take((size_t)rows * kMmWideNodes * 2);
+  l.wide_lbs = take((size_t)rows * kMmWideStages * kMmWideNodes * 2);
   l.sorted = take((size_t)rows * width * 8);
   l.prefix = take((size_t)rows * width * 8);
   l.bytes = o;
@@ -226,7 +228,7 @@ __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
   if (request) {
     const S* xg = static_cast<const S*>(p.scores) +
                   (p.score_rows != nullptr ? (int64_t)p.score_rows[r] : (int64_t)r) * p.score_s0;
-    for (int i = tid; i < n; i += kMmThreads) s_x[i] = xg[i];
+    stage_row<kMmThreads>(s_x, xg, n);
     const double total = block_pairwise_sum<kMmThreads>(s_tree, n, [&](int i) { return mm_clamped(s_x[i]); });
     const double equal = __ddiv_rn(1.0, (double)(n > 1 ? n : 1));
     auto share = [&](int i) { return total > 0.0 ? __ddiv_rn(mm_clamped(s_x[i]), total) : equal; };
@@ -297,10 +299,6 @@ constexpr int kCsChunk = 32;   // shares of a row per stage
 constexpr int kCsStages = 8;   // stages in the ring: 7 in flight while one is added up
 constexpr size_t kCsSmem = (size_t)kCsStages * kCsChunk * 32 * sizeof(double);
 
-__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-
 __global__ void __launch_bounds__(32) mm_cumsum_kernel(const MmParams p) {
   chain_release();
   chain_wait();  // what the launch before this one wrote
@@ -364,7 +362,7 @@ __global__ void __launch_bounds__(32) mm_cumsum_kernel(const MmParams p) {
 // interleaved so their loads overlap.
 constexpr int kMmSpec = 3;
 constexpr int kMmNodes = (1 << kMmSpec) - 1;
-static_assert((kMmBisection - kMmWideSteps) % kMmSpec == 0, "whole rounds after the wide steps");
+static_assert((kMmBisection - kMmWideStages * kMmWideSteps) % kMmSpec == 0, "whole rounds after the wide steps");
 constexpr int kMmLevelThreads = 512;
 constexpr int kMmAhead = 2;  // next shares per request staged in shared memory for the leftover blocks
 constexpr int kMmFewLeftovers = 64;  // up to this many leftover blocks: argmin per block, no heap
@@ -401,12 +399,11 @@ __host__ __device__ inline MmLevelSmem mm_level_smem(int rows) {
   return l;
 }
 
-// Level of node n of the first kMmWideSteps steps' tree (node 0 the first step's level; node n's
-// children 2n + 1 when its level does not fit the budget, so `high` falls to it, and 2n + 2 when it
-// fits and `low` rises to it): the midpoints the sequential bisection computes on that path.
-__device__ __forceinline__ double mm_wide_level(int n) {
+// Level of node n of a stage's tree whose first step splits [lo, hi] (node n's children: 2n + 1 when
+// its level does not fit the budget, so `high` falls to it, and 2n + 2 when it fits and `low` rises to
+// it): the midpoints the sequential bisection computes on that path.
+__device__ __forceinline__ double mm_tree_level(int n, double lo, double hi) {
   const int depth = 31 - __clz(n + 1);
-  double lo = 0.0, hi = 1.0;
   for (int d = 0; d < depth; ++d) {
     const double mid = (lo + hi) / 2;
     if (((n + 1) >> (depth - d - 1)) & 1) lo = mid; else hi = mid;  // an even child: the level fit
@@ -414,30 +411,57 @@ __device__ __forceinline__ double mm_wide_level(int n) {
   return (lo + hi) / 2;
 }
 
+// The bisection through the wide stages [0, stages): low and high after their steps, and the wide
+// levels (indices into the stages' nodes) of the last step that fit and the last that did not (-1:
+// none).
+struct MmWalk {
+  double low, high;
+  int lo_node, hi_node;
+};
+
+__device__ __forceinline__ MmWalk mm_wide_walk(const MmState* st, int stages) {
+  MmWalk w{0.0, 1.0, -1, -1};
+  const long long free_ = __ldcg(&st->free_);
+  for (int g = 0; g < stages; ++g) {
+    for (int d = 0, n = 0; d < kMmWideSteps; ++d) {
+      const double level = (w.low + w.high) / 2;
+      if (__ldcg(&st->wide[g * kMmWideNodes + n]) <= free_) {
+        w.low = level, w.lo_node = g * kMmWideNodes + n, n = 2 * n + 2;
+      } else {
+        w.high = level, w.hi_node = g * kMmWideNodes + n, n = 2 * n + 1;
+      }
+    }
+  }
+  return w;
+}
+
 constexpr int kMmWideThreads = 256;
 
-// Grid (requests / kMmWideThreads, kMmWideNodes): thread (r, n) runs request r's search at node n's
-// level over its whole row, keeps the result for mm_level_kernel and adds the request's blocks to the
+// Stage g, grid (requests / kMmWideThreads, kMmWideNodes): thread (r, n) walks the earlier stages'
+// decisions, runs request r's search at node n's level between its results at the walk's two ends,
+// keeps the result for the later stages and mm_level_kernel and adds the request's blocks to the
 // node's total.
-__global__ void __launch_bounds__(kMmWideThreads) mm_wide_kernel(const MmParams p) {
+__global__ void __launch_bounds__(kMmWideThreads) mm_wide_kernel(const MmParams p, int g) {
   chain_release();
-  chain_wait();  // the running sums
+  chain_wait();  // the running sums, the earlier stages' totals
   __shared__ long long s_part[kMmWideThreads / 32];
   if (p.state->mode != kMmSelect) return;
   const int n = blockIdx.y, r = blockIdx.x * kMmWideThreads + threadIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const double level = mm_wide_level(n);
+  const MmWalk w = mm_wide_walk(p.state, g);
+  const double level = mm_tree_level(n, w.low, w.high);
   long long take = 0;
   const int m = r < p.rows ? p.row_m[r] : -1;
   if (m >= 0) {
     const double base = p.base[r], off = 2.0 * (double)p.req[r];
     const double x = (level - base) - 1e-12 + off;
-    int lo = 0, hi = m;
+    int lo = w.lo_node >= 0 ? p.wide_lbs[(size_t)w.lo_node * p.rows + r] : 0;
+    int hi = w.hi_node >= 0 ? p.wide_lbs[(size_t)w.hi_node * p.rows + r] : m;
     while (lo < hi) {  // the first j with prefix[j] + off >= x
       const int md = (lo + hi) >> 1;
       if (p.prefix[(int64_t)md * p.rows + r] + off < x) lo = md + 1; else hi = md;
     }
-    p.wide_lbs[(size_t)n * p.rows + r] = (uint16_t)lo;
+    p.wide_lbs[(size_t)(g * kMmWideNodes + n) * p.rows + r] = (uint16_t)lo;
     take = level - base <= 1e-12 ? 0 : (lo + 1 < m ? lo + 1 : m);
   }
   for (int o = 16; o > 0; o >>= 1) take += __shfl_xor_sync(kFullMask, take, o);
@@ -445,8 +469,8 @@ __global__ void __launch_bounds__(kMmWideThreads) mm_wide_kernel(const MmParams 
   __syncthreads();
   if (threadIdx.x == 0) {
     long long t = 0;
-    for (int w = 0; w < kMmWideThreads / 32; ++w) t += s_part[w];
-    atomicAdd(reinterpret_cast<unsigned long long*>(&p.state->wide[n]), (unsigned long long)t);
+    for (int k = 0; k < kMmWideThreads / 32; ++k) t += s_part[k];
+    atomicAdd(reinterpret_cast<unsigned long long*>(&p.state->wide[g * kMmWideNodes + n]), (unsigned long long)t);
   }
 }
 
@@ -487,25 +511,17 @@ __global__ void __launch_bounds__(kMmLevelThreads) mm_level_kernel(const MmParam
     s_base[r] = p.base[r];
     s_off[r] = 2.0 * (double)p.req[r];
   }
-  // the first kMmWideSteps steps: the path through mm_wide_kernel's levels, and each request's search
-  // results at the path's two ends
-  double low = 0.0, high = 1.0;
-  int wide_lo = -1, wide_hi = -1;
-  for (int d = 0, n = 0; d < kMmWideSteps; ++d) {
-    const double level = mm_wide_level(n);
-    if (__ldcg(&st->wide[n]) <= free_) {
-      low = level, wide_lo = n, n = 2 * n + 2;
-    } else {
-      high = level, wide_hi = n, n = 2 * n + 1;
-    }
-  }
+  // the wide stages' steps: the path through their levels, and each request's search results at the
+  // path's two ends
+  const MmWalk walk = mm_wide_walk(st, kMmWideStages);
+  double low = walk.low, high = walk.high;
   for (int r = tid; r < p.rows; r += kMmLevelThreads) {
     const int m = s_m[r];
-    s_lo[r] = m >= 0 && wide_lo >= 0 ? p.wide_lbs[(size_t)wide_lo * p.rows + r] : 0;
-    s_hi[r] = m >= 0 && wide_hi >= 0 ? p.wide_lbs[(size_t)wide_hi * p.rows + r] : (m > 0 ? m : 0);
+    s_lo[r] = m >= 0 && walk.lo_node >= 0 ? p.wide_lbs[(size_t)walk.lo_node * p.rows + r] : 0;
+    s_hi[r] = m >= 0 && walk.hi_node >= 0 ? p.wide_lbs[(size_t)walk.hi_node * p.rows + r] : (m > 0 ? m : 0);
   }
   __syncthreads();
-  for (int round = 0; round < (kMmBisection - kMmWideSteps) / kMmSpec; ++round) {
+  for (int round = 0; round < (kMmBisection - kMmWideStages * kMmWideSteps) / kMmSpec; ++round) {
     // the levels of the tree: node n's children are 2n + 1 (its level did not fit: high = mid) and
     // 2n + 2 (it fit: low = mid); every thread builds the same tree
     double lo_v[kMmNodes], hi_v[kMmNodes], mid[kMmNodes];
@@ -604,7 +620,7 @@ __global__ void __launch_bounds__(kMmLevelThreads) mm_level_kernel(const MmParam
       if (lo_node >= 0) s_lo[r] = s_lbs[(size_t)r * kMmNodes + lo_node];
       if (hi_node >= 0) s_hi[r] = s_lbs[(size_t)r * kMmNodes + hi_node];
     }
-    // (the next round's first barrier comes after every thread's last read of s_tot and s_lbs here)
+    // (the next bisection round's first barrier comes after every thread's last read of s_tot and s_lbs here)
   }
   long long used = 0;
   for (int r = tid; r < p.rows; r += kMmLevelThreads) {  // the blocks each request takes at `low`
@@ -789,9 +805,11 @@ static int allocate_maxmin(const S* scores, int64_t score_stride, const int32_t*
   if (rc != EKV_OK) return rc;
   launch_chained(mm_cumsum_kernel, dim3((rows + 31) / 32), dim3(32), kCsSmem, s, p);
   if ((rc = check_launch("mm_cumsum_kernel")) != EKV_OK) return rc;
-  launch_chained(mm_wide_kernel, dim3((rows + kMmWideThreads - 1) / kMmWideThreads, kMmWideNodes), dim3(kMmWideThreads),
-                 0, s, p);
-  if ((rc = check_launch("mm_wide_kernel")) != EKV_OK) return rc;
+  for (int g = 0; g < kMmWideStages; ++g) {
+    launch_chained(mm_wide_kernel, dim3((rows + kMmWideThreads - 1) / kMmWideThreads, kMmWideNodes),
+                   dim3(kMmWideThreads), 0, s, p, g);
+    if ((rc = check_launch("mm_wide_kernel")) != EKV_OK) return rc;
+  }
   launch_chained(mm_level_kernel, dim3(1), dim3(kMmLevelThreads), level_smem, s, p);
   return check_launch("mm_level_kernel");
 }

@@ -229,16 +229,6 @@ __device__ __forceinline__ uint32_t share_key(float x) {
   return x > 0.f ? __float_as_uint(x) : 0u;
 }
 
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 // n 32-bit words from global to shared memory (16-byte aligned) without blocking the thread.
 __device__ __forceinline__ void stage_words(uint32_t* dst, const uint32_t* src, int n) {
   int done = 0;

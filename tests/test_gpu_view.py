@@ -193,6 +193,34 @@ def test_maxmin_leftover_blocks_by_argmin_and_by_heap():
     assert {"few", "many"} <= seen, seen
 
 
+def test_plan_view_maxmin_at_the_view_stress_size_matches_the_controller():
+    """1024 requests of up to 8192 blocks (the bench's shape): every bisection stage, searches over
+    whole rows and the full sort, against the oracle's controller pipeline."""
+    from ekv.runtime.block_view import plan_view
+
+    rng = np.random.default_rng(73)
+    rows, width = 1024, 8192
+    row_blocks = rng.integers(1, width + 1, rows).astype(np.int32)
+    lens = (row_blocks * 16 - rng.integers(0, 16, rows)).astype(np.int32)
+    table = rng.integers(0, 1 << 20, (rows, width)).astype(np.int32)
+    scores = rng.dirichlet(np.full(width, 0.3), rows).astype(np.float32)
+    scores[3, :] = 0.0  # a request without evidence: equal shares
+    for fraction in (0.2, 0.5):
+        keep = oa.controller_keep(row_blocks, width, lambda r, n: scores[r, :n].astype(np.float64), fraction,
+                                  "maxmin", recent_blocks=4)
+        mask = torch.empty(rows, width, dtype=torch.uint8).cuda()
+        view, view_lens = plan_view(
+            torch.from_numpy(table).cuda(), torch.from_numpy(lens).cuda(), 16, torch.from_numpy(row_blocks).cuda(),
+            scores=torch.from_numpy(scores).cuda(), policy="maxmin", budget_fraction=fraction, recent_blocks=4,
+            mask_out=mask)
+        got = mask.cpu().numpy().astype(bool)
+        inside = np.arange(width)[None, :] < row_blocks[:, None]
+        np.testing.assert_array_equal(got & inside, keep.astype(bool) & inside, err_msg=f"fraction {fraction}")
+        ref_view, ref_lens = ov.compact_block_table(table, lens, keep.astype(bool), 16)
+        np.testing.assert_array_equal(view.cpu().numpy(), ref_view, err_msg=f"fraction {fraction}")
+        np.testing.assert_array_equal(view_lens.cpu().numpy(), ref_lens, err_msg=f"fraction {fraction}")
+
+
 def test_plan_view_maxmin_with_a_shared_budget_matches_the_controller():
     from ekv.runtime.block_view import plan_view
 

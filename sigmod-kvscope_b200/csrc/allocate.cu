@@ -480,8 +480,10 @@ __global__ void __launch_bounds__(1024) sum_quota_kernel(const SumParams p) {
 // The committed mask straight from the threshold, without ranking any row: block b of request r is
 // kept when it is pinned (block 0 and [ps, n)), past the request, or unpinned with a gain key above the
 // threshold, or equal to it at an index above i*, or at i* when the row's tie there is taken. Grid
-// (width / kSumMaskSpan, rows); four positions per thread.
-constexpr int kSumMaskSpan = 4 * kSumThreads;
+// (width / kSumMaskSpan, rows); a thread takes kSumMaskGroups groups of four adjacent positions, every
+// key loaded before any is used (fewer, fuller CTAs: the pass is a single wave of loads, not several).
+constexpr int kSumMaskGroups = 4;
+constexpr int kSumMaskSpan = 4 * kSumMaskGroups * kSumThreads;
 __global__ void __launch_bounds__(kSumThreads) sum_mask_kernel(const SumParams p) {
   chain_release();
   chain_wait();  // what the launch before this one wrote
@@ -494,23 +496,41 @@ __global__ void __launch_bounds__(kSumThreads) sum_mask_kernel(const SumParams p
   const bool take = p.row_at[r] != 0;
   const unsigned long long* kr = p.keys + (int64_t)r * p.width;
   uint8_t* out = p.mask_out + (int64_t)r * p.mask_s0;
-  const int b0 = blockIdx.x * kSumMaskSpan + 4 * threadIdx.x;
+  const int c0 = blockIdx.x * kSumMaskSpan + 4 * threadIdx.x;  // group g starts at c0 + g * 4 * kSumThreads
+  unsigned long long km[kSumMaskGroups][4];  // (predicated loads, no early exit between them)
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int b = b0 + j;
-    if (b >= p.width) break;
-    bool keep = true;  // not a request, a pin, or past the request
-    if (n > 0 && b >= 1 && b < ps) {
-      if (mode == kSumAll) {
-        keep = true;
-      } else if (mode == kSumNone) {
-        keep = false;
-      } else {
-        const unsigned long long km = kr[b] & mask;
-        keep = km > prefix || (km == prefix && (b > istar || (b == istar && take)));
-      }
+  for (int g = 0; g < kSumMaskGroups; ++g)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int b = c0 + g * 4 * kSumThreads + j;
+      const bool ranked = mode == kSumSelect && n > 0 && b >= 1 && b < ps && b < p.width;
+      km[g][j] = ranked ? kr[b] & mask : 0ull;
     }
-    out[b] = keep ? 1 : 0;
+#pragma unroll
+  for (int g = 0; g < kSumMaskGroups; ++g) {
+    const int b0 = c0 + g * 4 * kSumThreads;
+    uint32_t bytes = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int b = b0 + j;
+      bool keep = true;  // not a request, a pin, or past the request
+      if (n > 0 && b >= 1 && b < ps) {
+        if (mode == kSumAll) {
+          keep = true;
+        } else if (mode == kSumNone) {
+          keep = false;
+        } else {
+          const unsigned long long k = km[g][j];
+          keep = k > prefix || (k == prefix && (b > istar || (b == istar && take)));
+        }
+      }
+      bytes |= (keep ? 1u : 0u) << (8 * j);
+    }
+    if (b0 + 4 <= p.width && (reinterpret_cast<uintptr_t>(out + b0) & 3) == 0) {
+      *reinterpret_cast<uint32_t*>(out + b0) = bytes;
+    } else {
+      for (int j = 0; j < 4 && b0 + j < p.width; ++j) out[b0 + j] = (uint8_t)(bytes >> (8 * j));
+    }
   }
 }
 

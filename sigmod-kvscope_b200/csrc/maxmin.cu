@@ -18,9 +18,9 @@
 //     levels evaluated over every SM (their searches span most of a row: one SM's loads would be the
 //     bottleneck).
 //   mm_level_kernel, one CTA: the rest of the bisection (a binary search per request and a reduction
-//     per step) and the leftover blocks through a binary heap in shared memory. The row quotas it writes make
-//     ekv_view_build (EKV_POLICY_UNIFORM: equal shares to the older block) keep exactly the reference's
-//     blocks.
+//     per step) and the leftover blocks through a binary heap in shared memory. The row quotas it
+//     writes make ekv_view_build (EKV_POLICY_UNIFORM: equal shares to the older block) keep exactly
+//     the reference's blocks.
 #include <type_traits>
 
 #include "ekv_common.cuh"
@@ -358,8 +358,9 @@ __global__ void __launch_bounds__(32) mm_cumsum_kernel(const MmParams p) {
 // probe (a binary tree: a step that fits the budget raises `low`, else it lowers `high`) are evaluated
 // together, then the path through them is taken. Each evaluation is, per request, the searchsorted of
 // allocation.py:146-150 -- the first j with prefix[j] + offset >= x -- confined to the request's
-// results at the round's two ends (the result grows with the level), the 2^S - 1 searches of a request
-// interleaved so their loads overlap.
+// results at the round's two ends (the result grows with the level). mm_wide_kernel takes the first
+// kMmWideStages * kMmWideSteps steps over the whole GPU; mm_level_kernel, one CTA, the rest, its
+// threads running the 2^S - 1 searches of two requests each side by side so their loads overlap.
 constexpr int kMmSpec = 3;
 constexpr int kMmNodes = (1 << kMmSpec) - 1;
 static_assert((kMmBisection - kMmWideStages * kMmWideSteps) % kMmSpec == 0, "whole rounds after the wide steps");

@@ -175,7 +175,14 @@ class RecordingPlane(AuditPlane):
         return sorted(self._layer_of, key=lambda name: self._layer_of[name])
 
     def select(self, audited: np.ndarray, token_start: np.ndarray) -> None:
-        """Choose the rows to record in the next step, and the token index of each row's query."""
+        """Choose the rows to record in the next step, and the token index of each row's query
+        (runtime/audit_kernel.py:190-194: the first ``len(audited)`` rows change, the rest keep their
+        values; shapes that torch's copy would refuse raise RuntimeError).
+
+        Unlike the reference's two pageable copies, which block the host, both arrays go to the device
+        in one asynchronous copy on the current stream from a pinned staging buffer: work launched on
+        that stream afterwards sees them. Two staging buffers alternate; a call waits only for the copy
+        made from its buffer two calls earlier."""
         audited = np.asarray(audited)
         rows = len(audited)
         try:  # the shapes torch's copy into the first `rows` rows accepts

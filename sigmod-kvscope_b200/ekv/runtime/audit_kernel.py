@@ -181,8 +181,9 @@ class RecordingPlane(AuditPlane):
 
         Unlike the reference's two pageable copies, which block the host, both arrays go to the device
         in one asynchronous copy on the current stream from a pinned staging buffer: work launched on
-        that stream afterwards sees them. Two staging buffers alternate; a call waits only for the copy
-        made from its buffer two calls earlier."""
+        that stream afterwards sees them; a caller that records on another stream orders it after this
+        one first (``other.wait_stream(torch.cuda.current_stream())``). Two staging buffers alternate; a
+        call waits only for the copy made from its buffer two calls earlier."""
         audited = np.asarray(audited)
         rows = len(audited)
         try:  # the shapes torch's copy into the first `rows` rows accepts

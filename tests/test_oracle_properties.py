@@ -67,3 +67,23 @@ def test_oracle_allocation_keeps_the_pins_spends_the_budget_and_keeps_the_order(
         flags = table[order, 3].astype(bool)
         n_kept = int(flags.sum())
         assert flags[:n_kept].all() and not flags[n_kept:].any(), (trial, weights is not None)
+
+
+@pytest.mark.parametrize("objective", ["sum", "uniform", "maxmin"])
+def test_oracle_controller_keep_spends_the_controller_budget(objective):
+    """controller.py:420-437: measured rows (longer than the cap) share max(pins, ceil(f * blocks));
+    every other row, and every position past a row's length, is kept."""
+    rng = np.random.default_rng(211 + len(objective))
+    rows, width = 256, 4096
+    row_blocks = rng.integers(0, width + 1, rows).astype(np.int32)
+    scores = rng.dirichlet(np.full(width, 0.3), rows).astype(np.float32)
+    for fraction, cap in ((0.2, 0), (0.5, 64), (0.9, 0)):
+        keep = oa.controller_keep(row_blocks, width, lambda r, n: scores[r, :n].astype(np.float64), fraction,
+                                  objective, recent_blocks=4, cap_above_blocks=cap)
+        chosen = (row_blocks > cap) & (row_blocks > 0)
+        inside = np.arange(width)[None, :] < row_blocks[:, None]
+        assert keep[~chosen].all() and keep[~inside].all()
+        total = int(row_blocks[chosen].sum())
+        pins = sum(int(oa.controller_pins(int(n), 4).sum()) for n in row_blocks[chosen])
+        want = min(total, max(pins, int(np.ceil(fraction * total))))
+        assert int(keep[inside & chosen[:, None]].sum()) == want, (fraction, cap)

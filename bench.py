@@ -432,9 +432,13 @@ def reference_arm(args, cfg: dict) -> None:
             rates.append(units / sec)
     value = statistics.median(rates)
     per_step = [{"kind": "port", "cores": sample.threads, "sample": sample.describe(units)}]
+    # one whole-job step of the workload (every rank's heads of every layer) at that rate
+    heads_all = args.gpus if args.mode == "reference" else cfg["kv_heads"]
+    step_units = int(sample.lens.astype(np.int64).sum()) * cfg["layers"] * heads_all
     line = {
         "impl": "reference", "metric": "audited KV tokens/s", "value": value, "unit": "audited KV tokens/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_units / value * 1e3, "higher_is_better": True,
         "scaling": "weak", "dtype": "bf16", "data": "synthetic",
         "config": {"workload": args.config, "mode": args.mode, "rows": cfg["rows"], "layers": cfg["layers"]},
         "cpu_baseline": {k: per_step[-1][k] for k in ("kind", "cores", "sample")} | {"value": value,

@@ -7,14 +7,19 @@
 One step is one audit step of the configured model over synthetic seeded inputs: the audit kernel
 for every layer (captured in one CUDA graph, as the engine captures its decode step), which also
 leaves the exact per-block shares on the device; with N > 1 ranks (one per GPU, KV heads split over
-the ranks) one NCCL all-reduce combines the ranks' shares. ``value`` is whole-job audited KV tokens/s
-(one token = one (row, position, layer, audited KV head) key vector) with inputs resident in HBM;
-``e2e`` is the same through the public API with the step's host inputs copied in from pinned memory
-and its shares copied out every step. ``view`` times the block-view build of the view stress shape
-(1024 rows x 8192 blocks, per-row `sum` budgets), row-sharded over the ranks.
+the ranks) one NCCL all-reduce averages the ranks' shares, captured in the step's graph and run while
+the next step records (two share buffers alternate; the last step's all-reduce runs inside the timed
+region too). ``value`` is whole-job audited KV tokens/s (one token = one (row, position, layer,
+audited KV head) key vector) with inputs resident in HBM; ``e2e`` is the same through the public API
+with the step's host inputs copied in from pinned memory and its shares copied out every step.
+``view`` times the block-view build of the view stress shape (1024 rows x 8192 blocks, per-row `sum`
+budgets), row-sharded over the ranks. ``strong_70b`` times the Llama-3-70B-shaped step in all-heads
+mode (every KV head of every layer, split over the ranks: a fixed total, strong scaling). ``parity``
+checks sampled rows of the final (rank-combined) shares against the oracle run on each rank's own
+inputs, after the timed regions.
 
 ``--impl reference`` times the reference algorithm on the host cores instead (the C restatement of
-the reference kernel in oracle/, all threads), on a bounded sample of the same workload.
+the reference kernel in oracle/, every host thread), on a bounded sample of the same workload.
 """
 
 from __future__ import annotations
@@ -56,6 +61,8 @@ CONFIGS = {
 # --pools 1`: one 2.6 GB pool, every layer a head of its own) scaled by 4, the traffic growing with the
 # layers (every layer reads its own keys once).
 NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"llama8b": 4 * (614.871e6 + 5.805e6)}
+NCU_TRAFFIC_SOURCE = ("ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum of the record kernel, "
+                      "bench.py --layers 8 --pools 1 (8 of the 32 layers), scaled by 4; profiles/record_kernel_llama8b.md")
 
 
 def lengths(spec, rows: int, rng: np.random.Generator) -> np.ndarray:
@@ -80,8 +87,16 @@ def measured_peak() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
+def host_threads() -> int:
+    """Every host core this process may run on (not OMP_NUM_THREADS, which torchrun sets to 1)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 class ClockSampler:
-    """nvidia-smi clock and throttle samples every 100 ms during the timed region."""
+    """nvidia-smi clock and throttle samples every 100 ms while the sampler is open."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -130,10 +145,35 @@ class ClockSampler:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "span": "warm-up through the last timed section"}
 
 
 # ---- the workload -------------------------------------------------------------------------------------
+
+
+def plan(cfg: dict, mode: str, world: int) -> dict:
+    """What a rank's workload holds, computed on the host alone (both arms report the same config)."""
+    if cfg["kv_heads"] % world:
+        raise SystemExit(f"{cfg['kv_heads']} KV heads do not split over {world} GPUs")
+    lens = lengths(cfg["lens"], cfg["rows"], np.random.default_rng(0)).astype(np.int32)
+    kv_local = cfg["kv_heads"] // world
+    heads = kv_local if mode == "all-heads" else 1
+    # reference mode: a layer audits one KV head, head layer % kv_heads (the reference's rule), so
+    # ceil(layers / kv_heads) pools give every layer keys of its own, as a model's layers have; all-heads
+    # mode reads every head of a layer's pool and cycles over the configured pools
+    pools = cfg["pools"] if mode == "all-heads" or cfg.get("pools_fixed") else -(-cfg["layers"] // kv_local)
+    return dict(lens=lens, kv_local=kv_local, heads=heads, pools=pools, width=int(math.ceil(lens.max() / BLOCK)),
+                units_rank=int(lens.astype(np.int64).sum()) * cfg["layers"] * heads)
+
+
+def line_config(name: str, cfg: dict, mode: str, record: str, world: int) -> dict:
+    p = plan(cfg, mode, world)
+    return {"workload": name, "mode": mode, "record": record, "rows": cfg["rows"], "layers": cfg["layers"],
+            "q_heads": cfg["q_heads"], "kv_heads": cfg["kv_heads"], "kv_heads_per_gpu": p["kv_local"],
+            "audited_heads_per_layer_per_gpu": p["heads"], "block_size": BLOCK, "tile_blocks": TILE_BLOCKS,
+            "mean_len": float(p["lens"].mean()), "width": p["width"], "pools": p["pools"],
+            "l2": f"inputs larger than L2: {p['units_rank'] / cfg['layers'] * 256 / 1e6:.0f} MB of keys per launch",
+            "parallelism": f"tp{world} (KV heads)"}
 
 
 class Workload:
@@ -143,13 +183,12 @@ class Workload:
         self.cfg = cfg
         self.rows, self.layers = cfg["rows"], cfg["layers"]
         self.group_rows = cfg["q_heads"] // cfg["kv_heads"]
-        if cfg["kv_heads"] % world:
-            raise SystemExit(f"{cfg['kv_heads']} KV heads do not split over {world} GPUs")
-        self.kv_local = cfg["kv_heads"] // world
-        self.heads = self.kv_local if mode == "all-heads" else 1
+        p = plan(cfg, mode, world)
+        self.kv_local, self.heads = p["kv_local"], p["heads"]
         rng = np.random.default_rng(seed)  # identical on every rank: one batch, heads split
         self.lens = lengths(cfg["lens"], self.rows, rng).astype(np.int32)
-        self.width = int(math.ceil(self.lens.max() / BLOCK))
+        assert np.array_equal(self.lens, p["lens"])
+        self.width = p["width"]
         blocks = -(-self.lens // BLOCK)
         pool = max(cfg["pool"], int(blocks.sum()) + 1)
         self.pool = pool
@@ -163,13 +202,9 @@ class Workload:
         self.table_host = table
         dev = torch.device("cuda", torch.cuda.current_device())
         gen = torch.Generator(device=dev).manual_seed(1000 + rank)
-        # reference mode: a layer audits one KV head, head layer % kv_heads (the reference's rule), so
-        # ceil(layers / kv_heads) pools give every layer keys of its own, as a model's layers have; all-heads
-        # mode reads every head of a layer's pool and cycles over the configured pools
-        n_pools = cfg["pools"] if mode == "all-heads" or cfg.get("pools_fixed") else -(-self.layers // self.kv_local)
         self.caches = [
             torch.randn(pool, 2, BLOCK, self.kv_local, HEAD_DIM, device=dev, generator=gen, dtype=torch.bfloat16)
-            for _ in range(n_pools)
+            for _ in range(p["pools"])
         ]
         tokens = self.rows
         self.queries = [  # every layer's query of the step, resident in HBM
@@ -188,12 +223,15 @@ class Workload:
     def units_per_step(self) -> int:
         return int(self.lens.astype(np.int64).sum()) * self.layers * self.heads
 
-    def cache(self, layer: int) -> torch.Tensor:
-        """The KV pool of a layer. In reference mode layer l reads head l % kv_heads of pool
-        l // kv_heads: no two layers read the same keys, so no read is served from L2 by another layer's."""
+    def pool_index(self, layer: int) -> int:
+        """In reference mode layer l reads head l % kv_heads of pool l // kv_heads: no two layers read the
+        same keys, so no read is served from L2 by another layer's."""
         if self.heads > 1 or self.cfg.get("pools_fixed"):
-            return self.caches[layer % len(self.caches)]
-        return self.caches[(layer // self.kv_local) % len(self.caches)]
+            return layer % len(self.caches)
+        return (layer // self.kv_local) % len(self.caches)
+
+    def cache(self, layer: int) -> torch.Tensor:
+        return self.caches[self.pool_index(layer)]
 
     def keys(self, layer: int) -> torch.Tensor:
         return self.cache(layer)[:, 0]
@@ -240,12 +278,15 @@ def capture(fn) -> torch.cuda.CUDAGraph:
     return graph
 
 
-def timed(fn, steps: int, warmup: int, dist_on: bool) -> float:
-    """Seconds for `steps` calls of fn, max over ranks; CUDA events on the current stream."""
+def timed(fn, steps: int, warmup: int, dist_on: bool, finish=None) -> float:
+    """Seconds for `steps` calls of fn (then `finish`, inside the timed region), max over ranks; CUDA
+    events on the current stream."""
     import torch.distributed as dist
 
     for _ in range(warmup):
         fn()
+    if finish is not None:
+        finish()
     torch.cuda.synchronize()
     if dist_on:
         dist.barrier()
@@ -254,6 +295,8 @@ def timed(fn, steps: int, warmup: int, dist_on: bool) -> float:
     start.record()
     for _ in range(steps):
         fn()
+    if finish is not None:
+        finish()
     end.record()
     torch.cuda.synchronize()
     seconds = start.elapsed_time(end) / 1e3
@@ -263,6 +306,102 @@ def timed(fn, steps: int, warmup: int, dist_on: bool) -> float:
         dist.barrier()
         seconds = float(t.item())
     return seconds
+
+
+class Stepper:
+    """One audit step as the timed loop calls it: a CUDA graph on one rank; with ranks, the graphs of a
+    StepCombiner (this step recorded, the previous step's shares combined) and a final flush."""
+
+    def __init__(self, plane, record, dist_on: bool) -> None:
+        self.plane = plane
+        self.combiner = None
+        if dist_on:
+            from ekv.observe.ranks import StepCombiner
+
+            self.combiner = StepCombiner(plane, record)
+            self.step, self.finish = self.combiner.step, self.combiner.flush
+        else:
+            self.graph = capture(record)
+            self.step, self.finish = self.graph.replay, None
+
+    def shares(self) -> torch.Tensor:
+        """The last step's (combined) shares, once `finish` has run."""
+        return self.combiner.last() if self.combiner is not None else self.plane.shares()
+
+    def release(self) -> None:
+        if self.combiner is not None:
+            self.combiner.release()
+        self.graph = self.step = self.finish = None
+
+
+# ---- parity of the combined shares (a checker, after the timed regions) --------------------------------
+
+
+def oracle_row_shares(w: Workload, sample: np.ndarray) -> np.ndarray:
+    """This rank's shares of the sampled rows from the oracle (the C restatement of the reference kernel on
+    this rank's own keys and queries, then the reference normalisation): float64 [len(sample), width]."""
+    from oracle import audit as oaud
+    from oracle import cpu as ocpu
+    from oracle import shares as osh
+
+    ocpu.build()
+    g = w.group_rows
+    lens = w.lens[sample]
+    blocks = -(-lens // BLOCK)
+    ids = np.unique(np.concatenate([w.table_host[r, :n] for r, n in zip(sample, blocks, strict=True)]))
+    remap = np.zeros(w.pool, dtype=np.int32)
+    remap[ids] = np.arange(len(ids), dtype=np.int32)
+    table = np.where(np.arange(w.width)[None, :] < blocks[:, None], remap[w.table_host[sample]], 0).astype(np.int32)
+    ids_dev = torch.from_numpy(ids.astype(np.int64)).to(w.caches[0].device)
+    lse = oaud.new_table(w.layers, len(sample), w.width, w.heads * g)
+    one = oaud.new_table(1, len(sample), w.width, g)
+    qrow = w.qrow[sample]
+    select = np.ones(len(sample), dtype=np.uint8)
+    # the layers that read one (pool, KV head), so each head's keys cross to the host once
+    groups: dict[tuple[int, int], list[tuple[int, int]]] = {}
+    for layer in range(w.layers):
+        heads = [layer % w.kv_local] if w.heads == 1 else list(range(w.kv_local))
+        for slot, h in enumerate(heads):
+            groups.setdefault((w.pool_index(layer), h), []).append((layer, slot))
+    for (pool, h), uses in groups.items():
+        keys = w.caches[pool][ids_dev, 0, :, h : h + 1].contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+        for layer, slot in uses:
+            q = w.query(layer)[:, h * g : (h + 1) * g].contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+            one.fill(np.nan)
+            ocpu.tile_lse(q, keys, "bf16", table, lens, qrow, select, 1, one, w.scale, 0, 0, BLOCK, TILE_BLOCKS)
+            lse[:, layer, :, :, slot * g : (slot + 1) * g] = one[:, 0]
+    u = osh.log_weights(lse, w.layers, np.arange(len(sample)), TILE_BLOCKS)
+    return osh.normalize_rows(u, blocks, TILE_BLOCKS)
+
+
+def parity_check(w: Workload, combined: torch.Tensor, rank: int, world: int, dist_on: bool, rows: int) -> dict | None:
+    """Sampled rows of the final shares against the mean over ranks of every rank's oracle shares
+    (RankedShareSource.read, observe/ranks.py:117-119), gathered to rank 0. Every rank takes part."""
+    import torch.distributed as dist
+
+    from oracle import shares as osh
+
+    sample = np.unique(np.linspace(0, w.rows - 1, rows).round().astype(np.int64))
+    mine = torch.from_numpy(oracle_row_shares(w, sample)).to(combined.device)
+    if dist_on:
+        gathered = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(gathered, mine)
+    else:
+        gathered = [mine]
+    if rank != 0:
+        return None
+    want = osh.mean_over_ranks([t.cpu().numpy() for t in gathered])
+    got = combined[torch.from_numpy(sample).to(combined.device)].cpu().numpy().astype(np.float64)
+    same_nan = bool(np.array_equal(np.isnan(got), np.isnan(want)))
+    f = np.isfinite(want) & np.isfinite(got)
+    rel = np.abs(got[f] - want[f]) / np.maximum(np.abs(want[f]), 1e-9)
+    close = bool(np.allclose(got, want, rtol=1e-3, atol=1e-9, equal_nan=True))
+    return {"rows": int(len(sample)), "ranks": world, "max_rel": float(rel.max()) if rel.size else 0.0,
+            "ok": same_nan and close, "tolerance": "rtol 1e-3, atol 1e-9, same NaN rows",
+            "against": "mean over ranks of each rank's oracle shares"}
+
+
+# ---- sections of our arm ---------------------------------------------------------------------------------
 
 
 def view_bench(rank: int, world: int, steps: int, warmup: int, dist_on: bool) -> dict:
@@ -356,13 +495,55 @@ def view_bench(rank: int, world: int, steps: int, warmup: int, dist_on: bool) ->
     return result
 
 
+def record_roofline(plane, w: Workload, steps: int, warmup: int, dist_on: bool) -> dict:
+    """The record kernel alone (one launch per audit step of every layer), timed over its own launches."""
+    graph = capture(lambda: audit_step_resident(plane, w, shares=False))
+    launch_seconds = timed(graph.replay, steps, warmup, dist_on) / steps
+    del graph
+    units = w.units_per_step()
+    b_unit = bytes_per_unit(w.heads * w.group_rows)
+    achieved = units * b_unit / launch_seconds / 1e9
+    peak, peak_kind = measured_peak()
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "peak_kind": peak_kind, "kernel": "record_kernel", "bytes_per_unit": b_unit, "units_per_launch": units,
+            "launch_us": launch_seconds * 1e6}
+
+
+def strong_70b(args, rank: int, world: int, dist_on: bool) -> dict:
+    """The Llama-3-70B-shaped step in all-heads mode: every KV head of every layer, split over the ranks."""
+    cfg = CONFIGS["llama70b"]
+    w = Workload(cfg, rank, world, "all-heads")
+    plane = make_plane(w, deferred=True)
+    stepper = Stepper(plane, lambda: audit_step_resident(plane, w), dist_on)
+    steps = max(10, min(args.steps, 40))
+    seconds = timed(stepper.step, steps, args.warmup, dist_on, stepper.finish)
+    if plane.status():
+        raise SystemExit(f"the audit kernel reported status {plane.status()} (70B all-heads step)")
+    parity = parity_check(w, stepper.shares(), rank, world, dist_on, rows=3)
+    stepper.release()
+    roofline = record_roofline(plane, w, steps, args.warmup, dist_on)
+    units_all = w.units_per_step() * world
+    result = {"value": units_all * steps / seconds, "unit": "audited KV tokens/s", "steps": steps,
+              "warmup": args.warmup, "ms_per_step": seconds / steps * 1e3, "units_per_step": units_all,
+              "scaling": "strong", "config": line_config("llama70b", cfg, "all-heads", "deferred", world),
+              "roofline": roofline, "parity": parity,
+              "note": "every KV head of every layer (cells of kv_heads_per_gpu x 8 query rows), the total split "
+                      "over the ranks; shares averaged over the ranks in the step's graph"}
+    plane.close()
+    del plane, w
+    torch.cuda.empty_cache()
+    return result
+
+
 # ---- the CPU arms ----------------------------------------------------------------------------------------
 
 
 class CpuSample:
     """The C restatement of the reference kernel (oracle/audit_cpu.c) on every host thread, over a
     sample of the workload: all its rows and lengths, one KV head's keys (the audited head of a
-    layer), repeated for as many layers as the time target allows."""
+    layer), repeated for as many layers as the time target allows; then the rest of the reference's
+    CPU path on that sample: the normalisation, the controller's `sum` allocation at budget 0.5 and
+    the compaction."""
 
     def __init__(self, cfg: dict) -> None:
         from oracle import audit as oaud
@@ -374,6 +555,7 @@ class CpuSample:
         self.lens = lengths(cfg["lens"], cfg["rows"], rng).astype(np.int32)
         self.g_rows = cfg["q_heads"] // cfg["kv_heads"]
         self.rows = cfg["rows"]
+        self.cfg_layers = cfg["layers"]
         self.width = int(math.ceil(self.lens.max() / BLOCK))
         blocks = -(-self.lens // BLOCK)
         pool = int(blocks.sum()) + 1
@@ -388,8 +570,9 @@ class CpuSample:
         for r, n in enumerate(blocks):
             self.table[r, :n] = ids[start : start + n]
             start += n
-        self.threads = ocpu.threads()
+        self.threads = host_threads()
         self.layers = 1
+        self.lse = None
 
     def run(self, layers: int) -> tuple[float, int]:
         lse = self.oaud.new_table(layers, self.rows, self.width, self.g_rows)
@@ -399,24 +582,55 @@ class CpuSample:
         for layer in range(layers):
             self.ocpu.tile_lse(self.q16, self.k16, "bf16", self.table, self.lens, qrow, select, 1, lse,
                                1 / math.sqrt(HEAD_DIM), layer, 0, BLOCK, TILE_BLOCKS, self.threads)
-        return time.perf_counter() - t0, int(self.lens.astype(np.int64).sum()) * layers
+        seconds = time.perf_counter() - t0
+        self.lse = lse
+        return seconds, int(self.lens.astype(np.int64).sum()) * layers
 
     def calibrate(self, seconds_target: float) -> None:
         sec, units = self.run(1)
         self.layers = max(1, int(seconds_target / max(sec, 1e-6)))
 
+    def later_stages(self) -> dict:
+        """Seconds of the normalisation (scaled to every layer of a step), the allocation and the
+        compaction over the last run's table."""
+        from oracle import allocation as oa
+        from oracle import shares as osh
+        from oracle import view as oview
+
+        layers = self.lse.shape[1]
+        row_blocks = -(-self.lens // BLOCK)
+        t0 = time.perf_counter()
+        u = osh.log_weights(self.lse, layers, np.arange(self.rows), TILE_BLOCKS)
+        share = osh.normalize_rows(u, row_blocks, TILE_BLOCKS)
+        t1 = time.perf_counter()
+        scores = np.nan_to_num(share, nan=0.0)
+        keep = oa.controller_keep(row_blocks, self.width, lambda r, n: scores[r, :n], 0.5, "sum", recent_blocks=4)
+        t2 = time.perf_counter()
+        oview.compact_block_table(self.table, self.lens, keep, BLOCK)
+        t3 = time.perf_counter()
+        return {"normalize": (t1 - t0) * self.cfg_layers / layers, "allocate_sum": t2 - t1, "compact": t3 - t2}
+
     def describe(self, units: int) -> str:
         return (f"{self.rows} rows x {self.layers} layers of the workload ({units} key vectors, one KV head's keys "
-                f"per layer), C restatement of tile_lse_kernel on {self.threads} OpenMP threads")
+                f"per layer), C restatement of tile_lse_kernel on {self.threads} OpenMP threads; then the numpy "
+                f"normalisation, the controller's sum allocation (budget 0.5, 4 recent blocks) and the compaction")
 
 
-def cpu_sample(cfg: dict, seconds_target: float) -> dict:
-    """Audited tokens/s of the reference algorithm on the host cores, over a bounded sample."""
+def cpu_sample(cfg: dict, seconds_target: float, heads_all: int) -> dict:
+    """Audited tokens/s of the reference algorithm on the host cores, over a bounded sample, and the
+    reference's whole CPU path per step at that rate."""
     sample = CpuSample(cfg)
     sample.calibrate(seconds_target)
     sec, units = sample.run(sample.layers)
-    return {"value": units / sec, "unit": "audited KV tokens/s", "cores": sample.threads, "kind": "port",
-            "sample": sample.describe(units), "seconds": round(sec, 2)}
+    rate = units / sec
+    stages = sample.later_stages()
+    step_units = int(sample.lens.astype(np.int64).sum()) * cfg["layers"] * heads_all
+    stages_ms = {"tile_lse": step_units / rate * 1e3} | {k: v * 1e3 for k, v in stages.items()}
+    path_ms = sum(stages_ms.values())
+    return {"value": rate, "unit": "audited KV tokens/s", "cores": sample.threads, "kind": "port",
+            "sample": sample.describe(units), "seconds": round(sec, 2),
+            "stages_ms_per_step": {k: round(v, 3) for k, v in stages_ms.items()},
+            "path_ms_per_step": round(path_ms, 3), "path_value": step_units / path_ms * 1e3}
 
 
 def reference_arm(args, cfg: dict) -> None:
@@ -431,7 +645,6 @@ def reference_arm(args, cfg: dict) -> None:
         if step >= args.warmup:
             rates.append(units / sec)
     value = statistics.median(rates)
-    per_step = [{"kind": "port", "cores": sample.threads, "sample": sample.describe(units)}]
     # one whole-job step of the workload (every rank's heads of every layer) at that rate
     heads_all = args.gpus if args.mode == "reference" else cfg["kv_heads"]
     step_units = int(sample.lens.astype(np.int64).sum()) * cfg["layers"] * heads_all
@@ -439,10 +652,10 @@ def reference_arm(args, cfg: dict) -> None:
         "impl": "reference", "metric": "audited KV tokens/s", "value": value, "unit": "audited KV tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": step_units / value * 1e3, "higher_is_better": True,
-        "scaling": "weak", "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": args.config, "mode": args.mode, "rows": cfg["rows"], "layers": cfg["layers"]},
-        "cpu_baseline": {k: per_step[-1][k] for k in ("kind", "cores", "sample")} | {"value": value,
-                                                                                     "unit": "audited KV tokens/s"},
+        "scaling": "weak" if args.mode == "reference" else "strong", "dtype": "bf16", "data": "synthetic",
+        "config": line_config(args.config, cfg, args.mode, args.record, args.gpus),
+        "cpu_baseline": {"kind": "port", "cores": sample.threads, "sample": sample.describe(units), "value": value,
+                         "unit": "audited KV tokens/s"},
         "e2e": {"value": value, "unit": "audited KV tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "vs_baseline": None,
     }
@@ -463,6 +676,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the timed CPU sample")
     ap.add_argument("--no-view", action="store_true", help="skip the block-view build timing")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end timing")
+    ap.add_argument("--no-strong", action="store_true", help="skip the 70B all-heads strong-scaling step")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the final shares")
     ap.add_argument("--pools", type=int, default=None,
                     help="a fixed number of KV pools cycled over the layers (default: reference mode gives every "
                          "layer keys of its own)")
@@ -508,110 +723,115 @@ def main() -> None:
     import ekv.build
 
     ekv.build.build()
-    from ekv.observe.ranks import allreduce_shares
 
     w = Workload(cfg, rank, world, args.mode)
     plane = make_plane(w, deferred=args.record == "deferred")
-    if args.record == "deferred":
-        graph = capture(lambda: audit_step_resident(plane, w))
-    else:
-        graph = capture(lambda: audit_step(plane, w))
-    share = plane.shares()
-
-    def step():
-        graph.replay()
-        if dist_on:
-            allreduce_shares(share)
+    record = (lambda: audit_step_resident(plane, w)) if args.record == "deferred" else (lambda: audit_step(plane, w))
+    stepper = Stepper(plane, record, dist_on)
 
     with ClockSampler(local) as clocks:
-        seconds = timed(step, args.steps, args.warmup, dist_on)
-    status = plane.status()
-    if status:
-        raise SystemExit(f"the audit kernel reported status {status}")
-    per_layer = None
-    if args.record == "deferred" and not args.no_e2e:
-        # the same step recorded layer by layer (a launch per layer), for comparison
-        plane_pl = make_plane(w, deferred=False)
-        graph_pl = capture(lambda: audit_step(plane_pl, w))
-        pl_seconds = timed(graph_pl.replay, args.steps, args.warmup, dist_on)
-        per_layer = {"value": w.units_per_step() * world * args.steps / pl_seconds, "unit": "audited KV tokens/s",
-                     "ms_per_step": pl_seconds / args.steps * 1e3}
-        del graph_pl
-    units_rank = w.units_per_step()
-    units_all = units_rank * world
-    value = units_all * args.steps / seconds
-    # the roofline of the dominant kernel: the record kernel alone, one launch per audit step
-    # (deferred) or per layer (per-layer), timed over its own launches
-    if args.record == "deferred":
-        record_graph = capture(lambda: audit_step_resident(plane, w, shares=False))
-        launch_seconds = timed(record_graph.replay, args.steps, args.warmup, dist_on) / args.steps
-        per_launch_units = units_rank
-        del record_graph
-    else:
-        launch_seconds = seconds / args.steps / w.layers
-        per_launch_units = units_rank / w.layers
-    per_launch_bytes = per_launch_units * bytes_per_unit(w.heads * w.group_rows)
-    achieved = per_launch_bytes / launch_seconds / 1e9
-    peak, peak_kind = measured_peak()
+        seconds = timed(stepper.step, args.steps, args.warmup, dist_on, stepper.finish)
+        status = plane.status()
+        if status:
+            raise SystemExit(f"the audit kernel reported status {status}")
+        parity = None
+        if not args.no_parity:
+            parity = parity_check(w, stepper.shares(), rank, world, dist_on, rows=4)
+        stepper.release()
+        per_layer = None
+        if args.record == "deferred" and not args.no_e2e:
+            # the same step recorded layer by layer (a launch per layer), for comparison
+            plane_pl = make_plane(w, deferred=False)
+            graph_pl = capture(lambda: audit_step(plane_pl, w))
+            pl_seconds = timed(graph_pl.replay, args.steps, args.warmup, dist_on)
+            per_layer = {"value": w.units_per_step() * world * args.steps / pl_seconds, "unit": "audited KV tokens/s",
+                         "ms_per_step": pl_seconds / args.steps * 1e3}
+            del graph_pl
+            plane_pl.close()
+        units_rank = w.units_per_step()
+        units_all = units_rank * world
+        value = units_all * args.steps / seconds
+        # the roofline of the dominant kernel: the record kernel alone, one launch per audit step
+        # (deferred) or per layer (per-layer), timed over its own launches
+        if args.record == "deferred":
+            roofline = record_roofline(plane, w, args.steps, args.warmup, dist_on)
+        else:
+            peak, peak_kind = measured_peak()
+            launch_seconds = seconds / args.steps / w.layers
+            b_unit = bytes_per_unit(w.heads * w.group_rows)
+            achieved = units_rank / w.layers * b_unit / launch_seconds / 1e9
+            roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                        "peak_kind": peak_kind, "kernel": "record_kernel", "bytes_per_unit": b_unit,
+                        "units_per_launch": units_rank / w.layers, "launch_us": launch_seconds * 1e6}
+        roofline["note"] = ("record kernel alone, one launch per audit step of every layer (per-layer: one per "
+                            "layer); CUDA events over its own timed launches")
 
-    # e2e: the step's host inputs in from pinned memory, the shares out, every step
-    # (the engine's block table and lengths: one copy; the selection: RecordingPlane.select, one copy)
-    # Each step's shares land in one of two pinned buffers; the host waits for a step's shares after it
-    # has queued the next step, so the GPU does not idle while the host issues a step.
-    pinned_inputs = torch.from_numpy(w.inputs_host).pin_memory()
-    out_host = [torch.empty(share.shape, dtype=share.dtype).pin_memory() for _ in range(2)]
-    out_ready = [torch.cuda.Event(), torch.cuda.Event()]
-    issued = [0]
+        # e2e: the step's host inputs in from pinned memory, the shares out, every step (the engine's block
+        # table and lengths: one copy; the selection: RecordingPlane.select, one copy). Each step's shares
+        # land in one of two pinned buffers and the host waits for them after it has queued the next step;
+        # with ranks, a step's shares are complete (combined) once the next step's graph has run.
+        pinned_inputs = torch.from_numpy(w.inputs_host).pin_memory()
+        share0 = plane.shares()
+        out_host = [torch.empty(share0.shape, dtype=share0.dtype).pin_memory() for _ in range(2)]
+        out_ready = [torch.cuda.Event(), torch.cuda.Event()]
+        issued = [0]
+        api_stepper = Stepper(plane, lambda: audit_step(plane, w), dist_on)
 
-    api_graph = capture(lambda: audit_step(plane, w)) if args.record == "deferred" else graph
+        def e2e_step():
+            i = issued[0]
+            issued[0] += 1
+            w.inputs.copy_(pinned_inputs, non_blocking=True)
+            plane.select(w.select, w.qrow)
+            api_stepper.step()
+            if dist_on:  # the previous step's shares are complete (combined) once this step's graph has run
+                if i == 0:
+                    return
+                combiner = api_stepper.combiner
+                buffer, done = combiner.buffers[(combiner.steps - 2) % 2], i - 1
+            else:
+                buffer, done = plane.shares(), i
+            out_host[done % 2].copy_(buffer, non_blocking=True)
+            out_ready[done % 2].record()
+            if done > 0:
+                out_ready[(done - 1) % 2].synchronize()  # the copy one step earlier has landed on the host
 
-    def e2e_step():
-        i = issued[0]
-        issued[0] += 1
-        w.inputs.copy_(pinned_inputs, non_blocking=True)
-        plane.select(w.select, w.qrow)
-        api_graph.replay()
-        if dist_on:
-            allreduce_shares(share)
-        out_host[i % 2].copy_(share, non_blocking=True)
-        out_ready[i % 2].record()
-        if i > 0:
-            out_ready[(i - 1) % 2].synchronize()  # the previous step's shares are on the host
+        def e2e_finish():
+            if dist_on and issued[0] > 0:  # the last step's combine and its copy out
+                last = api_stepper.finish()
+                out_host[(issued[0] - 1) % 2].copy_(last, non_blocking=True)
+            issued[0] = 0
 
-    e2e_seconds = timed(e2e_step, args.steps, args.warmup, dist_on) if not args.no_e2e else float("nan")
-    h2d = pinned_inputs.nbytes + 5 * w.rows  # select(): a token row (int32) and a flag per row
-    d2h = out_host[0].nbytes
-    view = None if args.no_view else view_bench(rank, world, args.steps, args.warmup, dist_on)
+        e2e_seconds = timed(e2e_step, args.steps, args.warmup, dist_on, e2e_finish) if not args.no_e2e else float("nan")
+        api_stepper.release()
+        h2d = pinned_inputs.nbytes + 5 * w.rows  # select(): a token row (int32) and a flag per row
+        d2h = out_host[0].nbytes
+        view = None if args.no_view else view_bench(rank, world, args.steps, args.warmup, dist_on)
+        strong = None
+        if not args.no_strong and args.config == "llama8b" and not args.layers and not args.pools:
+            plane.close()
+            del plane, stepper, api_stepper
+            w.caches, w.queries = [], []  # the 70B step's pools take their place
+            torch.cuda.empty_cache()
+            strong = strong_70b(args, rank, world, dist_on)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_sample(cfg, seconds_target=10.0)
+        cpu = cpu_sample(cfg, seconds_target=10.0, heads_all=w.heads * world)
     if dist_on:
         dist.barrier()
-        del graph
         dist.destroy_process_group()
     if rank != 0:
         return
-    traffic = NCU_TRAFFIC_PER_LAUNCH.get(args.config) if (args.mode == "reference" and args.record == "deferred"
-                                                          and not args.layers and not args.pools
-                                                          and world == 1) else None
+    traffic_applies = (args.mode == "reference" and args.record == "deferred" and not args.layers and not args.pools
+                       and world == 1)
+    roofline["traffic"] = NCU_TRAFFIC_PER_LAUNCH.get(args.config) if traffic_applies else None
+    roofline["traffic_source"] = NCU_TRAFFIC_SOURCE if roofline["traffic"] is not None else None
     line = {
         "metric": "audited KV tokens/s", "value": value, "unit": "audited KV tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": seconds / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak" if args.mode == "reference" else "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": args.config, "mode": args.mode, "record": args.record, "rows": w.rows,
-                   "layers": w.layers,
-                   "q_heads": cfg["q_heads"], "kv_heads": cfg["kv_heads"], "kv_heads_per_gpu": w.kv_local,
-                   "audited_heads_per_layer_per_gpu": w.heads, "block_size": BLOCK, "tile_blocks": TILE_BLOCKS,
-                   "mean_len": float(w.lens.mean()), "width": w.width, "pools": len(w.caches),
-                   "l2": f"inputs larger than L2: {units_rank / w.layers * 256 / 1e6:.0f} MB of keys per launch",
-                   "parallelism": f"tp{world} (KV heads)"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "peak_kind": peak_kind, "kernel": "record_kernel",
-                     "bytes_per_unit": bytes_per_unit(w.heads * w.group_rows), "units_per_launch": per_launch_units,
-                     "launch_us": launch_seconds * 1e6,
-                     "note": "record kernel alone, one launch per audit step of every layer (per-layer: one per "
-                             "layer); CUDA events over its own timed launches"},
+        "config": line_config(args.config, cfg, args.mode, args.record, world),
+        "roofline": roofline,
         "e2e": {"value": units_all * args.steps / e2e_seconds, "unit": "audited KV tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "note": "RecordingPlane.select (one copy from pinned staging), then RecordingPlane.record per "
@@ -623,8 +843,12 @@ def main() -> None:
         # per layer plus the share and combine kernels (per-layer)
         "gpu_launches": args.steps * (4 if args.record == "deferred" else w.layers + 2),
         "clocks": clocks.summary(),
+        "parity": parity,
+        "combine": ("one NCCL all-reduce (average) per step in the step's CUDA graph, overlapping the next "
+                    "step's audit; the last step's inside the timed region") if dist_on else None,
         "per_layer_launches": per_layer,
         "view": view,
+        "strong_70b": strong,
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)

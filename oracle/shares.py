@@ -64,6 +64,48 @@ def normalize(u: np.ndarray, row_blocks: np.ndarray, tile_blocks: int, aggregate
     return out
 
 
+def normalize_rows(u: np.ndarray, row_blocks: np.ndarray, tile_blocks: int, aggregate: str = "mean") -> np.ndarray:
+    """``normalize`` with each row's (layer, query row) share vectors computed at once.
+
+    The same arithmetic (observe/tile_shares.py:82-103) in float64, vectorised over a row's layers and
+    query rows instead of looping over them, for checks at full model sizes (80 layers x 64 query rows).
+    The per-vector sums run in NumPy's order rather than one after another, a difference of a few units
+    in the last place of float64; tests hold both forms to each other.
+    """
+    if aggregate not in ("mean", "max"):
+        raise ValueError(f"unknown aggregate {aggregate!r}")
+    if u.ndim != 4:
+        raise ValueError("u must be [layers, rows, blocks, query_rows]")
+    layers, rows, width, query_rows = u.shape
+    row_blocks = np.asarray(row_blocks)
+    if row_blocks.shape != (rows,) or tile_blocks < 1:
+        raise ValueError("row_blocks must give one length per row, and tile_blocks must be positive")
+    out = np.full((rows, width), np.nan)
+    b = np.arange(width)
+    for r in range(rows):
+        n = int(row_blocks[r])
+        tail_start = (n // tile_blocks) * tile_blocks
+        valid_tail = max(n - tail_start, 1)
+        regain = np.where((n % tile_blocks != 0) & (b >= tail_start) & (b < n), np.log(tile_blocks / valid_tail), 0.0)
+        x = np.where((b < n)[None, :, None], u[:, r].astype(np.float64), np.nan) + regain[None, :, None]  # [L, W, Q]
+        finite = np.isfinite(x)
+        peak = np.where(finite, x, -np.inf).max(axis=1, keepdims=True)
+        has = np.isfinite(peak)
+        w = np.where(finite, np.exp(np.where(finite, x, 0.0) - np.where(has, peak, 0.0)), 0.0)
+        total = w.sum(axis=1, keepdims=True)
+        share = np.divide(w, total, out=np.zeros_like(w), where=total > 0)
+        count = int(has.sum())
+        if count == 0:
+            continue  # no evidence: the row stays NaN (:103)
+        if aggregate == "max":
+            acc = share.max(axis=(0, 2))
+            t = acc.sum()
+            out[r] = acc / t if t > 0 else np.zeros(width)
+        else:
+            out[r] = share.sum(axis=(0, 2)) / count
+    return out
+
+
 def contributors(u: np.ndarray, row_blocks: np.ndarray, tile_blocks: int) -> np.ndarray:
     """The number of (layer, query row) pairs of each row with at least one finite cell."""
     layers, rows, width, query_rows = u.shape

@@ -26,6 +26,15 @@ int check_launch(const char* what) {
   return fail(EKV_ECUDA, "%s: %s", what, cudaGetErrorString(err));
 }
 
+int current_device(int* device) {
+  *device = 0;
+  const cudaError_t err = cudaGetDevice(device);
+  if (err != cudaSuccess) return fail(EKV_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
+  if (*device < 0 || *device >= kMaxDevices)
+    return fail(EKV_ENOTSUP, "device %d: this library serves devices 0 to %d", *device, kMaxDevices - 1);
+  return EKV_OK;
+}
+
 }  // namespace ekv
 
 extern "C" const char* ekv_last_error_string(void) { return ekv::g_error; }

@@ -584,11 +584,12 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
   p.cand_key = reinterpret_cast<unsigned long long*>(base + l.cand_key);
   p.cand_at = reinterpret_cast<unsigned int*>(base + l.cand_at);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(base, 0, l.zeroed, s) != cudaSuccess) return check_launch("cudaMemsetAsync(sum workspace)");
   int device = 0, sms = 0;
-  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices ||
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+  const int dev_rc = current_device(&device);
+  if (dev_rc != EKV_OK) return dev_rc;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
     return check_launch("cudaDeviceGetAttribute");
+  if (cudaMemsetAsync(base, 0, l.zeroed, s) != cudaSuccess) return check_launch("cudaMemsetAsync(sum workspace)");
   const size_t prep_smem = (size_t)width * sizeof(S);
   static size_t configured[kMaxDevices] = {};
   if (configured[device] < prep_smem) {

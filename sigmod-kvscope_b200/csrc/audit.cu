@@ -792,8 +792,10 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
   static int grid_of[kMaxDevices] = {};
   static size_t smem_of[kMaxDevices] = {};
   int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
-    return check_launch("cudaGetDevice");
+  {
+    const int dev_rc = current_device(&device);
+    if (dev_rc != EKV_OK) return dev_rc;
+  }
   auto kernel = record_kernel<TT, NT, D, T>;
   if (grid_of[device] == 0 || smem_of[device] != smem) {
     int sms = 0, per_sm = 0, optin = 0;
@@ -1034,16 +1036,19 @@ extern "C" int ekv_audit_launch(
                                  : dispatch<__half>(p, tt, finalize, 0, layers, s);
 }
 
-extern "C" int ekv_audit_step(
-    const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table, const int32_t* lens,
-    const int32_t* qrow, const uint8_t* select, const uint32_t* flag, float* lse, float scale,
-    int layer0, int n_layers, int group, int rotate, int q_layout, int64_t q_stride_token, int64_t q_stride_head,
-    int64_t k_stride_block, int64_t k_stride_pos, int64_t k_stride_head, int64_t table_stride,
-    int layers, int rows, int width, int group_rows, int block_size, int tile_blocks, int head_dim,
-    int dtype, int heads, int kv_heads, int64_t pool_blocks, int64_t q_tokens, float* share_out,
-    int32_t* contributors, int aggregate, void* workspace, size_t workspace_bytes,
-    uint32_t* status, void* stream) {
-  clear_error();
+namespace {
+
+// The audit step of ekv_audit_step. With clear_tickets, the workspace's row tickets are zeroed on the
+// stream after every argument has been checked and before the first launch (a workspace whose last
+// user may have left them non-zero).
+int audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table, const int32_t* lens,
+               const int32_t* qrow, const uint8_t* select, const uint32_t* flag, float* lse, float scale,
+               int layer0, int n_layers, int group, int rotate, int q_layout, int64_t q_stride_token,
+               int64_t q_stride_head, int64_t k_stride_block, int64_t k_stride_pos, int64_t k_stride_head,
+               int64_t table_stride, int layers, int rows, int width, int group_rows, int block_size,
+               int tile_blocks, int head_dim, int dtype, int heads, int kv_heads, int64_t pool_blocks,
+               int64_t q_tokens, float* share_out, int32_t* contributors, int aggregate, void* workspace,
+               size_t workspace_bytes, uint32_t* status, void* stream, bool clear_tickets) {
   if (!q_layers || !k_layers) return fail(EKV_EINVAL, "the per-layer address arrays must not be NULL");
   AuditParams p{};
   const int rc = prepare(p, table, lens, qrow, select, flag, lse, scale, q_stride_token, q_stride_head,
@@ -1064,9 +1069,34 @@ extern "C" int ekv_audit_step(
   const int enc = encode_key_map(&p.kmap0, workspace, p, dtype);
   if (enc != EKV_OK) return enc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (clear_tickets) {
+    const WorkspaceLayout w = workspace_layout(layers, rows, width);
+    if (cudaMemsetAsync(static_cast<uint8_t*>(workspace) + w.row_tickets, 0, w.contrib - w.row_tickets, s) !=
+        cudaSuccess)
+      return check_launch("cudaMemsetAsync(row tickets)");
+  }
   const int tt = block_size * tile_blocks;
   return dtype == EKV_DTYPE_BF16 ? dispatch<__nv_bfloat16>(p, tt, true, layer0, n_layers, s)
                                  : dispatch<__half>(p, tt, true, layer0, n_layers, s);
+}
+
+}  // namespace
+
+extern "C" int ekv_audit_step(
+    const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table, const int32_t* lens,
+    const int32_t* qrow, const uint8_t* select, const uint32_t* flag, float* lse, float scale,
+    int layer0, int n_layers, int group, int rotate, int q_layout, int64_t q_stride_token, int64_t q_stride_head,
+    int64_t k_stride_block, int64_t k_stride_pos, int64_t k_stride_head, int64_t table_stride,
+    int layers, int rows, int width, int group_rows, int block_size, int tile_blocks, int head_dim,
+    int dtype, int heads, int kv_heads, int64_t pool_blocks, int64_t q_tokens, float* share_out,
+    int32_t* contributors, int aggregate, void* workspace, size_t workspace_bytes,
+    uint32_t* status, void* stream) {
+  clear_error();
+  return audit_step(q_layers, k_layers, table, lens, qrow, select, flag, lse, scale, layer0, n_layers, group,
+                    rotate, q_layout, q_stride_token, q_stride_head, k_stride_block, k_stride_pos, k_stride_head,
+                    table_stride, layers, rows, width, group_rows, block_size, tile_blocks, head_dim, dtype, heads,
+                    kv_heads, pool_blocks, q_tokens, share_out, contributors, aggregate, workspace,
+                    workspace_bytes, status, stream, false);
 }
 
 // ---- the audit step without a caller-provided workspace ---------------------------------------------
@@ -1084,6 +1114,67 @@ static __device__ __align__(256) uint8_t g_audit_scratch[EKV_AUDIT_STATIC_SCRATC
 #include <mutex>
 
 extern "C" size_t ekv_audit_static_scratch_bytes(void) { return EKV_AUDIT_STATIC_SCRATCH_BYTES; }
+
+namespace {
+
+// The device address of g_audit_scratch in the current context, looked up with cudaGetSymbolAddress
+// the first time a context calls (the lookup loads the module on that device, so that first call
+// belongs before any stream capture) and kept per device together with the context's ID: a new
+// context on the same ordinal (after cudaDeviceReset, or another process-level context) has its own
+// copy of the module and looks the address up again.
+int static_scratch(void** out) {
+  *out = nullptr;
+  int device = 0;
+  const int rc = current_device(&device);
+  if (rc != EKV_OK) return rc;
+  static const auto get_current = []() -> PFN_cuCtxGetCurrent_v4000 {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f);
+  }();
+  static const auto get_id = []() -> PFN_cuCtxGetId_v12000 {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<PFN_cuCtxGetId_v12000>(f);
+  }();
+  if (get_current == nullptr || get_id == nullptr)
+    return fail(EKV_ENOTSUP, "the driver does not export cuCtxGetCurrent and cuCtxGetId");
+  // A thread that has not used the runtime yet has no current context: the symbol lookup makes the
+  // device's primary context current, and its ID is read after it.
+  auto context_id = [&](unsigned long long* id) {
+    CUcontext ctx = nullptr;
+    return get_current(&ctx) == CUDA_SUCCESS && ctx != nullptr && get_id(ctx, id) == CUDA_SUCCESS;
+  };
+  unsigned long long ctx_id = 0;
+  const bool known = context_id(&ctx_id);
+  struct Entry {
+    unsigned long long ctx_id;
+    void* ptr;
+  };
+  static Entry entries[kMaxDevices] = {};
+  static std::mutex setup;
+  std::lock_guard<std::mutex> lock(setup);
+  Entry& e = entries[device];
+  if (!known || e.ptr == nullptr || e.ctx_id != ctx_id) {
+    void* ptr = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&ptr, g_audit_scratch);
+    if (err != cudaSuccess || ptr == nullptr)
+      return fail(EKV_ECUDA, "cudaGetSymbolAddress(static audit workspace): %s", cudaGetErrorString(err));
+    if (!known && !context_id(&ctx_id)) return fail(EKV_ECUDA, "device %d has no current context", device);
+    e.ctx_id = ctx_id;
+    e.ptr = ptr;
+  }
+  *out = e.ptr;
+  return EKV_OK;
+}
+
+}  // namespace
 
 extern "C" int ekv_audit_step_static(
     const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table, const int32_t* lens,
@@ -1103,33 +1194,14 @@ extern "C" int ekv_audit_step_static(
                 "a step of %d layers x %d rows x %d blocks needs %zu bytes of workspace; the static one holds %u: "
                 "pass a workspace to ekv_audit_step instead",
                 layers, rows, width, need, (unsigned)EKV_AUDIT_STATIC_SCRATCH_BYTES);
-  int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
-    return check_launch("cudaGetDevice");
-  // The array's name is a host-side stand-in; the device address is looked up once per device, with
-  // that device current.
-  static void* scratch_of[kMaxDevices] = {};
-  static std::mutex setup;
   void* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(setup);
-    if (scratch_of[device] == nullptr) {
-      void* ptr = nullptr;
-      const cudaError_t err = cudaGetSymbolAddress(&ptr, g_audit_scratch);
-      if (err != cudaSuccess || ptr == nullptr)
-        return fail(EKV_ECUDA, "cudaGetSymbolAddress(static audit workspace): %s", cudaGetErrorString(err));
-      scratch_of[device] = ptr;
-    }
-    scratch = scratch_of[device];
-  }
-  // The array keeps the last call's contents: the row tickets must start at zero.
-  const WorkspaceLayout w = workspace_layout(layers, rows, width);
-  if (cudaMemsetAsync(static_cast<uint8_t*>(scratch) + w.row_tickets, 0, w.contrib - w.row_tickets,
-                      static_cast<cudaStream_t>(stream)) != cudaSuccess)
-    return check_launch("cudaMemsetAsync(static audit workspace)");
-  return ekv_audit_step(q_layers, k_layers, table, lens, qrow, select, flag, lse, scale, layer0, n_layers,
-                        group, rotate, q_layout, q_stride_token, q_stride_head, k_stride_block, k_stride_pos,
-                        k_stride_head, table_stride, layers, rows, width, group_rows, block_size, tile_blocks,
-                        head_dim, dtype, heads, kv_heads, pool_blocks, q_tokens, share_out, contributors,
-                        aggregate, scratch, EKV_AUDIT_STATIC_SCRATCH_BYTES, status, stream);
+  const int rc = static_scratch(&scratch);
+  if (rc != EKV_OK) return rc;
+  // The array keeps the last call's contents: audit_step zeroes the row tickets once every argument
+  // has been checked, so a refused call leaves the array as it was.
+  return audit_step(q_layers, k_layers, table, lens, qrow, select, flag, lse, scale, layer0, n_layers, group,
+                    rotate, q_layout, q_stride_token, q_stride_head, k_stride_block, k_stride_pos, k_stride_head,
+                    table_stride, layers, rows, width, group_rows, block_size, tile_blocks, head_dim, dtype, heads,
+                    kv_heads, pool_blocks, q_tokens, share_out, contributors, aggregate, scratch,
+                    EKV_AUDIT_STATIC_SCRATCH_BYTES, status, stream, true);
 }

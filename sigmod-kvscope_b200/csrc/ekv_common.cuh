@@ -23,6 +23,9 @@ void clear_error();
 int check_launch(const char* what);
 
 constexpr int kMaxDevices = 64;  // per-device one-time kernel attributes
+// The current device's ordinal in *device: EKV_OK, EKV_ECUDA when the runtime cannot say, or EKV_ENOTSUP
+// for an ordinal at or past kMaxDevices (the per-device caches of the entry points hold that many).
+int current_device(int* device);
 
 inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 inline int cdiv(int a, int b) { return (a + b - 1) / b; }

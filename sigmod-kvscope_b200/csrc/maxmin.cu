@@ -781,8 +781,10 @@ static int allocate_maxmin(const S* scores, int64_t score_stride, const int32_t*
   const size_t prep_smem = mm_prep_smem<S>(width);
   const size_t level_smem = mm_level_smem(rows).bytes;
   int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
-    return check_launch("cudaGetDevice");
+  {
+    const int dev_rc = current_device(&device);
+    if (dev_rc != EKV_OK) return dev_rc;
+  }
   static size_t prep_set[kMaxDevices] = {}, level_set[kMaxDevices] = {};
   static bool cumsum_set[kMaxDevices] = {};
   if (!cumsum_set[device]) {

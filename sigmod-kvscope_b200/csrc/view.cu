@@ -605,8 +605,10 @@ int launch_view(const ViewParams& p, cudaStream_t stream) {
   const size_t smem = view_smem_bytes<K>(p.width);
   static size_t configured[kMaxDevices] = {};
   int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
-    return check_launch("cudaGetDevice");
+  {
+    const int dev_rc = current_device(&device);
+    if (dev_rc != EKV_OK) return dev_rc;
+  }
   if (configured[device] < smem) {
     if (cudaFuncSetAttribute(view_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(view_kernel)");
@@ -643,8 +645,10 @@ extern "C" int ekv_allocate_quotas(const int32_t* row_blocks, const int32_t* mea
   }
   static bool configured[kMaxDevices] = {};
   int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
-    return check_launch("cudaGetDevice");
+  {
+    const int dev_rc = current_device(&device);
+    if (dev_rc != EKV_OK) return dev_rc;
+  }
   if (!configured[device]) {
     if (cudaFuncSetAttribute(quota_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kQuotaMaxRows * (int)sizeof(double)) != cudaSuccess)

@@ -382,6 +382,17 @@ class RecordingPlane(AuditPlane):
         """
         return self._share
 
+    def direct_shares(self, out: torch.Tensor) -> None:
+        """Write the shares of the launches that follow into ``out`` (float32 [rows, width] on the plane's
+        device) instead of the plane's own buffer; ``shares()`` then returns ``out``. Launches already
+        captured in a CUDA graph keep the buffer they were captured with, so two buffers captured in two
+        graphs let one step's shares be combined across ranks while the next step writes the other."""
+        if out.dtype != torch.float32 or tuple(out.shape) != (self.rows, self.width) or not out.is_contiguous():
+            raise ValueError(f"the share buffer must be a contiguous float32 [{self.rows}, {self.width}] tensor")
+        if out.device != self._device:
+            raise ValueError("the share buffer must be on the plane's device")
+        self._share = out
+
     def status(self) -> int:
         """The EKV_STATUS_* bits the kernel raised since the last ``clear_status`` (synchronises)."""
         return int(self._status.item())

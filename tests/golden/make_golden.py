@@ -1,8 +1,9 @@
 """Generate the golden fixtures of tests/golden/ by running the reference's own code.
 
-Run in a container that has the reference checkout (default /root/reference, or $EKV_REFERENCE):
+Run in a container that has the reference checkout, named by $EKV_REFERENCE (its root directory, the
+one that holds ``runtime/`` and ``observe/``):
 
-    python tests/golden/make_golden.py
+    EKV_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference read-only and runs, on CPU:
   * its Triton audit kernel ``tile_lse_kernel`` (runtime/audit_kernel.py:34-109) under
@@ -26,7 +27,9 @@ import os
 import sys
 
 os.environ["TRITON_INTERPRET"] = "1"
-REFERENCE = os.environ.get("EKV_REFERENCE", "/root/reference")
+REFERENCE = os.environ.get("EKV_REFERENCE")
+if not REFERENCE or not os.path.isdir(os.path.join(REFERENCE, "runtime")):
+    raise SystemExit("set EKV_REFERENCE to the reference checkout (the directory holding runtime/ and observe/)")
 sys.path.insert(0, REFERENCE)
 
 import numpy as np  # noqa: E402

@@ -87,6 +87,26 @@ def test_oracle_normalize_matches_reference_cases():
             np.testing.assert_allclose(got, g[f"{aggregate}{i}"], rtol=1e-12, atol=1e-15, equal_nan=True)
 
 
+def test_vectorised_normalize_matches_reference_cases_and_the_loop_form():
+    """normalize_rows, the per-row vectorised form used at full model sizes, against the reference's
+    outputs and against normalize on random cells with NaN holes, partial tails and empty rows."""
+    g = load_golden("shares_cases")
+    for i in range(12):
+        for aggregate in ("mean", "max"):
+            got = osh.normalize_rows(g[f"u{i}"], g[f"rb{i}"], int(g[f"tb{i}"]), aggregate)
+            np.testing.assert_allclose(got, g[f"{aggregate}{i}"], rtol=1e-12, atol=1e-15, equal_nan=True)
+    rng = np.random.default_rng(4)
+    for trial in range(6):
+        layers, rows, width, q = 3, 5, 23, 1 + trial % 4
+        u = rng.normal(0, 3, (layers, rows, width, q)).astype(np.float32)
+        u[rng.random(u.shape) < 0.1] = np.nan
+        row_blocks = rng.integers(0, width + 1, rows)
+        for aggregate in ("mean", "max"):
+            a = osh.normalize(u, row_blocks, 1 + trial % 3, aggregate)
+            b = osh.normalize_rows(u, row_blocks, 1 + trial % 3, aggregate)
+            np.testing.assert_allclose(b, a, rtol=1e-12, atol=1e-15, equal_nan=True)
+
+
 def test_oracle_log_weights_match_read_tile_rows():
     g = load_golden("shares_cases")
     table_layers, layers, rows, width, group, tile_blocks = 4, 3, 5, 6, 2, 2

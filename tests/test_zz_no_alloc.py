@@ -19,6 +19,9 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import audit as oaud
+from oracle import shares as osh
+
 pytestmark = pytest.mark.gpu
 
 LSE_TOL = dict(rtol=1e-4, atol=1e-4)
@@ -88,6 +91,52 @@ def test_the_static_workspace_step_equals_the_workspace_step_on_two_calls():
         np.testing.assert_allclose(sb, sa, equal_nan=True, err_msg=f"call {call}", **SHARE_TOL)
         assert torch.equal(contrib_a, contrib_b)
         assert np.isnan(sb[2]).all() and np.isnan(sb[3]).all()  # an empty row and an unselected row
+    # the last static call against the oracle as well: the restatement of the reference kernel, one KV
+    # head per layer (head layer % kv_heads), then the reference normalisation of the cells
+    ref = oracle_table(x)
+    got = lse_b.cpu().numpy()
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    np.testing.assert_allclose(got[~np.isnan(ref)], ref[~np.isnan(ref)], **LSE_TOL)
+    lens, select = x["lens"].cpu().numpy(), x["select"].cpu().numpy()
+    row_blocks = np.where(select != 0, -(-lens // 16), 0)
+    live = np.flatnonzero(row_blocks > 0)
+    expect = np.full((x["rows"], x["width"]), np.nan)
+    expect[live] = osh.normalize(osh.log_weights(ref, x["layers"], live, 2), row_blocks[live], 2)
+    np.testing.assert_allclose(share_b.cpu().numpy().astype(np.float64), expect, equal_nan=True, **SHARE_TOL)
+
+
+def oracle_table(x) -> np.ndarray:
+    lse = oaud.new_table(x["layers"], x["rows"], x["width"], 4)
+    for layer in range(x["layers"]):
+        oaud.tile_lse(x["qs"][layer].float().cpu().numpy(), x["ks"][layer].float().cpu().numpy(),
+                      x["table"].cpu().numpy(), x["lens"].cpu().numpy(), x["qrow"].cpu().numpy(),
+                      x["select"].cpu().numpy(), 1, lse, 1 / math.sqrt(128), layer, layer % x["kv_heads"], 16, 2)
+    return lse
+
+
+def test_a_refused_call_launches_nothing():
+    """Arguments the step refuses (a group size past 16) return EINVAL before any work is queued: the
+    outputs keep their contents, and the next valid call still gives the workspace step's result."""
+    import ekv._lib as L
+
+    lib = L.load()
+    x = make_inputs(seed=5)
+    lse, share, contrib, status = outputs(x)
+    args = common_args(x, lse)
+    args[23] = 17  # query rows per KV head
+    rc = lib.ekv_audit_step_static(*args, share.data_ptr(), contrib.data_ptr(), L.AGG_MEAN, status.data_ptr(),
+                                   L.current_stream())
+    assert rc == L.EINVAL
+    torch.cuda.synchronize()
+    assert torch.isnan(lse).all() and bool((share == -1.0).all()) and bool((contrib == -1).all())
+    rc = lib.ekv_audit_step_static(*common_args(x, lse), share.data_ptr(), contrib.data_ptr(), L.AGG_MEAN,
+                                   status.data_ptr(), L.current_stream())
+    L.check(rc, "ekv_audit_step_static")
+    torch.cuda.synchronize()
+    ref = oracle_table(x)
+    got = lse.cpu().numpy()
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    np.testing.assert_allclose(got[~np.isnan(ref)], ref[~np.isnan(ref)], **LSE_TOL)
 
 
 def test_a_step_beyond_the_static_workspace_is_rejected():

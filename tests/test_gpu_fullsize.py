@@ -248,8 +248,8 @@ def test_long_context_view_end_to_end(short_rows, runtime_dir):
     want_view, want_lens = oview.compact_block_table(s.table_host, s.lens, keep.astype(bool), BLOCK)
     np.testing.assert_array_equal(view.cpu().numpy(), want_view)
     np.testing.assert_array_equal(view_lens.cpu().numpy(), want_lens)
+    # the budget is spent exactly: the measured rows keep max(pins, ceil(0.2 * their blocks)) blocks
     measured = row_blocks > 256
     assert (keep[~measured] == 1).all()
-    kept = keep[measured].sum(axis=1)
-    assert int(kept.sum()) == max(int(sum(min(6, n) for n in row_blocks[measured])),
-                                  math.ceil(0.2 * int(row_blocks[measured].sum())))
+    kept = sum(int(keep[r, : row_blocks[r]].sum()) for r in np.flatnonzero(measured))
+    assert kept == max(6 * int(measured.sum()), math.ceil(0.2 * int(row_blocks[measured].sum())))

@@ -48,6 +48,7 @@ extern "C" {
 #define EKV_POLICY_SUM 0     /* highest share first; equal shares: the newer block first           */
 #define EKV_POLICY_UNIFORM 1 /* highest share first; equal shares: the older block first           */
 #define EKV_POLICY_NEWEST 2  /* the fixed rule scores = arange(n): the newest open blocks           */
+#define EKV_POLICY_MAXMIN 3  /* ekv_allocate_pinned_f64's objective: raise the lowest retained share */
 
 /* Tiles of one audit work item (a chunk of a row): the unit a warp of the audit kernel takes. */
 #define EKV_AUDIT_CHUNK_TILES 8
@@ -325,6 +326,30 @@ int ekv_allocate_maxmin_f64(const double* scores, int64_t score_stride, const in
                             const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,
                             int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
                             int32_t* quota, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace ekv_allocate_pinned_f64 needs (256-byte aligned); 0 when width > 16383. */
+size_t ekv_allocate_pinned_workspace_bytes(int rows, int width);
+
+/*
+ * ekv_allocate_pinned_f64 -- allocate(requests, budget, objective) with any pinned blocks.
+ *
+ * Replaces allocate (observe/allocation.py:55-76 with _uniform :79-91, _greedy :94-118 and
+ * _water_level :121-166) for requests whose Request.pinned marks any blocks (:37-44), not only the
+ * controller's block 0 and newest suffix. Row r is request r: its n = row_blocks[r] (<= width) float64
+ * scores scores[r][0..n) (NaN counts as 0), pinned[r][0..n) (uint8, nonzero: always kept, not counted
+ * against the open blocks), weights[r] (float64 [rows], `sum` only; NULL: 1.0). objective is
+ * EKV_POLICY_SUM, EKV_POLICY_UNIFORM or EKV_POLICY_MAXMIN. The caller has already checked what the
+ * reference checks on the host: budget >= the pinned blocks of every request, and budget < the blocks
+ * of every request (else every block is kept). Each request's shares are computed once, as
+ * Request.shares computes them (max(score, 0) / total, total NumPy's pairwise sum in block order), and
+ * ranked with the reference's tie rules; mask_out[r][0..n) (uint8, row stride mask_stride) receives
+ * each request's keep mask, [n, width) zero. width <= 16383 (maxmin: 8191). Seven to fourteen kernels
+ * and one memset on `stream`, no host synchronisation.
+ */
+int ekv_allocate_pinned_f64(const double* scores, int64_t score_stride, const uint8_t* pinned,
+                            int64_t pinned_stride, const double* weights, const int32_t* row_blocks, int objective,
+                            int64_t budget, int rows, int width, uint8_t* mask_out, int64_t mask_stride,
+                            void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * ekv_view_build_f64 -- ekv_view_build in ranking mode over float64 scores.

@@ -79,6 +79,10 @@ struct SumParams {
   unsigned long long* keys;  // [rows][width] keys of the unpinned blocks [1, ps)
   unsigned long long* cand_key;  // [rows * width]
   unsigned int* cand_at;         // [rows * width] (row << 15) | block
+  // float64 rows that already hold each request's shares, a pinned block marked by +inf (the pinned
+  // allocation, ekv_allocate_pinned_f64): no total is taken, and a pinned block outranks every gain
+  bool presummed;
+  const long long* budget_add;  // may be NULL: blocks added on the device to a budget given as a count
 };
 
 struct SumLayout {
@@ -118,6 +122,9 @@ __device__ __forceinline__ double clamped(double s) { return s > 0.0 ? s : 0.0; 
 
 // The order-preserving key of request r's gain at a block with score s: the bits of the
 // non-negative float64 gain (0 for a gain of +-0), each operation rounded as NumPy rounds it.
+// The key of a pinned block in a presummed row: the bits of +inf, above every finite gain.
+constexpr unsigned long long kPinnedKey = 0x7ff0000000000000ull;
+
 template <typename S>
 __device__ __forceinline__ unsigned long long gain_key(S s, double total, double w, int n) {
   const double share = total > 0.0 ? __ddiv_rn(clamped(s), total) : __ddiv_rn(1.0, (double)(n > 1 ? n : 1));
@@ -208,7 +215,7 @@ __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p
   for (int i = tid; i < kSumBins; i += kSumThreads) s_hist[i] = 0;
   if (request) {
     stage_row<kSumThreads>(s_x, xg, n);
-    const double sum = block_pairwise_sum<kSumThreads>(s_tree, n, [&](int i) { return clamped(s_x[i]); });
+    const double sum = p.presummed ? 1.0 : block_pairwise_sum<kSumThreads>(s_tree, n, [&](int i) { return clamped(s_x[i]); });
     if (tid == 0) s_total = sum;
     __syncthreads();
     const double total = s_total;
@@ -217,7 +224,7 @@ __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p
     unsigned long long dmask0;
     digit_of(0, shift0, dmask0);
     for (int b = 1 + tid; b < ps; b += kSumThreads) {  // the keys and pass 0 of the select
-      const unsigned long long key = gain_key(s_x[b], total, w, n);
+      const unsigned long long key = p.presummed && isinf((double)s_x[b]) ? kPinnedKey : gain_key(s_x[b], total, w, n);
       kr[b] = key;
       atomicAdd(&s_hist[(key >> shift0) & dmask0], 1u);
     }
@@ -246,6 +253,8 @@ __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p
     if (budget < 0) {
       budget = (long long)ceil(p.fraction * (double)blocks);
       if (budget < must) budget = must;
+    } else if (p.budget_add != nullptr) {
+      budget += *p.budget_add;
     }
     const long long free_ = budget - must;
     if (budget >= blocks || free_ >= total_open) {
@@ -548,7 +557,8 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
                         const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,
                         int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
                         int32_t* quota, uint8_t* mask_out, int64_t mask_stride, void* workspace,
-                        size_t workspace_bytes, void* stream) {
+                        size_t workspace_bytes, void* stream, bool presummed = false,
+                        const long long* budget_add = nullptr) {
   constexpr int max_width = sizeof(S) == 8 ? kSumMaxWidth / 2 : kSumMaxWidth;  // the prep kernel stages a row
   clear_error();
   if (!scores || !row_blocks || !quota) return fail(EKV_EINVAL, "a required pointer is NULL");
@@ -570,6 +580,7 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
   p.measured = measured_blocks; p.recent = recent_blocks; p.cap = cap_above_blocks;
   p.fraction = budget_fraction; p.budget = (long long)budget; p.rows = rows; p.width = width; p.quota = quota;
   p.mask_out = mask_out; p.mask_s0 = mask_stride;
+  p.presummed = presummed; p.budget_add = budget_add;
   p.state = reinterpret_cast<SumState*>(base + l.state);
   p.hist = reinterpret_cast<unsigned int*>(base + l.hist);
   p.ties = reinterpret_cast<unsigned int*>(base + l.ties);
@@ -619,6 +630,20 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
   launch_chained(sum_mask_kernel, dim3(cdiv(width, kSumMaskSpan), rows), dim3(kSumThreads), 0, s, p);
   return check_launch("sum_mask_kernel");
 }
+
+namespace ekv {
+
+// The `sum` objective over presummed float64 rows (see SumParams::presummed), its mask written straight
+// from the threshold.
+int presummed_sum(const double* shares, int64_t share_s0, const double* weights, const int32_t* row_blocks,
+                  const int32_t* measured, long long budget, const long long* budget_add, int rows, int width,
+                  int32_t* quota, uint8_t* mask_out, int64_t mask_s0, void* workspace, size_t workspace_bytes,
+                  cudaStream_t stream) {
+  return allocate_sum<double>(shares, share_s0, nullptr, weights, row_blocks, measured, -1, -1, 0.0, budget, rows,
+                              width, quota, mask_out, mask_s0, workspace, workspace_bytes, stream, true, budget_add);
+}
+
+}  // namespace ekv
 
 extern "C" int ekv_allocate_sum(const float* scores, int64_t score_stride, const double* weights,
                                 const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,

@@ -66,6 +66,9 @@ struct MmParams {
   double* sorted;   // [width][rows] unpinned shares in decreasing order (block-major: a warp's rows adjacent)
   double* prefix;   // [width][rows] their running sums
   uint16_t* wide_lbs;  // [kMmWideStages * kMmWideNodes][rows] each request's search result at the wide levels
+  // float64 rows that already hold each request's shares (the pinned allocation): no total is taken
+  bool presummed;
+  const long long* budget_add;  // may be NULL: blocks added on the device to a budget given as a count
 };
 
 struct MmLayout {
@@ -229,7 +232,8 @@ __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
     const S* xg = static_cast<const S*>(p.scores) +
                   (p.score_rows != nullptr ? (int64_t)p.score_rows[r] : (int64_t)r) * p.score_s0;
     stage_row<kMmThreads>(s_x, xg, n);
-    const double total = block_pairwise_sum<kMmThreads>(s_tree, n, [&](int i) { return mm_clamped(s_x[i]); });
+    const double total =
+        p.presummed ? 1.0 : block_pairwise_sum<kMmThreads>(s_tree, n, [&](int i) { return mm_clamped(s_x[i]); });
     const double equal = __ddiv_rn(1.0, (double)(n > 1 ? n : 1));
     auto share = [&](int i) { return total > 0.0 ? __ddiv_rn(mm_clamped(s_x[i]), total) : equal; };
     // the pinned blocks in index order: block 0 and [ps, n) (every block when ps == 0)
@@ -273,6 +277,8 @@ __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
     if (budget < 0) {
       budget = (long long)ceil(p.fraction * (double)blocks);
       if (budget < must) budget = must;
+    } else if (p.budget_add != nullptr) {
+      budget += *p.budget_add;
     }
     const long long free_ = budget - must;
     st->free_ = free_;
@@ -748,7 +754,8 @@ template <typename S>
 static int allocate_maxmin(const S* scores, int64_t score_stride, const int32_t* score_rows,
                            const int32_t* row_blocks, const int32_t* measured_blocks, int recent_blocks,
                            int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
-                           int32_t* quota, void* workspace, size_t workspace_bytes, void* stream) {
+                           int32_t* quota, void* workspace, size_t workspace_bytes, void* stream,
+                           bool presummed = false, const long long* budget_add = nullptr) {
   clear_error();
   if (!scores || !row_blocks || !quota) return fail(EKV_EINVAL, "a required pointer is NULL");
   if (rows <= 0 || width <= 0) return fail(EKV_EINVAL, "rows and width must be positive");
@@ -768,6 +775,7 @@ static int allocate_maxmin(const S* scores, int64_t score_stride, const int32_t*
   p.measured = measured_blocks;
   p.recent = recent_blocks; p.cap = cap_above_blocks; p.fraction = budget_fraction; p.budget = (long long)budget;
   p.rows = rows; p.width = width; p.quota = quota;
+  p.presummed = presummed; p.budget_add = budget_add;
   p.state = reinterpret_cast<MmState*>(base + l.state);
   p.base = reinterpret_cast<double*>(base + l.base);
   p.row_m = reinterpret_cast<int*>(base + l.row_m);
@@ -816,6 +824,18 @@ static int allocate_maxmin(const S* scores, int64_t score_stride, const int32_t*
   launch_chained(mm_level_kernel, dim3(1), dim3(kMmLevelThreads), level_smem, s, p);
   return check_launch("mm_level_kernel");
 }
+
+namespace ekv {
+
+// The maxmin quotas of presummed float64 rows whose pins are block 0 and [measured[r], n).
+int presummed_maxmin(const double* shares, int64_t share_s0, const int32_t* row_blocks, const int32_t* measured,
+                     long long budget, const long long* budget_add, int rows, int width, int32_t* quota,
+                     void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return allocate_maxmin<double>(shares, share_s0, nullptr, row_blocks, measured, -1, -1, 0.0, budget, rows, width,
+                                 quota, workspace, workspace_bytes, stream, true, budget_add);
+}
+
+}  // namespace ekv
 
 extern "C" int ekv_allocate_maxmin(const float* scores, int64_t score_stride, const int32_t* row_blocks,
                                    const int32_t* measured_blocks, int recent_blocks, int cap_above_blocks,

@@ -27,6 +27,7 @@ struct QuotaParams {
   const double* row_fraction;
   int rows, width;  // width > 0: a request holds min(row_blocks, width) blocks
   int32_t* quota;
+  const long long* budget_add;  // may be NULL: blocks added on the device to a budget given as a count
 };
 
 // The blocks of a request of row_blocks blocks: its length, at most the row width (controller.py:414).
@@ -88,6 +89,8 @@ __global__ void __launch_bounds__(kQuotaThreads) quota_kernel(const QuotaParams 
   if (budget < 0) {
     budget = (long long)ceil(p.fraction * (double)total);
     if (budget < floor_) budget = floor_;
+  } else if (p.budget_add != nullptr) {
+    budget += *p.budget_add;
   }
   const bool keep_all = budget >= total;
   const long long free_ = budget - floor_;
@@ -212,6 +215,8 @@ struct ViewParams {
   // per-row budgets computed in the kernel (ekv_view_build_fractions) instead of read from quota
   const double* row_fraction;
   int cap;
+  // float64 rows that already hold each request's shares (the pinned allocation): ranked as they are
+  bool presummed;
 };
 
 // Row flags of ekv_decode_view (full_rows): the row reads every block / decodes / is audited.
@@ -422,7 +427,7 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
     if constexpr (kWide) {
       const double* s_x = reinterpret_cast<const double*>(keys);
       PairwiseTree& tree = *reinterpret_cast<PairwiseTree*>(smem_view + (size_t)w_pad * (sizeof(K) + 4));
-      const double total = block_pairwise_sum<kViewThreads>(tree, n_a, [&](int i) {
+      const double total = p.presummed ? 1.0 : block_pairwise_sum<kViewThreads>(tree, n_a, [&](int i) {
         const double s = s_x[i];
         return s > 0.0 ? s : 0.0;
       });
@@ -601,6 +606,48 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
 }
 
 template <typename K>
+int launch_view(const ViewParams& p, cudaStream_t stream);
+
+int launch_quota(const QuotaParams& p, size_t smem, cudaStream_t stream) {
+  static bool configured[kMaxDevices] = {};
+  int device = 0;
+  {
+    const int dev_rc = current_device(&device);
+    if (dev_rc != EKV_OK) return dev_rc;
+  }
+  if (!configured[device]) {
+    if (cudaFuncSetAttribute(quota_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kQuotaMaxRows * (int)sizeof(double)) != cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(quota_kernel)");
+    configured[device] = true;
+  }
+  launch_chained(quota_kernel, dim3(1), dim3(kQuotaThreads), smem, stream, p);
+  return check_launch("quota_kernel");
+}
+
+// The uniform quotas of rows whose pins are block 0 and [measured[r], n), with `budget` blocks plus
+// *budget_add (on the device) shared by every row.
+int presummed_quotas(const int32_t* row_blocks, const int32_t* measured, long long budget,
+                     const long long* budget_add, int rows, int width, int32_t* quota, cudaStream_t stream) {
+  if (rows > kQuotaMaxRows) return fail(EKV_ENOTSUP, "%d rows share one budget; at most %d", rows, kQuotaMaxRows);
+  QuotaParams p{row_blocks, measured, -1, -1, 0.0, budget, nullptr, rows, width, quota, budget_add};
+  return launch_quota(p, (size_t)rows * sizeof(double), stream);
+}
+
+// The committed mask (no view) of float64 rows that hold shares, ranked by share, equal shares to the
+// older block, with the quotas given and pins block 0 and [measured[r], n).
+int presummed_mask(const int32_t* row_blocks, const int32_t* quota, const int32_t* measured, const double* shares,
+                   int64_t share_s0, int rows, int width, uint8_t* mask_out, int64_t mask_s0, cudaStream_t stream) {
+  if (width > kViewMaxWidth) return fail(EKV_ENOTSUP, "width %d > %d (a row is staged in shared memory)", width, kViewMaxWidth);
+  ViewParams p{};
+  p.row_blocks = row_blocks; p.quota = quota; p.measured = measured; p.recent = -1;
+  p.scores = shares; p.score_s0 = share_s0; p.policy = EKV_POLICY_UNIFORM;
+  p.rows = rows; p.width = width; p.block_size = 1; p.mask_out = mask_out; p.mask_s0 = mask_s0; p.cap = -1;
+  p.presummed = true;
+  return launch_view<unsigned long long>(p, stream);
+}
+
+template <typename K>
 int launch_view(const ViewParams& p, cudaStream_t stream) {
   const size_t smem = view_smem_bytes<K>(p.width);
   static size_t configured[kMaxDevices] = {};
@@ -643,22 +690,9 @@ extern "C" int ekv_allocate_quotas(const int32_t* row_blocks, const int32_t* mea
   } else if (rows > 65536) {
     return fail(EKV_ENOTSUP, "rows <= 65536");
   }
-  static bool configured[kMaxDevices] = {};
-  int device = 0;
-  {
-    const int dev_rc = current_device(&device);
-    if (dev_rc != EKV_OK) return dev_rc;
-  }
-  if (!configured[device]) {
-    if (cudaFuncSetAttribute(quota_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kQuotaMaxRows * (int)sizeof(double)) != cudaSuccess)
-      return check_launch("cudaFuncSetAttribute(quota_kernel)");
-    configured[device] = true;
-  }
   QuotaParams p{row_blocks, measured_blocks, recent_blocks, cap_above_blocks, budget_fraction,
-                (long long)budget, row_fraction, rows, width, quota};
-  launch_chained(quota_kernel, dim3(1), dim3(kQuotaThreads), smem, static_cast<cudaStream_t>(stream), p);
-  return check_launch("quota_kernel");
+                (long long)budget, row_fraction, rows, width, quota, nullptr};
+  return launch_quota(p, smem, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ekv_view_build(const int32_t* table, int64_t table_stride, const int32_t* seq_lens,

@@ -19,7 +19,7 @@ DTYPE_F16, DTYPE_BF16 = 0, 1
 AGG_MEAN, AGG_MAX = 0, 1
 SHARE_FINALIZE = 2
 STATUS_BAD_BLOCK_ID, STATUS_LEN_OVER_WIDTH, STATUS_BAD_QROW, STATUS_WAIT_TIMEOUT = 1, 2, 4, 8
-POLICY_SUM, POLICY_UNIFORM, POLICY_NEWEST = 0, 1, 2
+POLICY_SUM, POLICY_UNIFORM, POLICY_NEWEST, POLICY_MAXMIN = 0, 1, 2, 3
 AUDIT_CHUNK_TILES = 8
 
 _c = ctypes
@@ -87,6 +87,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "ekv_allocate_maxmin_f64": (
         _i32, [_p, _i64, _p, _p, _p, _i32, _i32, _f64, _i64, _i32, _i32, _p, _p, ctypes.c_size_t, _p],
+    ),
+    "ekv_allocate_pinned_workspace_bytes": (ctypes.c_size_t, [_i32, _i32]),
+    "ekv_allocate_pinned_f64": (
+        _i32, [_p, _i64, _p, _i64, _p, _p, _i32, _i64, _i32, _i32, _p, _i64, _p, ctypes.c_size_t, _p],
     ),
     "ekv_view_build_f64": (
         _i32,

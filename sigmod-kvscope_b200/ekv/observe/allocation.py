@@ -61,8 +61,8 @@ class Request:
         return scores / total
 
 
-def _pin_start(pinned: np.ndarray) -> int:
-    """``ps`` with pinned == {0} | [ps, n) (the controller's pins); RuntimeError for other pin sets."""
+def _pin_start(pinned: np.ndarray) -> int | None:
+    """``ps`` with pinned == {0} | [ps, n) (the controller's pins), or None for any other pin set."""
     n = len(pinned)
     if n == 0:
         return 0
@@ -72,9 +72,7 @@ def _pin_start(pinned: np.ndarray) -> int:
     expected = np.zeros(n, dtype=bool)
     expected[0] = True
     expected[tail:] = True
-    if not np.array_equal(pinned, expected):
-        raise RuntimeError("the device allocation supports pins of block 0 and a newest suffix only")
-    return tail
+    return tail if np.array_equal(pinned, expected) else None
 
 
 def _score_layout(scores: torch.Tensor, row_blocks: torch.Tensor, score_rows: torch.Tensor | None) -> tuple[int, int]:
@@ -193,13 +191,15 @@ def allocate(requests: Sequence[Request], budget: int, objective: Objective = "s
     for r, req in enumerate(requests):
         s = np.asarray(req.scores, dtype=np.float64)
         scores[r, : sizes[r]] = np.where(np.isnan(s), 0.0, s)
-    # pins {0} | [pin_start, n): passed as the "measured" start, with no recent pins of their own
-    pin_starts = torch.tensor([_pin_start(p) for p in pinned], dtype=torch.int32)
     device = torch.device("cuda", torch.cuda.current_device())
     lib = _lib.load()
     stream = _lib.current_stream()
     row_blocks = torch.tensor(sizes, dtype=torch.int32).to(device)
-    measured = pin_starts.to(device)
+    starts = [_pin_start(p) for p in pinned]
+    if any(start is None for start in starts):
+        return _allocate_pinned(scores, pinned, sizes, requests, budget, objective, row_blocks)
+    # pins {0} | [pin_start, n): passed as the "measured" start, with no recent pins of their own
+    measured = torch.tensor(starts, dtype=torch.int32).to(device)
     quota = torch.empty(rows, dtype=torch.int32, device=device)
     scores_t = torch.from_numpy(scores).to(device)
     if objective == "uniform":
@@ -221,5 +221,36 @@ def allocate(requests: Sequence[Request], budget: int, objective: Objective = "s
             mask.data_ptr(), width, stream,
         )
         _lib.check(rc, "ekv_view_build_f64")
+    out = mask.cpu().numpy().astype(bool)
+    return [out[r, : sizes[r]].copy() for r in range(rows)]
+
+
+def _allocate_pinned(scores: np.ndarray, pinned: list[np.ndarray], sizes: list[int], requests: Sequence[Request],
+                     budget: int, objective: Objective, row_blocks: torch.Tensor) -> list[np.ndarray]:
+    """``allocate`` for pins other than block 0 and a newest suffix (``ekv_allocate_pinned_f64``): the shares
+    are computed and ranked on the device with the pinned blocks brought to the kernels' pin shape."""
+    rows, width = scores.shape
+    lib = _lib.load()
+    size = int(lib.ekv_allocate_pinned_workspace_bytes(rows, width))
+    if size == 0:
+        raise RuntimeError(f"requests of {width} blocks with arbitrary pins exceed the device allocation's 16383")
+    device = row_blocks.device
+    pin = np.zeros((rows, width), dtype=np.uint8)
+    for r, p in enumerate(pinned):
+        pin[r, : sizes[r]] = p
+    scores_t = torch.from_numpy(scores).to(device)
+    pin_t = torch.from_numpy(pin).to(device)
+    weights = None
+    if objective == "sum":
+        weights = torch.tensor([float(r.weight) for r in requests], dtype=torch.float64).to(device)
+    code = {"sum": _lib.POLICY_SUM, "uniform": _lib.POLICY_UNIFORM, "maxmin": _lib.POLICY_MAXMIN}[objective]
+    workspace = torch.empty(size + 256, dtype=torch.uint8, device=device)
+    base = (workspace.data_ptr() + 255) // 256 * 256
+    mask = torch.empty(rows, width, dtype=torch.uint8, device=device)
+    rc = lib.ekv_allocate_pinned_f64(
+        scores_t.data_ptr(), width, pin_t.data_ptr(), width, _lib.ptr(weights), row_blocks.data_ptr(), code,
+        int(budget), rows, width, mask.data_ptr(), width, base, size, _lib.current_stream(),
+    )
+    _lib.check(rc, "ekv_allocate_pinned_f64")
     out = mask.cpu().numpy().astype(bool)
     return [out[r, : sizes[r]].copy() for r in range(rows)]

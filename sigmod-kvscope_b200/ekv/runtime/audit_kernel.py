@@ -23,7 +23,7 @@ import numpy as np
 import torch
 
 from .. import _lib
-from .audit import AuditPlane, runtime_dir
+from .audit import AuditPlane, StatBlock, runtime_dir
 
 TILE_BLOCKS = 2  # blocks per tile: one value per tile, as the reference kernel records
 
@@ -69,7 +69,6 @@ class RecordingPlane(AuditPlane):
             raise ValueError(f"unknown aggregate {aggregate!r}")
         if heads < 1:
             raise ValueError("heads must be positive")
-        self._layers = layers
         self.rows, self.width, self.group_rows, self.block_size = rows, width, group_rows, block_size
         self.heads = heads
         self.cell = heads * group_rows  # values per (layer, row, block)
@@ -82,8 +81,8 @@ class RecordingPlane(AuditPlane):
         lse_bytes = 2 * layers * rows * width * self.cell * 4
         self._lse = self._allocate(lse_bytes)
         self._cuda.cudaMemset(ctypes.c_void_p(self._lse), 0xFF, ctypes.c_size_t(lse_bytes))  # NaN: unwritten
-        self._flag_dev = self._allocate(4)
-        self._table_dev = self._allocate(layers * 8)
+        # the block's control words: its own, so there is nothing to discover
+        self._block = StatBlock(self._allocate(4), self._allocate(layers * 8), layers)
         self._cuda.cudaMemset(ctypes.c_void_p(self._flag_dev), 0, ctypes.c_size_t(4))
         self._cuda.cudaMemset(ctypes.c_void_p(self._table_dev), 0, ctypes.c_size_t(layers * 8))
         device = torch.device("cuda", torch.cuda.current_device())
@@ -157,15 +156,13 @@ class RecordingPlane(AuditPlane):
         with open(path.replace("ekv_pass_", "ekv_coverage_"), "a") as f:
             f.write(json.dumps(coverage) + "\n")
 
-    def _discover(self) -> bool:
-        return True  # the block exists from construction
-
     def close(self) -> None:
         """Free the cudaMalloc blocks (the tensors go with the object)."""
         for address in (self._lse, self._flag_dev, self._table_dev):
             if address:
                 self._cuda.cudaFree(ctypes.c_void_p(address))
-        self._lse = self._flag_dev = self._table_dev = 0
+        self._lse = 0
+        self._block = None
 
     # -- the engine-facing calls -------------------------------------------------------------------
 

@@ -204,14 +204,29 @@ def plan_view(
     )
 
 
+# One host record per scheduler row: the fields the scheduler-facing decisions read and the controller's
+# writes change (audit: the row's next decode step is an audit; audited: its request has had a completed
+# audit; blocks: the request's length in blocks at that audit).
+_ROW = np.dtype([("audit", "?"), ("audited", "?"), ("blocks", "<i8")])
+
+
 class DecodeView:
     """The committed read policy of one serving process, and the view it gives each decode batch.
 
-    Same contract as the reference's DecodeView (block_view.py:59-401): the controller's
-    generations arrive through the ``write_*`` methods; an expired or never-committed lease gives
-    the identity view; a row asked to audit reads in full for one decode step, which consumes the
-    request; prefill rows read in full; released blocks are never read. The keep algebra and the
-    compaction run in one device kernel per step into fixed-address buffers (CUDA-graph safe).
+    The reference's contract (runtime/block_view.py:59-401): the controller's generations arrive through
+    the ``write_*`` methods; an expired or never-committed lease gives the identity view; a row asked to
+    audit reads in full for one decode step, which consumes the request; prefill rows read in full;
+    released blocks are never read.
+
+    State lives where it is used. The committed mask and the released blocks are device tensors (one
+    ``[2, rows + 2, width]`` uint8 tensor: plane 0 the policy, plane 1 the released blocks, and two spare
+    rows holding a fresh row's values): a commit is one asynchronous copy, a reassignment of rows one
+    gather on the device, and ``build`` reads them in place in one ``ekv_decode_view`` launch into
+    fixed-address view buffers (CUDA-graph safe). The per-row flags the host decides with (audit
+    requests, completed audits and their lengths) are one host record array whose fields are the public
+    ``audit_rows``, ``row_audited`` and ``audited_blocks``. ``keep`` and ``released`` read the device state
+    back as host arrays (and assigning them writes it). The device is the current CUDA device, or
+    ``device``; without one the writes still work and ``build`` raises.
     """
 
     def __init__(
@@ -221,6 +236,8 @@ class DecodeView:
         block_size: int,
         audit: StatisticSwitch | None = None,
         prefill_audit: bool = False,
+        *,
+        device: torch.device | None = None,
     ) -> None:
         if min(rows, width, block_size) <= 0:
             raise ValueError("view dimensions must be positive")
@@ -229,36 +246,70 @@ class DecodeView:
         self.rows, self.width, self.block_size = rows, width, block_size
         self.audit = audit
         self.prefill_audit = prefill_audit
-        self.final_prefill = np.zeros(rows, dtype=bool)
-        self.on_prefill_audit: Callable[[], None] | None = None
-        self.keep = np.ones((rows, width), dtype=bool)
-        self.released = np.zeros((rows, width), dtype=bool)
-        self.released_version = 0
-        self.row_audited = np.zeros(rows, dtype=bool)
-        self.audited_blocks = np.zeros(rows, dtype=np.int64)
-        self._pending_blocks = np.zeros(rows, dtype=np.int64)
-        self.audit_rows = np.zeros(rows, dtype=bool)
-        self.last_audit_rows = np.zeros(rows, dtype=bool)
-        self.deadline_ns = 0
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+        self.device = device
+        self._records = np.zeros(rows + 2, dtype=_ROW)  # the two spares: a new request's row, an empty row
+        self.audit_rows = self._records["audit"][:rows]
+        self.row_audited = self._records["audited"][:rows]
+        self.audited_blocks = self._records["blocks"][:rows]
+        self.final_prefill = np.zeros(rows, dtype=bool)  # rows computing their prompt's last tokens next step
+        self.last_audit_rows = np.zeros(rows, dtype=bool)  # rows read in full at the last completed audit
+        self._masks = torch.zeros(2, rows + 2, width, dtype=torch.uint8, device=device)
+        self._masks[0] = 1  # no commit yet: every block
+        self._any_released = False
         self.version = 0
+        self.released_version = 0
+        self.deadline_ns = 0
         self.audit_step = False
-        self.audits_completed = 0
         self.audits_started = 0
+        self.audits_completed = 0
+        # hooks of the serving integration: before a build, when an audit starts, whether one may start, and
+        # when an audit step serves a prefilling row (the plane's check)
+        self.before_build: Callable[[], None] | None = None
         self.on_audit_start: Callable[[], None] | None = None
         self.audit_gate: Callable[[], bool] | None = None
-        self.before_build: Callable[[], None] | None = None
+        self.on_prefill_audit: Callable[[], None] | None = None
+        # the audit step in flight: its rows, and the lengths in blocks it read them at (device or host)
         self._audit_pending = False
         self._pending_rows = np.zeros(rows, dtype=bool)
-        self._counts: torch.Tensor | None = None
-        self._flag_ring: list[torch.Tensor] | None = None
-        self._flag_slot = 0
-        self._device: torch.device | None = None
-        self._device_keep: torch.Tensor | None = None
-        self._device_version = -1
-        self._device_released: torch.Tensor | None = None
-        self._released_device_version = -1
+        self._pending_blocks: torch.Tensor | np.ndarray | None = None
+        self._counts = torch.zeros(5, dtype=torch.int64, device=device)
         self._table: torch.Tensor | None = None
         self._lens: torch.Tensor | None = None
+        self._flag_ring: list[torch.Tensor] | None = None
+        self._flag_slot = 0
+
+    # -- the device state, read back and written as host arrays ------------------------------------
+
+    @property
+    def keep(self) -> np.ndarray:
+        """The committed mask, bool [rows, width] (a copy read from the device)."""
+        return self._masks[0, : self.rows].cpu().numpy().astype(bool)
+
+    @keep.setter
+    def keep(self, mask: np.ndarray) -> None:
+        self._upload(0, np.asarray(mask) != 0)
+
+    @property
+    def released(self) -> np.ndarray:
+        """The released blocks, bool [rows, width] (a copy read from the device)."""
+        return self._masks[1, : self.rows].cpu().numpy().astype(bool)
+
+    @released.setter
+    def released(self, mask: np.ndarray) -> None:
+        mask = np.asarray(mask) != 0
+        self._upload(1, mask)
+        self._any_released = bool(mask.any())
+        self.released_version += 1
+
+    def _upload(self, plane: int, mask: np.ndarray) -> None:
+        if mask.shape != (self.rows, self.width):
+            raise ValueError(f"mask shape {mask.shape} != view shape {(self.rows, self.width)}")
+        host = torch.from_numpy(mask.astype(np.uint8))
+        if self.device.type == "cuda":
+            host = host.pin_memory()
+        self._masks[plane, : self.rows].copy_(host, non_blocking=True)
 
     # -- the controller-facing writes ------------------------------------------------------------
 
@@ -266,10 +317,7 @@ class DecodeView:
         """Commit one generation: ``mask[row, block]`` nonzero means read that block."""
         if log_weight is not None:
             raise ValueError("a block-table view enforces hard keep decisions only")
-        mask = np.asarray(mask)
-        if mask.shape != self.keep.shape:
-            raise ValueError(f"mask shape {mask.shape} != view shape {self.keep.shape}")
-        self.keep = mask != 0
+        self.keep = mask
         self.version += 1
         return 1
 
@@ -280,54 +328,63 @@ class DecodeView:
     def write_audit_rows(self, requested: np.ndarray) -> int:
         """Ask for an audit of the marked rows; each request is consumed by one decode step."""
         requested = np.asarray(requested, dtype=bool)
-        if requested.shape != self.audit_rows.shape:
-            raise ValueError(f"audit shape {requested.shape} != {self.audit_rows.shape}")
-        if requested.any() and self.audit is None:
+        if requested.shape != (self.rows,):
+            raise ValueError(f"audit shape {requested.shape} != {(self.rows,)}")
+        if self.audit is None and requested.any():
             raise ValueError("an audit was requested but the view has no audit plane to switch the statistic on")
-        self.audit_rows |= requested
+        np.logical_or(self.audit_rows, requested, out=self.audit_rows)
         return 1
 
     def write_final_prefill(self, rows: np.ndarray) -> None:
+        """Mark the rows that compute the last tokens of their prompt in the next step (that step only)."""
         rows = np.asarray(rows, dtype=bool)
-        if rows.shape[0] > self.rows:
-            raise ValueError(f"{rows.shape[0]} rows exceed the view's {self.rows}")
-        self.final_prefill[:] = False
-        self.final_prefill[: rows.shape[0]] = rows
+        if len(rows) > self.rows:
+            raise ValueError(f"{len(rows)} rows exceed the view's {self.rows}")
+        self.final_prefill.fill(False)
+        self.final_prefill[: len(rows)] = rows
 
     def write_release(self, mask: np.ndarray) -> list[tuple[int, int]]:
-        """Mark blocks released; only blocks an audit of the row's request covered, never block 0 or
-        the last block at that audit. Returns the new (row, block) pairs."""
+        """Release the marked blocks a completed audit of the row's request covered, except block 0 and the
+        request's last block at that audit; returns the (row, block) pairs released now."""
         mask = np.asarray(mask) != 0
-        if mask.shape != self.released.shape:
-            raise ValueError(f"release shape {mask.shape} != view shape {self.released.shape}")
-        eligible = np.zeros_like(mask)
-        for row in np.flatnonzero(self.row_audited):
-            eligible[row, : max(int(self.audited_blocks[row]) - 1, 0)] = True
-        eligible[:, 0] = False
-        new = mask & eligible & ~self.released
-        rows, blocks = np.nonzero(new)
-        if rows.size:
-            self.released |= new
+        if mask.shape != (self.rows, self.width):
+            raise ValueError(f"release shape {mask.shape} != view shape {(self.rows, self.width)}")
+        # the covered blocks of a row: [1, blocks - 1) once its request has had an audit
+        covered_end = np.where(self.row_audited, np.maximum(self.audited_blocks - 1, 0), 0)
+        if not covered_end.any() or not mask.any():
+            return []
+        dev = self.device
+        pos = torch.arange(self.width, device=dev)
+        covered = (pos[None, :] >= 1) & (pos[None, :] < torch.from_numpy(covered_end).to(dev)[:, None])
+        freed = self._masks[1, : self.rows]
+        fresh = torch.from_numpy(mask).to(dev) & covered & (freed == 0)
+        pairs = fresh.nonzero().cpu().tolist()
+        if pairs:
+            freed |= fresh.to(torch.uint8)
+            self._any_released = True
             self.released_version += 1
-        return list(zip(rows.tolist(), blocks.tolist(), strict=True))
+        return [(int(r), int(b)) for r, b in pairs]
 
     def reassign_rows(self, moved: dict[int, int], new: list[int], empty: list[int]) -> None:
-        """The scheduler changed which request each row holds (reference :166-199)."""
-        keep, audit = self.keep.copy(), self.audit_rows.copy()
-        released, audited, blocks = self.released.copy(), self.row_audited.copy(), self.audited_blocks.copy()
-        for row, old in moved.items():
-            keep[row], audit[row] = self.keep[old], self.audit_rows[old]
-            released[row], audited[row], blocks[row] = self.released[old], self.row_audited[old], self.audited_blocks[old]
-        for row in new:
-            keep[row], audit[row] = True, self.audit is not None
-            released[row], audited[row], blocks[row] = False, False, 0
-        for row in empty:
-            keep[row], audit[row] = True, False
-            released[row], audited[row], blocks[row] = False, False, 0
-        self.keep, self.audit_rows = keep, audit
-        if (released != self.released).any():
+        """The scheduler changed which request each row holds (reference :166-199): a moved request takes its
+        row's state along, a new one starts with full reads (and, with an audit plane, an audit at its first
+        decode step), an empty row holds nothing. One gather of the host records and one of the device
+        masks, from a source row per row (the two spares give the fresh rows)."""
+        spare_new, spare_empty = self.rows, self.rows + 1
+        source = np.arange(self.rows)
+        if moved:
+            source[np.fromiter(moved.keys(), dtype=np.int64)] = np.fromiter(moved.values(), dtype=np.int64)
+        source[np.asarray(new, dtype=np.int64)] = spare_new
+        source[np.asarray(empty, dtype=np.int64)] = spare_empty
+        self._records[spare_new] = (self.audit is not None, False, 0)
+        self._records[spare_empty] = (False, False, 0)
+        self._records[: self.rows] = self._records[source]
+        # the spare device rows hold a fresh row: every block kept, none released
+        self._masks[0, self.rows :] = 1
+        self._masks[1, self.rows :] = 0
+        self._masks[:, : self.rows] = self._masks[:, torch.from_numpy(source).to(self.device)]
+        if self._any_released:
             self.released_version += 1
-        self.released, self.row_audited, self.audited_blocks = released, audited, blocks
         self.version += 1
 
     # -- the engine-facing view -----------------------------------------------------------------
@@ -335,31 +392,15 @@ class DecodeView:
     def active(self) -> bool:
         return self.deadline_ns > time.monotonic_ns()
 
-    def build(
-        self, table: torch.Tensor, seq_lens: torch.Tensor, query_lens: torch.Tensor
-    ) -> tuple[torch.Tensor, torch.Tensor]:
-        """The view buffers (table, lengths) for a batch of ``len(query_lens)`` rows (reference :225-295)."""
-        if self.before_build is not None:
-            self.before_build()
-        live = self.active()
-        self.finish_audit()
-        self._device = table.device
-        num_reqs = len(query_lens)
-        width = table.shape[1]
-        if width != self.width or num_reqs > self.rows:
-            raise ValueError(f"batch ({num_reqs} rows, {width} blocks) exceeds view ({self.rows}, {self.width})")
-        if self._table is None:
-            self._table = torch.zeros(self.rows, width, dtype=torch.int32, device=table.device)
-            self._lens = torch.zeros(self.rows, dtype=torch.int32, device=table.device)
-        assert self._lens is not None
-        decode = query_lens.numpy() == 1
-        servable = decode | (self.final_prefill[:num_reqs] & self.prefill_audit)
-        self.final_prefill[:] = False
+    def _begin_step(self, servable: np.ndarray, decode: np.ndarray | None) -> np.ndarray:
+        """The rows this step audits, out of the first ``len(servable)``: requested and servable, when the gate
+        allows an audit now. Their requests are consumed, the step is marked and published as started."""
+        n = len(servable)
         audited = np.zeros(self.rows, dtype=bool)
-        audited[:num_reqs] = self.audit_rows[:num_reqs] & servable
+        np.logical_and(self.audit_rows[:n], servable, out=audited[:n])
         if audited.any() and not self.may_audit():
-            audited[:] = False
-        if (audited[:num_reqs] & ~decode).any() and self.on_prefill_audit is not None:
+            audited.fill(False)  # the requests wait for a step after the controller has read the last audit
+        if decode is not None and self.on_prefill_audit is not None and (audited[:n] & ~decode).any():
             self.on_prefill_audit()
         self.audit_rows[audited] = False
         self.audit_step = bool(audited.any())
@@ -367,39 +408,63 @@ class DecodeView:
         self._pending_rows = audited
         if self.audit_step:
             self.start_audit()
-            size = self.block_size
-            self._pending_blocks[:num_reqs] = ((seq_lens[:num_reqs] + size - 1) // size).cpu().numpy()
-        # one flag byte per row: it reads every block (an expired lease, an audited row, a prefill row),
-        # it decodes, it is audited; the view kernel applies them and counts the reads (:272-329)
-        full = np.ones(num_reqs, dtype=bool) if not live else (audited[:num_reqs] | ~decode)
-        flags = full.astype(np.uint8) | (decode.astype(np.uint8) << 1) | (audited[:num_reqs].astype(np.uint8) << 2)
-        row_flags = self._flags_on(flags, table.device)
-        keep = self._keep_on(table.device)[:num_reqs]
-        released = self._released_on(table.device)[:num_reqs] if self.released.any() else None
-        if self.audit is not None:
-            starts = np.concatenate(([0], np.cumsum(query_lens.numpy())[:-1]))
-            self.audit.select(audited[:num_reqs], starts)
-            self.audit.set(self.audit_step)
-        if self._counts is None:
-            self._counts = torch.zeros(5, dtype=torch.int64, device=table.device)
-        t = table[:num_reqs]
+        return audited
+
+    def build(
+        self, table: torch.Tensor, seq_lens: torch.Tensor, query_lens: torch.Tensor
+    ) -> tuple[torch.Tensor, torch.Tensor]:
+        """The view buffers (table, lengths) for a batch of ``len(query_lens)`` rows (reference :225-295).
+
+        ``query_lens`` (host) is the tokens each row computes: one token decodes and gets the view; more is a
+        prefill, which reads in full. The lease is read once, first; the keep algebra, the compaction and
+        the read counters then run in one kernel with no host synchronisation."""
+        if self.before_build is not None:
+            self.before_build()
+        live = self.active()
+        self.finish_audit()
+        n = len(query_lens)
+        if table.shape[1] != self.width or n > self.rows:
+            raise ValueError(f"batch ({n} rows, {table.shape[1]} blocks) exceeds view ({self.rows}, {self.width})")
+        if table.device != self.device or self.device.type != "cuda":
+            raise RuntimeError(f"the view builds on its CUDA device {self.device}; the batch is on {table.device}")
+        t = table[:n]
         if t.dtype != torch.int32 or seq_lens.dtype != torch.int32 or t.stride(1) != 1:
             raise ValueError("the block table (rows contiguous) and the lengths must be int32")
+        if self._table is None:
+            self._table = torch.zeros(self.rows, self.width, dtype=torch.int32, device=self.device)
+            self._lens = torch.zeros(self.rows, dtype=torch.int32, device=self.device)
+        decode = query_lens.numpy() == 1
+        servable = decode | (self.final_prefill[:n] & self.prefill_audit)
+        self.final_prefill.fill(False)
+        audited = self._begin_step(servable, decode)
+        if self.audit_step:  # each audited request's length in blocks, kept on the device until the step ends
+            self._pending_blocks = (seq_lens[:n].long() + self.block_size - 1) // self.block_size
+        # one flag byte per row for the kernel: reads every block (no live lease, audited, prefilling), decodes,
+        # audited
+        full = ~decode | audited[:n] if live else np.ones(n, dtype=bool)
+        flags = full.astype(np.uint8) | (decode.astype(np.uint8) << 1) | (audited[:n].astype(np.uint8) << 2)
+        row_flags = self._flags_on(flags)
+        if self.audit is not None:
+            starts = np.zeros(n, dtype=np.int64)
+            np.cumsum(query_lens.numpy()[:-1], out=starts[1:])
+            self.audit.select(audited[:n], starts)
+            self.audit.set(self.audit_step)
+        keep, freed = self._masks[0, :n], self._masks[1, :n]
         rc = _lib.load().ekv_decode_view(
             t.data_ptr(), t.stride(0), seq_lens.data_ptr(), keep.data_ptr(), keep.stride(0), row_flags.data_ptr(),
-            _ptr(released), 0 if released is None else released.stride(0), int(not live), num_reqs, width,
+            freed.data_ptr() if self._any_released else None, freed.stride(0), int(not live), n, self.width,
             self.block_size, self._table.data_ptr(), self._table.stride(0), self._lens.data_ptr(),
             self._counts.data_ptr(), _lib.current_stream(),
         )
         _lib.check(rc, "ekv_decode_view")
-        return self._table[:num_reqs], self._lens[:num_reqs]
+        return self._table[:n], self._lens[:n]
 
-    def _flags_on(self, flags: np.ndarray, device: torch.device) -> torch.Tensor:
+    def _flags_on(self, flags: np.ndarray) -> torch.Tensor:
         """The row flags on the device, through a ring of pinned buffers: no copy waits for the device."""
         if self._flag_ring is None:
             self._flag_ring = [torch.empty(self.rows, dtype=torch.uint8).pin_memory() for _ in range(4)]
             self._flag_done: list[torch.cuda.Event | None] = [None] * 4
-            self._flags_dev = torch.zeros(self.rows, dtype=torch.uint8, device=device)
+            self._flags_dev = torch.zeros(self.rows, dtype=torch.uint8, device=self.device)
         slot = self._flag_slot = (self._flag_slot + 1) % len(self._flag_ring)
         if self._flag_done[slot] is not None:
             self._flag_done[slot].synchronize()  # its copy four steps ago has long finished
@@ -410,23 +475,6 @@ class DecodeView:
         self._flag_done[slot] = done
         return self._flags_dev
 
-    def _count(self, read_lens, full_lens, decoding, audited=None, expired: bool = False) -> None:
-        """Read counters of decode rows: read, full, audited, untrimmed-live, expired (reference :297-329)."""
-        if self._counts is None:
-            self._counts = torch.zeros(5, dtype=torch.int64, device=read_lens.device)
-        size = self.block_size
-        read = (read_lens.long() + size - 1) // size
-        full = (full_lens.long() + size - 1) // size
-        whole = read_lens == full_lens
-        if decoding is not None:
-            read, full = read * decoding, full * decoding
-        in_audit = torch.zeros_like(whole) if audited is None else audited
-        live_whole = whole & ~in_audit & (not expired)
-        zero = torch.zeros((), dtype=torch.int64, device=read.device)
-        self._counts += torch.stack(
-            [read.sum(), full.sum(), (read * in_audit).sum(), (read * live_whole).sum(), read.sum() if expired else zero]
-        )
-
     @property
     def buffers(self) -> tuple[torch.Tensor, torch.Tensor]:
         if self._table is None or self._lens is None:
@@ -434,25 +482,25 @@ class DecodeView:
         return self._table, self._lens
 
     def reads(self) -> tuple[int, int]:
-        if self._counts is None:
-            return 0, 0
-        read, full = (int(x) for x in self._counts.tolist()[:2])
-        return read, full
+        read, full = self._counts[:2].tolist()
+        return int(read), int(full)
 
     def read_breakdown(self) -> dict[str, int]:
         names = ("read", "full", "audit", "untrimmed", "expired")
-        if self._counts is None:
-            return dict.fromkeys(names, 0)
-        return dict(zip(names, (int(x) for x in self._counts.tolist()), strict=True))
+        return {name: int(x) for name, x in zip(names, self._counts.tolist(), strict=True)}
 
     def skip(self, seq_lens: torch.Tensor, query_lens: torch.Tensor) -> None:
-        """A shared-prefix batch reads the engine's own table; its decode rows count as full reads."""
+        """A shared-prefix batch reads the engine's own table and records nothing; its decode rows count as
+        full reads read with a live policy and no evidence."""
         self.finish_audit()
         self.audit_step = False
         if self.audit is not None:
             self.audit.set(False)
+        n = len(query_lens)
         decoding = torch.from_numpy(query_lens.numpy() == 1).to(seq_lens.device)
-        self._count(seq_lens[: len(query_lens)], seq_lens[: len(query_lens)], decoding)
+        blocks = ((seq_lens[:n].long() + self.block_size - 1) // self.block_size * decoding).sum()
+        zero = torch.zeros((), dtype=torch.int64, device=blocks.device)
+        self._counts += torch.stack([blocks, blocks, zero, blocks, zero]).to(self._counts.device)
 
     def may_audit(self) -> bool:
         return self.audit_gate is None or self.audit_gate()
@@ -463,178 +511,198 @@ class DecodeView:
             self.on_audit_start()
 
     def finish_audit(self) -> None:
-        """Count the previous step as a completed audit once the device has finished it (one sync)."""
+        """Count the step before as a completed audit, once the work queued for it on this stream has run: its
+        statistic is then complete (an audit step's only wait). Runs before rows are reassigned."""
         if not self._audit_pending:
             return
-        if self._device is not None and self._device.type == "cuda":
-            torch.cuda.synchronize(self._device)
-        self.last_audit_rows = self._pending_rows
-        self.row_audited |= self._pending_rows
-        self.audited_blocks[self._pending_rows] = self._pending_blocks[self._pending_rows]
+        if self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).synchronize()
+        blocks = self._pending_blocks
+        if isinstance(blocks, torch.Tensor):
+            blocks = blocks.cpu().numpy()  # already computed: the wait above covers it
+        rows = self._pending_rows
+        self.last_audit_rows = rows
+        self.row_audited[rows] = True
+        k = len(blocks)  # the audited rows are rows of that batch
+        self.audited_blocks[:k][rows[:k]] = np.asarray(blocks)[rows[:k]]
         self.audits_completed += 1
         self._audit_pending = False
 
-    def _keep_on(self, device: torch.device) -> torch.Tensor:
-        if self._device_keep is None or self._device_version != self.version:
-            self._device_keep = torch.from_numpy(self.keep.astype(np.uint8)).to(device, non_blocking=True)
-            self._device_version = self.version
-        return self._device_keep
 
-    def _released_on(self, device: torch.device) -> torch.Tensor:
-        if self._device_released is None or self._released_device_version != self.released_version:
-            self._device_released = torch.from_numpy(self.released.astype(np.uint8)).to(device, non_blocking=True)
-            self._released_device_version = self.released_version
-        return self._device_released
-
-
-# -- vLLM integration (the patch targets of the reference, block_view.py:404-626) ---------------------
+# -- vLLM integration: the reference's patch targets (runtime/block_view.py:404-626) -------------------------
+#
+# The process's view and audit plane are made by its first attention batch (the engine's own row count,
+# table width and block size), so the CUDA graphs vLLM captures then read the view's fixed buffers.
 
 _view: DecodeView | None = None
 _plane: AuditPlane | None = None
-_layers: tuple[str, ...] = ()
+_layers: tuple[str, ...] = ()  # the attention layers of the one KV-cache group the view serves
 
 
 def _enabled(name: str) -> bool:
     return os.environ.get(name, "") not in ("", "0", "false")
 
 
-def _audit_plane(builder, cam) -> AuditPlane | None:
-    """The plane that records the statistic: the audit kernel's (EKV_AUDIT_KERNEL) or none.
-
-    The reference's compiler pass (EKV_ATTN_SHARE) instruments Triton kernels; this build has no
-    Triton path, so asking for it is an error."""
-    if _enabled("EKV_ATTN_SHARE"):
-        raise RuntimeError("EKV_ATTN_SHARE needs the Triton compiler pass; this build records with EKV_AUDIT_KERNEL")
-    if _enabled("EKV_AUDIT_KERNEL"):
-        from .audit_kernel import RecordingPlane
-
-        model, parallel = builder.vllm_config.model_config, builder.vllm_config.parallel_config
-        return RecordingPlane(
-            layers=model.get_num_layers_by_block_type(parallel, "attention"),
-            rows=builder.vllm_config.scheduler_config.max_num_seqs,
-            width=cam.block_table_tensor.shape[1],
-            group_rows=model.get_num_attention_heads(parallel) // model.get_num_kv_heads(parallel),
-            block_size=builder.kv_cache_spec.block_size,
-        )
-    return None
-
-
-def require_supported_attention(builder) -> None:
-    """Refuse a cache group the view cannot trim exactly: anything but plain full causal attention
-    over one cache group (reference :436-469)."""
+def _refusals(builder):
+    """Why the view cannot trim this cache group exactly, first reason first (nothing for plain full causal
+    decoder attention over one cache group): the cache spec, then each layer."""
     from vllm.v1.attention.backend import AttentionType
     from vllm.v1.kv_cache_interface import FullAttentionSpec
 
     spec = builder.kv_cache_spec
     if type(spec) is not FullAttentionSpec:
-        raise RuntimeError(f"the view supports full causal attention only; this cache group is {type(spec).__name__}")
-    if spec.sliding_window is not None or spec.attention_chunk_size is not None:
-        raise RuntimeError("the view does not support a sliding window or chunked attention in a cache group")
-    layers = builder.vllm_config.compilation_config.static_forward_context
+        yield f"the view supports full causal attention only; this cache group is {type(spec).__name__}"
+    elif spec.sliding_window is not None or spec.attention_chunk_size is not None:
+        yield "the view does not support a sliding window or chunked attention in a cache group"
+    context = builder.vllm_config.compilation_config.static_forward_context
     for name in builder.layer_names:
-        layer = layers[name]
+        layer = context[name]
         if layer.sliding_window is not None:
-            raise RuntimeError(f"layer {name} has a sliding window: the view cannot trim its blocks exactly")
-        if getattr(layer.impl, "alibi_slopes", None) is not None:
-            raise RuntimeError(f"layer {name} has a position bias (ALiBi): the view cannot trim its blocks")
-        if layer.attn_type != AttentionType.DECODER:
-            raise RuntimeError(f"layer {name} is {layer.attn_type.value} attention: the view supports decoder attention")
+            yield f"layer {name} has a sliding window: the view cannot trim its blocks exactly"
+        elif getattr(layer.impl, "alibi_slopes", None) is not None:
+            yield f"layer {name} has a position bias (ALiBi): the view cannot trim its blocks"
+        elif layer.attn_type != AttentionType.DECODER:
+            yield f"layer {name} is {layer.attn_type.value} attention: the view supports decoder attention"
 
 
-def _view_for(builder, cam) -> DecodeView:
+def require_supported_attention(builder) -> None:
+    """Raise RuntimeError with the first reason the view cannot serve this cache group (reference :436-469):
+    a cache spec other than plain full attention, or a layer with a sliding window, a position bias or
+    attention other than decoder self-attention."""
+    reason = next(_refusals(builder), None)
+    if reason is not None:
+        raise RuntimeError(reason)
+
+
+def _audit_plane(builder, batch) -> AuditPlane | None:
+    """The plane that records the statistic: the audit kernel's (EKV_AUDIT_KERNEL), or none. The reference's
+    other recorder, its Triton compiler pass (EKV_ATTN_SHARE), has no counterpart here: asking for it is an
+    error."""
+    if _enabled("EKV_ATTN_SHARE"):
+        raise RuntimeError("EKV_ATTN_SHARE needs the Triton compiler pass; this build records with EKV_AUDIT_KERNEL")
+    if not _enabled("EKV_AUDIT_KERNEL"):
+        return None
+    from .audit_kernel import RecordingPlane
+
+    config = builder.vllm_config
+    model, parallel = config.model_config, config.parallel_config
+    return RecordingPlane(
+        layers=model.get_num_layers_by_block_type(parallel, "attention"),
+        rows=config.scheduler_config.max_num_seqs,
+        width=batch.block_table_tensor.shape[1],
+        group_rows=model.get_num_attention_heads(parallel) // model.get_num_kv_heads(parallel),
+        block_size=builder.kv_cache_spec.block_size,
+    )
+
+
+def _view_for(builder, batch) -> DecodeView:
+    """The process's view, made by the first batch; a second KV-cache group is refused."""
     global _view, _plane, _layers
-    layers = tuple(builder.layer_names)
+    names = tuple(builder.layer_names)
     if _view is None:
         require_supported_attention(builder)
-        _plane = _audit_plane(builder, cam)
         if _enabled("EKV_PREFILL_AUDIT"):
             raise RuntimeError("EKV_PREFILL_AUDIT needs the compiler pass's statistic (EKV_ATTN_SHARE)")
+        plane = _audit_plane(builder, batch)
         _view = DecodeView(
             rows=builder.vllm_config.scheduler_config.max_num_seqs,
-            width=cam.block_table_tensor.shape[1],
+            width=batch.block_table_tensor.shape[1],
             block_size=builder.kv_cache_spec.block_size,
-            audit=_plane,
+            audit=plane,
         )
-        _layers = layers
-    if layers != _layers:
+        _plane, _layers = plane, names
+    elif names != _layers:
         raise RuntimeError("a block-table view supports one KV-cache group; this model has several")
     return _view
 
 
-def _query_lens(cam) -> torch.Tensor:
-    starts = cam.query_start_loc_cpu[: cam.num_reqs + 1]
-    return starts[1:] - starts[:-1]
+def _query_lens(batch) -> torch.Tensor:
+    """Tokens each row computes this step, from the host copy of the batch's query offsets."""
+    return torch.diff(batch.query_start_loc_cpu[: batch.num_reqs + 1])
+
+
+def _patch(cls, name: str, marker: str, wrap: Callable) -> bool:
+    """Replace ``cls.name`` by ``wrap(original)`` once, tagging the replacement with ``marker``."""
+    original = getattr(cls, name)
+    if getattr(original, marker, False):
+        return False
+    replacement = wrap(original)
+    setattr(replacement, marker, True)
+    setattr(cls, name, replacement)
+    return True
+
+
+def _viewed_triton_build(original):
+    """Triton's builder takes the batch as it is; its metadata's table and lengths are then the view's."""
+
+    def build(self, common_prefix_len, common_attn_metadata, fast_build=False):
+        metadata = original(self, common_prefix_len, common_attn_metadata, fast_build)
+        batch = common_attn_metadata
+        view = _view_for(self, batch)
+        if common_prefix_len > 0:  # a shared-prefix cascade reads the engine's own table
+            view.skip(batch.seq_lens, _query_lens(batch))
+        else:
+            metadata.block_table, metadata.seq_lens = view.build(batch.block_table_tensor, batch.seq_lens,
+                                                                 _query_lens(batch))
+        return metadata
+
+    return build
+
+
+def _viewed_flashinfer_build(original):
+    """FlashInfer's builder plans its launch on the host from the lengths, so it is given the view's table
+    and lengths as the batch."""
+
+    def build(self, common_prefix_len, common_attn_metadata, fast_build=False):
+        batch = common_attn_metadata
+        view = _view_for(self, batch)
+        if common_prefix_len > 0:
+            view.skip(batch.seq_lens, _query_lens(batch))
+            return original(self, common_prefix_len, batch, fast_build)
+        table, lens = view.build(batch.block_table_tensor, batch.seq_lens, _query_lens(batch))
+        viewed = batch.replace(block_table_tensor=table, seq_lens=lens, max_seq_len=int(lens.max()), _seq_lens_cpu=None)
+        return original(self, common_prefix_len, viewed, fast_build)
+
+    return build
 
 
 def install_decode_view() -> int:
-    """Give every attention batch of the Triton and FlashInfer backends its view (reference :504-560)."""
+    """Give every attention batch of vLLM's Triton and FlashInfer backends its view, before the engine is
+    created (reference :504-560). Returns the builders patched now."""
     from vllm.v1.attention.backends.flashinfer import FlashInferMetadataBuilder
     from vllm.v1.attention.backends.triton_attn import TritonAttentionMetadataBuilder
 
-    patched = 0
-    triton_build = TritonAttentionMetadataBuilder.build
-    if not getattr(triton_build, "_ekv_decode_view", False):
+    targets = ((TritonAttentionMetadataBuilder, _viewed_triton_build),
+               (FlashInferMetadataBuilder, _viewed_flashinfer_build))
+    return sum(_patch(cls, "build", "_ekv_decode_view", wrap) for cls, wrap in targets)
 
-        def build_triton(self, common_prefix_len, common_attn_metadata, fast_build=False):
-            metadata = triton_build(self, common_prefix_len, common_attn_metadata, fast_build)
-            cam = common_attn_metadata
-            view = _view_for(self, cam)
-            if common_prefix_len > 0:
-                view.skip(cam.seq_lens, _query_lens(cam))
-                return metadata
-            metadata.block_table, metadata.seq_lens = view.build(cam.block_table_tensor, cam.seq_lens, _query_lens(cam))
-            return metadata
 
-        build_triton._ekv_decode_view = True
-        TritonAttentionMetadataBuilder.build = build_triton
-        patched += 1
-    flashinfer_build = FlashInferMetadataBuilder.build
-    if not getattr(flashinfer_build, "_ekv_decode_view", False):
+def _recording_forward(original):
+    """After the layer's attention, the audit kernel records it from the view's buffers (a profiling run,
+    which has no batch, records nothing). The launch is the same every step: graphs capture it."""
+    from .audit_kernel import RecordingPlane
 
-        def build_flashinfer(self, common_prefix_len, common_attn_metadata, fast_build=False):
-            cam = common_attn_metadata
-            view = _view_for(self, cam)
-            if common_prefix_len > 0:
-                view.skip(cam.seq_lens, _query_lens(cam))
-                return flashinfer_build(self, common_prefix_len, cam, fast_build)
-            table, lens = view.build(cam.block_table_tensor, cam.seq_lens, _query_lens(cam))
-            seen = cam.replace(block_table_tensor=table, seq_lens=lens, max_seq_len=int(lens.max()), _seq_lens_cpu=None)
-            return flashinfer_build(self, common_prefix_len, seen, fast_build)
+    def forward(self, layer, query, key, value, kv_cache, attn_metadata, *args, **kwargs):
+        output = original(self, layer, query, key, value, kv_cache, attn_metadata, *args, **kwargs)
+        if attn_metadata is not None:
+            view = current_view()
+            if not isinstance(view.audit, RecordingPlane):
+                raise RuntimeError("the audit kernel is installed but the view has no recording plane")
+            table, lens = view.buffers
+            view.audit.record(layer.layer_name, table, lens, query, kv_cache, self.scale)
+        return output
 
-        build_flashinfer._ekv_decode_view = True
-        FlashInferMetadataBuilder.build = build_flashinfer
-        patched += 1
-    return patched
+    return forward
 
 
 def install_audit_kernel() -> int:
-    """After each attention layer of the Triton and FlashInfer backends, record the statistic
-    (reference :563-596). The launch is the same every step, so CUDA graphs capture it."""
+    """Record the statistic after each attention layer of vLLM's Triton and FlashInfer backends (reference
+    :563-596), with EKV_AUDIT_KERNEL set, before the engine is created. Returns the implementations patched."""
     from vllm.v1.attention.backends.flashinfer import FlashInferImpl
     from vllm.v1.attention.backends.triton_attn import TritonAttentionImpl
 
-    from .audit_kernel import RecordingPlane
-
-    patched = 0
-    for impl in (TritonAttentionImpl, FlashInferImpl):
-        original = impl.forward
-        if getattr(original, "_ekv_audit_kernel", False):
-            continue
-
-        def forward(self, layer, query, key, value, kv_cache, attn_metadata, *args, _original=original, **kwargs):
-            output = _original(self, layer, query, key, value, kv_cache, attn_metadata, *args, **kwargs)
-            if attn_metadata is not None:
-                view = current_view()
-                if not isinstance(view.audit, RecordingPlane):
-                    raise RuntimeError("the audit kernel is installed but the view has no recording plane")
-                table, lens = view.buffers
-                view.audit.record(layer.layer_name, table, lens, query, kv_cache, self.scale)
-            return output
-
-        forward._ekv_audit_kernel = True
-        impl.forward = forward
-        patched += 1
-    return patched
+    return sum(_patch(impl, "forward", "_ekv_audit_kernel", _recording_forward)
+               for impl in (TritonAttentionImpl, FlashInferImpl))
 
 
 def current_view() -> DecodeView:
@@ -644,13 +712,15 @@ def current_view() -> DecodeView:
 
 
 def attach_audit_plane(runner) -> DecodeView:
-    """The view, with the audit plane given the engine's per-layer KV-cache addresses (reference :599-626)."""
+    """The view, once the audit plane holds each layer's KV-cache address (reference :599-626): the audit
+    kernel numbers layers by name, so its table follows its layer names; another plane takes the runner's
+    caches in order."""
     from .audit_kernel import RecordingPlane
 
     view = current_view()
     if isinstance(_plane, RecordingPlane):
-        layers = runner.compilation_config.static_forward_context
-        _plane.attach([layers[name].kv_cache.data_ptr() for name in _plane.layer_names])
+        context = runner.compilation_config.static_forward_context
+        _plane.attach([context[name].kv_cache.data_ptr() for name in _plane.layer_names])
     elif _plane is not None:
         _plane.attach([cache.data_ptr() for cache in runner.kv_caches if cache is not None])
     return view

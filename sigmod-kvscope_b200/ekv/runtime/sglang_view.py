@@ -28,15 +28,15 @@ def kv_pointers(pool) -> list[int]:
 
 
 class SlotView(DecodeView):
-    """The view of SGLang. It keeps the policy and the audits of ``DecodeView`` and compacts the key-value list of a
-    decode batch on the device. It reads fewer blocks and does not give their memory back to the engine."""
+    """The view of SGLang: ``DecodeView``'s policy, audits and counters over SGLang's key-value list. It
+    reads fewer blocks and gives none of their memory back to the engine, so it releases nothing."""
 
     def __init__(
         self, rows: int, width: int, block_size: int, audit: StatisticSwitch | None, device: torch.device
     ) -> None:
-        super().__init__(rows, width, block_size, audit=audit)
+        super().__init__(rows, width, block_size, audit=audit, device=device)
         self.compactor = SlotCompactor(width, block_size, device)
-        self._counts = self.compactor.counts  # reads() and read_breakdown() read the counters the kernel adds to
+        self._counts = self.compactor.counts  # the compaction kernel adds the read counters here
 
     def write_release(self, mask: np.ndarray) -> list[tuple[int, int]]:
         if np.asarray(mask).any():
@@ -46,33 +46,24 @@ class SlotView(DecodeView):
     def rewrite(
         self, indptr: torch.Tensor, slots: torch.Tensor, lengths: np.ndarray, n_rows: int, entries: int
     ) -> torch.Tensor:
-        """Rewrite a decode batch's list in place to the view, and return the new length of each of its rows.
+        """Rewrite a decode batch's list in place to the view; the new length of each of its ``n_rows`` rows.
 
-        ``lengths`` holds the tokens of each request, from the host, so an audit needs no device read. The batch has
-        ``n_rows`` rows, more than the requests when a CUDA graph fills its batch, and ``entries`` list entries. The
-        bookkeeping is that of ``DecodeView.build`` for a batch in which every row decodes."""
+        ``lengths`` holds each request's tokens (host), so an audit reads nothing back; a CUDA graph's batch
+        has more rows than requests, and the list ``entries`` entries. Every row decodes: the bookkeeping is
+        ``DecodeView.build``'s for such a batch (``_begin_step``)."""
         self.finish_audit()
         lengths = np.asarray(lengths)
         requests = len(lengths)
         if requests > self.rows:
             raise ValueError(f"batch of {requests} requests exceeds the view's {self.rows} rows")
-        self._device = indptr.device
-        audited = np.zeros(self.rows, dtype=bool)
-        audited[:requests] = self.audit_rows[:requests]
-        if audited.any() and not self.may_audit():
-            audited[:] = False  # the requests wait for a step after the controller has read the last audit
-        self.audit_rows[audited] = False  # an audit request is consumed by the step that serves it
-        self.audit_step = bool(audited.any())
-        self._audit_pending = self.audit_step
-        self._pending_rows = audited
-        audit = None
+        audited = self._begin_step(np.ones(requests, dtype=bool), None)
+        audit_rows = None
         if self.audit_step:
-            self.start_audit()
-            self._pending_blocks[:requests] = -(-lengths // self.block_size)
-            audit = torch.from_numpy(audited.astype(np.uint8)).to(indptr.device)
+            self._pending_blocks = -(-lengths // self.block_size)
+            audit_rows = torch.from_numpy(audited.astype(np.uint8)).to(indptr.device)
             if self.audit is not None:
                 self.audit.select(audited[:requests], np.arange(requests))
         if self.audit is not None:
             self.audit.set(self.audit_step)
-        keep = self._keep_on(indptr.device)
-        return self.compactor.compact(indptr, slots, keep, audit, self.active(), requests, n_rows, entries)
+        return self.compactor.compact(indptr, slots, self._masks[0], audit_rows, self.active(), requests, n_rows,
+                                      entries)

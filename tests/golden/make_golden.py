@@ -15,6 +15,7 @@ It imports the reference read-only and runs, on CPU:
   * ``SlotCompactor.compact`` (runtime/sglang_compact.py), the SGLang CSR compaction, both Triton
     kernels under the interpreter;
   * ``allocate`` on float64 scores whose shares round together (``float64_cases``);
+  * ``allocate`` with pinned blocks anywhere in a request (``pinned_cases``);
   * ``Controller._absorb_audit`` and ``Controller._allocate`` (observe/controller.py) over a sequence
     of audits, with stand-ins for the mailbox writer and the share source (``controller_cases``).
 Inputs are seeded; the fixtures hold inputs and outputs, so the tests never need the reference.
@@ -485,6 +486,59 @@ def controller_cases():
     print("controller_cases written")
 
 
+def pinned_cases():
+    """allocate() with Request.pinned marking any blocks (observe/allocation.py:37-44): middle blocks,
+    none at all, every block, the first or last left open; all three objectives, weights under `sum`,
+    ties across requests and requests without evidence."""
+    rng = np.random.default_rng(67)
+    cases = {}
+    for i in range(120):
+        n_req = int(rng.integers(1, 8))
+        sizes = rng.integers(1, 90, n_req)
+        kind = i % 4
+        scores, pinned = [], []
+        for n in sizes:
+            if kind == 0:
+                x = rng.integers(0, 4, n).astype(np.float64)  # many ties, within and across requests
+            elif kind == 1:
+                x = rng.dirichlet(np.full(n, 0.3)) if n > 1 else rng.random(1)
+            elif kind == 2:
+                x = _near_ties(rng, n)
+            else:
+                x = np.where(rng.random(n) < 0.3, 0.0, rng.random(n))
+            scores.append(x)
+            style = int(rng.integers(0, 5))
+            if style == 0:
+                p = np.zeros(n, dtype=bool)  # no pins
+            elif style == 1:
+                p = rng.random(n) < 0.3  # anywhere
+            elif style == 2:
+                p = rng.random(n) < 0.8  # most
+            elif style == 3:
+                p = np.ones(n, dtype=bool)  # every block
+            else:
+                p = np.zeros(n, dtype=bool)
+                p[n // 2] = True  # one middle block
+            pinned.append(p)
+        if i % 13 == 5:
+            scores[0][:] = 0.0  # no evidence: equal shares
+        objective = ("sum", "uniform", "maxmin")[i % 3]
+        weights = np.ones(n_req)
+        if objective == "sum" and i % 2:
+            weights = rng.choice([1.0, 0.5, 2.0, 0.0, 1.0 / 3.0], n_req)
+        must = sum(int(p.sum()) for p in pinned)
+        total = int(sizes.sum())
+        budget = int(rng.integers(must, total + 1))
+        requests = [Request(scores=x, weight=float(w), pinned=p) for x, w, p in zip(scores, weights, pinned, strict=True)]
+        masks = allocate(requests, budget, objective)
+        cases[f"sizes{i}"], cases[f"scores{i}"], cases[f"weights{i}"] = sizes, np.concatenate(scores), weights
+        cases[f"pinned{i}"], cases[f"budget{i}"] = np.concatenate(pinned), np.int64(budget)
+        cases[f"objective{i}"] = objective
+        cases[f"mask{i}"] = np.concatenate(masks)
+    np.savez_compressed(os.path.join(HERE, "pinned_cases.npz"), **cases)
+    print("pinned_cases written")
+
+
 def all_cases():
     audit_case("audit_cfg1_fp16", 0, rows=4, q_heads=8, kv_heads=2, layers=1, len_lo=100, len_hi=600, pool=256, dtype="fp16")
     audit_case("audit_layers_fp16", 1, rows=6, q_heads=8, kv_heads=2, layers=3, len_lo=1, len_hi=300, pool=256,
@@ -497,6 +551,7 @@ def all_cases():
     maxmin_cases()
     float64_cases()
     controller_cases()
+    pinned_cases()
 
 
 if __name__ == "__main__":

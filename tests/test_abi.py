@@ -197,4 +197,4 @@ def test_step_and_stash_validate_before_launching(lib):
 
 
 def test_abi_version(lib):
-    assert lib.ekv_abi_version() == 4
+    assert lib.ekv_abi_version() == 5

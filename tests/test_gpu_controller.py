@@ -41,6 +41,46 @@ def test_allocate_on_float64_scores_matches_the_reference():
         np.testing.assert_array_equal(np.concatenate(masks), g[f"mask{i}"], err_msg=f"case {i}")
 
 
+def test_allocate_with_pins_anywhere_matches_the_reference():
+    """allocate() with Request.pinned marking any blocks (observe/allocation.py:37-75): the reference's own
+    outputs over 120 cases of every objective, bit for bit (ekv_allocate_pinned_f64)."""
+    from ekv.observe.allocation import Request, allocate
+
+    g = load_golden("pinned_cases")
+    paths = set()
+    for i in range(120):
+        sizes = g[f"sizes{i}"]
+        bounds = np.concatenate([[0], np.cumsum(sizes)])
+        requests = [
+            Request(scores=g[f"scores{i}"][bounds[j] : bounds[j + 1]], weight=float(g[f"weights{i}"][j]),
+                    pinned=g[f"pinned{i}"][bounds[j] : bounds[j + 1]])
+            for j in range(len(sizes))
+        ]
+        masks = allocate(requests, int(g[f"budget{i}"]), str(g[f"objective{i}"]))
+        np.testing.assert_array_equal(np.concatenate(masks), g[f"mask{i}"], err_msg=f"case {i}")
+        paths.add(str(g[f"objective{i}"]))
+    assert paths == {"sum", "uniform", "maxmin"}
+
+
+@pytest.mark.parametrize("objective", ["sum", "uniform", "maxmin"])
+def test_allocate_with_random_pins_at_larger_sizes_matches_the_oracle(objective):
+    """Beyond the fixture's sizes: 40 requests of up to 3000 blocks, pins anywhere, near-tied scores."""
+    from ekv.observe.allocation import Request, allocate
+
+    rng = np.random.default_rng(5 + len(objective))
+    sizes = rng.integers(1, 3001, 40)
+    scores = [np.round(rng.random(n), 3) for n in sizes]  # three decimals: many exact ties
+    pinned = [rng.random(n) < rng.choice([0.0, 0.05, 0.5]) for n in sizes]
+    weights = rng.choice([1.0, 0.5, 2.0], len(sizes)) if objective == "sum" else np.ones(len(sizes))
+    must = sum(int(p.sum()) for p in pinned)
+    for budget in (must, (must + int(sizes.sum())) // 2, int(sizes.sum()) - 1):
+        want = oa.allocate(scores, budget, objective, pinned, list(weights))
+        got = allocate([Request(scores=s, weight=float(w), pinned=p) for s, w, p in zip(scores, weights, pinned,
+                                                                                           strict=True)],
+                       budget, objective)
+        np.testing.assert_array_equal(np.concatenate(got), np.concatenate(want), err_msg=f"budget {budget}")
+
+
 def run_ledger(g, c, fresh_dtype=torch.float64):
     from ekv.observe.controller import ShareLedger, audit_row_blocks
 

@@ -607,9 +607,9 @@ def test_decode_view_counters_follow_the_reference_count():
         if step % 3 == 0:
             view.write_audit_rows(rng.random(rows) < 0.2)
         if step == 10:
-            view.released[:] = rng.random((rows, width)) < 0.1
-            view.released[:, 0] = False
-            view.released_version += 1
+            freed = rng.random((rows, width)) < 0.1
+            freed[:, 0] = False
+            view.released = freed  # written to the device state
         t, vl = view.build(torch.from_numpy(table).cuda(), torch.from_numpy(lens).cuda(), torch.from_numpy(query))
         audited = view._pending_rows[:n]
         decoding = query == 1

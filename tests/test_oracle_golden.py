@@ -232,6 +232,23 @@ def test_oracle_maxmin_matches_the_reference_allocate():
         np.testing.assert_array_equal(np.concatenate(masks), g[f"mask{i}"], err_msg=f"case {i}")
 
 
+def pinned_case(g, i):
+    sizes = g[f"sizes{i}"]
+    bounds = np.concatenate([[0], np.cumsum(sizes)])
+    cut = [slice(bounds[j], bounds[j + 1]) for j in range(len(sizes))]
+    return ([g[f"scores{i}"][c] for c in cut], [g[f"pinned{i}"][c] for c in cut], list(g[f"weights{i}"]),
+            int(g[f"budget{i}"]), str(g[f"objective{i}"]))
+
+
+def test_oracle_allocation_with_pins_anywhere_matches_the_reference():
+    """Request.pinned marking any blocks (none, every one, middle ones): allocate() run by make_golden.py."""
+    g = load_golden("pinned_cases")
+    for i in range(120):
+        scores, pinned, weights, budget, objective = pinned_case(g, i)
+        masks = oa.allocate(scores, budget, objective, pinned, weights)
+        np.testing.assert_array_equal(np.concatenate(masks), g[f"mask{i}"], err_msg=f"case {i}")
+
+
 def test_oracle_float64_allocation_matches_the_reference():
     """Every objective on float64 scores whose shares (and weighted gains) round together."""
     g = load_golden("float64_cases")

@@ -767,49 +767,58 @@ def main() -> None:
                             "layer); CUDA events over its own timed launches")
 
         # e2e: the step's host inputs in from pinned memory, the shares out, every step (the engine's block
-        # table and lengths: one copy; the selection: RecordingPlane.select, one copy). Each step's shares
-        # land in one of two pinned buffers and the host waits for them after it has queued the next step;
-        # with ranks, a step's shares are complete (combined) once the next step's graph has run.
+        # table and lengths: one copy; the selection: RecordingPlane.select, one copy). The steps alternate
+        # two share buffers (a StepCombiner's two graphs; with ranks, a step's shares are combined while
+        # the next step records): each step's shares are copied out on a copy stream once they are complete,
+        # the next step writing the other buffer meanwhile, and the host waits for them one step later.
+        from ekv.observe.ranks import StepCombiner
+
         pinned_inputs = torch.from_numpy(w.inputs_host).pin_memory()
         share0 = plane.shares()
         out_host = [torch.empty(share0.shape, dtype=share0.dtype).pin_memory() for _ in range(2)]
-        out_ready = [torch.cuda.Event(), torch.cuda.Event()]
-        issued = [0]
-        api_stepper = Stepper(plane, lambda: audit_step(plane, w), dist_on)
+        copied = [torch.cuda.Event(), torch.cuda.Event()]
+        copy_stream = torch.cuda.Stream()
+        api = StepCombiner(plane, lambda: audit_step(plane, w))
+        e2e = {"copied": -1, "pending": [False, False]}  # the last step copied out; copies not yet waited for
+
+        def copy_out(step: int) -> None:
+            b = step % 2
+            copy_stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(copy_stream):
+                out_host[b].copy_(api.buffers[b], non_blocking=True)
+                copied[b].record(copy_stream)
+            e2e["copied"], e2e["pending"][b] = step, True
 
         def e2e_step():
-            i = issued[0]
-            issued[0] += 1
             w.inputs.copy_(pinned_inputs, non_blocking=True)
             plane.select(w.select, w.qrow)
-            api_stepper.step()
-            if dist_on:  # the previous step's shares are complete (combined) once this step's graph has run
-                if i == 0:
-                    return
-                combiner = api_stepper.combiner
-                buffer, done = combiner.buffers[(combiner.steps - 2) % 2], i - 1
-            else:
-                buffer, done = plane.shares(), i
-            out_host[done % 2].copy_(buffer, non_blocking=True)
-            out_ready[done % 2].record()
-            if done > 0:
-                out_ready[(done - 1) % 2].synchronize()  # the copy one step earlier has landed on the host
+            b = api.steps % 2  # the buffer this step records into: its last copy out must have run
+            if e2e["pending"][b]:
+                torch.cuda.current_stream().wait_event(copied[b])
+            api.step()
+            done = api.steps - 1 if not dist_on else api.steps - 2  # the last step whose shares are complete
+            if done > e2e["copied"]:
+                copy_out(done)
+                prev = 1 - done % 2
+                if e2e["pending"][prev]:
+                    copied[prev].synchronize()  # the host holds the step before's shares
+                    e2e["pending"][prev] = False
 
         def e2e_finish():
-            if dist_on and issued[0] > 0:  # the last step's combine and its copy out
-                last = api_stepper.finish()
-                out_host[(issued[0] - 1) % 2].copy_(last, non_blocking=True)
-            issued[0] = 0
+            if dist_on and api.steps - 1 > e2e["copied"]:
+                api.flush()  # the last step's combine
+                copy_out(api.steps - 1)
+            torch.cuda.current_stream().wait_stream(copy_stream)  # every copy out inside the timed region
 
         e2e_seconds = timed(e2e_step, args.steps, args.warmup, dist_on, e2e_finish) if not args.no_e2e else float("nan")
-        api_stepper.release()
+        api.release()
         h2d = pinned_inputs.nbytes + 5 * w.rows  # select(): a token row (int32) and a flag per row
         d2h = out_host[0].nbytes
         view = None if args.no_view else view_bench(rank, world, args.steps, args.warmup, dist_on)
         strong = None
         if not args.no_strong and args.config == "llama8b" and not args.layers and not args.pools:
             plane.close()
-            del plane, stepper, api_stepper
+            del plane, stepper, api
             w.caches, w.queries = [], []  # the 70B step's pools take their place
             torch.cuda.empty_cache()
             strong = strong_70b(args, rank, world, dist_on)
@@ -835,10 +844,10 @@ def main() -> None:
         "e2e": {"value": units_all * args.steps / e2e_seconds, "unit": "audited KV tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "note": "RecordingPlane.select (one copy from pinned staging), then RecordingPlane.record per "
-                        "layer (a query stash per layer, one launch of every layer after the last) in a CUDA "
-                        "graph; the block table and lengths in by one copy from pinned host memory, shares "
-                        "out to pinned memory, the host waiting for them after queueing the next step; KV "
-                        "cache resident"},
+                        "layer (a query stash per layer on parallel side streams, one launch of every layer "
+                        "after the last) in CUDA graphs alternating two share buffers; the block table and "
+                        "lengths in by one copy from pinned host memory, each step's shares out to pinned "
+                        "memory on a copy stream, the host waiting for them one step later; KV cache resident"},
         # per step: the descriptor, record, share and combine kernels (deferred), or a record kernel
         # per layer plus the share and combine kernels (per-layer)
         "gpu_launches": args.steps * (4 if args.record == "deferred" else w.layers + 2),

@@ -80,8 +80,11 @@ struct AuditParams {
   int aggregate;
   uint32_t* row_tickets;    // [rows]
   uint32_t* item_counter;   // items handed out beyond each warp's first (zeroed by kmap_kernel); NULL: static order
-  int32_t* contrib_layer;   // [layers][rows]
-  float* share_layer;       // [layers][rows][width]
+  // the share's normaliser, made by the record kernel: the chunks of each (layer, row, head) finished
+  // this step, and each (layer, row, query row)'s log total over its tiles as (M, S), the total being
+  // S * exp(M) (S == 0: no data). NULL: the launch makes no shares.
+  uint32_t* lh_tickets;     // [layers][rows][kMaxQ]
+  float2* row_lse;          // [layers][rows][kMaxQ]
   uint32_t* status;
 };
 
@@ -157,6 +160,58 @@ struct Cursor {
   long long item;  // index into the launch's items; >= the total when done
   int layer, head, row, t0, t, t_end;
 };
+
+// The log total of each query row of (layer, row, head) over the row's n_tiles tiles, from the cells the
+// record kernel wrote (tile t's cell is its first block's): lane l merges tiles l, l + 32, ... in order,
+// then the lanes merge by xor-shuffles, the same order on every launch. A tile without data (m = -inf
+// or l = 0) adds nothing. Four query rows at a time, every cell load of a round issued before any is
+// merged.
+__device__ __forceinline__ void merge_row_lse(const AuditParams& p, int layer, int row, int head, int n_tiles, int lane) {
+  const size_t plane = (size_t)p.layers * p.rows * p.width * p.Q;
+  const size_t lr = (size_t)layer * p.rows + row;
+  const float* cm = p.lse + lr * p.width * p.Q + head * p.G;
+  const float* cl = cm + plane;
+  const int stride = p.tile_blocks * p.Q;  // floats from one tile's cell to the next tile's
+  float2* out = p.row_lse + lr * kMaxQ + head * p.G;
+  constexpr int kTiles = 4;  // tiles of a lane per round
+  for (int g0 = 0; g0 < p.G; g0 += 4) {
+    const int ng = p.G - g0 < 4 ? p.G - g0 : 4;
+    float M[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, S[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int t0 = lane; t0 < n_tiles; t0 += 32 * kTiles) {
+      float mv[kTiles][4], lv[kTiles][4];
+#pragma unroll
+      for (int u = 0; u < kTiles; ++u) {
+        const int t = t0 + 32 * u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const bool ok = t < n_tiles && k < ng;
+          const size_t at = (size_t)(ok ? t : 0) * stride + g0 + (ok ? k : 0);
+          mv[u][k] = ok ? __ldcg(cm + at) : -INFINITY;
+          lv[u][k] = ok ? __ldcg(cl + at) : 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kTiles; ++u)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (mv[u][k] > -INFINITY && lv[u][k] > 0.f) lse_merge(M[k], S[k], mv[u][k], lv[u][k]);
+    }
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float m2 = __shfl_xor_sync(kFullMask, M[k], off), s2 = __shfl_xor_sync(kFullMask, S[k], off);
+        lse_merge(M[k], S[k], m2, s2);
+      }
+    if (lane < ng) {
+      float m = M[0], sv = S[0];
+#pragma unroll
+      for (int k = 1; k < 4; ++k)
+        if (lane == k) m = M[k], sv = S[k];
+      out[g0 + lane] = make_float2(m, m > -INFINITY ? sv : 0.f);
+    }
+  }
+}
 
 template <int TT, int NT, int D, typename T>
 __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __grid_constant__ AuditParams p) {
@@ -531,6 +586,25 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
       }
     }
     if (++out.t >= out.t_end) {
+      if (p.row_lse != nullptr) {
+        // The item's cells are written. Its chunk counts towards its (layer, row, head); the warp that
+        // finishes the last chunk merges the row's cells into the query rows' log totals. The warp barrier
+        // orders every lane's cell stores before lane 0's release of the count, which the last warp
+        // acquires before it reads them.
+        const int n_tiles = (s_blocks[out.row] + p.tile_blocks - 1) / p.tile_blocks;
+        const uint32_t n_chunks = (uint32_t)((n_tiles + kChunkTiles - 1) / kChunkTiles);
+        uint32_t* ticket = p.lh_tickets + ((size_t)out.layer * p.rows + out.row) * kMaxQ + out.head;
+        __syncwarp();
+        uint32_t done = 0;
+        if (lane == 0) done = atomic_add_acq_rel(ticket, 1u);
+        done = __shfl_sync(kFullMask, done, 0);
+        __syncwarp();  // lane 0's acquire, before any lane reads another warp's cells
+        if (done + 1 == n_chunks) {
+          merge_row_lse(p, out.layer, out.row, out.head, n_tiles, lane);
+          __syncwarp();
+          if (lane == 0) *ticket = 0u;  // ready for the next step
+        }
+      }
       ++n_used;
       __syncwarp();
       decode(s_queue[warp][n_used % kItemQueue], out);
@@ -543,172 +617,45 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
   }
 }
 
-// ---- the share kernel: one CTA of kShareWarps warps per (layer, row) ---------------------------------
-
-constexpr int kShareWarps = 4;
-constexpr int kShareThreads = kShareWarps * 32;
-constexpr int kShareBatch = 8;  // tiles whose cells a lane loads before it uses any
-
-// The block shares of layer L of row r (n blocks) from the cells of the row's tiles, into
-// share_layer[L][r][:n], and the number of query rows with data into contrib_layer[L][r]. Thread t
-// takes query row kl + 32 a (kl = t % lanes_q) of tiles rep, rep + reps, ... (rep = t / lanes_q,
-// reps = kShareThreads / lanes_q), lanes_q being the query rows rounded up to a power of two (at most
-// 32). The log totals are merged over a thread's tiles in order, over the replicas of a warp by
-// xor-shuffles (lse_merge is commutative: both partners hold the same result), then over the warps in
-// warp order: the same order on every launch.
-__device__ __forceinline__ void share_task(const AuditParams& p, int L, int r, int n, float* s_lse, int* s_has,
-                                           float (*s_wm)[kMaxQ], float (*s_ws)[kMaxQ]) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int Q = p.Q, TB = p.tile_blocks;
-  const int n_tiles = (n + TB - 1) / TB;
-  const size_t lr = (size_t)L * p.rows + r;
-  const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
-  const float* cm = p.lse + lr * p.width * Q;  // tile t's cell: its first block, t * TB
-  const float* cl = cm + plane;
-  int qp = 1;
-  while (qp < Q) qp <<= 1;
-  const int lanes_q = qp < 32 ? qp : 32;
-  const int reps = kShareThreads / lanes_q;
-  const int kpl = qp > 32 ? qp / 32 : 1;  // query rows per thread (kMaxQ = 128: at most 4)
-  const int kl = lane % lanes_q, rep = tid / lanes_q;
-  const int steps = (n_tiles + reps - 1) / reps;
-
-  // 1. the log total of each query row
-  const float log_tb = logf((float)TB);
-  for (int a = 0; a < kpl; ++a) {
-    const int k = kl + 32 * a;
-    const bool active = k < Q;
-    float M = -INFINITY, S = 0.f;
-    for (int j0 = 0; j0 < steps; j0 += kShareBatch) {
-      float mv[kShareBatch], lv[kShareBatch];
-#pragma unroll
-      for (int u = 0; u < kShareBatch; ++u) {
-        const int t = rep + reps * (j0 + u);
-        const bool ok = active && t < n_tiles;
-        const size_t cell = (size_t)(ok ? t : 0) * TB * Q + (active ? k : 0);
-        mv[u] = ok ? __ldcg(cm + cell) : -INFINITY;
-        lv[u] = ok ? __ldcg(cl + cell) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < kShareBatch; ++u)
-        if (mv[u] > -INFINITY && lv[u] > 0.f) lse_merge(M, S, mv[u], lv[u]);  // a tile with no data is skipped
-    }
-    for (int off = lanes_q; off < 32; off <<= 1) {
-      const float m2 = __shfl_xor_sync(kFullMask, M, off), s2 = __shfl_xor_sync(kFullMask, S, off);
-      lse_merge(M, S, m2, s2);
-    }
-    if (lane < lanes_q && active) s_wm[warp][k] = M, s_ws[warp][k] = S;
-  }
-  __syncthreads();
-  if (tid < Q) {  // over the warps, in warp order
-    float M = s_wm[0][tid], S = s_ws[0][tid];
-    for (int w = 1; w < kShareWarps; ++w) lse_merge(M, S, s_wm[w][tid], s_ws[w][tid]);
-    const bool h = M > -INFINITY;
-    s_has[tid] = h;
-    s_lse[tid] = h ? M + logf(S) + log_tb : 0.f;  // log of the sum over blocks of exp(u), plus log(TB)
-  }
-  __syncthreads();
-  if (warp == 0) {
-    int has = 0;
-    for (int k = lane; k < Q; k += 32) has += s_has[k];
-    for (int off = 16; off > 0; off >>= 1) has += __shfl_xor_sync(kFullMask, has, off);
-    if (lane == 0) p.contrib_layer[lr] = has;
-  }
-
-  // 2. every tile's share, summed (mean) or maxed (max) over the query rows: exp(u - lse) =
-  // exp(m + log(l) - (M + log S)) = l * exp(m - lse); the blocks of a partial last tile get its weight
-  // back, exp(u + log(TB / tail) - lse) = exp(u - lse) * TB / tail
-  const bool agg_max = p.aggregate == EKV_AGG_MAX;
-  const int tail = n % TB;
-  float* sl = p.share_layer + lr * p.width;
-  for (int j0 = 0; j0 < steps; j0 += kShareBatch) {
-    float e[kShareBatch];
-#pragma unroll
-    for (int u = 0; u < kShareBatch; ++u) e[u] = 0.f;
-    for (int a = 0; a < kpl; ++a) {
-      const int k = kl + 32 * a;
-      const bool active = k < Q && s_has[k < Q ? k : 0];
-      const float lse = active ? s_lse[k] : 0.f;
-      float mv[kShareBatch], lv[kShareBatch];
-#pragma unroll
-      for (int u = 0; u < kShareBatch; ++u) {
-        const int t = rep + reps * (j0 + u);
-        const bool ok = active && t < n_tiles;
-        const size_t cell = (size_t)(ok ? t : 0) * TB * Q + (ok ? k : 0);
-        mv[u] = ok ? __ldcg(cm + cell) : -INFINITY;
-        lv[u] = ok ? __ldcg(cl + cell) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < kShareBatch; ++u) {
-        // a cell without data (m = -inf, l = 0) or never written (NaN) fails the test and has no share
-        const float sh = (mv[u] > -INFINITY && lv[u] > 0.f) ? lv[u] * __expf(mv[u] - lse) : 0.f;
-        e[u] = agg_max ? fmaxf(e[u], sh) : e[u] + sh;
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kShareBatch; ++u) {
-      for (int off = 1; off < lanes_q; off <<= 1) {
-        const float o = __shfl_xor_sync(kFullMask, e[u], off);
-        e[u] = agg_max ? fmaxf(e[u], o) : e[u] + o;
-      }
-      const int t = rep + reps * (j0 + u);
-      if (t < n_tiles && kl == 0) {
-        const int b0 = t * TB, b1 = min(b0 + TB, n);
-        const float v = (tail && b1 == n) ? e[u] * ((float)TB / (float)tail) : e[u];
-        for (int b = b0; b < b1; ++b) sl[b] = v;
-      }
-    }
-  }
-}
-
-// Grid: one CTA per (layer, row) pair of the layers [layer0, layer0 + n_layers).
-__global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams p) {
-  __shared__ float s_lse[kMaxQ];
-  __shared__ int s_has[kMaxQ];
-  __shared__ float s_wm[kShareWarps][kMaxQ], s_ws[kShareWarps][kMaxQ];
-  chain_release();
-  chain_wait();  // the record kernel's cells
-  if (*p.flag == 0) return;  // nothing was recorded this step
-  const long long pair = blockIdx.x;
-  if (pair >= (long long)p.n_layers * p.rows) return;
-  const int L = p.layer0 + (int)(pair / p.rows), r = (int)(pair % p.rows);
-  const RowInfo ri = row_info(p, r, false);
-  if (ri.n_chunks == 0) {  // the row records nothing: no contributors
-    if (threadIdx.x == 0) p.contrib_layer[(size_t)L * p.rows + r] = 0;
-    return;
-  }
-  share_task(p, L, r, ri.n_blocks, s_lse, s_has, s_wm, s_ws);
-}
-
-// ---- the combine kernel: a row's layers into its final share --------------------------------------------
+// ---- the combine kernel: the cells and log totals of a row's layers into its final share -------------
 //
-// Grid (width / kCombineThreads, rows), one block per thread: the sum (mean) or max over the layers
-// [layer0, layer0 + n_layers) with data, in layer order, divided by the contributors (mean) or, by
-// the CTA that finishes the row last (a ticket), by the row's total (max). A row that records nothing
-// is NaN with no contributors.
+// Grid (tiles of the width / kCombineTiles, rows), kCombineTiles x kCombineSlices threads: thread
+// (tile j, slice k) takes tile t0 + j of the layers la + k, la + k + kCombineSlices, ... of
+// [layer0, layer0 + n_layers) with data. A block b of tile t (its cell is the tile's first block's) gets,
+// over those layers and their query rows with data, exp(u_b) / sum_b' exp(u_b') = l exp(m - M) / S / n_t
+// (n_t the tile's blocks in the row: the blocks of a partial last tile share its whole weight, the
+// reference's regain), summed and divided by the contributors (mean) or maxed, the row then divided
+// by its total by the CTA that finishes the row last (max). The slices combine in slice order. A row
+// that records nothing, or has no contributor, is NaN; blocks past the row are 0.
+constexpr int kCombineTiles = 32;
+constexpr int kCombineSlices = 4;
+static_assert(kCombineTiles * kCombineSlices == kCombineThreads, "a thread per (tile, slice)");
+
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditParams p) {
-  __shared__ uint8_t s_on[kMaxLayers];
   __shared__ int s_c[kCombineThreads / 32];
   __shared__ float s_red[kCombineThreads / 32];
+  __shared__ float s_part[kCombineSlices][kCombineTiles];
   __shared__ int s_last;
   const int r = blockIdx.y, tid = threadIdx.x;
   chain_release();
-  chain_wait();  // the share kernel's layer shares
+  chain_wait();  // the record kernel's cells and log totals
   if (*p.flag == 0) return;  // nothing was recorded this step
   const RowInfo ri = row_info(p, r, false);
   float* out = p.share_out + (size_t)r * p.width;
-  const int b = blockIdx.x * kCombineThreads + tid;
+  const int TB = p.tile_blocks, Q = p.Q;
+  const int t0 = blockIdx.x * kCombineTiles;
+  const int b_lo = t0 * TB, b_hi = min((t0 + kCombineTiles) * TB, p.width);  // this CTA's blocks
   if (ri.n_chunks == 0) {
-    if (b < p.width) out[b] = NAN;
+    for (int b = b_lo + tid; b < b_hi; b += kCombineThreads) out[b] = NAN;
     if (blockIdx.x == 0 && tid == 0) p.contrib_out[r] = 0;
     return;
   }
   const int la = p.layer0, lb = p.layer0 + p.n_layers;
+  // the contributors: (layer, query row) pairs with data
   int c = 0;
-  for (int k = la + tid; k < lb; k += kCombineThreads) {
-    const int ck = __ldcg(p.contrib_layer + (size_t)k * p.rows + r);
-    s_on[k - la] = ck != 0;
-    c += ck;
+  for (int i = tid; i < (lb - la) * Q; i += kCombineThreads) {
+    const int L = la + i / Q, q = i % Q;
+    c += __ldcg(&p.row_lse[((size_t)L * p.rows + r) * kMaxQ + q].y) > 0.f;
   }
   for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(kFullMask, c, off);
   if ((tid & 31) == 0) s_c[tid >> 5] = c;
@@ -716,32 +663,53 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditPar
   int contributors = 0;
   for (int w = 0; w < kCombineThreads / 32; ++w) contributors += s_c[w];
   if (blockIdx.x == 0 && tid == 0) p.contrib_out[r] = contributors;
+  if (contributors == 0) {
+    for (int b = b_lo + tid; b < b_hi; b += kCombineThreads) out[b] = NAN;
+    return;
+  }
   const bool agg_max = p.aggregate == EKV_AGG_MAX;
-  const int n = ri.n_blocks;
-  if (b < p.width) {
-    float v = 0.f;
-    if (contributors == 0) {
-      v = NAN;
-    } else if (b < n) {
-      constexpr int U = 32;  // layers loaded before any is added, then added in layer order
-      for (int k0 = la; k0 < lb; k0 += U) {
-        float x[U];
+  const int n = ri.n_blocks, n_tiles = (n + TB - 1) / TB;
+  const int j = tid % kCombineTiles, k = tid / kCombineTiles;
+  const int t = t0 + j;
+  const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
+  float v = 0.f;
+  if (t < n_tiles) {
+    for (int L = la + k; L < lb; L += kCombineSlices) {
+      const size_t lr = (size_t)L * p.rows + r;
+      const float* cm = p.lse + (lr * p.width + (size_t)t * TB) * Q;
+      const float2* tot = p.row_lse + lr * kMaxQ;
+      for (int q0 = 0; q0 < Q; q0 += 8) {  // eight query rows' loads in flight, then their shares
+        float m[8], l[8];
+        float2 z[8];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int k = k0 + u < lb ? k0 + u : la;
-          x[u] = __ldcg(p.share_layer + ((size_t)k * p.rows + r) * p.width + b);
+        for (int u = 0; u < 8; ++u) {
+          const bool ok = q0 + u < Q;
+          z[u] = ok ? __ldcg(tot + q0 + u) : make_float2(0.f, 0.f);
+          m[u] = ok ? __ldcg(cm + q0 + u) : -INFINITY;
+          l[u] = ok ? __ldcg(cm + plane + q0 + u) : 0.f;
         }
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int k = k0 + u;
-          if (k < lb && s_on[k - la]) v = agg_max ? fmaxf(v, x[u]) : v + x[u];
+        for (int u = 0; u < 8; ++u) {
+          // a query row without data, or a cell without data (m = -inf, l = 0), has no share
+          const float sh = (z[u].y > 0.f && m[u] > -INFINITY && l[u] > 0.f) ? l[u] / z[u].y * __expf(m[u] - z[u].x)
+                                                                            : 0.f;
+          v = agg_max ? fmaxf(v, sh) : v + sh;
         }
       }
-      if (!agg_max) v /= (float)contributors;
     }
-    out[b] = v;
   }
-  if (!agg_max || contributors == 0) return;
+  s_part[k][j] = v;
+  __syncthreads();
+  if (k == 0) {
+    for (int kk = 1; kk < kCombineSlices; ++kk) v = agg_max ? fmaxf(v, s_part[kk][j]) : v + s_part[kk][j];
+    const int bt0 = t * TB;
+    if (bt0 < p.width) {
+      const int in_row = t < n_tiles ? min(TB, n - bt0) : 0;  // the tile's blocks in the row
+      const float each = in_row > 0 ? (agg_max ? v / (float)in_row : v / (float)in_row / (float)contributors) : 0.f;
+      for (int b = bt0; b < bt0 + TB && b < p.width; ++b) out[b] = b < n ? each : 0.f;
+    }
+  }
+  if (!agg_max) return;
   // max: the last CTA of the row divides the row by its total
   __threadfence();
   __syncthreads();
@@ -750,11 +718,11 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditPar
   if (!s_last) return;
   __threadfence();
   float part = 0.f;
-  for (int k = tid; k < n; k += kCombineThreads) part += __ldcg(out + k);
+  for (int b = tid; b < n; b += kCombineThreads) part += __ldcg(out + b);
   const float total = block_sum_fixed_order<kCombineThreads>(part, s_red);
-  for (int k = tid; k < n; k += kCombineThreads) {
-    const float v = __ldcg(out + k);
-    out[k] = total > 0.f ? v / total : 0.f;
+  for (int b = tid; b < n; b += kCombineThreads) {
+    const float x = __ldcg(out + b);
+    out[b] = total > 0.f ? x / total : 0.f;
   }
   if (tid == 0) p.row_tickets[r] = 0;  // ready for the next step
 }
@@ -824,11 +792,8 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
   AuditParams ps = p;
   ps.layer0 = share0;
   ps.n_layers = share_layers;
-  const long long pairs = (long long)share_layers * p.rows;
-  launch_chained(share_kernel, dim3((unsigned)pairs), dim3(kShareThreads), 0, stream, ps);
-  rc = check_launch("share_kernel");
-  if (rc != EKV_OK) return rc;
-  launch_chained(combine_kernel, dim3(cdiv(p.width, kCombineThreads), p.rows), dim3(kCombineThreads), 0, stream, ps);
+  launch_chained(combine_kernel, dim3(cdiv(cdiv(p.width, p.tile_blocks), kCombineTiles), p.rows),
+                 dim3(kCombineThreads), 0, stream, ps);
   return check_launch("combine_kernel");
 }
 
@@ -847,17 +812,20 @@ int dispatch(const AuditParams& p, int tt, bool finalize, int share0, int share_
   return fail(EKV_ENOTSUP, "no audit kernel for a tile of %d tokens", tt);
 }
 
+// The workspace: [row_tickets, row_lse) holds tickets and counters, all zero between steps.
 struct WorkspaceLayout {
-  size_t row_tickets, counters, contrib, share, kmaps, total;
+  size_t row_tickets, counters, lh_tickets, row_lse, kmaps, total;
 };
 
 WorkspaceLayout workspace_layout(int layers, int rows, int width) {
+  (void)width;  // the share's per-layer state is per (layer, row, query row), whatever the width
   WorkspaceLayout w{};
+  const size_t cells = (size_t)layers * rows * kMaxQ;
   w.row_tickets = 0;
   w.counters = round_up((size_t)rows * 4, 256);
-  w.contrib = w.counters + 256;
-  w.share = w.contrib + round_up((size_t)layers * rows * 4, 256);
-  w.kmaps = w.share + round_up((size_t)layers * rows * width * 4, 256);
+  w.lh_tickets = w.counters + 256;
+  w.row_lse = w.lh_tickets + round_up(cells * 4, 256);
+  w.kmaps = w.row_lse + round_up(cells * sizeof(float2), 256);
   w.total = w.kmaps + round_up((size_t)layers * sizeof(CUtensorMap), 256);
   return w;
 }
@@ -942,8 +910,8 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
     uint8_t* base = static_cast<uint8_t*>(workspace);
     p.row_tickets = reinterpret_cast<uint32_t*>(base + w.row_tickets);
     p.item_counter = need_workspace ? reinterpret_cast<uint32_t*>(base + w.counters) : nullptr;
-    p.contrib_layer = reinterpret_cast<int32_t*>(base + w.contrib);
-    p.share_layer = reinterpret_cast<float*>(base + w.share);
+    p.lh_tickets = reinterpret_cast<uint32_t*>(base + w.lh_tickets);
+    p.row_lse = reinterpret_cast<float2*>(base + w.row_lse);
     p.kmaps = need_workspace ? reinterpret_cast<const CUtensorMap*>(base + w.kmaps) : nullptr;
   }
   return EKV_OK;
@@ -1071,7 +1039,7 @@ int audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (clear_tickets) {
     const WorkspaceLayout w = workspace_layout(layers, rows, width);
-    if (cudaMemsetAsync(static_cast<uint8_t*>(workspace) + w.row_tickets, 0, w.contrib - w.row_tickets, s) !=
+    if (cudaMemsetAsync(static_cast<uint8_t*>(workspace) + w.row_tickets, 0, w.row_lse - w.row_tickets, s) !=
         cudaSuccess)
       return check_launch("cudaMemsetAsync(row tickets)");
   }

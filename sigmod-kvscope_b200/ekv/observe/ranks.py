@@ -31,6 +31,8 @@ def allreduce_shares(share: torch.Tensor, group: dist.ProcessGroup | None = None
 
     NCCL averages in the collective itself (one launch); backends without an averaging reduction
     (gloo) sum and then divide by the world size."""
+    if not dist.is_initialized():
+        return share  # one process: its shares are the mean
     world = dist.get_world_size(group)
     if world > 1:
         if dist.get_backend(group) == "nccl":
@@ -52,7 +54,9 @@ class StepCombiner:
     when the next step's graph is. ``flush()`` combines the last step's shares (one all-reduce, eager).
 
     Every rank must call ``step`` and ``flush`` the same number of times, in the same order. The
-    graphs hold NCCL work: ``release()`` them before the process group is destroyed.
+    graphs hold NCCL work: ``release()`` them before the process group is destroyed. In a single process
+    (no process group) there is nothing to combine, and the two graphs just alternate the share buffers,
+    so one step's shares can be read out while the next step writes the other buffer.
     """
 
     def __init__(self, plane, record: Callable[[], None], group: dist.ProcessGroup | None = None) -> None:

@@ -48,6 +48,8 @@ class RecordingPlane(AuditPlane):
     table filled and records the others layer by layer.
     """
 
+    _SIDE_STREAMS = 8  # deferred recording: the layers' stash copies run on this many parallel branches
+
     def __init__(
         self,
         layers: int,
@@ -108,6 +110,7 @@ class RecordingPlane(AuditPlane):
         self._rows_index = torch.arange(rows, dtype=torch.int32, device=device)
         self._key_shape: tuple | None = None
         self._step_addresses: dict[tuple, tuple[torch.Tensor, torch.Tensor]] = {}
+        self._side: list[torch.cuda.Stream] | None = None  # the stash copies' streams (deferred recording)
         torch.cuda.synchronize()
         self._publish()
 
@@ -295,14 +298,25 @@ class RecordingPlane(AuditPlane):
             self._stash_addresses = torch.tensor(addresses, dtype=torch.uint64, device=self._device)
         if self._stash.dtype != query.dtype:
             raise ValueError("every layer's query must have the same dtype")
+        # The layer's stash copy runs on a side stream forked from the caller's stream here (after the
+        # layer's attention, which made the query), so it overlaps whatever the caller queues next instead
+        # of lengthening its stream; the side streams join the caller's before the step's launch. Under
+        # capture the forks and the join become branches of the graph.
+        main = torch.cuda.ExternalStream(stream, device=self._device)
+        if self._side is None:
+            self._side = [torch.cuda.Stream(device=self._device) for _ in range(self._SIDE_STREAMS)]
+        side = self._side[layer % len(self._side)]
+        side.wait_stream(main)
         rc = self._lib.ekv_audit_stash(
             query.data_ptr(), query.stride(0), query.stride(1), self._token.data_ptr(), self.rows, query.shape[0],
             group, self.heads, self.group_rows, query.shape[2], self._stash[layer].data_ptr(), self._status.data_ptr(),
-            stream,
+            side.cuda_stream,
         )
         _lib.check(rc, "ekv_audit_stash")
         if layer != self._layers - 1:
             return
+        for branch in self._side[: min(len(self._side), self._layers)]:
+            main.wait_stream(branch)
         stash = self._stash[0]
         rc = self._lib.ekv_audit_step(
             self._stash_addresses.data_ptr(), self._table_dev, table.data_ptr(), lens.data_ptr(),

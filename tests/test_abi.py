@@ -43,20 +43,22 @@ def test_constants_agree_with_the_header():
     assert int(defines["EKV_EINVAL"]) == L.EINVAL and int(defines["EKV_ENOTSUP"]) == L.ENOTSUP
     assert int(defines["EKV_SHARE_FINALIZE"]) == L.SHARE_FINALIZE
     assert int(defines["EKV_POLICY_SUM"]) == L.POLICY_SUM and int(defines["EKV_POLICY_NEWEST"]) == L.POLICY_NEWEST
+    assert int(defines["EKV_POLICY_MAXMIN"]) == L.POLICY_MAXMIN
     assert int(defines["EKV_AUDIT_CHUNK_TILES"]) == L.AUDIT_CHUNK_TILES
     assert int(defines["EKV_DTYPE_BF16"]) == L.DTYPE_BF16
 
 
 def test_workspace_size(lib):
-    # row tickets [rows] + the step's item counter + contributors [layers][rows] + shares
-    # [layers][rows][width] + a 128-byte key-cache descriptor per layer
+    # row tickets [rows] + the step's item counter + a ticket (uint32) and a log total (two float32)
+    # per (layer, row, query row: up to 128) + a 128-byte key-cache descriptor per layer
     layers, rows, width = 32, 64, 512
 
     def up(x):
         return -(-x // 256) * 256
 
-    want = up(rows * 4) + 256 + up(layers * rows * 4) + up(layers * rows * width * 4) + up(layers * 128)
+    want = up(rows * 4) + 256 + up(layers * rows * 128 * 4) + up(layers * rows * 128 * 8) + up(layers * 128)
     assert lib.ekv_audit_workspace_bytes(layers, rows, width) == want
+    assert lib.ekv_audit_workspace_bytes(layers, rows, 4 * width) == want  # the width does not change it
     assert lib.ekv_audit_workspace_bytes(0, rows, width) == 0
 
 

@@ -60,10 +60,9 @@ const char* ekv_last_error_string(void);
 int ekv_abi_version(void);
 
 /* Bytes of workspace the share pass of ekv_audit_launch / ekv_audit_step needs for a table of
- * `layers` layers and `rows` rows (the width does not change it): a ticket per row, a ticket and a
- * log total per (layer, row, query row) -- the share's normaliser, which the record kernel makes as it
- * finishes a row's last chunk -- and, for ekv_audit_step, a work counter and the key cache's TMA
- * descriptor per layer (128 bytes each), rewritten by every step. It must be zero before the first
+ * `layers` layers and `rows` rows (the width does not change it): a ticket per row, a log total per
+ * (layer, row, query row) -- the share's normaliser -- and, for ekv_audit_step, a work counter and the
+ * key cache's TMA descriptor per layer (128 bytes each), rewritten by every step. It must be zero before the first
  * launch (every launch leaves the tickets zero again) and 256-byte aligned. */
 size_t ekv_audit_workspace_bytes(int layers, int rows, int width);
 

@@ -80,10 +80,8 @@ struct AuditParams {
   int aggregate;
   uint32_t* row_tickets;    // [rows]
   uint32_t* item_counter;   // items handed out beyond each warp's first (zeroed by kmap_kernel); NULL: static order
-  // the share's normaliser, made by the record kernel: the chunks of each (layer, row, head) finished
-  // this step, and each (layer, row, query row)'s log total over its tiles as (M, S), the total being
-  // S * exp(M) (S == 0: no data). NULL: the launch makes no shares.
-  uint32_t* lh_tickets;     // [layers][rows][kMaxQ]
+  // the share's normaliser: each (layer, row, query row)'s log total over its tiles as (M, S), the total
+  // being S * exp(M) (S == 0: no data), made by lse_kernel after the record kernel
   float2* row_lse;          // [layers][rows][kMaxQ]
   uint32_t* status;
 };
@@ -165,7 +163,7 @@ struct Cursor {
 // record kernel wrote (tile t's cell is its first block's): lane l merges tiles l, l + 32, ... in order,
 // then the lanes merge by xor-shuffles, the same order on every launch. A tile without data (m = -inf
 // or l = 0) adds nothing. Four query rows at a time, every cell load of a round issued before any is
-// merged.
+// merged. One warp.
 __device__ __forceinline__ void merge_row_lse(const AuditParams& p, int layer, int row, int head, int n_tiles, int lane) {
   const size_t plane = (size_t)p.layers * p.rows * p.width * p.Q;
   const size_t lr = (size_t)layer * p.rows + row;
@@ -586,25 +584,6 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
       }
     }
     if (++out.t >= out.t_end) {
-      if (p.row_lse != nullptr) {
-        // The item's cells are written. Its chunk counts towards its (layer, row, head); the warp that
-        // finishes the last chunk merges the row's cells into the query rows' log totals. The warp barrier
-        // orders every lane's cell stores before lane 0's release of the count, which the last warp
-        // acquires before it reads them.
-        const int n_tiles = (s_blocks[out.row] + p.tile_blocks - 1) / p.tile_blocks;
-        const uint32_t n_chunks = (uint32_t)((n_tiles + kChunkTiles - 1) / kChunkTiles);
-        uint32_t* ticket = p.lh_tickets + ((size_t)out.layer * p.rows + out.row) * kMaxQ + out.head;
-        __syncwarp();
-        uint32_t done = 0;
-        if (lane == 0) done = atomic_add_acq_rel(ticket, 1u);
-        done = __shfl_sync(kFullMask, done, 0);
-        __syncwarp();  // lane 0's acquire, before any lane reads another warp's cells
-        if (done + 1 == n_chunks) {
-          merge_row_lse(p, out.layer, out.row, out.head, n_tiles, lane);
-          __syncwarp();
-          if (lane == 0) *ticket = 0u;  // ready for the next step
-        }
-      }
       ++n_used;
       __syncwarp();
       decode(s_queue[warp][n_used % kItemQueue], out);
@@ -615,6 +594,28 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
     for (long long i = unwaited; i < issued; ++i)
       mbar_wait_bounded(&my_bars[i % STAGES], (uint32_t)((i / STAGES) & 1), p.status);
   }
+}
+
+// ---- the share's normaliser: a warp per (layer, row, head) ----------------------------------------------
+//
+// Grid: kLseWarps warps per CTA over the (layer, row, head) triples of [layer0, layer0 + n_layers), in
+// that order (a CTA's warps read neighbouring rows of one layer, cells the record kernel has just written,
+// still in L2).
+constexpr int kLseWarps = 4;
+
+__global__ void __launch_bounds__(kLseWarps * 32) lse_kernel(const AuditParams p) {
+  chain_release();
+  chain_wait();  // the record kernel's cells
+  if (*p.flag == 0) return;  // nothing was recorded this step
+  const int lane = threadIdx.x & 31;
+  const long long triple = (long long)blockIdx.x * kLseWarps + (threadIdx.x >> 5);
+  if (triple >= (long long)p.n_layers * p.rows * p.heads) return;
+  const int head = (int)(triple % p.heads);
+  const long long lr = triple / p.heads;
+  const int row = (int)(lr % p.rows), layer = p.layer0 + (int)(lr / p.rows);
+  const RowInfo ri = row_info(p, row, false);
+  if (ri.n_chunks == 0) return;  // the combine writes the row NaN
+  merge_row_lse(p, layer, row, head, ri.n_tiles, lane);
 }
 
 // ---- the combine kernel: the cells and log totals of a row's layers into its final share -------------
@@ -792,6 +793,11 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
   AuditParams ps = p;
   ps.layer0 = share0;
   ps.n_layers = share_layers;
+  const long long triples = (long long)share_layers * p.rows * p.heads;
+  launch_chained(lse_kernel, dim3((unsigned)((triples + kLseWarps - 1) / kLseWarps)), dim3(kLseWarps * 32), 0, stream,
+                 ps);
+  rc = check_launch("lse_kernel");
+  if (rc != EKV_OK) return rc;
   launch_chained(combine_kernel, dim3(cdiv(cdiv(p.width, p.tile_blocks), kCombineTiles), p.rows),
                  dim3(kCombineThreads), 0, stream, ps);
   return check_launch("combine_kernel");
@@ -814,7 +820,7 @@ int dispatch(const AuditParams& p, int tt, bool finalize, int share0, int share_
 
 // The workspace: [row_tickets, row_lse) holds tickets and counters, all zero between steps.
 struct WorkspaceLayout {
-  size_t row_tickets, counters, lh_tickets, row_lse, kmaps, total;
+  size_t row_tickets, counters, row_lse, kmaps, total;
 };
 
 WorkspaceLayout workspace_layout(int layers, int rows, int width) {
@@ -823,8 +829,7 @@ WorkspaceLayout workspace_layout(int layers, int rows, int width) {
   const size_t cells = (size_t)layers * rows * kMaxQ;
   w.row_tickets = 0;
   w.counters = round_up((size_t)rows * 4, 256);
-  w.lh_tickets = w.counters + 256;
-  w.row_lse = w.lh_tickets + round_up(cells * 4, 256);
+  w.row_lse = w.counters + 256;
   w.kmaps = w.row_lse + round_up(cells * sizeof(float2), 256);
   w.total = w.kmaps + round_up((size_t)layers * sizeof(CUtensorMap), 256);
   return w;
@@ -910,7 +915,6 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
     uint8_t* base = static_cast<uint8_t*>(workspace);
     p.row_tickets = reinterpret_cast<uint32_t*>(base + w.row_tickets);
     p.item_counter = need_workspace ? reinterpret_cast<uint32_t*>(base + w.counters) : nullptr;
-    p.lh_tickets = reinterpret_cast<uint32_t*>(base + w.lh_tickets);
     p.row_lse = reinterpret_cast<float2*>(base + w.row_lse);
     p.kmaps = need_workspace ? reinterpret_cast<const CUtensorMap*>(base + w.kmaps) : nullptr;
   }

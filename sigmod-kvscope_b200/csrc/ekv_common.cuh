@@ -106,14 +106,6 @@ __device__ __forceinline__ void stage_row(T* dst, const T* src, int n) {
 }
 
 
-// atomicAdd with acquire-release semantics at GPU scope: a thread's earlier writes (and, after a warp
-// or CTA barrier, its partners') are visible to a thread whose acquire reads a later value.
-__device__ __forceinline__ uint32_t atomic_add_acq_rel(uint32_t* address, uint32_t value) {
-  uint32_t old;
-  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(address), "r"(value) : "memory");
-  return old;
-}
-
 __device__ __forceinline__ void set_status(uint32_t* status, uint32_t bits) {
   if (status != nullptr) atomicOr(status, bits);
 }

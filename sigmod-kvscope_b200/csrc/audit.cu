@@ -83,6 +83,7 @@ struct AuditParams {
   // the share's normaliser: each (layer, row, query row)'s log total over its tiles as (M, S), the total
   // being S * exp(M) (S == 0: no data), made by lse_kernel after the record kernel
   float2* row_lse;          // [layers][rows][kMaxQ]
+  int32_t* row_contrib;     // [rows] (layer, query row) pairs with data, summed by lse_kernel, zeroed by the combine
   uint32_t* status;
 };
 
@@ -616,116 +617,114 @@ __global__ void __launch_bounds__(kLseWarps * 32) lse_kernel(const AuditParams p
   const RowInfo ri = row_info(p, row, false);
   if (ri.n_chunks == 0) return;  // the combine writes the row NaN
   merge_row_lse(p, layer, row, head, ri.n_tiles, lane);
+  __syncwarp();
+  if (lane == 0) {  // the contributors: query rows with data
+    const float2* tot = p.row_lse + ((size_t)layer * p.rows + row) * kMaxQ + head * p.G;
+    int c = 0;
+    for (int g = 0; g < p.G; ++g) c += tot[g].y > 0.f;
+    if (c) atomicAdd(p.row_contrib + row, c);
+  }
 }
 
 // ---- the combine kernel: the cells and log totals of a row's layers into its final share -------------
 //
-// Grid (tiles of the width / kCombineTiles, rows), kCombineTiles x kCombineSlices threads: thread
-// (tile j, slice k) takes tile t0 + j of the layers la + k, la + k + kCombineSlices, ... of
-// [layer0, layer0 + n_layers) with data. A block b of tile t (its cell is the tile's first block's) gets,
-// over those layers and their query rows with data, exp(u_b) / sum_b' exp(u_b') = l exp(m - M) / S / n_t
-// (n_t the tile's blocks in the row: the blocks of a partial last tile share its whole weight, the
-// reference's regain), summed and divided by the contributors (mean) or maxed, the row then divided
-// by its total by the CTA that finishes the row last (max). The slices combine in slice order. A row
-// that records nothing, or has no contributor, is NaN; blocks past the row are 0.
-constexpr int kCombineTiles = 32;
-constexpr int kCombineSlices = 4;
-static_assert(kCombineTiles * kCombineSlices == kCombineThreads, "a thread per (tile, slice)");
+// Grid (tiles of the width / tiles per CTA, rows), four warps. A warp takes 32 / lanes_q tiles and its
+// lanes the query rows (lanes_q of them, the query rows rounded up to a power of two, at most 32; a lane
+// takes query rows q, q + lanes_q, ...), so the cells a warp loads are contiguous; every lane goes over
+// every layer of [layer0, layer0 + n_layers), four layers' loads in flight at a time. A block b of tile t
+// (its cell is the tile's first block's) gets, over the layers and query rows with data,
+// exp(u_b) / sum_b' exp(u_b') = l exp(m - M) / S / n_t (n_t the tile's blocks in the row: the blocks of a
+// partial last tile share its whole weight, the reference's regain), summed over the query rows by
+// xor-shuffles and divided by the contributors (mean) or maxed, the row then divided by its total by the
+// CTA that finishes the row last (max). A row that records nothing, or has no contributor, is NaN; blocks
+// past the row are 0. The CTA that finishes a row last zeroes its contributor count for the next step.
+constexpr int kCombineWarps = kCombineThreads / 32;
+
+__host__ __device__ inline int combine_lanes_q(int Q) {
+  int q = 1;
+  while (q < Q && q < 32) q <<= 1;
+  return q;
+}
 
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditParams p) {
-  __shared__ int s_c[kCombineThreads / 32];
   __shared__ float s_red[kCombineThreads / 32];
-  __shared__ float s_part[kCombineSlices][kCombineTiles];
   __shared__ int s_last;
-  const int r = blockIdx.y, tid = threadIdx.x;
+  const int r = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   chain_release();
-  chain_wait();  // the record kernel's cells and log totals
+  chain_wait();  // the record kernel's cells, lse_kernel's log totals and contributor counts
   if (*p.flag == 0) return;  // nothing was recorded this step
   const RowInfo ri = row_info(p, r, false);
   float* out = p.share_out + (size_t)r * p.width;
   const int TB = p.tile_blocks, Q = p.Q;
-  const int t0 = blockIdx.x * kCombineTiles;
-  const int b_lo = t0 * TB, b_hi = min((t0 + kCombineTiles) * TB, p.width);  // this CTA's blocks
-  if (ri.n_chunks == 0) {
-    for (int b = b_lo + tid; b < b_hi; b += kCombineThreads) out[b] = NAN;
-    if (blockIdx.x == 0 && tid == 0) p.contrib_out[r] = 0;
-    return;
-  }
-  const int la = p.layer0, lb = p.layer0 + p.n_layers;
-  // the contributors: (layer, query row) pairs with data
-  int c = 0;
-  for (int i = tid; i < (lb - la) * Q; i += kCombineThreads) {
-    const int L = la + i / Q, q = i % Q;
-    c += __ldcg(&p.row_lse[((size_t)L * p.rows + r) * kMaxQ + q].y) > 0.f;
-  }
-  for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(kFullMask, c, off);
-  if ((tid & 31) == 0) s_c[tid >> 5] = c;
-  __syncthreads();
-  int contributors = 0;
-  for (int w = 0; w < kCombineThreads / 32; ++w) contributors += s_c[w];
+  const int lanes_q = combine_lanes_q(Q), tiles_w = 32 / lanes_q;
+  const int t0 = blockIdx.x * kCombineWarps * tiles_w;
+  const int b_lo = t0 * TB, b_hi = min((t0 + kCombineWarps * tiles_w) * TB, p.width);  // this CTA's blocks
+  const int contributors = ri.n_chunks ? __ldcg(p.row_contrib + r) : 0;
   if (blockIdx.x == 0 && tid == 0) p.contrib_out[r] = contributors;
-  if (contributors == 0) {
-    for (int b = b_lo + tid; b < b_hi; b += kCombineThreads) out[b] = NAN;
-    return;
-  }
   const bool agg_max = p.aggregate == EKV_AGG_MAX;
-  const int n = ri.n_blocks, n_tiles = (n + TB - 1) / TB;
-  const int j = tid % kCombineTiles, k = tid / kCombineTiles;
-  const int t = t0 + j;
-  const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
-  float v = 0.f;
-  if (t < n_tiles) {
-    for (int L = la + k; L < lb; L += kCombineSlices) {
-      const size_t lr = (size_t)L * p.rows + r;
-      const float* cm = p.lse + (lr * p.width + (size_t)t * TB) * Q;
-      const float2* tot = p.row_lse + lr * kMaxQ;
-      for (int q0 = 0; q0 < Q; q0 += 8) {  // eight query rows' loads in flight, then their shares
-        float m[8], l[8];
-        float2 z[8];
+  if (contributors > 0) {
+    const int n = ri.n_blocks, n_tiles = (n + TB - 1) / TB;
+    const int t = t0 + warp * tiles_w + lane / lanes_q, q0 = lane % lanes_q;
+    const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
+    float v = 0.f;
+    if (t < n_tiles) {
+      constexpr int U = 4;  // layers whose loads are in flight together
+      const int la = p.layer0, lb = p.layer0 + p.n_layers;
+      for (int L0 = la; L0 < lb; L0 += U) {
+        for (int q = q0; q < Q; q += lanes_q) {
+          float m[U], l[U];
+          float2 z[U];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const bool ok = q0 + u < Q;
-          z[u] = ok ? __ldcg(tot + q0 + u) : make_float2(0.f, 0.f);
-          m[u] = ok ? __ldcg(cm + q0 + u) : -INFINITY;
-          l[u] = ok ? __ldcg(cm + plane + q0 + u) : 0.f;
-        }
+          for (int u = 0; u < U; ++u) {
+            const bool ok = L0 + u < lb;
+            const size_t lr = (size_t)(ok ? L0 + u : la) * p.rows + r;
+            z[u] = ok ? __ldcg(p.row_lse + lr * kMaxQ + q) : make_float2(0.f, 0.f);
+            const float* cm = p.lse + (lr * p.width + (size_t)t * TB) * Q + q;
+            m[u] = ok ? __ldcg(cm) : -INFINITY;
+            l[u] = ok ? __ldcg(cm + plane) : 0.f;
+          }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          // a query row without data, or a cell without data (m = -inf, l = 0), has no share
-          const float sh = (z[u].y > 0.f && m[u] > -INFINITY && l[u] > 0.f) ? l[u] / z[u].y * __expf(m[u] - z[u].x)
-                                                                            : 0.f;
-          v = agg_max ? fmaxf(v, sh) : v + sh;
+          for (int u = 0; u < U; ++u) {
+            // a query row without data, or a cell without data (m = -inf, l = 0), has no share
+            const float sh = (z[u].y > 0.f && m[u] > -INFINITY && l[u] > 0.f) ? l[u] / z[u].y * __expf(m[u] - z[u].x)
+                                                                              : 0.f;
+            v = agg_max ? fmaxf(v, sh) : v + sh;
+          }
         }
       }
     }
-  }
-  s_part[k][j] = v;
-  __syncthreads();
-  if (k == 0) {
-    for (int kk = 1; kk < kCombineSlices; ++kk) v = agg_max ? fmaxf(v, s_part[kk][j]) : v + s_part[kk][j];
+    for (int off = 1; off < lanes_q; off <<= 1) {
+      const float o = __shfl_xor_sync(kFullMask, v, off);
+      v = agg_max ? fmaxf(v, o) : v + o;
+    }
     const int bt0 = t * TB;
-    if (bt0 < p.width) {
+    if (q0 == 0 && bt0 < p.width && t < t0 + kCombineWarps * tiles_w) {
       const int in_row = t < n_tiles ? min(TB, n - bt0) : 0;  // the tile's blocks in the row
       const float each = in_row > 0 ? (agg_max ? v / (float)in_row : v / (float)in_row / (float)contributors) : 0.f;
       for (int b = bt0; b < bt0 + TB && b < p.width; ++b) out[b] = b < n ? each : 0.f;
     }
+  } else {
+    for (int b = b_lo + tid; b < b_hi; b += kCombineThreads) out[b] = NAN;
   }
-  if (!agg_max) return;
-  // max: the last CTA of the row divides the row by its total
+  if (ri.n_chunks == 0) return;  // no contributor count to reset
+  // the CTA that finishes the row last: the row's total (max) and the count's reset
   __threadfence();
   __syncthreads();
   if (tid == 0) s_last = atomicAdd(&p.row_tickets[r], 1u) == gridDim.x - 1;
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  float part = 0.f;
-  for (int b = tid; b < n; b += kCombineThreads) part += __ldcg(out + b);
-  const float total = block_sum_fixed_order<kCombineThreads>(part, s_red);
-  for (int b = tid; b < n; b += kCombineThreads) {
-    const float x = __ldcg(out + b);
-    out[b] = total > 0.f ? x / total : 0.f;
+  if (agg_max && contributors > 0) {
+    const int n = ri.n_blocks;
+    float part = 0.f;
+    for (int b = tid; b < n; b += kCombineThreads) part += __ldcg(out + b);
+    const float total = block_sum_fixed_order<kCombineThreads>(part, s_red);
+    for (int b = tid; b < n; b += kCombineThreads) {
+      const float x = __ldcg(out + b);
+      out[b] = total > 0.f ? x / total : 0.f;
+    }
   }
-  if (tid == 0) p.row_tickets[r] = 0;  // ready for the next step
+  if (tid == 0) p.row_tickets[r] = 0, p.row_contrib[r] = 0;  // ready for the next step
 }
 
 // One tensor map per layer of a step: the host-encoded template with the layer's key-cache address
@@ -798,7 +797,8 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
                  ps);
   rc = check_launch("lse_kernel");
   if (rc != EKV_OK) return rc;
-  launch_chained(combine_kernel, dim3(cdiv(cdiv(p.width, p.tile_blocks), kCombineTiles), p.rows),
+  const int tiles_per_cta = kCombineWarps * (32 / combine_lanes_q(p.Q));
+  launch_chained(combine_kernel, dim3(cdiv(cdiv(p.width, p.tile_blocks), tiles_per_cta), p.rows),
                  dim3(kCombineThreads), 0, stream, ps);
   return check_launch("combine_kernel");
 }
@@ -820,7 +820,7 @@ int dispatch(const AuditParams& p, int tt, bool finalize, int share0, int share_
 
 // The workspace: [row_tickets, row_lse) holds tickets and counters, all zero between steps.
 struct WorkspaceLayout {
-  size_t row_tickets, counters, row_lse, kmaps, total;
+  size_t row_tickets, counters, row_contrib, row_lse, kmaps, total;
 };
 
 WorkspaceLayout workspace_layout(int layers, int rows, int width) {
@@ -829,7 +829,8 @@ WorkspaceLayout workspace_layout(int layers, int rows, int width) {
   const size_t cells = (size_t)layers * rows * kMaxQ;
   w.row_tickets = 0;
   w.counters = round_up((size_t)rows * 4, 256);
-  w.row_lse = w.counters + 256;
+  w.row_contrib = w.counters + 256;
+  w.row_lse = w.row_contrib + round_up((size_t)rows * 4, 256);
   w.kmaps = w.row_lse + round_up(cells * sizeof(float2), 256);
   w.total = w.kmaps + round_up((size_t)layers * sizeof(CUtensorMap), 256);
   return w;
@@ -916,6 +917,7 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
     p.row_tickets = reinterpret_cast<uint32_t*>(base + w.row_tickets);
     p.item_counter = need_workspace ? reinterpret_cast<uint32_t*>(base + w.counters) : nullptr;
     p.row_lse = reinterpret_cast<float2*>(base + w.row_lse);
+    p.row_contrib = reinterpret_cast<int32_t*>(base + w.row_contrib);
     p.kmaps = need_workspace ? reinterpret_cast<const CUtensorMap*>(base + w.kmaps) : nullptr;
   }
   return EKV_OK;

@@ -172,28 +172,40 @@ __device__ __forceinline__ void merge_row_lse(const AuditParams& p, int layer, i
   const float* cl = cm + plane;
   const int stride = p.tile_blocks * p.Q;  // floats from one tile's cell to the next tile's
   float2* out = p.row_lse + lr * kMaxQ + head * p.G;
-  constexpr int kTiles = 4;  // tiles of a lane per round
+  // four query rows in one 16-byte load when the cells allow it (G and Q multiples of 4)
+  const bool vec = (p.G & 3) == 0 && (p.Q & 3) == 0 && (reinterpret_cast<uintptr_t>(p.lse) & 15) == 0;
+  constexpr int kTiles = 8;  // tiles of a lane per round, every load of a round in flight together
   for (int g0 = 0; g0 < p.G; g0 += 4) {
     const int ng = p.G - g0 < 4 ? p.G - g0 : 4;
     float M[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, S[4] = {0.f, 0.f, 0.f, 0.f};
     for (int t0 = lane; t0 < n_tiles; t0 += 32 * kTiles) {
-      float mv[kTiles][4], lv[kTiles][4];
+      float4 mv[kTiles], lv[kTiles];
 #pragma unroll
       for (int u = 0; u < kTiles; ++u) {
         const int t = t0 + 32 * u;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const bool ok = t < n_tiles && k < ng;
-          const size_t at = (size_t)(ok ? t : 0) * stride + g0 + (ok ? k : 0);
-          mv[u][k] = ok ? __ldcg(cm + at) : -INFINITY;
-          lv[u][k] = ok ? __ldcg(cl + at) : 0.f;
+        const bool ok = t < n_tiles;
+        const size_t at = (size_t)(ok ? t : 0) * stride + g0;
+        if (vec) {
+          mv[u] = ok ? __ldcg(reinterpret_cast<const float4*>(cm + at)) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+          lv[u] = ok ? __ldcg(reinterpret_cast<const float4*>(cl + at)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+          mv[u].x = ok ? __ldcg(cm + at) : -INFINITY;
+          mv[u].y = ok && ng > 1 ? __ldcg(cm + at + 1) : -INFINITY;
+          mv[u].z = ok && ng > 2 ? __ldcg(cm + at + 2) : -INFINITY;
+          mv[u].w = ok && ng > 3 ? __ldcg(cm + at + 3) : -INFINITY;
+          lv[u].x = ok ? __ldcg(cl + at) : 0.f;
+          lv[u].y = ok && ng > 1 ? __ldcg(cl + at + 1) : 0.f;
+          lv[u].z = ok && ng > 2 ? __ldcg(cl + at + 2) : 0.f;
+          lv[u].w = ok && ng > 3 ? __ldcg(cl + at + 3) : 0.f;
         }
       }
 #pragma unroll
-      for (int u = 0; u < kTiles; ++u)
+      for (int u = 0; u < kTiles; ++u) {
+        const float mk[4] = {mv[u].x, mv[u].y, mv[u].z, mv[u].w}, lk[4] = {lv[u].x, lv[u].y, lv[u].z, lv[u].w};
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          if (mv[u][k] > -INFINITY && lv[u][k] > 0.f) lse_merge(M[k], S[k], mv[u][k], lv[u][k]);
+          if (mk[k] > -INFINITY && lk[k] > 0.f) lse_merge(M[k], S[k], mk[k], lk[k]);
+      }
     }
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1)
@@ -628,21 +640,26 @@ __global__ void __launch_bounds__(kLseWarps * 32) lse_kernel(const AuditParams p
 
 // ---- the combine kernel: the cells and log totals of a row's layers into its final share -------------
 //
-// Grid (tiles of the width / tiles per CTA, rows), four warps. A warp takes 32 / lanes_q tiles and its
-// lanes the query rows (lanes_q of them, the query rows rounded up to a power of two, at most 32; a lane
-// takes query rows q, q + lanes_q, ...), so the cells a warp loads are contiguous; every lane goes over
-// every layer of [layer0, layer0 + n_layers), four layers' loads in flight at a time. A block b of tile t
-// (its cell is the tile's first block's) gets, over the layers and query rows with data,
-// exp(u_b) / sum_b' exp(u_b') = l exp(m - M) / S / n_t (n_t the tile's blocks in the row: the blocks of a
-// partial last tile share its whole weight, the reference's regain), summed over the query rows by
-// xor-shuffles and divided by the contributors (mean) or maxed, the row then divided by its total by the
-// CTA that finishes the row last (max). A row that records nothing, or has no contributor, is NaN; blocks
-// past the row are 0. The CTA that finishes a row last zeroes its contributor count for the next step.
+// Grid (tiles of the width / kCombineWarps, rows): a warp per tile. Its lanes split the (layer, query row)
+// pairs of [layer0, layer0 + n_layers): lanes_q lanes over the query rows (four at a time in 16-byte loads
+// when the cells allow, else one; lanes_q = those groups rounded up to a power of two, at most 32) times
+// 32 / lanes_q slices of the layers (slice k takes layers layer0 + k, + 32 / lanes_q, ...), four layers'
+// loads in flight at a time. The tile's block b (its cell is the tile's first block's) gets, over the pairs
+// with data, exp(u_b) / sum_b' exp(u_b') = l exp(m - M) / S / n_t (n_t the tile's blocks in the row: the
+// blocks of a partial last tile share its whole weight, the reference's regain), summed over the lanes by
+// xor-shuffles (the same order on every launch) and divided by the contributors (mean), or maxed, the row
+// then divided by its total by the CTA that finishes the row last (max). A row that records nothing, or
+// has no contributor, is NaN; blocks past the row are 0. The CTA that finishes a row last zeroes its
+// contributor count for the next step.
 constexpr int kCombineWarps = kCombineThreads / 32;
 
+// query rows of one lane's load: four (a 16-byte load) when the cells allow it
+__host__ __device__ inline int combine_vec(int Q) { return (Q & 3) == 0 ? 4 : 1; }
+
 __host__ __device__ inline int combine_lanes_q(int Q) {
+  const int groups = Q / combine_vec(Q);
   int q = 1;
-  while (q < Q && q < 32) q <<= 1;
+  while (q < groups && q < 32) q <<= 1;
   return q;
 }
 
@@ -656,55 +673,73 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditPar
   const RowInfo ri = row_info(p, r, false);
   float* out = p.share_out + (size_t)r * p.width;
   const int TB = p.tile_blocks, Q = p.Q;
-  const int lanes_q = combine_lanes_q(Q), tiles_w = 32 / lanes_q;
-  const int t0 = blockIdx.x * kCombineWarps * tiles_w;
-  const int b_lo = t0 * TB, b_hi = min((t0 + kCombineWarps * tiles_w) * TB, p.width);  // this CTA's blocks
+  const int t = blockIdx.x * kCombineWarps + warp;
   const int contributors = ri.n_chunks ? __ldcg(p.row_contrib + r) : 0;
   if (blockIdx.x == 0 && tid == 0) p.contrib_out[r] = contributors;
   const bool agg_max = p.aggregate == EKV_AGG_MAX;
+  const int bt0 = t * TB;  // the tile's first block
   if (contributors > 0) {
     const int n = ri.n_blocks, n_tiles = (n + TB - 1) / TB;
-    const int t = t0 + warp * tiles_w + lane / lanes_q, q0 = lane % lanes_q;
-    const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
     float v = 0.f;
     if (t < n_tiles) {
-      constexpr int U = 4;  // layers whose loads are in flight together
+      const int V = combine_vec(Q), lanes_q = combine_lanes_q(Q), slices = 32 / lanes_q;
+      const int qg = lane % lanes_q, slice = lane / lanes_q;
+      const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
       const int la = p.layer0, lb = p.layer0 + p.n_layers;
-      for (int L0 = la; L0 < lb; L0 += U) {
-        for (int q = q0; q < Q; q += lanes_q) {
-          float m[U], l[U];
-          float2 z[U];
+      constexpr int U = 4;  // layers whose loads are in flight together
+      for (int q = qg * V; q < Q; q += lanes_q * V) {
+        for (int L0 = la + slice; L0 < lb; L0 += U * slices) {
+          float4 m[U], l[U], zm[U], zs[U];
 #pragma unroll
           for (int u = 0; u < U; ++u) {
-            const bool ok = L0 + u < lb;
-            const size_t lr = (size_t)(ok ? L0 + u : la) * p.rows + r;
-            z[u] = ok ? __ldcg(p.row_lse + lr * kMaxQ + q) : make_float2(0.f, 0.f);
-            const float* cm = p.lse + (lr * p.width + (size_t)t * TB) * Q + q;
-            m[u] = ok ? __ldcg(cm) : -INFINITY;
-            l[u] = ok ? __ldcg(cm + plane) : 0.f;
+            const int L = L0 + u * slices;
+            const bool ok = L < lb;
+            const size_t lr = (size_t)(ok ? L : la) * p.rows + r;
+            const float* cm = p.lse + (lr * p.width + (size_t)bt0) * Q + q;
+            const float2* z = p.row_lse + lr * kMaxQ + q;
+            if (V == 4) {
+              m[u] = ok ? __ldcg(reinterpret_cast<const float4*>(cm)) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+              l[u] = ok ? __ldcg(reinterpret_cast<const float4*>(cm + plane)) : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float4 z01 = ok ? __ldcg(reinterpret_cast<const float4*>(z)) : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float4 z23 = ok ? __ldcg(reinterpret_cast<const float4*>(z + 2)) : make_float4(0.f, 0.f, 0.f, 0.f);
+              zm[u] = make_float4(z01.x, z01.z, z23.x, z23.z);
+              zs[u] = make_float4(z01.y, z01.w, z23.y, z23.w);
+            } else {
+              m[u] = make_float4(ok ? __ldcg(cm) : -INFINITY, -INFINITY, -INFINITY, -INFINITY);
+              l[u] = make_float4(ok ? __ldcg(cm + plane) : 0.f, 0.f, 0.f, 0.f);
+              const float2 z0 = ok ? __ldcg(z) : make_float2(0.f, 0.f);
+              zm[u] = make_float4(z0.x, 0.f, 0.f, 0.f);
+              zs[u] = make_float4(z0.y, 0.f, 0.f, 0.f);
+            }
           }
 #pragma unroll
           for (int u = 0; u < U; ++u) {
-            // a query row without data, or a cell without data (m = -inf, l = 0), has no share
-            const float sh = (z[u].y > 0.f && m[u] > -INFINITY && l[u] > 0.f) ? l[u] / z[u].y * __expf(m[u] - z[u].x)
-                                                                              : 0.f;
-            v = agg_max ? fmaxf(v, sh) : v + sh;
+            const float mk[4] = {m[u].x, m[u].y, m[u].z, m[u].w}, lk[4] = {l[u].x, l[u].y, l[u].z, l[u].w};
+            const float Mk[4] = {zm[u].x, zm[u].y, zm[u].z, zm[u].w}, Sk[4] = {zs[u].x, zs[u].y, zs[u].z, zs[u].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              // a query row without data, or a cell without data (m = -inf, l = 0), has no share
+              const float sh = (Sk[k] > 0.f && mk[k] > -INFINITY && lk[k] > 0.f) ? lk[k] / Sk[k] * __expf(mk[k] - Mk[k])
+                                                                                 : 0.f;
+              v = agg_max ? fmaxf(v, sh) : v + sh;
+            }
           }
         }
       }
     }
-    for (int off = 1; off < lanes_q; off <<= 1) {
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
       const float o = __shfl_xor_sync(kFullMask, v, off);
       v = agg_max ? fmaxf(v, o) : v + o;
     }
-    const int bt0 = t * TB;
-    if (q0 == 0 && bt0 < p.width && t < t0 + kCombineWarps * tiles_w) {
+    if (lane < TB && bt0 + lane < p.width) {
+      const int b = bt0 + lane;
       const int in_row = t < n_tiles ? min(TB, n - bt0) : 0;  // the tile's blocks in the row
       const float each = in_row > 0 ? (agg_max ? v / (float)in_row : v / (float)in_row / (float)contributors) : 0.f;
-      for (int b = bt0; b < bt0 + TB && b < p.width; ++b) out[b] = b < n ? each : 0.f;
+      out[b] = b < n ? each : 0.f;
     }
-  } else {
-    for (int b = b_lo + tid; b < b_hi; b += kCombineThreads) out[b] = NAN;
+  } else if (lane < TB && bt0 + lane < p.width) {
+    out[bt0 + lane] = NAN;
   }
   if (ri.n_chunks == 0) return;  // no contributor count to reset
   // the CTA that finishes the row last: the row's total (max) and the count's reset
@@ -797,8 +832,7 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
                  ps);
   rc = check_launch("lse_kernel");
   if (rc != EKV_OK) return rc;
-  const int tiles_per_cta = kCombineWarps * (32 / combine_lanes_q(p.Q));
-  launch_chained(combine_kernel, dim3(cdiv(cdiv(p.width, p.tile_blocks), tiles_per_cta), p.rows),
+  launch_chained(combine_kernel, dim3(cdiv(cdiv(p.width, p.tile_blocks), kCombineWarps), p.rows),
                  dim3(kCombineThreads), 0, stream, ps);
   return check_launch("combine_kernel");
 }

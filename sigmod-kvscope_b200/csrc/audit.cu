@@ -44,7 +44,6 @@ constexpr int kMaxQ = 128;
 constexpr int kMaxRows = 2048;
 constexpr int kMaxLayers = 1024;
 constexpr int kChunkTiles = EKV_AUDIT_CHUNK_TILES;
-constexpr int kCombineThreads = 128;
 constexpr int kMinCtas = 12 / kWarps > 0 ? 12 / kWarps : 1;  // registers for 12 warps per SM
 constexpr int kItemQueue = 16;  // items a warp has taken but not yet consumed (at most STAGES + 2)
 
@@ -78,12 +77,10 @@ struct AuditParams {
   float* share_out;
   int32_t* contrib_out;
   int aggregate;
-  uint32_t* row_tickets;    // [rows]
   uint32_t* item_counter;   // items handed out beyond each warp's first (zeroed by kmap_kernel); NULL: static order
   // the share's normaliser: each (layer, row, query row)'s log total over its tiles as (M, S), the total
-  // being S * exp(M) (S == 0: no data), made by lse_kernel after the record kernel
+  // being S * exp(M) (S == 0: no data), made by share_kernel's first pass
   float2* row_lse;          // [layers][rows][kMaxQ]
-  int32_t* row_contrib;     // [rows] (layer, query row) pairs with data, summed by lse_kernel, zeroed by the combine
   uint32_t* status;
 };
 
@@ -609,84 +606,75 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
   }
 }
 
-// ---- the share's normaliser: a warp per (layer, row, head) ----------------------------------------------
+// ---- the share kernel: one CTA per row ---------------------------------------------------------------------
 //
-// Grid: kLseWarps warps per CTA over the (layer, row, head) triples of [layer0, layer0 + n_layers), in
-// that order (a CTA's warps read neighbouring rows of one layer, cells the record kernel has just written,
-// still in L2).
-constexpr int kLseWarps = 4;
+// Pass 1: warp w merges the (layer, head) pairs w, w + kShareWarps, ... of [layer0, layer0 + n_layers)
+// into the query rows' log totals (merge_row_lse; row_lse in the workspace). Pass 2, after a barrier: warp
+// w takes the row's tiles in groups; its lanes split (tile, layer slice, query rows): lanes_q lanes over
+// the query rows (four at a time in 16-byte loads when the cells allow, else one), `slices` slices of the
+// layers (slice k takes layers layer0 + k, + slices, ...: about four per lane, their loads in flight
+// together) and the rest over neighbouring tiles. A tile's block b (its cell is the tile's first block's)
+// gets, over the (layer, query row) pairs with data, exp(u_b) / sum_b' exp(u_b') = l exp(m - M) / S / n_t
+// (n_t the tile's blocks in the row: a partial last tile's blocks share its whole weight, the reference's
+// regain), summed over the tile's lanes by xor-shuffles (the same order on every launch) and divided by the
+// contributors (mean), or maxed and the row divided by its total (max, a fixed-order CTA sum). A row that
+// records nothing, or has no contributor, is NaN; blocks past the row are 0.
+constexpr int kShareWarps = 16;
+constexpr int kShareThreads = kShareWarps * 32;
 
-__global__ void __launch_bounds__(kLseWarps * 32) lse_kernel(const AuditParams p) {
+// query rows of one lane's load: four (a 16-byte load) when the cells allow it
+__host__ __device__ inline int share_vec(int Q) { return (Q & 3) == 0 ? 4 : 1; }
+
+__global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams p) {
+  __shared__ float s_red[kShareWarps];
+  __shared__ int s_c[kShareWarps];
+  const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   chain_release();
   chain_wait();  // the record kernel's cells
   if (*p.flag == 0) return;  // nothing was recorded this step
-  const int lane = threadIdx.x & 31;
-  const long long triple = (long long)blockIdx.x * kLseWarps + (threadIdx.x >> 5);
-  if (triple >= (long long)p.n_layers * p.rows * p.heads) return;
-  const int head = (int)(triple % p.heads);
-  const long long lr = triple / p.heads;
-  const int row = (int)(lr % p.rows), layer = p.layer0 + (int)(lr / p.rows);
-  const RowInfo ri = row_info(p, row, false);
-  if (ri.n_chunks == 0) return;  // the combine writes the row NaN
-  merge_row_lse(p, layer, row, head, ri.n_tiles, lane);
-  __syncwarp();
-  if (lane == 0) {  // the contributors: query rows with data
-    const float2* tot = p.row_lse + ((size_t)layer * p.rows + row) * kMaxQ + head * p.G;
-    int c = 0;
-    for (int g = 0; g < p.G; ++g) c += tot[g].y > 0.f;
-    if (c) atomicAdd(p.row_contrib + row, c);
-  }
-}
-
-// ---- the combine kernel: the cells and log totals of a row's layers into its final share -------------
-//
-// Grid (tiles of the width / kCombineWarps, rows): a warp per tile. Its lanes split the (layer, query row)
-// pairs of [layer0, layer0 + n_layers): lanes_q lanes over the query rows (four at a time in 16-byte loads
-// when the cells allow, else one; lanes_q = those groups rounded up to a power of two, at most 32) times
-// 32 / lanes_q slices of the layers (slice k takes layers layer0 + k, + 32 / lanes_q, ...), four layers'
-// loads in flight at a time. The tile's block b (its cell is the tile's first block's) gets, over the pairs
-// with data, exp(u_b) / sum_b' exp(u_b') = l exp(m - M) / S / n_t (n_t the tile's blocks in the row: the
-// blocks of a partial last tile share its whole weight, the reference's regain), summed over the lanes by
-// xor-shuffles (the same order on every launch) and divided by the contributors (mean), or maxed, the row
-// then divided by its total by the CTA that finishes the row last (max). A row that records nothing, or
-// has no contributor, is NaN; blocks past the row are 0. The CTA that finishes a row last zeroes its
-// contributor count for the next step.
-constexpr int kCombineWarps = kCombineThreads / 32;
-
-// query rows of one lane's load: four (a 16-byte load) when the cells allow it
-__host__ __device__ inline int combine_vec(int Q) { return (Q & 3) == 0 ? 4 : 1; }
-
-__host__ __device__ inline int combine_lanes_q(int Q) {
-  const int groups = Q / combine_vec(Q);
-  int q = 1;
-  while (q < groups && q < 32) q <<= 1;
-  return q;
-}
-
-__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditParams p) {
-  __shared__ float s_red[kCombineThreads / 32];
-  __shared__ int s_last;
-  const int r = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  chain_release();
-  chain_wait();  // the record kernel's cells, lse_kernel's log totals and contributor counts
-  if (*p.flag == 0) return;  // nothing was recorded this step
   const RowInfo ri = row_info(p, r, false);
   float* out = p.share_out + (size_t)r * p.width;
-  const int TB = p.tile_blocks, Q = p.Q;
-  const int t = blockIdx.x * kCombineWarps + warp;
-  const int contributors = ri.n_chunks ? __ldcg(p.row_contrib + r) : 0;
-  if (blockIdx.x == 0 && tid == 0) p.contrib_out[r] = contributors;
+  if (ri.n_chunks == 0) {
+    for (int b = tid; b < p.width; b += kShareThreads) out[b] = NAN;
+    if (tid == 0) p.contrib_out[r] = 0;
+    return;
+  }
+  const int TB = p.tile_blocks, Q = p.Q, n = ri.n_blocks, n_tiles = ri.n_tiles;
+  const int la = p.layer0, n_layers = p.n_layers;
+  // ---- pass 1: the log totals, and the contributors: (layer, query row) pairs with data ----------------
+  for (int j = warp; j < n_layers * p.heads; j += kShareWarps)
+    merge_row_lse(p, la + j / p.heads, r, j % p.heads, n_tiles, lane);
+  __syncthreads();  // every warp's totals, written to the workspace, are visible to the CTA
+  int c = 0;
+  for (int i = tid; i < n_layers * Q; i += kShareThreads)
+    c += __ldcg(&p.row_lse[((size_t)(la + i / Q) * p.rows + r) * kMaxQ + i % Q].y) > 0.f;
+  for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(kFullMask, c, off);
+  if (lane == 0) s_c[warp] = c;
+  __syncthreads();
+  int contributors = 0;
+  for (int w = 0; w < kShareWarps; ++w) contributors += s_c[w];
+  if (tid == 0) p.contrib_out[r] = contributors;
+  if (contributors == 0) {
+    for (int b = tid; b < p.width; b += kShareThreads) out[b] = NAN;
+    return;
+  }
+  // ---- pass 2: every tile's share ------------------------------------------------------------------
+  constexpr int U = 4;  // layers of a lane whose loads are in flight together
+  const int V = share_vec(Q);
+  int lanes_q = 1;
+  while (lanes_q < Q / V && lanes_q < 32) lanes_q <<= 1;
+  int slices = 1;  // a power of two, at most 32 / lanes_q, about U layers per lane
+  while (slices < 32 / lanes_q && slices * U < n_layers) slices <<= 1;
+  const int tiles_w = 32 / (lanes_q * slices);  // tiles of a warp per round
+  const int qg = lane % lanes_q, slice = (lane / lanes_q) % slices, tsub = lane / (lanes_q * slices);
+  const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
   const bool agg_max = p.aggregate == EKV_AGG_MAX;
-  const int bt0 = t * TB;  // the tile's first block
-  if (contributors > 0) {
-    const int n = ri.n_blocks, n_tiles = (n + TB - 1) / TB;
+  const int lb = la + n_layers;
+  for (int tb = warp * tiles_w; tb < n_tiles; tb += kShareWarps * tiles_w) {
+    const int t = tb + tsub;
     float v = 0.f;
     if (t < n_tiles) {
-      const int V = combine_vec(Q), lanes_q = combine_lanes_q(Q), slices = 32 / lanes_q;
-      const int qg = lane % lanes_q, slice = lane / lanes_q;
-      const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
-      const int la = p.layer0, lb = p.layer0 + p.n_layers;
-      constexpr int U = 4;  // layers whose loads are in flight together
+      const int bt0 = t * TB;
       for (int q = qg * V; q < Q; q += lanes_q * V) {
         for (int L0 = la + slice; L0 < lb; L0 += U * slices) {
           float4 m[U], l[U], zm[U], zs[U];
@@ -727,39 +715,26 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditPar
         }
       }
     }
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
+    for (int off = 1; off < lanes_q * slices; off <<= 1) {  // over the lanes of this tile
       const float o = __shfl_xor_sync(kFullMask, v, off);
       v = agg_max ? fmaxf(v, o) : v + o;
     }
-    if (lane < TB && bt0 + lane < p.width) {
-      const int b = bt0 + lane;
-      const int in_row = t < n_tiles ? min(TB, n - bt0) : 0;  // the tile's blocks in the row
-      const float each = in_row > 0 ? (agg_max ? v / (float)in_row : v / (float)in_row / (float)contributors) : 0.f;
-      out[b] = b < n ? each : 0.f;
-    }
-  } else if (lane < TB && bt0 + lane < p.width) {
-    out[bt0 + lane] = NAN;
-  }
-  if (ri.n_chunks == 0) return;  // no contributor count to reset
-  // the CTA that finishes the row last: the row's total (max) and the count's reset
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&p.row_tickets[r], 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  if (agg_max && contributors > 0) {
-    const int n = ri.n_blocks;
-    float part = 0.f;
-    for (int b = tid; b < n; b += kCombineThreads) part += __ldcg(out + b);
-    const float total = block_sum_fixed_order<kCombineThreads>(part, s_red);
-    for (int b = tid; b < n; b += kCombineThreads) {
-      const float x = __ldcg(out + b);
-      out[b] = total > 0.f ? x / total : 0.f;
+    if (t < n_tiles && (lane % (lanes_q * slices)) < TB) {
+      const int b = t * TB + lane % (lanes_q * slices);
+      const int in_row = min(TB, n - t * TB);  // the tile's blocks in the row
+      if (b < n) out[b] = agg_max ? v / (float)in_row : v / (float)in_row / (float)contributors;
     }
   }
-  if (tid == 0) p.row_tickets[r] = 0, p.row_contrib[r] = 0;  // ready for the next step
+  for (int b = n + tid; b < p.width; b += kShareThreads) out[b] = 0.f;  // past the row
+  if (!agg_max) return;
+  __syncthreads();  // every block's value of the row is written
+  float part = 0.f;
+  for (int b = tid; b < n; b += kShareThreads) part += __ldcg(out + b);
+  const float total = block_sum_fixed_order<kShareThreads>(part, s_red);
+  for (int b = tid; b < n; b += kShareThreads) {
+    const float x = __ldcg(out + b);
+    out[b] = total > 0.f ? x / total : 0.f;
+  }
 }
 
 // One tensor map per layer of a step: the host-encoded template with the layer's key-cache address
@@ -827,14 +802,8 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
   AuditParams ps = p;
   ps.layer0 = share0;
   ps.n_layers = share_layers;
-  const long long triples = (long long)share_layers * p.rows * p.heads;
-  launch_chained(lse_kernel, dim3((unsigned)((triples + kLseWarps - 1) / kLseWarps)), dim3(kLseWarps * 32), 0, stream,
-                 ps);
-  rc = check_launch("lse_kernel");
-  if (rc != EKV_OK) return rc;
-  launch_chained(combine_kernel, dim3(cdiv(cdiv(p.width, p.tile_blocks), kCombineWarps), p.rows),
-                 dim3(kCombineThreads), 0, stream, ps);
-  return check_launch("combine_kernel");
+  launch_chained(share_kernel, dim3(p.rows), dim3(kShareThreads), 0, stream, ps);
+  return check_launch("share_kernel");
 }
 
 template <typename T>
@@ -852,19 +821,19 @@ int dispatch(const AuditParams& p, int tt, bool finalize, int share0, int share_
   return fail(EKV_ENOTSUP, "no audit kernel for a tile of %d tokens", tt);
 }
 
-// The workspace: [row_tickets, row_lse) holds tickets and counters, all zero between steps.
+// The workspace: the step's work counter (zeroed by kmap_kernel before each step), the log totals and
+// the per-layer tensor maps.
 struct WorkspaceLayout {
-  size_t row_tickets, counters, row_contrib, row_lse, kmaps, total;
+  size_t counters, row_lse, kmaps, total;
 };
 
 WorkspaceLayout workspace_layout(int layers, int rows, int width) {
   (void)width;  // the share's per-layer state is per (layer, row, query row), whatever the width
   WorkspaceLayout w{};
   const size_t cells = (size_t)layers * rows * kMaxQ;
-  w.row_tickets = 0;
-  w.counters = round_up((size_t)rows * 4, 256);
-  w.row_contrib = w.counters + 256;
-  w.row_lse = w.row_contrib + round_up((size_t)rows * 4, 256);
+  (void)rows;
+  w.counters = 0;
+  w.row_lse = w.counters + 256;
   w.kmaps = w.row_lse + round_up(cells * sizeof(float2), 256);
   w.total = w.kmaps + round_up((size_t)layers * sizeof(CUtensorMap), 256);
   return w;
@@ -948,10 +917,8 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
       return fail(EKV_ERANGE, "the audit workspace holds %zu bytes, the launch needs %zu", workspace_bytes, w.total);
     if ((uintptr_t)workspace & 255) return fail(EKV_EINVAL, "the audit workspace must be 256-byte aligned");
     uint8_t* base = static_cast<uint8_t*>(workspace);
-    p.row_tickets = reinterpret_cast<uint32_t*>(base + w.row_tickets);
     p.item_counter = need_workspace ? reinterpret_cast<uint32_t*>(base + w.counters) : nullptr;
     p.row_lse = reinterpret_cast<float2*>(base + w.row_lse);
-    p.row_contrib = reinterpret_cast<int32_t*>(base + w.row_contrib);
     p.kmaps = need_workspace ? reinterpret_cast<const CUtensorMap*>(base + w.kmaps) : nullptr;
   }
   return EKV_OK;
@@ -1046,9 +1013,9 @@ extern "C" int ekv_audit_launch(
 
 namespace {
 
-// The audit step of ekv_audit_step. With clear_tickets, the workspace's row tickets are zeroed on the
+// The audit step of ekv_audit_step. With clear_counters, the workspace's work counter is zeroed on the
 // stream after every argument has been checked and before the first launch (a workspace whose last
-// user may have left them non-zero).
+// user may have left it non-zero).
 int audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table, const int32_t* lens,
                const int32_t* qrow, const uint8_t* select, const uint32_t* flag, float* lse, float scale,
                int layer0, int n_layers, int group, int rotate, int q_layout, int64_t q_stride_token,
@@ -1056,7 +1023,7 @@ int audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t
                int64_t table_stride, int layers, int rows, int width, int group_rows, int block_size,
                int tile_blocks, int head_dim, int dtype, int heads, int kv_heads, int64_t pool_blocks,
                int64_t q_tokens, float* share_out, int32_t* contributors, int aggregate, void* workspace,
-               size_t workspace_bytes, uint32_t* status, void* stream, bool clear_tickets) {
+               size_t workspace_bytes, uint32_t* status, void* stream, bool clear_counters) {
   if (!q_layers || !k_layers) return fail(EKV_EINVAL, "the per-layer address arrays must not be NULL");
   AuditParams p{};
   const int rc = prepare(p, table, lens, qrow, select, flag, lse, scale, q_stride_token, q_stride_head,
@@ -1077,11 +1044,11 @@ int audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t
   const int enc = encode_key_map(&p.kmap0, workspace, p, dtype);
   if (enc != EKV_OK) return enc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (clear_tickets) {
+  if (clear_counters) {
     const WorkspaceLayout w = workspace_layout(layers, rows, width);
-    if (cudaMemsetAsync(static_cast<uint8_t*>(workspace) + w.row_tickets, 0, w.row_lse - w.row_tickets, s) !=
+    if (cudaMemsetAsync(static_cast<uint8_t*>(workspace) + w.counters, 0, w.row_lse - w.counters, s) !=
         cudaSuccess)
-      return check_launch("cudaMemsetAsync(row tickets)");
+      return check_launch("cudaMemsetAsync(work counter)");
   }
   const int tt = block_size * tile_blocks;
   return dtype == EKV_DTYPE_BF16 ? dispatch<__nv_bfloat16>(p, tt, true, layer0, n_layers, s)
@@ -1205,7 +1172,7 @@ extern "C" int ekv_audit_step_static(
   void* scratch = nullptr;
   const int rc = static_scratch(&scratch);
   if (rc != EKV_OK) return rc;
-  // The array keeps the last call's contents: audit_step zeroes the row tickets once every argument
+  // The array keeps the last call's contents: audit_step zeroes the work counter once every argument
   // has been checked, so a refused call leaves the array as it was.
   return audit_step(q_layers, k_layers, table, lens, qrow, select, flag, lse, scale, layer0, n_layers, group,
                     rotate, q_layout, q_stride_token, q_stride_head, k_stride_block, k_stride_pos, k_stride_head,

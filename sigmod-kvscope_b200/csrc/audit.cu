@@ -719,10 +719,10 @@ __global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams 
       const float o = __shfl_xor_sync(kFullMask, v, off);
       v = agg_max ? fmaxf(v, o) : v + o;
     }
-    if (t < n_tiles && (lane % (lanes_q * slices)) < TB) {
-      const int b = t * TB + lane % (lanes_q * slices);
+    if (t < n_tiles && lane % (lanes_q * slices) == 0) {  // the tile's first lane writes its blocks
       const int in_row = min(TB, n - t * TB);  // the tile's blocks in the row
-      if (b < n) out[b] = agg_max ? v / (float)in_row : v / (float)in_row / (float)contributors;
+      const float each = agg_max ? v / (float)in_row : v / (float)in_row / (float)contributors;
+      for (int j = 0; j < in_row; ++j) out[t * TB + j] = each;
     }
   }
   for (int b = n + tid; b < p.width; b += kShareThreads) out[b] = 0.f;  // past the row

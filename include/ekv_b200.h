@@ -60,9 +60,11 @@ const char* ekv_last_error_string(void);
 int ekv_abi_version(void);
 
 /* Bytes of workspace the share pass of ekv_audit_launch / ekv_audit_step needs for a table of
- * `layers` layers and `rows` rows (the width does not change it): a log total per (layer, row, query
- * row) -- the share's normaliser -- and, for ekv_audit_step, a work counter and the key cache's TMA
- * descriptor per layer (128 bytes each), all rewritten by every step. It must be 256-byte aligned. */
+ * `layers` layers and `rows` rows (the width does not change it): a ticket and a contributor count per
+ * row, a log total per (layer, row, query row) -- the share's normaliser -- and, for ekv_audit_step, a
+ * work counter and the key cache's TMA descriptor per layer (128 bytes each), rewritten by every step.
+ * It must be zero before the first launch (every launch leaves the tickets and counts zero again) and
+ * 256-byte aligned. */
 size_t ekv_audit_workspace_bytes(int layers, int rows, int width);
 
 /*
@@ -149,8 +151,8 @@ int ekv_audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int
  * library holds until exit, and rejects with EKV_ERANGE a step whose ekv_audit_workspace_bytes()
  * exceeds it. The caller still passes every input and output. It allocates nothing: the first call on
  * a device looks the array's device address up (cudaGetSymbolAddress), so make that first call before
- * any stream capture. Every call shares the array and clears its work counter first; calls whose
- * launches overlap on the GPU race.
+ * any stream capture. Every call shares the array and clears its tickets and counters first; calls
+ * whose launches overlap on the GPU race.
  */
 size_t ekv_audit_static_scratch_bytes(void);
 int ekv_audit_step_static(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table,

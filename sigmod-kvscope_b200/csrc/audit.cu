@@ -79,8 +79,10 @@ struct AuditParams {
   int aggregate;
   uint32_t* item_counter;   // items handed out beyond each warp's first (zeroed by kmap_kernel); NULL: static order
   // the share's normaliser: each (layer, row, query row)'s log total over its tiles as (M, S), the total
-  // being S * exp(M) (S == 0: no data), made by share_kernel's first pass
+  // being S * exp(M) (S == 0: no data), made by lse_kernel after the record kernel
   float2* row_lse;          // [layers][rows][kMaxQ]
+  uint32_t* row_tickets;    // [rows] the combine's CTAs that have finished a row
+  int32_t* row_contrib;     // [rows] (layer, query row) pairs with data, summed by lse_kernel, zeroed by the combine
   uint32_t* status;
 };
 
@@ -606,86 +608,104 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
   }
 }
 
-// ---- the share kernel: one CTA per row ---------------------------------------------------------------------
+// ---- the share's normaliser: a warp per (layer, row, head) ----------------------------------------------
 //
-// Pass 1: warp w merges the (layer, head) pairs w, w + kShareWarps, ... of [layer0, layer0 + n_layers)
-// into the query rows' log totals (merge_row_lse; row_lse in the workspace). Pass 2, after a barrier: warp
-// w takes the row's tiles in groups; its lanes split (tile, layer slice, query rows): lanes_q lanes over
-// the query rows (four at a time in 16-byte loads when the cells allow, else one), `slices` slices of the
-// layers (slice k takes layers layer0 + k, + slices, ...: about four per lane, their loads in flight
-// together) and the rest over neighbouring tiles. A tile's block b (its cell is the tile's first block's)
-// gets, over the (layer, query row) pairs with data, exp(u_b) / sum_b' exp(u_b') = l exp(m - M) / S / n_t
-// (n_t the tile's blocks in the row: a partial last tile's blocks share its whole weight, the reference's
-// regain), summed over the tile's lanes by xor-shuffles (the same order on every launch) and divided by the
-// contributors (mean), or maxed and the row divided by its total (max, a fixed-order CTA sum). A row that
-// records nothing, or has no contributor, is NaN; blocks past the row are 0.
-constexpr int kShareWarps = 16;
-constexpr int kShareThreads = kShareWarps * 32;
+// Grid: kLseWarps warps per CTA over the (layer, row, head) triples of [layer0, layer0 + n_layers), in that
+// order (a CTA's warps read neighbouring rows of one layer: cells the record kernel has just written, in
+// L2). The warp also adds its query rows with data to the row's contributor count.
+constexpr int kLseWarps = 4;
 
-// query rows of one lane's load: four (a 16-byte load) when the cells allow it
-__host__ __device__ inline int share_vec(int Q) { return (Q & 3) == 0 ? 4 : 1; }
-
-__global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams p) {
-  __shared__ float s_red[kShareWarps];
-  __shared__ int s_c[kShareWarps];
-  const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+__global__ void __launch_bounds__(kLseWarps * 32) lse_kernel(const AuditParams p) {
   chain_release();
   chain_wait();  // the record kernel's cells
   if (*p.flag == 0) return;  // nothing was recorded this step
+  const int lane = threadIdx.x & 31;
+  const long long triple = (long long)blockIdx.x * kLseWarps + (threadIdx.x >> 5);
+  if (triple >= (long long)p.n_layers * p.rows * p.heads) return;
+  const int head = (int)(triple % p.heads);
+  const long long lr = triple / p.heads;
+  const int row = (int)(lr % p.rows), layer = p.layer0 + (int)(lr / p.rows);
+  const RowInfo ri = row_info(p, row, false);
+  if (ri.n_chunks == 0) return;  // the combine writes the row NaN
+  merge_row_lse(p, layer, row, head, ri.n_tiles, lane);
+  __syncwarp();
+  if (lane == 0) {  // the contributors: query rows with data
+    const float2* tot = p.row_lse + ((size_t)layer * p.rows + row) * kMaxQ + head * p.G;
+    int c = 0;
+    for (int g = 0; g < p.G; ++g) c += tot[g].y > 0.f;
+    if (c) atomicAdd(p.row_contrib + row, c);
+  }
+}
+
+// ---- the combine kernel: cells and log totals into the final share, a CTA per (row, span of tiles) ----------
+//
+// Grid (spans of the width's tiles, rows), kCombineThreads threads. A warp's lanes split (tile, layer slice,
+// query rows): share_lanes_q lanes over the query rows (four at a time in 16-byte loads when the cells
+// allow, else one), `slices` slices of the layers (slice k takes layers layer0 + k, + slices, ...: about
+// four per lane, every load of a lane in flight together) and the rest over neighbouring tiles, which the
+// CTA's warps continue (share_span tiles a CTA). A tile's block b (its cell is the tile's first block's)
+// gets, over the (layer, query row) pairs with data, exp(u_b) / sum_b' exp(u_b') = l exp(m - M) / S / n_t
+// (n_t the tile's blocks in the row: a partial last tile's blocks share its whole weight, the reference's
+// regain), summed over the tile's lanes by xor-shuffles (the same order on every launch) and divided by the
+// contributors (mean), or maxed and the row divided by its total by the CTA that finishes the row last
+// (max). A row that records nothing, or has no contributor, is NaN; blocks past the row are 0. The CTA that
+// finishes a row last zeroes its contributor count for the next step.
+constexpr int kCombineThreads = 128;
+constexpr int kCombineU = 4;  // layers of a lane whose loads are in flight together
+
+struct ShareLanes {
+  int V, lanes_q, slices, tiles_w;  // query rows per load, lanes over query rows, layer slices, tiles a warp
+};
+
+__host__ __device__ inline ShareLanes share_lanes(int Q, int n_layers) {
+  ShareLanes s{};
+  s.V = (Q & 3) == 0 ? 4 : 1;
+  s.lanes_q = 1;
+  while (s.lanes_q < Q / s.V && s.lanes_q < 32) s.lanes_q <<= 1;
+  s.slices = 1;
+  while (s.slices < 32 / s.lanes_q && s.slices * kCombineU < n_layers) s.slices <<= 1;
+  s.tiles_w = 32 / (s.lanes_q * s.slices);
+  return s;
+}
+
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditParams p) {
+  __shared__ float s_red[kCombineThreads / 32];
+  __shared__ int s_last;
+  const int r = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  chain_release();
+  chain_wait();  // the record kernel's cells, lse_kernel's log totals and contributor counts
+  if (*p.flag == 0) return;  // nothing was recorded this step
   const RowInfo ri = row_info(p, r, false);
   float* out = p.share_out + (size_t)r * p.width;
-  if (ri.n_chunks == 0) {
-    for (int b = tid; b < p.width; b += kShareThreads) out[b] = NAN;
-    if (tid == 0) p.contrib_out[r] = 0;
-    return;
-  }
-  const int TB = p.tile_blocks, Q = p.Q, n = ri.n_blocks, n_tiles = ri.n_tiles;
-  const int la = p.layer0, n_layers = p.n_layers;
-  // ---- pass 1: the log totals, and the contributors: (layer, query row) pairs with data ----------------
-  for (int j = warp; j < n_layers * p.heads; j += kShareWarps)
-    merge_row_lse(p, la + j / p.heads, r, j % p.heads, n_tiles, lane);
-  __syncthreads();  // every warp's totals, written to the workspace, are visible to the CTA
-  int c = 0;
-  for (int i = tid; i < n_layers * Q; i += kShareThreads)
-    c += __ldcg(&p.row_lse[((size_t)(la + i / Q) * p.rows + r) * kMaxQ + i % Q].y) > 0.f;
-  for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(kFullMask, c, off);
-  if (lane == 0) s_c[warp] = c;
-  __syncthreads();
-  int contributors = 0;
-  for (int w = 0; w < kShareWarps; ++w) contributors += s_c[w];
-  if (tid == 0) p.contrib_out[r] = contributors;
-  if (contributors == 0) {
-    for (int b = tid; b < p.width; b += kShareThreads) out[b] = NAN;
-    return;
-  }
-  // ---- pass 2: every tile's share ------------------------------------------------------------------
-  constexpr int U = 4;  // layers of a lane whose loads are in flight together
-  const int V = share_vec(Q);
-  int lanes_q = 1;
-  while (lanes_q < Q / V && lanes_q < 32) lanes_q <<= 1;
-  int slices = 1;  // a power of two, at most 32 / lanes_q, about U layers per lane
-  while (slices < 32 / lanes_q && slices * U < n_layers) slices <<= 1;
-  const int tiles_w = 32 / (lanes_q * slices);  // tiles of a warp per round
-  const int qg = lane % lanes_q, slice = (lane / lanes_q) % slices, tsub = lane / (lanes_q * slices);
-  const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
+  const int TB = p.tile_blocks, Q = p.Q;
+  const ShareLanes sl = share_lanes(Q, p.n_layers);
+  const int span = (kCombineThreads / 32) * sl.tiles_w;
+  const int t0 = blockIdx.x * span;
+  const int b_lo = t0 * TB, b_hi = min((t0 + span) * TB, p.width);  // this CTA's blocks
+  const int contributors = ri.n_chunks ? __ldcg(p.row_contrib + r) : 0;
+  if (blockIdx.x == 0 && tid == 0) p.contrib_out[r] = contributors;
   const bool agg_max = p.aggregate == EKV_AGG_MAX;
-  const int lb = la + n_layers;
-  for (int tb = warp * tiles_w; tb < n_tiles; tb += kShareWarps * tiles_w) {
-    const int t = tb + tsub;
+  if (contributors > 0) {
+    const int n = ri.n_blocks, n_tiles = (n + TB - 1) / TB;
+    const int group = sl.lanes_q * sl.slices;  // lanes of one tile
+    const int qg = lane % sl.lanes_q, slice = (lane / sl.lanes_q) % sl.slices;
+    const int t = t0 + warp * sl.tiles_w + lane / group;
+    const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
+    const int la = p.layer0, lb = p.layer0 + p.n_layers;
     float v = 0.f;
     if (t < n_tiles) {
       const int bt0 = t * TB;
-      for (int q = qg * V; q < Q; q += lanes_q * V) {
-        for (int L0 = la + slice; L0 < lb; L0 += U * slices) {
-          float4 m[U], l[U], zm[U], zs[U];
+      for (int q = qg * sl.V; q < Q; q += sl.lanes_q * sl.V) {
+        for (int L0 = la + slice; L0 < lb; L0 += kCombineU * sl.slices) {
+          float4 m[kCombineU], l[kCombineU], zm[kCombineU], zs[kCombineU];
 #pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int L = L0 + u * slices;
+          for (int u = 0; u < kCombineU; ++u) {
+            const int L = L0 + u * sl.slices;
             const bool ok = L < lb;
             const size_t lr = (size_t)(ok ? L : la) * p.rows + r;
             const float* cm = p.lse + (lr * p.width + (size_t)bt0) * Q + q;
             const float2* z = p.row_lse + lr * kMaxQ + q;
-            if (V == 4) {
+            if (sl.V == 4) {
               m[u] = ok ? __ldcg(reinterpret_cast<const float4*>(cm)) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
               l[u] = ok ? __ldcg(reinterpret_cast<const float4*>(cm + plane)) : make_float4(0.f, 0.f, 0.f, 0.f);
               const float4 z01 = ok ? __ldcg(reinterpret_cast<const float4*>(z)) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -701,7 +721,7 @@ __global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams 
             }
           }
 #pragma unroll
-          for (int u = 0; u < U; ++u) {
+          for (int u = 0; u < kCombineU; ++u) {
             const float mk[4] = {m[u].x, m[u].y, m[u].z, m[u].w}, lk[4] = {l[u].x, l[u].y, l[u].z, l[u].w};
             const float Mk[4] = {zm[u].x, zm[u].y, zm[u].z, zm[u].w}, Sk[4] = {zs[u].x, zs[u].y, zs[u].z, zs[u].w};
 #pragma unroll
@@ -715,26 +735,38 @@ __global__ void __launch_bounds__(kShareThreads) share_kernel(const AuditParams 
         }
       }
     }
-    for (int off = 1; off < lanes_q * slices; off <<= 1) {  // over the lanes of this tile
+    for (int off = 1; off < group; off <<= 1) {  // over the lanes of one tile
       const float o = __shfl_xor_sync(kFullMask, v, off);
       v = agg_max ? fmaxf(v, o) : v + o;
     }
-    if (t < n_tiles && lane % (lanes_q * slices) == 0) {  // the tile's first lane writes its blocks
-      const int in_row = min(TB, n - t * TB);  // the tile's blocks in the row
-      const float each = agg_max ? v / (float)in_row : v / (float)in_row / (float)contributors;
-      for (int j = 0; j < in_row; ++j) out[t * TB + j] = each;
+    if (lane % group == 0 && t < t0 + span) {  // the tile's first lane writes its blocks
+      const int bt0 = t * TB;
+      const int in_row = t < n_tiles ? min(TB, n - bt0) : 0;
+      const float each = in_row > 0 ? (agg_max ? v / (float)in_row : v / (float)in_row / (float)contributors) : 0.f;
+      for (int b = bt0; b < bt0 + TB && b < p.width; ++b) out[b] = b < n ? each : 0.f;
+    }
+  } else {
+    for (int b = b_lo + tid; b < b_hi; b += kCombineThreads) out[b] = NAN;
+  }
+  if (ri.n_chunks == 0) return;  // no contributor count to reset
+  // the CTA that finishes the row last: the row's total (max) and the count's reset
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&p.row_tickets[r], 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (agg_max && contributors > 0) {
+    const int n = ri.n_blocks;
+    float part = 0.f;
+    for (int b = tid; b < n; b += kCombineThreads) part += __ldcg(out + b);
+    const float total = block_sum_fixed_order<kCombineThreads>(part, s_red);
+    for (int b = tid; b < n; b += kCombineThreads) {
+      const float x = __ldcg(out + b);
+      out[b] = total > 0.f ? x / total : 0.f;
     }
   }
-  for (int b = n + tid; b < p.width; b += kShareThreads) out[b] = 0.f;  // past the row
-  if (!agg_max) return;
-  __syncthreads();  // every block's value of the row is written
-  float part = 0.f;
-  for (int b = tid; b < n; b += kShareThreads) part += __ldcg(out + b);
-  const float total = block_sum_fixed_order<kShareThreads>(part, s_red);
-  for (int b = tid; b < n; b += kShareThreads) {
-    const float x = __ldcg(out + b);
-    out[b] = total > 0.f ? x / total : 0.f;
-  }
+  if (tid == 0) p.row_tickets[r] = 0, p.row_contrib[r] = 0;  // ready for the next step
 }
 
 // One tensor map per layer of a step: the host-encoded template with the layer's key-cache address
@@ -802,8 +834,15 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
   AuditParams ps = p;
   ps.layer0 = share0;
   ps.n_layers = share_layers;
-  launch_chained(share_kernel, dim3(p.rows), dim3(kShareThreads), 0, stream, ps);
-  return check_launch("share_kernel");
+  const long long triples = (long long)share_layers * p.rows * p.heads;
+  launch_chained(lse_kernel, dim3((unsigned)((triples + kLseWarps - 1) / kLseWarps)), dim3(kLseWarps * 32), 0, stream,
+                 ps);
+  rc = check_launch("lse_kernel");
+  if (rc != EKV_OK) return rc;
+  const int span = (kCombineThreads / 32) * share_lanes(p.Q, share_layers).tiles_w;
+  launch_chained(combine_kernel, dim3(cdiv(cdiv(p.width, p.tile_blocks), span), p.rows), dim3(kCombineThreads), 0,
+                 stream, ps);
+  return check_launch("combine_kernel");
 }
 
 template <typename T>
@@ -821,18 +860,19 @@ int dispatch(const AuditParams& p, int tt, bool finalize, int share0, int share_
   return fail(EKV_ENOTSUP, "no audit kernel for a tile of %d tokens", tt);
 }
 
-// The workspace: the step's work counter (zeroed by kmap_kernel before each step), the log totals and
-// the per-layer tensor maps.
+// The workspace: [row_tickets, row_lse) holds the tickets, contributor counts and the work counter, zero
+// between steps; then the log totals and the per-layer tensor maps.
 struct WorkspaceLayout {
-  size_t counters, row_lse, kmaps, total;
+  size_t row_tickets, row_contrib, counters, row_lse, kmaps, total;
 };
 
 WorkspaceLayout workspace_layout(int layers, int rows, int width) {
   (void)width;  // the share's per-layer state is per (layer, row, query row), whatever the width
   WorkspaceLayout w{};
   const size_t cells = (size_t)layers * rows * kMaxQ;
-  (void)rows;
-  w.counters = 0;
+  w.row_tickets = 0;
+  w.row_contrib = round_up((size_t)rows * 4, 256);
+  w.counters = w.row_contrib + round_up((size_t)rows * 4, 256);
   w.row_lse = w.counters + 256;
   w.kmaps = w.row_lse + round_up(cells * sizeof(float2), 256);
   w.total = w.kmaps + round_up((size_t)layers * sizeof(CUtensorMap), 256);
@@ -919,6 +959,8 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
     uint8_t* base = static_cast<uint8_t*>(workspace);
     p.item_counter = need_workspace ? reinterpret_cast<uint32_t*>(base + w.counters) : nullptr;
     p.row_lse = reinterpret_cast<float2*>(base + w.row_lse);
+    p.row_tickets = reinterpret_cast<uint32_t*>(base + w.row_tickets);
+    p.row_contrib = reinterpret_cast<int32_t*>(base + w.row_contrib);
     p.kmaps = need_workspace ? reinterpret_cast<const CUtensorMap*>(base + w.kmaps) : nullptr;
   }
   return EKV_OK;
@@ -1013,9 +1055,9 @@ extern "C" int ekv_audit_launch(
 
 namespace {
 
-// The audit step of ekv_audit_step. With clear_counters, the workspace's work counter is zeroed on the
+// The audit step of ekv_audit_step. With clear_counters, the workspace's tickets and counters are zeroed on the
 // stream after every argument has been checked and before the first launch (a workspace whose last
-// user may have left it non-zero).
+// user may have left them non-zero).
 int audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table, const int32_t* lens,
                const int32_t* qrow, const uint8_t* select, const uint32_t* flag, float* lse, float scale,
                int layer0, int n_layers, int group, int rotate, int q_layout, int64_t q_stride_token,
@@ -1046,9 +1088,9 @@ int audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (clear_counters) {
     const WorkspaceLayout w = workspace_layout(layers, rows, width);
-    if (cudaMemsetAsync(static_cast<uint8_t*>(workspace) + w.counters, 0, w.row_lse - w.counters, s) !=
+    if (cudaMemsetAsync(static_cast<uint8_t*>(workspace) + w.row_tickets, 0, w.row_lse - w.row_tickets, s) !=
         cudaSuccess)
-      return check_launch("cudaMemsetAsync(work counter)");
+      return check_launch("cudaMemsetAsync(tickets and counters)");
   }
   const int tt = block_size * tile_blocks;
   return dtype == EKV_DTYPE_BF16 ? dispatch<__nv_bfloat16>(p, tt, true, layer0, n_layers, s)
@@ -1172,7 +1214,7 @@ extern "C" int ekv_audit_step_static(
   void* scratch = nullptr;
   const int rc = static_scratch(&scratch);
   if (rc != EKV_OK) return rc;
-  // The array keeps the last call's contents: audit_step zeroes the work counter once every argument
+  // The array keeps the last call's contents: audit_step zeroes its tickets and counters once every argument
   // has been checked, so a refused call leaves the array as it was.
   return audit_step(q_layers, k_layers, table, lens, qrow, select, flag, lse, scale, layer0, n_layers, group,
                     rotate, q_layout, q_stride_token, q_stride_head, k_stride_block, k_stride_pos, k_stride_head,

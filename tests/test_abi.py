@@ -49,14 +49,14 @@ def test_constants_agree_with_the_header():
 
 
 def test_workspace_size(lib):
-    # the step's item counter + a log total (two float32) per (layer, row, query row: up to 128) + a
-    # 128-byte key-cache descriptor per layer
+    # row tickets [rows] + contributors [rows] + the step's item counter + a log total (two float32) per
+    # (layer, row, query row: up to 128) + a 128-byte key-cache descriptor per layer
     layers, rows, width = 32, 64, 512
 
     def up(x):
         return -(-x // 256) * 256
 
-    want = 256 + up(layers * rows * 128 * 8) + up(layers * 128)
+    want = up(rows * 4) + up(rows * 4) + 256 + up(layers * rows * 128 * 8) + up(layers * 128)
     assert lib.ekv_audit_workspace_bytes(layers, rows, width) == want
     assert lib.ekv_audit_workspace_bytes(layers, rows, 4 * width) == want  # the width does not change it
     assert lib.ekv_audit_workspace_bytes(0, rows, width) == 0

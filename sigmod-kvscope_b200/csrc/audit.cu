@@ -617,15 +617,16 @@ constexpr int kLseWarps = 4;
 
 __global__ void __launch_bounds__(kLseWarps * 32) lse_kernel(const AuditParams p) {
   chain_release();
-  chain_wait();  // the record kernel's cells
-  if (*p.flag == 0) return;  // nothing was recorded this step
   const int lane = threadIdx.x & 31;
   const long long triple = (long long)blockIdx.x * kLseWarps + (threadIdx.x >> 5);
-  if (triple >= (long long)p.n_layers * p.rows * p.heads) return;
+  const bool in_grid = triple < (long long)p.n_layers * p.rows * p.heads;
   const int head = (int)(triple % p.heads);
   const long long lr = triple / p.heads;
-  const int row = (int)(lr % p.rows), layer = p.layer0 + (int)(lr / p.rows);
+  const int row = in_grid ? (int)(lr % p.rows) : 0, layer = p.layer0 + (int)(lr / p.rows);
+  // the row's length and selection are the step's inputs, not the record kernel's: read while it ends
   const RowInfo ri = row_info(p, row, false);
+  chain_wait();  // the record kernel's cells
+  if (!in_grid || *p.flag == 0) return;  // nothing was recorded this step
   if (ri.n_chunks == 0) return;  // the combine writes the row NaN
   merge_row_lse(p, layer, row, head, ri.n_tiles, lane);
   __syncwarp();
@@ -673,16 +674,18 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditPar
   __shared__ int s_last;
   const int r = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   chain_release();
+  // the row's length and selection are the step's inputs, not the kernels' before: read while they end
+  const RowInfo ri = row_info(p, r, false);
   chain_wait();  // the record kernel's cells, lse_kernel's log totals and contributor counts
   if (*p.flag == 0) return;  // nothing was recorded this step
-  const RowInfo ri = row_info(p, r, false);
   float* out = p.share_out + (size_t)r * p.width;
   const int TB = p.tile_blocks, Q = p.Q;
   const ShareLanes sl = share_lanes(Q, p.n_layers);
   const int span = (kCombineThreads / 32) * sl.tiles_w;
   const int t0 = blockIdx.x * span;
   const int b_lo = t0 * TB, b_hi = min((t0 + span) * TB, p.width);  // this CTA's blocks
-  const int contributors = ri.n_chunks ? __ldcg(p.row_contrib + r) : 0;
+  const int counted = __ldcg(p.row_contrib + r);  // (its load in flight with the cells' below)
+  const int contributors = ri.n_chunks ? counted : 0;
   if (blockIdx.x == 0 && tid == 0) p.contrib_out[r] = contributors;
   const bool agg_max = p.aggregate == EKV_AGG_MAX;
   if (contributors > 0) {

@@ -414,16 +414,23 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
   // (address arithmetic only: without a view, laid is 0 and the table is never read)
   const int32_t* trow = reinterpret_cast<const int32_t*>(reinterpret_cast<uintptr_t>(p.table) +
                                                          (uintptr_t)((int64_t)r * p.table_s0 * 4));
-  stage_words(reinterpret_cast<uint32_t*>(trow_s), reinterpret_cast<const uint32_t*>(trow), laid);
-  cp_async_commit();
+  if (!by_threshold) {  // (with a ranking, the staging buffer first holds the select's candidates)
+    stage_words(reinterpret_cast<uint32_t*>(trow_s), reinterpret_cast<const uint32_t*>(trow), laid);
+    cp_async_commit();
+  }
 
   K prefix = 0, pmask = 0;
   int k_eq = 0, eq_total = 0;
   if (by_threshold) {
-    cp_async_wait<1>();  // the scores have landed (the table may still be in flight)
+    reinterpret_cast<int4*>(s_hist)[threadIdx.x] = make_int4(0, 0, 0, 0);  // (ordered by the barrier below)
+    cp_async_wait<0>();  // the scores have landed
     __syncthreads();
-    // keys are handled four at a time; position 0 and positions from ps on are not keys
+    // The keys, and the first digit's histogram as they are written. Positions 0 and from ps on are not
+    // keys; they are handled four at a time.
     const int groups = (ps + 3) >> 2;
+    int shift0;
+    K dmask0;
+    ViewKey<K>::digit(0, shift0, dmask0);
     if constexpr (kWide) {
       const double* s_x = reinterpret_cast<const double*>(keys);
       PairwiseTree& tree = *reinterpret_cast<PairwiseTree*>(smem_view + (size_t)w_pad * (sizeof(K) + 4));
@@ -432,8 +439,11 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
         return s > 0.0 ? s : 0.0;
       });
       const double w = p.weights != nullptr ? p.weights[r] : 1.0;
-      for (int b = threadIdx.x; b < 4 * groups; b += kViewThreads)  // in place: each thread its own positions
-        keys[b] = b < ps ? share_key64(s_x[b], total, w, n_a) : 0ull;
+      for (int b = threadIdx.x; b < 4 * groups; b += kViewThreads) {  // in place: each thread its own positions
+        const K key = b < ps ? share_key64(s_x[b], total, w, n_a) : 0ull;
+        keys[b] = key;
+        if (b >= 1 && b < ps) atomicAdd(&s_hist[(int)((key >> shift0) & dmask0)], 1);
+      }
     } else {
       uint4* keys4 = reinterpret_cast<uint4*>(keys);
       for (int g = threadIdx.x; g < groups; g += kViewThreads) {
@@ -441,24 +451,55 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
         v.x = share_key(__uint_as_float(v.x)), v.y = share_key(__uint_as_float(v.y));
         v.z = share_key(__uint_as_float(v.z)), v.w = share_key(__uint_as_float(v.w));
         keys4[g] = v;
+        const uint32_t kv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (4 * g + j >= 1 && 4 * g + j < ps) atomicAdd(&s_hist[(int)((kv[j] >> shift0) & dmask0)], 1);
       }
     }
-    reinterpret_cast<int4*>(s_hist)[threadIdx.x] = make_int4(0, 0, 0, 0);
-    __syncthreads();
     int k = q;
+    // After the first digit only the keys of its chosen bin matter: they are gathered into a candidate list
+    // (in the table's staging buffer, whose copy starts after the select) when it holds them, and the later
+    // digits are counted over the list alone.
+    K* cand = reinterpret_cast<K*>(trow_s);
+    const int cand_cap = (int)((size_t)w_pad * 4 / sizeof(K));
+    __shared__ int s_ncand;
+    bool listed = false;
 #pragma unroll 1
     for (int pass = 0; pass < ViewKey<K>::kPasses; ++pass) {
       int shift;
       K dmask;
       ViewKey<K>::digit(pass, shift, dmask);
-      for (int g = threadIdx.x; g < groups; g += kViewThreads) {
-        K kv[4];
-        ViewKey<K>::load4(keys, g, kv);
+      if (pass > 0 && !listed && eq_total <= cand_cap) {
+        if (threadIdx.x == 0) s_ncand = 0;
+        __syncthreads();
+        for (int g = threadIdx.x; g < groups; g += kViewThreads) {
+          K kv[4];
+          ViewKey<K>::load4(keys, g, kv);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int b = 4 * g + j;
-          const bool in = b >= 1 && b < ps && (kv[j] & pmask) == prefix;
-          if (in) atomicAdd(&s_hist[(int)((kv[j] >> shift) & dmask)], 1);
+          for (int j = 0; j < 4; ++j) {
+            const int b = 4 * g + j;
+            if (b >= 1 && b < ps && (kv[j] & pmask) == prefix) cand[atomicAdd(&s_ncand, 1)] = kv[j];
+          }
+        }
+        __syncthreads();
+        listed = true;
+      }
+      if (listed) {
+        for (int i = threadIdx.x; i < s_ncand; i += kViewThreads) {
+          const K key = cand[i];
+          if ((key & pmask) == prefix) atomicAdd(&s_hist[(int)((key >> shift) & dmask)], 1);
+        }
+      } else if (pass > 0) {
+        for (int g = threadIdx.x; g < groups; g += kViewThreads) {
+          K kv[4];
+          ViewKey<K>::load4(keys, g, kv);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int b = 4 * g + j;
+            const bool in = b >= 1 && b < ps && (kv[j] & pmask) == prefix;
+            if (in) atomicAdd(&s_hist[(int)((kv[j] >> shift) & dmask)], 1);
+          }
         }
       }
       __syncthreads();
@@ -497,6 +538,9 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
       if (eq_total == k) break;  // all of them are kept: the prefix is the threshold
     }
     k_eq = k;
+    __syncthreads();  // the candidate list is read no more: the table row may land in its place
+    stage_words(reinterpret_cast<uint32_t*>(trow_s), reinterpret_cast<const uint32_t*>(trow), laid);
+    cp_async_commit();
   }
   const bool ties = eq_total != k_eq;  // only then do keys equal to the threshold need their rank
   const bool older_first = p.policy == EKV_POLICY_UNIFORM;

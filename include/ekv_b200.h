@@ -59,12 +59,10 @@ const char* ekv_last_error_string(void);
 /* ABI version of this library: bumped on any change of a signature or of a documented contract. */
 int ekv_abi_version(void);
 
-/* Bytes of workspace the share pass of ekv_audit_launch / ekv_audit_step needs for a table of
- * `layers` layers and `rows` rows (the width does not change it): a ticket and a contributor count per
- * row, a log total per (layer, row, query row) -- the share's normaliser -- and, for ekv_audit_step, a
- * work counter and the key cache's TMA descriptor per layer (128 bytes each), rewritten by every step.
- * It must be zero before the first launch (every launch leaves the tickets and counts zero again) and
- * 256-byte aligned. */
+/* Bytes of workspace ekv_audit_step needs for a table of `layers` layers (rows and width do not change
+ * it): the step's work counter and the key cache's TMA descriptor per layer (128 bytes each), both
+ * rewritten by every step, so its contents never matter; 256-byte aligned. ekv_audit_launch needs
+ * none: its workspace arguments may be NULL and 0 (a workspace given is not used). */
 size_t ekv_audit_workspace_bytes(int layers, int rows, int width);
 
 /*
@@ -84,12 +82,12 @@ size_t ekv_audit_workspace_bytes(int layers, int rows, int width);
  * reference's sampling (one KV group per layer, group = layer % kv_heads, :250).
  *
  * With share_out != NULL and EKV_SHARE_FINALIZE (the step's last layer) the same call then turns
- * the cells of every layer [0, layers) into the exact per-block attention share: a kernel with one
- * warp per (layer, row) reads the cells back from L2 and forms the block shares as
+ * the cells of every layer [0, layers) into the exact per-block attention share: one kernel, a
+ * cluster of CTAs per row, reads the cells back from L2 and forms the block shares as
  * normalize_tile_lse computes them (observe/tile_shares.py:58-103 with row_blocks =
- * ceil(lens/block_size)), then a combine kernel takes the mean or max over layers and query rows
- * into share_out [rows][width] and contributors [rows] (query rows with data); a row that is not
- * selected or has no data is NaN.
+ * ceil(lens/block_size)), taking the mean or max over layers and query rows, into share_out
+ * [rows][width] and contributors [rows] ((layer, query row) pairs with data); a row that is not
+ * selected or has no data is NaN. The share pass handles rows of up to 32768 tiles.
  * status (optional) receives EKV_STATUS_* bits. q_tokens bounds qrow. Supported: head_dim 128,
  * block_size a multiple of 8 (the key cache is read a block at a time through a TMA tensor map),
  * block_size*tile_blocks in {16, 32, 64}, tile_blocks <= 8, heads*group_rows <= 128,
@@ -126,7 +124,8 @@ int ekv_audit_stash(const void* q, int64_t q_stride_token, int64_t q_stride_head
  * (KV head) * group_rows + g) or as a stash (q_layout 1: query head h * group_rows + g). The KV head
  * of layer L is (group + L) % kv_heads with rotate != 0 (the reference's sampling), else
  * group + h for h < heads. The workspace is required: it holds each layer's key-cache descriptor
- * (built on the device from k_layers by a small kernel ahead of the record kernel). share_out and
+ * (built on the device from k_layers by a small kernel ahead of the record kernel) and the work
+ * counter of the record kernel's dynamic items. share_out and
  * contributors are optional: without them only the cells are recorded.
  */
 int ekv_audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table,
@@ -147,12 +146,13 @@ int ekv_audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int
  * when they record -- a binding with no CUDA allocator of its own (a cgo or ctypes caller that only
  * holds the engine's tensors), or engine code after memory profiling has sized the KV-cache pool,
  * where one more allocation can fail or fragment it. This entry point takes no workspace: it uses a
- * static device array of ekv_audit_static_scratch_bytes() bytes (16 MiB) that every GPU loading the
- * library holds until exit, and rejects with EKV_ERANGE a step whose ekv_audit_workspace_bytes()
- * exceeds it. The caller still passes every input and output. It allocates nothing: the first call on
- * a device looks the array's device address up (cudaGetSymbolAddress), so make that first call before
- * any stream capture. Every call shares the array and clears its tickets and counters first; calls
- * whose launches overlap on the GPU race.
+ * static device array of ekv_audit_static_scratch_bytes() bytes (128.25 KiB: the workspace of a step
+ * of 1024 layers, the most this build accepts) that every GPU loading the library holds until exit,
+ * and rejects with EKV_ERANGE a step whose ekv_audit_workspace_bytes() exceeds it. The caller still
+ * passes every input and output. It allocates nothing: the first call on a device looks the array's
+ * device address up (cudaGetSymbolAddress), so make that first call before any stream capture. Every
+ * call shares the array (each step rewrites all of it that it reads); calls whose launches overlap on
+ * the GPU race.
  */
 size_t ekv_audit_static_scratch_bytes(void);
 int ekv_audit_step_static(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table,

@@ -18,18 +18,21 @@
 // C fragment's rows and query rows on its columns, so the tile max and sum are three xor-shuffles
 // per column: tile_lse_kernel's computation (runtime/audit_kernel.py:70-96), stored as at :97-109.
 //
-// Shares. After the record kernel, the share kernel gives each (layer, row) one warp, which reads the
-// row's cells back from L2 (eight tiles' loads in flight per lane): u = m + log(l) - log(tile_blocks)
-// per tile (observe/tile_shares.py:172-173), the row's log total per query row, and every block's
-// share with the partial tail tile's weight given back to its blocks (:82-103). The combine kernel
-// then sums or maxes the layers in layer order into the row's final share, a thread per block. Every
-// sum has a fixed order, so the output is deterministic.
+// Shares. After the record kernel, one share kernel reads the cells back from L2, a CTA per (row, group
+// of layers): u = m + log(l) - log(tile_blocks) per tile (observe/tile_shares.py:172-173), each query
+// row's log total, and every tile's share from the same cells still in registers; the CTA that finishes
+// a row last adds the groups and gives the partial tail tile's weight back to its blocks (:82-103).
+// Every sum has a fixed order, so the output is deterministic.
+#include <cooperative_groups.h>
+#include <type_traits>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include "ekv_common.cuh"
 
 namespace ekv {
+
+namespace cg = cooperative_groups;
 
 // Warps per CTA of the record kernel and ring stages per warp (tiles of 32 tokens; tiles of 16 hold
 // twice as many, tiles of 64 half as many). Overridable at build time for tuning sweeps.
@@ -78,11 +81,9 @@ struct AuditParams {
   int32_t* contrib_out;
   int aggregate;
   uint32_t* item_counter;   // items handed out beyond each warp's first (zeroed by kmap_kernel); NULL: static order
-  // the share's normaliser: each (layer, row, query row)'s log total over its tiles as (M, S), the total
-  // being S * exp(M) (S == 0: no data), made by lse_kernel after the record kernel
-  float2* row_lse;          // [layers][rows][kMaxQ]
-  uint32_t* row_tickets;    // [rows] the combine's CTAs that have finished a row
-  int32_t* row_contrib;     // [rows] (layer, query row) pairs with data, summed by lse_kernel, zeroed by the combine
+  // the share pass (set on the host): query rows per load (4 or 1), units per layer (Q / V), layers per group,
+  // groups, tiles of the width each CTA of a row's cluster writes, log2 of tile_blocks
+  int share_V, share_QG, share_Lg, share_groups, share_slice, tb_shift;
   uint32_t* status;
 };
 
@@ -159,70 +160,6 @@ struct Cursor {
   int layer, head, row, t0, t, t_end;
 };
 
-// The log total of each query row of (layer, row, head) over the row's n_tiles tiles, from the cells the
-// record kernel wrote (tile t's cell is its first block's): lane l merges tiles l, l + 32, ... in order,
-// then the lanes merge by xor-shuffles, the same order on every launch. A tile without data (m = -inf
-// or l = 0) adds nothing. Four query rows at a time, every cell load of a round issued before any is
-// merged. One warp.
-__device__ __forceinline__ void merge_row_lse(const AuditParams& p, int layer, int row, int head, int n_tiles, int lane) {
-  const size_t plane = (size_t)p.layers * p.rows * p.width * p.Q;
-  const size_t lr = (size_t)layer * p.rows + row;
-  const float* cm = p.lse + lr * p.width * p.Q + head * p.G;
-  const float* cl = cm + plane;
-  const int stride = p.tile_blocks * p.Q;  // floats from one tile's cell to the next tile's
-  float2* out = p.row_lse + lr * kMaxQ + head * p.G;
-  // four query rows in one 16-byte load when the cells allow it (G and Q multiples of 4)
-  const bool vec = (p.G & 3) == 0 && (p.Q & 3) == 0 && (reinterpret_cast<uintptr_t>(p.lse) & 15) == 0;
-  constexpr int kTiles = 8;  // tiles of a lane per round, every load of a round in flight together
-  for (int g0 = 0; g0 < p.G; g0 += 4) {
-    const int ng = p.G - g0 < 4 ? p.G - g0 : 4;
-    float M[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, S[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int t0 = lane; t0 < n_tiles; t0 += 32 * kTiles) {
-      float4 mv[kTiles], lv[kTiles];
-#pragma unroll
-      for (int u = 0; u < kTiles; ++u) {
-        const int t = t0 + 32 * u;
-        const bool ok = t < n_tiles;
-        const size_t at = (size_t)(ok ? t : 0) * stride + g0;
-        if (vec) {
-          mv[u] = ok ? __ldcg(reinterpret_cast<const float4*>(cm + at)) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-          lv[u] = ok ? __ldcg(reinterpret_cast<const float4*>(cl + at)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        } else {
-          mv[u].x = ok ? __ldcg(cm + at) : -INFINITY;
-          mv[u].y = ok && ng > 1 ? __ldcg(cm + at + 1) : -INFINITY;
-          mv[u].z = ok && ng > 2 ? __ldcg(cm + at + 2) : -INFINITY;
-          mv[u].w = ok && ng > 3 ? __ldcg(cm + at + 3) : -INFINITY;
-          lv[u].x = ok ? __ldcg(cl + at) : 0.f;
-          lv[u].y = ok && ng > 1 ? __ldcg(cl + at + 1) : 0.f;
-          lv[u].z = ok && ng > 2 ? __ldcg(cl + at + 2) : 0.f;
-          lv[u].w = ok && ng > 3 ? __ldcg(cl + at + 3) : 0.f;
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kTiles; ++u) {
-        const float mk[4] = {mv[u].x, mv[u].y, mv[u].z, mv[u].w}, lk[4] = {lv[u].x, lv[u].y, lv[u].z, lv[u].w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          if (mk[k] > -INFINITY && lk[k] > 0.f) lse_merge(M[k], S[k], mk[k], lk[k]);
-      }
-    }
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float m2 = __shfl_xor_sync(kFullMask, M[k], off), s2 = __shfl_xor_sync(kFullMask, S[k], off);
-        lse_merge(M[k], S[k], m2, s2);
-      }
-    if (lane < ng) {
-      float m = M[0], sv = S[0];
-#pragma unroll
-      for (int k = 1; k < 4; ++k)
-        if (lane == k) m = M[k], sv = S[k];
-      out[g0 + lane] = make_float2(m, m > -INFINITY ? sv : 0.f);
-    }
-  }
-}
-
 template <int TT, int NT, int D, typename T>
 __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __grid_constant__ AuditParams p) {
   using Lay = Layout<D>;
@@ -247,7 +184,10 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
   __shared__ long long s_queue[kWarps][kItemQueue];  // each warp's items in the order it took them
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  chain_wait();  // the query stash, the tensor maps and the item counter come from the launches before
+  // The share kernel may take the SMs this grid leaves as it ends (it waits for the cells itself). The
+  // flag and the rows' lengths, selection and query rows are the step's inputs, written before its chain
+  // of launches, so the rows are set up while the launches before this one end.
+  chain_release();
   if (*p.flag == 0) return;  // the statistic is off: nothing is recorded (:64)
 
   // ---- the rows of the step and the items: chunks per row, prefix-summed in shared memory --------
@@ -270,6 +210,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
     if (threadIdx.x == 0) prefix[p.rows] = carry;
     __syncthreads();
   }
+  chain_wait();  // the query stash, the tensor maps and the item counter come from the launches before
   const int chunks_per_lh = prefix[p.rows];
   const long long total_items = (long long)chunks_per_lh * p.heads * p.n_layers;
   const long long workers = (long long)gridDim.x * kWarps;
@@ -608,168 +549,419 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) record_kernel(const __g
   }
 }
 
-// ---- the share's normaliser: a warp per (layer, row, head) ----------------------------------------------
+// ---- the share pass: a cluster of CTAs per row, each CTA some groups of layers ---------------------------
 //
-// Grid: kLseWarps warps per CTA over the (layer, row, head) triples of [layer0, layer0 + n_layers), in that
-// order (a CTA's warps read neighbouring rows of one layer: cells the record kernel has just written, in
-// L2). The warp also adds its query rows with data to the row's contributor count.
-constexpr int kLseWarps = 4;
-
-__global__ void __launch_bounds__(kLseWarps * 32) lse_kernel(const AuditParams p) {
-  chain_release();
-  const int lane = threadIdx.x & 31;
-  const long long triple = (long long)blockIdx.x * kLseWarps + (threadIdx.x >> 5);
-  const bool in_grid = triple < (long long)p.n_layers * p.rows * p.heads;
-  const int head = (int)(triple % p.heads);
-  const long long lr = triple / p.heads;
-  const int row = in_grid ? (int)(lr % p.rows) : 0, layer = p.layer0 + (int)(lr / p.rows);
-  // the row's length and selection are the step's inputs, not the record kernel's: read while it ends
-  const RowInfo ri = row_info(p, row, false);
-  chain_wait();  // the record kernel's cells
-  if (!in_grid || *p.flag == 0) return;  // nothing was recorded this step
-  if (ri.n_chunks == 0) return;  // the combine writes the row NaN
-  merge_row_lse(p, layer, row, head, ri.n_tiles, lane);
-  __syncwarp();
-  if (lane == 0) {  // the contributors: query rows with data
-    const float2* tot = p.row_lse + ((size_t)layer * p.rows + row) * kMaxQ + head * p.G;
-    int c = 0;
-    for (int g = 0; g < p.G; ++g) c += tot[g].y > 0.f;
-    if (c) atomicAdd(p.row_contrib + row, c);
-  }
-}
-
-// ---- the combine kernel: cells and log totals into the final share, a CTA per (row, span of tiles) ----------
-//
-// Grid (spans of the width's tiles, rows), kCombineThreads threads. A warp's lanes split (tile, layer slice,
-// query rows): share_lanes_q lanes over the query rows (four at a time in 16-byte loads when the cells
-// allow, else one), `slices` slices of the layers (slice k takes layers layer0 + k, + slices, ...: about
-// four per lane, every load of a lane in flight together) and the rest over neighbouring tiles, which the
-// CTA's warps continue (share_span tiles a CTA). A tile's block b (its cell is the tile's first block's)
-// gets, over the (layer, query row) pairs with data, exp(u_b) / sum_b' exp(u_b') = l exp(m - M) / S / n_t
+// A unit is (layer, V query rows): V = 4 when the cells allow 16-byte loads, else 1. A group is Lg layers of
+// one row, Lg * Q / V units, about four, spread over the CTA's warps; the row's C CTAs (a cluster) take groups
+// rank, rank + C, ... For a unit a warp reads the tiles' cells (lane l: tiles l, l + 32, ...), takes each query
+// row's largest m among its cells with data (l > 0, m > -inf), each cell's weight w = l exp(m - M), their sum
+// S (xor-shuffles: the same order on every launch), and gives every tile its share over the unit's query rows
+// with data, w / S = exp(u_b) / sum_b' exp(u_b') with u = m + log(l) - log(tile_blocks) (summed, or maxed for
+// the max aggregate). A row of at most kShareBatch tiles keeps a unit's cells in registers throughout and a
+// warp adds all its units' shares before the CTA adds its warps; a longer row is read twice per unit, a batch
+// of tiles at a time (a running maximum and a rescaled sum first, then the shares). The C CTAs of the row then read each other's per-tile sums (distributed shared
+// memory, in rank order) and each writes a slice of the row: each block of tile t gets the tile's sum / n_t
 // (n_t the tile's blocks in the row: a partial last tile's blocks share its whole weight, the reference's
-// regain), summed over the tile's lanes by xor-shuffles (the same order on every launch) and divided by the
-// contributors (mean), or maxed and the row divided by its total by the CTA that finishes the row last
-// (max). A row that records nothing, or has no contributor, is NaN; blocks past the row are 0. The CTA that
-// finishes a row last zeroes its contributor count for the next step.
-constexpr int kCombineThreads = 128;
-constexpr int kCombineU = 4;  // layers of a lane whose loads are in flight together
+// regain) divided by the contributors, the (layer, query row) pairs with data (mean), or the row divided by its
+// total (max). A row that records nothing, or has no contributor, is NaN; blocks past the row are 0.
+constexpr int kShareMaxWarps = 16;
+constexpr int kShareRegTiles = 8;  // tiles a lane holds at once
+constexpr int kShareBatch = 32 * kShareRegTiles;
+constexpr int kShareMaxCluster = 8;   // the portable cluster size
+constexpr int kShareMaxTiles = 32768;  // a row's partials in shared memory (128 KB)
 
-struct ShareLanes {
-  int V, lanes_q, slices, tiles_w;  // query rows per load, lanes over query rows, layer slices, tiles a warp
+struct ShareShape {
+  int V, QG, Lg, groups, warps, cluster;  // query rows per load, units per layer, layers per group, groups,
+                                          // warps per CTA, CTAs per row
 };
 
-__host__ __device__ inline ShareLanes share_lanes(int Q, int n_layers) {
-  ShareLanes s{};
-  s.V = (Q & 3) == 0 ? 4 : 1;
-  s.lanes_q = 1;
-  while (s.lanes_q < Q / s.V && s.lanes_q < 32) s.lanes_q <<= 1;
-  s.slices = 1;
-  while (s.slices < 32 / s.lanes_q && s.slices * kCombineU < n_layers) s.slices <<= 1;
-  s.tiles_w = 32 / (s.lanes_q * s.slices);
+// lse_aligned: the cell table starts on a 16-byte boundary.
+inline ShareShape share_shape(int Q, int n_layers, bool lse_aligned) {
+  ShareShape s{};
+  s.V = (Q & 3) == 0 && lse_aligned ? 4 : 1;
+  s.QG = Q / s.V;
+  s.Lg = s.QG >= 4 ? 1 : 4 / s.QG;  // about four units a group, one per warp, or more warps for wide cells
+  if (s.Lg > n_layers) s.Lg = n_layers;
+  s.groups = (n_layers + s.Lg - 1) / s.Lg;
+  const int units = s.Lg * s.QG;
+  s.warps = units < kShareMaxWarps ? units : kShareMaxWarps;
+  s.cluster = s.groups < kShareMaxCluster ? s.groups : kShareMaxCluster;
   return s;
 }
 
-__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const AuditParams p) {
-  __shared__ float s_red[kCombineThreads / 32];
-  __shared__ int s_last;
-  const int r = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+// The cells of the warp's tiles t0 + lane + 32 i, i < SL, V query rows each. A cell without data (l = 0,
+// m = -inf or NaN) is marked m = -inf, l = 0; so is a tile past the row.
+template <int V, int SL>
+__device__ __forceinline__ void load_unit_tiles(const float* cm, const float* cl, int tile_stride, int t0, int n_tiles,
+                                                int lane, float (&m)[SL][V], float (&l)[SL][V]) {
+#pragma unroll
+  for (int i = 0; i < SL; ++i) {
+    const int t = t0 + lane + 32 * i;
+    const bool ok = t < n_tiles;
+    const size_t at = (size_t)(ok ? t : 0) * tile_stride;
+    if constexpr (V == 4) {
+      const float4 a = ok ? __ldcg(reinterpret_cast<const float4*>(cm + at)) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      const float4 b = ok ? __ldcg(reinterpret_cast<const float4*>(cl + at)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      m[i][0] = a.x, m[i][1] = a.y, m[i][2] = a.z, m[i][3] = a.w;
+      l[i][0] = b.x, l[i][1] = b.y, l[i][2] = b.z, l[i][3] = b.w;
+    } else {
+      m[i][0] = ok ? __ldcg(cm + at) : -INFINITY;
+      l[i][0] = ok ? __ldcg(cl + at) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const bool data = l[i][k] > 0.f && m[i][k] > -INFINITY;
+      m[i][k] = data ? m[i][k] : -INFINITY;
+      l[i][k] = data ? l[i][k] : 0.f;
+    }
+  }
+}
+
+// The largest m over the lane's tiles.
+template <int V, int SL>
+__device__ __forceinline__ void unit_max(float (&M)[V], const float (&m)[SL][V]) {
+#pragma unroll
+  for (int i = 0; i < SL; ++i)
+#pragma unroll
+    for (int k = 0; k < V; ++k) M[k] = fmaxf(M[k], m[i][k]);
+}
+
+// Each cell's weight w = l exp(m - M) (0 without data), written over l, and its sum into S.
+template <int V, int SL>
+__device__ __forceinline__ void unit_weights(float (&S)[V], const float (&M)[V], const float (&m)[SL][V],
+                                             float (&l)[SL][V]) {
+#pragma unroll
+  for (int i = 0; i < SL; ++i)
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float w = m[i][k] > -INFINITY ? l[i][k] * __expf(m[i][k] - M[k]) : 0.f;
+      l[i][k] = w;
+      S[k] += w;
+    }
+}
+
+template <int V>
+__device__ __forceinline__ void lanes_max(float (&x)[V]) {
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1)
+#pragma unroll
+    for (int k = 0; k < V; ++k) x[k] = fmaxf(x[k], __shfl_xor_sync(kFullMask, x[k], off));
+}
+
+template <int V>
+__device__ __forceinline__ void lanes_sum(float (&x)[V]) {
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1)
+#pragma unroll
+    for (int k = 0; k < V; ++k) x[k] += __shfl_xor_sync(kFullMask, x[k], off);
+}
+
+// acc[i] gets tile i's share over the query rows, w * inv (summed, or maxed).
+template <int V, int SL>
+__device__ __forceinline__ void add_unit_shares(float (&acc)[kShareRegTiles], const float (&w)[SL][V],
+                                                const float (&inv)[V], bool agg_max) {
+#pragma unroll
+  for (int i = 0; i < SL; ++i)
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float sh = w[i][k] * inv[k];
+      acc[i] = agg_max ? fmaxf(acc[i], sh) : acc[i] + sh;
+    }
+}
+
+// The reciprocal of each query row's total weight (0 without data); the query rows with data.
+template <int V>
+__device__ __forceinline__ int unit_inverse(float (&inv)[V], const float (&S)[V]) {
+  int cnt = 0;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    inv[k] = S[k] > 0.f ? __frcp_rn(S[k]) : 0.f;
+    cnt += S[k] > 0.f;
+  }
+  return cnt;
+}
+
+// A unit of a row of at most 32 * SL tiles, every cell in registers: the maximum, the weights and their sum,
+// the shares added into acc; the query rows with data.
+template <int V, int SL>
+__device__ __forceinline__ int unit_in_registers(float (&acc)[kShareRegTiles], const float* cm, const float* cl,
+                                                 int tile_stride, int n_tiles, int lane, bool agg_max) {
+  float m[SL][V], l[SL][V], M[V], S[V], inv[V];
+  load_unit_tiles<V, SL>(cm, cl, tile_stride, 0, n_tiles, lane, m, l);
+#pragma unroll
+  for (int k = 0; k < V; ++k) M[k] = -INFINITY, S[k] = 0.f;
+  unit_max<V, SL>(M, m);
+  lanes_max<V>(M);
+  unit_weights<V, SL>(S, M, m, l);
+  lanes_sum<V>(S);
+  const int cnt = unit_inverse<V>(inv, S);
+  add_unit_shares<V, SL>(acc, l, inv, agg_max);
+  return cnt;
+}
+
+template <int V>
+__global__ void __launch_bounds__(kShareMaxWarps * 32) share_kernel(const AuditParams p) {
+  extern __shared__ float s_part[];  // [tiles of the width]: this CTA's groups' partial per tile
+  __shared__ float s_acc[kShareMaxWarps][kShareBatch];
+  __shared__ float2 s_norm[kShareMaxWarps][8];  // (M, 1 / S) of a warp's units' query rows (the long-row path)
+  __shared__ int s_cnt[kShareMaxWarps];
+  __shared__ float s_red[kShareMaxWarps];
+  __shared__ int s_count;    // this CTA's (layer, query row) pairs with data
+  __shared__ float s_total;  // (max) the total of this CTA's slice of the row
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank(), C = (int)cluster.num_blocks();
+  const int r = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = blockDim.x >> 5;
   chain_release();
-  // the row's length and selection are the step's inputs, not the kernels' before: read while they end
+  // the row's length and selection are the step's inputs, not the record kernel's: read while it ends
   const RowInfo ri = row_info(p, r, false);
-  chain_wait();  // the record kernel's cells, lse_kernel's log totals and contributor counts
-  if (*p.flag == 0) return;  // nothing was recorded this step
+  chain_wait();  // the record kernel's cells
+  if (*p.flag == 0) return;  // nothing was recorded this step (the same for every CTA)
   float* out = p.share_out + (size_t)r * p.width;
-  const int TB = p.tile_blocks, Q = p.Q;
-  const ShareLanes sl = share_lanes(Q, p.n_layers);
-  const int span = (kCombineThreads / 32) * sl.tiles_w;
-  const int t0 = blockIdx.x * span;
-  const int b_lo = t0 * TB, b_hi = min((t0 + span) * TB, p.width);  // this CTA's blocks
-  const int counted = __ldcg(p.row_contrib + r);  // (its load in flight with the cells' below)
-  const int contributors = ri.n_chunks ? counted : 0;
-  if (blockIdx.x == 0 && tid == 0) p.contrib_out[r] = contributors;
+  if (ri.n_chunks == 0) {  // the row records nothing: NaN (the same for the whole cluster)
+    for (int b = rank * blockDim.x + tid; b < p.width; b += C * blockDim.x) out[b] = NAN;
+    if (rank == 0 && tid == 0) p.contrib_out[r] = 0;
+    return;
+  }
+  const int Q = p.Q, QG = p.share_QG, TB = p.tile_blocks;
+  const int n = ri.n_blocks, n_tiles = ri.n_tiles;
+  const int groups = p.share_groups;
+  const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
+  const int tile_stride = TB * Q;  // floats from one tile's cell (its first block's) to the next tile's
   const bool agg_max = p.aggregate == EKV_AGG_MAX;
-  if (contributors > 0) {
-    const int n = ri.n_blocks, n_tiles = (n + TB - 1) / TB;
-    const int group = sl.lanes_q * sl.slices;  // lanes of one tile
-    const int qg = lane % sl.lanes_q, slice = (lane / sl.lanes_q) % sl.slices;
-    const int t = t0 + warp * sl.tiles_w + lane / group;
-    const size_t plane = (size_t)p.layers * p.rows * p.width * Q;
-    const int la = p.layer0, lb = p.layer0 + p.n_layers;
-    float v = 0.f;
-    if (t < n_tiles) {
-      const int bt0 = t * TB;
-      for (int q = qg * sl.V; q < Q; q += sl.lanes_q * sl.V) {
-        for (int L0 = la + slice; L0 < lb; L0 += kCombineU * sl.slices) {
-          float4 m[kCombineU], l[kCombineU], zm[kCombineU], zs[kCombineU];
+  int cnt = 0;  // this warp's (layer, query row) pairs with data
+  // Unit u of a group is its layer u / QG and query rows (u % QG) * V ...; a warp's units are u = warp,
+  // warp + warps, ..., walked as (layer, query-row unit) pairs without a division.
+  struct Unit {
+    int l, q;
+  };
+  const Unit u0{warp / QG, warp % QG}, du{warps / QG, warps % QG};
+  auto step = [&](Unit u) {
+    u.l += du.l, u.q += du.q;
+    if (u.q >= QG) u.q -= QG, ++u.l;
+    return u;
+  };
+  auto group_layers = [&](int g) { return min(p.share_Lg, p.n_layers - g * p.share_Lg); };
+  auto unit_cells = [&](int g, Unit u, const float*& cm, const float*& cl) {
+    const size_t lr = (size_t)(p.layer0 + g * p.share_Lg + u.l) * p.rows + r;
+    cm = p.lse + lr * p.width * Q + u.q * V;
+    cl = cm + plane;
+  };
+  float acc[kShareRegTiles];
+  if (n_tiles <= kShareBatch) {
+    // Every tile of a unit in registers: its maximum, the weights and their sum, the shares. A warp takes its
+    // units of every group of the CTA in turn (groups rank, rank + C, ...; in each, units warp, warp + warps,
+    // ...) with no barrier between them, adding into one set of per-tile sums; the CTA adds its warps once.
+    // With at most two slots a lane the next unit's cells are loaded while the current one is computed.
 #pragma unroll
-          for (int u = 0; u < kCombineU; ++u) {
-            const int L = L0 + u * sl.slices;
-            const bool ok = L < lb;
-            const size_t lr = (size_t)(ok ? L : la) * p.rows + r;
-            const float* cm = p.lse + (lr * p.width + (size_t)bt0) * Q + q;
-            const float2* z = p.row_lse + lr * kMaxQ + q;
-            if (sl.V == 4) {
-              m[u] = ok ? __ldcg(reinterpret_cast<const float4*>(cm)) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-              l[u] = ok ? __ldcg(reinterpret_cast<const float4*>(cm + plane)) : make_float4(0.f, 0.f, 0.f, 0.f);
-              const float4 z01 = ok ? __ldcg(reinterpret_cast<const float4*>(z)) : make_float4(0.f, 0.f, 0.f, 0.f);
-              const float4 z23 = ok ? __ldcg(reinterpret_cast<const float4*>(z + 2)) : make_float4(0.f, 0.f, 0.f, 0.f);
-              zm[u] = make_float4(z01.x, z01.z, z23.x, z23.z);
-              zs[u] = make_float4(z01.y, z01.w, z23.y, z23.w);
-            } else {
-              m[u] = make_float4(ok ? __ldcg(cm) : -INFINITY, -INFINITY, -INFINITY, -INFINITY);
-              l[u] = make_float4(ok ? __ldcg(cm + plane) : 0.f, 0.f, 0.f, 0.f);
-              const float2 z0 = ok ? __ldcg(z) : make_float2(0.f, 0.f);
-              zm[u] = make_float4(z0.x, 0.f, 0.f, 0.f);
-              zs[u] = make_float4(z0.y, 0.f, 0.f, 0.f);
-            }
-          }
+    for (int i = 0; i < kShareRegTiles; ++i) acc[i] = 0.f;
+    struct Cursor {
+      int g;
+      Unit u;
+    };
+    auto settle = [&](Cursor c) {  // the first unit at or after c
+      while (c.g < groups && c.u.l >= group_layers(c.g)) c.g += C, c.u = u0;
+      return c;
+    };
+    auto walk = [&](auto slots_tag) {
+      constexpr int SL = decltype(slots_tag)::value;
+      auto load = [&](Cursor c, float (&m)[SL][V], float (&l)[SL][V]) {
+        const float *cm, *cl;
+        unit_cells(c.g, c.u, cm, cl);
+        load_unit_tiles<V, SL>(cm, cl, tile_stride, 0, n_tiles, lane, m, l);
+      };
+      auto compute = [&](float (&m)[SL][V], float (&l)[SL][V]) {
+        float M[V], S[V], inv[V];
 #pragma unroll
-          for (int u = 0; u < kCombineU; ++u) {
-            const float mk[4] = {m[u].x, m[u].y, m[u].z, m[u].w}, lk[4] = {l[u].x, l[u].y, l[u].z, l[u].w};
-            const float Mk[4] = {zm[u].x, zm[u].y, zm[u].z, zm[u].w}, Sk[4] = {zs[u].x, zs[u].y, zs[u].z, zs[u].w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              // a query row without data, or a cell without data (m = -inf, l = 0), has no share
-              const float sh = (Sk[k] > 0.f && mk[k] > -INFINITY && lk[k] > 0.f) ? lk[k] / Sk[k] * __expf(mk[k] - Mk[k])
-                                                                                 : 0.f;
-              v = agg_max ? fmaxf(v, sh) : v + sh;
-            }
-          }
+        for (int k = 0; k < V; ++k) M[k] = -INFINITY, S[k] = 0.f;
+        unit_max<V, SL>(M, m);
+        lanes_max<V>(M);
+        unit_weights<V, SL>(S, M, m, l);
+        lanes_sum<V>(S);
+        cnt += unit_inverse<V>(inv, S);
+        add_unit_shares<V, SL>(acc, l, inv, agg_max);
+      };
+      Cursor c = settle(Cursor{rank, u0});
+      if (c.g >= groups) return;
+      float ma[SL][V], la[SL][V];
+      load(c, ma, la);
+      if constexpr (SL > 2) {
+        while (true) {
+          compute(ma, la);
+          c = settle(Cursor{c.g, step(c.u)});
+          if (c.g >= groups) break;
+          load(c, ma, la);
+        }
+      } else {
+        float mb[SL][V], lb[SL][V];
+        while (true) {
+          Cursor n = settle(Cursor{c.g, step(c.u)});
+          if (n.g < groups) load(n, mb, lb);
+          compute(ma, la);
+          if (n.g >= groups) break;
+          c = settle(Cursor{n.g, step(n.u)});
+          if (c.g < groups) load(c, ma, la);
+          compute(mb, lb);
+          if (c.g >= groups) break;
         }
       }
-    }
-    for (int off = 1; off < group; off <<= 1) {  // over the lanes of one tile
-      const float o = __shfl_xor_sync(kFullMask, v, off);
-      v = agg_max ? fmaxf(v, o) : v + o;
-    }
-    if (lane % group == 0 && t < t0 + span) {  // the tile's first lane writes its blocks
-      const int bt0 = t * TB;
-      const int in_row = t < n_tiles ? min(TB, n - bt0) : 0;
-      const float each = in_row > 0 ? (agg_max ? v / (float)in_row : v / (float)in_row / (float)contributors) : 0.f;
-      for (int b = bt0; b < bt0 + TB && b < p.width; ++b) out[b] = b < n ? each : 0.f;
+    };
+    // the slots in use (the same for the whole CTA), rounded up to a compiled count
+    const int slots = (n_tiles + 31) >> 5;
+    if (slots <= 1) walk(std::integral_constant<int, 1>{});
+    else if (slots <= 2) walk(std::integral_constant<int, 2>{});
+    else if (slots <= 4) walk(std::integral_constant<int, 4>{});
+    else walk(std::integral_constant<int, kShareRegTiles>{});
+#pragma unroll
+    for (int i = 0; i < kShareRegTiles; ++i) s_acc[warp][lane + 32 * i] = acc[i];
+    __syncthreads();
+    for (int t = tid; t < n_tiles; t += blockDim.x) {
+      float v = 0.f;
+      for (int w = 0; w < warps; ++w) v = agg_max ? fmaxf(v, s_acc[w][t]) : v + s_acc[w][t];
+      s_part[t] = v;
     }
   } else {
-    for (int b = b_lo + tid; b < b_hi; b += kCombineThreads) out[b] = NAN;
-  }
-  if (ri.n_chunks == 0) return;  // no contributor count to reset
-  // the CTA that finishes the row last: the row's total (max) and the count's reset
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&p.row_tickets[r], 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  if (agg_max && contributors > 0) {
-    const int n = ri.n_blocks;
-    float part = 0.f;
-    for (int b = tid; b < n; b += kCombineThreads) part += __ldcg(out + b);
-    const float total = block_sum_fixed_order<kCombineThreads>(part, s_red);
-    for (int b = tid; b < n; b += kCombineThreads) {
-      const float x = __ldcg(out + b);
-      out[b] = total > 0.f ? x / total : 0.f;
+    // Long rows, a group at a time: each unit's maximum and total weight in one pass over every batch of tiles
+    // (a running maximum and a sum rescaled when it grows: one exponential a cell), kept in s_norm (at most
+    // eight query rows a warp in a group: see share_shape), then the shares a batch at a time (a second read),
+    // the warps added per batch into s_part.
+    for (int g = rank; g < groups; g += C) {
+      const bool first = g == rank;
+      const int layers_g = group_layers(g);
+      int j = 0;
+      for (Unit u = u0; u.l < layers_g; u = step(u), ++j) {
+        const float *cm, *cl;
+        unit_cells(g, u, cm, cl);
+        float M[V], S[V], inv[V];
+#pragma unroll
+        for (int k = 0; k < V; ++k) M[k] = -INFINITY, S[k] = 0.f;
+        for (int t0 = 0; t0 < n_tiles; t0 += kShareBatch) {
+          float m[kShareRegTiles][V], l[kShareRegTiles][V];
+          load_unit_tiles<V, kShareRegTiles>(cm, cl, tile_stride, t0, n_tiles, lane, m, l);
+#pragma unroll
+          for (int i = 0; i < kShareRegTiles; ++i)
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+              const bool data = m[i][k] > -INFINITY;
+              const float d = m[i][k] - M[k];  // +inf while M is -inf
+              const float e = __expf(-fabsf(d));
+              const bool up = d > 0.f;
+              S[k] = data ? (up ? fmaf(S[k], e, l[i][k]) : fmaf(l[i][k], e, S[k])) : S[k];
+              M[k] = data && up ? m[i][k] : M[k];
+            }
+        }
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1)
+#pragma unroll
+          for (int k = 0; k < V; ++k) {
+            const float m2 = __shfl_xor_sync(kFullMask, M[k], off), s2 = __shfl_xor_sync(kFullMask, S[k], off);
+            lse_merge(M[k], S[k], m2, s2);
+          }
+        cnt += unit_inverse<V>(inv, S);
+        if (lane == 0)
+#pragma unroll
+          for (int k = 0; k < V; ++k) s_norm[warp][j * V + k] = make_float2(M[k], inv[k]);
+      }
+      __syncwarp();
+      for (int t0 = 0; t0 < n_tiles; t0 += kShareBatch) {
+#pragma unroll
+        for (int i = 0; i < kShareRegTiles; ++i) acc[i] = 0.f;
+        int j = 0;
+        for (Unit u = u0; u.l < layers_g; u = step(u), ++j) {
+          const float *cm, *cl;
+          unit_cells(g, u, cm, cl);
+          float m[kShareRegTiles][V], l[kShareRegTiles][V], M[V], inv[V], S[V];
+#pragma unroll
+          for (int k = 0; k < V; ++k) {
+            const float2 z = s_norm[warp][j * V + k];
+            M[k] = z.x, inv[k] = z.y, S[k] = 0.f;
+          }
+          load_unit_tiles<V, kShareRegTiles>(cm, cl, tile_stride, t0, n_tiles, lane, m, l);
+          unit_weights<V, kShareRegTiles>(S, M, m, l);
+          add_unit_shares<V, kShareRegTiles>(acc, l, inv, agg_max);
+        }
+#pragma unroll
+        for (int i = 0; i < kShareRegTiles; ++i) s_acc[warp][lane + 32 * i] = acc[i];
+        __syncthreads();
+        for (int t = tid; t < kShareBatch && t0 + t < n_tiles; t += blockDim.x) {
+          float v = 0.f;
+          for (int w = 0; w < warps; ++w) v = agg_max ? fmaxf(v, s_acc[w][t]) : v + s_acc[w][t];
+          const float prev = s_part[t0 + t];
+          s_part[t0 + t] = first ? v : (agg_max ? fmaxf(prev, v) : prev + v);
+        }
+        __syncthreads();
+      }
+      __syncwarp();  // s_norm is written again by the next group
     }
   }
-  if (tid == 0) p.row_tickets[r] = 0, p.row_contrib[r] = 0;  // ready for the next step
+  if (lane == 0) s_cnt[warp] = cnt;
+  __syncthreads();
+  if (tid == 0) {
+    int c = 0;
+    for (int w = 0; w < warps; ++w) c += s_cnt[w];
+    s_count = c;
+  }
+  cluster.sync();  // every CTA's partials and count are complete and visible to the cluster
+  int contributors = 0;
+  for (int j = 0; j < C; ++j) contributors += *cluster.map_shared_rank(&s_count, j);
+  if (rank == 0 && tid == 0) p.contrib_out[r] = contributors;
+  // this CTA's slice of the row: tiles [t_lo, t_hi)
+  const int width_tiles = (p.width + TB - 1) >> p.tb_shift, per = p.share_slice;
+  const int t_lo = min(rank * per, width_tiles), t_hi = min(t_lo + per, width_tiles);
+  if (contributors == 0) {
+    for (int b = t_lo * TB + tid; b < min(t_hi * TB, p.width); b += blockDim.x) out[b] = NAN;
+  } else {
+    float row_total = 0.f;  // (max) this thread's blocks' sum
+    for (int t = t_lo + tid; t < t_hi; t += blockDim.x) {
+      float v = 0.f;
+      if (t < n_tiles)
+        for (int j = 0; j < C; ++j) {
+          const float x = cluster.map_shared_rank(s_part, j)[t];
+          v = agg_max ? fmaxf(v, x) : v + x;
+        }
+      const int bt0 = t * TB;
+      const int in_row = t < n_tiles ? min(TB, n - bt0) : 0;
+      const float each = in_row > 0 ? v * __frcp_rn(agg_max ? (float)in_row : (float)(in_row * contributors)) : 0.f;
+      for (int b = bt0; b < bt0 + TB && b < p.width; ++b) {
+        out[b] = b < n ? each : 0.f;
+        if (b < n) row_total += each;
+      }
+    }
+    if (agg_max) {
+      // the row's total in a fixed order (xor-shuffles, the warps in order, the CTAs in rank order), then
+      // each CTA divides its slice by it
+      for (int off = 16; off > 0; off >>= 1) row_total += __shfl_xor_sync(kFullMask, row_total, off);
+      if (lane == 0) s_red[warp] = row_total;
+      __syncthreads();
+      if (tid == 0) {
+        float part = 0.f;
+        for (int w = 0; w < warps; ++w) part += s_red[w];
+        s_total = part;
+      }
+      cluster.sync();
+      float total = 0.f;
+      for (int j = 0; j < C; ++j) total += *cluster.map_shared_rank(&s_total, j);
+      const float inv_total = total > 0.f ? __frcp_rn(total) : 0.f;
+      for (int t = t_lo + tid; t < t_hi && t < n_tiles; t += blockDim.x)
+        for (int b = t * TB; b < t * TB + TB && b < n; ++b) out[b] *= inv_total;
+    }
+  }
+  cluster.sync();  // no CTA leaves while another may still read its shared memory
+}
+
+// The share kernel's shared-memory limit, set once per device to the most any launch asks for (one setting
+// for every caller: the kernel is the same whatever the record kernel's template arguments).
+inline int configure_share_kernel(int device) {
+  static bool configured[kMaxDevices] = {};
+  if (!configured[device]) {
+    if (cudaFuncSetAttribute(share_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kShareMaxTiles * (int)sizeof(float)) != cudaSuccess ||
+        cudaFuncSetAttribute(share_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kShareMaxTiles * (int)sizeof(float)) != cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(share_kernel)");
+    configured[device] = true;
+  }
+  return EKV_OK;
 }
 
 // One tensor map per layer of a step: the host-encoded template with the layer's key-cache address
@@ -837,15 +1029,19 @@ int launch_audit(const AuditParams& p, bool finalize, int share0, int share_laye
   AuditParams ps = p;
   ps.layer0 = share0;
   ps.n_layers = share_layers;
-  const long long triples = (long long)share_layers * p.rows * p.heads;
-  launch_chained(lse_kernel, dim3((unsigned)((triples + kLseWarps - 1) / kLseWarps)), dim3(kLseWarps * 32), 0, stream,
-                 ps);
-  rc = check_launch("lse_kernel");
+  const ShareShape sh = share_shape(p.Q, share_layers, (reinterpret_cast<uintptr_t>(p.lse) & 15) == 0);
+  ps.share_V = sh.V;
+  ps.share_QG = sh.QG;
+  ps.share_Lg = sh.Lg;
+  ps.share_groups = sh.groups;
+  ps.share_slice = cdiv(cdiv(p.width, p.tile_blocks), sh.cluster);
+  ps.tb_shift = __builtin_ctz((unsigned)p.tile_blocks);
+  const size_t share_smem = (size_t)cdiv(p.width, p.tile_blocks) * sizeof(float);
+  rc = configure_share_kernel(device);
   if (rc != EKV_OK) return rc;
-  const int span = (kCombineThreads / 32) * share_lanes(p.Q, share_layers).tiles_w;
-  launch_chained(combine_kernel, dim3(cdiv(cdiv(p.width, p.tile_blocks), span), p.rows), dim3(kCombineThreads), 0,
-                 stream, ps);
-  return check_launch("combine_kernel");
+  launch_chained_cluster(sh.V == 4 ? share_kernel<4> : share_kernel<1>, dim3(sh.cluster, p.rows), dim3(sh.warps * 32),
+                         share_smem, stream, (unsigned)sh.cluster, ps);
+  return check_launch("share_kernel");
 }
 
 template <typename T>
@@ -863,21 +1059,17 @@ int dispatch(const AuditParams& p, int tt, bool finalize, int share0, int share_
   return fail(EKV_ENOTSUP, "no audit kernel for a tile of %d tokens", tt);
 }
 
-// The workspace: [row_tickets, row_lse) holds the tickets, contributor counts and the work counter, zero
-// between steps; then the log totals and the per-layer tensor maps.
+// The workspace: the step's work counter (zeroed by kmap_kernel) and the per-layer tensor maps.
 struct WorkspaceLayout {
-  size_t row_tickets, row_contrib, counters, row_lse, kmaps, total;
+  size_t counters, kmaps, total;
 };
 
 WorkspaceLayout workspace_layout(int layers, int rows, int width) {
-  (void)width;  // the share's per-layer state is per (layer, row, query row), whatever the width
+  (void)rows;
+  (void)width;  // the share pass keeps its partials in shared memory
   WorkspaceLayout w{};
-  const size_t cells = (size_t)layers * rows * kMaxQ;
-  w.row_tickets = 0;
-  w.row_contrib = round_up((size_t)rows * 4, 256);
-  w.counters = w.row_contrib + round_up((size_t)rows * 4, 256);
-  w.row_lse = w.counters + 256;
-  w.kmaps = w.row_lse + round_up(cells * sizeof(float2), 256);
+  w.counters = 0;
+  w.kmaps = 256;
   w.total = w.kmaps + round_up((size_t)layers * sizeof(CUtensorMap), 256);
   return w;
 }
@@ -954,17 +1146,16 @@ int prepare(AuditParams& p, const int32_t* table, const int32_t* lens, const int
   p.kv_heads = kv_heads; p.pool_blocks = pool_blocks; p.q_tokens = q_tokens; p.status = status;
   p.share_out = share_out; p.contrib_out = contributors; p.aggregate = aggregate;
   if (share_out && !contributors) return fail(EKV_EINVAL, "share_out needs contributors");
-  if (share_out || need_workspace) {
+  if (share_out && cdiv(width, tile_blocks) > kShareMaxTiles)
+    return fail(EKV_ENOTSUP, "width %d: the share pass holds up to %d tiles of a row", width, kShareMaxTiles);
+  if (need_workspace) {
     const WorkspaceLayout w = workspace_layout(layers, rows, width);
     if (!workspace || workspace_bytes < w.total)
       return fail(EKV_ERANGE, "the audit workspace holds %zu bytes, the launch needs %zu", workspace_bytes, w.total);
     if ((uintptr_t)workspace & 255) return fail(EKV_EINVAL, "the audit workspace must be 256-byte aligned");
     uint8_t* base = static_cast<uint8_t*>(workspace);
-    p.item_counter = need_workspace ? reinterpret_cast<uint32_t*>(base + w.counters) : nullptr;
-    p.row_lse = reinterpret_cast<float2*>(base + w.row_lse);
-    p.row_tickets = reinterpret_cast<uint32_t*>(base + w.row_tickets);
-    p.row_contrib = reinterpret_cast<int32_t*>(base + w.row_contrib);
-    p.kmaps = need_workspace ? reinterpret_cast<const CUtensorMap*>(base + w.kmaps) : nullptr;
+    p.item_counter = reinterpret_cast<uint32_t*>(base + w.counters);
+    p.kmaps = reinterpret_cast<const CUtensorMap*>(base + w.kmaps);
   }
   return EKV_OK;
 }
@@ -1058,9 +1249,7 @@ extern "C" int ekv_audit_launch(
 
 namespace {
 
-// The audit step of ekv_audit_step. With clear_counters, the workspace's tickets and counters are zeroed on the
-// stream after every argument has been checked and before the first launch (a workspace whose last
-// user may have left them non-zero).
+// The audit step of ekv_audit_step and ekv_audit_step_static.
 int audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t* table, const int32_t* lens,
                const int32_t* qrow, const uint8_t* select, const uint32_t* flag, float* lse, float scale,
                int layer0, int n_layers, int group, int rotate, int q_layout, int64_t q_stride_token,
@@ -1068,7 +1257,7 @@ int audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t
                int64_t table_stride, int layers, int rows, int width, int group_rows, int block_size,
                int tile_blocks, int head_dim, int dtype, int heads, int kv_heads, int64_t pool_blocks,
                int64_t q_tokens, float* share_out, int32_t* contributors, int aggregate, void* workspace,
-               size_t workspace_bytes, uint32_t* status, void* stream, bool clear_counters) {
+               size_t workspace_bytes, uint32_t* status, void* stream) {
   if (!q_layers || !k_layers) return fail(EKV_EINVAL, "the per-layer address arrays must not be NULL");
   AuditParams p{};
   const int rc = prepare(p, table, lens, qrow, select, flag, lse, scale, q_stride_token, q_stride_head,
@@ -1089,12 +1278,6 @@ int audit_step(const uint64_t* q_layers, const uint64_t* k_layers, const int32_t
   const int enc = encode_key_map(&p.kmap0, workspace, p, dtype);
   if (enc != EKV_OK) return enc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (clear_counters) {
-    const WorkspaceLayout w = workspace_layout(layers, rows, width);
-    if (cudaMemsetAsync(static_cast<uint8_t*>(workspace) + w.row_tickets, 0, w.row_lse - w.row_tickets, s) !=
-        cudaSuccess)
-      return check_launch("cudaMemsetAsync(tickets and counters)");
-  }
   const int tt = block_size * tile_blocks;
   return dtype == EKV_DTYPE_BF16 ? dispatch<__nv_bfloat16>(p, tt, true, layer0, n_layers, s)
                                  : dispatch<__half>(p, tt, true, layer0, n_layers, s);
@@ -1116,7 +1299,7 @@ extern "C" int ekv_audit_step(
                     rotate, q_layout, q_stride_token, q_stride_head, k_stride_block, k_stride_pos, k_stride_head,
                     table_stride, layers, rows, width, group_rows, block_size, tile_blocks, head_dim, dtype, heads,
                     kv_heads, pool_blocks, q_tokens, share_out, contributors, aggregate, workspace,
-                    workspace_bytes, status, stream, false);
+                    workspace_bytes, status, stream);
 }
 
 // ---- the audit step without a caller-provided workspace ---------------------------------------------
@@ -1127,7 +1310,9 @@ extern "C" int ekv_audit_step(
 // them the step's workspace lives in this file-scope array, which every GPU that loads the library
 // holds until the process exits. Every call shares it: calls whose launches overlap on the GPU race.
 
-#define EKV_AUDIT_STATIC_SCRATCH_BYTES (16u << 20)
+// The workspace of the widest step this build accepts: the work counter and kMaxLayers tensor maps.
+#define EKV_AUDIT_STATIC_SCRATCH_BYTES (256u + 1024u * 128u)
+static_assert(EKV_AUDIT_STATIC_SCRATCH_BYTES >= 256 + kMaxLayers * sizeof(CUtensorMap), "the static workspace holds every step");
 
 static __device__ __align__(256) uint8_t g_audit_scratch[EKV_AUDIT_STATIC_SCRATCH_BYTES];
 
@@ -1217,11 +1402,11 @@ extern "C" int ekv_audit_step_static(
   void* scratch = nullptr;
   const int rc = static_scratch(&scratch);
   if (rc != EKV_OK) return rc;
-  // The array keeps the last call's contents: audit_step zeroes its tickets and counters once every argument
-  // has been checked, so a refused call leaves the array as it was.
+  // Nothing in the array needs clearing: every step's kmap_kernel rewrites the tensor maps and zeroes the work
+  // counter before the record kernel reads them.
   return audit_step(q_layers, k_layers, table, lens, qrow, select, flag, lse, scale, layer0, n_layers, group,
                     rotate, q_layout, q_stride_token, q_stride_head, k_stride_block, k_stride_pos, k_stride_head,
                     table_stride, layers, rows, width, group_rows, block_size, tile_blocks, head_dim, dtype, heads,
                     kv_heads, pool_blocks, q_tokens, share_out, contributors, aggregate, scratch,
-                    EKV_AUDIT_STATIC_SCRATCH_BYTES, status, stream, true);
+                    EKV_AUDIT_STATIC_SCRATCH_BYTES, status, stream);
 }

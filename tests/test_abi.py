@@ -49,16 +49,17 @@ def test_constants_agree_with_the_header():
 
 
 def test_workspace_size(lib):
-    # row tickets [rows] + contributors [rows] + the step's item counter + a log total (two float32) per
-    # (layer, row, query row: up to 128) + a 128-byte key-cache descriptor per layer
+    # the step's item counter + a 128-byte key-cache descriptor per layer; rows and width do not change it
     layers, rows, width = 32, 64, 512
 
     def up(x):
         return -(-x // 256) * 256
 
-    want = up(rows * 4) + up(rows * 4) + 256 + up(layers * rows * 128 * 8) + up(layers * 128)
+    want = 256 + up(layers * 128)
     assert lib.ekv_audit_workspace_bytes(layers, rows, width) == want
-    assert lib.ekv_audit_workspace_bytes(layers, rows, 4 * width) == want  # the width does not change it
+    assert lib.ekv_audit_workspace_bytes(layers, 2 * rows, 4 * width) == want
+    # the static workspace holds the widest step this build accepts (1024 layers) and no more
+    assert lib.ekv_audit_static_scratch_bytes() == lib.ekv_audit_workspace_bytes(1024, rows, width)
     assert lib.ekv_audit_workspace_bytes(0, rows, width) == 0
 
 
@@ -89,7 +90,8 @@ def audit_args(**over):
         (dict(ts=4), L.EINVAL),
         (dict(agg=5), L.EINVAL),
         (dict(out=ctypes.c_void_p(0x3000)), L.EINVAL),  # no contributors
-        (dict(out=ctypes.c_void_p(0x3000), contrib=ctypes.c_void_p(0x4000), ws=None), L.ERANGE),
+        # rows of more tiles than the share pass holds (32768)
+        (dict(out=ctypes.c_void_p(0x3000), contrib=ctypes.c_void_p(0x4000), width=65538, ts=65538), L.ENOTSUP),
         (dict(rows=4096), L.ENOTSUP),
     ],
 )
@@ -199,4 +201,4 @@ def test_step_and_stash_validate_before_launching(lib):
 
 
 def test_abi_version(lib):
-    assert lib.ekv_abi_version() == 5
+    assert lib.ekv_abi_version() == 6

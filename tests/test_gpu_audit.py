@@ -263,18 +263,28 @@ def test_random_rows_match_the_oracle(q_heads, kv_heads, tile_blocks, dtype):
     compare_shares(ref, lens, select, block_size, tile_blocks, run.share.cpu().numpy())
 
 
-def test_all_heads_mode_matches_the_oracle():
-    rows, width, layers, q_heads, kv_heads = 4, 24, 2, 32, 8
-    lens = [377, 16, 200, 384]
+@pytest.mark.parametrize(
+    "q_heads, heads, width, lens",
+    [
+        (32, 8, 24, [377, 16, 200, 384]),  # 32 values a cell: eight warps of four
+        (128, 8, 24, [377, 16, 200, 384]),  # 128 values: two units a warp, log totals kept
+        (72, 5, 24, [377, 16, 200, 384]),  # G = 9, 45 values: single loads, log totals merged again per batch
+        (32, 8, 600, [9600, 16, 4100, 9599]),  # rows of 300 tiles: the cells read again, in two batches
+        (72, 5, 600, [9600, 16, 4100, 9599]),
+    ],
+)
+def test_all_heads_mode_matches_the_oracle(q_heads, heads, width, lens):
+    """Every shape of the share pass: cells of 32, 45 and 128 values, rows of more tiles than a warp holds."""
+    rows, layers, kv_heads = 4, 2, 8
     select = [1, 1, 1, 1]
     gen_layers = [random_case(40 + layer, rows, width, q_heads, kv_heads, lens) for layer in range(layers)]
     _, _, table, lens_t, qrow = gen_layers[0]
     run = None
     for layer in range(layers):
         run = launch(gen_layers[layer][0], gen_layers[layer][1], table, lens_t, qrow, select, True, layers, layer,
-                     q_heads // kv_heads, heads=kv_heads, group=0, run=run)
+                     q_heads // kv_heads, heads=heads, group=0, run=run)
     ref = oracle_case(table, lens_t, qrow, select, [g[0] for g in gen_layers], [g[1] for g in gen_layers],
-                      q_heads // kv_heads, 16, 2, heads=kv_heads, groups=[0] * layers)
+                      q_heads // kv_heads, 16, 2, heads=heads, groups=[0] * layers)
     got = run.lse.cpu().numpy()
     w = ~np.isnan(ref)
     assert np.array_equal(np.isnan(got), np.isnan(ref))

@@ -146,10 +146,10 @@ def test_a_step_beyond_the_static_workspace_is_rejected():
     x = make_inputs()
     lse, share, contrib, status = outputs(x)
     args = common_args(x, lse)
-    # a table of 1024 layers x 2048 rows: its workspace is far beyond the static one, so the call is
-    # refused before anything is launched (checked first, as the buffers here are not that large)
-    assert lib.ekv_audit_workspace_bytes(1024, 2048, x["width"]) > lib.ekv_audit_static_scratch_bytes()
-    args[20], args[21] = 1024, 2048
+    # a table of 2048 layers: its workspace is beyond the static one, so the call is refused before
+    # anything is launched (checked first, as the buffers here are not that large)
+    assert lib.ekv_audit_workspace_bytes(2048, x["rows"], x["width"]) > lib.ekv_audit_static_scratch_bytes()
+    args[20] = 2048
     rc = lib.ekv_audit_step_static(*args, share.data_ptr(), contrib.data_ptr(), L.AGG_MEAN, status.data_ptr(),
                                    L.current_stream())
     assert rc == L.ERANGE

@@ -4,7 +4,8 @@
 //
 // The view kernel runs one CTA per row. Ranking mode turns max(score, 0) (float32, NaN as 0) into
 // an order-preserving uint32 key and finds the quota-th largest key of the row's unpinned blocks by
-// a four-pass MSB radix select (256-bin shared-memory histograms). Keys above the threshold are
+// an MSB radix select (digits of 11, 11 and 9 bits over a 2048-bin shared-memory histogram; float64
+// gain keys take six digits), while the table row is copied in. Keys above the threshold are
 // kept; of the keys equal to it, the first (uniform: older blocks first, allocation.py:89) or last
 // (sum: newer blocks first, allocation.py:107-113) ones fill the quota, found with a block-wide
 // scan. A second block-wide scan over the keep flags places kept blocks first and the others after
@@ -225,7 +226,9 @@ constexpr uint8_t kRowFull = 1, kRowDecoding = 2, kRowAudited = 4;
 constexpr int kViewThreads = 512;
 constexpr int kViewWarps = kViewThreads / 32;
 constexpr int kViewMaxWidth = 16384;               // rows staged in shared memory: 8 bytes per position
-constexpr int kViewMaxIters = kViewMaxWidth / kViewThreads;
+constexpr int kViewSeg = 128;                      // positions of a segment: four per lane of a warp
+constexpr int kViewMaxSegs = kViewMaxWidth / kViewSeg;
+static_assert(kViewMaxSegs <= 4 * 32, "one warp scans the segments, four per lane");
 constexpr int kViewBins = 2048;                    // radix-select digits of 11, 11 and 9 bits
 static_assert(kViewBins == 4 * kViewThreads, "each thread owns four histogram bins");
 
@@ -258,24 +261,33 @@ __device__ __forceinline__ void copy_words(int32_t* dst, const int32_t* src, int
 }
 
 
-// Exclusive scan of one count per warp (warp 0 scans): {this warp's base, the total}.
-__device__ __forceinline__ int2 warp_bases(int count, int* s_w) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Exclusive scan of the n per-segment counts c[0..n) in place (warp 0, four a lane); c[n] = the total, returned
+// to every thread. n <= kViewMaxSegs. Barriers before (the counts are written) and after.
+__device__ __forceinline__ int segment_scan(int* c, int n) {
   __syncthreads();
-  if (lane == 0) s_w[warp] = count;
-  __syncthreads();
-  if (warp == 0) {
-    int v = lane < kViewWarps ? s_w[lane] : 0;
-    int inc = v;
-    for (int off = 1; off < 32; off <<= 1) {
-      const int n = __shfl_up_sync(kFullMask, inc, off);
-      if (lane >= off) inc += n;
+  if ((threadIdx.x >> 5) == 0) {
+    const int lane = threadIdx.x & 31;
+    int v[4], sum = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[k] = 4 * lane + k < n ? c[4 * lane + k] : 0;
+      sum += v[k];
     }
-    if (lane < kViewWarps) s_w[lane] = inc - v;
-    if (lane == kViewWarps - 1) s_w[kViewWarps] = inc;
+    int incl = sum;
+    for (int off = 1; off < 32; off <<= 1) {
+      const int x = __shfl_up_sync(kFullMask, incl, off);
+      if (lane >= off) incl += x;
+    }
+    int run = incl - sum;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (4 * lane + k < n) c[4 * lane + k] = run;
+      run += v[k];
+    }
+    if (lane == 31) c[n] = incl;
   }
   __syncthreads();
-  return make_int2(s_w[warp], s_w[kViewWarps]);
+  return c[n];
 }
 
 // The order keys of the ranking. Float32 scores: the bits of max(score, 0), three digits (bits 30-20,
@@ -323,8 +335,9 @@ __device__ __forceinline__ unsigned long long share_key64(double s, double total
 
 template <typename K>
 __host__ __device__ constexpr size_t view_smem_bytes(int width) {
-  // keys (the staged scores, then the keys, then the view row) + the table row (+ the pairwise-sum tree)
-  return (size_t)((width + kViewThreads - 1) / kViewThreads * kViewThreads) * (sizeof(K) + 4) +
+  // keys (the staged scores, then the keys, then the view row) + the table row (+ the pairwise-sum tree), each
+  // padded to whole segments
+  return (size_t)((width + kViewSeg - 1) / kViewSeg * kViewSeg) * (sizeof(K) + 4) +
          (sizeof(K) == 8 ? sizeof(PairwiseTree) : 0);
 }
 
@@ -336,25 +349,33 @@ __host__ __device__ constexpr size_t view_smem_bytes(int width) {
 // with that prefix is kept and the select stops early. The equal-key count comes from the last
 // histogram, so the scan that ranks equal keys by position runs only when some of them must be dropped.
 //
-// The layout: only positions [0, min(blocks, width)) can be kept, so those are laid out warp-striped
-// (warp w owns [w * 32 * iters, (w + 1) * 32 * iters), lane l of iteration i holds base + 32 * i + l,
-// so a ballot per iteration orders a warp's positions), and the rest of the row, never kept, keeps its
-// place: the view there is the table. With mask_out the layout covers the whole width, as every
-// position's committed flag is written; with no view (mask_out only) the kernel ends there.
+// The layout: only positions [0, min(blocks, width)) can be kept, so those are laid out, in segments of 128
+// positions that the warps take in turn (warp w: segments w, w + 16, ...; lane l holds positions
+// 128 * s + 4 * l + k, read and written 16 bytes at a time); the rest of the row, never kept, keeps its
+// place: the view there is the table. A segment's keep flags are four ballots, one per k (bit l of ballot
+// k: position 4 * l + k), so the kept positions before a lane's are popcounts of the ballots below its
+// bit, and a scan of the segments' counts gives each segment's first place. With mask_out the flags cover
+// the whole width, as every position's committed flag is written; with no view (mask_out only) the kernel
+// ends there.
 template <typename K>
-__global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) {
+__global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_kernel(const ViewParams p) {
   chain_release();
   chain_wait();  // what the launch before this one wrote
   extern __shared__ __align__(16) unsigned char smem_view[];
   __shared__ __align__(16) int s_hist[kViewBins];
   __shared__ int s_w[kViewWarps + 1];
   __shared__ int s_pick[3];
-  __shared__ uint32_t s_bits[kViewWarps][kViewMaxIters];  // each warp's keep ballots, per iteration
+  __shared__ uint4 s_bits[kViewMaxSegs];  // each segment's four keep ballots
+  // after the select, the histogram's space holds each segment's kept positions (then the kept positions
+  // before it) and, with ties, its equal keys (then the equal keys before it)
+  int* s_seg = s_hist;
+  int* s_eq = s_hist + 2 * kViewMaxSegs;
+  static_assert(4 * kViewMaxSegs + 2 <= kViewBins, "the segment counts fit the histogram's space");
   constexpr bool kWide = sizeof(K) == 8;
   const int r = blockIdx.x;
   const int W = p.width, BS = p.block_size;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int w_pad = (W + kViewThreads - 1) / kViewThreads * kViewThreads;
+  const int w_pad = (W + kViewSeg - 1) / kViewSeg * kViewSeg;
   K* keys = reinterpret_cast<K*>(smem_view);                                       // [w_pad]
   int32_t* trow_s = reinterpret_cast<int32_t*>(smem_view + (size_t)w_pad * sizeof(K));  // [w_pad]: the table row
 
@@ -363,9 +384,8 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
   const int blocks = seq > 0 ? (seq + BS - 1) / BS : 0;
   uint8_t* mrow = p.mask_out ? p.mask_out + (int64_t)r * p.mask_s0 : nullptr;
   const int live = mrow != nullptr ? W : (blocks < W ? blocks : W);
-  const int iters = (live + kViewThreads - 1) / kViewThreads;
-  const int wbase = warp * 32 * iters;
-  const int laid = !has_view ? 0 : (iters * kViewThreads < W ? iters * kViewThreads : W);  // positions laid out
+  const int n_segs = (live + kViewSeg - 1) / kViewSeg;               // segments flagged
+  const int laid = !has_view ? 0 : min((live + 3) & ~3, W);            // positions laid out
 
   // ---- the row's committed mask: pins + selection (ranking mode) or the given mask ---------------
   const bool rank_mode = p.keep == nullptr;
@@ -414,16 +434,15 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
   // (address arithmetic only: without a view, laid is 0 and the table is never read)
   const int32_t* trow = reinterpret_cast<const int32_t*>(reinterpret_cast<uintptr_t>(p.table) +
                                                          (uintptr_t)((int64_t)r * p.table_s0 * 4));
-  if (!by_threshold) {  // (with a ranking, the staging buffer first holds the select's candidates)
-    stage_words(reinterpret_cast<uint32_t*>(trow_s), reinterpret_cast<const uint32_t*>(trow), laid);
-    cp_async_commit();
-  }
+  // the table row lands while the row is ranked
+  stage_words(reinterpret_cast<uint32_t*>(trow_s), reinterpret_cast<const uint32_t*>(trow), laid);
+  cp_async_commit();
 
   K prefix = 0, pmask = 0;
   int k_eq = 0, eq_total = 0;
   if (by_threshold) {
     reinterpret_cast<int4*>(s_hist)[threadIdx.x] = make_int4(0, 0, 0, 0);  // (ordered by the barrier below)
-    cp_async_wait<0>();  // the scores have landed
+    cp_async_wait<1>();  // the scores have landed (the table row, committed after them, may still be in flight)
     __syncthreads();
     // The keys, and the first digit's histogram as they are written. Positions 0 and from ps on are not
     // keys; they are handled four at a time.
@@ -458,39 +477,12 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
       }
     }
     int k = q;
-    // After the first digit only the keys of its chosen bin matter: they are gathered into a candidate list
-    // (in the table's staging buffer, whose copy starts after the select) when it holds them, and the later
-    // digits are counted over the list alone.
-    K* cand = reinterpret_cast<K*>(trow_s);
-    const int cand_cap = (int)((size_t)w_pad * 4 / sizeof(K));
-    __shared__ int s_ncand;
-    bool listed = false;
 #pragma unroll 1
     for (int pass = 0; pass < ViewKey<K>::kPasses; ++pass) {
       int shift;
       K dmask;
       ViewKey<K>::digit(pass, shift, dmask);
-      if (pass > 0 && !listed && eq_total <= cand_cap) {
-        if (threadIdx.x == 0) s_ncand = 0;
-        __syncthreads();
-        for (int g = threadIdx.x; g < groups; g += kViewThreads) {
-          K kv[4];
-          ViewKey<K>::load4(keys, g, kv);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int b = 4 * g + j;
-            if (b >= 1 && b < ps && (kv[j] & pmask) == prefix) cand[atomicAdd(&s_ncand, 1)] = kv[j];
-          }
-        }
-        __syncthreads();
-        listed = true;
-      }
-      if (listed) {
-        for (int i = threadIdx.x; i < s_ncand; i += kViewThreads) {
-          const K key = cand[i];
-          if ((key & pmask) == prefix) atomicAdd(&s_hist[(int)((key >> shift) & dmask)], 1);
-        }
-      } else if (pass > 0) {
+      if (pass > 0) {  // (pass 0's histogram was counted as the keys were made)
         for (int g = threadIdx.x; g < groups; g += kViewThreads) {
           K kv[4];
           ViewKey<K>::load4(keys, g, kv);
@@ -538,23 +530,23 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
       if (eq_total == k) break;  // all of them are kept: the prefix is the threshold
     }
     k_eq = k;
-    __syncthreads();  // the candidate list is read no more: the table row may land in its place
-    stage_words(reinterpret_cast<uint32_t*>(trow_s), reinterpret_cast<const uint32_t*>(trow), laid);
-    cp_async_commit();
   }
   const bool ties = eq_total != k_eq;  // only then do keys equal to the threshold need their rank
   const bool older_first = p.policy == EKV_POLICY_UNIFORM;
 
   // ---- ties: each equal key's rank among the equal keys, in position order --------------------
-  int eq_base = 0;
   if (ties) {
-    int cnt = 0;
-    for (int i = 0; i < iters; ++i) {
-      const int b = wbase + 32 * i + lane;
-      const bool eq = b >= 1 && b < ps && (keys[b] & pmask) == prefix;
-      cnt += __popc(__ballot_sync(kFullMask, eq));
+    for (int sg = warp; sg < n_segs; sg += kViewWarps) {
+      const int b0 = kViewSeg * sg + 4 * lane;
+      K kv[4];
+      ViewKey<K>::load4(keys, b0 >> 2, kv);
+      int cnt = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) cnt += b0 + k >= 1 && b0 + k < ps && (kv[k] & pmask) == prefix;
+      for (int off = 16; off > 0; off >>= 1) cnt += __shfl_xor_sync(kFullMask, cnt, off);
+      if (lane == 0) s_eq[sg] = cnt;
     }
-    eq_base = warp_bases(cnt, s_w).x;
+    segment_scan(s_eq, n_segs);
   }
 
   const uint8_t flags = p.full_rows != nullptr ? p.full_rows[r] : 0;
@@ -562,69 +554,114 @@ __global__ void __launch_bounds__(kViewThreads) view_kernel(const ViewParams p) 
   const uint8_t* krow = rank_mode ? nullptr : p.keep + (int64_t)r * p.keep_s0;
   const uint8_t* rrow = p.released ? p.released + (int64_t)r * p.released_s0 : nullptr;
 
-  // ---- pass 1: the final keep flag of every laid-out position, as one ballot per iteration ---------
-  int kept_count = 0, eq_seen = eq_base;
+  // ---- pass 1: the final keep flag of every flagged position, as four ballots per segment -------------
   if (rank_mode && by_threshold && !ties && mrow == nullptr && rrow == nullptr && !full) {
-    // the common case: a key at or above the threshold is kept; outside [1, open_hi) every block is
-    for (int i = 0; i < iters; ++i) {
-      const int b = wbase + 32 * i + lane;
-      const K key = (b >= 1 && b < open_hi) ? keys[b] & pmask : ~(K)0;
-      const bool keep = (key >= prefix || b == 0 || b == blocks - 1) && b < blocks && b < W;
-      const uint32_t bits = __ballot_sync(kFullMask, keep);
-      if (lane == 0) s_bits[warp][i] = bits;
-      kept_count += __popc(bits);
-    }
-  } else
-  for (int i = 0; i < iters; ++i) {
-    const int b = wbase + 32 * i + lane;
-    const bool in_row = b < W;
-    bool c = in_row;  // the committed mask at b
-    if (!rank_mode) {
-      c = in_row && krow[b] != 0;
-    } else if (b >= 1 && b < open_hi) {
-      if (newest) {
-        c = b >= ps - q;
-      } else if (by_threshold) {
-        const K key = keys[b] & pmask;
-        c = key > prefix || (key == prefix && !ties);  // every equal key is kept unless too many
+    // the common case: a key at or above the threshold is kept; outside [1, open_hi) every block is. A segment
+    // inside [1, min(open_hi, blocks - 1)) needs the key test alone.
+    const int inner = min(open_hi, blocks - 1);
+    for (int sg = warp; sg < n_segs; sg += kViewWarps) {
+      const int b0 = kViewSeg * sg + 4 * lane;
+      K kv[4];
+      ViewKey<K>::load4(keys, b0 >> 2, kv);
+      uint32_t plane[4];
+      if (sg > 0 && kViewSeg * (sg + 1) <= inner) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) plane[k] = __ballot_sync(kFullMask, (kv[k] & pmask) >= prefix);
       } else {
-        c = false;  // nothing selected
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int b = b0 + k;
+          const K key = (b >= 1 && b < open_hi) ? kv[k] & pmask : ~(K)0;
+          plane[k] = __ballot_sync(kFullMask, (key >= prefix || b == 0 || b == blocks - 1) && b < blocks && b < W);
+        }
+      }
+      if (lane == 0) {
+        s_bits[sg] = make_uint4(plane[0], plane[1], plane[2], plane[3]);
+        s_seg[sg] = __popc(plane[0]) + __popc(plane[1]) + __popc(plane[2]) + __popc(plane[3]);
       }
     }
-    if (ties) {
-      const bool eq = b >= 1 && b < ps && (keys[b] & pmask) == prefix;
-      const uint32_t eqb = __ballot_sync(kFullMask, eq);
-      if (eq) {
-        const int before = eq_seen + __popc(eqb & lanes_below());
-        c = older_first ? before < k_eq : (eq_total - before - 1) < k_eq;
+  } else {
+    for (int sg = warp; sg < n_segs; sg += kViewWarps) {
+      const int b0 = kViewSeg * sg + 4 * lane;
+      K kv[4] = {0, 0, 0, 0};
+      if (by_threshold) ViewKey<K>::load4(keys, b0 >> 2, kv);
+      bool c[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int b = b0 + k;
+        c[k] = b < W;  // the committed mask at b
+        if (!rank_mode) {
+          c[k] = b < W && krow[b] != 0;
+        } else if (b >= 1 && b < open_hi) {
+          if (newest) {
+            c[k] = b >= ps - q;
+          } else if (by_threshold) {
+            const K key = kv[k] & pmask;
+            c[k] = key > prefix || (key == prefix && !ties);  // every equal key is kept unless too many
+          } else {
+            c[k] = false;  // nothing selected
+          }
+        }
       }
-      eq_seen += __popc(eqb);
+      if (ties) {
+        // each equal key's rank among the equal keys in position order: those of the segments before, of the
+        // lanes below, then this lane's before k
+        bool eq[4];
+        int below = s_eq[sg];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int b = b0 + k;
+          eq[k] = b >= 1 && b < ps && (kv[k] & pmask) == prefix;
+          below += __popc(__ballot_sync(kFullMask, eq[k]) & lanes_below());
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (eq[k]) {
+            c[k] = older_first ? below < k_eq : (eq_total - below - 1) < k_eq;
+            ++below;
+          }
+      }
+      uint32_t plane[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int b = b0 + k;
+        const bool in_row = b < W;
+        if (mrow != nullptr && in_row) mrow[b] = c[k];
+        bool keep = c[k] || full;
+        if (rrow != nullptr && in_row && rrow[b]) keep = false;  // a released block is never read (block_view.py:280-281)
+        keep = (keep || b == 0 || b == blocks - 1) && b < blocks && in_row;
+        plane[k] = __ballot_sync(kFullMask, keep);
+      }
+      if (lane == 0) {
+        s_bits[sg] = make_uint4(plane[0], plane[1], plane[2], plane[3]);
+        s_seg[sg] = __popc(plane[0]) + __popc(plane[1]) + __popc(plane[2]) + __popc(plane[3]);
+      }
     }
-    if (mrow != nullptr && in_row) mrow[b] = c;
-    bool keep = c || full;
-    if (rrow != nullptr && in_row && rrow[b]) keep = false;  // a released block is never read (block_view.py:280-281)
-    keep = (keep || b == 0 || b == blocks - 1) && b < blocks && in_row;
-    const uint32_t bits = __ballot_sync(kFullMask, keep);
-    if (lane == 0) s_bits[warp][i] = bits;
-    kept_count += __popc(bits);
   }
-  const int2 kb = warp_bases(kept_count, s_w);  // (its barrier also ends every key read)
-  const int kept_base = kb.x, kept_total = kb.y;
+  const int kept_total = segment_scan(s_seg, n_segs);  // (its barriers also end every key read)
 
   // ---- pass 2: kept ids first, then the others, both in position order, into shared memory -------
   cp_async_wait<0>();
   __syncthreads();  // the table row has landed
   uint32_t* out = reinterpret_cast<uint32_t*>(keys);
-  int kept = kept_base;
-  for (int i = 0; i < iters; ++i) {
-    const int b = wbase + 32 * i + lane;
-    const uint32_t bits = s_bits[warp][i];
-    const int before = kept + __popc(bits & lanes_below());
-    if (b < laid) {
-      const uint32_t id = static_cast<uint32_t>(trow_s[b]);
-      if ((bits >> lane) & 1u) out[before] = id; else out[kept_total + (b - before)] = id;
+  for (int sg = warp; sg < n_segs && kViewSeg * sg < laid; sg += kViewWarps) {
+    const int b0 = kViewSeg * sg + 4 * lane;
+    const uint4 pl = s_bits[sg];
+    const uint32_t plane[4] = {pl.x, pl.y, pl.z, pl.w};
+    int before = s_seg[sg];  // kept positions before this lane's first
+#pragma unroll
+    for (int k = 0; k < 4; ++k) before += __popc(plane[k] & lanes_below());
+    if (b0 < laid) {
+      const uint4 ids4 = *reinterpret_cast<const uint4*>(trow_s + b0);
+      const uint32_t ids[4] = {ids4.x, ids4.y, ids4.z, ids4.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int b = b0 + k;
+        const bool keep = (plane[k] >> lane) & 1u;
+        if (b < laid) out[keep ? before : kept_total + (b - before)] = ids[k];
+        before += keep;
+      }
     }
-    kept += __popc(bits);
   }
   __syncthreads();
   int32_t* vrow = p.view + (int64_t)r * p.view_s0;

@@ -16,9 +16,9 @@
 //      float64 gain) and the histogram of their first digits; the CTA that finishes last sets the
 //      budget and picks that digit.
 //   2. The rest of an MSB radix select of the `free`-th largest key (digits of 11 bits, the last of
-//      8): sum_keys_pass_kernel reads every key again, counts per row the keys above the first
-//      digit and moves the keys of that digit to a candidate list; passes 2-5 read the candidates
-//      only. Each CTA histograms in shared memory and merges; the CTA that finishes last picks the
+//      8): sum_keys_pass_kernel (a CTA per row) reads every key again, counts per row the keys above
+//      the first digit and moves the keys of that digit to a candidate list; passes 2-5 read the
+//      candidates only. Each CTA histograms in shared memory and merges; the CTA that finishes last picks the
 //      digit. No CTA waits for another.
 //   3. sum_ties_kernel over the candidates: keys above the threshold per row and ties per block
 //      index; the CTA that finishes last finds the index i* at which the ties needed run out (ties
@@ -34,7 +34,6 @@ namespace ekv {
 constexpr int kSumThreads = 256;
 constexpr int kSumBins = 2048;
 constexpr int kSumPasses = 6;
-constexpr int kSumChunk = 2048;   // blocks of one row per CTA in the passes over every key
 constexpr int kSumMaxWidth = 32768;
 constexpr int kSumMaxRows = 1 << 17;  // a candidate's place is (row << 15) | block
 
@@ -200,9 +199,10 @@ __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p
   chain_release();
   chain_wait();  // what the launch before this one wrote
   extern __shared__ __align__(16) unsigned char sum_smem[];
-  S* s_x = reinterpret_cast<S*>(sum_smem);  // [width]: the row's scores
+  S* s_x = reinterpret_cast<S*>(sum_smem);  // [width]: the row's scores, then the pairwise sum's scratch
+  const PairwiseScratch s_tree =
+      pairwise_scratch(sum_smem + ((size_t)p.width * sizeof(S) + 15) / 16 * 16, pairwise_nodes(p.width));
   __shared__ unsigned int s_hist[kSumBins];
-  __shared__ PairwiseTree s_tree;
   __shared__ double s_total;
   __shared__ bool s_last;
   const int r = blockIdx.x, tid = threadIdx.x;
@@ -271,77 +271,92 @@ __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p
   if (st->mode == kSumSelect) pick_digit(st, p.hist, 0);  // pass 0 of the select
 }
 
-// Pass 1 over every key: grid (width / kSumChunk, rows). It counts each row's keys above the digit of
-// pass 0 and moves the keys of that digit to the candidates (each CTA's in one piece).
+// Pass 1 over every key: a CTA per row. It counts the row's keys above the digit of pass 0 and appends the
+// keys of that digit to the candidates in two sweeps: the first counts them (and their next digit), one
+// atomic gives the row its place in the list, the second (the keys again, from L2) writes them there.
 __global__ void __launch_bounds__(kSumThreads) sum_keys_pass_kernel(const SumParams p) {
   chain_release();
   chain_wait();  // what the launch before this one wrote
   constexpr int pass = 1;
+  constexpr int kPer = 8;  // keys a thread has in flight
   __shared__ unsigned int s_hist[kSumBins];
-  __shared__ unsigned long long s_ckey[kSumChunk];  // this CTA's candidates, moved out in one piece
-  __shared__ unsigned int s_cat[kSumChunk];
-  __shared__ unsigned int s_ncand, s_base;
+  __shared__ int s_warp[kSumThreads / 32 + 1];  // each warp's candidates, then the warps' places
   __shared__ int s_above;
+  __shared__ unsigned int s_base;
   __shared__ bool s_last;
-  const int tid = threadIdx.x, lane = tid & 31, r = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.x;
   SumState* st = p.state;
   if (st->mode != kSumSelect) return;  // (uniform over the grid)
   const bool histogram = !st->found;
   int shift;
   unsigned long long dmask;
   digit_of(pass, shift, dmask);
-  const unsigned long long prefix = st->prefix;
   int shift0;
   unsigned long long dmask0;
   digit_of(0, shift0, dmask0);
+  const unsigned long long top_mask = dmask0 << shift0, top_want = st->prefix & top_mask;
   for (int i = tid; i < kSumBins; i += kSumThreads) s_hist[i] = 0;
-  if (tid == 0) s_above = 0, s_ncand = 0;
+  if (tid == 0) s_above = 0;
   __syncthreads();
-  const int n = p.row_n[r], ps = p.row_ps[r];
+  const int n = p.row_n[r], ps = n > 0 ? p.row_ps[r] : 0;
   const unsigned long long* kr = p.keys + (int64_t)r * p.width;
-  const int lo = 1 + blockIdx.x * kSumChunk, hi = min(lo + kSumChunk, ps);
-  int above = 0;
-  if (n > 0) {
-    constexpr int kPer = kSumChunk / kSumThreads;  // keys a thread reads, all loads issued first
+  int above = 0, mine = 0;  // keys above the digit; this warp's candidates (the same in every lane)
+  for (int base = 1; base < ps; base += kPer * kSumThreads) {  // (the same trip count for every thread)
     unsigned long long keys[kPer];
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
-      const int b = lo + j * kSumThreads + tid;
-      keys[j] = b < hi ? kr[b] : 0ull;
+      const int b = base + j * kSumThreads + tid;
+      keys[j] = b < ps ? kr[b] : 0ull;
     }
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {  // warp-uniform trip count
-      const int b = lo + j * kSumThreads + tid;
-      const bool in = b < hi;
-      const unsigned long long key = keys[j];
-      // the prefix is pass 0's digit
-      const unsigned long long top = key & (dmask0 << shift0);
-      const bool cand = in && top == (prefix & (dmask0 << shift0));
-      above += in && top > (prefix & (dmask0 << shift0));
-      if (cand && histogram) atomicAdd(&s_hist[(key >> shift) & dmask], 1u);
-      const unsigned int ballot = __ballot_sync(kFullMask, cand);
-      if (ballot) {
-        unsigned int at = 0;
-        if (lane == 0) at = atomicAdd(&s_ncand, (unsigned int)__popc(ballot));
-        at = __shfl_sync(kFullMask, at, 0) + __popc(ballot & ((1u << lane) - 1u));
-        if (cand) {
-          s_ckey[at] = key;
-          s_cat[at] = ((unsigned int)r << 15) | (unsigned int)b;
-        }
-      }
+    for (int j = 0; j < kPer; ++j) {
+      const int b = base + j * kSumThreads + tid;
+      const unsigned long long top = keys[j] & top_mask;
+      const bool cand = b < ps && top == top_want;
+      above += b < ps && top > top_want;
+      if (cand && histogram) atomicAdd(&s_hist[(keys[j] >> shift) & dmask], 1u);
+      mine += __popc(__ballot_sync(kFullMask, cand));
     }
   }
   for (int off = 16; off > 0; off >>= 1) above += __shfl_xor_sync(kFullMask, above, off);
-  if (lane == 0 && above) atomicAdd(&s_above, above);
-  __syncthreads();
-  if (tid == 0) {
-    if (s_above) atomicAdd(&p.row_above[r], s_above);
-    s_base = s_ncand ? atomicAdd(&st->n_cand, s_ncand) : 0u;
+  if (lane == 0) {
+    s_warp[warp] = mine;
+    if (above) atomicAdd(&s_above, above);
   }
   __syncthreads();
-  for (unsigned int i = tid; i < s_ncand; i += kSumThreads) {
-    p.cand_key[s_base + i] = s_ckey[i];
-    p.cand_at[s_base + i] = s_cat[i];
+  if (tid == 0) {
+    int total = 0;
+    for (int w = 0; w < kSumThreads / 32; ++w) {
+      const int c = s_warp[w];
+      s_warp[w] = total;
+      total += c;
+    }
+    s_base = total ? atomicAdd(&st->n_cand, (unsigned int)total) : 0u;
+    if (s_above) atomicAdd(&p.row_above[r], s_above);
+  }
+  __syncthreads();
+  if (mine) {  // the second sweep: this warp's candidates at its place, in the order it met them
+    unsigned int at = s_base + (unsigned int)s_warp[warp];
+    for (int base = 1; base < ps; base += kPer * kSumThreads) {
+      unsigned long long keys[kPer];
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int b = base + j * kSumThreads + tid;
+        keys[j] = b < ps ? __ldcg(kr + b) : 0ull;
+      }
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int b = base + j * kSumThreads + tid;
+        const bool cand = b < ps && (keys[j] & top_mask) == top_want;
+        const unsigned int ballot = __ballot_sync(kFullMask, cand);
+        if (cand) {
+          const unsigned int i = at + (unsigned int)__popc(ballot & lanes_below());
+          p.cand_key[i] = keys[j];
+          p.cand_at[i] = ((unsigned int)r << 15) | (unsigned int)b;
+        }
+        at += (unsigned int)__popc(ballot);
+      }
+    }
   }
   if (histogram)
     for (int i = tid; i < kSumBins; i += kSumThreads)
@@ -404,11 +419,19 @@ __global__ void __launch_bounds__(kSumThreads) sum_ties_kernel(const SumParams p
     if (in && key == prefix) atomicAdd(&p.ties[at & 32767u], 1u);
   }
   if (!last_cta(&st->ticket, &s_last)) return;
-  // ties are taken from the highest block index down; thread t owns indices [t * per, t * per + per)
+  // ties are taken from the highest block index down; thread t owns indices [t * per, t * per + per), read
+  // eight at a time with all eight loads in flight
+  constexpr int kTieChunk = 8;
   const int per = (p.width + kSumThreads - 1) / kSumThreads;
   const int lo = tid * per, hi = min(lo + per, p.width);
   long long cnt = 0;
-  for (int i = lo; i < hi; ++i) cnt += __ldcg(p.ties + i);
+  for (int c0 = lo; c0 < hi; c0 += kTieChunk) {
+    unsigned int t[kTieChunk];
+#pragma unroll
+    for (int j = 0; j < kTieChunk; ++j) t[j] = c0 + j < hi ? __ldcg(p.ties + c0 + j) : 0u;
+#pragma unroll
+    for (int j = 0; j < kTieChunk; ++j) cnt += t[j];
+  }
   long long above = cnt;  // this thread's indices and those of the lanes above it
   for (int off = 1; off < 32; off <<= 1) {
     const long long v = __shfl_down_sync(kFullMask, above, off);
@@ -420,14 +443,24 @@ __global__ void __launch_bounds__(kSumThreads) sum_ties_kernel(const SumParams p
   for (int w2 = warp + 1; w2 < kSumThreads / 32; ++w2) taken += s_w[w2];
   const long long k = st->k;
   if (taken < k && taken + cnt >= k) {
-    for (int i = hi - 1; i >= lo; --i) {
-      const long long c = __ldcg(p.ties + i);
-      if (taken + c >= k) {
-        st->istar = i;
-        st->m = k - taken;
-        break;
+    bool done = false;
+    for (int c1 = hi; c1 > lo && !done; c1 -= kTieChunk) {  // chunks from the top, eight loads in flight
+      const int c0 = max(c1 - kTieChunk, lo);
+      unsigned int t[kTieChunk];
+#pragma unroll
+      for (int j = 0; j < kTieChunk; ++j) t[j] = c0 + j < c1 ? __ldcg(p.ties + c0 + j) : 0u;
+#pragma unroll
+      for (int j = kTieChunk - 1; j >= 0; --j) {
+        if (done || c0 + j >= c1) continue;
+        const long long c = t[j];
+        if (taken + c >= k) {
+          st->istar = c0 + j;
+          st->m = k - taken;
+          done = true;
+        } else {
+          taken += c;
+        }
       }
-      taken += c;
     }
   }
   if (tid == 0) st->ticket = 0;
@@ -601,7 +634,7 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
     return check_launch("cudaDeviceGetAttribute");
   if (cudaMemsetAsync(base, 0, l.zeroed, s) != cudaSuccess) return check_launch("cudaMemsetAsync(sum workspace)");
-  const size_t prep_smem = (size_t)width * sizeof(S);
+  const size_t prep_smem = ((size_t)width * sizeof(S) + 15) / 16 * 16 + pairwise_bytes(pairwise_nodes(width));
   static size_t configured[kMaxDevices] = {};
   if (configured[device] < prep_smem) {
     if (cudaFuncSetAttribute(sum_prep_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem) !=
@@ -612,7 +645,7 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
   launch_chained(sum_prep_kernel<S>, dim3(rows), dim3(kSumThreads), prep_smem, s, p);
   int rc = check_launch("sum_prep_kernel");
   if (rc == EKV_OK) {
-    launch_chained(sum_keys_pass_kernel, dim3(cdiv(width, kSumChunk), rows), dim3(kSumThreads), 0, s, p);
+    launch_chained(sum_keys_pass_kernel, dim3(rows), dim3(kSumThreads), 0, s, p);
     rc = check_launch("sum_keys_pass_kernel");
   }
   const int cand_grid = 2 * sms;

@@ -13,15 +13,37 @@
 
 namespace ekv {
 
-constexpr int kPairwiseMaxNodes = 1024;  // up to 32768 values: at most 512 leaves of more than 64 values
 constexpr int kPairwiseMaxLevels = 16;
 
-struct PairwiseTree {  // shared-memory scratch of block_pairwise_sum
-  int lo[kPairwiseMaxNodes], len[kPairwiseMaxNodes], left[kPairwiseMaxNodes];
-  double val[kPairwiseMaxNodes];
-  int level[kPairwiseMaxLevels + 2];
-  int nodes, depth;
+// The most nodes numpy's recursion makes for up to n values: one leaf up to 128 values, and every split of
+// more than 128 values gives halves of at least 64, so at most 129 nodes for 8192 values, 257 for 16384
+// and 513 for 32768.
+__host__ __device__ constexpr int pairwise_nodes(int n) {
+  return n <= 128 ? 1 : (n <= 8192 ? 129 : (n <= 16384 ? 257 : 513));
+}
+
+// Bytes of block_pairwise_sum's scratch for up to `nodes` nodes: the node values (float64), ranges and
+// children, the levels and two counters; a multiple of 8.
+__host__ __device__ constexpr size_t pairwise_bytes(int nodes) {
+  return (size_t)nodes * 8 + (((size_t)nodes * 3 + kPairwiseMaxLevels + 4) * 4 + 7) / 8 * 8;
+}
+
+// block_pairwise_sum's scratch, carved from pairwise_bytes(nodes) of 8-byte aligned shared memory.
+struct PairwiseScratch {
+  double* val;
+  int *lo, *len, *left, *level, *meta;  // meta: the nodes made, the depth
 };
+
+__device__ __forceinline__ PairwiseScratch pairwise_scratch(void* mem, int nodes) {
+  PairwiseScratch t;
+  t.val = static_cast<double*>(mem);
+  t.lo = reinterpret_cast<int*>(t.val + nodes);
+  t.len = t.lo + nodes;
+  t.left = t.len + nodes;
+  t.level = t.left + nodes;
+  t.meta = t.level + kPairwiseMaxLevels + 2;
+  return t;
+}
 
 // One leaf of at most 128 values; value(i) gives the i-th value as a double.
 template <typename V>
@@ -43,13 +65,13 @@ __device__ double pairwise_leaf(const V& value, int lo, int len) {
   return res;
 }
 
-// The sum of value(0 .. n) (n <= 32768) as numpy computes it; every thread of the CTA calls it and
-// gets the sum. THREADS = blockDim.x.
+// The sum of value(0 .. n) as numpy computes it, with a scratch of pairwise_nodes(n) nodes or more; every
+// thread of the CTA calls it and gets the sum. THREADS = blockDim.x.
 template <int THREADS, typename V>
-__device__ double block_pairwise_sum(PairwiseTree& t, int n, const V& value) {
+__device__ double block_pairwise_sum(const PairwiseScratch& t, int n, const V& value) {
   const int tid = threadIdx.x;
   __syncthreads();  // the scratch may still be read by an earlier call
-  if (tid == 0) t.lo[0] = 0, t.len[0] = n, t.nodes = 1, t.level[0] = 0, t.level[1] = 1, t.depth = 1;
+  if (tid == 0) t.lo[0] = 0, t.len[0] = n, t.meta[0] = 1, t.level[0] = 0, t.level[1] = 1, t.meta[1] = 1;
   __syncthreads();
   for (int d = 0; d < kPairwiseMaxLevels; ++d) {  // split the level's nodes; children go after the level
     const int a = t.level[d], b = t.level[d + 1];
@@ -61,19 +83,20 @@ __device__ double block_pairwise_sum(PairwiseTree& t, int n, const V& value) {
       } else {
         int n2 = len / 2;
         n2 -= n2 % 8;
-        const int c = atomicAdd(&t.nodes, 2);
+        const int c = atomicAdd(&t.meta[0], 2);
         t.lo[c] = lo, t.len[c] = n2, t.lo[c + 1] = lo + n2, t.len[c + 1] = len - n2;
         t.left[i] = c;
       }
     }
     __syncthreads();
-    if (tid == 0) t.level[d + 2] = t.nodes, t.depth = d + 1;
+    if (tid == 0) t.level[d + 2] = t.meta[0], t.meta[1] = d + 1;
     __syncthreads();
   }
-  for (int i = tid; i < t.nodes; i += THREADS)
+  const int nodes = t.meta[0];
+  for (int i = tid; i < nodes; i += THREADS)
     if (t.left[i] < 0) t.val[i] = pairwise_leaf(value, t.lo[i], t.len[i]);
   __syncthreads();
-  for (int d = t.depth - 1; d >= 0; --d) {  // each inner node: left + right, deepest level first
+  for (int d = t.meta[1] - 1; d >= 0; --d) {  // each inner node: left + right, deepest level first
     for (int i = t.level[d] + tid; i < t.level[d + 1]; i += THREADS)
       if (t.left[i] >= 0) t.val[i] = t.val[t.left[i]] + t.val[t.left[i] + 1];
     __syncthreads();

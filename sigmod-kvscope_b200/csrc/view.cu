@@ -338,7 +338,7 @@ __host__ __device__ constexpr size_t view_smem_bytes(int width) {
   // keys (the staged scores, then the keys, then the view row) + the table row (+ the pairwise-sum tree), each
   // padded to whole segments
   return (size_t)((width + kViewSeg - 1) / kViewSeg * kViewSeg) * (sizeof(K) + 4) +
-         (sizeof(K) == 8 ? sizeof(PairwiseTree) : 0);
+         (sizeof(K) == 8 ? pairwise_bytes(pairwise_nodes(width)) : 0);
 }
 
 // One CTA per row.
@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_ker
     ViewKey<K>::digit(0, shift0, dmask0);
     if constexpr (kWide) {
       const double* s_x = reinterpret_cast<const double*>(keys);
-      PairwiseTree& tree = *reinterpret_cast<PairwiseTree*>(smem_view + (size_t)w_pad * (sizeof(K) + 4));
+      const PairwiseScratch tree = pairwise_scratch(smem_view + (size_t)w_pad * (sizeof(K) + 4), pairwise_nodes(W));
       const double total = p.presummed ? 1.0 : block_pairwise_sum<kViewThreads>(tree, n_a, [&](int i) {
         const double s = s_x[i];
         return s > 0.0 ? s : 0.0;

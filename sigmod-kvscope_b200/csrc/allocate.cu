@@ -419,18 +419,37 @@ __global__ void __launch_bounds__(kSumThreads) sum_ties_kernel(const SumParams p
     if (in && key == prefix) atomicAdd(&p.ties[at & 32767u], 1u);
   }
   if (!last_cta(&st->ticket, &s_last)) return;
-  // ties are taken from the highest block index down; thread t owns indices [t * per, t * per + per), read
-  // eight at a time with all eight loads in flight
-  constexpr int kTieChunk = 8;
-  const int per = (p.width + kSumThreads - 1) / kSumThreads;
-  const int lo = tid * per, hi = min(lo + per, p.width);
+  // ties are taken from the highest block index down; thread t owns indices [t * per, t * per + per): up to
+  // 32 of them held in registers (read as eight 16-byte loads, all in flight), more read eight at a time
+  constexpr int kTieRegs = 32, kTieChunk = 8;
+  const bool in_regs = p.width <= kSumThreads * kTieRegs;
+  const int per = in_regs ? kTieRegs : (p.width + kSumThreads - 1) / kSumThreads;
+  const int lo = min(tid * per, p.width), hi = min(lo + per, p.width);
+  unsigned int t_reg[kTieRegs];
   long long cnt = 0;
-  for (int c0 = lo; c0 < hi; c0 += kTieChunk) {
-    unsigned int t[kTieChunk];
+  if (in_regs) {
 #pragma unroll
-    for (int j = 0; j < kTieChunk; ++j) t[j] = c0 + j < hi ? __ldcg(p.ties + c0 + j) : 0u;
+    for (int j = 0; j < kTieRegs; j += 4) {
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (lo + j + 3 < hi) {
+        v = __ldcg(reinterpret_cast<const uint4*>(p.ties + lo + j));
+      } else {
+        v.x = lo + j < hi ? __ldcg(p.ties + lo + j) : 0u;
+        v.y = lo + j + 1 < hi ? __ldcg(p.ties + lo + j + 1) : 0u;
+        v.z = lo + j + 2 < hi ? __ldcg(p.ties + lo + j + 2) : 0u;
+      }
+      t_reg[j] = v.x, t_reg[j + 1] = v.y, t_reg[j + 2] = v.z, t_reg[j + 3] = v.w;
+    }
 #pragma unroll
-    for (int j = 0; j < kTieChunk; ++j) cnt += t[j];
+    for (int j = 0; j < kTieRegs; ++j) cnt += t_reg[j];
+  } else {
+    for (int c0 = lo; c0 < hi; c0 += kTieChunk) {
+      unsigned int t[kTieChunk];
+#pragma unroll
+      for (int j = 0; j < kTieChunk; ++j) t[j] = c0 + j < hi ? __ldcg(p.ties + c0 + j) : 0u;
+#pragma unroll
+      for (int j = 0; j < kTieChunk; ++j) cnt += t[j];
+    }
   }
   long long above = cnt;  // this thread's indices and those of the lanes above it
   for (int off = 1; off < 32; off <<= 1) {
@@ -443,22 +462,38 @@ __global__ void __launch_bounds__(kSumThreads) sum_ties_kernel(const SumParams p
   for (int w2 = warp + 1; w2 < kSumThreads / 32; ++w2) taken += s_w[w2];
   const long long k = st->k;
   if (taken < k && taken + cnt >= k) {
-    bool done = false;
-    for (int c1 = hi; c1 > lo && !done; c1 -= kTieChunk) {  // chunks from the top, eight loads in flight
-      const int c0 = max(c1 - kTieChunk, lo);
-      unsigned int t[kTieChunk];
+    if (in_regs) {
+      bool done = false;
 #pragma unroll
-      for (int j = 0; j < kTieChunk; ++j) t[j] = c0 + j < c1 ? __ldcg(p.ties + c0 + j) : 0u;
-#pragma unroll
-      for (int j = kTieChunk - 1; j >= 0; --j) {
-        if (done || c0 + j >= c1) continue;
-        const long long c = t[j];
+      for (int j = kTieRegs - 1; j >= 0; --j) {
+        if (done || lo + j >= hi) continue;
+        const long long c = t_reg[j];
         if (taken + c >= k) {
-          st->istar = c0 + j;
+          st->istar = lo + j;
           st->m = k - taken;
           done = true;
         } else {
           taken += c;
+        }
+      }
+    } else {
+      bool done = false;
+      for (int c1 = hi; c1 > lo && !done; c1 -= kTieChunk) {  // chunks from the top, eight loads in flight
+        const int c0 = max(c1 - kTieChunk, lo);
+        unsigned int t[kTieChunk];
+#pragma unroll
+        for (int j = 0; j < kTieChunk; ++j) t[j] = c0 + j < c1 ? __ldcg(p.ties + c0 + j) : 0u;
+#pragma unroll
+        for (int j = kTieChunk - 1; j >= 0; --j) {
+          if (done || c0 + j >= c1) continue;
+          const long long c = t[j];
+          if (taken + c >= k) {
+            st->istar = c0 + j;
+            st->m = k - taken;
+            done = true;
+          } else {
+            taken += c;
+          }
         }
       }
     }

@@ -319,6 +319,29 @@ int ekv_allocate_sum_f64(const double* scores, int64_t score_stride, const int32
                          void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * ekv_view_build_sum_budget -- the controller's default decision and its view in one call: one `sum`
+ * budget over every measured row (Controller._allocate, observe/controller.py:398-451, with
+ * allocate(objective="sum"), observe/allocation.py:94-118), then compact_block_table
+ * (runtime/block_view.py:36-56) of every row.
+ *
+ * The select of ekv_allocate_sum / ekv_allocate_sum_f64 (score_bytes 4: float32 scores, 8: float64,
+ * score_rows as in ekv_allocate_sum_f64) finds the threshold gain; the view kernel then keeps, in every
+ * request, the unpinned blocks whose gain is above it (equal gains as the reference hands them out: newer
+ * blocks first, then earlier requests), with no per-row ranking and no quotas. The view, its lengths,
+ * full_rows and released as in ekv_view_build; mask_out (may be NULL) receives the committed mask. The
+ * result is the view ekv_view_build (_f64) writes with ekv_allocate_sum's (_f64's) quotas and the same
+ * pins and weights. width <= 16384. Same workspace as ekv_allocate_sum.
+ */
+int ekv_view_build_sum_budget(const void* scores, int score_bytes, int64_t score_stride, const int32_t* score_rows,
+                              const double* weights, const int32_t* row_blocks, const int32_t* measured_blocks,
+                              int recent_blocks, int cap_above_blocks, double budget_fraction, int64_t budget,
+                              const int32_t* table, int64_t table_stride, const int32_t* seq_lens,
+                              const uint8_t* full_rows, const uint8_t* released, int64_t released_stride, int rows,
+                              int width, int block_size, int32_t* view, int64_t view_stride, int32_t* view_lens,
+                              uint8_t* mask_out, int64_t mask_stride, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/*
  * ekv_allocate_maxmin_f64 -- ekv_allocate_maxmin over float64 scores; score_rows as in
  * ekv_allocate_sum_f64. The quotas are for ekv_view_build_f64 with EKV_POLICY_UNIFORM. width <= 8192,
  * rows <= 4096. Same workspace as ekv_allocate_maxmin.

@@ -39,4 +39,4 @@ int current_device(int* device) {
 
 extern "C" const char* ekv_last_error_string(void) { return ekv::g_error; }
 
-extern "C" int ekv_abi_version(void) { return 6; }
+extern "C" int ekv_abi_version(void) { return 7; }

@@ -28,27 +28,15 @@
 #include "ekv_common.cuh"
 #include "pairwise.cuh"
 #include "pins.cuh"
+#include "sum_state.cuh"
 
 namespace ekv {
 
 constexpr int kSumThreads = 256;
-constexpr int kSumBins = 2048;
+constexpr int kSumBins = 2048;  // digits of 11 bits (the last of 8)
 constexpr int kSumPasses = 6;
 constexpr int kSumMaxWidth = 32768;
 constexpr int kSumMaxRows = 1 << 17;  // a candidate's place is (row << 15) | block
-
-enum SumMode : int { kSumSelect = 0, kSumNone = 1, kSumAll = 2 };
-
-struct SumState {
-  unsigned long long prefix, mask;  // the threshold's known bits
-  long long k;                      // keys still to choose at the threshold's prefix
-  long long total_open, must, blocks;
-  int mode, found;
-  int istar;       // the lowest block index whose ties are (partly) taken
-  long long m;     // ties taken at istar, from the earliest rows
-  unsigned int n_cand;
-  unsigned int ticket;
-};
 
 struct SumParams {
   const void* scores;          // float or double [.][score_s0] (sum_prep_kernel<float> / <double>)
@@ -82,6 +70,9 @@ struct SumParams {
   // allocation, ekv_allocate_pinned_f64): no total is taken, and a pinned block outranks every gain
   bool presummed;
   const long long* budget_add;  // may be NULL: blocks added on the device to a budget given as a count
+  // the quotas are wanted (their counts need every tie pass); without them, a select that ended exactly on the
+  // threshold (every key with the prefix taken) leaves nothing for the tie passes to decide
+  bool need_ties;
 };
 
 struct SumLayout {
@@ -131,6 +122,9 @@ __device__ __forceinline__ unsigned long long gain_key(S s, double total, double
   return g > 0.0 ? (unsigned long long)__double_as_longlong(g) : 0ull;
 }
 
+// The digits of the 63-bit keys, most significant first: bits 52-62 (the exponent), 41-51, 30-40, 19-29,
+// 8-18 and 0-7. (A first digit of 13 bits leaves a quarter of the candidates, but the rows' finer
+// histograms put four times as many atomics on the global one, and the pass costs more than it saves.)
 __device__ __forceinline__ void digit_of(int pass, int& shift, unsigned long long& dmask) {
   shift = pass < 5 ? 52 - 11 * pass : 0;
   dmask = pass < 5 ? 2047ull : 255ull;
@@ -147,7 +141,8 @@ __device__ __forceinline__ bool last_cta(unsigned int* ticket, bool* s_last) {
 }
 
 // In the last CTA: the digit holding the k-th largest of the keys counted in `hist` (thread t owns
-// bins [8t, 8t + 8)); clears `hist` and updates the threshold. kSumThreads * 8 == kSumBins.
+// bins [kPer t, kPer t + kPer)); clears `hist` and updates the threshold.
+template <int kPer = kSumBins / kSumThreads>
 __device__ void pick_digit(SumState* st, unsigned int* hist, int pass) {
   __shared__ long long s_w[kSumThreads / 32];
   __shared__ int s_pick;
@@ -157,10 +152,14 @@ __device__ void pick_digit(SumState* st, unsigned int* hist, int pass) {
   int shift;
   unsigned long long dmask;
   digit_of(pass, shift, dmask);
-  unsigned int h[8];
+  unsigned int h[kPer];
   long long sum = 0;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) h[j] = __ldcg(hist + 8 * tid + j), sum += h[j];
+  for (int j = 0; j < kPer; j += 4) {
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(hist + kPer * tid + j));
+    h[j] = v.x, h[j + 1] = v.y, h[j + 2] = v.z, h[j + 3] = v.w;
+    sum += (long long)v.x + v.y + v.z + v.w;
+  }
   long long above = sum;  // this thread's bins and those of the lanes above it
   for (int off = 1; off < 32; off <<= 1) {
     const long long v = __shfl_down_sync(kFullMask, above, off);
@@ -172,9 +171,9 @@ __device__ void pick_digit(SumState* st, unsigned int* hist, int pass) {
   for (int w2 = warp + 1; w2 < kSumThreads / 32; ++w2) gt += s_w[w2];
   const long long k = st->k;
 #pragma unroll
-  for (int j = 7; j >= 0; --j) {
+  for (int j = kPer - 1; j >= 0; --j) {
     if (gt < k && gt + h[j] >= k) {
-      s_pick = 8 * tid + j;
+      s_pick = kPer * tid + j;
       s_above = gt;
       s_count = h[j];
     }
@@ -182,13 +181,14 @@ __device__ void pick_digit(SumState* st, unsigned int* hist, int pass) {
   }
   __syncthreads();
 #pragma unroll
-  for (int j = 0; j < 8; ++j) hist[8 * tid + j] = 0;  // ready for the next pass
+  for (int j = 0; j < kPer; j += 4) *reinterpret_cast<uint4*>(hist + kPer * tid + j) = make_uint4(0, 0, 0, 0);
   if (tid == 0) {
     const long long k2 = k - s_above;
     st->prefix |= (unsigned long long)s_pick << shift;
     st->mask |= dmask << shift;
     st->k = k2;
-    st->found = (long long)s_count == k2 || pass == kSumPasses - 1;  // every key with the prefix is taken
+    st->exact = (long long)s_count == k2;  // every key with the prefix is taken
+    st->found = st->exact || pass == kSumPasses - 1;
   }
 }
 
@@ -271,18 +271,22 @@ __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p
   if (st->mode == kSumSelect) pick_digit(st, p.hist, 0);  // pass 0 of the select
 }
 
-// Pass 1 over every key: a CTA per row. It counts the row's keys above the digit of pass 0 and appends the
-// keys of that digit to the candidates in two sweeps: the first counts them (and their next digit), one
-// atomic gives the row its place in the list, the second (the keys again, from L2) writes them there.
+// Pass 1 over every key: a CTA per row. It counts the row's keys above the digit of pass 0 and the next digit
+// of the keys of that digit, and appends those keys to the candidates: gathered in shared memory as they are
+// met, then copied to the row's place in the list (one atomic); a row with more than kSumStage of them is
+// read again (from L2) to write them there.
 __global__ void __launch_bounds__(kSumThreads) sum_keys_pass_kernel(const SumParams p) {
   chain_release();
   chain_wait();  // what the launch before this one wrote
   constexpr int pass = 1;
   constexpr int kPer = 8;  // keys a thread has in flight
+  constexpr int kSumStage = 2048;
   __shared__ unsigned int s_hist[kSumBins];
+  __shared__ unsigned long long s_ckey[kSumStage];
+  __shared__ unsigned int s_cat[kSumStage];
   __shared__ int s_warp[kSumThreads / 32 + 1];  // each warp's candidates, then the warps' places
   __shared__ int s_above;
-  __shared__ unsigned int s_base;
+  __shared__ unsigned int s_base, s_staged;
   __shared__ bool s_last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.x;
   SumState* st = p.state;
@@ -296,7 +300,7 @@ __global__ void __launch_bounds__(kSumThreads) sum_keys_pass_kernel(const SumPar
   digit_of(0, shift0, dmask0);
   const unsigned long long top_mask = dmask0 << shift0, top_want = st->prefix & top_mask;
   for (int i = tid; i < kSumBins; i += kSumThreads) s_hist[i] = 0;
-  if (tid == 0) s_above = 0;
+  if (tid == 0) s_above = 0, s_staged = 0;
   __syncthreads();
   const int n = p.row_n[r], ps = n > 0 ? p.row_ps[r] : 0;
   const unsigned long long* kr = p.keys + (int64_t)r * p.width;
@@ -315,7 +319,17 @@ __global__ void __launch_bounds__(kSumThreads) sum_keys_pass_kernel(const SumPar
       const bool cand = b < ps && top == top_want;
       above += b < ps && top > top_want;
       if (cand && histogram) atomicAdd(&s_hist[(keys[j] >> shift) & dmask], 1u);
-      mine += __popc(__ballot_sync(kFullMask, cand));
+      const unsigned int ballot = __ballot_sync(kFullMask, cand);
+      if (ballot) {
+        unsigned int at = 0;
+        if (lane == 0) at = atomicAdd(&s_staged, (unsigned int)__popc(ballot));
+        at = __shfl_sync(kFullMask, at, 0) + (unsigned int)__popc(ballot & lanes_below());
+        if (cand && at < (unsigned int)kSumStage) {
+          s_ckey[at] = keys[j];
+          s_cat[at] = ((unsigned int)r << 15) | (unsigned int)b;
+        }
+      }
+      mine += __popc(ballot);
     }
   }
   for (int off = 16; off > 0; off >>= 1) above += __shfl_xor_sync(kFullMask, above, off);
@@ -335,7 +349,13 @@ __global__ void __launch_bounds__(kSumThreads) sum_keys_pass_kernel(const SumPar
     if (s_above) atomicAdd(&p.row_above[r], s_above);
   }
   __syncthreads();
-  if (mine) {  // the second sweep: this warp's candidates at its place, in the order it met them
+  const unsigned int staged = s_staged;
+  if (staged <= (unsigned int)kSumStage) {
+    for (unsigned int i = tid; i < staged; i += kSumThreads) {
+      p.cand_key[s_base + i] = s_ckey[i];
+      p.cand_at[s_base + i] = s_cat[i];
+    }
+  } else if (mine) {  // the second sweep: this warp's candidates at its place, in the order it met them
     unsigned int at = s_base + (unsigned int)s_warp[warp];
     for (int base = 1; base < ps; base += kPer * kSumThreads) {
       unsigned long long keys[kPer];
@@ -403,7 +423,7 @@ __global__ void __launch_bounds__(kSumThreads) sum_ties_kernel(const SumParams p
   __shared__ bool s_last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   SumState* st = p.state;
-  if (st->mode != kSumSelect) return;
+  if (st->mode != kSumSelect || (!p.need_ties && st->exact)) return;  // (uniform over the grid)
   const unsigned long long prefix = st->prefix, mask = st->mask;
   const unsigned int count = st->n_cand;
   for (unsigned int base = blockIdx.x * kSumThreads; base < count; base += gridDim.x * kSumThreads) {
@@ -507,7 +527,7 @@ __global__ void __launch_bounds__(kSumThreads) sum_kept_kernel(const SumParams p
   chain_wait();  // what the launch before this one wrote
   const int tid = threadIdx.x;
   const SumState* st = p.state;
-  if (st->mode != kSumSelect) return;
+  if (st->mode != kSumSelect || (!p.need_ties && st->exact)) return;
   const unsigned long long prefix = st->prefix, mask = st->mask;
   const unsigned int istar = (unsigned int)st->istar, count = st->n_cand;
   const int lane = tid & 31;
@@ -530,6 +550,7 @@ __global__ void __launch_bounds__(1024) sum_quota_kernel(const SumParams p) {
   const int tid = threadIdx.x;
   const SumState* st = p.state;
   const int mode = st->mode;
+  if (!p.need_ties && (mode != kSumSelect || st->exact)) return;  // no quotas wanted, no ties to hand out
   const long long m = st->m;
   int carry = 0;
   for (int base = 0; base < p.rows; base += 1024) {
@@ -542,14 +563,14 @@ __global__ void __launch_bounds__(1024) sum_quota_kernel(const SumParams p) {
     carry += total;
     if (!in) continue;
     if (n == 0) {
-      p.quota[r] = -1;  // not a request: it reads in full
+      if (p.quota) p.quota[r] = -1;  // not a request: it reads in full
     } else if (mode != kSumSelect) {
       const int ps = p.row_ps[r];
-      p.quota[r] = mode == kSumAll ? (ps > 1 ? ps - 1 : 0) : 0;
+      if (p.quota) p.quota[r] = mode == kSumAll ? (ps > 1 ? ps - 1 : 0) : 0;
     } else {
       const int take = at && before < m ? 1 : 0;
-      p.quota[r] = p.row_above[r] + p.row_kept[r] + take;
-      p.row_at[r] = take;  // from here on: the row's tie at i* is taken (sum_mask_kernel)
+      if (p.quota) p.quota[r] = p.row_above[r] + p.row_kept[r] + take;
+      p.row_at[r] = take;  // from here on: the row's tie at i* is taken (sum_mask_kernel, the view)
     }
   }
 }
@@ -615,6 +636,20 @@ __global__ void __launch_bounds__(kSumThreads) sum_mask_kernel(const SumParams p
 
 using namespace ekv;
 
+// The view a shared-budget build writes (ekv_view_build_sum_budget).
+struct SumViewOut {
+  const int32_t* table;
+  int64_t table_s0;
+  const int32_t* seq_lens;
+  const uint8_t* full_rows;
+  const uint8_t* released;
+  int64_t released_s0;
+  int block_size;
+  int32_t* view;
+  int64_t view_s0;
+  int32_t* view_lens;
+};
+
 extern "C" size_t ekv_allocate_sum_workspace_bytes(int rows, int width) {
   if (rows <= 0 || width <= 0) return 0;
   return sum_layout(rows, width).bytes;
@@ -626,10 +661,10 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
                         int cap_above_blocks, double budget_fraction, int64_t budget, int rows, int width,
                         int32_t* quota, uint8_t* mask_out, int64_t mask_stride, void* workspace,
                         size_t workspace_bytes, void* stream, bool presummed = false,
-                        const long long* budget_add = nullptr) {
+                        const long long* budget_add = nullptr, const SumViewOut* view = nullptr) {
   constexpr int max_width = sizeof(S) == 8 ? kSumMaxWidth / 2 : kSumMaxWidth;  // the prep kernel stages a row
   clear_error();
-  if (!scores || !row_blocks || !quota) return fail(EKV_EINVAL, "a required pointer is NULL");
+  if (!scores || !row_blocks || (!quota && !mask_out && !view)) return fail(EKV_EINVAL, "a required pointer is NULL");
   if (rows <= 0 || width <= 0) return fail(EKV_EINVAL, "rows and width must be positive");
   if (width > max_width) return fail(EKV_ENOTSUP, "width %d > %d", width, max_width);
   if (rows > kSumMaxRows) return fail(EKV_ENOTSUP, "rows %d > %d", rows, kSumMaxRows);
@@ -648,7 +683,7 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
   p.measured = measured_blocks; p.recent = recent_blocks; p.cap = cap_above_blocks;
   p.fraction = budget_fraction; p.budget = (long long)budget; p.rows = rows; p.width = width; p.quota = quota;
   p.mask_out = mask_out; p.mask_s0 = mask_stride;
-  p.presummed = presummed; p.budget_add = budget_add;
+  p.presummed = presummed; p.budget_add = budget_add; p.need_ties = quota != nullptr;
   p.state = reinterpret_cast<SumState*>(base + l.state);
   p.hist = reinterpret_cast<unsigned int*>(base + l.hist);
   p.ties = reinterpret_cast<unsigned int*>(base + l.ties);
@@ -694,7 +729,12 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
   launch_chained(sum_kept_kernel, dim3(cand_grid), dim3(kSumThreads), 0, s, p);
   if ((rc = check_launch("sum_kept_kernel")) != EKV_OK) return rc;
   launch_chained(sum_quota_kernel, dim3(1), dim3(1024), 0, s, p);
-  if ((rc = check_launch("sum_quota_kernel")) != EKV_OK || mask_out == nullptr) return rc;
+  if ((rc = check_launch("sum_quota_kernel")) != EKV_OK) return rc;
+  if (view != nullptr)  // the view (and the mask) straight from the threshold
+    return launch_sum_view(view->table, view->table_s0, view->seq_lens, view->full_rows, view->released,
+                           view->released_s0, rows, width, view->block_size, view->view, view->view_s0,
+                           view->view_lens, mask_out, mask_stride, p.state, p.keys, p.row_n, p.row_ps, p.row_at, s);
+  if (mask_out == nullptr) return rc;
   launch_chained(sum_mask_kernel, dim3(cdiv(width, kSumMaskSpan), rows), dim3(kSumThreads), 0, s, p);
   return check_launch("sum_mask_kernel");
 }
@@ -730,4 +770,32 @@ extern "C" int ekv_allocate_sum_f64(const double* scores, int64_t score_stride, 
   return allocate_sum<double>(scores, score_stride, score_rows, weights, row_blocks, measured_blocks,
                               recent_blocks, cap_above_blocks, budget_fraction, budget, rows, width, quota,
                               mask_out, mask_stride, workspace, workspace_bytes, stream);
+}
+
+extern "C" int ekv_view_build_sum_budget(const void* scores, int score_bytes, int64_t score_stride,
+                                         const int32_t* score_rows, const double* weights, const int32_t* row_blocks,
+                                         const int32_t* measured_blocks, int recent_blocks, int cap_above_blocks,
+                                         double budget_fraction, int64_t budget, const int32_t* table,
+                                         int64_t table_stride, const int32_t* seq_lens, const uint8_t* full_rows,
+                                         const uint8_t* released, int64_t released_stride, int rows, int width,
+                                         int block_size, int32_t* view, int64_t view_stride, int32_t* view_lens,
+                                         uint8_t* mask_out, int64_t mask_stride, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (!table || !seq_lens || !view || !view_lens) return fail(EKV_EINVAL, "a required pointer is NULL");
+  if (score_bytes != 4 && score_bytes != 8) return fail(EKV_EINVAL, "score_bytes %d: 4 (float32) or 8 (float64)", score_bytes);
+  if (score_bytes == 4 && score_rows) return fail(EKV_EINVAL, "score_rows reads float64 scores only");
+  if (block_size <= 0) return fail(EKV_EINVAL, "block_size must be positive");
+  if (width > 16384) return fail(EKV_ENOTSUP, "width %d > 16384 (a view row is staged in shared memory)", width);
+  if (table_stride < width || view_stride < width) return fail(EKV_EINVAL, "a row stride is below the width");
+  if (released && released_stride < width) return fail(EKV_EINVAL, "released_stride < width");
+  const SumViewOut out{table, table_stride, seq_lens, full_rows, released, released_stride, block_size, view,
+                       view_stride, view_lens};
+  if (score_bytes == 4)
+    return allocate_sum<float>(static_cast<const float*>(scores), score_stride, nullptr, weights, row_blocks,
+                               measured_blocks, recent_blocks, cap_above_blocks, budget_fraction, budget, rows, width,
+                               nullptr, mask_out, mask_stride, workspace, workspace_bytes, stream, false, nullptr, &out);
+  return allocate_sum<double>(static_cast<const double*>(scores), score_stride, score_rows, weights, row_blocks,
+                              measured_blocks, recent_blocks, cap_above_blocks, budget_fraction, budget, rows, width,
+                              nullptr, mask_out, mask_stride, workspace, workspace_bytes, stream, false, nullptr, &out);
 }

@@ -4,9 +4,9 @@
 // 0.0; up to 128 values eight accumulators r[j] += a[i + j] over whole groups of 8, combined as
 // ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)), then the rest one by one; above 128 values
 // pairwise_sum(a, n2) + pairwise_sum(a + n2, n - n2) with n2 = n / 2 rounded down to a multiple of 8.
-// Here the tree is built one level at a time (every node of a level splits in parallel and records its
-// children), the leaves are summed in parallel, and the levels are combined from the bottom up: the
-// same additions in the same order as numpy's recursion.
+// Here the tree is built one level at a time (every node of a level splits and records its children),
+// the leaves are summed in parallel, and the levels are combined from the bottom up: the same additions
+// in the same order as numpy's recursion.
 #pragma once
 
 #include "ekv_common.cuh"
@@ -66,41 +66,62 @@ __device__ double pairwise_leaf(const V& value, int lo, int len) {
 }
 
 // The sum of value(0 .. n) as numpy computes it, with a scratch of pairwise_nodes(n) nodes or more; every
-// thread of the CTA calls it and gets the sum. THREADS = blockDim.x.
+// thread of the CTA calls it and gets the sum. THREADS = blockDim.x (a multiple of 32). The tree (a few
+// hundred nodes at most) is built and combined by warp 0 alone, a level at a time with warp barriers; the
+// leaves are summed by the whole CTA.
 template <int THREADS, typename V>
 __device__ double block_pairwise_sum(const PairwiseScratch& t, int n, const V& value) {
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
   __syncthreads();  // the scratch may still be read by an earlier call
-  if (tid == 0) t.lo[0] = 0, t.len[0] = n, t.meta[0] = 1, t.level[0] = 0, t.level[1] = 1, t.meta[1] = 1;
-  __syncthreads();
-  for (int d = 0; d < kPairwiseMaxLevels; ++d) {  // split the level's nodes; children go after the level
-    const int a = t.level[d], b = t.level[d + 1];
-    if (a == b) break;
-    for (int i = a + tid; i < b; i += THREADS) {
-      const int lo = t.lo[i], len = t.len[i];
-      if (len <= 128) {
-        t.left[i] = -1;
-      } else {
-        int n2 = len / 2;
-        n2 -= n2 % 8;
-        const int c = atomicAdd(&t.meta[0], 2);
-        t.lo[c] = lo, t.len[c] = n2, t.lo[c + 1] = lo + n2, t.len[c + 1] = len - n2;
-        t.left[i] = c;
+  if (tid < 32) {
+    // level d holds nodes [level[d], level[d + 1]); a node of more than 128 values splits, its children
+    // placed after the level in node order (a ballot gives each splitting node its children's place)
+    if (lane == 0) t.lo[0] = 0, t.len[0] = n, t.level[0] = 0, t.level[1] = 1;
+    __syncwarp();
+    int nodes = 1, depth = 1;
+    for (int d = 0; d < kPairwiseMaxLevels; ++d) {
+      const int a = t.level[d], b = t.level[d + 1];
+      if (a == b) break;
+      int next = b;
+      for (int i0 = a; i0 < b; i0 += 32) {
+        const int i = i0 + lane;
+        const int len = i < b ? t.len[i] : 0;
+        const bool split = len > 128;
+        const unsigned int ballot = __ballot_sync(kFullMask, split);
+        if (i < b) {
+          if (split) {
+            const int c = next + 2 * __popc(ballot & lanes_below());
+            int n2 = len / 2;
+            n2 -= n2 % 8;
+            const int lo = t.lo[i];
+            t.lo[c] = lo, t.len[c] = n2, t.lo[c + 1] = lo + n2, t.len[c + 1] = len - n2;
+            t.left[i] = c;
+          } else {
+            t.left[i] = -1;
+          }
+        }
+        next += 2 * __popc(ballot);
       }
+      if (lane == 0) t.level[d + 2] = next;
+      nodes = next;
+      depth = d + 1;
+      __syncwarp();
     }
-    __syncthreads();
-    if (tid == 0) t.level[d + 2] = t.meta[0], t.meta[1] = d + 1;
-    __syncthreads();
+    if (lane == 0) t.meta[0] = nodes, t.meta[1] = depth;
   }
+  __syncthreads();
   const int nodes = t.meta[0];
   for (int i = tid; i < nodes; i += THREADS)
     if (t.left[i] < 0) t.val[i] = pairwise_leaf(value, t.lo[i], t.len[i]);
   __syncthreads();
-  for (int d = t.meta[1] - 1; d >= 0; --d) {  // each inner node: left + right, deepest level first
-    for (int i = t.level[d] + tid; i < t.level[d + 1]; i += THREADS)
-      if (t.left[i] >= 0) t.val[i] = t.val[t.left[i]] + t.val[t.left[i] + 1];
-    __syncthreads();
+  if (tid < 32) {
+    for (int d = t.meta[1] - 1; d >= 0; --d) {  // each inner node: left + right, deepest level first
+      for (int i = t.level[d] + lane; i < t.level[d + 1]; i += 32)
+        if (t.left[i] >= 0) t.val[i] = t.val[t.left[i]] + t.val[t.left[i] + 1];
+      __syncwarp();
+    }
   }
+  __syncthreads();
   return t.val[0];
 }
 

@@ -14,6 +14,7 @@
 #include "ekv_common.cuh"
 #include "pairwise.cuh"
 #include "pins.cuh"
+#include "sum_state.cuh"
 
 namespace ekv {
 
@@ -218,6 +219,13 @@ struct ViewParams {
   int cap;
   // float64 rows that already hold each request's shares (the pinned allocation): ranked as they are
   bool presummed;
+  // threshold mode (launch_sum_view): the keep decision of a shared `sum` budget's select, from its state, gain
+  // keys [rows][width] and per-row blocks, pin starts and taken ties; no ranking
+  const SumState* sum_state;
+  const unsigned long long* sum_keys;
+  const int32_t* sum_row_n;
+  const int32_t* sum_row_ps;
+  const int32_t* sum_row_at;
 };
 
 // Row flags of ekv_decode_view (full_rows): the row reads every block / decodes / is audited.
@@ -388,10 +396,24 @@ __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_ker
   const int laid = !has_view ? 0 : min((live + 3) & ~3, W);            // positions laid out
 
   // ---- the row's committed mask: pins + selection (ranking mode) or the given mask ---------------
-  const bool rank_mode = p.keep == nullptr;
+  const bool sum_mode = p.sum_state != nullptr;
+  const bool rank_mode = p.keep == nullptr && !sum_mode;
   int ps = 0, q = 0, open_hi = 1, n_a = 0;  // the selection applies to positions [1, open_hi)
   bool by_threshold = false, newest = false;
-  if (rank_mode) {
+  int s_mode = kSumAll, s_istar = 0;
+  unsigned long long s_prefix = 0, s_mask = 0;
+  bool s_take = false;
+  const unsigned long long* s_keys = nullptr;
+  if (sum_mode) {
+    // a request (n > 0) keeps its unpinned blocks [1, ps) by the threshold; any other row reads in full
+    n_a = p.sum_row_n[r];
+    ps = p.sum_row_ps[r];
+    s_mode = p.sum_state->mode;
+    s_prefix = p.sum_state->prefix, s_mask = p.sum_state->mask, s_istar = p.sum_state->istar;
+    s_take = p.sum_row_at[r] != 0;
+    s_keys = p.sum_keys + (int64_t)r * W;
+    if (n_a > 0 && s_mode != kSumAll && ps > 1) open_hi = ps;
+  } else if (rank_mode) {
     n_a = p.row_blocks[r];
     const bool request = n_a > p.cap && n_a > 0;
     n_a = n_a < 0 ? 0 : (n_a > W ? W : n_a);
@@ -551,7 +573,7 @@ __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_ker
 
   const uint8_t flags = p.full_rows != nullptr ? p.full_rows[r] : 0;
   const bool full = (flags & kRowFull) != 0;
-  const uint8_t* krow = rank_mode ? nullptr : p.keep + (int64_t)r * p.keep_s0;
+  const uint8_t* krow = rank_mode || sum_mode ? nullptr : p.keep + (int64_t)r * p.keep_s0;
   const uint8_t* rrow = p.released ? p.released + (int64_t)r * p.released_s0 : nullptr;
 
   // ---- pass 1: the final keep flag of every flagged position, as four ballots per segment -------------
@@ -590,7 +612,9 @@ __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_ker
       for (int k = 0; k < 4; ++k) {
         const int b = b0 + k;
         c[k] = b < W;  // the committed mask at b
-        if (!rank_mode) {
+        if (sum_mode) {
+          if (b >= 1 && b < open_hi) c[k] = sum_keeps(s_mode, __ldg(s_keys + b) & s_mask, s_prefix, b, s_istar, s_take);
+        } else if (!rank_mode) {
           c[k] = b < W && krow[b] != 0;
         } else if (b >= 1 && b < open_hi) {
           if (newest) {
@@ -726,6 +750,20 @@ int presummed_mask(const int32_t* row_blocks, const int32_t* quota, const int32_
   p.rows = rows; p.width = width; p.block_size = 1; p.mask_out = mask_out; p.mask_s0 = mask_s0; p.cap = -1;
   p.presummed = true;
   return launch_view<unsigned long long>(p, stream);
+}
+
+int launch_sum_view(const int32_t* table, int64_t table_s0, const int32_t* seq_lens, const uint8_t* full_rows,
+                    const uint8_t* released, int64_t released_s0, int rows, int width, int block_size, int32_t* view,
+                    int64_t view_s0, int32_t* view_lens, uint8_t* mask_out, int64_t mask_s0, const SumState* state,
+                    const unsigned long long* keys, const int32_t* row_n, const int32_t* row_ps, const int32_t* row_at,
+                    cudaStream_t stream) {
+  if (width > kViewMaxWidth) return fail(EKV_ENOTSUP, "width %d > %d (a view row is staged in shared memory)", width, kViewMaxWidth);
+  ViewParams p{};
+  p.table = table; p.table_s0 = table_s0; p.seq_lens = seq_lens; p.full_rows = full_rows; p.released = released;
+  p.released_s0 = released_s0; p.rows = rows; p.width = width; p.block_size = block_size; p.view = view;
+  p.view_s0 = view_s0; p.view_lens = view_lens; p.mask_out = mask_out; p.mask_s0 = mask_s0; p.cap = -1;
+  p.sum_state = state; p.sum_keys = keys; p.sum_row_n = row_n; p.sum_row_ps = row_ps; p.sum_row_at = row_at;
+  return launch_view<uint32_t>(p, stream);
 }
 
 template <typename K>

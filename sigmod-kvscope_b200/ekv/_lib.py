@@ -85,6 +85,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ekv_allocate_sum_f64": (
         _i32, [_p, _i64, _p, _p, _p, _p, _i32, _i32, _f64, _i64, _i32, _i32, _p, _p, _i64, _p, ctypes.c_size_t, _p],
     ),
+    "ekv_view_build_sum_budget": (
+        _i32,
+        [_p, _i32, _i64, _p, _p, _p, _p, _i32, _i32, _f64, _i64,  # scores .. budget
+         _p, _i64, _p, _p, _p, _i64, _i32, _i32, _i32,  # table .. block_size
+         _p, _i64, _p, _p, _i64, _p, ctypes.c_size_t, _p],  # view .. stream
+    ),
     "ekv_allocate_maxmin_f64": (
         _i32, [_p, _i64, _p, _p, _p, _i32, _i32, _f64, _i64, _i32, _i32, _p, _p, ctypes.c_size_t, _p],
     ),

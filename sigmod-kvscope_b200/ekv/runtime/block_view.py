@@ -100,6 +100,45 @@ def _view_build(
     return view, view_lens
 
 
+def _sum_budget_fits(table: torch.Tensor, seq_lens: torch.Tensor, scores: torch.Tensor) -> bool:
+    """Whether a shared `sum` budget and its view can be one ekv_view_build_sum_budget call: int32 table rows
+    of at most 16384 blocks and float32 or float64 scores of the table's width."""
+    return (table.dtype == torch.int32 and seq_lens.dtype == torch.int32 and table.stride(1) == 1
+            and 0 < int(table.shape[1]) <= 16384 and scores.dtype in (torch.float32, torch.float64)
+            and scores.dim() == 2 and int(scores.shape[1]) == int(table.shape[1]) and scores.stride(1) == 1
+            and int(scores.shape[0]) >= int(table.shape[0]))
+
+
+def _sum_budget_view(table, seq_lens, block_size, row_blocks, scores, budget_fraction, recent_blocks,
+                     cap_above_blocks, measured, weights, released, full_rows, mask_out, out):
+    """The shared `sum` budget's decision and the view in one call: the select finds the threshold gain and
+    the view keeps every request's blocks above it (ekv_view_build_sum_budget), no per-row ranking."""
+    rows, width = int(table.shape[0]), int(table.shape[1])
+    view, view_lens = out if out is not None else (
+        torch.empty(rows, width, dtype=torch.int32, device=table.device),
+        torch.empty(rows, dtype=torch.int32, device=table.device),
+    )
+    if rows == 0:
+        return view, view_lens
+    u8 = [None if t is None else (t.to(torch.uint8) if t.dtype != torch.uint8 else t).contiguous()
+          for t in (released, full_rows)]
+    released, full_rows = u8
+    lib = _lib.load()
+    size = int(lib.ekv_allocate_sum_workspace_bytes(rows, width))
+    workspace = torch.empty(size + 256, dtype=torch.uint8, device=table.device)
+    base = (workspace.data_ptr() + 255) // 256 * 256
+    rc = lib.ekv_view_build_sum_budget(
+        scores.data_ptr(), scores.element_size(), scores.stride(0), None, _ptr(weights), row_blocks.data_ptr(),
+        _ptr(measured), int(recent_blocks), int(cap_above_blocks), budget_fraction, -1, table.data_ptr(),
+        table.stride(0), seq_lens.data_ptr(), _ptr(full_rows), _ptr(released),
+        released.stride(0) if released is not None else 0, rows, width, int(block_size), view.data_ptr(),
+        view.stride(0), view_lens.data_ptr(), _ptr(mask_out), mask_out.stride(0) if mask_out is not None else 0,
+        base, size, _lib.current_stream(),
+    )
+    _lib.check(rc, "ekv_view_build_sum_budget")
+    return view, view_lens
+
+
 def compact_block_table(
     table: torch.Tensor, seq_lens: torch.Tensor, keep: torch.Tensor, block_size: int
 ) -> tuple[torch.Tensor, torch.Tensor]:
@@ -178,6 +217,10 @@ def plan_view(
         # one budget over every measured row: the global greedy of the controller's default objective
         if scores is None:
             raise ValueError("the sum objective ranks by scores")
+        if _sum_budget_fits(table, seq_lens, scores):
+            return _sum_budget_view(table, seq_lens, block_size, row_blocks, scores, float(budget_fraction),
+                                    recent_blocks, cap_above_blocks, measured, weights, released, full_rows,
+                                    mask_out, out)
         from ..observe.allocation import sum_quotas
 
         sum_quotas(scores, row_blocks, quota, measured=measured, recent_blocks=recent_blocks,

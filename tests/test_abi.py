@@ -201,4 +201,4 @@ def test_step_and_stash_validate_before_launching(lib):
 
 
 def test_abi_version(lib):
-    assert lib.ekv_abi_version() == 6
+    assert lib.ekv_abi_version() == 7

@@ -492,6 +492,50 @@ def test_per_row_budgets_in_one_kernel_match_the_two_launch_path(policy):
     np.testing.assert_array_equal(lens1.cpu().numpy(), lens2.cpu().numpy())
 
 
+@pytest.mark.parametrize("dtype", ["float32", "float64"])
+def test_shared_sum_view_from_the_threshold_matches_quotas_and_ranking(dtype):
+    """ekv_view_build_sum_budget (the select's threshold applied in the view kernel, no per-row ranking)
+    against ekv_allocate_sum's quotas followed by the ranking view: length caps, measured suffixes, recent
+    pins, weights, empty rows, full rows, released blocks and many equal scores, bit for bit."""
+    from ekv.observe.allocation import sum_quotas
+    from ekv.runtime.block_view import _view_build, plan_view
+
+    rng = np.random.default_rng({"float32": 7, "float64": 8}[dtype])
+    dev = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    for trial in range(6):
+        rows, width = int(rng.integers(1, 300)), int(rng.integers(8, 1200))
+        row_blocks = rng.integers(0, width + 100, rows).astype(np.int32)
+        row_blocks[:: 11] = 0
+        measured = (row_blocks - rng.integers(0, 40, rows)).clip(0).astype(np.int32) if trial % 2 else None
+        lens = (np.minimum(row_blocks, width) * 16 - rng.integers(0, 16, rows)).clip(0).astype(np.int32)
+        table = rng.integers(0, 1 << 20, (rows, width)).astype(np.int32)
+        scores = rng.dirichlet(np.full(width, 0.3), rows)
+        if trial % 3 == 0:
+            scores = np.round(scores, 3)  # many equal gains: the threshold falls among ties
+        scores = scores.astype(np.float32 if dtype == "float32" else np.float64)
+        weights = rng.uniform(0.5, 2.0, rows) if trial % 2 == 0 else None
+        full = (rng.random(rows) < 0.1).astype(np.uint8)
+        released = (rng.random((rows, width)) < 0.05).astype(np.uint8)
+        cap = int(rng.choice([0, 4]))
+        fraction = float(rng.choice([0.1, 0.3, 0.6, 0.95]))
+        args = dict(measured=None if measured is None else dev(measured), recent_blocks=3, full_rows=dev(full),
+                    released=dev(released))
+        w = None if weights is None else dev(weights)
+        rb, sc = dev(row_blocks), dev(scores)
+        mask1 = torch.empty(rows, width, dtype=torch.uint8).cuda()
+        view1, lens1 = plan_view(dev(table), dev(lens), 16, rb, scores=sc, policy="sum", budget_fraction=fraction,
+                                 cap_above_blocks=cap, weights=w, mask_out=mask1, **args)
+        quota = torch.empty(rows, dtype=torch.int32).cuda()
+        sum_quotas(sc, rb, quota, measured=args["measured"], recent_blocks=3, cap_above_blocks=cap,
+                   budget_fraction=fraction, weights=w)
+        mask2 = torch.empty(rows, width, dtype=torch.uint8).cuda()
+        view2, lens2 = _view_build(dev(table), dev(lens), 16, row_blocks=rb, quota=quota, scores=sc, policy="sum",
+                                   mask_out=mask2, weights=w, **args)
+        np.testing.assert_array_equal(mask1.cpu().numpy(), mask2.cpu().numpy(), err_msg=f"trial {trial}")
+        np.testing.assert_array_equal(view1.cpu().numpy(), view2.cpu().numpy(), err_msg=f"trial {trial}")
+        np.testing.assert_array_equal(lens1.cpu().numpy(), lens2.cpu().numpy(), err_msg=f"trial {trial}")
+
+
 def test_full_size_view_stress_properties():
     """1024 rows x 8192: the view is a permutation of the row, kept ids come first in their original
     order, the kept count is pins + quota, and the length formula holds."""

@@ -734,6 +734,9 @@ def main() -> None:
         status = plane.status()
         if status:
             raise SystemExit(f"the audit kernel reported status {status}")
+        # the roofline of the dominant kernel: the record kernel alone, one launch per audit step (deferred),
+        # timed over its own launches right after the step, on the same plane and inputs
+        roofline = record_roofline(plane, w, args.steps, args.warmup, dist_on) if args.record == "deferred" else None
         parity = None
         if not args.no_parity:
             parity = parity_check(w, stepper.shares(), rank, world, dist_on, rows=4)
@@ -751,11 +754,8 @@ def main() -> None:
         units_rank = w.units_per_step()
         units_all = units_rank * world
         value = units_all * args.steps / seconds
-        # the roofline of the dominant kernel: the record kernel alone, one launch per audit step
-        # (deferred) or per layer (per-layer), timed over its own launches
-        if args.record == "deferred":
-            roofline = record_roofline(plane, w, args.steps, args.warmup, dist_on)
-        else:
+        # per-layer: the record kernel is the step, a launch per layer
+        if roofline is None:
             peak, peak_kind = measured_peak()
             launch_seconds = seconds / args.steps / w.layers
             b_unit = bytes_per_unit(w.heads * w.group_rows)

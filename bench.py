@@ -848,9 +848,9 @@ def main() -> None:
                         "after the last) in CUDA graphs alternating two share buffers; the block table and "
                         "lengths in by one copy from pinned host memory, each step's shares out to pinned "
                         "memory on a copy stream, the host waiting for them one step later; KV cache resident"},
-        # per step: the descriptor, record, share and combine kernels (deferred), or a record kernel
-        # per layer plus the share and combine kernels (per-layer)
-        "gpu_launches": args.steps * (4 if args.record == "deferred" else w.layers + 2),
+        # per step: the descriptor, record and share kernels (deferred), or a record kernel per layer plus
+        # the share kernel (per-layer)
+        "gpu_launches": args.steps * (3 if args.record == "deferred" else w.layers + 1),
         "clocks": clocks.summary(),
         "parity": parity,
         "combine": ("one NCCL all-reduce (average) per step in the step's CUDA graph, overlapping the next "

@@ -415,7 +415,8 @@ def test_one_step_launch_equals_per_layer_launches():
     assert torch.equal(run.contrib, step.contrib)
     assert torch.isnan(step.share[2]).all() and torch.isnan(step.share[3]).all()
     assert step.contrib.tolist() == [20, 20, 0, 0, 20, 20, 20]
-    # the tickets are left zero for the next step: a second step gives the same result
+    # nothing of a step carries over into the next (the work counter and tensor maps are rewritten): a second
+    # step gives the same result
     rc = L.load().ekv_audit_step(
         q_addr.data_ptr(), k_addr.data_ptr(), td.data_ptr(), ld.data_ptr(), rd.data_ptr(), sel.data_ptr(),
         flag.data_ptr(), step.lse.data_ptr(), 1 / math.sqrt(128), 0, layers, 0, 1, 0, qs[0].stride(0), qs[0].stride(1),

@@ -602,6 +602,40 @@ __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_ker
         s_seg[sg] = __popc(plane[0]) + __popc(plane[1]) + __popc(plane[2]) + __popc(plane[3]);
       }
     }
+  } else if (sum_mode && mrow == nullptr && rrow == nullptr && !full) {
+    // the shared `sum` threshold, common case: an unpinned block by its gain key (two 16-byte loads for a
+    // lane's four), every other block of the request kept; a segment inside [1, min(open_hi, blocks - 1))
+    // needs the key test alone
+    const int inner = min(open_hi, blocks - 1);
+    for (int sg = warp; sg < n_segs; sg += kViewWarps) {
+      const int b0 = kViewSeg * sg + 4 * lane;
+      unsigned long long gk[4] = {0, 0, 0, 0};
+      if (b0 + 3 < open_hi && (reinterpret_cast<uintptr_t>(s_keys + b0) & 15) == 0) {
+        const ulonglong2 a = __ldg(reinterpret_cast<const ulonglong2*>(s_keys + b0));
+        const ulonglong2 c = __ldg(reinterpret_cast<const ulonglong2*>(s_keys + b0 + 2));
+        gk[0] = a.x, gk[1] = a.y, gk[2] = c.x, gk[3] = c.y;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) gk[k] = b0 + k >= 1 && b0 + k < open_hi ? __ldg(s_keys + b0 + k) : 0ull;
+      }
+      uint32_t plane[4];
+      if (sg > 0 && kViewSeg * (sg + 1) <= inner) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          plane[k] = __ballot_sync(kFullMask, sum_keeps(s_mode, gk[k] & s_mask, s_prefix, b0 + k, s_istar, s_take));
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int b = b0 + k;
+          const bool c = b >= 1 && b < open_hi ? sum_keeps(s_mode, gk[k] & s_mask, s_prefix, b, s_istar, s_take) : true;
+          plane[k] = __ballot_sync(kFullMask, (c || b == 0 || b == blocks - 1) && b < blocks && b < W);
+        }
+      }
+      if (lane == 0) {
+        s_bits[sg] = make_uint4(plane[0], plane[1], plane[2], plane[3]);
+        s_seg[sg] = __popc(plane[0]) + __popc(plane[1]) + __popc(plane[2]) + __popc(plane[3]);
+      }
+    }
   } else {
     for (int sg = warp; sg < n_segs; sg += kViewWarps) {
       const int b0 = kViewSeg * sg + 4 * lane;

@@ -7,10 +7,10 @@
 // an MSB radix select (digits of 11, 11 and 9 bits over a 2048-bin shared-memory histogram; float64
 // gain keys take six digits), while the table row is copied in. Keys above the threshold are
 // kept; of the keys equal to it, the first (uniform: older blocks first, allocation.py:89) or last
-// (sum: newer blocks first, allocation.py:107-113) ones fill the quota, found with a block-wide
-// scan. A second block-wide scan over the keep flags places kept blocks first and the others after
-// them, both in their original order: the stable partition of compact_block_table
-// (runtime/block_view.py:52).
+// (sum: newer blocks first, allocation.py:107-113) ones fill the quota, ranked by the equal keys of
+// the warps before and a running count within each warp's run of positions. The warps' counts of
+// kept blocks place kept blocks first and the others after them, both in their original order: the
+// stable partition of compact_block_table (runtime/block_view.py:52).
 #include "ekv_common.cuh"
 #include "pairwise.cuh"
 #include "pins.cuh"
@@ -269,33 +269,13 @@ __device__ __forceinline__ void copy_words(int32_t* dst, const int32_t* src, int
 }
 
 
-// Exclusive scan of the n per-segment counts c[0..n) in place (warp 0, four a lane); c[n] = the total, returned
-// to every thread. n <= kViewMaxSegs. Barriers before (the counts are written) and after.
-__device__ __forceinline__ int segment_scan(int* c, int n) {
-  __syncthreads();
-  if ((threadIdx.x >> 5) == 0) {
-    const int lane = threadIdx.x & 31;
-    int v[4], sum = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      v[k] = 4 * lane + k < n ? c[4 * lane + k] : 0;
-      sum += v[k];
-    }
-    int incl = sum;
-    for (int off = 1; off < 32; off <<= 1) {
-      const int x = __shfl_up_sync(kFullMask, incl, off);
-      if (lane >= off) incl += x;
-    }
-    int run = incl - sum;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (4 * lane + k < n) c[4 * lane + k] = run;
-      run += v[k];
-    }
-    if (lane == 31) c[n] = incl;
-  }
-  __syncthreads();
-  return c[n];
+// The per-warp counts c[0..kViewWarps) (written before a barrier): the sum over the warps before this one
+// (*before) and over every warp (returned), to every lane.
+__device__ __forceinline__ int warp_counts_prefix(const int* c, int* before) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int v = lane < kViewWarps ? c[lane] : 0;
+  *before = __reduce_add_sync(kFullMask, lane < warp ? v : 0);
+  return __reduce_add_sync(kFullMask, v);
 }
 
 // The order keys of the ranking. Float32 scores: the bits of max(score, 0), three digits (bits 30-20,
@@ -357,14 +337,15 @@ __host__ __device__ constexpr size_t view_smem_bytes(int width) {
 // with that prefix is kept and the select stops early. The equal-key count comes from the last
 // histogram, so the scan that ranks equal keys by position runs only when some of them must be dropped.
 //
-// The layout: only positions [0, min(blocks, width)) can be kept, so those are laid out, in segments of 128
-// positions that the warps take in turn (warp w: segments w, w + 16, ...; lane l holds positions
-// 128 * s + 4 * l + k, read and written 16 bytes at a time); the rest of the row, never kept, keeps its
-// place: the view there is the table. A segment's keep flags are four ballots, one per k (bit l of ballot
-// k: position 4 * l + k), so the kept positions before a lane's are popcounts of the ballots below its
-// bit, and a scan of the segments' counts gives each segment's first place. With mask_out the flags cover
-// the whole width, as every position's committed flag is written; with no view (mask_out only) the kernel
-// ends there.
+// The layout: only positions [0, min(blocks, width)) can be kept, so those are laid out; the rest of the row,
+// never kept, keeps its place (the view there is the table, copied while the row is ranked). The laid-out
+// positions form segments of 128 and each warp takes a contiguous run of segments; lane l holds positions
+// 128 * s + 32 * k + l (k = 0..3), so a segment's keep flags are four ballots, ballot k covering 32
+// consecutive positions. The kept positions before a lane's are the warp's running count plus popcounts of
+// the ballots, and one barrier with the warps' counts gives each warp its first place and the row's kept
+// total: every store of a ballot's kept ids (and of its dropped ids, placed after all kept ones) is then a
+// contiguous run of the view row. With mask_out the flags cover the whole width, as every position's
+// committed flag is written; with no view (mask_out only) the kernel ends there.
 template <typename K>
 __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_kernel(const ViewParams p) {
   chain_release();
@@ -374,18 +355,14 @@ __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_ker
   __shared__ int s_w[kViewWarps + 1];
   __shared__ int s_pick[3];
   __shared__ uint4 s_bits[kViewMaxSegs];  // each segment's four keep ballots
-  // after the select, the histogram's space holds each segment's kept positions (then the kept positions
-  // before it) and, with ties, its equal keys (then the equal keys before it)
-  int* s_seg = s_hist;
-  int* s_eq = s_hist + 2 * kViewMaxSegs;
-  static_assert(4 * kViewMaxSegs + 2 <= kViewBins, "the segment counts fit the histogram's space");
+  __shared__ int s_kept[kViewWarps], s_eqw[kViewWarps];  // each warp's kept positions and equal keys
   constexpr bool kWide = sizeof(K) == 8;
   const int r = blockIdx.x;
   const int W = p.width, BS = p.block_size;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int w_pad = (W + kViewSeg - 1) / kViewSeg * kViewSeg;
   K* keys = reinterpret_cast<K*>(smem_view);                                       // [w_pad]
-  int32_t* trow_s = reinterpret_cast<int32_t*>(smem_view + (size_t)w_pad * sizeof(K));  // [w_pad]: the table row
+  int32_t* trow_s = reinterpret_cast<int32_t*>(smem_view + (size_t)w_pad * sizeof(K));  // [w_pad]: the staged table row
 
   const bool has_view = p.view != nullptr;
   const int seq = p.seq_lens != nullptr ? p.seq_lens[r] : 0;
@@ -456,9 +433,12 @@ __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_ker
   // (address arithmetic only: without a view, laid is 0 and the table is never read)
   const int32_t* trow = reinterpret_cast<const int32_t*>(reinterpret_cast<uintptr_t>(p.table) +
                                                          (uintptr_t)((int64_t)r * p.table_s0 * 4));
-  // the table row lands while the row is ranked
+  // the table row lands while the row is ranked; past the laid-out positions nothing is kept, so the view
+  // there is the table, copied now
   stage_words(reinterpret_cast<uint32_t*>(trow_s), reinterpret_cast<const uint32_t*>(trow), laid);
   cp_async_commit();
+  int32_t* vrow = has_view ? p.view + (int64_t)r * p.view_s0 : nullptr;
+  if (has_view) copy_words(vrow, trow, laid, W);
 
   K prefix = 0, pmask = 0;
   int k_eq = 0, eq_total = 0;
@@ -556,19 +536,26 @@ __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_ker
   const bool ties = eq_total != k_eq;  // only then do keys equal to the threshold need their rank
   const bool older_first = p.policy == EKV_POLICY_UNIFORM;
 
-  // ---- ties: each equal key's rank among the equal keys, in position order --------------------
+  // each warp's run of segments
+  const int per_warp = (n_segs + kViewWarps - 1) / kViewWarps;
+  const int sg_lo = min(warp * per_warp, n_segs), sg_hi = min(sg_lo + per_warp, n_segs);
+
+  // ---- ties: the equal keys of the warps before this one (each equal key's rank, in position order, is
+  // that count plus the equal keys before it in this warp's run)
+  int eq_run = 0;
   if (ties) {
-    for (int sg = warp; sg < n_segs; sg += kViewWarps) {
-      const int b0 = kViewSeg * sg + 4 * lane;
-      K kv[4];
-      ViewKey<K>::load4(keys, b0 >> 2, kv);
-      int cnt = 0;
+    int cnt = 0;
+    for (int sg = sg_lo; sg < sg_hi; ++sg) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) cnt += b0 + k >= 1 && b0 + k < ps && (kv[k] & pmask) == prefix;
-      for (int off = 16; off > 0; off >>= 1) cnt += __shfl_xor_sync(kFullMask, cnt, off);
-      if (lane == 0) s_eq[sg] = cnt;
+      for (int k = 0; k < 4; ++k) {
+        const int b = kViewSeg * sg + 32 * k + lane;
+        cnt += b >= 1 && b < ps && (keys[b] & pmask) == prefix;
+      }
     }
-    segment_scan(s_eq, n_segs);
+    cnt = __reduce_add_sync(kFullMask, cnt);
+    if (lane == 0) s_eqw[warp] = cnt;
+    __syncthreads();
+    warp_counts_prefix(s_eqw, &eq_run);
   }
 
   const uint8_t flags = p.full_rows != nullptr ? p.full_rows[r] : 0;
@@ -577,154 +564,120 @@ __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_ker
   const uint8_t* rrow = p.released ? p.released + (int64_t)r * p.released_s0 : nullptr;
 
   // ---- pass 1: the final keep flag of every flagged position, as four ballots per segment -------------
+  int kept_mine = 0;
   if (rank_mode && by_threshold && !ties && mrow == nullptr && rrow == nullptr && !full) {
     // the common case: a key at or above the threshold is kept; outside [1, open_hi) every block is. A segment
     // inside [1, min(open_hi, blocks - 1)) needs the key test alone.
     const int inner = min(open_hi, blocks - 1);
-    for (int sg = warp; sg < n_segs; sg += kViewWarps) {
-      const int b0 = kViewSeg * sg + 4 * lane;
-      K kv[4];
-      ViewKey<K>::load4(keys, b0 >> 2, kv);
+    for (int sg = sg_lo; sg < sg_hi; ++sg) {
+      const int b0 = kViewSeg * sg + lane;
       uint32_t plane[4];
       if (sg > 0 && kViewSeg * (sg + 1) <= inner) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) plane[k] = __ballot_sync(kFullMask, (kv[k] & pmask) >= prefix);
+        for (int k = 0; k < 4; ++k) plane[k] = __ballot_sync(kFullMask, (keys[b0 + 32 * k] & pmask) >= prefix);
       } else {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const int b = b0 + k;
-          const K key = (b >= 1 && b < open_hi) ? kv[k] & pmask : ~(K)0;
+          const int b = b0 + 32 * k;
+          const K key = (b >= 1 && b < open_hi) ? keys[b] & pmask : ~(K)0;
           plane[k] = __ballot_sync(kFullMask, (key >= prefix || b == 0 || b == blocks - 1) && b < blocks && b < W);
         }
       }
-      if (lane == 0) {
-        s_bits[sg] = make_uint4(plane[0], plane[1], plane[2], plane[3]);
-        s_seg[sg] = __popc(plane[0]) + __popc(plane[1]) + __popc(plane[2]) + __popc(plane[3]);
-      }
+      if (lane == 0) s_bits[sg] = make_uint4(plane[0], plane[1], plane[2], plane[3]);
+      kept_mine += __popc(plane[0]) + __popc(plane[1]) + __popc(plane[2]) + __popc(plane[3]);
     }
   } else if (sum_mode && mrow == nullptr && rrow == nullptr && !full) {
-    // the shared `sum` threshold, common case: an unpinned block by its gain key (two 16-byte loads for a
-    // lane's four), every other block of the request kept; a segment inside [1, min(open_hi, blocks - 1))
-    // needs the key test alone
+    // the shared `sum` threshold, common case: an unpinned block by its gain key, every other block of the
+    // request kept; a segment inside [1, min(open_hi, blocks - 1)) needs the key test alone
     const int inner = min(open_hi, blocks - 1);
-    for (int sg = warp; sg < n_segs; sg += kViewWarps) {
-      const int b0 = kViewSeg * sg + 4 * lane;
-      unsigned long long gk[4] = {0, 0, 0, 0};
-      if (b0 + 3 < open_hi && (reinterpret_cast<uintptr_t>(s_keys + b0) & 15) == 0) {
-        const ulonglong2 a = __ldg(reinterpret_cast<const ulonglong2*>(s_keys + b0));
-        const ulonglong2 c = __ldg(reinterpret_cast<const ulonglong2*>(s_keys + b0 + 2));
-        gk[0] = a.x, gk[1] = a.y, gk[2] = c.x, gk[3] = c.y;
-      } else {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) gk[k] = b0 + k >= 1 && b0 + k < open_hi ? __ldg(s_keys + b0 + k) : 0ull;
-      }
+    for (int sg = sg_lo; sg < sg_hi; ++sg) {
+      const int b0 = kViewSeg * sg + lane;
       uint32_t plane[4];
       if (sg > 0 && kViewSeg * (sg + 1) <= inner) {
+        unsigned long long gk[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) gk[k] = __ldg(s_keys + b0 + 32 * k);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          plane[k] = __ballot_sync(kFullMask, sum_keeps(s_mode, gk[k] & s_mask, s_prefix, b0 + k, s_istar, s_take));
+          plane[k] = __ballot_sync(kFullMask, sum_keeps(s_mode, gk[k] & s_mask, s_prefix, b0 + 32 * k, s_istar, s_take));
       } else {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const int b = b0 + k;
-          const bool c = b >= 1 && b < open_hi ? sum_keeps(s_mode, gk[k] & s_mask, s_prefix, b, s_istar, s_take) : true;
+          const int b = b0 + 32 * k;
+          const bool c = b >= 1 && b < open_hi ? sum_keeps(s_mode, __ldg(s_keys + b) & s_mask, s_prefix, b, s_istar, s_take) : true;
           plane[k] = __ballot_sync(kFullMask, (c || b == 0 || b == blocks - 1) && b < blocks && b < W);
         }
       }
-      if (lane == 0) {
-        s_bits[sg] = make_uint4(plane[0], plane[1], plane[2], plane[3]);
-        s_seg[sg] = __popc(plane[0]) + __popc(plane[1]) + __popc(plane[2]) + __popc(plane[3]);
-      }
+      if (lane == 0) s_bits[sg] = make_uint4(plane[0], plane[1], plane[2], plane[3]);
+      kept_mine += __popc(plane[0]) + __popc(plane[1]) + __popc(plane[2]) + __popc(plane[3]);
     }
   } else {
-    for (int sg = warp; sg < n_segs; sg += kViewWarps) {
-      const int b0 = kViewSeg * sg + 4 * lane;
-      K kv[4] = {0, 0, 0, 0};
-      if (by_threshold) ViewKey<K>::load4(keys, b0 >> 2, kv);
-      bool c[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int b = b0 + k;
-        c[k] = b < W;  // the committed mask at b
-        if (sum_mode) {
-          if (b >= 1 && b < open_hi) c[k] = sum_keeps(s_mode, __ldg(s_keys + b) & s_mask, s_prefix, b, s_istar, s_take);
-        } else if (!rank_mode) {
-          c[k] = b < W && krow[b] != 0;
-        } else if (b >= 1 && b < open_hi) {
-          if (newest) {
-            c[k] = b >= ps - q;
-          } else if (by_threshold) {
-            const K key = kv[k] & pmask;
-            c[k] = key > prefix || (key == prefix && !ties);  // every equal key is kept unless too many
-          } else {
-            c[k] = false;  // nothing selected
-          }
-        }
-      }
-      if (ties) {
-        // each equal key's rank among the equal keys in position order: those of the segments before, of the
-        // lanes below, then this lane's before k
-        bool eq[4];
-        int below = s_eq[sg];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int b = b0 + k;
-          eq[k] = b >= 1 && b < ps && (kv[k] & pmask) == prefix;
-          below += __popc(__ballot_sync(kFullMask, eq[k]) & lanes_below());
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          if (eq[k]) {
-            c[k] = older_first ? below < k_eq : (eq_total - below - 1) < k_eq;
-            ++below;
-          }
-      }
+    for (int sg = sg_lo; sg < sg_hi; ++sg) {
+      const int b0 = kViewSeg * sg + lane;
       uint32_t plane[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const int b = b0 + k;
+        const int b = b0 + 32 * k;
+        const K kv = by_threshold && b < ps ? keys[b] & pmask : (K)0;
+        bool c = b < W;  // the committed mask at b
+        if (sum_mode) {
+          if (b >= 1 && b < open_hi) c = sum_keeps(s_mode, __ldg(s_keys + b) & s_mask, s_prefix, b, s_istar, s_take);
+        } else if (!rank_mode) {
+          c = b < W && krow[b] != 0;
+        } else if (b >= 1 && b < open_hi) {
+          if (newest) {
+            c = b >= ps - q;
+          } else if (by_threshold) {
+            c = kv > prefix || (kv == prefix && !ties);  // every equal key is kept unless too many
+          } else {
+            c = false;  // nothing selected
+          }
+        }
+        if (ties) {
+          // an equal key's rank among the equal keys in position order: those before this ballot, then the
+          // lanes below
+          const bool eq = b >= 1 && b < ps && kv == prefix;
+          const uint32_t eq_bits = __ballot_sync(kFullMask, eq);
+          const int below = eq_run + __popc(eq_bits & lanes_below());
+          if (eq) c = older_first ? below < k_eq : (eq_total - below - 1) < k_eq;
+          eq_run += __popc(eq_bits);
+        }
         const bool in_row = b < W;
-        if (mrow != nullptr && in_row) mrow[b] = c[k];
-        bool keep = c[k] || full;
+        if (mrow != nullptr && in_row) mrow[b] = c;
+        bool keep = c || full;
         if (rrow != nullptr && in_row && rrow[b]) keep = false;  // a released block is never read (block_view.py:280-281)
         keep = (keep || b == 0 || b == blocks - 1) && b < blocks && in_row;
         plane[k] = __ballot_sync(kFullMask, keep);
       }
-      if (lane == 0) {
-        s_bits[sg] = make_uint4(plane[0], plane[1], plane[2], plane[3]);
-        s_seg[sg] = __popc(plane[0]) + __popc(plane[1]) + __popc(plane[2]) + __popc(plane[3]);
-      }
+      if (lane == 0) s_bits[sg] = make_uint4(plane[0], plane[1], plane[2], plane[3]);
+      kept_mine += __popc(plane[0]) + __popc(plane[1]) + __popc(plane[2]) + __popc(plane[3]);
     }
   }
-  const int kept_total = segment_scan(s_seg, n_segs);  // (its barriers also end every key read)
-
-  // ---- pass 2: kept ids first, then the others, both in position order, into shared memory -------
+  if (lane == 0) s_kept[warp] = kept_mine;
   cp_async_wait<0>();
-  __syncthreads();  // the table row has landed
-  uint32_t* out = reinterpret_cast<uint32_t*>(keys);
-  for (int sg = warp; sg < n_segs && kViewSeg * sg < laid; sg += kViewWarps) {
-    const int b0 = kViewSeg * sg + 4 * lane;
+  __syncthreads();  // the warps' counts are in, the table row has landed and every key read has ended
+  int before = 0;  // kept positions before this warp's first
+  const int kept_total = warp_counts_prefix(s_kept, &before);
+
+  // ---- pass 2: kept ids first, then the others, both in position order -------------------------------
+  for (int sg = sg_lo; sg < sg_hi && kViewSeg * sg < laid; ++sg) {
     const uint4 pl = s_bits[sg];
     const uint32_t plane[4] = {pl.x, pl.y, pl.z, pl.w};
-    int before = s_seg[sg];  // kept positions before this lane's first
+    int32_t ids[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) before += __popc(plane[k] & lanes_below());
-    if (b0 < laid) {
-      const uint4 ids4 = *reinterpret_cast<const uint4*>(trow_s + b0);
-      const uint32_t ids[4] = {ids4.x, ids4.y, ids4.z, ids4.w};
+    for (int k = 0; k < 4; ++k) {
+      const int b = kViewSeg * sg + 32 * k + lane;
+      ids[k] = b < laid ? trow_s[b] : 0;
+    }
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int b = b0 + k;
-        const bool keep = (plane[k] >> lane) & 1u;
-        if (b < laid) out[keep ? before : kept_total + (b - before)] = ids[k];
-        before += keep;
-      }
+    for (int k = 0; k < 4; ++k) {
+      const int b = kViewSeg * sg + 32 * k + lane;
+      const bool keep = (plane[k] >> lane) & 1u;
+      const int kb = before + __popc(plane[k] & lanes_below());  // kept positions before b
+      if (b < laid) vrow[keep ? kb : kept_total + (b - kb)] = ids[k];
+      before += __popc(plane[k]);
     }
   }
-  __syncthreads();
-  int32_t* vrow = p.view + (int64_t)r * p.view_s0;
-  copy_words(vrow, reinterpret_cast<const int32_t*>(out), 0, laid);
-  if (has_view) copy_words(vrow, trow, laid, W);  // past the laid-out positions nothing is kept: the view is the table
   if (threadIdx.x == 0 && has_view) {
     const int last = seq - (blocks - 1) * BS;
     const int view_len = blocks > 0 ? (kept_total - 1) * BS + last : 0;

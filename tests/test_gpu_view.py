@@ -454,6 +454,51 @@ def test_view_stress_rows_match_the_oracle(policy):
     np.testing.assert_array_equal(view_lens.cpu().numpy(), ref_lens)
 
 
+@pytest.mark.parametrize("policy", ["sum", "uniform"])
+@pytest.mark.parametrize("with_mask", [False, True])
+def test_wide_rows_of_equal_scores_match_the_oracle(policy, with_mask):
+    """Rows of up to 8192 blocks whose scores take four values, so the threshold always falls among equal keys
+    that span every warp's run of positions: which of them are kept (newer first under `sum`, older first
+    under `uniform`) follows the oracle, with and without the committed mask written."""
+    from ekv.runtime.block_view import plan_view
+
+    rng = np.random.default_rng(11 if policy == "sum" else 12)
+    rows, width = 96, 8192
+    n = rng.integers(2000, width + 1, rows).astype(np.int32)
+    n[:4] = [width, width - 1, 2049, 2048]
+    table = rng.integers(0, 1 << 20, (rows, width)).astype(np.int32)
+    scores = rng.integers(0, 4, (rows, width)).astype(np.float32)
+    fraction = rng.uniform(0.05, 0.95, rows)
+    lens = (n * 16 - rng.integers(0, 16, rows)).astype(np.int32)
+    dev = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    mask = torch.empty(rows, width, dtype=torch.uint8).cuda() if with_mask else None
+    view, view_lens = plan_view(dev(table), dev(lens), 16, dev(n), scores=dev(scores), policy=policy,
+                                row_fraction=dev(fraction), recent_blocks=0, mask_out=mask)
+    keep = oa.per_row_keep(n, width, scores.astype(np.float64), fraction, policy)
+    if with_mask:
+        np.testing.assert_array_equal(mask.cpu().numpy(), keep)
+    ref_view, ref_lens = ov.compact_block_table(table, lens, keep, 16)
+    np.testing.assert_array_equal(view.cpu().numpy(), ref_view)
+    np.testing.assert_array_equal(view_lens.cpu().numpy(), ref_lens)
+
+
+def test_wide_float64_requests_of_equal_scores_match_the_oracle():
+    """The float64 ranking (allocate over one wide request, its gains ranked as float64 keys) with the
+    threshold among equal gains spread over the whole row."""
+    from ekv.observe.allocation import Request, allocate
+
+    rng = np.random.default_rng(13)
+    for trial in range(6):
+        objective = "sum" if trial % 2 else "uniform"
+        n = int(rng.integers(3000, 8193))
+        scores = rng.integers(0, 4, n).astype(np.float64)
+        pinned = oa.controller_pins(n, int(rng.integers(0, 6)))
+        budget = int(rng.integers(int(pinned.sum()) + 1, n))
+        (got,) = allocate([Request(scores=scores, pinned=pinned)], budget, objective)
+        (want,) = oa.allocate([scores], budget, objective, [pinned])
+        np.testing.assert_array_equal(got, want, err_msg=f"trial {trial}")
+
+
 @pytest.mark.parametrize("policy", ["sum", "uniform", "newest"])
 def test_per_row_budgets_in_one_kernel_match_the_two_launch_path(policy):
     """ekv_view_build_fractions (quotas computed in the view kernel) against ekv_allocate_quotas followed by

@@ -349,7 +349,6 @@ __host__ __device__ constexpr size_t view_smem_bytes(int width) {
 template <typename K>
 __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_kernel(const ViewParams p) {
   chain_release();
-  chain_wait();  // what the launch before this one wrote
   extern __shared__ __align__(16) unsigned char smem_view[];
   __shared__ __align__(16) int s_hist[kViewBins];
   __shared__ int s_w[kViewWarps + 1];
@@ -371,9 +370,22 @@ __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_ker
   const int live = mrow != nullptr ? W : (blocks < W ? blocks : W);
   const int n_segs = (live + kViewSeg - 1) / kViewSeg;               // segments flagged
   const int laid = !has_view ? 0 : min((live + 3) & ~3, W);            // positions laid out
+  // (address arithmetic only: without a view, laid is 0 and the table is never read)
+  const int32_t* trow = reinterpret_cast<const int32_t*>(reinterpret_cast<uintptr_t>(p.table) +
+                                                         (uintptr_t)((int64_t)r * p.table_s0 * 4));
+  int32_t* vrow = has_view ? p.view + (int64_t)r * p.view_s0 : nullptr;
+  const bool sum_mode = p.sum_state != nullptr;
+  if (sum_mode) {
+    // Threshold mode follows the select's kernels, none of which writes the caller's table or lengths (they
+    // were complete before the select's first kernel started): the table row is staged, and past the
+    // laid-out positions copied to the view, while those kernels finish.
+    stage_words(reinterpret_cast<uint32_t*>(trow_s), reinterpret_cast<const uint32_t*>(trow), laid);
+    cp_async_commit();
+    if (has_view) copy_words(vrow, trow, laid, W);
+  }
+  chain_wait();  // what the launch before this one wrote
 
   // ---- the row's committed mask: pins + selection (ranking mode) or the given mask ---------------
-  const bool sum_mode = p.sum_state != nullptr;
   const bool rank_mode = p.keep == nullptr && !sum_mode;
   int ps = 0, q = 0, open_hi = 1, n_a = 0;  // the selection applies to positions [1, open_hi)
   bool by_threshold = false, newest = false;
@@ -430,15 +442,13 @@ __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_ker
     }
     cp_async_commit();
   }
-  // (address arithmetic only: without a view, laid is 0 and the table is never read)
-  const int32_t* trow = reinterpret_cast<const int32_t*>(reinterpret_cast<uintptr_t>(p.table) +
-                                                         (uintptr_t)((int64_t)r * p.table_s0 * 4));
-  // the table row lands while the row is ranked; past the laid-out positions nothing is kept, so the view
-  // there is the table, copied now
-  stage_words(reinterpret_cast<uint32_t*>(trow_s), reinterpret_cast<const uint32_t*>(trow), laid);
-  cp_async_commit();
-  int32_t* vrow = has_view ? p.view + (int64_t)r * p.view_s0 : nullptr;
-  if (has_view) copy_words(vrow, trow, laid, W);
+  if (!sum_mode) {
+    // the table row lands while the row is ranked; past the laid-out positions nothing is kept, so the view
+    // there is the table, copied now
+    stage_words(reinterpret_cast<uint32_t*>(trow_s), reinterpret_cast<const uint32_t*>(trow), laid);
+    cp_async_commit();
+    if (has_view) copy_words(vrow, trow, laid, W);
+  }
 
   K prefix = 0, pmask = 0;
   int k_eq = 0, eq_total = 0;

@@ -234,9 +234,8 @@ constexpr uint8_t kRowFull = 1, kRowDecoding = 2, kRowAudited = 4;
 constexpr int kViewThreads = 512;
 constexpr int kViewWarps = kViewThreads / 32;
 constexpr int kViewMaxWidth = 16384;               // rows staged in shared memory: 8 bytes per position
-constexpr int kViewSeg = 128;                      // positions of a segment: four per lane of a warp
-constexpr int kViewMaxSegs = kViewMaxWidth / kViewSeg;
-static_assert(kViewMaxSegs <= 4 * 32, "one warp scans the segments, four per lane");
+constexpr int kViewSeg = 128;                      // positions of a segment: four ballots of 32 positions
+constexpr int kViewMaxSegs = kViewMaxWidth / kViewSeg;  // (each segment's ballots kept in shared memory)
 constexpr int kViewBins = 2048;                    // radix-select digits of 11, 11 and 9 bits
 static_assert(kViewBins == 4 * kViewThreads, "each thread owns four histogram bins");
 

@@ -45,30 +45,13 @@ __device__ __forceinline__ PairwiseScratch pairwise_scratch(void* mem, int nodes
   return t;
 }
 
-// One leaf of at most 128 values; value(i) gives the i-th value as a double.
-template <typename V>
-__device__ double pairwise_leaf(const V& value, int lo, int len) {
-  if (len < 8) {
-    double res = 0.0;
-    for (int i = 0; i < len; ++i) res += value(lo + i);
-    return res;
-  }
-  double r[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) r[j] = value(lo + j);
-  int i = 8;
-  for (; i < len - (len % 8); i += 8)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) r[j] += value(lo + i + j);
-  double res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
-  for (; i < len; ++i) res += value(lo + i);
-  return res;
-}
-
 // The sum of value(0 .. n) as numpy computes it, with a scratch of pairwise_nodes(n) nodes or more; every
 // thread of the CTA calls it and gets the sum. THREADS = blockDim.x (a multiple of 32). The tree (a few
 // hundred nodes at most) is built and combined by warp 0 alone, a level at a time with warp barriers; the
-// leaves are summed by the whole CTA.
+// leaves are summed by the whole CTA, eight lanes a leaf: lane j keeps numpy's accumulator r[j] (its
+// additions in numpy's order), the eight are combined by shuffles in numpy's order, and lane 0 adds the rest.
+// The lanes of a leaf read eight adjacent values, so leaves that start 128 values apart share a bank only
+// between the four leaves of a warp.
 template <int THREADS, typename V>
 __device__ double block_pairwise_sum(const PairwiseScratch& t, int n, const V& value) {
   const int tid = threadIdx.x, lane = tid & 31;
@@ -111,8 +94,26 @@ __device__ double block_pairwise_sum(const PairwiseScratch& t, int n, const V& v
   }
   __syncthreads();
   const int nodes = t.meta[0];
-  for (int i = tid; i < nodes; i += THREADS)
-    if (t.left[i] < 0) t.val[i] = pairwise_leaf(value, t.lo[i], t.len[i]);
+  const int oct = tid >> 3, j = tid & 7;
+  for (int i0 = 0; i0 < nodes; i0 += THREADS / 8) {  // (the same trip count in every lane)
+    const int i = i0 + oct;
+    const bool leaf = i < nodes && t.left[i] < 0;
+    const int lo = leaf ? t.lo[i] : 0, len = leaf ? t.len[i] : 0;
+    const int whole = len - len % 8;  // values in whole groups of eight (none below 8 values)
+    double r = 0.0;
+    if (len >= 8) {
+      r = value(lo + j);
+      for (int k = 8; k < whole; k += 8) r += value(lo + k + j);
+    }
+    r += __shfl_xor_sync(kFullMask, r, 1);  // r0 + r1, r2 + r3, ...
+    r += __shfl_xor_sync(kFullMask, r, 2);  // (r0 + r1) + (r2 + r3), ...
+    r += __shfl_xor_sync(kFullMask, r, 4);  // ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7))
+    if (leaf && j == 0) {
+      double res = len >= 8 ? r : 0.0;  // below 8 values a plain loop from 0.0
+      for (int k = len >= 8 ? whole : 0; k < len; ++k) res += value(lo + k);
+      t.val[i] = res;
+    }
+  }
   __syncthreads();
   if (tid < 32) {
     for (int d = t.meta[1] - 1; d >= 0; --d) {  // each inner node: left + right, deepest level first

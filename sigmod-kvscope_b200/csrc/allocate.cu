@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(kSumThreads) sum_prep_kernel(const SumParams p
   extern __shared__ __align__(16) unsigned char sum_smem[];
   S* s_x = reinterpret_cast<S*>(sum_smem);  // [width]: the row's scores, then the pairwise sum's scratch
   const PairwiseScratch s_tree =
-      pairwise_scratch(sum_smem + ((size_t)p.width * sizeof(S) + 15) / 16 * 16, pairwise_nodes(p.width));
+      pairwise_scratch(sum_smem + ((size_t)p.width * sizeof(S) + 15) / 16 * 16, pairwise_slots(p.width));
   __shared__ unsigned int s_hist[kSumBins];
   __shared__ double s_total;
   __shared__ bool s_last;
@@ -704,7 +704,7 @@ static int allocate_sum(const S* scores, int64_t score_stride, const int32_t* sc
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
     return check_launch("cudaDeviceGetAttribute");
   if (cudaMemsetAsync(base, 0, l.zeroed, s) != cudaSuccess) return check_launch("cudaMemsetAsync(sum workspace)");
-  const size_t prep_smem = ((size_t)width * sizeof(S) + 15) / 16 * 16 + pairwise_bytes(pairwise_nodes(width));
+  const size_t prep_smem = ((size_t)width * sizeof(S) + 15) / 16 * 16 + pairwise_bytes(pairwise_slots(width));
   static size_t configured[kMaxDevices] = {};
   if (configured[device] < prep_smem) {
     if (cudaFuncSetAttribute(sum_prep_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem) !=

@@ -122,7 +122,7 @@ __host__ __device__ __forceinline__ size_t mm_prep_smem(int width) {
   const size_t keys = (size_t)mm_sort_n(width) * sizeof(S);
   const size_t blocks = ((size_t)mm_sort_n(width) * 2 + 15) / 16 * 16;
   const size_t sort = keys + blocks + (size_t)kMmWarps * kMmCountStride * 2;
-  const size_t tree = pairwise_bytes(pairwise_nodes(width));
+  const size_t tree = pairwise_bytes(pairwise_slots(width));
   return scores + (sort > tree ? sort : tree);
 }
 
@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(kMmThreads) mm_prep_kernel(const MmParams p) {
   uint16_t* s_blk = reinterpret_cast<uint16_t*>(s_key + N);
   uint16_t* s_cnt = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(s_blk) + ((size_t)N * 2 + 15) / 16 * 16);
   __shared__ int s_scan[kMmThreads / 32 + 1];
-  const PairwiseScratch s_tree = pairwise_scratch(s_key, pairwise_nodes(p.width));  // until the keys are written
+  const PairwiseScratch s_tree = pairwise_scratch(s_key, pairwise_slots(p.width));  // until the keys are written
   const int ps = request ? pin_start(n, p.recent, p.measured, r) : 0;
   const int m = ps > 1 ? ps - 1 : 0;  // unpinned blocks [1, ps)
   if (request) {

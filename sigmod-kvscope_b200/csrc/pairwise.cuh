@@ -4,101 +4,68 @@
 // 0.0; up to 128 values eight accumulators r[j] += a[i + j] over whole groups of 8, combined as
 // ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)), then the rest one by one; above 128 values
 // pairwise_sum(a, n2) + pairwise_sum(a + n2, n - n2) with n2 = n / 2 rounded down to a multiple of 8.
-// Here the tree is built one level at a time (every node of a level splits and records its children),
-// the leaves are summed in parallel, and the levels are combined from the bottom up: the same additions
-// in the same order as numpy's recursion.
+// The recursion's shape depends on n alone, and the right half is never the smaller, so its deepest leaves
+// lie D levels down the path that always takes the right half. Here every node is named by a slot of D
+// bits, the path from the root (a 1 takes the right half), its trailing bits zero below the node's own
+// level: the leaves are summed in parallel into their slots, and the levels are combined from the bottom
+// up, each inner node adding its right half's slot to its own: the same additions in the same order as
+// numpy's recursion.
 #pragma once
 
 #include "ekv_common.cuh"
 
 namespace ekv {
 
-constexpr int kPairwiseMaxLevels = 16;
-
-// The most nodes numpy's recursion makes for up to n values: one leaf up to 128 values, and every split of
-// more than 128 values gives halves of at least 64, so at most 129 nodes for 8192 values, 257 for 16384
-// and 513 for 32768.
-__host__ __device__ constexpr int pairwise_nodes(int n) {
-  return n <= 128 ? 1 : (n <= 8192 ? 129 : (n <= 16384 ? 257 : 513));
+// Slots of block_pairwise_sum for up to n values, 2^D: every right half is at most n / 2 + 8 values, so D
+// is at most 7 for 8192 values, 8 for 16384 and 9 for 32768.
+__host__ __device__ constexpr int pairwise_slots(int n) {
+  return n <= 128 ? 1 : (n <= 8192 ? 128 : (n <= 16384 ? 256 : 512));
 }
 
-// Bytes of block_pairwise_sum's scratch for up to `nodes` nodes: the node values (float64), ranges and
-// children, the levels and two counters; a multiple of 8.
-__host__ __device__ constexpr size_t pairwise_bytes(int nodes) {
-  return (size_t)nodes * 8 + (((size_t)nodes * 3 + kPairwiseMaxLevels + 4) * 4 + 7) / 8 * 8;
-}
+// Bytes of block_pairwise_sum's scratch of `slots` slots (one float64 each).
+__host__ __device__ constexpr size_t pairwise_bytes(int slots) { return (size_t)slots * 8; }
 
-// block_pairwise_sum's scratch, carved from pairwise_bytes(nodes) of 8-byte aligned shared memory.
+// block_pairwise_sum's scratch, carved from pairwise_bytes(slots) of 8-byte aligned shared memory.
 struct PairwiseScratch {
   double* val;
-  int *lo, *len, *left, *level, *meta;  // meta: the nodes made, the depth
 };
 
-__device__ __forceinline__ PairwiseScratch pairwise_scratch(void* mem, int nodes) {
-  PairwiseScratch t;
-  t.val = static_cast<double*>(mem);
-  t.lo = reinterpret_cast<int*>(t.val + nodes);
-  t.len = t.lo + nodes;
-  t.left = t.len + nodes;
-  t.level = t.left + nodes;
-  t.meta = t.level + kPairwiseMaxLevels + 2;
-  return t;
+__device__ __forceinline__ PairwiseScratch pairwise_scratch(void* mem, int slots) {
+  (void)slots;
+  return PairwiseScratch{static_cast<double*>(mem)};
 }
 
-// The sum of value(0 .. n) as numpy computes it, with a scratch of pairwise_nodes(n) nodes or more; every
-// thread of the CTA calls it and gets the sum. THREADS = blockDim.x (a multiple of 32). The tree (a few
-// hundred nodes at most) is built and combined by warp 0 alone, a level at a time with warp barriers; the
-// leaves are summed by the whole CTA, eight lanes a leaf: lane j keeps numpy's accumulator r[j] (its
-// additions in numpy's order), the eight are combined by shuffles in numpy's order, and lane 0 adds the rest.
-// The lanes of a leaf read eight adjacent values, so leaves that start 128 values apart share a bank only
-// between the four leaves of a warp.
+// The sum of value(0 .. n) as numpy computes it, with a scratch of pairwise_slots(n) slots or more; every
+// thread of the CTA calls it and gets the sum. THREADS = blockDim.x (a multiple of 32). Each leaf is summed
+// by eight lanes: lane j keeps numpy's accumulator r[j] (its additions in numpy's order), the eight are
+// combined by shuffles in numpy's order, and lane 0 adds the rest; the lanes of a leaf read eight adjacent
+// values. Warp 0 combines the levels.
 template <int THREADS, typename V>
 __device__ double block_pairwise_sum(const PairwiseScratch& t, int n, const V& value) {
   const int tid = threadIdx.x, lane = tid & 31;
+  int D = 0;  // the depth of the deepest leaf
+  for (int m = n; m > 128; m -= (m / 2) & ~7) ++D;
+  const int slots = 1 << D;
   __syncthreads();  // the scratch may still be read by an earlier call
-  if (tid < 32) {
-    // level d holds nodes [level[d], level[d + 1]); a node of more than 128 values splits, its children
-    // placed after the level in node order (a ballot gives each splitting node its children's place)
-    if (lane == 0) t.lo[0] = 0, t.len[0] = n, t.level[0] = 0, t.level[1] = 1;
-    __syncwarp();
-    int nodes = 1, depth = 1;
-    for (int d = 0; d < kPairwiseMaxLevels; ++d) {
-      const int a = t.level[d], b = t.level[d + 1];
-      if (a == b) break;
-      int next = b;
-      for (int i0 = a; i0 < b; i0 += 32) {
-        const int i = i0 + lane;
-        const int len = i < b ? t.len[i] : 0;
-        const bool split = len > 128;
-        const unsigned int ballot = __ballot_sync(kFullMask, split);
-        if (i < b) {
-          if (split) {
-            const int c = next + 2 * __popc(ballot & lanes_below());
-            int n2 = len / 2;
-            n2 -= n2 % 8;
-            const int lo = t.lo[i];
-            t.lo[c] = lo, t.len[c] = n2, t.lo[c + 1] = lo + n2, t.len[c + 1] = len - n2;
-            t.left[i] = c;
-          } else {
-            t.left[i] = -1;
-          }
-        }
-        next += 2 * __popc(ballot);
-      }
-      if (lane == 0) t.level[d + 2] = next;
-      nodes = next;
-      depth = d + 1;
-      __syncwarp();
-    }
-    if (lane == 0) t.meta[0] = nodes, t.meta[1] = depth;
-  }
-  __syncthreads();
-  const int nodes = t.meta[0];
+  // the leaves: slot s follows its bits from the root until a node of at most 128 values; that leaf is the
+  // slot's when the bits below the leaf's level are zero
   const int oct = tid >> 3, j = tid & 7;
-  for (int i0 = 0; i0 < nodes; i0 += THREADS / 8) {  // (the same trip count in every lane)
-    const int i = i0 + oct;
-    const bool leaf = i < nodes && t.left[i] < 0;
-    const int lo = leaf ? t.lo[i] : 0, len = leaf ? t.len[i] : 0;
+  for (int s0 = 0; s0 < slots; s0 += THREADS / 8) {  // (the same trip count in every lane)
+    const int s = s0 + oct;
+    int lo = 0, len = n, depth = 0;
+    if (s < slots) {
+      for (; depth < D && len > 128; ++depth) {
+        const int half = (len / 2) & ~7;
+        if ((s >> (D - 1 - depth)) & 1) {
+          lo += half;
+          len -= half;
+        } else {
+          len = half;
+        }
+      }
+    }
+    const bool leaf = s < slots && (s & ((1 << (D - depth)) - 1)) == 0;
+    if (!leaf) len = 0;
     const int whole = len - len % 8;  // values in whole groups of eight (none below 8 values)
     double r = 0.0;
     if (len >= 8) {
@@ -111,14 +78,30 @@ __device__ double block_pairwise_sum(const PairwiseScratch& t, int n, const V& v
     if (leaf && j == 0) {
       double res = len >= 8 ? r : 0.0;  // below 8 values a plain loop from 0.0
       for (int k = len >= 8 ? whole : 0; k < len; ++k) res += value(lo + k);
-      t.val[i] = res;
+      t.val[s] = res;
     }
   }
   __syncthreads();
   if (tid < 32) {
-    for (int d = t.meta[1] - 1; d >= 0; --d) {  // each inner node: left + right, deepest level first
-      for (int i = t.level[d] + lane; i < t.level[d + 1]; i += 32)
-        if (t.left[i] >= 0) t.val[i] = t.val[t.left[i]] + t.val[t.left[i] + 1];
+    // level d, deepest first: node k (its d bits) is the slot k << (D - d); an inner node (every ancestor and
+    // itself of more than 128 values) adds its right half, at slot + 2^(D - d - 1)
+    for (int d = D - 1; d >= 0; --d) {
+      for (int k = lane; k < (1 << d); k += 32) {
+        int len = n;
+        bool inner = true;
+        for (int e = 0; e < d && inner; ++e) {
+          if (len <= 128) {
+            inner = false;
+          } else {
+            const int half = (len / 2) & ~7;
+            len = ((k >> (d - 1 - e)) & 1) ? len - half : half;
+          }
+        }
+        if (inner && len > 128) {
+          const int s = k << (D - d);
+          t.val[s] = t.val[s] + t.val[s + (1 << (D - d - 1))];
+        }
+      }
       __syncwarp();
     }
   }

@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(kPinThreads) pin_slots_kernel(const PinParams 
   chain_release();
   chain_wait();  // what the launch before this one wrote
   extern __shared__ __align__(16) unsigned char pin_smem[];
-  const PairwiseScratch s_tree = pairwise_scratch(pin_smem + (size_t)p.width * 8, pairwise_nodes(p.width));
+  const PairwiseScratch s_tree = pairwise_scratch(pin_smem + (size_t)p.width * 8, pairwise_slots(p.width));
   __shared__ int s_scan[kPinThreads / 32 + 1];
   double* s_x = reinterpret_cast<double*>(pin_smem);  // [width]
   const int r = blockIdx.x, tid = threadIdx.x;
@@ -230,7 +230,7 @@ extern "C" int ekv_allocate_pinned_f64(const double* scores, int64_t score_strid
     const int dev_rc = current_device(&device);
     if (dev_rc != EKV_OK) return dev_rc;
   }
-  const size_t smem = (size_t)width * 8 + pairwise_bytes(pairwise_nodes(width));
+  const size_t smem = (size_t)width * 8 + pairwise_bytes(pairwise_slots(width));
   static size_t configured[kMaxDevices] = {};
   if (configured[device] < smem) {
     if (cudaFuncSetAttribute(pin_slots_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)

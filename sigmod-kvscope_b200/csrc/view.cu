@@ -322,10 +322,10 @@ __device__ __forceinline__ unsigned long long share_key64(double s, double total
 
 template <typename K>
 __host__ __device__ constexpr size_t view_smem_bytes(int width) {
-  // keys (the staged scores, then the keys, then the view row) + the table row (+ the pairwise-sum tree), each
+  // keys (the staged scores, then the keys, then the view row) + the table row (+ the pairwise sum's slots), each
   // padded to whole segments
   return (size_t)((width + kViewSeg - 1) / kViewSeg * kViewSeg) * (sizeof(K) + 4) +
-         (sizeof(K) == 8 ? pairwise_bytes(pairwise_nodes(width)) : 0);
+         (sizeof(K) == 8 ? pairwise_bytes(pairwise_slots(width)) : 0);
 }
 
 // One CTA per row.
@@ -463,7 +463,7 @@ __global__ void __launch_bounds__(kViewThreads, sizeof(K) == 4 ? 3 : 2) view_ker
     ViewKey<K>::digit(0, shift0, dmask0);
     if constexpr (kWide) {
       const double* s_x = reinterpret_cast<const double*>(keys);
-      const PairwiseScratch tree = pairwise_scratch(smem_view + (size_t)w_pad * (sizeof(K) + 4), pairwise_nodes(W));
+      const PairwiseScratch tree = pairwise_scratch(smem_view + (size_t)w_pad * (sizeof(K) + 4), pairwise_slots(W));
       const double total = p.presummed ? 1.0 : block_pairwise_sum<kViewThreads>(tree, n_a, [&](int i) {
         const double s = s_x[i];
         return s > 0.0 ? s : 0.0;

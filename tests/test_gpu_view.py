@@ -304,6 +304,49 @@ def test_sum_totals_follow_numpys_pairwise_summation():
     assert order_sensitive >= 10  # the totals of permuted copies differ: the summation order matters
 
 
+def test_pairwise_totals_of_rows_longer_than_8192_values():
+    """Rows of 8193 to 32768 values, whose pairwise recursion is 8 or 9 levels deep: three permutations of one
+    row hold the same scores, so which of their equal gains are kept follows the last bits of their float64
+    totals. Float64 rows through allocate() (up to 16384 values), float32 rows through ekv_allocate_sum (up to
+    32768), against the oracle."""
+    import ekv._lib as L
+    from ekv.observe.allocation import Request, allocate
+
+    rng = np.random.default_rng(29)
+    order_sensitive = 0
+    for n in (8193, 12001, 16384):
+        base = np.exp(rng.normal(0.0, 4.0, n)).astype(np.float32).astype(np.float64)
+        scores = [base, rng.permutation(base), rng.permutation(base)]
+        order_sensitive += len({float(np.sum(x)) for x in scores}) > 1
+        pinned = [oa.controller_pins(n, 4) for _ in scores]
+        budget = int(rng.integers(sum(int(p.sum()) for p in pinned) + 1, 3 * n - 1))
+        got = allocate([Request(scores=x, pinned=p) for x, p in zip(scores, pinned, strict=True)], budget, "sum")
+        want = oa.allocate(scores, budget, "sum", pinned)
+        for a, b in zip(got, want, strict=True):
+            np.testing.assert_array_equal(a, b, err_msg=f"float64, {n} values")
+    lib = L.load()
+    for n in (16385, 24007, 32768):
+        base = np.exp(rng.normal(0.0, 4.0, n)).astype(np.float32)
+        rows = np.stack([base, rng.permutation(base), rng.permutation(base)])
+        order_sensitive += len({float(np.sum(x.astype(np.float64))) for x in rows}) > 1
+        pinned = [oa.controller_pins(n, 4) for _ in rows]
+        must = sum(int(p.sum()) for p in pinned)
+        budget = int(rng.integers(must + 1, 3 * n - 1))
+        scores = torch.from_numpy(rows).cuda()
+        row_blocks = torch.full((3,), n, dtype=torch.int32).cuda()
+        quota = torch.empty(3, dtype=torch.int32).cuda()
+        ws_bytes = int(lib.ekv_allocate_sum_workspace_bytes(3, n))
+        ws = torch.empty(ws_bytes + 256, dtype=torch.uint8).cuda()
+        rc = lib.ekv_allocate_sum(scores.data_ptr(), scores.stride(0), None, row_blocks.data_ptr(), None, 4, -1, 0.0,
+                                  budget, 3, n, quota.data_ptr(), (ws.data_ptr() + 255) // 256 * 256, ws_bytes,
+                                  L.current_stream())
+        L.check(rc, "ekv_allocate_sum")
+        want = oa.allocate([x.astype(np.float64) for x in rows], budget, "sum", pinned)
+        want_quota = [int(m.sum()) - int(p.sum()) for m, p in zip(want, pinned, strict=True)]
+        assert quota.cpu().tolist() == want_quota, f"float32, {n} values"
+    assert order_sensitive >= 4  # the totals of permuted copies differ: the summation order matters
+
+
 def test_plan_view_sum_with_a_shared_budget_matches_the_controller():
     """The controller's default objective: one budget over every measured row (cap, recent pins and
     unmeasured suffixes), then the view, against the oracle's controller and compaction."""
